@@ -1,0 +1,352 @@
+#!/usr/bin/env python3
+"""Decode throughput of the Qwen3-0.6B-shape W8A8 decoder at T = 2048 on B200,
+with the int8 GEMV's HBM bandwidth against the measured peak.
+
+Workload (batch 1): synthetic N(0, 0.02) weights
+(seed 0) quantized per output channel, static KV scales from an fp32
+calibration run on 16 seeded tokens; a seeded uniform prompt of
+2048 - warmup - steps tokens (2032 by default) prefilled in 16-row chunks; then
+`warmup` untimed and `steps` timed greedy decode steps, ending at position 2047.
+
+value  device-resident decode: the captured step graph (on-device advance of
+       token and position + the whole forward + argmax) replayed back to back,
+       CUDA events on the launching stream, tokens / s (sum over ranks).
+e2e    the same steps through LlamaDevice.forward: per step a pinned
+       host-to-device copy of (token, pos) and a device-to-host copy of the
+       logits [vocab] fp32, greedy sampling on the host.
+roofline  the classifier GEMV (151936 x 1024, the largest weight stream of the
+       step) timed alone with CUDA events; algorithmic bytes N*K + 4N + K + 4N.
+cpu_baseline  the CPU oracle (NumPy restatement of the reference's device
+       numerics) decoding on this host's cores from the same KV-cache state.
+
+--impl reference times the reference's CPU path (the oracle port: the reference
+is Python and does not travel) on the same config and metric; rank 0 only.
+Multi-GPU: one process per GPU, independent replicas ("scaling": "weak"); the
+batch-1 path has no exchange step in this build.
+"""
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "decode tok/s (Qwen3-0.6B shape W8A8, T=2048)"
+FPGA_TOKS = 3.41          # KV260 overlay, Qwen3-0.6B decode at T = 2048 (docs/results_v2.3.md:93-94)
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+class Clocks:
+    """nvidia-smi samples during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+         "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index, self.proc, self.lines = index, None, []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                                          "-i", str(self.index), "-lms", "200"], stdout=subprocess.PIPE,
+                                         stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *a):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+def dist_init():
+    ws = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if ws > 1:
+        import datetime
+
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=None)
+    return ws, rank, local
+
+
+def max_over_ranks(v, ws):
+    if ws == 1:
+        return v
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([v], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def barrier(ws):
+    if ws > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def cpu_threads():
+    try:
+        from threadpoolctl import threadpool_info
+        return max([i.get("num_threads", 1) for i in threadpool_info()] or [1])
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def oracle_decode(cfg, qw, kv_scales, kc, vc, start, tokens, all_layers=True):
+    """Time the oracle's decode steps at positions start, start + 1, ... from a
+    given cache state (kc / vc [layers, seq_len, kv_dim] int8)."""
+    from oracle import model as OM
+    ora = OM.OracleDecoder(cfg, qw, kv_scales)
+    ora.kc[:], ora.vc[:] = kc, vc
+    ora._w64 = _NoCache()
+    t0 = time.perf_counter()
+    for i, t in enumerate(tokens):
+        ora.forward(int(t), start + i)
+    return time.perf_counter() - t0
+
+
+class _NoCache(dict):
+    """Convert the int8 weights to float64 per use instead of keeping 8 bytes
+    per parameter resident (the C2 model would hold 4.8 GB)."""
+
+    def __setitem__(self, k, v):
+        pass
+
+
+def build_model(cfg, seed):
+    from torch2riscv_accelerator_b200.weights import QuantWeights
+    calib = np.random.default_rng(seed + 1).integers(0, cfg.vocab, 16)
+    return QuantWeights(cfg, seed=seed, calib_tokens=calib)
+
+
+def run_reference(args, cfg, ws, rank):
+    """The reference's CPU path on the host cores: the oracle port (NumPy
+    restatement of DeviceModel / hf_generic numerics) decoding batch-1 steps at
+    T ~ 2048 from a seeded synthetic int8 KV-cache state (the prompt is not
+    prefilled on the CPU: 2032 oracle prefill steps would take hours)."""
+    if rank != 0:
+        return
+    qw = build_model(cfg, args.seed)
+    P = cfg.seq_len - args.warmup - args.steps
+    rng = np.random.default_rng(args.seed + 2)
+    kc = np.zeros((cfg.layers, cfg.seq_len, cfg.kv_dim), np.int8)
+    vc = np.zeros_like(kc)
+    kc[:, :P] = rng.integers(-127, 128, (cfg.layers, P, cfg.kv_dim), dtype=np.int8)
+    vc[:, :P] = rng.integers(-127, 128, (cfg.layers, P, cfg.kv_dim), dtype=np.int8)
+    toks = rng.integers(0, cfg.vocab, args.warmup + args.steps)
+    oracle_decode(cfg, qw, qw.kv_scales, kc, vc, P, toks[:args.warmup])
+    dt = oracle_decode(cfg, qw, qw.kv_scales, kc, vc, P + args.warmup, toks[args.warmup:])
+    v = args.steps / dt
+    cores = len(os.sched_getaffinity(0))
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1e3 * dt / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": v / FPGA_TOKS, "dtype": "int8", "data": "synthetic",
+            "config": config_of(cfg, args, ws),
+            "cpu_baseline": {"value": v, "unit": "tok/s", "cores": cpu_threads(), "kind": "port",
+                             "sample": f"{args.steps} full decode steps (all {cfg.layers} layers + classifier) at "
+                                       f"positions {P + args.warmup}..{cfg.seq_len - 1} from a seeded int8 KV cache; "
+                                       f"{cores} cores visible"},
+            "e2e": {"value": v, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def config_of(cfg, args, ws):
+    P = cfg.seq_len - args.warmup - args.steps
+    return {"workload": f"{cfg.name}-shape W8A8 decode, batch 1 per GPU, T=2048: {P}-token prompt prefilled in "
+                        f"16-row chunks, then {args.warmup} untimed + {args.steps} timed greedy decode steps",
+            "model": cfg.name, "global_batch": ws, "seq_len": cfg.seq_len, "prompt": P,
+            "parallelism": f"replicas x{ws}", "attention": cfg.attn,
+            "l2": "no flush: the step streams 596 MB of weights + 117 MB of KV, over 4x the 126 MB L2"}
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=13)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--config", default="Qwen3-0.6B")
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-steps", type=int, default=2)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    from torch2riscv_accelerator_b200.config import CONFIGS
+    cfg = CONFIGS[args.config]
+    ws, rank, local = dist_init()
+    if args.warmup + args.steps > 64:
+        raise SystemExit("warmup + steps must leave a prompt of >= 1984 tokens (at most 64)")
+    if args.impl == "reference":
+        run_reference(args, cfg, ws, rank)
+        barrier(ws)
+        return
+
+    import torch
+
+    from torch2riscv_accelerator_b200 import ops
+    from torch2riscv_accelerator_b200.model import DeviceDecoder
+    from torch2riscv_accelerator_b200.runtime import LlamaDevice
+    torch.cuda.set_device(local)
+    qw = build_model(cfg, args.seed)
+    dec = DeviceDecoder(cfg, qw, qw.kv_scales)
+    dev = LlamaDevice(dec)
+    P = cfg.seq_len - args.warmup - args.steps
+    prompt = np.random.default_rng(args.seed + 3).integers(0, cfg.vocab, P)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    dev.prefill(prompt)
+    prefill_s = time.perf_counter() - t0
+    st = torch.cuda.current_stream()
+
+    # ---- value: device-resident decode steps (captured step graph)
+    g = dec.capture_decode_step()
+    start_tok = int(dec.next_token[0].item())
+
+    def rewind():
+        dec.pos[0] = P - 1
+        dec.next_token[0] = start_tok
+
+    rewind()
+    for _ in range(args.warmup):
+        g.replay()
+    barrier(ws)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        e0.record(st)
+        for _ in range(args.steps):
+            g.replay()
+        e1.record(st)
+        torch.cuda.synchronize()
+    barrier(ws)
+    dt = max_over_ranks(e0.elapsed_time(e1) / 1e3, ws)
+    value = ws * args.steps / dt
+    final_pos = int(dec.pos[0].item())
+
+    # ---- e2e: LlamaDevice.forward with host inputs / outputs
+    rewind()
+    dev.pos = P
+    tok = start_tok
+    for _ in range(args.warmup):
+        tok = int(np.argmax(dev.forward(tok)))
+    barrier(ws)
+    torch.cuda.synchronize()
+    h0, h1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    h0.record(st)
+    for _ in range(args.steps):
+        tok = int(np.argmax(dev.forward(tok)))
+    h1.record(st)
+    torch.cuda.synchronize()
+    barrier(ws)
+    dt_e2e = max_over_ranks(h0.elapsed_time(h1) / 1e3, ws)
+
+    # ---- roofline: the classifier GEMV alone
+    peak, peak_src = peaks()
+    x1 = dec.x[:1]
+    n_rep = 20
+    for _ in range(3):
+        ops.linear_fused(x1, dec.cls_q, dec.cls_s, norm_g=dec.rms_final, eps=cfg.eps, out=dec.logits[:1])
+    torch.cuda.synchronize()
+    r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    r0.record(st)
+    for _ in range(n_rep):
+        ops.linear_fused(x1, dec.cls_q, dec.cls_s, norm_g=dec.rms_final, eps=cfg.eps, out=dec.logits[:1])
+    r1.record(st)
+    torch.cuda.synchronize()
+    t_gemv = r0.elapsed_time(r1) / 1e3 / n_rep
+    N, K = cfg.vocab, cfg.dim
+    gemv_bytes = N * K + 4 * N + K + 4 * N
+    achieved = gemv_bytes / t_gemv / 1e9
+    step_bytes = dec.weight_bytes() + dec.kv_bytes(cfg.seq_len - 8)
+
+    # ---- CPU baseline: the oracle from the same cache state (rank 0, N = 1)
+    cpu = None
+    if rank == 0 and ws == 1 and not args.no_cpu_baseline:
+        L = cfg.layers
+        kc = np.stack([dec.kv_rows(l, cfg.seq_len)[0] for l in range(L)])
+        vc = np.stack([dec.kv_rows(l, cfg.seq_len)[1] for l in range(L)])
+        toks = np.random.default_rng(5).integers(0, cfg.vocab, args.cpu_steps)
+        cdt = oracle_decode(cfg, qw, qw.kv_scales, kc, vc, P, toks)
+        cpu = {"value": args.cpu_steps / cdt, "unit": "tok/s", "cores": cpu_threads(), "kind": "port",
+               "sample": f"{args.cpu_steps} full decode steps (all {L} layers + classifier) at positions "
+                         f"{P}..{P + args.cpu_steps - 1} from the GPU's KV-cache state (NumPy oracle, float64 "
+                         f"BLAS for exact int dots)"}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1e3 * dt / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": value / FPGA_TOKS, "dtype": "int8",
+            "data": "synthetic (N(0,0.02) weights seed 0, uniform prompt ids)",
+            "config": config_of(cfg, args, ws),
+            "e2e": {"value": ws * args.steps / dt_e2e, "unit": "tok/s", "h2d_bytes_per_step": 8,
+                    "d2h_bytes_per_step": 4 * cfg.vocab},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": None, "peak_source": peak_src,
+                         "kernel": f"linear_kernel (classifier GEMV {N}x{K}, rmsnorm+quant prologue)",
+                         "bytes_per_launch": gemv_bytes, "us_per_launch": t_gemv * 1e6},
+            "step_roofline": {"bytes_per_step": step_bytes, "achieved_gbs": step_bytes / (dt / args.steps) / 1e9,
+                              "frac": step_bytes / (dt / args.steps) / 1e9 / peak},
+            "cpu_baseline": cpu,
+            "gpu_launches": args.steps * (1 + dec.kernel_launches(1)),
+            "clocks": clk.summary(),
+            "prefill": {"tokens": P, "seconds": prefill_s, "tok_s": P / prefill_s},
+            "final_pos": final_pos,
+        }
+        print(json.dumps(line), flush=True)
+    barrier(ws)
+    if ws > 1:
+        import torch.distributed as dist
+        del g
+        dec.graphs.clear()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

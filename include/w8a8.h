@@ -1,0 +1,138 @@
+/* C ABI of the B200 W8A8 decode path (libw8a8_b200.so).
+ *
+ * Drop-in backend for the operators that Torch2RISCV-accelerator's host runtime
+ * submits to the overlay as descriptor lists (llm/compile_model.py builds them,
+ * llm/sa_funcsim.py is their bit-exact model, driver/pynq_matmul.py
+ * Device.submit/wait runs them). Each entry point replaces one fused dispatch
+ * and states the reference code it replaces.
+ *
+ * Conventions
+ * - All pointers are device pointers (cudaMalloc / torch tensors), row-major,
+ *   16-byte aligned; int8 row lengths (k, hidden) are multiples of 16.
+ * - `stream` is a cudaStream_t (NULL: the legacy default stream). Calls are
+ *   asynchronous and stream-ordered; nothing allocates, nothing synchronizes.
+ * - Return 0 (W8A8_OK) or an error code; nothing is launched on an error
+ *   (arguments are checked before any launch). No exceptions cross the ABI.
+ * - Numerics are the overlay's: fp32 steps rounded once each (RNE, never fused),
+ *   EXP/RECIP/RSQRT from the SFU tables (llm/sfu.py), fixed D = 16 lane sums,
+ *   int8 = RNE saturated to +-127 with NaN -> 0.
+ */
+#ifndef W8A8_B200_H
+#define W8A8_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define W8A8_OK 0
+#define W8A8_EINVAL 1   /* a null pointer, a bad size or an unsupported value */
+#define W8A8_EALIGN 2   /* a pointer or a row length off the 16-byte grid */
+#define W8A8_ECUDA 3    /* the CUDA launch failed (cudaGetLastError) */
+#define W8A8_ESCRATCH 4 /* the scratch buffer is smaller than required */
+
+#define W8A8_ABI_VERSION 1
+#define W8A8_MAX_ROWS 16 /* query rows per call (decode: 1, prefill chunk: 16) */
+
+/* ABI version (W8A8_ABI_VERSION) and a message for a status code. */
+int w8a8_abi_version(void);
+const char* w8a8_status_string(int status);
+
+/* Elementwise SFU: func 0 EXP, 1 RECIP, 2 RSQRT (llm/sfu.py:69, :85, :99),
+ * 3 SiLU g*RECIP(1 + EXP(-g)) (llm/ref_model.py:249). */
+int w8a8_sfu(int func, const float* x, float* y, int64_t n, void* stream);
+
+/* Per-token dynamic int8 of `rows` rows of k values: s_x = max|x| * F(1/127),
+ * xq = i8(x * RECIP(s_x)). Replaces DeviceModel.quant_act (llm/ref_model.py:191)
+ * and compile_layer.quant_act (llm/compile_layer.py:66-77). */
+int w8a8_quant_act(const float* x, int rows, int k, int8_t* xq, float* s_x, void* stream);
+
+/* RMSNorm rows: y = (x * RSQRT(red_sum16(x*x) * F(1/n) + eps)) * g.
+ * Replaces DeviceModel.rmsnorm (llm/ref_model.py:204) and
+ * ModelCompiler.rmsnorm (llm/compile_model.py:147-156). */
+int w8a8_rmsnorm(const float* x, const float* g, int rows, int n, float eps, float* y, void* stream);
+
+/* Embedding rows: x[m] = f32(emb_q[tokens[m]]) * emb_s[tokens[m]].
+ * Replaces ModelCompiler.embed (llm/compile_model.py:192-201). */
+int w8a8_embed(const int32_t* tokens, int rows, const int8_t* emb_q, const float* emb_s, int dim, float* x,
+               void* stream);
+
+/* W8A8 linear on int8 activations: acc = xq . W^T (int32), y = (f32(acc) * s_w) * s_x,
+ * or y = resid + that when resid is not NULL (resid may equal y).
+ * w: [n, k] int8 rows, s_w: [n]; xq: [rows, k], s_x: [rows]; y: [rows, n];
+ * acc: [rows, n] int32 or NULL (only without resid). Replaces DeviceModel.linear
+ * (llm/ref_model.py:198), compile_layer.linear (llm/compile_layer.py:93-182), the
+ * GEMV command SaFuncSim.gemv (llm/sa_funcsim.py:138-162) and linear(w2) +
+ * residual (llm/compile_model.py:343-344). */
+int w8a8_linear(const int8_t* xq, const float* s_x, int rows, int k, const int8_t* w, const float* s_w, int n,
+                const float* resid, float* y, int32_t* acc, void* stream);
+
+/* Fused [rmsnorm ->] quant_act -> W8A8 linear [-> + residual] on fp32 rows x [rows, k].
+ * norm_g: [k] RMSNorm gain, or NULL for quant_act(x) alone; resid: [rows, n] or
+ * NULL (y = resid + linear; resid may equal y); s_x_out: [rows] or NULL.
+ * Replaces the sequences rmsnorm + linear(wqkv / wcls) and linear(wo / w2) +
+ * residual of ModelCompiler.layer / final (llm/compile_model.py:333-349). */
+int w8a8_linear_fused(const float* x, const float* norm_g, float eps, int rows, int k, const int8_t* w,
+                      const float* s_w, int n, const float* resid, float* y, float* s_x_out, void* stream);
+
+/* Decode SwiGLU dispatch: [rmsnorm ->] quant_act(x) -> gate and up W8A8 GEMVs ->
+ * h = (g * RECIP(1 + EXP(-g))) * u -> amax -> h_q = i8(h * RECIP(amax * F(1/127))).
+ * w_gate, w_up: [hidden, k]; h: [rows, hidden] fp32; h_q: [rows, hidden] int8,
+ * s_h: [rows]. scratch: w8a8_ffn_scratch_bytes() bytes, zero before the first
+ * call, left zero by every call. Replaces ModelCompiler.ffn_up with fused SiLU
+ * (llm/compile_model.py:295-328) and the FFN region of the IREE plugin
+ * (FfnPlan, compiler/plugins/sa/transforms/SahlKernels.h:130-141). */
+size_t w8a8_ffn_scratch_bytes(int rows);
+int w8a8_ffn_swiglu(const float* x, const float* norm_g, float eps, int rows, int k, const int8_t* w_gate,
+                    const float* s_gate, const int8_t* w_up, const float* s_up, int hidden, float* h,
+                    int8_t* h_q, float* s_h, void* scratch, size_t scratch_bytes, void* stream);
+
+/* Fused per-layer attention of one sequence over its int8 KV cache. */
+typedef struct {
+    int rows;                  /* query rows M (1: decode step, <= 16: prefill chunk) */
+    int heads, kv_heads, head_dim, seq_len;
+    int variant;               /* 0 NORM (llm/ref_model.py:233-243), 1 QSUM (hf_generic.py:264-292) */
+    const int32_t* pos;        /* [rows] positions, device */
+    const float* qkv;          /* [rows, (heads + 2 kv_heads) head_dim]: q | k | v */
+    const float* q_norm;       /* [head_dim] QK-norm gains, or NULL (no QK-norm) */
+    const float* k_norm;
+    float eps;
+    const float* rope_cos;     /* [seq_len, head_dim], pair-repeated */
+    const float* rope_sin;
+    float inv_sk, inv_sv;      /* F(1/s_k), F(1/s_v) */
+    float a_k, a_v;            /* F(s_k/sqrt(head_dim)), F(s_v/127) */
+    int8_t* k_cache;           /* [kv_heads, seq_len, head_dim] this layer's K, written at pos */
+    int8_t* v_cache;
+    float* att;                /* [rows, heads head_dim] out */
+    void* scratch;             /* w8a8_attn_scratch_bytes() bytes, zero before the first call */
+    size_t scratch_bytes;
+} W8A8AttnArgs;
+
+/* QK-norm, RoPE, the K/V rows appended at pos, per-head quant_act of q,
+ * int32 scores, the softmax (global max first, no online rescaling), int8 p,
+ * int32 p.V, dequantized head outputs. Row m attends positions <= pos[m]; all
+ * rows' K/V are written before any row's attention. Replaces
+ * ModelCompiler.rope + kv_append + attention (llm/compile_model.py:203-293),
+ * DeviceModel.forward :225-243, hf_generic.sa_attention + SaCache.update
+ * (:190-293) and the attention regions AttnLayerPlan / AttnChunkPlan
+ * (SahlKernels.h:155-177). */
+size_t w8a8_attn_scratch_bytes(int rows, int heads, int kv_heads, int head_dim, int seq_len);
+int w8a8_attn(const W8A8AttnArgs* args, void* stream);
+
+/* Greedy token per row (np.argmax: the first maximum). Replaces
+ * Sampler.__call__ at temperature 0 (llm/runtime.py:55-57). */
+int w8a8_argmax(const float* logits, int rows, int n, int32_t* out, void* stream);
+
+/* One step of the on-device greedy decode loop: tokens[m] = next[m],
+ * pos[m] += 1 for m < rows (<= 32), so that a captured decode step can replay
+ * back to back without the host. Replaces the host loop of
+ * LlamaDevice.generate (llm/runtime.py:127-148) feeding argmax tokens back. */
+int w8a8_decode_advance(int32_t* tokens, int32_t* pos, const int32_t* next, int rows, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* W8A8_B200_H */

@@ -57,6 +57,29 @@ def attention_rows(q, kc, vc, positions, a_k, a_v, heads, kv_heads, head_dim, va
     return out
 
 
+def attn_layer(cfg, qkv, pos, kc, vc, consts, cos_tab, sin_tab, q_norm=None, k_norm=None):
+    """One layer's attention for rows qkv [M, q|k|v] at positions pos: QK-norm
+    (`qhf.py:335-337`), RoPE, the rows' int8 K/V written into kc / vc
+    [T, kv_dim] first (`llm/ref_model.py:228-229`), then attention_rows."""
+    c = cfg
+    M, H, Hk, hd = qkv.shape[0], c.heads, c.kv_heads, c.head_dim
+    inv_sk, inv_sv, a_k, a_v = consts
+    pos = np.asarray(pos, np.int64)
+    cos, sin = cos_tab[pos], sin_tab[pos]
+    q = qkv[:, :c.q_dim].reshape(M, H, hd)
+    k = qkv[:, c.q_dim:c.q_dim + c.kv_dim].reshape(M, Hk, hd)
+    v = qkv[:, c.q_dim + c.kv_dim:]
+    if q_norm is not None:
+        q = N.rmsnorm(q.reshape(M * H, hd), q_norm, c.eps).reshape(M, H, hd)
+        k = N.rmsnorm(k.reshape(M * Hk, hd), k_norm, c.eps).reshape(M, Hk, hd)
+    q = N.rope(q, cos[:, None, :], sin[:, None, :]).reshape(M, -1)
+    k = N.rope(k, cos[:, None, :], sin[:, None, :]).reshape(M, -1)
+    for m in range(M):
+        kc[pos[m]] = N.to_i8((k[m] * inv_sk).astype(F))
+        vc[pos[m]] = N.to_i8((v[m] * inv_sv).astype(F))
+    return attention_rows(q, kc, vc, pos, a_k, a_v, H, Hk, hd, c.attn)
+
+
 def moe_ffn_row(x, t, cfg):
     """One row of the Mixtral-style MoE block (`hf_generic.QMixtralMoe.route` /
     `_row` :641-657): router W8A8 logits, Top-k (descending; ties -> lower id,
@@ -118,24 +141,12 @@ class OracleDecoder:
         M = tokens.size
         H, Hk, hd = c.heads, c.kv_heads, c.head_dim
         x = (qw.emb_q[tokens].astype(F) * qw.emb_s[tokens][:, None]).astype(F)
-        cos, sin = qw.cos[pos], qw.sin[pos]                          # [M, hd]
         for l in range(c.layers):
             t = qw.layers[l]
-            inv_sk, inv_sv, a_k, a_v = self.consts[l]
             xq, s_x = N.quant_act(N.rmsnorm(x, t["rms_att"], c.eps))
             qkv = self._lin(xq, s_x, ("qkv", l), t["wqkv"], t["s_wqkv"])
-            q = qkv[:, :c.q_dim].reshape(M, H, hd)
-            k = qkv[:, c.q_dim:c.q_dim + c.kv_dim].reshape(M, Hk, hd)
-            v = qkv[:, c.q_dim + c.kv_dim:]
-            if c.qk_norm:
-                q = N.rmsnorm(q.reshape(M * H, hd), t["q_norm"], c.eps).reshape(M, H, hd)
-                k = N.rmsnorm(k.reshape(M * Hk, hd), t["k_norm"], c.eps).reshape(M, Hk, hd)
-            q = N.rope(q, cos[:, None, :], sin[:, None, :]).reshape(M, -1)
-            k = N.rope(k, cos[:, None, :], sin[:, None, :]).reshape(M, -1)
-            for m in range(M):                                       # all rows' K/V first
-                self.kc[l, pos[m]] = N.to_i8((k[m] * inv_sk).astype(F))
-                self.vc[l, pos[m]] = N.to_i8((v[m] * inv_sv).astype(F))
-            att = attention_rows(q, self.kc[l], self.vc[l], pos, a_k, a_v, H, Hk, hd, c.attn)
+            att = attn_layer(c, qkv, pos, self.kc[l], self.vc[l], self.consts[l], qw.cos, qw.sin,
+                             t.get("q_norm"), t.get("k_norm"))
             aq, s_a = N.quant_act(att)
             x = (x + self._lin(aq, s_a, ("wo", l), t["wo"], t["s_wo"])).astype(F)
             xn = N.rmsnorm(x, t["rms_ffn"], c.eps)

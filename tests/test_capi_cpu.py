@@ -1,0 +1,74 @@
+"""The C-ABI library on the CPU: it loads, exports every entry point that
+include/w8a8.h declares, and rejects bad arguments before launching anything
+(no GPU needed: validation runs before any CUDA call)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+from conftest import ROOT
+from torch2riscv_accelerator_b200 import _lib
+
+
+def header_functions():
+    text = open(os.path.join(ROOT, "include", "w8a8.h")).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(w8a8_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_library_exports_every_declared_symbol(lib):
+    names = header_functions()
+    assert len(names) >= 12
+    for n in names:
+        assert hasattr(lib, n), n
+        assert n in _lib.PROTOTYPES, f"{n} has no ctypes prototype"
+
+
+def test_abi_version_and_status_strings(lib):
+    assert lib.w8a8_abi_version() == _lib.ABI_VERSION
+    for s in range(5):
+        assert lib.w8a8_status_string(s)
+
+
+def test_argument_checks_return_status_without_launch(lib):
+    assert lib.w8a8_linear(None, None, 1, 64, None, None, 64, None, None, None, None) == _lib.W8A8_EINVAL
+    assert lib.w8a8_linear(8, 8, 1, 64, 16, 16, 64, None, 16, None, None) == _lib.W8A8_EALIGN     # misaligned w
+    assert lib.w8a8_linear(16, 16, 1, 60, 16, 16, 64, None, 16, None, None) == _lib.W8A8_EALIGN   # k % 16
+    assert lib.w8a8_linear(16, 16, 17, 64, 16, 16, 64, None, 16, None, None) == _lib.W8A8_EINVAL  # rows > 16
+    assert lib.w8a8_linear(16, 16, 1, 64, 16, 16, 64, 16, 16, 16, None) == _lib.W8A8_EINVAL       # resid + acc
+    assert lib.w8a8_linear_fused(16, 16, 0.0, 16, 16384, 16, 16, 64, None, 16, None, None) == _lib.W8A8_EINVAL
+    assert lib.w8a8_sfu(7, 16, 16, 10, None) == _lib.W8A8_EINVAL
+    assert lib.w8a8_sfu(0, None, None, 0, None) == _lib.W8A8_OK                                 # empty: no-op
+    assert lib.w8a8_ffn_swiglu(16, 16, 0.0, 1, 64, 16, 16, 16, 16, 64, 16, 16, 16, 16, 0, None) == \
+        _lib.W8A8_ESCRATCH
+    assert lib.w8a8_argmax(None, 1, 1, None, None) == _lib.W8A8_EINVAL
+
+
+def _attn_args(**kw):
+    base = dict(rows=1, heads=4, kv_heads=2, head_dim=32, seq_len=64, variant=0, pos=16, qkv=16, q_norm=None,
+                k_norm=None, eps=1e-5, rope_cos=16, rope_sin=16, inv_sk=1.0, inv_sv=1.0, a_k=1.0, a_v=1.0,
+                k_cache=16, v_cache=16, att=16, scratch=16,
+                scratch_bytes=_lib.load().w8a8_attn_scratch_bytes(1, 4, 2, 32, 64))
+    base.update(kw)
+    return _lib.W8A8AttnArgs(**base)
+
+
+@pytest.mark.parametrize("kw,status", [
+    (dict(rows=0), _lib.W8A8_EINVAL), (dict(rows=17), _lib.W8A8_EINVAL), (dict(heads=5), _lib.W8A8_EINVAL),
+    (dict(heads=32, kv_heads=2), _lib.W8A8_EINVAL), (dict(variant=2), _lib.W8A8_EINVAL),
+    (dict(head_dim=24), _lib.W8A8_EALIGN), (dict(k_cache=8), _lib.W8A8_EALIGN),
+    (dict(q_norm=16), _lib.W8A8_EINVAL), (dict(scratch_bytes=100), _lib.W8A8_ESCRATCH),
+    (dict(qkv=None), _lib.W8A8_EINVAL)])
+def test_attn_argument_checks(lib, kw, status):
+    a = _attn_args(**kw)
+    assert lib.w8a8_attn(ctypes.byref(a), None) == status
+
+
+def test_scratch_sizes_grow_with_rows_and_length(lib):
+    a = lib.w8a8_attn_scratch_bytes(1, 16, 8, 128, 2048)
+    b = lib.w8a8_attn_scratch_bytes(16, 16, 8, 128, 2048)
+    c = lib.w8a8_attn_scratch_bytes(1, 16, 8, 128, 4096)
+    assert 0 < a < b and a < c
+    assert lib.w8a8_attn_scratch_bytes(0, 16, 8, 128, 2048) == 0
+    assert lib.w8a8_ffn_scratch_bytes(16) >= 256 + 64

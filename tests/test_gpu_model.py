@@ -1,0 +1,147 @@
+"""Whole-decoder parity on the GPU: the runtime (LlamaDevice over the C-ABI
+kernels, CUDA graphs) against the reference's golden outputs and the oracle."""
+import hashlib
+
+import numpy as np
+import pytest
+import torch
+
+from conftest import golden
+from oracle import model as OM
+from torch2riscv_accelerator_b200 import config as C
+from torch2riscv_accelerator_b200 import weights as W
+from torch2riscv_accelerator_b200.model import DeviceDecoder
+from torch2riscv_accelerator_b200.runtime import LlamaDevice
+
+pytestmark = pytest.mark.gpu
+F = np.float32
+
+
+def _tiny(key):
+    g = golden("dm_tiny.npz")
+    dim, hidden, layers, heads, kv_heads, vocab, seq = [int(v) for v in g[f"{key}_cfg"]]
+    cfg = C.ModelConfig(f"tiny-{key}", dim, hidden, layers, heads, kv_heads, dim // heads, vocab, seq,
+                        theta=10000.0, eps=1e-5, tied=False, attn="norm", rope="llama2c")
+    w = {n[len(key) + 3:]: g[n] for n in g.files if n.startswith(f"{key}_w_")}
+    return g, cfg, w
+
+
+@pytest.mark.parametrize("key", ["a", "b"])
+@pytest.mark.parametrize("graphs", [True, False])
+def test_decode_equals_reference_devicemodel(key, graphs):
+    """Logits bit-exact with DeviceModel(SfuExact) (and SaFuncSim) every token;
+    the int8 KV cache bit-exact after the run."""
+    g, cfg, w = _tiny(key)
+    dev = LlamaDevice((cfg, W.from_fp32(cfg, w), g[f"{key}_kv"]), graphs=graphs)
+    for pos, t in enumerate(g["tokens"]):
+        lg = dev.forward(int(t))
+        assert lg.tobytes() == g[f"{key}_logits"][pos].tobytes(), f"pos {pos}"
+    n = len(g["tokens"])
+    for l in range(cfg.layers):
+        k, v = dev.dec.kv_rows(l, n)
+        assert np.array_equal(k, g[f"{key}_kc"][l, :n]) and np.array_equal(v, g[f"{key}_vc"][l, :n])
+
+
+def test_c0_shape_equals_reference_devicemodel():
+    """stories15M shape with seeded synthetic weights: sha256 of every token's
+    logits equals DeviceModel(SfuExact, d=16)'s."""
+    g = golden("dm_c0.npz")
+    cfg = C.C0
+    w = W.fp32_model(cfg, int(g["seed"]), gains="random")
+    dev = LlamaDevice((cfg, W.from_fp32(cfg, w), g["kv"]))
+    for pos, t in enumerate(g["tokens"]):
+        lg = dev.forward(int(t))
+        assert int(np.argmax(lg)) == int(g["argmax"][pos])
+        assert hashlib.sha256(lg.tobytes()).hexdigest() == str(g["logits_sha"][pos]), f"pos {pos}"
+
+
+def _qwen3_tiny(attn):
+    cfg = C.ModelConfig("tiny-qwen3", 64, 128, 2, 4, 2, 32, 96, 64, theta=1e6, eps=1e-6, tied=True, qk_norm=True,
+                        attn=attn, rope="hf")
+    return cfg, W.fp32_model(cfg, 21, gains="random", std=0.2)
+
+
+@pytest.mark.parametrize("attn,fixture", [("qsum", "hf_qwen3.npz"), ("norm", "qhf_qwen3.npz")])
+def test_hf_path_equals_oracle_and_near_reference(attn, fixture):
+    """QK-norm, GQA, tied, theta 1e6: bit-exact with the oracle; within the
+    reduction-order tolerance of the reference's eager HF-path model."""
+    g = golden(fixture)
+    cfg, w = _qwen3_tiny(attn)
+    qw = W.from_fp32(cfg, w)
+    dev = LlamaDevice((cfg, qw, g["kv"]))
+    ora = OM.OracleDecoder(cfg, OM.quantize_model(cfg, w), g["kv"])
+    for pos, t in enumerate(g["tokens"]):
+        lg = dev.forward(int(t))
+        want = ora.forward(int(t), pos)
+        assert lg.tobytes() == want.tobytes(), f"pos {pos}"
+        ref = g["logits"][pos]
+        assert np.max(np.abs(lg - ref)) <= 2e-3 * float(ref.max() - ref.min())
+
+
+def test_prefill_chunks_equal_decode_steps():
+    """A prompt prefilled in 16-row chunks (the last at P - 16) gives the same
+    KV cache and last logits as feeding it token by token
+    (`docs/results_v2.3.md:33-37`: prefill vs decode-only bit-exact)."""
+    cfg = C.ModelConfig("pf", 128, 256, 2, 8, 2, 16, 200, 256, theta=5e5, eps=1e-5, tied=True, attn="qsum",
+                        rope="hf")
+    qw = W.QuantWeights(cfg, seed=5, gains="random")
+    kv = np.full((cfg.layers, 2), 0.02, F)
+    toks = np.random.default_rng(3).integers(0, cfg.vocab, 45)
+    a = LlamaDevice((cfg, qw, kv))
+    la = a.prefill(toks)
+    b = LlamaDevice(a.dec if False else DeviceDecoder(cfg, qw, kv))
+    for t in toks:
+        lb = b.forward(int(t))
+    assert la.tobytes() == lb.tobytes()
+    for l in range(cfg.layers):
+        ka, va = a.dec.kv_rows(l, len(toks))
+        kb, vb = b.dec.kv_rows(l, len(toks))
+        assert np.array_equal(ka, kb) and np.array_equal(va, vb)
+
+
+@pytest.mark.parametrize("attn", ["qsum", "norm"])
+def test_long_context_equals_oracle(attn):
+    """Positions across the 128-position chunk boundaries (127, 128, 129, 255,
+    256, 300): GPU logits and KV bit-exact with the oracle."""
+    cfg = C.ModelConfig("long", 64, 128, 2, 4, 2, 16, 128, 512, theta=1e4, eps=1e-5, tied=False, attn=attn,
+                        rope="hf")
+    w = W.fp32_model(cfg, 9, gains="random", std=0.1)
+    kv = np.array([[0.05, 0.04], [0.06, 0.05]], F)
+    dev = LlamaDevice((cfg, W.from_fp32(cfg, w), kv))
+    ora = OM.OracleDecoder(cfg, OM.quantize_model(cfg, w), kv)
+    toks = np.random.default_rng(1).integers(0, cfg.vocab, 301)
+    dev.prefill(toks[:127])
+    ora.forward_rows(toks[:127], range(127))
+    for p in range(127, 301):
+        lg = dev.forward(int(toks[p]))
+        want = ora.forward(int(toks[p]), p)
+        if p in (127, 128, 129, 255, 256, 300):
+            assert lg.tobytes() == want.tobytes(), f"pos {p}"
+    for l in range(cfg.layers):
+        k, v = dev.dec.kv_rows(l, 301)
+        assert np.array_equal(k, ora.kc[l, :301]) and np.array_equal(v, ora.vc[l, :301])
+
+
+def test_c2_full_dims_two_layers_equals_oracle():
+    """Qwen3-0.6B dimensions (dim 1024, 16/8 heads of 128, QK-norm, hidden 3072)
+    truncated to 2 layers and a 4096-token vocabulary: bit-exact with the
+    oracle for a 20-token prefill and 3 decode steps."""
+    cfg = C.C2.with_(layers=2, vocab=4096)
+    w = W.fp32_model(cfg, 2, gains="random")
+    kv = np.array([[0.04, 0.03], [0.05, 0.02]], F)
+    dev = LlamaDevice((cfg, W.from_fp32(cfg, w), kv))
+    ora = OM.OracleDecoder(cfg, OM.quantize_model(cfg, w), kv)
+    toks = np.random.default_rng(2).integers(0, cfg.vocab, 23)
+    assert dev.prefill(toks[:20]).tobytes() == ora.forward_rows(toks[:20], range(20)).tobytes()
+    for p in range(20, 23):
+        assert dev.forward(int(toks[p])).tobytes() == ora.forward(int(toks[p]), p).tobytes()
+
+
+def test_generate_greedy_matches_forward_argmax():
+    g, cfg, w = _tiny("b")
+    dev = LlamaDevice((cfg, W.from_fp32(cfg, w), g["b_kv"]))
+    prompt = [int(t) for t in g["tokens"][:4]]
+    out = list(dev.generate(prompt, steps=12, stop_at_bos=False))
+    want = [int(np.argmax(g["b_logits"][p])) for p in range(3, 11)]
+    assert out[:3] == prompt[1:4]
+    assert out[3:4] == want[:1]

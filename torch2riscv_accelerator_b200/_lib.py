@@ -1,0 +1,72 @@
+"""ctypes binding of libw8a8_b200.so (the C ABI of include/w8a8.h).
+
+There is no fallback: if the library is missing or cannot be loaded, load()
+raises. The prototypes below are the header's, one per entry point.
+"""
+import ctypes as C
+import os
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libw8a8_b200.so")
+
+W8A8_OK, W8A8_EINVAL, W8A8_EALIGN, W8A8_ECUDA, W8A8_ESCRATCH = 0, 1, 2, 3, 4
+ABI_VERSION = 1
+
+
+class W8A8AttnArgs(C.Structure):
+    _fields_ = [("rows", C.c_int), ("heads", C.c_int), ("kv_heads", C.c_int), ("head_dim", C.c_int),
+                ("seq_len", C.c_int), ("variant", C.c_int), ("pos", C.c_void_p), ("qkv", C.c_void_p),
+                ("q_norm", C.c_void_p), ("k_norm", C.c_void_p), ("eps", C.c_float), ("rope_cos", C.c_void_p),
+                ("rope_sin", C.c_void_p), ("inv_sk", C.c_float), ("inv_sv", C.c_float), ("a_k", C.c_float),
+                ("a_v", C.c_float), ("k_cache", C.c_void_p), ("v_cache", C.c_void_p), ("att", C.c_void_p),
+                ("scratch", C.c_void_p), ("scratch_bytes", C.c_size_t)]
+
+
+P, I, F, Z, L = C.c_void_p, C.c_int, C.c_float, C.c_size_t, C.c_int64
+PROTOTYPES = {
+    "w8a8_abi_version": (I, []),
+    "w8a8_status_string": (C.c_char_p, [I]),
+    "w8a8_sfu": (I, [I, P, P, L, P]),
+    "w8a8_quant_act": (I, [P, I, I, P, P, P]),
+    "w8a8_rmsnorm": (I, [P, P, I, I, F, P, P]),
+    "w8a8_embed": (I, [P, I, P, P, I, P, P]),
+    "w8a8_linear": (I, [P, P, I, I, P, P, I, P, P, P, P]),
+    "w8a8_linear_fused": (I, [P, P, F, I, I, P, P, I, P, P, P, P]),
+    "w8a8_ffn_scratch_bytes": (Z, [I]),
+    "w8a8_ffn_swiglu": (I, [P, P, F, I, I, P, P, P, P, I, P, P, P, P, Z, P]),
+    "w8a8_attn_scratch_bytes": (Z, [I, I, I, I, I]),
+    "w8a8_attn": (I, [C.POINTER(W8A8AttnArgs), P]),
+    "w8a8_argmax": (I, [P, I, I, P, P]),
+    "w8a8_decode_advance": (I, [P, P, P, I, P]),
+}
+
+_LIB = None
+
+
+class W8A8Error(RuntimeError):
+    def __init__(self, fn, status, msg):
+        super().__init__(f"{fn}: status {status} ({msg})")
+        self.fn, self.status = fn, status
+
+
+def load(path=LIB_PATH):
+    """Load the library once and bind the prototypes; raises if it is absent."""
+    global _LIB
+    if _LIB is not None:
+        return _LIB
+    if not os.path.exists(path):
+        raise RuntimeError(f"{path} is missing: build it with `python -m torch2riscv_accelerator_b200.build` "
+                           "(there is no CPU fallback)")
+    lib = C.CDLL(path)
+    for name, (res, args) in PROTOTYPES.items():
+        fn = getattr(lib, name)
+        fn.restype, fn.argtypes = res, args
+    if lib.w8a8_abi_version() != ABI_VERSION:
+        raise RuntimeError(f"{path}: ABI version {lib.w8a8_abi_version()}, expected {ABI_VERSION}")
+    _LIB = lib
+    return lib
+
+
+def check(fn_name, status):
+    if status != W8A8_OK:
+        raise W8A8Error(fn_name, status, load().w8a8_status_string(status).decode())

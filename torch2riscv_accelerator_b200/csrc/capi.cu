@@ -1,0 +1,147 @@
+// The extern "C" entry points of include/w8a8.h: argument checks, then the
+// launches of the kernels in linear.cu, attn.cu and misc.cu.
+#include <cstdint>
+
+#include "../../include/w8a8.h"
+#include "w8a8_internal.h"
+
+using namespace w8a8;
+
+namespace {
+
+inline cudaStream_t S(void* s) { return static_cast<cudaStream_t>(s); }
+inline bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+inline int cuda_status(cudaError_t e) { return e == cudaSuccess ? W8A8_OK : W8A8_ECUDA; }
+inline float inv_of(int n) { return (float)(1.0 / (double)n); }   // F(1.0 / n), as the host computes it
+
+}  // namespace
+
+extern "C" {
+
+int w8a8_abi_version(void) { return W8A8_ABI_VERSION; }
+
+const char* w8a8_status_string(int s) {
+    switch (s) {
+        case W8A8_OK: return "ok";
+        case W8A8_EINVAL: return "invalid argument (null pointer, size or value)";
+        case W8A8_EALIGN: return "pointer or row length not on the 16-byte grid";
+        case W8A8_ECUDA: return "CUDA launch failed";
+        case W8A8_ESCRATCH: return "scratch buffer too small";
+        default: return "unknown status";
+    }
+}
+
+int w8a8_sfu(int func, const float* x, float* y, int64_t n, void* stream) {
+    if (func < 0 || func > 3 || n < 0 || (n > 0 && (!x || !y))) return W8A8_EINVAL;
+    if (n == 0) return W8A8_OK;
+    return cuda_status(launch_sfu(func, x, y, n, S(stream)));
+}
+
+int w8a8_quant_act(const float* x, int rows, int k, int8_t* xq, float* s_x, void* stream) {
+    if (!x || !xq || !s_x || rows <= 0 || k <= 0) return W8A8_EINVAL;
+    return cuda_status(launch_quant_act(x, rows, k, xq, s_x, S(stream)));
+}
+
+int w8a8_rmsnorm(const float* x, const float* g, int rows, int n, float eps, float* y, void* stream) {
+    if (!x || !g || !y || rows <= 0 || n <= 0) return W8A8_EINVAL;
+    return cuda_status(launch_rmsnorm(x, g, rows, n, eps, inv_of(n), y, S(stream)));
+}
+
+int w8a8_embed(const int32_t* tokens, int rows, const int8_t* emb_q, const float* emb_s, int dim, float* x,
+               void* stream) {
+    if (!tokens || !emb_q || !emb_s || !x || rows <= 0 || dim <= 0) return W8A8_EINVAL;
+    return cuda_status(launch_embed(tokens, rows, emb_q, emb_s, dim, x, S(stream)));
+}
+
+static int check_linear(int rows, int k, const void* w, const float* s_w, int n, const void* y) {
+    if (!w || !s_w || !y || rows <= 0 || rows > W8A8_MAX_ROWS || k <= 0 || n <= 0) return W8A8_EINVAL;
+    if (k % 16 || !al16(w)) return W8A8_EALIGN;
+    const int mr = rows <= 1 ? 1 : rows <= 2 ? 2 : rows <= 4 ? 4 : rows <= 8 ? 8 : 16;   // staged rows
+    if ((size_t)mr * k > 200 * 1024) return W8A8_EINVAL;                                 // shared memory
+    return W8A8_OK;
+}
+
+int w8a8_linear(const int8_t* xq, const float* s_x, int rows, int k, const int8_t* w, const float* s_w, int n,
+                const float* resid, float* y, int32_t* acc, void* stream) {
+    int st = check_linear(rows, k, w, s_w, n, y);
+    if (st) return st;
+    if (!xq || !s_x || (resid && acc)) return W8A8_EINVAL;
+    if (!al16(xq)) return W8A8_EALIGN;
+    LinearParams p{};
+    p.m = rows, p.n = n, p.k = k, p.xq = xq, p.s_x = s_x, p.w = w, p.s_w = s_w, p.y = y, p.acc = acc;
+    p.resid = resid;
+    return cuda_status(launch_linear(p, PRO_I8, resid ? EPI_RESID : EPI_STORE, S(stream)));
+}
+
+int w8a8_linear_fused(const float* x, const float* norm_g, float eps, int rows, int k, const int8_t* w,
+                      const float* s_w, int n, const float* resid, float* y, float* s_x_out, void* stream) {
+    int st = check_linear(rows, k, w, s_w, n, y);
+    if (st) return st;
+    if (!x) return W8A8_EINVAL;
+    if (!al16(x) || (norm_g && !al16(norm_g))) return W8A8_EALIGN;
+    LinearParams p{};
+    p.m = rows, p.n = n, p.k = k, p.x = x, p.norm_g = norm_g, p.eps = eps, p.inv_k = inv_of(k);
+    p.w = w, p.s_w = s_w, p.y = y, p.resid = resid, p.s_x_out = s_x_out;
+    const int pro = norm_g ? PRO_RMSQ : PRO_QUANT;
+    const int epi = resid ? EPI_RESID : EPI_STORE;
+    if (pro == PRO_RMSQ && epi == EPI_RESID) return W8A8_EINVAL;
+    return cuda_status(launch_linear(p, pro, epi, S(stream)));
+}
+
+size_t w8a8_ffn_scratch_bytes(int rows) { return 256 + 4 * (size_t)(rows > 0 ? rows : 0); }
+
+int w8a8_ffn_swiglu(const float* x, const float* norm_g, float eps, int rows, int k, const int8_t* w_gate,
+                    const float* s_gate, const int8_t* w_up, const float* s_up, int hidden, float* h,
+                    int8_t* h_q, float* s_h, void* scratch, size_t scratch_bytes, void* stream) {
+    int st = check_linear(rows, k, w_gate, s_gate, hidden, h);
+    if (st) return st;
+    if (!x || !norm_g || !w_up || !s_up || !h_q || !s_h || !scratch) return W8A8_EINVAL;
+    if (!al16(x) || !al16(norm_g) || !al16(w_up) || !al16(scratch)) return W8A8_EALIGN;
+    if (scratch_bytes < w8a8_ffn_scratch_bytes(rows)) return W8A8_ESCRATCH;
+    LinearParams p{};
+    p.m = rows, p.n = hidden, p.k = k, p.x = x, p.norm_g = norm_g, p.eps = eps, p.inv_k = inv_of(k);
+    p.w = w_gate, p.s_w = s_gate, p.w2 = w_up, p.s_w2 = s_up, p.y = h, p.hq = h_q, p.s_h = s_h;
+    p.counter = static_cast<uint32_t*>(scratch);
+    p.amax_bits = reinterpret_cast<uint32_t*>(static_cast<char*>(scratch) + 256);
+    return cuda_status(launch_linear(p, PRO_RMSQ, EPI_SWIGLU, S(stream)));
+}
+
+size_t w8a8_attn_scratch_bytes(int rows, int heads, int kv_heads, int head_dim, int seq_len) {
+    if (rows <= 0 || heads <= 0 || kv_heads <= 0 || head_dim <= 0 || seq_len <= 0) return 0;
+    return attn_scratch_bytes(rows, heads, kv_heads, head_dim, seq_len);
+}
+
+int w8a8_attn(const W8A8AttnArgs* a, void* stream) {
+    if (!a) return W8A8_EINVAL;
+    if (a->rows <= 0 || a->rows > kMaxRows || a->heads <= 0 || a->kv_heads <= 0 || a->heads % a->kv_heads ||
+        a->heads / a->kv_heads > 8 || a->head_dim <= 0 || a->head_dim > 256 || a->seq_len <= 0 ||
+        (a->variant != 0 && a->variant != 1))
+        return W8A8_EINVAL;
+    if (!a->pos || !a->qkv || !a->rope_cos || !a->rope_sin || !a->k_cache || !a->v_cache || !a->att || !a->scratch)
+        return W8A8_EINVAL;
+    if ((a->q_norm == nullptr) != (a->k_norm == nullptr)) return W8A8_EINVAL;
+    if (a->head_dim % 16 || !al16(a->k_cache) || !al16(a->v_cache) || !al16(a->scratch)) return W8A8_EALIGN;
+    if (a->scratch_bytes < attn_scratch_bytes(a->rows, a->heads, a->kv_heads, a->head_dim, a->seq_len))
+        return W8A8_ESCRATCH;
+    AttnParams p{};
+    p.rows = a->rows, p.heads = a->heads, p.kv_heads = a->kv_heads, p.head_dim = a->head_dim;
+    p.seq_len = a->seq_len, p.variant = a->variant, p.qk_norm = a->q_norm != nullptr;
+    p.pos = a->pos, p.qkv = a->qkv, p.q_norm = a->q_norm, p.k_norm = a->k_norm, p.eps = a->eps;
+    p.inv_hd = inv_of(a->head_dim), p.cos = a->rope_cos, p.sin = a->rope_sin;
+    p.inv_sk = a->inv_sk, p.inv_sv = a->inv_sv, p.a_k = a->a_k, p.a_v = a->a_v;
+    p.kc = a->k_cache, p.vc = a->v_cache, p.att = a->att;
+    attn_carve(p, a->scratch);
+    return cuda_status(launch_attn(p, S(stream)));
+}
+
+int w8a8_argmax(const float* logits, int rows, int n, int32_t* out, void* stream) {
+    if (!logits || !out || rows <= 0 || n <= 0) return W8A8_EINVAL;
+    return cuda_status(launch_argmax(logits, rows, n, out, S(stream)));
+}
+
+int w8a8_decode_advance(int32_t* tokens, int32_t* pos, const int32_t* next, int rows, void* stream) {
+    if (!tokens || !pos || !next || rows <= 0 || rows > 32) return W8A8_EINVAL;
+    return cuda_status(launch_decode_advance(tokens, pos, next, rows, S(stream)));
+}
+
+}  // extern "C"

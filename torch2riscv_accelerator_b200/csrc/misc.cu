@@ -1,0 +1,139 @@
+// Small kernels of the decode path: embedding dequant, RMSNorm, quant_act,
+// greedy argmax, and elementwise SFU evaluation (the device functions exposed
+// for testing).
+#include "w8a8_internal.h"
+#include "w8a8_math.cuh"
+
+namespace w8a8 {
+
+// x = f32(q[tok]) * s[tok]  (llm/ref_model.py:221, hf_generic.QEmbedding :698-706)
+__global__ void embed_kernel(const int32_t* tokens, const int8_t* emb_q, const float* emb_s, int dim, float* x) {
+    const int m = blockIdx.x;
+    const int tok = tokens[m];
+    const float s = emb_s[tok];
+    const int8_t* q = emb_q + (size_t)tok * dim;
+    for (int i = threadIdx.x; i < dim; i += blockDim.x) x[(size_t)m * dim + i] = fmul(i2f(q[i]), s);
+}
+
+cudaError_t launch_embed(const int32_t* tokens, int m, const int8_t* emb_q, const float* emb_s, int dim,
+                         float* x, cudaStream_t st) {
+    embed_kernel<<<m, 256, 0, st>>>(tokens, emb_q, emb_s, dim, x);
+    return cudaGetLastError();
+}
+
+// RMSNorm rows (llm/ref_model.py:204-207): ss = red_sum16(x*x),
+// r = RSQRT(ss*F(1/n) + eps), y = (x*r)*g
+__global__ void rmsnorm_kernel(const float* x, const float* g, int n, float eps, float inv_n, float* y) {
+    __shared__ float r;
+    const int m = blockIdx.x, tid = threadIdx.x;
+    const float* xr = x + (size_t)m * n;
+    if (tid < 32) {
+        float ss = red_sum16([&](int i) { float v = xr[i]; return fmul(v, v); }, n, tid);
+        if (tid == 0) r = sfu_rsqrt(fadd(fmul(ss, inv_n), eps));
+    }
+    __syncthreads();
+    for (int i = tid; i < n; i += blockDim.x) y[(size_t)m * n + i] = fmul(fmul(xr[i], r), g[i]);
+}
+
+cudaError_t launch_rmsnorm(const float* x, const float* g, int m, int n, float eps, float inv_n, float* y,
+                           cudaStream_t st) {
+    rmsnorm_kernel<<<m, 256, 0, st>>>(x, g, n, eps, inv_n, y);
+    return cudaGetLastError();
+}
+
+// quant_act rows (llm/ref_model.py:191-196)
+__global__ void quant_act_kernel(const float* x, int k, int8_t* xq, float* s_x) {
+    __shared__ float red[32];
+    const int m = blockIdx.x, tid = threadIdx.x;
+    const float* xr = x + (size_t)m * k;
+    float a = 0.f;
+    for (int i = tid; i < k; i += blockDim.x) a = nanmax(a, fabsf(xr[i]));
+    a = block_nanmax(a, red);
+    const float s = fmul(a, W8A8_C127);
+    const float inv = sfu_recip(s);
+    for (int i = tid; i < k; i += blockDim.x) xq[(size_t)m * k + i] = (int8_t)to_i8(fmul(xr[i], inv));
+    if (tid == 0) s_x[m] = s;
+}
+
+cudaError_t launch_quant_act(const float* x, int m, int k, int8_t* xq, float* s_x, cudaStream_t st) {
+    quant_act_kernel<<<m, 256, 0, st>>>(x, k, xq, s_x);
+    return cudaGetLastError();
+}
+
+// Greedy sampling (llm/runtime.py:55-57, np.argmax: the first maximum; a NaN
+// wins as np.argmax's first NaN does).
+struct ArgMax {
+    float v;
+    int i;
+};
+
+__device__ __forceinline__ ArgMax better(ArgMax a, ArgMax b) {
+    const bool an = a.v != a.v, bn = b.v != b.v;
+    if (an || bn) {
+        if (an && bn) return a.i < b.i ? a : b;
+        return an ? a : b;
+    }
+    if (a.v > b.v) return a;
+    if (b.v > a.v) return b;
+    return a.i < b.i ? a : b;
+}
+
+__global__ void argmax_kernel(const float* logits, int n, int32_t* out) {
+    __shared__ ArgMax red[32];
+    const int m = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const float* row = logits + (size_t)m * n;
+    ArgMax best{-INFINITY, n};
+    for (int i = tid; i < n; i += blockDim.x) best = better(best, ArgMax{row[i], i});
+    for (int o = 16; o > 0; o >>= 1) {
+        ArgMax other{__shfl_xor_sync(0xffffffffu, best.v, o), __shfl_xor_sync(0xffffffffu, best.i, o)};
+        best = better(best, other);
+    }
+    if (lane == 0) red[warp] = best;
+    __syncthreads();
+    if (warp == 0) {
+        best = lane < (int)(blockDim.x >> 5) ? red[lane] : ArgMax{-INFINITY, n};
+        for (int o = 16; o > 0; o >>= 1) {
+            ArgMax other{__shfl_xor_sync(0xffffffffu, best.v, o), __shfl_xor_sync(0xffffffffu, best.i, o)};
+            best = better(best, other);
+        }
+        if (lane == 0) out[m] = best.i < n ? best.i : 0;
+    }
+}
+
+cudaError_t launch_argmax(const float* logits, int m, int n, int32_t* out, cudaStream_t st) {
+    argmax_kernel<<<m, 1024, 0, st>>>(logits, n, out);
+    return cudaGetLastError();
+}
+
+// func: 0 EXP, 1 RECIP, 2 RSQRT, 3 SiLU gate g*sigma(g) (u = 1)
+__global__ void sfu_kernel(int func, const float* x, float* y, long long n) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+        const float v = x[i];
+        y[i] = func == 0 ? sfu_exp(v) : func == 1 ? sfu_recip(v) : func == 2 ? sfu_rsqrt(v) : silu_gate(v, 1.f);
+    }
+}
+
+cudaError_t launch_sfu(int func, const float* x, float* y, long long n, cudaStream_t st) {
+    long long blocks = (n + 255) / 256;
+    if (blocks > 148 * 16) blocks = 148 * 16;
+    if (blocks < 1) blocks = 1;
+    sfu_kernel<<<(int)blocks, 256, 0, st>>>(func, x, y, n);
+    return cudaGetLastError();
+}
+
+// The on-device decode loop's step: the previous step's greedy tokens become
+// this step's inputs, one position later (llm/runtime.py:127-148 on the host).
+__global__ void decode_advance_kernel(int32_t* tokens, int32_t* pos, const int32_t* next, int rows) {
+    const int m = threadIdx.x;
+    if (m < rows) {
+        tokens[m] = next[m];
+        pos[m] += 1;
+    }
+}
+
+cudaError_t launch_decode_advance(int32_t* tokens, int32_t* pos, const int32_t* next, int rows, cudaStream_t st) {
+    decode_advance_kernel<<<1, 32, 0, st>>>(tokens, pos, next, rows);
+    return cudaGetLastError();
+}
+
+}  // namespace w8a8

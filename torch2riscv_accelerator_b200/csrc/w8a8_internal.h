@@ -1,0 +1,79 @@
+// Kernel parameter blocks and launchers shared by the .cu files of the library.
+#pragma once
+#include <cstddef>
+#include <cstdint>
+#include <cuda_runtime.h>
+
+namespace w8a8 {
+
+enum Prologue { PRO_I8 = 0, PRO_QUANT = 1, PRO_RMSQ = 2 };
+enum Epilogue { EPI_STORE = 0, EPI_RESID = 1, EPI_SWIGLU = 2 };
+
+struct LinearParams {
+    int m, n, k;              // rows (tokens), outputs, inputs
+    const float* x;           // [m, k] fp32 input (PRO_QUANT, PRO_RMSQ)
+    const int8_t* xq;         // [m, k] int8 input (PRO_I8)
+    const float* s_x;         // [m] its scales (PRO_I8)
+    const float* norm_g;      // [k] RMSNorm gain (PRO_RMSQ)
+    float eps, inv_k;         // RMSNorm eps and F(1/k)
+    const int8_t* w;          // [n, k] int8 rows
+    const float* s_w;         // [n]
+    const int8_t* w2;         // [n, k] SwiGLU up rows (EPI_SWIGLU)
+    const float* s_w2;        // [n]
+    float* y;                 // [m, n] fp32 out (EPI_SWIGLU: h)
+    const float* resid;       // [m, n] residual (EPI_RESID; may alias y)
+    int32_t* acc;             // [m, n] raw int32 accumulators (optional)
+    float* s_x_out;           // [m] activation scales of the prologue (optional)
+    int8_t* hq;               // [m, n] SwiGLU int8 output
+    float* s_h;               // [m] its scales
+    uint32_t* amax_bits;      // [m] scratch, zero between launches (EPI_SWIGLU)
+    uint32_t* counter;        // [1] scratch, zero between launches (EPI_SWIGLU)
+};
+
+cudaError_t launch_linear(const LinearParams& p, int pro, int epi, cudaStream_t st);
+
+struct AttnParams {
+    int rows;                 // M query rows of one sequence
+    int heads, kv_heads, head_dim, seq_len;
+    int variant;              // 0 NORM, 1 QSUM
+    int qk_norm;
+    const int32_t* pos;       // [M] positions (device)
+    const float* qkv;         // [M, (H + 2 Hk) hd]
+    const float* q_norm;      // [hd] or null
+    const float* k_norm;      // [hd] or null
+    float eps, inv_hd;
+    const float* cos;         // [seq_len, hd]
+    const float* sin;
+    float inv_sk, inv_sv, a_k, a_v;
+    int8_t* kc;               // [Hk, seq_len, hd] this layer's K cache
+    int8_t* vc;               // [Hk, seq_len, hd]
+    float* att;               // [M, H hd] out
+    // scratch (carved by the host wrapper from one buffer)
+    int8_t* qq;               // [M, H, hd]
+    float* s_q;               // [M, H]
+    float* sc;                // [M, H, seq_len]
+    float* pmax;              // [M, H, nsplit]
+    int8_t* pq;               // [M, H, seq_len]
+    float* rq;                // [M, H]
+    int32_t* part;            // [M, H, nsplit, hd]
+    uint32_t* cnt;            // [2 Hk], zero between launches
+    int nsplit;               // ceil(seq_len / kChunk)
+};
+
+constexpr int kChunk = 128;   // cache positions per attention CTA
+constexpr int kMaxRows = 16;  // query rows per attention call
+
+size_t attn_scratch_bytes(int rows, int heads, int kv_heads, int head_dim, int seq_len);
+void attn_carve(AttnParams& p, void* scratch);
+cudaError_t launch_attn(const AttnParams& p, cudaStream_t st);
+
+cudaError_t launch_embed(const int32_t* tokens, int m, const int8_t* emb_q, const float* emb_s, int dim,
+                         float* x, cudaStream_t st);
+cudaError_t launch_argmax(const float* logits, int m, int n, int32_t* out, cudaStream_t st);
+cudaError_t launch_sfu(int func, const float* x, float* y, long long n, cudaStream_t st);
+cudaError_t launch_rmsnorm(const float* x, const float* g, int m, int n, float eps, float inv_n, float* y,
+                           cudaStream_t st);
+cudaError_t launch_decode_advance(int32_t* tokens, int32_t* pos, const int32_t* next, int rows, cudaStream_t st);
+cudaError_t launch_quant_act(const float* x, int m, int k, int8_t* xq, float* s_x, cudaStream_t st);
+
+}  // namespace w8a8

@@ -1,0 +1,171 @@
+"""The W8A8 decoder as a program of kernel launches on one GPU.
+
+The B200 counterpart of the overlay's static descriptor list
+(`llm/compile_model.py:351-374` ModelCompiler.build): built once per model,
+run once per token (or per 16-row prefill chunk), optionally captured as a CUDA
+graph so that only the (pos, token) inputs change between runs, as only the
+PARAM block and the argument block change between the reference's submits
+(`llm/compile_model.py:56-62`).
+
+HBM layout (all resident):
+- linear weights int8 row-major [out, in] (K contiguous: each output channel
+  one 16-byte aligned run), fp32 scales [out]; q|k|v rows fused (wqkv), gate
+  and up rows separate (the SwiGLU kernel reads both for the same channel);
+- the embedding int8 [vocab, dim] + fp32 [vocab], shared with a tied
+  classifier;
+- KV cache int8 [layers, kv_heads, seq_len, head_dim] for K and for V (a head's
+  positions contiguous);
+- RoPE tables fp32 [seq_len, head_dim], pair-repeated.
+Per layer and row: 1 fused rmsnorm+quant+GEMV (wqkv), 3 attention kernels,
+1 quant+GEMV+residual (wo), 1 SwiGLU kernel, 1 GEMV+residual (w2).
+"""
+import numpy as np
+import torch
+
+from . import ops
+from .weights import kv_consts
+
+I8, F32, I32 = torch.int8, torch.float32, torch.int32
+CHUNK = 16                                         # prefill rows per chunk (the reference's M)
+
+
+class DeviceDecoder:
+    def __init__(self, cfg, qw, kv_scales, device="cuda", max_rows=CHUNK):
+        cfg.validate()
+        if cfg.moe:
+            raise NotImplementedError("MoE layers: not on this path yet")
+        self.cfg, self.dev, self.max_rows = cfg, torch.device(device), max_rows
+        t = lambda a, dt=None: torch.as_tensor(np.ascontiguousarray(a), dtype=dt).to(self.dev)
+        self.emb_q, self.emb_s = t(qw.emb_q, I8), t(qw.emb_s, F32)
+        if cfg.tied and qw.cls_q is qw.emb_q:
+            self.cls_q, self.cls_s = self.emb_q, self.emb_s
+        else:
+            self.cls_q, self.cls_s = t(qw.cls_q, I8), t(qw.cls_s, F32)
+        self.rms_final = t(qw.rms_final, F32)
+        self.cos, self.sin = t(qw.cos, F32), t(qw.sin, F32)
+        self.layers = []
+        for lw in qw.layers:
+            d = {k: t(v) for k, v in lw.items()}
+            self.layers.append(d)
+        kv = np.asarray(kv_scales, np.float32)
+        self.consts = [kv_consts(kv[l, 0], kv[l, 1], cfg.head_dim) for l in range(cfg.layers)]
+        L, Hk, T, hd = cfg.layers, cfg.kv_heads, cfg.seq_len, cfg.head_dim
+        self.kc = torch.zeros(L, Hk, T, hd, dtype=I8, device=self.dev)
+        self.vc = torch.zeros(L, Hk, T, hd, dtype=I8, device=self.dev)
+        R = max_rows
+        z = lambda *s, dt=F32: torch.zeros(*s, dtype=dt, device=self.dev)
+        self.tokens, self.pos = z(R, dt=I32), z(R, dt=I32)
+        self.x, self.qkv, self.att = z(R, cfg.dim), z(R, cfg.qkv_dim), z(R, cfg.q_dim)
+        self.h, self.hq, self.s_h = z(R, cfg.hidden), z(R, cfg.hidden, dt=I8), z(R)
+        self.logits = z(R, cfg.vocab)
+        self.next_token = z(R, dt=I32)
+        self.attn_scratch = ops.attn_scratch(R, cfg.heads, cfg.kv_heads, hd, T, self.dev)
+        self.ffn_scratch = ops.ffn_scratch(R, self.dev)
+        self._args = {}
+        self.graphs = {}
+
+    # ------------------------------------------------------------ the program
+    def _attn_args(self, rows):
+        a = self._args.get(rows)
+        if a is None:
+            c = self.cfg
+            a = self._args[rows] = [
+                ops.attn_args(c, rows, self.pos, self.qkv, self.kc[l], self.vc[l], self.att, self.consts[l],
+                              self.cos, self.sin, self.attn_scratch, self.layers[l].get("q_norm"),
+                              self.layers[l].get("k_norm"))
+                for l in range(c.layers)]
+        return a
+
+    def run(self, rows, logits_rows=1, argmax=True):
+        """One pass over `rows` rows whose tokens / positions are in self.tokens /
+        self.pos: all rows' KV rows written, the logits of the last
+        `logits_rows` rows in self.logits[:logits_rows] (argmax in
+        self.next_token)."""
+        c = self.cfg
+        x, qkv, att = self.x[:rows], self.qkv[:rows], self.att[:rows]
+        h, hq, s_h = self.h[:rows], self.hq[:rows], self.s_h[:rows]
+        args = self._attn_args(rows)
+        ops.embed(self.tokens[:rows], self.emb_q, self.emb_s, out=x)
+        for l, w in enumerate(self.layers):
+            ops.linear_fused(x, w["wqkv"], w["s_wqkv"], norm_g=w["rms_att"], eps=c.eps, out=qkv)
+            ops.attn(args[l])
+            ops.linear_fused(att, w["wo"], w["s_wo"], resid=x, out=x)
+            ops.ffn_swiglu(x, w["rms_ffn"], c.eps, w["w1"], w["s_w1"], w["w3"], w["s_w3"], self.ffn_scratch,
+                           h=h, h_q=hq, s_h=s_h)
+            ops.linear(hq, s_h, w["w2"], w["s_w2"], out=x, resid=x)
+        xl = self.x[rows - logits_rows:rows]
+        ops.linear_fused(xl, self.cls_q, self.cls_s, norm_g=self.rms_final, eps=c.eps,
+                         out=self.logits[:logits_rows])
+        if argmax:
+            ops.argmax(self.logits[:logits_rows], out=self.next_token[:logits_rows])
+
+    def kernel_launches(self, rows=1):
+        """Kernels one run() launches (embed, per layer 1 + 3 + 1 + 1 + 1, the
+        classifier and the argmax)."""
+        return 1 + 7 * self.cfg.layers + 2
+
+    def capture(self, rows, logits_rows=1):
+        """Capture run(rows) as a CUDA graph (after one eager warm-up run)."""
+        s = torch.cuda.Stream(device=self.dev)
+        s.wait_stream(torch.cuda.current_stream(self.dev))
+        with torch.cuda.stream(s):
+            self.run(rows, logits_rows)
+        torch.cuda.current_stream(self.dev).wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self.run(rows, logits_rows)
+        self.graphs[(rows, logits_rows)] = g
+        return g
+
+    def decode_step(self):
+        """One on-device greedy decode step: the last step's argmax token at
+        the next position (w8a8_decode_advance), then run(1)."""
+        ops.decode_advance(self.tokens, self.pos, self.next_token, 1)
+        self.run(1)
+
+    def capture_decode_step(self):
+        """decode_step() as a CUDA graph (the warm-up's state change is undone)."""
+        saved = self.tokens.clone(), self.pos.clone(), self.next_token.clone()
+        s = torch.cuda.Stream(device=self.dev)
+        s.wait_stream(torch.cuda.current_stream(self.dev))
+        with torch.cuda.stream(s):
+            self.decode_step()
+        torch.cuda.current_stream(self.dev).wait_stream(s)
+        for dst, src in zip((self.tokens, self.pos, self.next_token), saved):
+            dst.copy_(src)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self.decode_step()
+        self.graphs["step"] = g
+        return g
+
+    def launch(self, rows, logits_rows=1, graph=True):
+        g = self.graphs.get((rows, logits_rows)) if graph else None
+        if graph and g is None:
+            g = self.capture(rows, logits_rows)
+        if g is not None:
+            g.replay()
+        else:
+            self.run(rows, logits_rows)
+
+    # --------------------------------------------------------------- state
+    def reset(self):
+        self.kc.zero_()
+        self.vc.zero_()
+
+    def kv_rows(self, layer, n):
+        """The cache of a layer in the reference's layout: K, V int8 [n, kv_dim]."""
+        k = self.kc[layer, :, :n].permute(1, 0, 2).reshape(n, -1)
+        v = self.vc[layer, :, :n].permute(1, 0, 2).reshape(n, -1)
+        return k.cpu().numpy(), v.cpu().numpy()
+
+    def weight_bytes(self):
+        """int8 weight bytes streamed per decode token (+ fp32 scales)."""
+        c = self.cfg
+        per_layer = c.dim * c.qkv_dim + c.q_dim * c.dim + 3 * c.dim * c.hidden
+        scales = 4 * (c.qkv_dim + c.dim + 2 * c.hidden + c.dim)
+        return c.layers * (per_layer + scales) + c.vocab * c.dim + 4 * c.vocab
+
+    def kv_bytes(self, t):
+        """KV bytes read by one decode step attending t positions."""
+        return self.cfg.layers * 2 * t * self.cfg.kv_dim

@@ -1,0 +1,142 @@
+"""The operator surface on CUDA tensors, one function per C-ABI entry point.
+
+Names and argument meanings follow the reference's operators
+(`llm/ref_model.py` DeviceModel: quant_act, linear, rmsnorm; `llm/compile_model.py`
+ModelCompiler: embed, attention, ffn_up; `llm/runtime.py` Sampler). Every call
+runs on the current torch CUDA stream and raises W8A8Error on a nonzero status.
+Tensors are passed as raw device pointers; torch only owns the memory.
+"""
+import numpy as np
+import torch
+
+from . import _lib
+
+F32, I8, I32 = torch.float32, torch.int8, torch.int32
+SFU_EXP, SFU_RECIP, SFU_RSQRT, SFU_SILU = 0, 1, 2, 3
+
+
+def _p(t):
+    return None if t is None else t.data_ptr()
+
+
+def _st():
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _need(t, dtype, name):
+    if not t.is_cuda or t.dtype != dtype or not t.is_contiguous():
+        raise ValueError(f"{name}: a contiguous CUDA {dtype} tensor is required, got {t.dtype} on {t.device}")
+
+
+def sfu(func, x, out=None):
+    _need(x, F32, "x")
+    out = torch.empty_like(x) if out is None else out
+    _lib.check("w8a8_sfu", _lib.load().w8a8_sfu(func, _p(x), _p(out), x.numel(), _st()))
+    return out
+
+
+def quant_act(x):
+    """x [rows, k] fp32 -> (xq int8 [rows, k], s_x [rows])."""
+    _need(x, F32, "x")
+    x2 = x.reshape(-1, x.shape[-1])
+    xq = torch.empty(x2.shape, dtype=I8, device=x.device)
+    s = torch.empty(x2.shape[0], dtype=F32, device=x.device)
+    _lib.check("w8a8_quant_act", _lib.load().w8a8_quant_act(_p(x2), x2.shape[0], x2.shape[1], _p(xq), _p(s), _st()))
+    return xq.reshape(x.shape), s
+
+
+def rmsnorm(x, g, eps):
+    _need(x, F32, "x")
+    x2 = x.reshape(-1, x.shape[-1])
+    y = torch.empty_like(x2)
+    _lib.check("w8a8_rmsnorm", _lib.load().w8a8_rmsnorm(_p(x2), _p(g), x2.shape[0], x2.shape[1], float(eps), _p(y),
+                                                       _st()))
+    return y.reshape(x.shape)
+
+
+def embed(tokens, emb_q, emb_s, out=None):
+    m, dim = tokens.numel(), emb_q.shape[1]
+    out = torch.empty(m, dim, dtype=F32, device=emb_q.device) if out is None else out
+    _lib.check("w8a8_embed", _lib.load().w8a8_embed(_p(tokens), m, _p(emb_q), _p(emb_s), dim, _p(out), _st()))
+    return out
+
+
+def linear(xq, s_x, w, s_w, out=None, acc=None, resid=None):
+    """W8A8 linear on int8 rows: y = (f32(xq . W^T) * s_w) * s_x [+ resid]."""
+    _need(xq, I8, "xq")
+    _need(w, I8, "w")
+    m, k = xq.shape
+    n = w.shape[0]
+    out = torch.empty(m, n, dtype=F32, device=w.device) if out is None else out
+    _lib.check("w8a8_linear", _lib.load().w8a8_linear(_p(xq), _p(s_x), m, k, _p(w), _p(s_w), n, _p(resid), _p(out),
+                                                     _p(acc), _st()))
+    return out
+
+
+def linear_fused(x, w, s_w, norm_g=None, eps=0.0, resid=None, out=None, s_x_out=None):
+    """[rmsnorm ->] quant_act -> linear [-> + resid] on fp32 rows x [m, k]."""
+    _need(x, F32, "x")
+    _need(w, I8, "w")
+    m, k = x.shape
+    n = w.shape[0]
+    out = torch.empty(m, n, dtype=F32, device=w.device) if out is None else out
+    _lib.check("w8a8_linear_fused", _lib.load().w8a8_linear_fused(
+        _p(x), _p(norm_g), float(eps), m, k, _p(w), _p(s_w), n, _p(resid), _p(out), _p(s_x_out), _st()))
+    return out
+
+
+def ffn_scratch(rows, device):
+    n = _lib.load().w8a8_ffn_scratch_bytes(rows)
+    return torch.zeros(n, dtype=torch.uint8, device=device)
+
+
+def ffn_swiglu(x, norm_g, eps, w_gate, s_gate, w_up, s_up, scratch, h=None, h_q=None, s_h=None):
+    """Decode SwiGLU dispatch: returns (h fp32, h_q int8, s_h)."""
+    _need(x, F32, "x")
+    m, k = x.shape
+    hidden = w_gate.shape[0]
+    dev = x.device
+    h = torch.empty(m, hidden, dtype=F32, device=dev) if h is None else h
+    h_q = torch.empty(m, hidden, dtype=I8, device=dev) if h_q is None else h_q
+    s_h = torch.empty(m, dtype=F32, device=dev) if s_h is None else s_h
+    _lib.check("w8a8_ffn_swiglu", _lib.load().w8a8_ffn_swiglu(
+        _p(x), _p(norm_g), float(eps), m, k, _p(w_gate), _p(s_gate), _p(w_up), _p(s_up), hidden, _p(h), _p(h_q),
+        _p(s_h), _p(scratch), scratch.numel(), _st()))
+    return h, h_q, s_h
+
+
+def attn_scratch(rows, heads, kv_heads, head_dim, seq_len, device):
+    n = _lib.load().w8a8_attn_scratch_bytes(rows, heads, kv_heads, head_dim, seq_len)
+    return torch.zeros(n, dtype=torch.uint8, device=device)
+
+
+VARIANTS = {"norm": 0, "qsum": 1}
+
+
+def attn_args(cfg, rows, pos, qkv, kc, vc, att, consts, cos, sin, scratch, q_norm=None, k_norm=None):
+    """The W8A8AttnArgs block of one layer (kept alive by the caller: a CUDA
+    graph replays the pointers it captured)."""
+    inv_sk, inv_sv, a_k, a_v = consts
+    return _lib.W8A8AttnArgs(
+        rows=rows, heads=cfg.heads, kv_heads=cfg.kv_heads, head_dim=cfg.head_dim, seq_len=cfg.seq_len,
+        variant=VARIANTS[cfg.attn], pos=_p(pos), qkv=_p(qkv), q_norm=_p(q_norm), k_norm=_p(k_norm),
+        eps=float(np.float32(cfg.eps)), rope_cos=_p(cos), rope_sin=_p(sin), inv_sk=float(inv_sk),
+        inv_sv=float(inv_sv), a_k=float(a_k), a_v=float(a_v), k_cache=_p(kc), v_cache=_p(vc), att=_p(att),
+        scratch=_p(scratch), scratch_bytes=scratch.numel())
+
+
+def attn(args):
+    import ctypes
+    _lib.check("w8a8_attn", _lib.load().w8a8_attn(ctypes.byref(args), _st()))
+
+
+def argmax(logits, out=None):
+    m, n = logits.reshape(-1, logits.shape[-1]).shape
+    out = torch.empty(m, dtype=I32, device=logits.device) if out is None else out
+    _lib.check("w8a8_argmax", _lib.load().w8a8_argmax(_p(logits), m, n, _p(out), _st()))
+    return out
+
+
+def decode_advance(tokens, pos, next_token, rows):
+    _lib.check("w8a8_decode_advance", _lib.load().w8a8_decode_advance(_p(tokens), _p(pos), _p(next_token), rows,
+                                                                     _st()))

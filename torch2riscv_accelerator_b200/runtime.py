@@ -1,0 +1,154 @@
+"""Host runtime with the reference's surface (`llm/runtime.py`): LlamaDevice
+(load once, per-token forward, generate, reset, close, stats) and run.c's
+Sampler, over DeviceDecoder on a B200 instead of the overlay's descriptor ring.
+
+Per token, as the reference does per submit (`llm/runtime.py:107-125`): the
+(pos, token) pair goes to the device (an 8-byte host-to-device copy into the
+graph's input buffers), the captured program replays, and the logits come back
+as a float32 copy. Prompts can also be prefilled in 16-row chunks at 0, M,
+2M, ... and a last one at P - M (`compile_model`'s L6 prefill,
+`compiler/runtime/tools/sa_llm_run.c:255-300`, `qhf.QModel.prefill` :356-364):
+every row is computed exactly as a decode step, so the KV cache and logits
+equal the decode-only run bit for bit.
+"""
+import time
+
+import numpy as np
+import torch
+
+from .model import CHUNK, DeviceDecoder
+
+F = np.float32
+BOS = 1
+
+
+class Sampler:
+    """run.c's sampler (temperature, top-p, xorshift RNG), `llm/runtime.py:37-72`."""
+    MASK = (1 << 64) - 1
+
+    def __init__(self, temperature=0.0, topp=0.9, seed=1):
+        self.t, self.topp, self.state = temperature, topp, seed & self.MASK or 1
+
+    def _u32(self):
+        s = self.state
+        s ^= s >> 12
+        s ^= (s << 25) & self.MASK
+        s ^= s >> 27
+        self.state = s
+        return ((s * 0x2545F4914F6CDD1D) & self.MASK) >> 32
+
+    def _f32(self):
+        return (self._u32() >> 8) / 16777216.0
+
+    def __call__(self, logits):
+        if self.t == 0:
+            return int(np.argmax(logits))
+        x = np.asarray(logits, F) / F(self.t)
+        p = np.exp((x - x.max()).astype(F)).astype(F)
+        p /= p.sum(dtype=F)
+        coin = self._f32()
+        if self.topp <= 0 or self.topp >= 1:
+            c = np.cumsum(p, dtype=F)
+            return int(min(np.searchsorted(c, coin, side="right"), p.size - 1))
+        cutoff = (1.0 - self.topp) / (p.size - 1)
+        idx = np.flatnonzero(p >= cutoff)
+        idx = idx[np.argsort(-p[idx], kind="stable")]
+        c = np.cumsum(p[idx], dtype=F)
+        last = int(min(np.searchsorted(c, F(self.topp), side="right"), idx.size - 1))
+        r = coin * float(c[last])
+        k = int(min(np.searchsorted(c[:last + 1], r, side="right"), last))
+        return int(idx[k])
+
+
+class LlamaDevice:
+    """One sequence on one GPU. model: a DeviceDecoder, or (cfg, QuantWeights,
+    kv_scales) to build one. graphs: replay captured CUDA graphs (default)."""
+
+    def __init__(self, model, device="cuda", graphs=True):
+        self.dec = model if isinstance(model, DeviceDecoder) else DeviceDecoder(*model, device=device)
+        self.cfg = self.dec.cfg
+        self.graphs = graphs
+        self.pos = 0
+        self.stats = []                                   # per token: (pos, wall seconds)
+        self._in = torch.zeros(2 * CHUNK, dtype=torch.int32).pin_memory()   # tokens | positions
+        self._out = torch.zeros(self.cfg.vocab, dtype=torch.float32).pin_memory()
+
+    def reset(self):
+        """Start a new sequence: empty KV cache, pos 0 (`llm/runtime.py:101-105`)."""
+        self.dec.reset()
+        self.pos = 0
+
+    def _submit(self, tokens, positions, logits=True, staging=None):
+        """Stage (tokens, positions) in pinned memory, copy them to the graph's
+        input buffers and launch. staging: a pinned [2*CHUNK] int32 slice that
+        stays untouched until the stream has consumed it (default: the
+        single-token buffer, safe because forward() synchronizes)."""
+        m = len(tokens)
+        buf = self._in if staging is None else staging
+        buf[:m] = torch.as_tensor(tokens, dtype=torch.int32)
+        buf[CHUNK:CHUNK + m] = torch.as_tensor(positions, dtype=torch.int32)
+        self.dec.tokens[:m].copy_(buf[:m], non_blocking=True)
+        self.dec.pos[:m].copy_(buf[CHUNK:CHUNK + m], non_blocking=True)
+        self.dec.launch(m, 1, graph=self.graphs)
+        if logits:
+            self._out.copy_(self.dec.logits[0], non_blocking=True)
+
+    def forward(self, token, perf=False):
+        """Logits (float32 copy) of token at the current position; advances pos."""
+        if self.pos >= self.cfg.seq_len:
+            raise ValueError(f"sequence full ({self.cfg.seq_len} positions)")
+        t0 = time.perf_counter()
+        self._submit([int(token)], [self.pos])
+        torch.cuda.current_stream().synchronize()
+        out = self._out.numpy().copy()
+        self.stats.append((self.pos, time.perf_counter() - t0))
+        self.pos += 1
+        return out
+
+    def prefill(self, tokens):
+        """Feed a prompt from the current position in 16-row chunks (a shorter
+        tail as a last chunk ending at the prompt's last token). Returns the
+        logits of its last token."""
+        toks = [int(t) for t in tokens]
+        p0, n = self.pos, len(toks)
+        if p0 + n > self.cfg.seq_len:
+            raise ValueError("prompt beyond the sequence length")
+        if n == 0:
+            raise ValueError("empty prompt")
+        starts = list(range(0, n - CHUNK + 1, CHUNK)) if n >= CHUNK else []
+        if not starts or starts[-1] + CHUNK < n:
+            starts.append(max(n - CHUNK, 0))
+        staging = torch.zeros(len(starts), 2 * CHUNK, dtype=torch.int32).pin_memory()
+        for i, s in enumerate(starts):
+            e = min(s + CHUNK, n)
+            self._submit(toks[s:e], list(range(p0 + s, p0 + e)), logits=i == len(starts) - 1, staging=staging[i])
+        torch.cuda.current_stream().synchronize()
+        self.pos = p0 + n
+        return self._out.numpy().copy()
+
+    def generate(self, prompt_tokens, steps=256, temperature=0.0, topp=0.9, seed=1, stop_at_bos=True,
+                 forced=None):
+        """Yield token ids run.c style (`llm/runtime.py:127-148`): the prompt's
+        tokens are fed first, then sampled tokens, until `steps` positions.
+        forced: teacher forcing; yields (argmax, logits) per position."""
+        self.reset()
+        toks = list(forced if forced is not None else prompt_tokens)
+        sample = Sampler(temperature, topp, seed)
+        token = toks[0]
+        for pos in range(min(steps, self.cfg.seq_len)):
+            logits = self.forward(token)
+            if forced is not None:
+                yield int(np.argmax(logits)), logits
+                if pos + 1 >= len(forced):
+                    return
+                token = forced[pos + 1]
+                continue
+            nxt = toks[pos + 1] if pos + 1 < len(toks) else sample(logits)
+            if nxt == BOS and stop_at_bos:
+                return
+            yield nxt
+            token = nxt
+
+    def close(self):
+        self.dec = None
+        torch.cuda.empty_cache()

@@ -83,28 +83,135 @@ class QuantWeights:
     (q|k|v rows fused as wqkv, w1|w3 as w13, `llm/export_w8a8.py:90-93`),
     fp32 gains, the int8 embedding (shared with a tied classifier)."""
 
-    def __init__(self, cfg, seed=0, gains="ones", layers=None, with_cls=True):
+    def __init__(self, cfg, seed=0, gains="ones", layers=None, with_cls=True, calib_tokens=None):
+        """calib_tokens: token ids of an fp32 calibration run; the static KV
+        scales it gives are in self.kv_scales (`compiler/frontend/qhf.py:245-251`
+        calibrate_kv: max|k|, max|v| per layer after RoPE / QK-norm, / 127)."""
         cfg.validate()
         self.cfg, self.seed = cfg, seed
         g = lambda n, l=-1: gen_tensor(cfg, seed, n, l, gains)
-        self.emb_q, self.emb_s = quantize_rows(g("tok"))
+        tok = g("tok")
+        self.emb_q, self.emb_s = quantize_rows(tok)
         if with_cls:
             self.cls_q, self.cls_s = (self.emb_q, self.emb_s) if cfg.tied else quantize_rows(g("wcls"))
         self.rms_final = g("rms_final")
+        self.cos, self.sin = rope_tables(cfg)
+        cal = None if calib_tokens is None else tok[np.asarray(calib_tokens)].astype(F)
+        del tok
+        L = cfg.layers if layers is None else layers
+        amax = np.zeros((L, 2), F)
         self.layers = []
-        for l in range(cfg.layers if layers is None else layers):
+        for l in range(L):
             t = {"rms_att": g("rms_att", l), "rms_ffn": g("rms_ffn", l)}
-            t["wqkv"], t["s_wqkv"] = quantize_rows(np.concatenate([g("wq", l), g("wk", l), g("wv", l)]))
-            t["wo"], t["s_wo"] = quantize_rows(g("wo", l))
+            f32 = {n: g(n, l) for n in ("wq", "wk", "wv", "wo")}
+            t["wqkv"], t["s_wqkv"] = quantize_rows(np.concatenate([f32["wq"], f32["wk"], f32["wv"]]))
+            t["wo"], t["s_wo"] = quantize_rows(f32["wo"])
             if cfg.qk_norm:
                 t["q_norm"], t["k_norm"] = g("q_norm", l), g("k_norm", l)
             if cfg.moe:
                 t["router"], t["s_router"] = quantize_rows(g("router", l))
                 for n in ("e_gate", "e_up", "e_down"):
-                    t[n], t["s_" + n] = quantize_rows(g(n, l))
+                    f32[n] = g(n, l)
+                    t[n], t["s_" + n] = quantize_rows(f32[n])
+                f32["router"] = g("router", l)
             else:
-                t["w1"], t["s_w1"] = quantize_rows(g("w1", l))
-                t["w3"], t["s_w3"] = quantize_rows(g("w3", l))
-                t["w2"], t["s_w2"] = quantize_rows(g("w2", l))
+                for n in ("w1", "w3", "w2"):
+                    f32[n] = g(n, l)
+                    t[n], t["s_" + n] = quantize_rows(f32[n])
+            if cal is not None:
+                cal, amax[l, 0], amax[l, 1] = calibrate_layer(cfg, cal, t, f32, self.cos, self.sin)
             self.layers.append(t)
-        self.cos, self.sin = rope_tables(cfg)
+        self.kv_scales = (np.maximum(amax, F(1e-8)) / F(127.0)).astype(F) if cal is not None else None
+
+
+def _rms32(x, g, eps):
+    return (x * (1.0 / np.sqrt(np.mean(x * x, axis=-1, keepdims=True) + F(eps))) * g).astype(F)
+
+
+def _swapneg(v):
+    sw = np.empty_like(v)
+    sw[..., 0::2], sw[..., 1::2] = -v[..., 1::2], v[..., 0::2]
+    return sw
+
+
+def calibrate_layer(cfg, x, t, f32, cos, sin):
+    """One layer of the fp32 model (`compiler/frontend/qhf.py:210-242`
+    Fp32Model.forward, all calibration tokens at once with a causal mask):
+    returns (x after the layer, max|k|, max|v|)."""
+    c = cfg
+    n = x.shape[0]
+    H, Hk, hd, G = c.heads, c.kv_heads, c.head_dim, c.group
+    xb = _rms32(x, t["rms_att"], c.eps)
+    q = (xb @ f32["wq"].T).reshape(n, H, hd)
+    k = (xb @ f32["wk"].T).reshape(n, Hk, hd)
+    v = (xb @ f32["wv"].T).reshape(n, Hk, hd)
+    if c.qk_norm:
+        q, k = _rms32(q, t["q_norm"], c.eps), _rms32(k, t["k_norm"], c.eps)
+    cs, sn = cos[:n, None, :], sin[:n, None, :]
+    q = (q * cs + _swapneg(q) * sn).astype(F)
+    k = (k * cs + _swapneg(k) * sn).astype(F)
+    s = np.einsum("qhd,thd->hqt", q, np.repeat(k, G, axis=1)) / F(np.sqrt(hd))
+    s = np.where(np.tril(np.ones((n, n), bool))[None], s, -np.inf)
+    p = np.exp(s - s.max(-1, keepdims=True))
+    p = p / p.sum(-1, keepdims=True)
+    att = np.einsum("hqt,thd->qhd", p, np.repeat(v, G, axis=1)).reshape(n, -1).astype(F)
+    x = (x + att @ f32["wo"].T).astype(F)
+    xb = _rms32(x, t["rms_ffn"], c.eps)
+    if c.moe:
+        logits = xb @ f32["router"].T
+        y = np.zeros_like(x)
+        for r in range(n):
+            ids = np.argsort(-logits[r], kind="stable")[:c.top_k]
+            e = np.exp(logits[r, ids] - logits[r, ids[0]])
+            w = e / e.sum()
+            for wk, i in zip(w, ids):
+                gg, uu = f32["e_gate"][i] @ xb[r], f32["e_up"][i] @ xb[r]
+                y[r] += wk * (f32["e_down"][i] @ (gg / (1 + np.exp(-gg)) * uu))
+        x = (x + y).astype(F)
+    else:
+        h1, h3 = xb @ f32["w1"].T, xb @ f32["w3"].T
+        x = (x + ((h1 / (1 + np.exp(-h1))) * h3) @ f32["w2"].T).astype(F)
+    return x, F(np.abs(k).max()), F(np.abs(v).max())
+
+
+def from_fp32(cfg, w):
+    """QuantWeights from fp32 tensors in the reference's naming
+    (`llm/checkpoint.py:33-59`: tok, rms_att, wq, wk, wv, wo, rms_ffn, w1, w2,
+    w3, rms_final, optional wcls; q_norm / k_norm for QK-norm models), e.g. a
+    llama2.c checkpoint; quantized per output row as `llm/export_w8a8.py:75-99`."""
+    cfg.validate()
+    qw = QuantWeights.__new__(QuantWeights)
+    qw.cfg, qw.seed = cfg, None
+    qw.emb_q, qw.emb_s = quantize_rows(w["tok"])
+    if cfg.tied or "wcls" not in w or w["wcls"] is w["tok"]:
+        qw.cls_q, qw.cls_s = qw.emb_q, qw.emb_s
+    else:
+        qw.cls_q, qw.cls_s = quantize_rows(w["wcls"])
+    qw.rms_final = np.asarray(w["rms_final"], F)
+    qw.layers = []
+    for l in range(cfg.layers):
+        t = {"rms_att": np.asarray(w["rms_att"][l], F), "rms_ffn": np.asarray(w["rms_ffn"][l], F)}
+        t["wqkv"], t["s_wqkv"] = quantize_rows(np.concatenate([w["wq"][l], w["wk"][l], w["wv"][l]]))
+        t["wo"], t["s_wo"] = quantize_rows(w["wo"][l])
+        for n in ("w1", "w3", "w2"):
+            t[n], t["s_" + n] = quantize_rows(w[n][l])
+        if cfg.qk_norm:
+            t["q_norm"], t["k_norm"] = np.asarray(w["q_norm"][l], F), np.asarray(w["k_norm"][l], F)
+        qw.layers.append(t)
+    qw.cos, qw.sin = rope_tables(cfg)
+    return qw
+
+
+def fp32_model(cfg, seed, gains="ones", std=0.02, layers=None):
+    """The synthetic model's fp32 tensors in the reference's naming."""
+    g = lambda n, l=-1: gen_tensor(cfg, seed, n, l, gains, std)
+    L = cfg.layers if layers is None else layers
+    w = {"tok": g("tok"), "rms_final": g("rms_final")}
+    names = ["rms_att", "rms_ffn", "wq", "wk", "wv", "wo", "w1", "w2", "w3"]
+    if cfg.qk_norm:
+        names += ["q_norm", "k_norm"]
+    for n in names:
+        w[n] = np.stack([g(n, l) for l in range(L)])
+    if not cfg.tied:
+        w["wcls"] = g("wcls")
+    return w
