@@ -286,11 +286,11 @@ cudaError_t launch_attn(const AttnParams& p, cudaStream_t st) {
     const int G = p.heads / p.kv_heads;
     size_t smem_s = (size_t)kChunk * (p.head_dim + 16) + (size_t)p.rows * G * p.head_dim;
     if (smem_s < (size_t)p.seq_len * 4) smem_s = (size_t)p.seq_len * 4;   // the softmax's e row
-    if (smem_s > 48 * 1024)
+    if (smem_s > 32 * 1024)
         cudaFuncSetAttribute(attn_scores, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_s);
     attn_scores<<<dim3(p.kv_heads, p.nsplit), kChunk, smem_s, st>>>(p);
     const size_t smem_v = (size_t)kChunk * p.head_dim + (size_t)p.rows * G * kChunk;
-    if (smem_v > 48 * 1024)
+    if (smem_v > 32 * 1024)
         cudaFuncSetAttribute(attn_pv, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_v);
     attn_pv<<<dim3(p.kv_heads, p.nsplit), pthreads, smem_v, st>>>(p);
     return cudaGetLastError();
