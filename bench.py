@@ -27,7 +27,6 @@ batch-1 path has no exchange step in this build.
 import argparse
 import json
 import os
-import subprocess
 import sys
 import threading
 import time
@@ -51,54 +50,63 @@ def peaks():
 
 
 class Clocks:
-    """nvidia-smi samples during the timed region."""
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
-         "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
-         "clocks_event_reasons.sw_power_cap")
+    """SM clock and clock-event reasons sampled through NVML every 2 ms while the
+    timed region runs (read only; nothing is set)."""
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+               0x80: "hw_power_brake_slowdown"}
 
-    def __init__(self, index):
-        self.index, self.proc, self.lines = index, None, []
+    def __init__(self, cuda_index):
+        self.cuda_index, self.samples, self.stop, self.h, self.nv = cuda_index, [], threading.Event(), None, None
+
+    def _handle(self):
+        import pynvml
+        pynvml.nvmlInit()
+        self.nv = pynvml
+        try:
+            import torch
+            pr = torch.cuda.get_device_properties(self.cuda_index)
+            bus = f"{pr.pci_domain_id:08X}:{pr.pci_bus_id:02X}:{pr.pci_device_id:02X}.0"
+            return pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            return pynvml.nvmlDeviceGetHandleByIndex(self.cuda_index)
+
+    def _loop(self):
+        nv = self.nv
+        reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            nv.nvmlDeviceGetCurrentClocksThrottleReasons
+        while True:
+            try:
+                self.samples.append((nv.nvmlDeviceGetClockInfo(self.h, nv.NVML_CLOCK_SM), int(reasons(self.h))))
+            except Exception:
+                pass
+            if self.stop.wait(0.002):
+                break
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
-                                          "-i", str(self.index), "-lms", "200"], stdout=subprocess.PIPE,
-                                         stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
+            self.h = self._handle()
+            self.max_mhz = self.nv.nvmlDeviceGetMaxClockInfo(self.h, self.nv.NVML_CLOCK_SM)
+            self.t = threading.Thread(target=self._loop, daemon=True)
             self.t.start()
         except Exception:
-            self.proc = None
+            self.h = None
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
-
     def __exit__(self, *a):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except Exception:
-                self.proc.kill()
+        self.stop.set()
+        if self.h is not None:
+            self.t.join(timeout=2)
 
     def summary(self):
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            f = [x.strip() for x in ln.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                sm.append(float(f[1]))
-                mx = float(f[2])
-            except ValueError:
-                continue
-            for n, v in zip(names, f[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        sm = [s for s, _ in self.samples]
+        bits = 0
+        for _, r in self.samples:
+            bits |= r
+        return {"sm_mhz": float(np.median(sm)), "sm_max_mhz": float(self.max_mhz),
+                "reasons": sorted(n for b, n in self.REASONS.items() if bits & b), "samples": len(sm),
+                "source": "NVML every 2 ms"}
 
 
 def dist_init():
@@ -240,17 +248,16 @@ def main():
     prompt = np.random.default_rng(args.seed + 3).integers(0, cfg.vocab, P)
     torch.cuda.synchronize()
     t0 = time.perf_counter()
-    dev.prefill(prompt)
+    start_tok = int(np.argmax(dev.prefill(prompt)))
     prefill_s = time.perf_counter() - t0
     st = torch.cuda.current_stream()
 
     # ---- value: device-resident decode steps (captured step graph)
     g = dec.capture_decode_step()
-    start_tok = int(dec.next_token[0].item())
 
     def rewind():
         dec.pos[0] = P - 1
-        dec.next_token[0] = start_tok
+        dec.set_next_token(start_tok)
 
     rewind()
     for _ in range(args.warmup):
@@ -291,12 +298,12 @@ def main():
     x1 = dec.x[:1]
     n_rep = 20
     for _ in range(3):
-        ops.linear_fused(x1, dec.cls_q, dec.cls_s, norm_g=dec.rms_final, eps=cfg.eps, out=dec.logits[:1])
+        ops.classifier(x1, dec.cls_q, dec.cls_s, dec.rms_final, cfg.eps, out=dec.logits[:1])
     torch.cuda.synchronize()
     r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     r0.record(st)
     for _ in range(n_rep):
-        ops.linear_fused(x1, dec.cls_q, dec.cls_s, norm_g=dec.rms_final, eps=cfg.eps, out=dec.logits[:1])
+        ops.classifier(x1, dec.cls_q, dec.cls_s, dec.rms_final, cfg.eps, out=dec.logits[:1])
     r1.record(st)
     torch.cuda.synchronize()
     t_gemv = r0.elapsed_time(r1) / 1e3 / n_rep

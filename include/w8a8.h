@@ -125,11 +125,22 @@ int w8a8_attn(const W8A8AttnArgs* args, void* stream);
  * Sampler.__call__ at temperature 0 (llm/runtime.py:55-57). */
 int w8a8_argmax(const float* logits, int rows, int n, int32_t* out, void* stream);
 
-/* One step of the on-device greedy decode loop: tokens[m] = next[m],
- * pos[m] += 1 for m < rows (<= 32), so that a captured decode step can replay
- * back to back without the host. Replaces the host loop of
- * LlamaDevice.generate (llm/runtime.py:127-148) feeding argmax tokens back. */
-int w8a8_decode_advance(int32_t* tokens, int32_t* pos, const int32_t* next, int rows, void* stream);
+/* Final RMSNorm -> quant_act -> classifier GEMV with the greedy argmax fused
+ * into the epilogue: logits [rows, n] fp32; argmax_key [rows] (zero before the
+ * call) receives the packed maximum (value, lowest index), which
+ * w8a8_decode_advance turns into the next token. Replaces ModelCompiler.final
+ * (llm/compile_model.py:347-349) and Sampler at temperature 0
+ * (llm/runtime.py:55-57). */
+int w8a8_classifier(const float* x, const float* norm_g, float eps, int rows, int k, const int8_t* w,
+                    const float* s_w, int n, float* logits, uint64_t* argmax_key, void* stream);
+
+/* One step of the on-device greedy decode loop, for m < rows (<= 32):
+ * tokens[m] = the index in argmax_key[m], next_token[m] = the same (if not NULL),
+ * argmax_key[m] = 0, pos[m] += 1; so that a captured decode step replays back to
+ * back without the host. Replaces the host loop of LlamaDevice.generate
+ * (llm/runtime.py:127-148) feeding greedy tokens back. */
+int w8a8_decode_advance(int32_t* tokens, int32_t* pos, uint64_t* argmax_key, int32_t* next_token, int rows,
+                        void* stream);
 
 #ifdef __cplusplus
 }

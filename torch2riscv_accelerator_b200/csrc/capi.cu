@@ -57,7 +57,7 @@ static int check_linear(int rows, int k, const void* w, const float* s_w, int n,
     if (!w || !s_w || !y || rows <= 0 || rows > W8A8_MAX_ROWS || k <= 0 || n <= 0) return W8A8_EINVAL;
     if (k % 16 || !al16(w)) return W8A8_EALIGN;
     const int mr = rows <= 1 ? 1 : rows <= 2 ? 2 : rows <= 4 ? 4 : rows <= 8 ? 8 : 16;   // staged rows
-    if ((size_t)mr * k > 200 * 1024) return W8A8_EINVAL;                                 // shared memory
+    if ((size_t)(mr + 4) * k > 200 * 1024) return W8A8_EINVAL;                           // shared memory
     return W8A8_OK;
 }
 
@@ -139,9 +139,23 @@ int w8a8_argmax(const float* logits, int rows, int n, int32_t* out, void* stream
     return cuda_status(launch_argmax(logits, rows, n, out, S(stream)));
 }
 
-int w8a8_decode_advance(int32_t* tokens, int32_t* pos, const int32_t* next, int rows, void* stream) {
-    if (!tokens || !pos || !next || rows <= 0 || rows > 32) return W8A8_EINVAL;
-    return cuda_status(launch_decode_advance(tokens, pos, next, rows, S(stream)));
+int w8a8_classifier(const float* x, const float* norm_g, float eps, int rows, int k, const int8_t* w,
+                    const float* s_w, int n, float* logits, uint64_t* argmax_key, void* stream) {
+    int st = check_linear(rows, k, w, s_w, n, logits);
+    if (st) return st;
+    if (!x || !norm_g) return W8A8_EINVAL;
+    if (!al16(x) || !al16(norm_g)) return W8A8_EALIGN;
+    LinearParams p{};
+    p.m = rows, p.n = n, p.k = k, p.x = x, p.norm_g = norm_g, p.eps = eps, p.inv_k = inv_of(k);
+    p.w = w, p.s_w = s_w, p.y = logits, p.argmax_key = reinterpret_cast<unsigned long long*>(argmax_key);
+    return cuda_status(launch_linear(p, PRO_RMSQ, EPI_STORE, S(stream)));
+}
+
+int w8a8_decode_advance(int32_t* tokens, int32_t* pos, uint64_t* argmax_key, int32_t* next_token, int rows,
+                        void* stream) {
+    if (!tokens || !pos || !argmax_key || rows <= 0 || rows > 32) return W8A8_EINVAL;
+    return cuda_status(launch_decode_advance(tokens, pos, reinterpret_cast<unsigned long long*>(argmax_key),
+                                             next_token, rows, S(stream)));
 }
 
 }  // extern "C"

@@ -30,12 +30,12 @@ constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
 
 template <int MR, int PRO>
-__device__ __forceinline__ void prologue(const LinearParams& p, int8_t* xs, int kpad, float* sx, float* red) {
+__device__ __forceinline__ void prologue(const LinearParams& p, int8_t* xs, float* xf, float* sx, float* red) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int k = p.k;
     if (PRO == PRO_I8) {
         for (int m = 0; m < MR; ++m) {
-            int4* dst = reinterpret_cast<int4*>(xs + (size_t)m * kpad);
+            int4* dst = reinterpret_cast<int4*>(xs + (size_t)m * k);
             const int4* src = reinterpret_cast<const int4*>(p.xq + (size_t)m * k);
             for (int c = tid; c < k / 16; c += kThreads) dst[c] = m < p.m ? __ldg(src + c) : make_int4(0, 0, 0, 0);
         }
@@ -43,28 +43,34 @@ __device__ __forceinline__ void prologue(const LinearParams& p, int8_t* xs, int 
         __syncthreads();
         return;
     }
-    __shared__ float rr[MR];
-    if (PRO == PRO_RMSQ) {
-        // ordered sum of squares: one warp per row
-        for (int m = warp; m < p.m; m += kWarps) {
-            const float* xr = p.x + (size_t)m * k;
-            float ss = red_sum16([&](int i) { float v = xr[i]; return fmul(v, v); }, k, lane);
-            if (lane == 0) rr[m] = sfu_rsqrt(fadd(fmul(ss, p.inv_k), p.eps));
-        }
-        __syncthreads();
-    }
+    __shared__ float rr;
+    // one row at a time through the fp32 staging buffer xf [k]: coalesced
+    // float4 loads, the ordered sum of squares from shared memory (warp 0),
+    // then amax and the int8 row.
     for (int m = 0; m < MR; ++m) {
-        char4* dst = reinterpret_cast<char4*>(xs + (size_t)m * kpad);
+        char4* dst = reinterpret_cast<char4*>(xs + (size_t)m * k);
         if (m >= p.m) {
             for (int c = tid; c < k / 4; c += kThreads) dst[c] = make_char4(0, 0, 0, 0);
             if (tid == 0) sx[m] = 0.f;
             continue;
         }
         const float4* xr = reinterpret_cast<const float4*>(p.x + (size_t)m * k);
+        float4* xf4 = reinterpret_cast<float4*>(xf);
+        __syncthreads();                                         // xf free (previous row done)
+        for (int c = tid; c < k / 4; c += kThreads) xf4[c] = xr[c];
+        __syncthreads();
+        float r = 1.f;
+        if (PRO == PRO_RMSQ) {
+            if (warp == 0) {
+                float ss = red_sum16([&](int i) { float v = xf[i]; return fmul(v, v); }, k, lane);
+                if (lane == 0) rr = sfu_rsqrt(fadd(fmul(ss, p.inv_k), p.eps));
+            }
+            __syncthreads();
+            r = rr;
+        }
         const float4* gr = reinterpret_cast<const float4*>(p.norm_g);
-        const float r = PRO == PRO_RMSQ ? rr[m] : 1.f;
         auto val = [&](int c) {
-            float4 v = xr[c];
+            float4 v = xf4[c];
             if (PRO == PRO_RMSQ) {
                 float4 g = __ldg(gr + c);
                 v.x = fmul(fmul(v.x, r), g.x);
@@ -95,6 +101,14 @@ __device__ __forceinline__ void prologue(const LinearParams& p, int8_t* xs, int 
     __syncthreads();
 }
 
+// Greedy argmax key: larger value first, then the lower index (np.argmax's
+// first maximum; NaN above everything, -0 as +0).
+__device__ __forceinline__ unsigned long long argmax_key(float v, int idx) {
+    uint32_t u = __float_as_uint(v == 0.f ? 0.f : v);
+    uint32_t ord = (v != v) ? 0xFFFFFFFFu : ((u & 0x80000000u) ? ~u : (u | 0x80000000u));
+    return ((unsigned long long)ord << 32) | (0xFFFFFFFFu - (uint32_t)idx);
+}
+
 template <int MR, int PRO, int EPI, int R>
 __global__ void __launch_bounds__(kThreads) linear_kernel(LinearParams p) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -105,8 +119,13 @@ __global__ void __launch_bounds__(kThreads) linear_kernel(LinearParams p) {
     __shared__ int last;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int k = p.k, kpad = k;                 // k % 16 == 0 (checked on the host)
-    if (EPI == EPI_SWIGLU && tid < MR) bamax[tid] = 0u;
-    prologue<MR, PRO>(p, xs, kpad, sx, red);
+    float* xf = reinterpret_cast<float*>(smem_raw + (size_t)MR * k);   // fp32 staging row [k]
+    __shared__ unsigned long long bkey[MR];
+    if (tid < MR) {
+        bamax[tid] = 0u;
+        bkey[tid] = 0ull;
+    }
+    prologue<MR, PRO>(p, xs, xf, sx, red);
 
     constexpr bool kTwo = EPI == EPI_SWIGLU;
     const int row0 = (blockIdx.x * kWarps + warp) * R;
@@ -174,6 +193,7 @@ __global__ void __launch_bounds__(kThreads) linear_kernel(LinearParams p) {
             if (EPI == EPI_STORE) {
                 p.y[o] = v;
                 if (p.acc != nullptr) p.acc[o] = acc[r][m];
+                if (p.argmax_key != nullptr) atomicMax(&bkey[m], argmax_key(v, n));
             } else if (EPI == EPI_RESID) {
                 p.y[o] = fadd(p.resid[o], v);
             } else {
@@ -183,6 +203,10 @@ __global__ void __launch_bounds__(kThreads) linear_kernel(LinearParams p) {
                 atomicMax(&bamax[m], __float_as_uint(fabsf(h)));
             }
         }
+    }
+    if (EPI == EPI_STORE && p.argmax_key != nullptr) {
+        __syncthreads();
+        if (tid < p.m && tid < MR) atomicMax(p.argmax_key + tid, bkey[tid]);
     }
     if (EPI != EPI_SWIGLU) return;
     // row amax across the grid, then the last CTA requantizes (quant_act of h)
@@ -212,7 +236,7 @@ template <int MR, int PRO, int EPI, int R>
 static cudaError_t launch_t(const LinearParams& p, cudaStream_t st) {
     const int rows_per_cta = kWarps * R;
     const int grid = (p.n + rows_per_cta - 1) / rows_per_cta;
-    const size_t smem = (size_t)MR * p.k;
+    const size_t smem = (size_t)MR * p.k + (PRO == PRO_I8 ? 0 : (size_t)p.k * 4);
     auto kern = linear_kernel<MR, PRO, EPI, R>;
     if (smem > 32 * 1024) {            // with the static shared arrays: opt in above the 48 KB default
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);

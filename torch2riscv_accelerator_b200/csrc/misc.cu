@@ -121,18 +121,25 @@ cudaError_t launch_sfu(int func, const float* x, float* y, long long n, cudaStre
     return cudaGetLastError();
 }
 
-// The on-device decode loop's step: the previous step's greedy tokens become
-// this step's inputs, one position later (llm/runtime.py:127-148 on the host).
-__global__ void decode_advance_kernel(int32_t* tokens, int32_t* pos, const int32_t* next, int rows) {
+// The on-device decode loop's step: the previous step's greedy token (the
+// packed key of the fused classifier argmax) becomes this step's input, one
+// position later; the key is cleared for the next classifier launch
+// (llm/runtime.py:127-148 on the host).
+__global__ void decode_advance_kernel(int32_t* tokens, int32_t* pos, unsigned long long* key, int32_t* next,
+                                      int rows) {
     const int m = threadIdx.x;
     if (m < rows) {
-        tokens[m] = next[m];
+        const int t = (int)(0xFFFFFFFFu - (uint32_t)(key[m] & 0xFFFFFFFFull));
+        tokens[m] = t;
+        if (next != nullptr) next[m] = t;
+        key[m] = 0ull;
         pos[m] += 1;
     }
 }
 
-cudaError_t launch_decode_advance(int32_t* tokens, int32_t* pos, const int32_t* next, int rows, cudaStream_t st) {
-    decode_advance_kernel<<<1, 32, 0, st>>>(tokens, pos, next, rows);
+cudaError_t launch_decode_advance(int32_t* tokens, int32_t* pos, unsigned long long* key, int32_t* next, int rows,
+                                  cudaStream_t st) {
+    decode_advance_kernel<<<1, 32, 0, st>>>(tokens, pos, key, next, rows);
     return cudaGetLastError();
 }
 

@@ -28,6 +28,7 @@ struct LinearParams {
     float* s_h;               // [m] its scales
     uint32_t* amax_bits;      // [m] scratch, zero between launches (EPI_SWIGLU)
     uint32_t* counter;        // [1] scratch, zero between launches (EPI_SWIGLU)
+    unsigned long long* argmax_key;   // [m] greedy keys (EPI_STORE, optional; zero before the launch)
 };
 
 cudaError_t launch_linear(const LinearParams& p, int pro, int epi, cudaStream_t st);
@@ -49,14 +50,11 @@ struct AttnParams {
     int8_t* vc;               // [Hk, seq_len, hd]
     float* att;               // [M, H hd] out
     // scratch (carved by the host wrapper from one buffer)
-    int8_t* qq;               // [M, H, hd]
-    float* s_q;               // [M, H]
-    float* sc;                // [M, H, seq_len]
-    float* pmax;              // [M, H, nsplit]
-    int8_t* pq;               // [M, H, seq_len]
-    float* rq;                // [M, H]
-    int32_t* part;            // [M, H, nsplit, hd]
-    uint32_t* cnt;            // [2 Hk], zero between launches
+    float* sc;                // [M, H, seq_len] scores
+    float* pmax;              // [M, H, nsplit] chunk maxima
+    int32_t* part;            // [M, H, nsplit, hd] int32 p.V partials
+    int32_t* psum;            // [M, H, nsplit] QSUM: sum of int8 e per chunk
+    uint32_t* cnt;            // [Hk] tickets, zero between launches
     int nsplit;               // ceil(seq_len / kChunk)
 };
 
@@ -73,7 +71,8 @@ cudaError_t launch_argmax(const float* logits, int m, int n, int32_t* out, cudaS
 cudaError_t launch_sfu(int func, const float* x, float* y, long long n, cudaStream_t st);
 cudaError_t launch_rmsnorm(const float* x, const float* g, int m, int n, float eps, float inv_n, float* y,
                            cudaStream_t st);
-cudaError_t launch_decode_advance(int32_t* tokens, int32_t* pos, const int32_t* next, int rows, cudaStream_t st);
+cudaError_t launch_decode_advance(int32_t* tokens, int32_t* pos, unsigned long long* key, int32_t* next, int rows,
+                                  cudaStream_t st);
 cudaError_t launch_quant_act(const float* x, int m, int k, int8_t* xq, float* s_x, cudaStream_t st);
 
 }  // namespace w8a8

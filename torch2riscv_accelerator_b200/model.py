@@ -59,6 +59,7 @@ class DeviceDecoder:
         self.h, self.hq, self.s_h = z(R, cfg.hidden), z(R, cfg.hidden, dt=I8), z(R)
         self.logits = z(R, cfg.vocab)
         self.next_token = z(R, dt=I32)
+        self.key = z(R, dt=torch.int64)                # packed greedy argmax per row (classifier epilogue)
         self.attn_scratch = ops.attn_scratch(R, cfg.heads, cfg.kv_heads, hd, T, self.dev)
         self.ffn_scratch = ops.ffn_scratch(R, self.dev)
         self._args = {}
@@ -76,11 +77,11 @@ class DeviceDecoder:
                 for l in range(c.layers)]
         return a
 
-    def run(self, rows, logits_rows=1, argmax=True):
+    def run(self, rows, logits_rows=1, argmax=False):
         """One pass over `rows` rows whose tokens / positions are in self.tokens /
         self.pos: all rows' KV rows written, the logits of the last
-        `logits_rows` rows in self.logits[:logits_rows] (argmax in
-        self.next_token)."""
+        `logits_rows` rows in self.logits[:logits_rows]; with argmax, their
+        greedy tokens packed in self.key (which must be zero before)."""
         c = self.cfg
         x, qkv, att = self.x[:rows], self.qkv[:rows], self.att[:rows]
         h, hq, s_h = self.h[:rows], self.hq[:rows], self.s_h[:rows]
@@ -94,15 +95,13 @@ class DeviceDecoder:
                            h=h, h_q=hq, s_h=s_h)
             ops.linear(hq, s_h, w["w2"], w["s_w2"], out=x, resid=x)
         xl = self.x[rows - logits_rows:rows]
-        ops.linear_fused(xl, self.cls_q, self.cls_s, norm_g=self.rms_final, eps=c.eps,
-                         out=self.logits[:logits_rows])
-        if argmax:
-            ops.argmax(self.logits[:logits_rows], out=self.next_token[:logits_rows])
+        ops.classifier(xl, self.cls_q, self.cls_s, self.rms_final, c.eps, out=self.logits[:logits_rows],
+                       argmax_key=self.key[:logits_rows] if argmax else None)
 
     def kernel_launches(self, rows=1):
-        """Kernels one run() launches (embed, per layer 1 + 3 + 1 + 1 + 1, the
-        classifier and the argmax)."""
-        return 1 + 7 * self.cfg.layers + 2
+        """Kernels one run() launches: embed, per layer the qkv GEMV, 2
+        attention kernels, wo, SwiGLU, w2, then the classifier."""
+        return 1 + 6 * self.cfg.layers + 1
 
     def capture(self, rows, logits_rows=1):
         """Capture run(rows) as a CUDA graph (after one eager warm-up run)."""
@@ -120,24 +119,28 @@ class DeviceDecoder:
     def decode_step(self):
         """One on-device greedy decode step: the last step's argmax token at
         the next position (w8a8_decode_advance), then run(1)."""
-        ops.decode_advance(self.tokens, self.pos, self.next_token, 1)
-        self.run(1)
+        ops.decode_advance(self.tokens, self.pos, self.key, 1, next_token=self.next_token)
+        self.run(1, argmax=True)
 
     def capture_decode_step(self):
         """decode_step() as a CUDA graph (the warm-up's state change is undone)."""
-        saved = self.tokens.clone(), self.pos.clone(), self.next_token.clone()
+        saved = self.tokens.clone(), self.pos.clone(), self.key.clone()
         s = torch.cuda.Stream(device=self.dev)
         s.wait_stream(torch.cuda.current_stream(self.dev))
         with torch.cuda.stream(s):
             self.decode_step()
         torch.cuda.current_stream(self.dev).wait_stream(s)
-        for dst, src in zip((self.tokens, self.pos, self.next_token), saved):
+        for dst, src in zip((self.tokens, self.pos, self.key), saved):
             dst.copy_(src)
         g = torch.cuda.CUDAGraph()
         with torch.cuda.graph(g):
             self.decode_step()
         self.graphs["step"] = g
         return g
+
+    def set_next_token(self, token):
+        """Seed the on-device decode loop: the next decode_step() feeds `token`."""
+        self.key[0] = 0xFFFFFFFF - int(token)
 
     def launch(self, rows, logits_rows=1, graph=True):
         g = self.graphs.get((rows, logits_rows)) if graph else None

@@ -137,6 +137,22 @@ def argmax(logits, out=None):
     return out
 
 
-def decode_advance(tokens, pos, next_token, rows):
-    _lib.check("w8a8_decode_advance", _lib.load().w8a8_decode_advance(_p(tokens), _p(pos), _p(next_token), rows,
-                                                                     _st()))
+def classifier(x, w, s_w, norm_g, eps, out=None, argmax_key=None):
+    """Final rmsnorm -> quant_act -> classifier GEMV [+ fused greedy argmax key]."""
+    _need(x, F32, "x")
+    m, k = x.shape
+    n = w.shape[0]
+    out = torch.empty(m, n, dtype=F32, device=w.device) if out is None else out
+    _lib.check("w8a8_classifier", _lib.load().w8a8_classifier(
+        _p(x), _p(norm_g), float(eps), m, k, _p(w), _p(s_w), n, _p(out), _p(argmax_key), _st()))
+    return out
+
+
+def key_token(key):
+    """The token index packed in an argmax key (host side)."""
+    return 0xFFFFFFFF - (int(key) & 0xFFFFFFFF)
+
+
+def decode_advance(tokens, pos, argmax_key, rows, next_token=None):
+    _lib.check("w8a8_decode_advance", _lib.load().w8a8_decode_advance(
+        _p(tokens), _p(pos), _p(argmax_key), _p(next_token), rows, _st()))
