@@ -253,7 +253,7 @@ def main():
     st = torch.cuda.current_stream()
 
     # ---- value: device-resident decode steps (captured step graph)
-    g = dec.capture_decode_step()
+    g = dec.capture_decode_step(start_tok, P - 1)
 
     def rewind():
         dec.pos[0] = P - 1
@@ -275,6 +275,8 @@ def main():
     dt = max_over_ranks(e0.elapsed_time(e1) / 1e3, ws)
     value = ws * args.steps / dt
     final_pos = int(dec.pos[0].item())
+    if ops.error_flags():
+        raise RuntimeError("device error flags set during the decode steps")
 
     # ---- e2e: LlamaDevice.forward with host inputs / outputs
     rewind()

@@ -54,10 +54,16 @@ int w8a8_quant_act(const float* x, int rows, int k, int8_t* xq, float* s_x, void
  * ModelCompiler.rmsnorm (llm/compile_model.py:147-156). */
 int w8a8_rmsnorm(const float* x, const float* g, int rows, int n, float eps, float* y, void* stream);
 
-/* Embedding rows: x[m] = f32(emb_q[tokens[m]]) * emb_s[tokens[m]].
- * Replaces ModelCompiler.embed (llm/compile_model.py:192-201). */
-int w8a8_embed(const int32_t* tokens, int rows, const int8_t* emb_q, const float* emb_s, int dim, float* x,
-               void* stream);
+/* Embedding rows: x[m] = f32(emb_q[tokens[m]]) * emb_s[tokens[m]], emb_q [vocab, dim].
+ * A token outside [0, vocab) gives a zero row and sets bit 0 of the device
+ * error flags. Replaces ModelCompiler.embed (llm/compile_model.py:192-201). */
+int w8a8_embed(const int32_t* tokens, int rows, const int8_t* emb_q, const float* emb_s, int vocab, int dim,
+               float* x, void* stream);
+
+/* Read and clear the current device's error flags (bit 0: an out-of-range
+ * token reached w8a8_embed). Synchronous with the device. Plays the role of the
+ * overlay's sticky list status (llm/sa_funcsim.py:62-66, firmware/rt/rt_fw.c:53-60). */
+int w8a8_error_flags(uint32_t* flags);
 
 /* W8A8 linear on int8 activations: acc = xq . W^T (int32), y = (f32(acc) * s_w) * s_x,
  * or y = resid + that when resid is not NULL (resid may equal y).

@@ -228,3 +228,15 @@ def test_attention_bit_exact(case):
     assert ok, (bad, got.ravel()[bad], want.ravel()[bad])
     ops.attn(args)                                               # again: the scratch counters were reset
     assert same_bits(host(att), want)[0]
+
+
+def test_embed_out_of_range_token_sets_error_flag():
+    """The embedding kernel's bounds check: a token outside the table reads
+    nothing, writes a zero row and raises the device error flag."""
+    rng = np.random.default_rng(12)
+    q, s = quantize_rows(rng.standard_normal((50, 32)).astype(F))
+    assert ops.error_flags() == 0
+    x = host(ops.embed(cu(np.array([3, 50, -1, 7], np.int32)), cu(q), cu(s)))
+    assert not x[1].any() and not x[2].any() and x[0].any() and x[3].any()
+    assert ops.error_flags() == 1
+    assert ops.error_flags() == 0                                # read and cleared

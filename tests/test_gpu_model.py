@@ -89,7 +89,7 @@ def test_prefill_chunks_equal_decode_steps():
     toks = np.random.default_rng(3).integers(0, cfg.vocab, 45)
     a = LlamaDevice((cfg, qw, kv))
     la = a.prefill(toks)
-    b = LlamaDevice(a.dec if False else DeviceDecoder(cfg, qw, kv))
+    b = LlamaDevice((cfg, qw, kv))
     for t in toks:
         lb = b.forward(int(t))
     assert la.tobytes() == lb.tobytes()
@@ -145,3 +145,30 @@ def test_generate_greedy_matches_forward_argmax():
     want = [int(np.argmax(g["b_logits"][p])) for p in range(3, 11)]
     assert out[:3] == prompt[1:4]
     assert out[3:4] == want[:1]
+
+
+def test_device_decode_loop_equals_host_loop():
+    """The captured on-device greedy step (w8a8_decode_advance + forward +
+    fused classifier argmax) feeds the same tokens and leaves the same KV cache
+    as the host loop of forward() + np.argmax."""
+    g, cfg, w = _tiny("b")
+    qw = W.from_fp32(cfg, w)
+    prompt = [int(t) for t in g["tokens"][:5]]
+    a = LlamaDevice((cfg, qw, g["b_kv"]))
+    t0 = int(np.argmax(a.prefill(prompt)))
+    fed, t = [], t0
+    for _ in range(6):
+        fed.append(t)
+        t = int(np.argmax(a.forward(t)))
+    b = DeviceDecoder(cfg, qw, g["b_kv"])
+    LlamaDevice(b).prefill(prompt)
+    step = b.capture_decode_step(t0, len(prompt) - 1)
+    got = []
+    for _ in range(6):
+        step.replay()
+        got.append(int(b.next_token[0].item()))
+    assert got == fed
+    for l in range(cfg.layers):
+        ka, va = a.dec.kv_rows(l, 11)
+        kb, vb = b.kv_rows(l, 11)
+        assert np.array_equal(ka, kb) and np.array_equal(va, vb)

@@ -47,10 +47,18 @@ int w8a8_rmsnorm(const float* x, const float* g, int rows, int n, float eps, flo
     return cuda_status(launch_rmsnorm(x, g, rows, n, eps, inv_of(n), y, S(stream)));
 }
 
-int w8a8_embed(const int32_t* tokens, int rows, const int8_t* emb_q, const float* emb_s, int dim, float* x,
-               void* stream) {
-    if (!tokens || !emb_q || !emb_s || !x || rows <= 0 || dim <= 0) return W8A8_EINVAL;
-    return cuda_status(launch_embed(tokens, rows, emb_q, emb_s, dim, x, S(stream)));
+int w8a8_embed(const int32_t* tokens, int rows, const int8_t* emb_q, const float* emb_s, int vocab, int dim,
+               float* x, void* stream) {
+    if (!tokens || !emb_q || !emb_s || !x || rows <= 0 || dim <= 0 || vocab <= 0) return W8A8_EINVAL;
+    return cuda_status(launch_embed(tokens, rows, emb_q, emb_s, vocab, dim, x, S(stream)));
+}
+
+int w8a8_error_flags(uint32_t* flags) {
+    if (!flags) return W8A8_EINVAL;
+    unsigned int v = 0;
+    int st = cuda_status(read_clear_errors(&v));
+    *flags = v;
+    return st;
 }
 
 static int check_linear(int rows, int k, const void* w, const float* s_w, int n, const void* y) {

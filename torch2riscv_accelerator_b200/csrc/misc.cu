@@ -6,19 +6,37 @@
 
 namespace w8a8 {
 
-// x = f32(q[tok]) * s[tok]  (llm/ref_model.py:221, hf_generic.QEmbedding :698-706)
-__global__ void embed_kernel(const int32_t* tokens, const int8_t* emb_q, const float* emb_s, int dim, float* x) {
+// Device error word of this library (bit 0: a token outside [0, vocab) reached
+// the embedding kernel). Read and cleared by w8a8_error_flags().
+__device__ unsigned int g_w8a8_errors;
+
+// x = f32(q[tok]) * s[tok]  (llm/ref_model.py:221, hf_generic.QEmbedding :698-706);
+// a token outside the table reads nothing: its row is zero and the error bit is set.
+__global__ void embed_kernel(const int32_t* tokens, const int8_t* emb_q, const float* emb_s, int vocab, int dim,
+                             float* x) {
     const int m = blockIdx.x;
     const int tok = tokens[m];
+    if (tok < 0 || tok >= vocab) {
+        for (int i = threadIdx.x; i < dim; i += blockDim.x) x[(size_t)m * dim + i] = 0.f;
+        if (threadIdx.x == 0) atomicOr(&g_w8a8_errors, 1u);
+        return;
+    }
     const float s = emb_s[tok];
     const int8_t* q = emb_q + (size_t)tok * dim;
     for (int i = threadIdx.x; i < dim; i += blockDim.x) x[(size_t)m * dim + i] = fmul(i2f(q[i]), s);
 }
 
-cudaError_t launch_embed(const int32_t* tokens, int m, const int8_t* emb_q, const float* emb_s, int dim,
+cudaError_t launch_embed(const int32_t* tokens, int m, const int8_t* emb_q, const float* emb_s, int vocab, int dim,
                          float* x, cudaStream_t st) {
-    embed_kernel<<<m, 256, 0, st>>>(tokens, emb_q, emb_s, dim, x);
+    embed_kernel<<<m, 256, 0, st>>>(tokens, emb_q, emb_s, vocab, dim, x);
     return cudaGetLastError();
+}
+
+cudaError_t read_clear_errors(unsigned int* out) {
+    cudaError_t e = cudaMemcpyFromSymbol(out, g_w8a8_errors, sizeof(unsigned int));
+    if (e != cudaSuccess) return e;
+    const unsigned int zero = 0;
+    return cudaMemcpyToSymbol(g_w8a8_errors, &zero, sizeof(unsigned int));
 }
 
 // RMSNorm rows (llm/ref_model.py:204-207): ss = red_sum16(x*x),

@@ -65,8 +65,9 @@ size_t attn_scratch_bytes(int rows, int heads, int kv_heads, int head_dim, int s
 void attn_carve(AttnParams& p, void* scratch);
 cudaError_t launch_attn(const AttnParams& p, cudaStream_t st);
 
-cudaError_t launch_embed(const int32_t* tokens, int m, const int8_t* emb_q, const float* emb_s, int dim,
+cudaError_t launch_embed(const int32_t* tokens, int m, const int8_t* emb_q, const float* emb_s, int vocab, int dim,
                          float* x, cudaStream_t st);
+cudaError_t read_clear_errors(unsigned int* out);
 cudaError_t launch_argmax(const float* logits, int m, int n, int32_t* out, cudaStream_t st);
 cudaError_t launch_sfu(int func, const float* x, float* y, long long n, cudaStream_t st);
 cudaError_t launch_rmsnorm(const float* x, const float* g, int m, int n, float eps, float inv_n, float* y,

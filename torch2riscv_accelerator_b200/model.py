@@ -122,8 +122,11 @@ class DeviceDecoder:
         ops.decode_advance(self.tokens, self.pos, self.key, 1, next_token=self.next_token)
         self.run(1, argmax=True)
 
-    def capture_decode_step(self):
-        """decode_step() as a CUDA graph (the warm-up's state change is undone)."""
+    def capture_decode_step(self, seed_token, seed_pos):
+        """decode_step() as a CUDA graph. The warm-up step runs from
+        (seed_token, seed_pos + 1); its state change is undone afterwards."""
+        self.set_next_token(seed_token)
+        self.pos[0] = seed_pos
         saved = self.tokens.clone(), self.pos.clone(), self.key.clone()
         s = torch.cuda.Stream(device=self.dev)
         s.wait_stream(torch.cuda.current_stream(self.dev))
@@ -140,6 +143,8 @@ class DeviceDecoder:
 
     def set_next_token(self, token):
         """Seed the on-device decode loop: the next decode_step() feeds `token`."""
+        if not 0 <= int(token) < self.cfg.vocab:
+            raise ValueError(f"token {token} outside the vocabulary")
         self.key[0] = 0xFFFFFFFF - int(token)
 
     def launch(self, rows, logits_rows=1, graph=True):

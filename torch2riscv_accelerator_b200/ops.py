@@ -55,10 +55,19 @@ def rmsnorm(x, g, eps):
 
 
 def embed(tokens, emb_q, emb_s, out=None):
-    m, dim = tokens.numel(), emb_q.shape[1]
+    m, (vocab, dim) = tokens.numel(), emb_q.shape
     out = torch.empty(m, dim, dtype=F32, device=emb_q.device) if out is None else out
-    _lib.check("w8a8_embed", _lib.load().w8a8_embed(_p(tokens), m, _p(emb_q), _p(emb_s), dim, _p(out), _st()))
+    _lib.check("w8a8_embed", _lib.load().w8a8_embed(_p(tokens), m, _p(emb_q), _p(emb_s), vocab, dim, _p(out),
+                                                   _st()))
     return out
+
+
+def error_flags():
+    """Read and clear the device error flags (bit 0: an out-of-range token)."""
+    import ctypes
+    v = ctypes.c_uint32(0)
+    _lib.check("w8a8_error_flags", _lib.load().w8a8_error_flags(ctypes.byref(v)))
+    return v.value
 
 
 def linear(xq, s_x, w, s_w, out=None, acc=None, resid=None):

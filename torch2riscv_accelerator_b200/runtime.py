@@ -84,6 +84,8 @@ class LlamaDevice:
         stays untouched until the stream has consumed it (default: the
         single-token buffer, safe because forward() synchronizes)."""
         m = len(tokens)
+        if min(tokens) < 0 or max(tokens) >= self.cfg.vocab:
+            raise ValueError(f"token outside [0, {self.cfg.vocab})")
         buf = self._in if staging is None else staging
         buf[:m] = torch.as_tensor(tokens, dtype=torch.int32)
         buf[CHUNK:CHUNK + m] = torch.as_tensor(positions, dtype=torch.int32)
