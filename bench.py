@@ -222,6 +222,7 @@ def main():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-steps", type=int, default=2)
+    ap.add_argument("--pdl", type=int, default=1, help="programmatic dependent launch between kernels (1) or not (0)")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
@@ -241,6 +242,8 @@ def main():
     from torch2riscv_accelerator_b200.model import DeviceDecoder
     from torch2riscv_accelerator_b200.runtime import LlamaDevice
     torch.cuda.set_device(local)
+    from torch2riscv_accelerator_b200 import _lib
+    _lib.load().w8a8_set_pdl(args.pdl)
     qw = build_model(cfg, args.seed)
     dec = DeviceDecoder(cfg, qw, qw.kv_scales)
     dev = LlamaDevice(dec)
@@ -346,7 +349,7 @@ def main():
             "gpu_launches": args.steps * (1 + dec.kernel_launches(1)),
             "clocks": clk.summary(),
             "prefill": {"tokens": P, "seconds": prefill_s, "tok_s": P / prefill_s},
-            "final_pos": final_pos,
+            "final_pos": final_pos, "pdl": bool(args.pdl),
         }
         print(json.dumps(line), flush=True)
     barrier(ws)

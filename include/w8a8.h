@@ -61,9 +61,17 @@ int w8a8_embed(const int32_t* tokens, int rows, const int8_t* emb_q, const float
                float* x, void* stream);
 
 /* Read and clear the current device's error flags (bit 0: an out-of-range
- * token reached w8a8_embed). Synchronous with the device. Plays the role of the
- * overlay's sticky list status (llm/sa_funcsim.py:62-66, firmware/rt/rt_fw.c:53-60). */
+ * token reached w8a8_embed; bit 1: a GEMV weight-tile wait gave up after its
+ * bounded spin and the kernel stopped early). Synchronous with the device.
+ * Plays the role of the overlay's sticky list status (llm/sa_funcsim.py:62-66,
+ * firmware/rt/rt_fw.c:53-60). */
 int w8a8_error_flags(uint32_t* flags);
+
+/* Launch the kernels with programmatic dependent launch (1, the default) or
+ * with plain stream ordering (0); returns the previous setting. Results are
+ * identical either way; with it a kernel starts streaming its weights while
+ * its predecessor finishes. Process-wide; not for concurrent callers. */
+int w8a8_set_pdl(int enable);
 
 /* W8A8 linear on int8 activations: acc = xq . W^T (int32), y = (f32(acc) * s_w) * s_x,
  * or y = resid + that when resid is not NULL (resid may equal y).

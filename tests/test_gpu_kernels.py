@@ -240,3 +240,26 @@ def test_embed_out_of_range_token_sets_error_flag():
     assert not x[1].any() and not x[2].any() and x[0].any() and x[3].any()
     assert ops.error_flags() == 1
     assert ops.error_flags() == 0                                # read and cleared
+
+
+@pytest.mark.parametrize("m", [1, 4])
+def test_classifier_fused_argmax(m):
+    """Final rmsnorm + quant + classifier with the greedy argmax in the epilogue:
+    logits bit-exact, the packed key's index = np.argmax (first maximum on ties)."""
+    rng = np.random.default_rng(m)
+    n, k = 32000, 288
+    w, sw = quantize_rows((rng.standard_normal((n, k)) * 0.02).astype(F))
+    w[7777] = w[123]                                            # a tie: the lower index must win
+    sw[7777] = sw[123]
+    w[123] *= 0
+    w[123] += 127
+    w[7777] = w[123]
+    x = rng.standard_normal((m, k)).astype(F)
+    x[:, :] = np.abs(x)
+    g = (1 + 0.1 * rng.standard_normal(k)).astype(F)
+    key = torch.zeros(m, dtype=torch.int64, device=DEV)
+    y = host(ops.classifier(cu(x), cu(w), cu(sw), cu(g), 1e-5, argmax_key=key))
+    xq, s = N.quant_act(N.rmsnorm(x, g, 1e-5))
+    want = N.linear(xq, s, w, sw)[0]
+    assert same_bits(y, want)[0]
+    assert [ops.key_token(v) for v in host(key)] == [int(np.argmax(r)) for r in want]

@@ -172,3 +172,26 @@ def test_device_decode_loop_equals_host_loop():
         ka, va = a.dec.kv_rows(l, 11)
         kb, vb = b.kv_rows(l, 11)
         assert np.array_equal(ka, kb) and np.array_equal(va, vb)
+
+
+def test_pdl_on_and_off_give_identical_results():
+    """Programmatic dependent launch only changes when kernels start: the logits
+    and cache of a prefill + decode run are the same bytes with and without it."""
+    from torch2riscv_accelerator_b200 import _lib
+    cfg = C.C2.with_(layers=2, vocab=2048, seq_len=256)
+    qw = W.QuantWeights(cfg, seed=4, gains="random")
+    kv = np.array([[0.04, 0.03], [0.05, 0.02]], F)
+    toks = np.random.default_rng(6).integers(0, cfg.vocab, 40)
+    out = []
+    lib = _lib.load()
+    old = lib.w8a8_set_pdl(1)
+    try:
+        for pdl in (1, 0):
+            lib.w8a8_set_pdl(pdl)
+            d = LlamaDevice((cfg, qw, kv))
+            lg = [d.prefill(toks[:33])] + [d.forward(int(t)) for t in toks[33:]]
+            out.append((np.stack(lg), d.dec.kv_rows(1, 40)))
+    finally:
+        lib.w8a8_set_pdl(old)
+    assert out[0][0].tobytes() == out[1][0].tobytes()
+    assert np.array_equal(out[0][1][0], out[1][1][0]) and np.array_equal(out[0][1][1], out[1][1][1])

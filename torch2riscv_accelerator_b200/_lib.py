@@ -31,6 +31,7 @@ PROTOTYPES = {
     "w8a8_rmsnorm": (I, [P, P, I, I, F, P, P]),
     "w8a8_embed": (I, [P, I, P, P, I, I, P, P]),
     "w8a8_error_flags": (I, [C.POINTER(C.c_uint32)]),
+    "w8a8_set_pdl": (I, [I]),
     "w8a8_linear": (I, [P, P, I, I, P, P, I, P, P, P, P]),
     "w8a8_linear_fused": (I, [P, P, F, I, I, P, P, I, P, P, P, P]),
     "w8a8_ffn_scratch_bytes": (Z, [I]),

@@ -25,6 +25,7 @@
 // Cache layout: [kv_heads, seq_len, head_dim] int8 per layer.
 #include "w8a8_internal.h"
 #include "w8a8_math.cuh"
+#include "pdl.cuh"
 
 namespace w8a8 {
 
@@ -108,7 +109,11 @@ __global__ void __launch_bounds__(kScoreThreads) attn_scores(AttnParams p) {
     int maxpos = 0;
     for (int m = 0; m < M; ++m) maxpos = max(maxpos, p.pos[m]);
     const int nvalid = min(kChunk, maxpos + 1 - t0);
-    if (nvalid <= 0) return;                                   // beyond every row: nothing to do
+    if (nvalid <= 0) {                                         // beyond every row: nothing to do
+        pdl_wait();
+        pdl_trigger();
+        return;
+    }
     // the chunk of K already in the cache
     const int vpr = hd / 16;
     const int8_t* kbase = p.kc + ((size_t)kvh * T + t0) * hd;
@@ -116,6 +121,10 @@ __global__ void __launch_bounds__(kScoreThreads) attn_scores(AttnParams p) {
         const int t = i / vpr, c = i % vpr;
         *reinterpret_cast<int4*>(ks + t * kstride + c * 16) = __ldg(reinterpret_cast<const int4*>(kbase) + i);
     }
+    // the rows above come from earlier steps (positions below this call's
+    // rows, whose own K rows are made below): loaded before the wait
+    pdl_wait();
+    pdl_trigger();
     __syncthreads();
     float* buf = fbuf + warp * hd;
     // q path of every row and query head of this KV head
@@ -199,6 +208,8 @@ __global__ void __launch_bounds__(kPvThreads) attn_pv(AttnParams p) {
     __shared__ int redi[32];
     __shared__ float rsum;
     __shared__ int last;
+    pdl_wait();
+    pdl_trigger();
     int maxpos = 0;
     for (int m = 0; m < M; ++m) maxpos = max(maxpos, p.pos[m]);
     const int nvalid = min(kChunk, maxpos + 1 - t0);
@@ -288,18 +299,18 @@ cudaError_t launch_attn(const AttnParams& p, cudaStream_t st) {
     const size_t qbytes = ((size_t)p.rows * G * p.head_dim + 15) & ~size_t(15);
     const size_t smem_s = (size_t)kChunk * (p.head_dim + 16) + qbytes + (size_t)kScoreWarps * p.head_dim * 4;
     if (smem_s > 32 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(attn_scores, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_s);
-        if (e != cudaSuccess) return e;
+        cudaError_t e0 = cudaFuncSetAttribute(attn_scores, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_s);
+        if (e0 != cudaSuccess) return e0;
     }
-    attn_scores<<<dim3(p.kv_heads, p.nsplit), kScoreThreads, smem_s, st>>>(p);
+    cudaError_t e = launch_k(attn_scores, dim3(p.kv_heads, p.nsplit), dim3(kScoreThreads), smem_s, st, p);
+    if (e != cudaSuccess) return e;
     size_t smem_v = (size_t)kChunk * p.head_dim + (size_t)p.rows * G * kChunk;
     if (p.variant == 0) smem_v = ((smem_v + 15) & ~size_t(15)) + (size_t)p.seq_len * 4;
     if (smem_v > 32 * 1024) {
-        cudaError_t e = cudaFuncSetAttribute(attn_pv, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_v);
+        e = cudaFuncSetAttribute(attn_pv, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem_v);
         if (e != cudaSuccess) return e;
     }
-    attn_pv<<<dim3(p.kv_heads, p.nsplit), kPvThreads, smem_v, st>>>(p);
-    return cudaGetLastError();
+    return launch_k(attn_pv, dim3(p.kv_heads, p.nsplit), dim3(kPvThreads), smem_v, st, p);
 }
 
 }  // namespace w8a8

@@ -7,6 +7,10 @@
 
 using namespace w8a8;
 
+namespace w8a8 {
+int g_use_pdl = 1;
+}
+
 namespace {
 
 inline cudaStream_t S(void* s) { return static_cast<cudaStream_t>(s); }
@@ -57,8 +61,14 @@ int w8a8_error_flags(uint32_t* flags) {
     if (!flags) return W8A8_EINVAL;
     unsigned int v = 0;
     int st = cuda_status(read_clear_errors(&v));
-    *flags = v;
+    *flags = v | gemv_read_clear_errors();
     return st;
+}
+
+int w8a8_set_pdl(int enable) {
+    const int old = g_use_pdl;
+    g_use_pdl = enable ? 1 : 0;
+    return old;
 }
 
 static int check_linear(int rows, int k, const void* w, const float* s_w, int n, const void* y) {

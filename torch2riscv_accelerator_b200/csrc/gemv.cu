@@ -1,0 +1,269 @@
+// W8A8 GEMV for decode rows (M <= 4): a persistent grid (one CTA per SM) that
+// streams the weight matrix through shared memory with 1-D bulk copies
+// (cp.async.bulk, completion on mbarriers), several tiles in flight per CTA.
+//
+// Weight tiles are independent of every earlier kernel, so each CTA issues its
+// first tiles before griddepcontrol.wait: under programmatic dependent launch
+// the weight stream of this layer overlaps the tail of the previous kernel.
+// After the wait come the activation prologue (the same fused rmsnorm /
+// quant_act as linear.cu) and the dot products from shared memory: a warp owns
+// one tile row (or a K-slice of it for long rows), lanes read consecutive
+// 16-byte chunks (no bank conflicts), dp4a per 4 bytes, shuffles sum the int32
+// partials (exact in any order). Epilogues as linear.cu: dequant
+// (f32(acc)*s_w)*s_x, + residual, SwiGLU with the row amax and the last CTA's
+// int8 requant, or the classifier's fused greedy argmax.
+// Reference semantics: llm/ref_model.py:191-202 (quant_act, linear),
+// llm/sa_funcsim.py:138-162 (the GEMV command), llm/compile_model.py:295-328
+// (ffn_up with fused SiLU).
+#include "linear_common.cuh"
+#include "pdl.cuh"
+
+namespace w8a8 {
+
+__device__ unsigned int g_gemv_errors;                        // bit 1: a tile wait gave up
+
+constexpr int kMaxStages = 8;
+constexpr size_t kRingBytes = 64 * 1024;                      // weight ring per CTA
+
+template <int MR, int EPI>
+__device__ __forceinline__ void epilogue_row(const LinearParams& p, int n, const int* acc, const int* acc2,
+                                             const float* sx, uint32_t* bamax, unsigned long long* bkey) {
+#pragma unroll
+    for (int m = 0; m < MR; ++m) {
+        if (m >= p.m) continue;
+        const size_t o = (size_t)m * p.n + n;
+        const float v = fmul(fmul(i2f(acc[m]), __ldg(p.s_w + n)), sx[m]);
+        if (EPI == EPI_STORE) {
+            p.y[o] = v;
+            if (p.acc != nullptr) p.acc[o] = acc[m];
+            if (p.argmax_key != nullptr) atomicMax(&bkey[m], argmax_key(v, n));
+        } else if (EPI == EPI_RESID) {
+            p.y[o] = fadd(p.resid[o], v);
+        } else {
+            const float u = fmul(fmul(i2f(acc2[m]), __ldg(p.s_w2 + n)), sx[m]);
+            const float h = silu_gate(v, u);
+            p.y[o] = h;
+            atomicMax(&bamax[m], __float_as_uint(fabsf(h)));
+        }
+    }
+}
+
+template <int MR, int PRO, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemv_kernel(LinearParams p, int tr, int slices, int stages, int ntiles) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    constexpr bool kTwo = EPI == EPI_SWIGLU;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int k = p.k, nch = k / 16;
+    const size_t tile_bytes = (size_t)tr * k;
+    const size_t stage_bytes = tile_bytes * (kTwo ? 2 : 1);
+    unsigned char* ring = smem;
+    int8_t* xs = reinterpret_cast<int8_t*>(smem + stages * stage_bytes);   // [MR][k]
+    float* xf = reinterpret_cast<float*>(xs + (size_t)MR * k);            // [k]
+    __shared__ __align__(8) uint64_t full[kMaxStages];
+    __shared__ float sx[MR];
+    __shared__ float red[32];
+    __shared__ uint32_t bamax[MR];
+    __shared__ unsigned long long bkey[MR];
+    __shared__ int spart[kWarps][2 * MR];
+    __shared__ int last;
+    const int my = (ntiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;   // tiles of this CTA
+    if (tid < MR) {
+        bamax[tid] = 0u;
+        bkey[tid] = 0ull;
+    }
+    if (tid == 0) {
+        for (int s = 0; s < stages; ++s) mbar_init(&full[s], 1);
+        mbar_fence_init();
+    }
+    __syncthreads();
+    auto issue = [&](int i) {                                  // thread 0: tile i of this CTA -> stage i % stages
+        const int s = i % stages;
+        const int row0 = ((int)blockIdx.x + i * (int)gridDim.x) * tr;
+        const uint32_t bytes = (uint32_t)(min(tr, p.n - row0) * k);
+        mbar_expect_tx(&full[s], bytes * (kTwo ? 2u : 1u));
+        bulk_g2s(ring + s * stage_bytes, p.w + (size_t)row0 * k, bytes, &full[s]);
+        if (kTwo) bulk_g2s(ring + s * stage_bytes + tile_bytes, p.w2 + (size_t)row0 * k, bytes, &full[s]);
+    };
+    if (tid == 0)
+        for (int i = 0; i < min(stages, my); ++i) issue(i);    // weights: before the wait
+    pdl_wait();
+    pdl_trigger();
+    prologue<MR, PRO>(p, xs, xf, sx, red);
+
+    const int rows_per_pass = kWarps / slices;                 // rows computed together (slices warps per row)
+    const int row_in = warp % rows_per_pass, sl = warp / rows_per_pass;
+    const int c_lo = sl * nch / slices, c_hi = (sl + 1) * nch / slices;
+    int i = 0;
+    for (; i < my; ++i) {
+        const int s = i % stages;
+        const bool ok = mbar_wait(&full[s], (uint32_t)((i / stages) & 1));
+        if (__syncthreads_or(!ok)) break;
+        const int row0 = ((int)blockIdx.x + i * (int)gridDim.x) * tr;
+        const int rows = min(tr, p.n - row0);
+        const int8_t* wt = reinterpret_cast<const int8_t*>(ring + s * stage_bytes);
+        for (int rb = 0; rb < tr; rb += rows_per_pass) {
+            const int r = rb + row_in;
+            int acc[MR], acc2[MR];
+#pragma unroll
+            for (int m = 0; m < MR; ++m) acc[m] = acc2[m] = 0;
+            if (r < rows) {
+                const int8_t* wr = wt + (size_t)r * k;
+                const int8_t* wr2 = wr + tile_bytes;
+#pragma unroll 4
+                for (int c = c_lo + lane; c < c_hi; c += 32) {
+                    const int4 w4 = *reinterpret_cast<const int4*>(wr + c * 16);
+                    int4 u4;
+                    if (kTwo) u4 = *reinterpret_cast<const int4*>(wr2 + c * 16);
+#pragma unroll
+                    for (int m = 0; m < MR; ++m) {
+                        const int4 x4 = *reinterpret_cast<const int4*>(xs + (size_t)m * k + c * 16);
+                        acc[m] = dp4a(w4.x, x4.x, dp4a(w4.y, x4.y, dp4a(w4.z, x4.z, dp4a(w4.w, x4.w, acc[m]))));
+                        if (kTwo)
+                            acc2[m] = dp4a(u4.x, x4.x, dp4a(u4.y, x4.y, dp4a(u4.z, x4.z, dp4a(u4.w, x4.w, acc2[m]))));
+                    }
+                }
+            }
+#pragma unroll
+            for (int m = 0; m < MR; ++m) {
+                acc[m] = warp_sum_i(acc[m]);
+                if (kTwo) acc2[m] = warp_sum_i(acc2[m]);
+            }
+            if (slices == 1) {
+                if (lane == 0 && r < rows) epilogue_row<MR, EPI>(p, row0 + r, acc, acc2, sx, bamax, bkey);
+            } else {
+                if (lane == 0) {
+#pragma unroll
+                    for (int m = 0; m < MR; ++m) {
+                        spart[warp][m] = acc[m];
+                        spart[warp][MR + m] = acc2[m];
+                    }
+                }
+                __syncthreads();
+                if (sl == 0 && lane == 0 && r < rows) {
+                    int a[MR], a2[MR];
+#pragma unroll
+                    for (int m = 0; m < MR; ++m) {
+                        a[m] = a2[m] = 0;
+                        for (int q = 0; q < slices; ++q) {
+                            a[m] += spart[q * rows_per_pass + row_in][m];
+                            a2[m] += spart[q * rows_per_pass + row_in][MR + m];
+                        }
+                    }
+                    epilogue_row<MR, EPI>(p, row0 + r, a, a2, sx, bamax, bkey);
+                }
+                __syncthreads();
+            }
+        }
+        __syncthreads();                                       // stage s consumed
+        if (tid == 0 && i + stages < my) issue(i + stages);
+    }
+    if (i < my) {                                              // a wait gave up: record, drain, stop
+        if (tid == 0) {
+            atomicOr(&g_gemv_errors, 2u);
+            for (int j = i; j < min(i + stages, my); ++j) mbar_wait(&full[j % stages], (uint32_t)((j / stages) & 1));
+        }
+        __syncthreads();
+        return;
+    }
+    if (EPI == EPI_STORE && p.argmax_key != nullptr) {
+        __syncthreads();
+        if (tid < p.m && tid < MR) atomicMax(p.argmax_key + tid, bkey[tid]);
+    }
+    if (EPI != EPI_SWIGLU) return;
+    // the row amax across the grid; the last CTA requantizes h (quant_act)
+    __syncthreads();
+    if (tid < p.m && tid < MR) atomicMax(p.amax_bits + tid, bamax[tid]);
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) last = atomicAdd(p.counter, 1u) == gridDim.x - 1;
+    __syncthreads();
+    if (!last) return;
+    __threadfence();
+    for (int m = 0; m < p.m; ++m) {
+        const float amax = __uint_as_float(__ldcg(p.amax_bits + m));
+        const float s = fmul(amax, W8A8_C127);
+        const float inv = sfu_recip(s);
+        const float* hr = p.y + (size_t)m * p.n;
+        int8_t* qr = p.hq + (size_t)m * p.n;
+        for (int j = tid; j < p.n; j += kThreads) qr[j] = (int8_t)to_i8(fmul(__ldcg(hr + j), inv));
+        if (tid == 0) p.s_h[m] = s;
+    }
+    __syncthreads();
+    if (tid < p.m) p.amax_bits[tid] = 0u;
+    if (tid == 0) *p.counter = 0u;
+}
+
+static int sm_count() {
+    static int cached[64] = {0};
+    int d = 0;
+    cudaGetDevice(&d);
+    if (d < 0 || d >= 64) d = 0;
+    if (cached[d] == 0) cudaDeviceGetAttribute(&cached[d], cudaDevAttrMultiProcessorCount, d);
+    return cached[d] > 0 ? cached[d] : 148;
+}
+
+struct Tiling {
+    int tr, slices, stages, ntiles, grid;
+    size_t smem;
+};
+
+// tile rows: about 16 KB per matrix (power of two, at most 64 rows); warps
+// split a row's K when a tile has fewer than 8 rows; a 64 KB ring of stages.
+static Tiling tiling(const LinearParams& p, int mr, int pro, int epi) {
+    Tiling t{};
+    int tr = 16384 / p.k;
+    tr = tr < 1 ? 1 : (tr > 64 ? 64 : tr);
+    int pw = 1;
+    while (pw * 2 <= tr) pw *= 2;
+    t.tr = pw;
+    t.slices = t.tr >= kWarps ? 1 : kWarps / t.tr;
+    const size_t stage = (size_t)t.tr * p.k * (epi == EPI_SWIGLU ? 2 : 1);
+    size_t st = kRingBytes / stage;
+    t.stages = (int)(st < 2 ? 2 : (st > (size_t)kMaxStages ? kMaxStages : st));
+    t.ntiles = (p.n + t.tr - 1) / t.tr;
+    t.grid = t.ntiles < sm_count() ? t.ntiles : sm_count();
+    t.smem = (size_t)t.stages * stage + (size_t)mr * p.k + (pro == PRO_I8 ? 0 : (size_t)p.k * 4);
+    return t;
+}
+
+template <int MR, int PRO, int EPI>
+static cudaError_t launch_g(const LinearParams& p, cudaStream_t st) {
+    const Tiling t = tiling(p, MR, PRO, EPI);
+    auto kern = gemv_kernel<MR, PRO, EPI>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)t.smem);
+    if (e != cudaSuccess) return e;
+    return launch_k(kern, dim3(t.grid), dim3(kThreads), t.smem, st, p, t.tr, t.slices, t.stages, t.ntiles);
+}
+
+template <int PRO, int EPI>
+static cudaError_t launch_gm(const LinearParams& p, cudaStream_t st) {
+    if (p.m <= 1) return launch_g<1, PRO, EPI>(p, st);
+    if (p.m <= 2) return launch_g<2, PRO, EPI>(p, st);
+    return launch_g<4, PRO, EPI>(p, st);
+}
+
+bool gemv_fits(const LinearParams& p, int pro, int epi) {
+    if (p.m > 4) return false;
+    const int mr = p.m <= 1 ? 1 : (p.m <= 2 ? 2 : 4);
+    return tiling(p, mr, pro, epi).smem <= 200 * 1024;
+}
+
+cudaError_t launch_gemv(const LinearParams& p, int pro, int epi, cudaStream_t st) {
+    if (pro == PRO_I8 && epi == EPI_STORE) return launch_gm<PRO_I8, EPI_STORE>(p, st);
+    if (pro == PRO_I8 && epi == EPI_RESID) return launch_gm<PRO_I8, EPI_RESID>(p, st);
+    if (pro == PRO_QUANT && epi == EPI_STORE) return launch_gm<PRO_QUANT, EPI_STORE>(p, st);
+    if (pro == PRO_QUANT && epi == EPI_RESID) return launch_gm<PRO_QUANT, EPI_RESID>(p, st);
+    if (pro == PRO_RMSQ && epi == EPI_STORE) return launch_gm<PRO_RMSQ, EPI_STORE>(p, st);
+    if (pro == PRO_RMSQ && epi == EPI_SWIGLU) return launch_gm<PRO_RMSQ, EPI_SWIGLU>(p, st);
+    return cudaErrorInvalidValue;
+}
+
+unsigned int gemv_read_clear_errors() {
+    unsigned int v = 0, zero = 0;
+    cudaMemcpyFromSymbol(&v, g_gemv_errors, sizeof(v));
+    cudaMemcpyToSymbol(g_gemv_errors, &zero, sizeof(zero));
+    return v;
+}
+
+}  // namespace w8a8

@@ -3,6 +3,7 @@
 // for testing).
 #include "w8a8_internal.h"
 #include "w8a8_math.cuh"
+#include "pdl.cuh"
 
 namespace w8a8 {
 
@@ -14,6 +15,8 @@ __device__ unsigned int g_w8a8_errors;
 // a token outside the table reads nothing: its row is zero and the error bit is set.
 __global__ void embed_kernel(const int32_t* tokens, const int8_t* emb_q, const float* emb_s, int vocab, int dim,
                              float* x) {
+    pdl_wait();
+    pdl_trigger();
     const int m = blockIdx.x;
     const int tok = tokens[m];
     if (tok < 0 || tok >= vocab) {
@@ -28,8 +31,7 @@ __global__ void embed_kernel(const int32_t* tokens, const int8_t* emb_q, const f
 
 cudaError_t launch_embed(const int32_t* tokens, int m, const int8_t* emb_q, const float* emb_s, int vocab, int dim,
                          float* x, cudaStream_t st) {
-    embed_kernel<<<m, 256, 0, st>>>(tokens, emb_q, emb_s, vocab, dim, x);
-    return cudaGetLastError();
+    return launch_k(embed_kernel, dim3(m), dim3(256), 0, st, tokens, emb_q, emb_s, vocab, dim, x);
 }
 
 cudaError_t read_clear_errors(unsigned int* out) {
@@ -42,6 +44,8 @@ cudaError_t read_clear_errors(unsigned int* out) {
 // RMSNorm rows (llm/ref_model.py:204-207): ss = red_sum16(x*x),
 // r = RSQRT(ss*F(1/n) + eps), y = (x*r)*g
 __global__ void rmsnorm_kernel(const float* x, const float* g, int n, float eps, float inv_n, float* y) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ float r;
     const int m = blockIdx.x, tid = threadIdx.x;
     const float* xr = x + (size_t)m * n;
@@ -55,12 +59,13 @@ __global__ void rmsnorm_kernel(const float* x, const float* g, int n, float eps,
 
 cudaError_t launch_rmsnorm(const float* x, const float* g, int m, int n, float eps, float inv_n, float* y,
                            cudaStream_t st) {
-    rmsnorm_kernel<<<m, 256, 0, st>>>(x, g, n, eps, inv_n, y);
-    return cudaGetLastError();
+    return launch_k(rmsnorm_kernel, dim3(m), dim3(256), 0, st, x, g, n, eps, inv_n, y);
 }
 
 // quant_act rows (llm/ref_model.py:191-196)
 __global__ void quant_act_kernel(const float* x, int k, int8_t* xq, float* s_x) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ float red[32];
     const int m = blockIdx.x, tid = threadIdx.x;
     const float* xr = x + (size_t)m * k;
@@ -74,8 +79,7 @@ __global__ void quant_act_kernel(const float* x, int k, int8_t* xq, float* s_x) 
 }
 
 cudaError_t launch_quant_act(const float* x, int m, int k, int8_t* xq, float* s_x, cudaStream_t st) {
-    quant_act_kernel<<<m, 256, 0, st>>>(x, k, xq, s_x);
-    return cudaGetLastError();
+    return launch_k(quant_act_kernel, dim3(m), dim3(256), 0, st, x, k, xq, s_x);
 }
 
 // Greedy sampling (llm/runtime.py:55-57, np.argmax: the first maximum; a NaN
@@ -97,6 +101,8 @@ __device__ __forceinline__ ArgMax better(ArgMax a, ArgMax b) {
 }
 
 __global__ void argmax_kernel(const float* logits, int n, int32_t* out) {
+    pdl_wait();
+    pdl_trigger();
     __shared__ ArgMax red[32];
     const int m = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const float* row = logits + (size_t)m * n;
@@ -119,12 +125,13 @@ __global__ void argmax_kernel(const float* logits, int n, int32_t* out) {
 }
 
 cudaError_t launch_argmax(const float* logits, int m, int n, int32_t* out, cudaStream_t st) {
-    argmax_kernel<<<m, 1024, 0, st>>>(logits, n, out);
-    return cudaGetLastError();
+    return launch_k(argmax_kernel, dim3(m), dim3(1024), 0, st, logits, n, out);
 }
 
 // func: 0 EXP, 1 RECIP, 2 RSQRT, 3 SiLU gate g*sigma(g) (u = 1)
 __global__ void sfu_kernel(int func, const float* x, float* y, long long n) {
+    pdl_wait();
+    pdl_trigger();
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
         const float v = x[i];
         y[i] = func == 0 ? sfu_exp(v) : func == 1 ? sfu_recip(v) : func == 2 ? sfu_rsqrt(v) : silu_gate(v, 1.f);
@@ -135,8 +142,7 @@ cudaError_t launch_sfu(int func, const float* x, float* y, long long n, cudaStre
     long long blocks = (n + 255) / 256;
     if (blocks > 148 * 16) blocks = 148 * 16;
     if (blocks < 1) blocks = 1;
-    sfu_kernel<<<(int)blocks, 256, 0, st>>>(func, x, y, n);
-    return cudaGetLastError();
+    return launch_k(sfu_kernel, dim3((int)blocks), dim3(256), 0, st, func, x, y, n);
 }
 
 // The on-device decode loop's step: the previous step's greedy token (the
@@ -145,6 +151,8 @@ cudaError_t launch_sfu(int func, const float* x, float* y, long long n, cudaStre
 // (llm/runtime.py:127-148 on the host).
 __global__ void decode_advance_kernel(int32_t* tokens, int32_t* pos, unsigned long long* key, int32_t* next,
                                       int rows) {
+    pdl_wait();
+    pdl_trigger();
     const int m = threadIdx.x;
     if (m < rows) {
         const int t = (int)(0xFFFFFFFFu - (uint32_t)(key[m] & 0xFFFFFFFFull));
@@ -157,8 +165,7 @@ __global__ void decode_advance_kernel(int32_t* tokens, int32_t* pos, unsigned lo
 
 cudaError_t launch_decode_advance(int32_t* tokens, int32_t* pos, unsigned long long* key, int32_t* next, int rows,
                                   cudaStream_t st) {
-    decode_advance_kernel<<<1, 32, 0, st>>>(tokens, pos, key, next, rows);
-    return cudaGetLastError();
+    return launch_k(decode_advance_kernel, dim3(1), dim3(32), 0, st, tokens, pos, key, next, rows);
 }
 
 }  // namespace w8a8

@@ -32,6 +32,9 @@ struct LinearParams {
 };
 
 cudaError_t launch_linear(const LinearParams& p, int pro, int epi, cudaStream_t st);
+bool gemv_fits(const LinearParams& p, int pro, int epi);
+cudaError_t launch_gemv(const LinearParams& p, int pro, int epi, cudaStream_t st);
+unsigned int gemv_read_clear_errors();
 
 struct AttnParams {
     int rows;                 // M query rows of one sequence
