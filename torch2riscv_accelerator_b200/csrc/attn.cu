@@ -228,8 +228,9 @@ __global__ void __launch_bounds__(kPvThreads) attn_pv(AttnParams p) {
             }
             const int nsp = (n + kChunk - 1) / kChunk;
             const float* pm = p.pmax + ((size_t)m * H + h) * p.nsplit;
-            float mx = -INFINITY;
-            for (int j = 0; j < nsp; ++j) mx = nanmax(mx, __ldcg(pm + j));
+            float mx = -INFINITY;                              // chunk maxima read in parallel
+            for (int j = lane; j < nsp; j += 32) mx = nanmax(mx, __ldcg(pm + j));
+            mx = warp_absmax(mx);
             const float* sr = p.sc + ((size_t)m * H + h) * T;
             if (p.variant == 0) {                              // NORM: the whole row for the ordered sum
                 for (int t = tid; t < n; t += kPvThreads) ebuf[t] = sfu_exp(fsub(__ldcg(sr + t), mx));
@@ -280,12 +281,15 @@ __global__ void __launch_bounds__(kPvThreads) attn_pv(AttnParams p) {
         float rq = 0.f;
         if (p.variant == 1) {
             int ssum = 0;
-            for (int j = 0; j < nsp; ++j) ssum += __ldcg(p.psum + ((size_t)m * H + h) * p.nsplit + j);
+            for (int j = lane; j < nsp; j += 32) ssum += __ldcg(p.psum + ((size_t)m * H + h) * p.nsplit + j);
+            ssum = warp_sum_i(ssum);
             rq = fmul(sfu_recip(i2f(ssum)), 127.f);            // sum <= 127 T: exact in fp32
         }
         for (int c = tid; c < hd; c += kPvThreads) {
             int acc = 0;
-            for (int j = 0; j < nsp; ++j) acc += __ldcg(p.part + (((size_t)m * H + h) * p.nsplit + j) * hd + c);
+            const int32_t* pp = p.part + ((size_t)m * H + h) * p.nsplit * hd + c;
+#pragma unroll 8
+            for (int j = 0; j < nsp; ++j) acc += __ldcg(pp + (size_t)j * hd);
             const float o = i2f(acc);
             p.att[((size_t)m * H + h) * hd + c] = p.variant == 0 ? fmul(o, p.a_v) : fmul(fmul(o, rq), p.a_v);
         }

@@ -23,7 +23,7 @@ namespace w8a8 {
 __device__ unsigned int g_gemv_errors;                        // bit 1: a tile wait gave up
 
 constexpr int kMaxStages = 8;
-constexpr size_t kRingBytes = 64 * 1024;                      // weight ring per CTA
+constexpr size_t kRingBytes = 96 * 1024;                      // weight ring per CTA
 
 template <int MR, int EPI>
 __device__ __forceinline__ void epilogue_row(const LinearParams& p, int n, const int* acc, const int* acc2,
@@ -91,9 +91,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     pdl_trigger();
     prologue<MR, PRO>(p, xs, xf, sx, red);
 
-    const int rows_per_pass = kWarps / slices;                 // rows computed together (slices warps per row)
+    // rows per pass: a warp owns one row of the pass (slices warps share a row
+    // when the tile has fewer than 8 rows)
+    const int rows_per_pass = kWarps / slices;
     const int row_in = warp % rows_per_pass, sl = warp / rows_per_pass;
     const int c_lo = sl * nch / slices, c_hi = (sl + 1) * nch / slices;
+    const int passes = (tr + rows_per_pass - 1) / rows_per_pass;   // at most 64 / 8 = 8
     int i = 0;
     for (; i < my; ++i) {
         const int s = i % stages;
@@ -102,41 +105,48 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int row0 = ((int)blockIdx.x + i * (int)gridDim.x) * tr;
         const int rows = min(tr, p.n - row0);
         const int8_t* wt = reinterpret_cast<const int8_t*>(ring + s * stage_bytes);
-        for (int rb = 0; rb < tr; rb += rows_per_pass) {
-            const int r = rb + row_in;
-            int acc[MR], acc2[MR];
+        int acc[8][MR], acc2[8][MR];
 #pragma unroll
-            for (int m = 0; m < MR; ++m) acc[m] = acc2[m] = 0;
-            if (r < rows) {
-                const int8_t* wr = wt + (size_t)r * k;
-                const int8_t* wr2 = wr + tile_bytes;
+        for (int q = 0; q < 8; ++q) {
+            const int r = q * rows_per_pass + row_in;
+#pragma unroll
+            for (int m = 0; m < MR; ++m) acc[q][m] = acc2[q][m] = 0;
+            if (q >= passes || r >= rows) continue;
+            const int8_t* wr = wt + (size_t)r * k;
+            const int8_t* wr2 = wr + tile_bytes;
 #pragma unroll 4
-                for (int c = c_lo + lane; c < c_hi; c += 32) {
-                    const int4 w4 = *reinterpret_cast<const int4*>(wr + c * 16);
-                    int4 u4;
-                    if (kTwo) u4 = *reinterpret_cast<const int4*>(wr2 + c * 16);
+            for (int c = c_lo + lane; c < c_hi; c += 32) {
+                const int4 w4 = *reinterpret_cast<const int4*>(wr + c * 16);
+                int4 u4;
+                if (kTwo) u4 = *reinterpret_cast<const int4*>(wr2 + c * 16);
 #pragma unroll
-                    for (int m = 0; m < MR; ++m) {
-                        const int4 x4 = *reinterpret_cast<const int4*>(xs + (size_t)m * k + c * 16);
-                        acc[m] = dp4a(w4.x, x4.x, dp4a(w4.y, x4.y, dp4a(w4.z, x4.z, dp4a(w4.w, x4.w, acc[m]))));
-                        if (kTwo)
-                            acc2[m] = dp4a(u4.x, x4.x, dp4a(u4.y, x4.y, dp4a(u4.z, x4.z, dp4a(u4.w, x4.w, acc2[m]))));
-                    }
+                for (int m = 0; m < MR; ++m) {
+                    const int4 x4 = *reinterpret_cast<const int4*>(xs + (size_t)m * k + c * 16);
+                    acc[q][m] = dp4a(w4.x, x4.x, dp4a(w4.y, x4.y, dp4a(w4.z, x4.z, dp4a(w4.w, x4.w, acc[q][m]))));
+                    if (kTwo)
+                        acc2[q][m] = dp4a(u4.x, x4.x, dp4a(u4.y, x4.y, dp4a(u4.z, x4.z, dp4a(u4.w, x4.w, acc2[q][m]))));
                 }
             }
+        }
+        __syncthreads();                                       // stage s consumed: refill it first
+        if (tid == 0 && i + stages < my) issue(i + stages);
+#pragma unroll
+        for (int q = 0; q < 8; ++q) {
+            if (q >= passes) break;
+            const int r = q * rows_per_pass + row_in;
 #pragma unroll
             for (int m = 0; m < MR; ++m) {
-                acc[m] = warp_sum_i(acc[m]);
-                if (kTwo) acc2[m] = warp_sum_i(acc2[m]);
+                acc[q][m] = warp_sum_i(acc[q][m]);
+                if (kTwo) acc2[q][m] = warp_sum_i(acc2[q][m]);
             }
             if (slices == 1) {
-                if (lane == 0 && r < rows) epilogue_row<MR, EPI>(p, row0 + r, acc, acc2, sx, bamax, bkey);
-            } else {
+                if (lane == 0 && r < rows) epilogue_row<MR, EPI>(p, row0 + r, acc[q], acc2[q], sx, bamax, bkey);
+            } else {                                           // passes == 1: combine the K-slices
                 if (lane == 0) {
 #pragma unroll
                     for (int m = 0; m < MR; ++m) {
-                        spart[warp][m] = acc[m];
-                        spart[warp][MR + m] = acc2[m];
+                        spart[warp][m] = acc[q][m];
+                        spart[warp][MR + m] = acc2[q][m];
                     }
                 }
                 __syncthreads();
@@ -145,9 +155,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int m = 0; m < MR; ++m) {
                         a[m] = a2[m] = 0;
-                        for (int q = 0; q < slices; ++q) {
-                            a[m] += spart[q * rows_per_pass + row_in][m];
-                            a2[m] += spart[q * rows_per_pass + row_in][MR + m];
+                        for (int z = 0; z < slices; ++z) {
+                            a[m] += spart[z * rows_per_pass + row_in][m];
+                            a2[m] += spart[z * rows_per_pass + row_in][MR + m];
                         }
                     }
                     epilogue_row<MR, EPI>(p, row0 + r, a, a2, sx, bamax, bkey);
@@ -155,8 +165,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                 __syncthreads();
             }
         }
-        __syncthreads();                                       // stage s consumed
-        if (tid == 0 && i + stages < my) issue(i + stages);
     }
     if (i < my) {                                              // a wait gave up: record, drain, stop
         if (tid == 0) {
