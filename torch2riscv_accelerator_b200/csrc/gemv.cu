@@ -25,22 +25,25 @@ __device__ unsigned int g_gemv_errors;                        // bit 1: a tile w
 constexpr int kMaxStages = 8;
 constexpr size_t kRingBytes = 96 * 1024;                      // weight ring per CTA
 
+// Row n is the j-th row of this CTA: its scales (and residuals) were staged in
+// shared memory (sw, sw2: [rows of the CTA]; rs: [MR][rows of the CTA]).
 template <int MR, int EPI>
-__device__ __forceinline__ void epilogue_row(const LinearParams& p, int n, const int* acc, const int* acc2,
-                                             const float* sx, uint32_t* bamax, unsigned long long* bkey) {
+__device__ __forceinline__ void epilogue_row(const LinearParams& p, int n, int j, int nj, const int* acc,
+                                             const int* acc2, const float* sx, const float* sw, const float* sw2,
+                                             const float* rs, uint32_t* bamax, unsigned long long* bkey) {
 #pragma unroll
     for (int m = 0; m < MR; ++m) {
         if (m >= p.m) continue;
         const size_t o = (size_t)m * p.n + n;
-        const float v = fmul(fmul(i2f(acc[m]), __ldg(p.s_w + n)), sx[m]);
+        const float v = fmul(fmul(i2f(acc[m]), sw[j]), sx[m]);
         if (EPI == EPI_STORE) {
             p.y[o] = v;
             if (p.acc != nullptr) p.acc[o] = acc[m];
             if (p.argmax_key != nullptr) atomicMax(&bkey[m], argmax_key(v, n));
         } else if (EPI == EPI_RESID) {
-            p.y[o] = fadd(p.resid[o], v);
+            p.y[o] = fadd(rs[m * nj + j], v);
         } else {
-            const float u = fmul(fmul(i2f(acc2[m]), __ldg(p.s_w2 + n)), sx[m]);
+            const float u = fmul(fmul(i2f(acc2[m]), sw2[j]), sx[m]);
             const float h = silu_gate(v, u);
             p.y[o] = h;
             atomicMax(&bamax[m], __float_as_uint(fabsf(h)));
@@ -60,6 +63,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     unsigned char* ring = smem;
     int8_t* xs = reinterpret_cast<int8_t*>(smem + stages * stage_bytes);   // [MR][k]
     float* xf = reinterpret_cast<float*>(xs + (size_t)MR * k);            // [k]
+    const int nj = ((ntiles + (int)gridDim.x - 1) / (int)gridDim.x) * tr;   // rows of a CTA, at most
+    float* sw = xf + (PRO == PRO_I8 ? 0 : k);                               // [nj] row scales
+    float* sw2 = sw + nj;                                                   // [nj] (SwiGLU up rows)
+    float* rs = sw2 + (kTwo ? nj : 0);                                      // [MR][nj] residual rows
     __shared__ __align__(8) uint64_t full[kMaxStages];
     __shared__ float sx[MR];
     __shared__ float red[32];
@@ -87,8 +94,28 @@ __global__ void __launch_bounds__(kThreads, 1)
     };
     if (tid == 0)
         for (int i = 0; i < min(stages, my); ++i) issue(i);    // weights: before the wait
+    // row j of this CTA = tile j / tr, row j % tr; its scales are constants too
+    for (int j = tid; j < my * tr; j += kThreads) {
+        const int n = ((int)blockIdx.x + (j / tr) * (int)gridDim.x) * tr + j % tr;
+        if (n < p.n) {
+            sw[j] = __ldg(p.s_w + n);
+            if (kTwo) sw2[j] = __ldg(p.s_w2 + n);
+        }
+    }
+    if (tid < 4) {                                             // warm L1 with the SFU tables of the prologue
+        const uint32_t* t = tid == 0 ? g_rec_t : tid == 1 ? g_rec_s : tid == 2 ? g_rsq_t : g_rsq_s;
+        const int lines = tid < 2 ? 2 : 4;
+        for (int l = 0; l < lines; ++l) asm volatile("prefetch.global.L1 [%0];" ::"l"(t + 32 * l));
+    }
     pdl_wait();
     pdl_trigger();
+    if (EPI == EPI_RESID) {                                    // residual rows: written by earlier kernels
+        for (int j = tid; j < my * tr * MR; j += kThreads) {
+            const int m = j / (my * tr), jj = j % (my * tr);
+            const int n = ((int)blockIdx.x + (jj / tr) * (int)gridDim.x) * tr + jj % tr;
+            if (n < p.n && m < p.m) rs[m * nj + jj] = p.resid[(size_t)m * p.n + n];
+        }
+    }
     prologue<MR, PRO>(p, xs, xf, sx, red);
 
     // rows per pass: a warp owns one row of the pass (slices warps share a row
@@ -140,7 +167,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                 if (kTwo) acc2[q][m] = warp_sum_i(acc2[q][m]);
             }
             if (slices == 1) {
-                if (lane == 0 && r < rows) epilogue_row<MR, EPI>(p, row0 + r, acc[q], acc2[q], sx, bamax, bkey);
+                if (lane == 0 && r < rows)
+                    epilogue_row<MR, EPI>(p, row0 + r, i * tr + r, nj, acc[q], acc2[q], sx, sw, sw2, rs, bamax, bkey);
             } else {                                           // passes == 1: combine the K-slices
                 if (lane == 0) {
 #pragma unroll
@@ -160,7 +188,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                             a2[m] += spart[z * rows_per_pass + row_in][MR + m];
                         }
                     }
-                    epilogue_row<MR, EPI>(p, row0 + r, a, a2, sx, bamax, bkey);
+                    epilogue_row<MR, EPI>(p, row0 + r, i * tr + r, nj, a, a2, sx, sw, sw2, rs, bamax, bkey);
                 }
                 __syncthreads();
             }
@@ -231,7 +259,9 @@ static Tiling tiling(const LinearParams& p, int mr, int pro, int epi) {
     t.stages = (int)(st < 2 ? 2 : (st > (size_t)kMaxStages ? kMaxStages : st));
     t.ntiles = (p.n + t.tr - 1) / t.tr;
     t.grid = t.ntiles < sm_count() ? t.ntiles : sm_count();
-    t.smem = (size_t)t.stages * stage + (size_t)mr * p.k + (pro == PRO_I8 ? 0 : (size_t)p.k * 4);
+    const size_t nj = (size_t)((t.ntiles + t.grid - 1) / t.grid) * t.tr;   // rows of a CTA, at most
+    t.smem = (size_t)t.stages * stage + (size_t)mr * p.k + (pro == PRO_I8 ? 0 : (size_t)p.k * 4) +
+             nj * 4 * ((epi == EPI_SWIGLU ? 2 : 1) + (epi == EPI_RESID ? mr : 0));
     return t;
 }
 
