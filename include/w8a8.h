@@ -62,7 +62,8 @@ int w8a8_embed(const int32_t* tokens, int rows, const int8_t* emb_q, const float
 
 /* Read and clear the current device's error flags (bit 0: an out-of-range
  * token reached w8a8_embed; bit 1: a GEMV weight-tile wait gave up after its
- * bounded spin and the kernel stopped early). Synchronous with the device.
+ * bounded spin and the kernel stopped early; bit 2: an attention chunk barrier
+ * gave up after its bounded spin: that call's output is not valid). Synchronous with the device.
  * Plays the role of the overlay's sticky list status (llm/sa_funcsim.py:62-66,
  * firmware/rt/rt_fw.c:53-60). */
 int w8a8_error_flags(uint32_t* flags);
@@ -134,6 +135,11 @@ typedef struct {
  * (SahlKernels.h:155-177). */
 size_t w8a8_attn_scratch_bytes(int rows, int heads, int kv_heads, int head_dim, int seq_len);
 int w8a8_attn(const W8A8AttnArgs* args, void* stream);
+/* One launch of (kv_heads x ceil(seq_len / 128)) CTAs whose chunks of a KV head
+ * meet at bounded barriers, so the whole grid must fit on the GPU at once:
+ * w8a8_attn returns W8A8_EINVAL when it does not (seq_len too long for the
+ * head count). The scratch must be zero before the first call; each call
+ * leaves it so. Calls sharing a scratch buffer must not overlap in time. */
 
 /* Greedy token per row (np.argmax: the first maximum). Replaces
  * Sampler.__call__ at temperature 0 (llm/runtime.py:55-57). */

@@ -61,7 +61,7 @@ int w8a8_error_flags(uint32_t* flags) {
     if (!flags) return W8A8_EINVAL;
     unsigned int v = 0;
     int st = cuda_status(read_clear_errors(&v));
-    *flags = v | gemv_read_clear_errors();
+    *flags = v | gemv_read_clear_errors() | attn_read_clear_errors();
     return st;
 }
 
@@ -141,6 +141,10 @@ int w8a8_attn(const W8A8AttnArgs* a, void* stream) {
     if (a->head_dim % 16 || !al16(a->k_cache) || !al16(a->v_cache) || !al16(a->scratch)) return W8A8_EALIGN;
     if (a->scratch_bytes < attn_scratch_bytes(a->rows, a->heads, a->kv_heads, a->head_dim, a->seq_len))
         return W8A8_ESCRATCH;
+    // the chunks of a KV head wait for one another: the whole grid must be resident
+    const int nsplit = (a->seq_len + kChunk - 1) / kChunk;
+    if ((long)a->kv_heads * nsplit > attn_max_ctas(a->rows, a->heads, a->kv_heads, a->head_dim, a->seq_len, a->variant))
+        return W8A8_EINVAL;
     AttnParams p{};
     p.rows = a->rows, p.heads = a->heads, p.kv_heads = a->kv_heads, p.head_dim = a->head_dim;
     p.seq_len = a->seq_len, p.variant = a->variant, p.qk_norm = a->q_norm != nullptr;

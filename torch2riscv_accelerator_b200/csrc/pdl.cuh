@@ -42,22 +42,55 @@ __device__ __forceinline__ void bulk_g2s(void* dst, const void* src, uint32_t by
         : "memory");
 }
 
-// Bounded wait for the mbarrier phase with the given parity: non-blocking
-// tests with a growing back-off, about 0.5 s at most. Returns false when it
-// gave up (the caller records an error and stops using the stage).
+// Bounded wait for the mbarrier phase with the given parity: try_wait suspends
+// the thread in hardware until the phase completes or a ~1 us time hint runs
+// out; at most 2^20 tries (about a second). Returns false when it gave up (the
+// caller records an error and stops using the stage).
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
     const uint32_t a = smem_u32(bar);
-    for (int i = 0; i < (1 << 22); ++i) {
+    for (int i = 0; i < (1 << 20); ++i) {
         uint32_t ok;
         asm volatile(
-            "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n selp.u32 %0, 1, 0, p;\n}\n"
             : "=r"(ok)
-            : "r"(a), "r"(parity)
+            : "r"(a), "r"(parity), "r"(1000u)
             : "memory");
         if (ok) return true;
-        if (i > 64) __nanosleep(i < 4096 ? 32 : 128);
     }
     return false;
+}
+
+// Sense-reversing barrier among `n` CTAs over global memory: count[0] counts
+// arrivals, gen[0] is bumped by the last one. Bounded: gives up after ~2^22
+// polls (about 0.2 s) and returns false. Call with the whole CTA; the CTA's
+// prior global writes are released before it arrives, and what the others
+// wrote is visible after it returns.
+__device__ __forceinline__ bool cta_barrier(unsigned int* count, volatile unsigned int* gen, unsigned int n) {
+    __shared__ int ok_s;
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const unsigned int g0 = *gen;
+        __threadfence();
+        int ok = 1;
+        if (atomicAdd(count, 1u) == n - 1) {
+            *count = 0u;
+            __threadfence();
+            atomicAdd((unsigned int*)gen, 1u);
+        } else {
+            int it = 0;
+            while (*gen == g0) {
+                if (++it > (1 << 22)) {
+                    ok = 0;
+                    break;
+                }
+                if (it > 32) __nanosleep(32);
+            }
+        }
+        __threadfence();
+        ok_s = ok;
+    }
+    __syncthreads();
+    return ok_s != 0;
 }
 
 }  // namespace w8a8

@@ -52,12 +52,13 @@ struct AttnParams {
     int8_t* kc;               // [Hk, seq_len, hd] this layer's K cache
     int8_t* vc;               // [Hk, seq_len, hd]
     float* att;               // [M, H hd] out
-    // scratch (carved by the host wrapper from one buffer)
-    float* sc;                // [M, H, seq_len] scores
-    float* pmax;              // [M, H, nsplit] chunk maxima
-    int32_t* part;            // [M, H, nsplit, hd] int32 p.V partials
-    int32_t* psum;            // [M, H, nsplit] QSUM: sum of int8 e per chunk
-    uint32_t* cnt;            // [Hk] tickets, zero between launches
+    // scratch (carved by the host wrapper from one buffer); every call leaves
+    // the accumulators and counters zero for the next one
+    float* sc;                // [M, H, seq_len] scores (NORM: the whole row for the ordered sum)
+    uint32_t* gmax;           // [M, H] ordered-int row maxima
+    int32_t* psum;            // [M, H] QSUM: sum of int8 e
+    int32_t* acc;             // [M, H, hd] int32 p.V sums
+    uint32_t* sync;           // [Hk, 32]: per KV head barrier (count, generation)
     int nsplit;               // ceil(seq_len / kChunk)
 };
 
@@ -65,6 +66,8 @@ constexpr int kChunk = 128;   // cache positions per attention CTA
 constexpr int kMaxRows = 16;  // query rows per attention call
 
 size_t attn_scratch_bytes(int rows, int heads, int kv_heads, int head_dim, int seq_len);
+int attn_max_ctas(int rows, int heads, int kv_heads, int head_dim, int seq_len, int variant);
+unsigned int attn_read_clear_errors();
 void attn_carve(AttnParams& p, void* scratch);
 cudaError_t launch_attn(const AttnParams& p, cudaStream_t st);
 
