@@ -118,12 +118,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     prologue<MR, PRO>(p, xs, xf, sx, red);
 
-    // rows per pass: a warp owns one row of the pass (slices warps share a row
-    // when the tile has fewer than 8 rows)
-    const int rows_per_pass = kWarps / slices;
-    const int row_in = warp % rows_per_pass, sl = warp / rows_per_pass;
-    const int c_lo = sl * nch / slices, c_hi = (sl + 1) * nch / slices;
-    const int passes = (tr + rows_per_pass - 1) / rows_per_pass;   // at most 64 / 8 = 8
+    // Thread t owns row r = t / S of the tile and K-slice s = t % S (S = 256 / tr
+    // threads per row): chunks s, s + S, ... of 16 bytes. Lanes of a warp read
+    // consecutive chunks (conflict-free), the S slices of a row are reduced with
+    // shuffles (and through shared memory when a row spans warps).
+    const int S = kThreads / tr, r = tid / S, sl = tid % S;
     int i = 0;
     for (; i < my; ++i) {
         const int s = i % stages;
@@ -131,68 +130,59 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (__syncthreads_or(!ok)) break;
         const int row0 = ((int)blockIdx.x + i * (int)gridDim.x) * tr;
         const int rows = min(tr, p.n - row0);
-        const int8_t* wt = reinterpret_cast<const int8_t*>(ring + s * stage_bytes);
-        int acc[8][MR], acc2[8][MR];
+        const int8_t* wr = reinterpret_cast<const int8_t*>(ring + s * stage_bytes) + (size_t)r * k;
+        const int8_t* wr2 = wr + tile_bytes;
+        int acc[MR], acc2[MR];
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-            const int r = q * rows_per_pass + row_in;
-#pragma unroll
-            for (int m = 0; m < MR; ++m) acc[q][m] = acc2[q][m] = 0;
-            if (q >= passes || r >= rows) continue;
-            const int8_t* wr = wt + (size_t)r * k;
-            const int8_t* wr2 = wr + tile_bytes;
+        for (int m = 0; m < MR; ++m) acc[m] = acc2[m] = 0;
+        if (r < rows) {
 #pragma unroll 4
-            for (int c = c_lo + lane; c < c_hi; c += 32) {
+            for (int c = sl; c < nch; c += S) {
                 const int4 w4 = *reinterpret_cast<const int4*>(wr + c * 16);
                 int4 u4;
                 if (kTwo) u4 = *reinterpret_cast<const int4*>(wr2 + c * 16);
 #pragma unroll
                 for (int m = 0; m < MR; ++m) {
                     const int4 x4 = *reinterpret_cast<const int4*>(xs + (size_t)m * k + c * 16);
-                    acc[q][m] = dp4a(w4.x, x4.x, dp4a(w4.y, x4.y, dp4a(w4.z, x4.z, dp4a(w4.w, x4.w, acc[q][m]))));
+                    acc[m] = dp4a(w4.w, x4.w, dp4a(w4.z, x4.z, dp4a(w4.y, x4.y, dp4a(w4.x, x4.x, acc[m]))));
                     if (kTwo)
-                        acc2[q][m] = dp4a(u4.x, x4.x, dp4a(u4.y, x4.y, dp4a(u4.z, x4.z, dp4a(u4.w, x4.w, acc2[q][m]))));
+                        acc2[m] = dp4a(u4.w, x4.w, dp4a(u4.z, x4.z, dp4a(u4.y, x4.y, dp4a(u4.x, x4.x, acc2[m]))));
                 }
             }
         }
         __syncthreads();                                       // stage s consumed: refill it first
         if (tid == 0 && i + stages < my) issue(i + stages);
+        const int sw_lanes = S < 32 ? S : 32;
 #pragma unroll
-        for (int q = 0; q < 8; ++q) {
-            if (q >= passes) break;
-            const int r = q * rows_per_pass + row_in;
-#pragma unroll
-            for (int m = 0; m < MR; ++m) {
-                acc[q][m] = warp_sum_i(acc[q][m]);
-                if (kTwo) acc2[q][m] = warp_sum_i(acc2[q][m]);
-            }
-            if (slices == 1) {
-                if (lane == 0 && r < rows)
-                    epilogue_row<MR, EPI>(p, row0 + r, i * tr + r, nj, acc[q], acc2[q], sx, sw, sw2, rs, bamax, bkey);
-            } else {                                           // passes == 1: combine the K-slices
-                if (lane == 0) {
-#pragma unroll
-                    for (int m = 0; m < MR; ++m) {
-                        spart[warp][m] = acc[q][m];
-                        spart[warp][MR + m] = acc2[q][m];
-                    }
-                }
-                __syncthreads();
-                if (sl == 0 && lane == 0 && r < rows) {
-                    int a[MR], a2[MR];
-#pragma unroll
-                    for (int m = 0; m < MR; ++m) {
-                        a[m] = a2[m] = 0;
-                        for (int z = 0; z < slices; ++z) {
-                            a[m] += spart[z * rows_per_pass + row_in][m];
-                            a2[m] += spart[z * rows_per_pass + row_in][MR + m];
-                        }
-                    }
-                    epilogue_row<MR, EPI>(p, row0 + r, i * tr + r, nj, a, a2, sx, sw, sw2, rs, bamax, bkey);
-                }
-                __syncthreads();
+        for (int m = 0; m < MR; ++m) {
+            for (int o = sw_lanes / 2; o > 0; o >>= 1) {
+                acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], o);
+                if (kTwo) acc2[m] += __shfl_xor_sync(0xffffffffu, acc2[m], o);
             }
         }
+        if (S > 32) {                                          // a row spans S / 32 warps
+            if (lane == 0) {
+#pragma unroll
+                for (int m = 0; m < MR; ++m) {
+                    spart[warp][m] = acc[m];
+                    spart[warp][MR + m] = acc2[m];
+                }
+            }
+            __syncthreads();
+            if (sl == 0) {
+#pragma unroll
+                for (int m = 0; m < MR; ++m) {
+                    acc[m] = acc2[m] = 0;
+                    for (int z = 0; z < S / 32; ++z) {
+                        acc[m] += spart[warp + z][m];
+                        acc2[m] += spart[warp + z][MR + m];
+                    }
+                }
+            }
+        }
+        if (sl == 0 && r < rows)
+            epilogue_row<MR, EPI>(p, row0 + r, i * tr + r, nj, acc, acc2, sx, sw, sw2, rs, bamax, bkey);
+        if (S > 32) __syncthreads();                           // spart reused by the next tile
     }
     if (i < my) {                                              // a wait gave up: record, drain, stop
         if (tid == 0) {
@@ -249,11 +239,11 @@ struct Tiling {
 static Tiling tiling(const LinearParams& p, int mr, int pro, int epi) {
     Tiling t{};
     int tr = 16384 / p.k;
-    tr = tr < 1 ? 1 : (tr > 64 ? 64 : tr);
+    tr = tr < 1 ? 1 : (tr > kThreads ? kThreads : tr);
     int pw = 1;
     while (pw * 2 <= tr) pw *= 2;
-    t.tr = pw;
-    t.slices = t.tr >= kWarps ? 1 : kWarps / t.tr;
+    t.tr = pw;                                                 // threads per row: kThreads / tr
+    t.slices = kThreads / t.tr;
     const size_t stage = (size_t)t.tr * p.k * (epi == EPI_SWIGLU ? 2 : 1);
     size_t st = kRingBytes / stage;
     t.stages = (int)(st < 2 ? 2 : (st > (size_t)kMaxStages ? kMaxStages : st));
