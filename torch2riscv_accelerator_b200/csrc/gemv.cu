@@ -51,12 +51,16 @@ __device__ __forceinline__ void epilogue_row(const LinearParams& p, int n, int j
     }
 }
 
+constexpr int kConsumers = kThreads;                          // 8 consumer warps
+constexpr int kGemvThreads = kThreads + 32;                   // + 1 producer warp
+
 template <int MR, int PRO, int EPI>
-__global__ void __launch_bounds__(kThreads, 1)
-    gemv_kernel(LinearParams p, int tr, int slices, int stages, int ntiles) {
+__global__ void __launch_bounds__(kGemvThreads, 1)
+    gemv_kernel(LinearParams p, int tr, int S, int stages, int ntiles) {
     extern __shared__ __align__(128) unsigned char smem[];
     constexpr bool kTwo = EPI == EPI_SWIGLU;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const bool producer = warp == kWarps;
     const int k = p.k, nch = k / 16;
     const size_t tile_bytes = (size_t)tr * k;
     const size_t stage_bytes = tile_bytes * (kTwo ? 2 : 1);
@@ -67,24 +71,28 @@ __global__ void __launch_bounds__(kThreads, 1)
     float* sw = xf + (PRO == PRO_I8 ? 0 : k);                               // [nj] row scales
     float* sw2 = sw + nj;                                                   // [nj] (SwiGLU up rows)
     float* rs = sw2 + (kTwo ? nj : 0);                                      // [MR][nj] residual rows
-    __shared__ __align__(8) uint64_t full[kMaxStages];
+    __shared__ __align__(8) uint64_t full[kMaxStages];         // tile landed (bulk-copy bytes)
+    __shared__ __align__(8) uint64_t empty[kMaxStages];        // the 8 consumer warps are done with it
     __shared__ float sx[MR];
     __shared__ float red[32];
     __shared__ uint32_t bamax[MR];
     __shared__ unsigned long long bkey[MR];
-    __shared__ int spart[kWarps][2 * MR];
-    __shared__ int last;
+    __shared__ int last, failed;
     const int my = (ntiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;   // tiles of this CTA
     if (tid < MR) {
         bamax[tid] = 0u;
         bkey[tid] = 0ull;
     }
     if (tid == 0) {
-        for (int s = 0; s < stages; ++s) mbar_init(&full[s], 1);
+        failed = 0;
+        for (int s = 0; s < stages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kWarps);
+        }
         mbar_fence_init();
     }
     __syncthreads();
-    auto issue = [&](int i) {                                  // thread 0: tile i of this CTA -> stage i % stages
+    auto issue = [&](int i) {                                  // tile i of this CTA -> stage i % stages
         const int s = i % stages;
         const int row0 = ((int)blockIdx.x + i * (int)gridDim.x) * tr;
         const uint32_t bytes = (uint32_t)(min(tr, p.n - row0) * k);
@@ -92,10 +100,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         bulk_g2s(ring + s * stage_bytes, p.w + (size_t)row0 * k, bytes, &full[s]);
         if (kTwo) bulk_g2s(ring + s * stage_bytes + tile_bytes, p.w2 + (size_t)row0 * k, bytes, &full[s]);
     };
-    if (tid == 0)
-        for (int i = 0; i < min(stages, my); ++i) issue(i);    // weights: before the wait
+    const int first = min(stages, my);
+    if (producer && lane == 0)
+        for (int i = 0; i < first; ++i) issue(i);              // weights: before the wait
     // row j of this CTA = tile j / tr, row j % tr; its scales are constants too
-    for (int j = tid; j < my * tr; j += kThreads) {
+    for (int j = tid; j < my * tr; j += kGemvThreads) {
         const int n = ((int)blockIdx.x + (j / tr) * (int)gridDim.x) * tr + j % tr;
         if (n < p.n) {
             sw[j] = __ldg(p.s_w + n);
@@ -110,7 +119,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     pdl_wait();
     pdl_trigger();
     if (EPI == EPI_RESID) {                                    // residual rows: written by earlier kernels
-        for (int j = tid; j < my * tr * MR; j += kThreads) {
+        for (int j = tid; j < my * tr * MR; j += kGemvThreads) {
             const int m = j / (my * tr), jj = j % (my * tr);
             const int n = ((int)blockIdx.x + (jj / tr) * (int)gridDim.x) * tr + jj % tr;
             if (n < p.n && m < p.m) rs[m * nj + jj] = p.resid[(size_t)m * p.n + n];
@@ -118,87 +127,78 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     prologue<MR, PRO>(p, xs, xf, sx, red);
 
-    // Thread t owns row r = t / S of the tile and K-slice s = t % S (S = 256 / tr
-    // threads per row): chunks s, s + S, ... of 16 bytes. Lanes of a warp read
-    // consecutive chunks (conflict-free), the S slices of a row are reduced with
-    // shuffles (and through shared memory when a row spans warps).
-    const int S = kThreads / tr, r = tid / S, sl = tid % S;
-    int i = 0;
-    for (; i < my; ++i) {
-        const int s = i % stages;
-        const bool ok = mbar_wait(&full[s], (uint32_t)((i / stages) & 1));
-        if (__syncthreads_or(!ok)) break;
-        const int row0 = ((int)blockIdx.x + i * (int)gridDim.x) * tr;
-        const int rows = min(tr, p.n - row0);
-        const int8_t* wr = reinterpret_cast<const int8_t*>(ring + s * stage_bytes) + (size_t)r * k;
-        const int8_t* wr2 = wr + tile_bytes;
-        int acc[MR], acc2[MR];
+    if (producer) {
+        if (lane == 0) {                                       // refill each stage once its consumers are done
+            for (int i = first; i < my; ++i) {
+                const int s = i % stages;
+                if (!mbar_wait(&empty[s], (uint32_t)(((i / stages) - 1) & 1))) {
+                    atomicOr(&g_gemv_errors, 2u);
+                    failed = 1;
+                    break;
+                }
+                issue(i);
+            }
+        }
+    } else {
+        // Consumer thread t owns row r = t / S of a tile and K-slice s = t % S
+        // (S <= 32 threads per row, within one warp): chunks s, s + S, ... of 16
+        // bytes; lanes read consecutive chunks (conflict-free); the row is summed
+        // with shuffles. A warp releases the stage before its epilogue.
+        const int r = tid / S, sl = tid % S;
+        for (int i = 0; i < my; ++i) {
+            const int s = i % stages;
+            if (!mbar_wait(&full[s], (uint32_t)((i / stages) & 1))) {
+                atomicOr(&g_gemv_errors, 2u);
+                failed = 1;
+                break;
+            }
+            const int row0 = ((int)blockIdx.x + i * (int)gridDim.x) * tr;
+            const int rows = min(tr, p.n - row0);
+            const int8_t* wr = reinterpret_cast<const int8_t*>(ring + s * stage_bytes) + (size_t)r * k;
+            const int8_t* wr2 = wr + tile_bytes;
+            int acc[MR], acc2[MR];
 #pragma unroll
-        for (int m = 0; m < MR; ++m) acc[m] = acc2[m] = 0;
-        if (r < rows) {
+            for (int m = 0; m < MR; ++m) acc[m] = acc2[m] = 0;
+            if (r < rows) {
 #pragma unroll 4
-            for (int c = sl; c < nch; c += S) {
-                const int4 w4 = *reinterpret_cast<const int4*>(wr + c * 16);
-                int4 u4;
-                if (kTwo) u4 = *reinterpret_cast<const int4*>(wr2 + c * 16);
+                for (int c = sl; c < nch; c += S) {
+                    const int4 w4 = *reinterpret_cast<const int4*>(wr + c * 16);
+                    int4 u4;
+                    if (kTwo) u4 = *reinterpret_cast<const int4*>(wr2 + c * 16);
 #pragma unroll
-                for (int m = 0; m < MR; ++m) {
-                    const int4 x4 = *reinterpret_cast<const int4*>(xs + (size_t)m * k + c * 16);
-                    acc[m] = dp4a(w4.w, x4.w, dp4a(w4.z, x4.z, dp4a(w4.y, x4.y, dp4a(w4.x, x4.x, acc[m]))));
-                    if (kTwo)
-                        acc2[m] = dp4a(u4.w, x4.w, dp4a(u4.z, x4.z, dp4a(u4.y, x4.y, dp4a(u4.x, x4.x, acc2[m]))));
-                }
-            }
-        }
-        __syncthreads();                                       // stage s consumed: refill it first
-        if (tid == 0 && i + stages < my) issue(i + stages);
-        const int sw_lanes = S < 32 ? S : 32;
-#pragma unroll
-        for (int m = 0; m < MR; ++m) {
-            for (int o = sw_lanes / 2; o > 0; o >>= 1) {
-                acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], o);
-                if (kTwo) acc2[m] += __shfl_xor_sync(0xffffffffu, acc2[m], o);
-            }
-        }
-        if (S > 32) {                                          // a row spans S / 32 warps
-            if (lane == 0) {
-#pragma unroll
-                for (int m = 0; m < MR; ++m) {
-                    spart[warp][m] = acc[m];
-                    spart[warp][MR + m] = acc2[m];
-                }
-            }
-            __syncthreads();
-            if (sl == 0) {
-#pragma unroll
-                for (int m = 0; m < MR; ++m) {
-                    acc[m] = acc2[m] = 0;
-                    for (int z = 0; z < S / 32; ++z) {
-                        acc[m] += spart[warp + z][m];
-                        acc2[m] += spart[warp + z][MR + m];
+                    for (int m = 0; m < MR; ++m) {
+                        const int4 x4 = *reinterpret_cast<const int4*>(xs + (size_t)m * k + c * 16);
+                        acc[m] = dp4a(w4.w, x4.w, dp4a(w4.z, x4.z, dp4a(w4.y, x4.y, dp4a(w4.x, x4.x, acc[m]))));
+                        if (kTwo)
+                            acc2[m] = dp4a(u4.w, x4.w, dp4a(u4.z, x4.z, dp4a(u4.y, x4.y, dp4a(u4.x, x4.x, acc2[m]))));
                     }
                 }
             }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+#pragma unroll
+            for (int m = 0; m < MR; ++m) {
+                for (int o = S / 2; o > 0; o >>= 1) {
+                    acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], o);
+                    if (kTwo) acc2[m] += __shfl_xor_sync(0xffffffffu, acc2[m], o);
+                }
+            }
+            if (sl == 0 && r < rows)
+                epilogue_row<MR, EPI>(p, row0 + r, i * tr + r, nj, acc, acc2, sx, sw, sw2, rs, bamax, bkey);
         }
-        if (sl == 0 && r < rows)
-            epilogue_row<MR, EPI>(p, row0 + r, i * tr + r, nj, acc, acc2, sx, sw, sw2, rs, bamax, bkey);
-        if (S > 32) __syncthreads();                           // spart reused by the next tile
     }
-    if (i < my) {                                              // a wait gave up: record, drain, stop
-        if (tid == 0) {
-            atomicOr(&g_gemv_errors, 2u);
-            for (int j = i; j < min(i + stages, my); ++j) mbar_wait(&full[j % stages], (uint32_t)((j / stages) & 1));
-        }
+    __syncthreads();
+    if (failed) {                                              // a wait gave up: drain what is in flight, stop
+        if (producer && lane == 0)
+            for (int s = 0; s < stages; ++s) mbar_wait(&full[s], 0u), mbar_wait(&full[s], 1u);
         __syncthreads();
         return;
     }
     if (EPI == EPI_STORE && p.argmax_key != nullptr) {
-        __syncthreads();
         if (tid < p.m && tid < MR) atomicMax(p.argmax_key + tid, bkey[tid]);
     }
     if (EPI != EPI_SWIGLU) return;
     // the row amax across the grid; the last CTA requantizes h (quant_act)
-    __syncthreads();
     if (tid < p.m && tid < MR) atomicMax(p.amax_bits + tid, bamax[tid]);
     __threadfence();
     __syncthreads();
@@ -212,7 +212,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float inv = sfu_recip(s);
         const float* hr = p.y + (size_t)m * p.n;
         int8_t* qr = p.hq + (size_t)m * p.n;
-        for (int j = tid; j < p.n; j += kThreads) qr[j] = (int8_t)to_i8(fmul(__ldcg(hr + j), inv));
+        for (int j = tid; j < p.n; j += kGemvThreads) qr[j] = (int8_t)to_i8(fmul(__ldcg(hr + j), inv));
         if (tid == 0) p.s_h[m] = s;
     }
     __syncthreads();
@@ -238,12 +238,12 @@ struct Tiling {
 // split a row's K when a tile has fewer than 8 rows; a 64 KB ring of stages.
 static Tiling tiling(const LinearParams& p, int mr, int pro, int epi) {
     Tiling t{};
-    int tr = 16384 / p.k;
-    tr = tr < 1 ? 1 : (tr > kThreads ? kThreads : tr);
+    int tr = 16384 / p.k;                                      // ~16 KB per matrix, at least 8 rows
+    tr = tr < kWarps ? kWarps : (tr > kConsumers ? kConsumers : tr);
     int pw = 1;
     while (pw * 2 <= tr) pw *= 2;
-    t.tr = pw;                                                 // threads per row: kThreads / tr
-    t.slices = kThreads / t.tr;
+    t.tr = pw;
+    t.slices = kConsumers / t.tr;                              // consumer threads per row, at most 32
     const size_t stage = (size_t)t.tr * p.k * (epi == EPI_SWIGLU ? 2 : 1);
     size_t st = kRingBytes / stage;
     t.stages = (int)(st < 2 ? 2 : (st > (size_t)kMaxStages ? kMaxStages : st));
@@ -261,7 +261,7 @@ static cudaError_t launch_g(const LinearParams& p, cudaStream_t st) {
     auto kern = gemv_kernel<MR, PRO, EPI>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)t.smem);
     if (e != cudaSuccess) return e;
-    return launch_k(kern, dim3(t.grid), dim3(kThreads), t.smem, st, p, t.tr, t.slices, t.stages, t.ntiles);
+    return launch_k(kern, dim3(t.grid), dim3(kGemvThreads), t.smem, st, p, t.tr, t.slices, t.stages, t.ntiles);
 }
 
 template <int PRO, int EPI>

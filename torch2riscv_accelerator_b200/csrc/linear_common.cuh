@@ -18,7 +18,7 @@ __device__ __forceinline__ void prologue(const LinearParams& p, int8_t* xs, floa
         for (int m = 0; m < MR; ++m) {
             int4* dst = reinterpret_cast<int4*>(xs + (size_t)m * k);
             const int4* src = reinterpret_cast<const int4*>(p.xq + (size_t)m * k);
-            for (int c = tid; c < k / 16; c += kThreads) dst[c] = m < p.m ? __ldg(src + c) : make_int4(0, 0, 0, 0);
+            for (int c = tid; c < k / 16; c += (int)blockDim.x) dst[c] = m < p.m ? __ldg(src + c) : make_int4(0, 0, 0, 0);
         }
         if (tid < MR) sx[tid] = tid < p.m ? p.s_x[tid] : 0.f;
         __syncthreads();
@@ -31,14 +31,14 @@ __device__ __forceinline__ void prologue(const LinearParams& p, int8_t* xs, floa
     for (int m = 0; m < MR; ++m) {
         char4* dst = reinterpret_cast<char4*>(xs + (size_t)m * k);
         if (m >= p.m) {
-            for (int c = tid; c < k / 4; c += kThreads) dst[c] = make_char4(0, 0, 0, 0);
+            for (int c = tid; c < k / 4; c += (int)blockDim.x) dst[c] = make_char4(0, 0, 0, 0);
             if (tid == 0) sx[m] = 0.f;
             continue;
         }
         const float4* xr = reinterpret_cast<const float4*>(p.x + (size_t)m * k);
         float4* xf4 = reinterpret_cast<float4*>(xf);
         __syncthreads();                                         // xf free (previous row done)
-        for (int c = tid; c < k / 4; c += kThreads) xf4[c] = xr[c];
+        for (int c = tid; c < k / 4; c += (int)blockDim.x) xf4[c] = xr[c];
         __syncthreads();
         float r = 1.f;
         if (PRO == PRO_RMSQ) {
@@ -62,14 +62,14 @@ __device__ __forceinline__ void prologue(const LinearParams& p, int8_t* xs, floa
             return v;
         };
         float a = 0.f;
-        for (int c = tid; c < k / 4; c += kThreads) {
+        for (int c = tid; c < k / 4; c += (int)blockDim.x) {
             float4 v = val(c);
             a = nanmax(a, nanmax(nanmax(fabsf(v.x), fabsf(v.y)), nanmax(fabsf(v.z), fabsf(v.w))));
         }
         a = block_nanmax(a, red);
         const float s = fmul(a, W8A8_C127);
         const float inv = sfu_recip(s);
-        for (int c = tid; c < k / 4; c += kThreads) {
+        for (int c = tid; c < k / 4; c += (int)blockDim.x) {
             float4 v = val(c);
             dst[c] = make_char4(to_i8(fmul(v.x, inv)), to_i8(fmul(v.y, inv)), to_i8(fmul(v.z, inv)),
                                 to_i8(fmul(v.w, inv)));

@@ -145,9 +145,17 @@ __device__ __forceinline__ float red_sum16(Fn v, int n, int lane) {
     if (lane < kLanes) {
         acc = lane < n ? v(lane) : 0.f;
         const int groups = (n + kLanes - 1) / kLanes;
-#pragma unroll 8
-        for (int g = 1; g < groups; ++g) {
-            int i = g * kLanes + lane;
+        const int full = n / kLanes;                         // groups without padding
+        int g = 1;
+        for (; g + 8 <= full; g += 8) {                      // 8 independent reads, then the ordered adds
+            float t[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) t[j] = v((g + j) * kLanes + lane);
+#pragma unroll
+            for (int j = 0; j < 8; ++j) acc = fadd(acc, t[j]);
+        }
+        for (; g < groups; ++g) {
+            const int i = g * kLanes + lane;
             acc = fadd(acc, i < n ? v(i) : 0.f);
         }
     }
