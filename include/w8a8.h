@@ -62,8 +62,7 @@ int w8a8_embed(const int32_t* tokens, int rows, const int8_t* emb_q, const float
 
 /* Read and clear the current device's error flags (bit 0: an out-of-range
  * token reached w8a8_embed; bit 1: a GEMV weight-tile wait gave up after its
- * bounded spin and the kernel stopped early; bit 2: an attention chunk barrier
- * gave up after its bounded spin: that call's output is not valid). Synchronous with the device.
+ * bounded spin and the kernel stopped early). Synchronous with the device.
  * Plays the role of the overlay's sticky list status (llm/sa_funcsim.py:62-66,
  * firmware/rt/rt_fw.c:53-60). */
 int w8a8_error_flags(uint32_t* flags);
@@ -121,7 +120,7 @@ typedef struct {
     int8_t* k_cache;           /* [kv_heads, seq_len, head_dim] this layer's K, written at pos */
     int8_t* v_cache;
     float* att;                /* [rows, heads head_dim] out */
-    void* scratch;             /* w8a8_attn_scratch_bytes() bytes, zero before the first call */
+    void* scratch;             /* unused (w8a8_attn_scratch_bytes() is 0); kept for the ABI layout */
     size_t scratch_bytes;
 } W8A8AttnArgs;
 
@@ -135,11 +134,12 @@ typedef struct {
  * (SahlKernels.h:155-177). */
 size_t w8a8_attn_scratch_bytes(int rows, int heads, int kv_heads, int head_dim, int seq_len);
 int w8a8_attn(const W8A8AttnArgs* args, void* stream);
-/* One launch of (kv_heads x ceil(seq_len / 128)) CTAs whose chunks of a KV head
- * meet at bounded barriers, so the whole grid must fit on the GPU at once:
- * w8a8_attn returns W8A8_EINVAL when it does not (seq_len too long for the
- * head count). The scratch must be zero before the first call; each call
- * leaves it so. Calls sharing a scratch buffer must not overlap in time. */
+/* One launch: a thread-block cluster of up to 8 CTAs per KV head, each CTA
+ * holding a chunk of up to 512 cache positions in shared memory; the chunks
+ * meet at the hardware cluster barrier and exchange maxima and int32 partial
+ * sums through distributed shared memory. w8a8_attn returns W8A8_EINVAL when
+ * seq_len needs more than 8 x 512 positions or the chunk does not fit in
+ * shared memory. */
 
 /* Greedy token per row (np.argmax: the first maximum). Replaces
  * Sampler.__call__ at temperature 0 (llm/runtime.py:55-57). */

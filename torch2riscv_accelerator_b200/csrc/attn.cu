@@ -3,71 +3,86 @@
 // each computed exactly as a decode row, compiler/frontend/hf_generic.py:306-363;
 // each head's cache is read once per call for all rows, docs/fusion_design.md 6.7).
 //
-// Grid (KV head, 128-position chunk); the chunks of one KV head meet twice at a
-// bounded barrier over global memory (all CTAs of the grid are resident at
-// once: the host checks the occupancy before launching):
+// One thread-block cluster per KV head: CS <= 8 CTAs, CTA j owning the cache
+// positions [j*chunk, (j+1)*chunk). The CTAs of a cluster exchange their chunk
+// maxima and int32 p.V partials through distributed shared memory and meet at
+// the hardware cluster barrier; nothing goes through global scratch memory.
 //  1. q path of the G query heads of the KV head, every row: QK-norm (RMSNorm
 //     over head_dim, D = 16 ordered sum), RoPE (v*cos + swapneg(v)*sin),
 //     per-head quant_act -> int8 q. The CTA whose chunk holds a row's position
 //     makes that row's K and V: QK-norm + RoPE + i8(k*inv_sk), i8(v*inv_sv),
 //     into the cache (llm/ref_model.py:225-229, hf_generic.SaCache.update
-//     :190-226) and into its tiles. Scores (f32(qq.k)*s_q)*a_k stay in shared
-//     memory; the chunk maxima go to a global atomic max per row and head.
-//     -- barrier A: the row maxima are final (the global max comes before any
-//     int8 rounding: no online softmax) --
-//  2. e = EXP(s - m); QSUM: eq = i8(127e), sum eq; NORM: the whole row's e (from
-//     the scores in global memory) for the ordered sum, pq = i8(127 e RECIP(sum))
-//     (llm/ref_model.py:233-242; hf_generic.py:275-290); int32 pq.V of the chunk,
-//     added into global int32 sums with atomics (exact in any order).
-//     -- barrier B --
-//  3. the chunk-0 CTA dequantizes: NORM f32(acc)*a_v; QSUM
-//     (f32(acc)*(RECIP(sum)*127))*a_v, and clears the sums and maxima.
+//     :190-226) and into its tiles. Scores (f32(qq.k)*s_q)*a_k and the chunk's
+//     maxima stay in shared memory.
+//     -- cluster barrier: every row maximum is the max over the cluster's chunk
+//     maxima (the global max comes before any int8 rounding: no online softmax)
+//  2. e = EXP(s - m); QSUM: eq = i8(127e) and the chunk's sum of eq; NORM: each
+//     CTA forms the whole row's e (reading the other chunks' scores) for the
+//     ordered sum, pq = i8(127 e RECIP(sum)) (llm/ref_model.py:233-242;
+//     hf_generic.py:275-290); int32 pq.V of the chunk.
+//     -- cluster barrier --
+//  3. CTA 0 adds the partials (exact in any order) and dequantizes: NORM
+//     f32(acc)*a_v; QSUM (f32(acc)*(RECIP(sum)*127))*a_v.
+//     -- cluster barrier: the others keep their shared memory until CTA 0 is done
 // Cache layout: [kv_heads, seq_len, head_dim] int8 per layer.
+#include <cooperative_groups.h>
+
 #include "pdl.cuh"
 #include "w8a8_internal.h"
 #include "w8a8_math.cuh"
 
+namespace cg = cooperative_groups;
+
 namespace w8a8 {
 
-__device__ unsigned int g_attn_errors;                         // bit 2: a chunk barrier gave up
-
 constexpr int kMaxG = 8;                                       // query heads per KV head
-constexpr int kAttnThreads = kChunk;                           // one thread per position
+constexpr int kAttnThreads = 256;
 constexpr int kAttnWarps = kAttnThreads / 32;
+constexpr int kMaxChunk = 512;
 
-static size_t al256(size_t b) { return (b + 255) & ~size_t(255); }
+struct AttnGeom {
+    int cs, chunk;
+};
 
-size_t attn_scratch_bytes(int rows, int heads, int kv_heads, int head_dim, int seq_len) {
-    const size_t M = rows, H = heads, hd = head_dim, T = seq_len;
-    return al256(M * H * T * 4) + al256(M * H * 4) + al256(M * H * 4) + al256(M * H * hd * 4) +
-           al256((size_t)kv_heads * 128);
+__host__ __device__ inline AttnGeom attn_geom(int seq_len) {
+    AttnGeom g;
+    const int blocks = (seq_len + 127) / 128;                  // 128-position blocks
+    g.cs = blocks < kMaxCluster ? blocks : kMaxCluster;
+    g.chunk = ((blocks + g.cs - 1) / g.cs) * 128;
+    return g;
 }
 
-void attn_carve(AttnParams& p, void* scratch) {
-    const size_t M = p.rows, H = p.heads, hd = p.head_dim, T = p.seq_len;
-    p.nsplit = (int)((T + kChunk - 1) / kChunk);
-    char* c = static_cast<char*>(scratch);
-    p.sc = reinterpret_cast<float*>(c);
-    c += al256(M * H * T * 4);
-    p.gmax = reinterpret_cast<uint32_t*>(c);
-    c += al256(M * H * 4);
-    p.psum = reinterpret_cast<int32_t*>(c);
-    c += al256(M * H * 4);
-    p.acc = reinterpret_cast<int32_t*>(c);
-    c += al256(M * H * hd * 4);
-    p.sync = reinterpret_cast<uint32_t*>(c);
+struct AttnSmem {                                              // offsets into the dynamic shared memory
+    size_t ks, vs, qs, fbuf, scs, ps, tab, gain, etab, pvp, ebuf, total;
+};
+
+__host__ __device__ inline AttnSmem attn_smem(int M, int G, int hd, int T, int chunk, int variant) {
+    auto a16 = [](size_t b) { return (b + 15) & ~size_t(15); };
+    AttnSmem s{};
+    size_t o = 0;
+    s.ks = o;   o += a16((size_t)chunk * (hd + 16));          // K tile, padded rows
+    s.vs = o;   o += a16((size_t)chunk * hd);                 // V tile
+    s.qs = o;   o += a16((size_t)M * G * hd);                 // int8 q rows
+    s.fbuf = o; o += a16((size_t)kAttnWarps * hd * 4);        // per-warp fp32 head vector
+    s.scs = o;  o += a16((size_t)M * G * chunk * 4);          // scores of the chunk
+    s.ps = o;   o += a16((size_t)M * G * chunk);              // int8 probabilities of the chunk
+    s.tab = o;  o += a16((size_t)M * 2 * hd * 4);             // cos | sin rows of each row's position
+    s.gain = o; o += a16((size_t)2 * hd * 4);                 // q_norm | k_norm gains
+    s.etab = o; o += a16(128 * 4);                            // the EXP table (T | S)
+    s.pvp = o;  o += a16((size_t)M * G * hd * 4);             // int32 p.V partials of the chunk
+    s.ebuf = o; o += variant == 0 ? a16((size_t)T * 4) : 0;   // NORM: the whole row's e
+    s.total = o;
+    return s;
 }
 
-// order-preserving uint encoding of a float for atomicMax (NaN above all, as
-// np.max propagates it; 0 is below every encoded value)
-__device__ __forceinline__ uint32_t ord_enc(float v) {
-    if (v != v) return 0xFFFFFFFFu;
-    const uint32_t u = __float_as_uint(v);
-    return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+size_t attn_smem_needed(int rows, int heads, int kv_heads, int head_dim, int seq_len, int variant) {
+    const AttnGeom g = attn_geom(seq_len);
+    return attn_smem(rows, heads / kv_heads, head_dim, seq_len, g.chunk, variant).total;
 }
-__device__ __forceinline__ float ord_dec(uint32_t e) {
-    if (e == 0xFFFFFFFFu) return __uint_as_float(kQNaN);
-    return __uint_as_float((e & 0x80000000u) ? (e & 0x7FFFFFFFu) : ~e);
+
+bool attn_supported(int rows, int heads, int kv_heads, int head_dim, int seq_len, int variant) {
+    const AttnGeom g = attn_geom(seq_len);
+    return g.chunk <= kMaxChunk && attn_smem_needed(rows, heads, kv_heads, head_dim, seq_len, variant) <= 200 * 1024;
 }
 
 __device__ __forceinline__ float warp_max(float v) {
@@ -104,35 +119,16 @@ __device__ __forceinline__ void warp_norm_rope(float* buf, int hd, const float* 
     __syncwarp();
 }
 
-struct AttnSmem {                                              // offsets into the dynamic shared memory
-    size_t ks, vs, qs, fbuf, scs, ps, tab, gain, ebuf, total;
-};
-
-__host__ __device__ inline AttnSmem attn_smem(int M, int G, int hd, int T, int variant) {
-    auto a16 = [](size_t b) { return (b + 15) & ~size_t(15); };
-    AttnSmem s{};
-    size_t o = 0;
-    s.ks = o;   o += a16((size_t)kChunk * (hd + 16));         // K tile, padded rows
-    s.vs = o;   o += a16((size_t)kChunk * hd);                // V tile
-    s.qs = o;   o += a16((size_t)M * G * hd);                 // int8 q rows
-    s.fbuf = o; o += a16((size_t)kAttnWarps * hd * 4);        // per-warp fp32 head vector
-    s.scs = o;  o += a16((size_t)M * G * kChunk * 4);         // scores of the chunk
-    s.ps = o;   o += a16((size_t)M * G * kChunk);             // int8 probabilities of the chunk
-    s.tab = o;  o += a16((size_t)M * 2 * hd * 4);             // cos | sin rows of each row's position
-    s.gain = o; o += a16((size_t)2 * hd * 4);                 // q_norm | k_norm gains
-    s.ebuf = o; o += variant == 0 ? a16((size_t)T * 4) : 0;   // NORM: the whole row's e
-    s.total = o;
-    return s;
-}
-
 __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
     extern __shared__ __align__(16) unsigned char sm[];
+    cg::cluster_group cl = cg::this_cluster();
     const int hd = p.head_dim, H = p.heads, Hk = p.kv_heads, G = H / Hk, M = p.rows, T = p.seq_len;
-    const int kvh = blockIdx.x, split = blockIdx.y, t0 = split * kChunk, tid = threadIdx.x;
+    const int CH = p.chunk, CS = p.nsplit, MG = M * G;
+    const int kvh = blockIdx.x, rank = (int)cl.block_rank(), t0 = rank * CH, tid = threadIdx.x;
     const int lane = tid & 31, warp = tid >> 5;
     const int kstride = hd + 16, vpr = hd / 16;
     const int qkv_dim = (H + 2 * Hk) * hd, q_dim = H * hd, kv_dim = Hk * hd;
-    const AttnSmem L = attn_smem(M, G, hd, T, p.variant);
+    const AttnSmem L = attn_smem(M, G, hd, T, CH, p.variant);
     int8_t* ks = reinterpret_cast<int8_t*>(sm + L.ks);
     int8_t* vs = reinterpret_cast<int8_t*>(sm + L.vs);
     int8_t* qs = reinterpret_cast<int8_t*>(sm + L.qs);
@@ -141,20 +137,27 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
     int8_t* ps = reinterpret_cast<int8_t*>(sm + L.ps);
     float* tabs = reinterpret_cast<float*>(sm + L.tab);         // row m: cos at [2m hd], sin at [(2m+1) hd]
     float* gains = reinterpret_cast<float*>(sm + L.gain);       // q_norm | k_norm
+    uint32_t* etab = reinterpret_cast<uint32_t*>(sm + L.etab);  // EXP T | S
+    int32_t* pvp = reinterpret_cast<int32_t*>(sm + L.pvp);
     float* ebuf = reinterpret_cast<float*>(sm + L.ebuf);
+    __shared__ float lmax[kMaxRows * kMaxG];
+    __shared__ float gmx[kMaxRows * kMaxG];
+    __shared__ int lsum[kMaxRows * kMaxG];
     __shared__ float sq[kMaxRows * kMaxG];
     __shared__ float wmax[kAttnWarps][kMaxRows * kMaxG];
     __shared__ int redi[32];
     __shared__ float rsum;
     __shared__ int lim_s[kMaxRows];
-    unsigned int* bar_count = p.sync + kvh * 32;
-    volatile unsigned int* bar_gen = p.sync + kvh * 32 + 1;
 
-    // ---- before the wait: positions, cache tiles of earlier positions, tables
+    // ---- before the wait: positions, cache tiles of earlier positions, constant tables
     int maxpos = 0;
     for (int m = 0; m < M; ++m) maxpos = max(maxpos, p.pos[m]);
-    const int nvalid = min(kChunk, maxpos + 1 - t0);
-    if (tid < M) lim_s[tid] = min(nvalid, p.pos[tid] + 1 - t0);   // positions of the chunk row m attends
+    const int nvalid = min(CH, maxpos + 1 - t0);
+    if (tid < M) lim_s[tid] = min(nvalid, p.pos[tid] + 1 - t0);  // positions of the chunk row m attends
+    if (tid < 64) {
+        etab[tid] = g_exp_t[tid];
+        etab[64 + tid] = g_exp_s[tid];
+    }
     if (nvalid > 0) {
         const int8_t* kbase = p.kc + ((size_t)kvh * T + t0) * hd;
         const int8_t* vbase = p.vc + ((size_t)kvh * T + t0) * hd;
@@ -177,11 +180,10 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
     pdl_wait();
     pdl_trigger();
     __syncthreads();
-    bool ok = true;
     if (nvalid > 0) {
         float* buf = fbuf + warp * hd;
         // q path of every row and query head of this KV head
-        for (int r = warp; r < M * G; r += kAttnWarps) {
+        for (int r = warp; r < MG; r += kAttnWarps) {
             const int m = r / G, h = kvh * G + r % G;
             const float* src = p.qkv + (size_t)m * qkv_dim + (size_t)h * hd;
             for (int c = lane; c < hd; c += 32) buf[c] = src[c];
@@ -200,7 +202,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
         // K and V rows of the positions in this chunk: into the cache and the tiles
         for (int m = warp; m < M; m += kAttnWarps) {
             const int pos = p.pos[m];
-            if (pos < t0 || pos >= t0 + kChunk) continue;
+            if (pos < t0 || pos >= t0 + CH) continue;
             const float* ksrc = p.qkv + (size_t)m * qkv_dim + q_dim + (size_t)kvh * hd;
             for (int c = lane; c < hd; c += 32) buf[c] = ksrc[c];
             __syncwarp();
@@ -220,13 +222,13 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
             __syncwarp();
         }
         __syncthreads();
-        // scores of the chunk: thread t <-> position t0 + t
-        for (int r = 0; r < M * G; ++r) {
-            const int m = r / G, h = kvh * G + r % G;
-            float s = -INFINITY;
-            if (tid < lim_s[m]) {
+        // scores of the chunk: thread t <-> positions t0 + t, t0 + t + 256, ...
+        for (int r = 0; r < MG; ++r) {
+            const int lim = lim_s[r / G];
+            float mx = -INFINITY;
+            for (int t = tid; t < lim; t += kAttnThreads) {
                 int a = 0;
-                const int4* kr = reinterpret_cast<const int4*>(ks + tid * kstride);
+                const int4* kr = reinterpret_cast<const int4*>(ks + t * kstride);
                 const int4* qr = reinterpret_cast<const int4*>(qs + r * hd);
                 for (int c = 0; c < vpr; ++c) {
                     const int4 x = kr[c], y = qr[c];
@@ -235,34 +237,46 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
                     a = dp4a(x.z, y.z, a);
                     a = dp4a(x.w, y.w, a);
                 }
-                s = fmul(fmul(i2f(a), sq[r]), p.a_k);
-                scs[r * kChunk + tid] = s;
-                if (p.variant == 0) p.sc[((size_t)m * H + h) * T + t0 + tid] = s;
+                const float s = fmul(fmul(i2f(a), sq[r]), p.a_k);
+                scs[r * CH + t] = s;
+                mx = nanmax(mx, s);
             }
-            s = warp_max(s);
-            if (lane == 0) wmax[warp][r] = s;
+            mx = warp_max(mx);
+            if (lane == 0) wmax[warp][r] = mx;
         }
         __syncthreads();
-        if (tid < M * G && lim_s[tid / G] > 0) {
+        if (tid < MG) {
             float s = wmax[0][tid];
             for (int w = 1; w < kAttnWarps; ++w) s = nanmax(s, wmax[w][tid]);
-            atomicMax(p.gmax + (size_t)(tid / G) * H + kvh * G + tid % G, ord_enc(s));
+            lmax[tid] = s;
         }
+    } else if (tid < MG) {
+        lmax[tid] = -INFINITY;
     }
-    ok = cta_barrier(bar_count, bar_gen, gridDim.y) && ok;     // A: the row maxima are final
+    cl.sync();                                                 // every chunk's maxima are in place
+    if (tid < MG) {
+        float mx = -INFINITY;
+        for (int j = 0; j < CS; ++j) mx = nanmax(mx, *cl.map_shared_rank(lmax + tid, j));
+        gmx[tid] = mx;
+    }
+    __syncthreads();
     if (nvalid > 0) {
-        for (int r = 0; r < M * G; ++r) {
-            const int m = r / G, h = kvh * G + r % G;
+        for (int r = 0; r < MG; ++r) {
+            const int m = r / G;
             const int lim = lim_s[m];
             if (lim <= 0) {
-                for (int t = tid; t < kChunk; t += kAttnThreads) ps[r * kChunk + t] = 0;
+                for (int t = tid; t < CH; t += kAttnThreads) ps[r * CH + t] = 0;
+                if (tid == 0) lsum[r] = 0;
                 continue;
             }
-            const float mx = ord_dec(__ldcg(p.gmax + (size_t)m * H + h));
+            const float mx = gmx[r];
             if (p.variant == 0) {                              // NORM: the whole row for the ordered sum
                 const int n = p.pos[m] + 1;
-                const float* sr = p.sc + ((size_t)m * H + h) * T;
-                for (int t = tid; t < n; t += kAttnThreads) ebuf[t] = sfu_exp(fsub(__ldcg(sr + t), mx));
+                for (int t = tid; t < n; t += kAttnThreads) {
+                    const int j = t / CH;
+                    const float s = *cl.map_shared_rank(scs + r * CH + (t - j * CH), j);
+                    ebuf[t] = sfu_exp_tab(fsub(s, mx), etab, etab + 64);
+                }
                 __syncthreads();
                 if (warp == 0) {
                     const float ssum = red_sum16([&](int i) { return ebuf[i]; }, n, lane);
@@ -270,77 +284,82 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
                 }
                 __syncthreads();
                 const float rc = rsum;
-                ps[r * kChunk + tid] = tid < lim ? (int8_t)to_i8(fmul(fmul(ebuf[t0 + tid], rc), 127.f)) : (int8_t)0;
+                for (int t = tid; t < CH; t += kAttnThreads)
+                    ps[r * CH + t] = t < lim ? (int8_t)to_i8(fmul(fmul(ebuf[t0 + t], rc), 127.f)) : (int8_t)0;
                 __syncthreads();
             } else {                                           // QSUM: this chunk's e only
-                int q = 0;
-                if (tid < lim) q = to_i8(fmul(sfu_exp(fsub(scs[r * kChunk + tid], mx)), 127.f));
-                ps[r * kChunk + tid] = (int8_t)q;
-                q = block_sum_i(q, redi);
-                if (tid == 0) atomicAdd(p.psum + (size_t)m * H + h, q);
+                int part = 0;
+                for (int t = tid; t < CH; t += kAttnThreads) {
+                    int q = 0;
+                    if (t < lim) q = to_i8(fmul(sfu_exp_tab(fsub(scs[r * CH + t], mx), etab, etab + 64), 127.f));
+                    ps[r * CH + t] = (int8_t)q;
+                    part += q;
+                }
+                part = block_sum_i(part, redi);
+                if (tid == 0) lsum[r] = part;
             }
         }
         __syncthreads();
         for (int c = tid; c < hd; c += kAttnThreads) {
-            for (int r = 0; r < M * G; ++r) {
-                const int m = r / G, h = kvh * G + r % G;
-                const int lim = lim_s[m];
-                if (lim <= 0) continue;
+            for (int r = 0; r < MG; ++r) {
+                const int lim = lim_s[r / G];
                 int a = 0;
 #pragma unroll 8
-                for (int t = 0; t < lim; ++t) a += (int)ps[r * kChunk + t] * (int)vs[t * hd + c];
-                atomicAdd(p.acc + ((size_t)m * H + h) * hd + c, a);
+                for (int t = 0; t < lim; ++t) a += (int)ps[r * CH + t] * (int)vs[t * hd + c];
+                pvp[r * hd + c] = a;
             }
         }
+    } else {
+        for (int i = tid; i < MG * hd; i += kAttnThreads) pvp[i] = 0;
+        if (tid < MG) lsum[tid] = 0;
     }
-    ok = cta_barrier(bar_count, bar_gen, gridDim.y) && ok;     // B: the sums are final
-    if (!ok && tid == 0) atomicOr(&g_attn_errors, 4u);
-    if (split != 0) return;
-    for (int r = 0; r < M * G; ++r) {
-        const int m = r / G, h = kvh * G + r % G;
-        const size_t mh = (size_t)m * H + h;
-        float rq = 0.f;
-        if (p.variant == 1) rq = fmul(sfu_recip(i2f(__ldcg(p.psum + mh))), 127.f);   // sum <= 127 T: exact
-        for (int c = tid; c < hd; c += kAttnThreads) {
-            const float o = i2f(__ldcg(p.acc + mh * hd + c));
-            p.att[mh * hd + c] = p.variant == 0 ? fmul(o, p.a_v) : fmul(fmul(o, rq), p.a_v);
-            p.acc[mh * hd + c] = 0;
-        }
-        if (tid == 0) {
-            p.psum[mh] = 0;
-            p.gmax[mh] = 0u;
+    cl.sync();                                                 // every chunk's partials are in place
+    if (rank == 0) {
+        for (int i = tid; i < MG * hd; i += kAttnThreads) {
+            const int r = i / hd, c = i % hd;
+            const int m = r / G, h = kvh * G + r % G;
+            int acc = 0, ssum = 0;
+            for (int j = 0; j < CS; ++j) {
+                acc += *cl.map_shared_rank(pvp + i, j);
+                if (p.variant == 1) ssum += *cl.map_shared_rank(lsum + r, j);
+            }
+            const float o = i2f(acc);
+            float out;
+            if (p.variant == 0) {
+                out = fmul(o, p.a_v);
+            } else {
+                const float rq = fmul(sfu_recip(i2f(ssum)), 127.f);   // sum <= 127 T: exact in fp32
+                out = fmul(fmul(o, rq), p.a_v);
+            }
+            p.att[((size_t)m * H + h) * hd + c] = out;
         }
     }
+    cl.sync();                                                 // CTA 0 is done reading the others' memory
 }
 
-static int attn_occupancy(size_t smem) {
-    int per_sm = 0, dev = 0, sms = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, attn_kernel, kAttnThreads, smem);
-    return per_sm * sms;
-}
-
-int attn_max_ctas(int rows, int heads, int kv_heads, int head_dim, int seq_len, int variant) {
-    const AttnSmem L = attn_smem(rows, heads / kv_heads, head_dim, seq_len, variant);
-    if (L.total > 200 * 1024) return 0;
-    cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.total);
-    return attn_occupancy(L.total);
-}
-
-cudaError_t launch_attn(const AttnParams& p, cudaStream_t st) {
-    const int G = p.heads / p.kv_heads;
-    const AttnSmem L = attn_smem(p.rows, G, p.head_dim, p.seq_len, p.variant);
+cudaError_t launch_attn(const AttnParams& q, cudaStream_t st) {
+    AttnParams p = q;
+    const AttnGeom g = attn_geom(p.seq_len);
+    p.nsplit = g.cs;
+    p.chunk = g.chunk;
+    const AttnSmem L = attn_smem(p.rows, p.heads / p.kv_heads, p.head_dim, p.seq_len, p.chunk, p.variant);
     cudaError_t e = cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.total);
     if (e != cudaSuccess) return e;
-    return launch_k(attn_kernel, dim3(p.kv_heads, p.nsplit), dim3(kAttnThreads), L.total, st, p);
-}
-
-unsigned int attn_read_clear_errors() {
-    unsigned int v = 0, zero = 0;
-    cudaMemcpyFromSymbol(&v, g_attn_errors, sizeof(v));
-    cudaMemcpyToSymbol(g_attn_errors, &zero, sizeof(zero));
-    return v;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(p.kv_heads, g.cs);
+    cfg.blockDim = dim3(kAttnThreads);
+    cfg.dynamicSmemBytes = L.total;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 1;
+    attr[0].val.clusterDim.y = g.cs;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = g_use_pdl ? 2 : 1;
+    return cudaLaunchKernelEx(&cfg, attn_kernel, p);
 }
 
 }  // namespace w8a8

@@ -61,7 +61,7 @@ int w8a8_error_flags(uint32_t* flags) {
     if (!flags) return W8A8_EINVAL;
     unsigned int v = 0;
     int st = cuda_status(read_clear_errors(&v));
-    *flags = v | gemv_read_clear_errors() | attn_read_clear_errors();
+    *flags = v | gemv_read_clear_errors();
     return st;
 }
 
@@ -125,8 +125,8 @@ int w8a8_ffn_swiglu(const float* x, const float* norm_g, float eps, int rows, in
 }
 
 size_t w8a8_attn_scratch_bytes(int rows, int heads, int kv_heads, int head_dim, int seq_len) {
-    if (rows <= 0 || heads <= 0 || kv_heads <= 0 || head_dim <= 0 || seq_len <= 0) return 0;
-    return attn_scratch_bytes(rows, heads, kv_heads, head_dim, seq_len);
+    (void)rows, (void)heads, (void)kv_heads, (void)head_dim, (void)seq_len;
+    return 0;                                                 // the cluster kernel needs no global scratch
 }
 
 int w8a8_attn(const W8A8AttnArgs* a, void* stream) {
@@ -135,16 +135,11 @@ int w8a8_attn(const W8A8AttnArgs* a, void* stream) {
         a->heads / a->kv_heads > 8 || a->head_dim <= 0 || a->head_dim > 256 || a->seq_len <= 0 ||
         (a->variant != 0 && a->variant != 1))
         return W8A8_EINVAL;
-    if (!a->pos || !a->qkv || !a->rope_cos || !a->rope_sin || !a->k_cache || !a->v_cache || !a->att || !a->scratch)
+    if (!a->pos || !a->qkv || !a->rope_cos || !a->rope_sin || !a->k_cache || !a->v_cache || !a->att)
         return W8A8_EINVAL;
     if ((a->q_norm == nullptr) != (a->k_norm == nullptr)) return W8A8_EINVAL;
-    if (a->head_dim % 16 || !al16(a->k_cache) || !al16(a->v_cache) || !al16(a->scratch)) return W8A8_EALIGN;
-    if (a->scratch_bytes < attn_scratch_bytes(a->rows, a->heads, a->kv_heads, a->head_dim, a->seq_len))
-        return W8A8_ESCRATCH;
-    // the chunks of a KV head wait for one another: the whole grid must be resident
-    const int nsplit = (a->seq_len + kChunk - 1) / kChunk;
-    if ((long)a->kv_heads * nsplit > attn_max_ctas(a->rows, a->heads, a->kv_heads, a->head_dim, a->seq_len, a->variant))
-        return W8A8_EINVAL;
+    if (a->head_dim % 16 || !al16(a->k_cache) || !al16(a->v_cache)) return W8A8_EALIGN;
+    if (!attn_supported(a->rows, a->heads, a->kv_heads, a->head_dim, a->seq_len, a->variant)) return W8A8_EINVAL;
     AttnParams p{};
     p.rows = a->rows, p.heads = a->heads, p.kv_heads = a->kv_heads, p.head_dim = a->head_dim;
     p.seq_len = a->seq_len, p.variant = a->variant, p.qk_norm = a->q_norm != nullptr;
@@ -152,7 +147,6 @@ int w8a8_attn(const W8A8AttnArgs* a, void* stream) {
     p.inv_hd = inv_of(a->head_dim), p.cos = a->rope_cos, p.sin = a->rope_sin;
     p.inv_sk = a->inv_sk, p.inv_sv = a->inv_sv, p.a_k = a->a_k, p.a_v = a->a_v;
     p.kc = a->k_cache, p.vc = a->v_cache, p.att = a->att;
-    attn_carve(p, a->scratch);
     return cuda_status(launch_attn(p, S(stream)));
 }
 

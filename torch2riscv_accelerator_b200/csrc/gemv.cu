@@ -71,6 +71,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1)
     float* sw = xf + (PRO == PRO_I8 ? 0 : k);                               // [nj] row scales
     float* sw2 = sw + nj;                                                   // [nj] (SwiGLU up rows)
     float* rs = sw2 + (kTwo ? nj : 0);                                      // [MR][nj] residual rows
+    float* gs = rs + (EPI == EPI_RESID ? MR * nj : 0);                      // [k] RMSNorm gain
     __shared__ __align__(8) uint64_t full[kMaxStages];         // tile landed (bulk-copy bytes)
     __shared__ __align__(8) uint64_t empty[kMaxStages];        // the 8 consumer warps are done with it
     __shared__ float sx[MR];
@@ -111,11 +112,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1)
             if (kTwo) sw2[j] = __ldg(p.s_w2 + n);
         }
     }
-    if (tid < 4) {                                             // warm L1 with the SFU tables of the prologue
-        const uint32_t* t = tid == 0 ? g_rec_t : tid == 1 ? g_rec_s : tid == 2 ? g_rsq_t : g_rsq_s;
-        const int lines = tid < 2 ? 2 : 4;
-        for (int l = 0; l < lines; ++l) asm volatile("prefetch.global.L1 [%0];" ::"l"(t + 32 * l));
-    }
+    if (PRO == PRO_RMSQ)                                       // the norm gain: a constant, staged now
+        for (int c = tid; c < k; c += kGemvThreads) gs[c] = __ldg(p.norm_g + c);
     pdl_wait();
     pdl_trigger();
     if (EPI == EPI_RESID) {                                    // residual rows: written by earlier kernels
@@ -125,7 +123,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1)
             if (n < p.n && m < p.m) rs[m * nj + jj] = p.resid[(size_t)m * p.n + n];
         }
     }
-    prologue<MR, PRO>(p, xs, xf, sx, red);
+    prologue<MR, PRO>(p, xs, xf, sx, red, gs);
 
     if (producer) {
         if (lane == 0) {                                       // refill each stage once its consumers are done
@@ -251,7 +249,8 @@ static Tiling tiling(const LinearParams& p, int mr, int pro, int epi) {
     t.grid = t.ntiles < sm_count() ? t.ntiles : sm_count();
     const size_t nj = (size_t)((t.ntiles + t.grid - 1) / t.grid) * t.tr;   // rows of a CTA, at most
     t.smem = (size_t)t.stages * stage + (size_t)mr * p.k + (pro == PRO_I8 ? 0 : (size_t)p.k * 4) +
-             nj * 4 * ((epi == EPI_SWIGLU ? 2 : 1) + (epi == EPI_RESID ? mr : 0));
+             nj * 4 * ((epi == EPI_SWIGLU ? 2 : 1) + (epi == EPI_RESID ? mr : 0)) +
+             (pro == PRO_RMSQ ? (size_t)p.k * 4 : 0);
     return t;
 }
 

@@ -11,7 +11,9 @@ constexpr int kWarps = 8;
 constexpr int kThreads = kWarps * 32;
 
 template <int MR, int PRO>
-__device__ __forceinline__ void prologue(const LinearParams& p, int8_t* xs, float* xf, float* sx, float* red) {
+// gain: the RMSNorm gain staged in shared memory, or null to read p.norm_g.
+__device__ __forceinline__ void prologue(const LinearParams& p, int8_t* xs, float* xf, float* sx, float* red,
+                                         const float* gain = nullptr) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int k = p.k;
     if (PRO == PRO_I8) {
@@ -49,11 +51,11 @@ __device__ __forceinline__ void prologue(const LinearParams& p, int8_t* xs, floa
             __syncthreads();
             r = rr;
         }
-        const float4* gr = reinterpret_cast<const float4*>(p.norm_g);
+        const float4* gr = reinterpret_cast<const float4*>(gain != nullptr ? gain : p.norm_g);
         auto val = [&](int c) {
             float4 v = xf4[c];
             if (PRO == PRO_RMSQ) {
-                float4 g = __ldg(gr + c);
+                float4 g = gr[c];
                 v.x = fmul(fmul(v.x, r), g.x);
                 v.y = fmul(fmul(v.y, r), g.y);
                 v.z = fmul(fmul(v.z, r), g.z);

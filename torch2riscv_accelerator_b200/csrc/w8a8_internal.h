@@ -52,23 +52,17 @@ struct AttnParams {
     int8_t* kc;               // [Hk, seq_len, hd] this layer's K cache
     int8_t* vc;               // [Hk, seq_len, hd]
     float* att;               // [M, H hd] out
-    // scratch (carved by the host wrapper from one buffer); every call leaves
-    // the accumulators and counters zero for the next one
-    float* sc;                // [M, H, seq_len] scores (NORM: the whole row for the ordered sum)
-    uint32_t* gmax;           // [M, H] ordered-int row maxima
-    int32_t* psum;            // [M, H] QSUM: sum of int8 e
-    int32_t* acc;             // [M, H, hd] int32 p.V sums
-    uint32_t* sync;           // [Hk, 32]: per KV head barrier (count, generation)
-    int nsplit;               // ceil(seq_len / kChunk)
+    int nsplit;               // CTAs per KV head (one thread-block cluster)
+    int chunk;                // cache positions per CTA
 };
 
-constexpr int kChunk = 128;   // cache positions per attention CTA
 constexpr int kMaxRows = 16;  // query rows per attention call
+constexpr int kMaxCluster = 8;  // attention CTAs per KV head (portable cluster size)
 
-size_t attn_scratch_bytes(int rows, int heads, int kv_heads, int head_dim, int seq_len);
-int attn_max_ctas(int rows, int heads, int kv_heads, int head_dim, int seq_len, int variant);
-unsigned int attn_read_clear_errors();
-void attn_carve(AttnParams& p, void* scratch);
+// 0 when the call is supported (the cache chunk of a CTA fits in shared memory),
+// else the shared memory it would need
+size_t attn_smem_needed(int rows, int heads, int kv_heads, int head_dim, int seq_len, int variant);
+bool attn_supported(int rows, int heads, int kv_heads, int head_dim, int seq_len, int variant);
 cudaError_t launch_attn(const AttnParams& p, cudaStream_t st);
 
 cudaError_t launch_embed(const int32_t* tokens, int m, const int8_t* emb_q, const float* emb_s, int vocab, int dim,

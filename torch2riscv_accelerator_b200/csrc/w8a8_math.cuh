@@ -26,18 +26,21 @@ constexpr int kLanes = 16;                  // D: the reduction lane count of th
 #define W8A8_C127 __uint_as_float(0x3C010204u)
 #define W8A8_LOG2E __uint_as_float(0x3FB8AA3Bu)
 
-__device__ __align__(16) static uint32_t g_exp_t[64] = W8A8_SFU_EXP_T_INIT;
-__device__ __align__(16) static uint32_t g_exp_s[64] = W8A8_SFU_EXP_S_INIT;
-__device__ __align__(16) static uint32_t g_rec_t[64] = W8A8_SFU_RECIP_T_INIT;
-__device__ __align__(16) static uint32_t g_rec_s[64] = W8A8_SFU_RECIP_S_INIT;
-__device__ __align__(16) static uint32_t g_rsq_t[128] = W8A8_SFU_RSQRT_T_INIT;
-__device__ __align__(16) static uint32_t g_rsq_s[128] = W8A8_SFU_RSQRT_S_INIT;
+// The SFU tables live in constant memory: the scalar uses (the scales of
+// quant_act, RMSNorm) index them uniformly across a warp. Kernels that evaluate
+// EXP per element stage the EXP table in shared memory (sfu_exp_tab).
+__constant__ __align__(16) static uint32_t g_exp_t[64] = W8A8_SFU_EXP_T_INIT;
+__constant__ __align__(16) static uint32_t g_exp_s[64] = W8A8_SFU_EXP_S_INIT;
+__constant__ __align__(16) static uint32_t g_rec_t[64] = W8A8_SFU_RECIP_T_INIT;
+__constant__ __align__(16) static uint32_t g_rec_s[64] = W8A8_SFU_RECIP_S_INIT;
+__constant__ __align__(16) static uint32_t g_rsq_t[128] = W8A8_SFU_RSQRT_T_INIT;
+__constant__ __align__(16) static uint32_t g_rsq_s[128] = W8A8_SFU_RSQRT_S_INIT;
 
 __device__ __forceinline__ float fmul(float a, float b) { return __fmul_rn(a, b); }
 __device__ __forceinline__ float fadd(float a, float b) { return __fadd_rn(a, b); }
 __device__ __forceinline__ float fsub(float a, float b) { return __fsub_rn(a, b); }
 __device__ __forceinline__ float i2f(int v) { return __int2float_rn(v); }
-__device__ __forceinline__ float tab(const uint32_t* t, int i) { return __uint_as_float(__ldg(t + i)); }
+__device__ __forceinline__ float tab(const uint32_t* t, int i) { return __uint_as_float(t[i]); }
 
 __device__ __forceinline__ int to_i8(float v) {
     if (v != v) return 0;
@@ -73,6 +76,24 @@ __device__ __forceinline__ float ldexp_ftz(float y, int n) {
 
 // EXP (llm/sfu.py:69-82): t = x*log2e, n = floor(t), f = t - n, u = 64f,
 // i = floor(u) (at most 63), r = u - i, y = T[i] + r*S[i], y * 2^n.
+// tt / ts: the table (T, S bit patterns) wherever the caller keeps it.
+__device__ __forceinline__ float sfu_exp_tab(float x, const uint32_t* tt, const uint32_t* ts) {
+    x = ftz(x);
+    if (x != x) return __uint_as_float(kQNaN);
+    if (x >= 89.f) return __uint_as_float(kPInf);
+    if (x <= -104.f) return 0.f;
+    float t = fmul(x, W8A8_LOG2E);
+    float fl = floorf(t);
+    int n = (int)fl;
+    float f = fsub(t, i2f(n));
+    float u = fmul(f, 64.f);
+    int i = (int)floorf(u);
+    i = i < 0 ? 0 : (i > 63 ? 63 : i);
+    float r = fsub(u, i2f(i));
+    float y = fadd(__uint_as_float(tt[i]), fmul(r, __uint_as_float(ts[i])));
+    return ldexp_ftz(y, n);
+}
+
 __device__ __forceinline__ float sfu_exp(float x) {
     x = ftz(x);
     if (x != x) return __uint_as_float(kQNaN);
