@@ -118,7 +118,8 @@ typedef struct {
     float inv_sk, inv_sv;      /* F(1/s_k), F(1/s_v) */
     float a_k, a_v;            /* F(s_k/sqrt(head_dim)), F(s_v/127) */
     int8_t* k_cache;           /* [kv_heads, seq_len, head_dim] this layer's K, written at pos */
-    int8_t* v_cache;
+    int8_t* v_cache;           /* [kv_heads, head_dim, seq_len] this layer's V, transposed
+                                  (seq_len a multiple of 16), written at pos */
     float* att;                /* [rows, heads head_dim] out */
     void* scratch;             /* unused (w8a8_attn_scratch_bytes() is 0); kept for the ABI layout */
     size_t scratch_bytes;

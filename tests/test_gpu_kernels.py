@@ -211,8 +211,8 @@ def test_attention_bit_exact(case):
     cos, sin = rope_tables(cfg)
     consts = kv_consts(F(0.05), F(0.03), hd)
     # device: cache [Hk, T, hd]
-    dk = cu(kc.reshape(T, Hk, hd).transpose(1, 0, 2))
-    dv = cu(vc.reshape(T, Hk, hd).transpose(1, 0, 2))
+    dk = cu(kc.reshape(T, Hk, hd).transpose(1, 0, 2))                  # [Hk, T, hd]
+    dv = cu(vc.reshape(T, Hk, hd).transpose(1, 2, 0))                  # [Hk, hd, T]
     att = torch.zeros(M, cfg.q_dim, device=DEV)
     scratch = ops.attn_scratch(M, H, Hk, hd, T, DEV)
     dpos, dqkv, dcos, dsin = cu(np.array(pos, np.int32)), cu(qkv), cu(cos), cu(sin)
@@ -222,7 +222,7 @@ def test_attention_bit_exact(case):
     got = host(att)
     want = OM.attn_layer(cfg, qkv, pos, kc, vc, consts, cos, sin, qn, kn)
     gk = host(dk).transpose(1, 0, 2).reshape(T, -1)
-    gv = host(dv).transpose(1, 0, 2).reshape(T, -1)
+    gv = host(dv).transpose(2, 0, 1).reshape(T, -1)
     assert np.array_equal(gk, kc) and np.array_equal(gv, vc), "KV rows"
     ok, bad = same_bits(got, want)
     assert ok, (bad, got.ravel()[bad], want.ravel()[bad])

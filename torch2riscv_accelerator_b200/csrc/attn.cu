@@ -24,7 +24,9 @@
 //  3. CTA 0 adds the partials (exact in any order) and dequantizes: NORM
 //     f32(acc)*a_v; QSUM (f32(acc)*(RECIP(sum)*127))*a_v.
 //     -- cluster barrier: the others keep their shared memory until CTA 0 is done
-// Cache layout: [kv_heads, seq_len, head_dim] int8 per layer.
+// Cache layout per layer: K [kv_heads, seq_len, head_dim] int8 (a position's
+// row contiguous), V transposed [kv_heads, head_dim, seq_len] int8 (a channel's
+// positions contiguous, so p.V is a dot product over positions).
 #include <cooperative_groups.h>
 
 #include "pdl.cuh"
@@ -60,8 +62,8 @@ __host__ __device__ inline AttnSmem attn_smem(int M, int G, int hd, int T, int c
     auto a16 = [](size_t b) { return (b + 15) & ~size_t(15); };
     AttnSmem s{};
     size_t o = 0;
-    s.ks = o;   o += a16((size_t)chunk * (hd + 16));          // K tile, padded rows
-    s.vs = o;   o += a16((size_t)chunk * hd);                 // V tile
+    s.ks = o;   o += a16((size_t)chunk * hd);                 // K tile [chunk][hd]
+    s.vs = o;   o += a16((size_t)hd * (chunk + 16));          // V^T tile [hd][chunk + 16] (padded rows)
     s.qs = o;   o += a16((size_t)M * G * hd);                 // int8 q rows
     s.fbuf = o; o += a16((size_t)kAttnWarps * hd * 4);        // per-warp fp32 head vector
     s.scs = o;  o += a16((size_t)M * G * chunk * 4);          // scores of the chunk
@@ -126,11 +128,11 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
     const int CH = p.chunk, CS = p.nsplit, MG = M * G;
     const int kvh = blockIdx.x, rank = (int)cl.block_rank(), t0 = rank * CH, tid = threadIdx.x;
     const int lane = tid & 31, warp = tid >> 5;
-    const int kstride = hd + 16, vpr = hd / 16;
+    const int vpr = hd / 16, vstride = CH + 16;
     const int qkv_dim = (H + 2 * Hk) * hd, q_dim = H * hd, kv_dim = Hk * hd;
     const AttnSmem L = attn_smem(M, G, hd, T, CH, p.variant);
-    int8_t* ks = reinterpret_cast<int8_t*>(sm + L.ks);
-    int8_t* vs = reinterpret_cast<int8_t*>(sm + L.vs);
+    int8_t* ks = reinterpret_cast<int8_t*>(sm + L.ks);          // [CH][hd]
+    int8_t* vs = reinterpret_cast<int8_t*>(sm + L.vs);          // [hd][CH + 16]: V transposed
     int8_t* qs = reinterpret_cast<int8_t*>(sm + L.qs);
     float* fbuf = reinterpret_cast<float*>(sm + L.fbuf);
     float* scs = reinterpret_cast<float*>(sm + L.scs);
@@ -144,8 +146,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
     __shared__ float gmx[kMaxRows * kMaxG];
     __shared__ int lsum[kMaxRows * kMaxG];
     __shared__ float sq[kMaxRows * kMaxG];
-    __shared__ float wmax[kAttnWarps][kMaxRows * kMaxG];
-    __shared__ int redi[32];
+    __shared__ float wred[kAttnWarps][kMaxRows * kMaxG];
+    __shared__ int wsum[kAttnWarps][kMaxRows * kMaxG];
     __shared__ float rsum;
     __shared__ int lim_s[kMaxRows];
 
@@ -153,18 +155,20 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
     int maxpos = 0;
     for (int m = 0; m < M; ++m) maxpos = max(maxpos, p.pos[m]);
     const int nvalid = min(CH, maxpos + 1 - t0);
+    const int nv16 = (nvalid + 15) & ~15;                      // V^T rows are read in 16-position words
     if (tid < M) lim_s[tid] = min(nvalid, p.pos[tid] + 1 - t0);  // positions of the chunk row m attends
     if (tid < 64) {
         etab[tid] = g_exp_t[tid];
         etab[64 + tid] = g_exp_s[tid];
     }
     if (nvalid > 0) {
-        const int8_t* kbase = p.kc + ((size_t)kvh * T + t0) * hd;
-        const int8_t* vbase = p.vc + ((size_t)kvh * T + t0) * hd;
-        for (int i = tid; i < nvalid * vpr; i += kAttnThreads) {
-            const int t = i / vpr, c = i % vpr;
-            *reinterpret_cast<int4*>(ks + t * kstride + c * 16) = __ldg(reinterpret_cast<const int4*>(kbase) + i);
-            reinterpret_cast<int4*>(vs)[i] = __ldg(reinterpret_cast<const int4*>(vbase) + i);
+        const int4* kbase = reinterpret_cast<const int4*>(p.kc + ((size_t)kvh * T + t0) * hd);
+        for (int i = tid; i < nvalid * vpr; i += kAttnThreads) reinterpret_cast<int4*>(ks)[i] = __ldg(kbase + i);
+        const int vw = nv16 / 16;                              // 16-byte words per V^T row
+        for (int i = tid; i < hd * vw; i += kAttnThreads) {
+            const int c = i / vw, w = i % vw;
+            *reinterpret_cast<int4*>(vs + c * vstride + w * 16) =
+                __ldg(reinterpret_cast<const int4*>(p.vc + ((size_t)kvh * hd + c) * T + t0) + w);
         }
         for (int i = tid; i < M * hd; i += kAttnThreads) {
             const int m = i / hd, c = i % hd, pos = p.pos[m];
@@ -209,28 +213,30 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
             warp_norm_rope(buf, hd, p.qk_norm ? gains + hd : nullptr, p.eps, p.inv_hd, tabs + 2 * m * hd,
                            tabs + (2 * m + 1) * hd, lane);
             int8_t* kdst = p.kc + ((size_t)kvh * T + pos) * hd;
-            int8_t* vdst = p.vc + ((size_t)kvh * T + pos) * hd;
             const float* vsrc = p.qkv + (size_t)m * qkv_dim + q_dim + kv_dim + (size_t)kvh * hd;
             for (int c = lane; c < hd; c += 32) {
                 const int8_t kq = (int8_t)to_i8(fmul(buf[c], p.inv_sk));
                 const int8_t vq = (int8_t)to_i8(fmul(vsrc[c], p.inv_sv));
                 kdst[c] = kq;
-                vdst[c] = vq;
-                ks[(pos - t0) * kstride + c] = kq;
-                vs[(pos - t0) * hd + c] = vq;
+                p.vc[((size_t)kvh * hd + c) * T + pos] = vq;
+                ks[(pos - t0) * hd + c] = kq;
+                vs[c * vstride + (pos - t0)] = vq;
             }
             __syncwarp();
         }
         __syncthreads();
-        // scores of the chunk: thread t <-> positions t0 + t, t0 + t + 256, ...
+        // scores: thread t <-> positions t0 + t (+ 256); the row's 16-byte words are
+        // read in a rotated order (conflict-free without padding)
         for (int r = 0; r < MG; ++r) {
             const int lim = lim_s[r / G];
             float mx = -INFINITY;
             for (int t = tid; t < lim; t += kAttnThreads) {
                 int a = 0;
-                const int4* kr = reinterpret_cast<const int4*>(ks + t * kstride);
+                const int4* kr = reinterpret_cast<const int4*>(ks + t * hd);
                 const int4* qr = reinterpret_cast<const int4*>(qs + r * hd);
-                for (int c = 0; c < vpr; ++c) {
+#pragma unroll 8
+                for (int j = 0; j < vpr; ++j) {
+                    const int c = (j + t) % vpr;
                     const int4 x = kr[c], y = qr[c];
                     a = dp4a(x.x, y.x, a);
                     a = dp4a(x.y, y.y, a);
@@ -242,12 +248,12 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
                 mx = nanmax(mx, s);
             }
             mx = warp_max(mx);
-            if (lane == 0) wmax[warp][r] = mx;
+            if (lane == 0) wred[warp][r] = mx;
         }
         __syncthreads();
         if (tid < MG) {
-            float s = wmax[0][tid];
-            for (int w = 1; w < kAttnWarps; ++w) s = nanmax(s, wmax[w][tid]);
+            float s = wred[0][tid];
+            for (int w = 1; w < kAttnWarps; ++w) s = nanmax(s, wred[w][tid]);
             lmax[tid] = s;
         }
     } else if (tid < MG) {
@@ -261,53 +267,69 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
     }
     __syncthreads();
     if (nvalid > 0) {
-        for (int r = 0; r < MG; ++r) {
-            const int m = r / G;
-            const int lim = lim_s[m];
-            if (lim <= 0) {
-                for (int t = tid; t < CH; t += kAttnThreads) ps[r * CH + t] = 0;
-                if (tid == 0) lsum[r] = 0;
-                continue;
-            }
-            const float mx = gmx[r];
-            if (p.variant == 0) {                              // NORM: the whole row for the ordered sum
-                const int n = p.pos[m] + 1;
-                for (int t = tid; t < n; t += kAttnThreads) {
-                    const int j = t / CH;
-                    const float s = *cl.map_shared_rank(scs + r * CH + (t - j * CH), j);
-                    ebuf[t] = sfu_exp_tab(fsub(s, mx), etab, etab + 64);
+        if (p.variant == 0) {                                  // NORM: each row's whole e for the ordered sum
+            for (int r = 0; r < MG; ++r) {
+                const int m = r / G;
+                const int lim = lim_s[m];
+                if (lim > 0) {
+                    const int n = p.pos[m] + 1;
+                    const float mx = gmx[r];
+                    for (int t = tid; t < n; t += kAttnThreads) {
+                        const int j = t / CH;
+                        const float s = *cl.map_shared_rank(scs + r * CH + (t - j * CH), j);
+                        ebuf[t] = sfu_exp_tab(fsub(s, mx), etab, etab + 64);
+                    }
+                    __syncthreads();
+                    if (warp == 0) {
+                        const float ssum = red_sum16([&](int i) { return ebuf[i]; }, n, lane);
+                        if (lane == 0) rsum = sfu_recip(ssum);
+                    }
+                    __syncthreads();
                 }
-                __syncthreads();
-                if (warp == 0) {
-                    const float ssum = red_sum16([&](int i) { return ebuf[i]; }, n, lane);
-                    if (lane == 0) rsum = sfu_recip(ssum);
-                }
-                __syncthreads();
                 const float rc = rsum;
                 for (int t = tid; t < CH; t += kAttnThreads)
                     ps[r * CH + t] = t < lim ? (int8_t)to_i8(fmul(fmul(ebuf[t0 + t], rc), 127.f)) : (int8_t)0;
                 __syncthreads();
-            } else {                                           // QSUM: this chunk's e only
-                int part = 0;
+            }
+        } else {                                               // QSUM: this chunk's e only, all rows in one pass
+            for (int r = 0; r < MG; ++r) {
+                const int lim = lim_s[r / G];
+                const float mx = gmx[r];
+                int sum = 0;
                 for (int t = tid; t < CH; t += kAttnThreads) {
                     int q = 0;
                     if (t < lim) q = to_i8(fmul(sfu_exp_tab(fsub(scs[r * CH + t], mx), etab, etab + 64), 127.f));
                     ps[r * CH + t] = (int8_t)q;
-                    part += q;
+                    sum += q;
                 }
-                part = block_sum_i(part, redi);
-                if (tid == 0) lsum[r] = part;
+                sum = warp_sum_i(sum);
+                if (lane == 0) wsum[warp][r] = sum;
+            }
+            __syncthreads();
+            if (tid < MG) {
+                int sum = 0;
+                for (int w = 0; w < kAttnWarps; ++w) sum += wsum[w][tid];
+                lsum[tid] = sum;
             }
         }
         __syncthreads();
-        for (int c = tid; c < hd; c += kAttnThreads) {
-            for (int r = 0; r < MG; ++r) {
-                const int lim = lim_s[r / G];
-                int a = 0;
-#pragma unroll 8
-                for (int t = 0; t < lim; ++t) a += (int)ps[r * CH + t] * (int)vs[t * hd + c];
-                pvp[r * hd + c] = a;
+        // p.V: thread <-> (row r, channel c) pairs; dp4a over 16-position words of
+        // the int8 probabilities and the V^T row (padded: conflict-free)
+        for (int i = tid; i < MG * hd; i += kAttnThreads) {
+            const int r = i / hd, c = i % hd;
+            const int words = (lim_s[r / G] + 15) / 16;
+            const int4* pr = reinterpret_cast<const int4*>(ps + r * CH);
+            const int4* vr = reinterpret_cast<const int4*>(vs + c * vstride);
+            int a0 = 0, a1 = 0;
+#pragma unroll 4
+            for (int w = 0; w < words; ++w) {
+                const int4 x = pr[w], y = vr[w];
+                a0 = dp4a(x.x, y.x, a0);
+                a1 = dp4a(x.y, y.y, a1);
+                a0 = dp4a(x.z, y.z, a0);
+                a1 = dp4a(x.w, y.w, a1);
             }
+            pvp[i] = a0 + a1;
         }
     } else {
         for (int i = tid; i < MG * hd; i += kAttnThreads) pvp[i] = 0;

@@ -138,7 +138,7 @@ int w8a8_attn(const W8A8AttnArgs* a, void* stream) {
     if (!a->pos || !a->qkv || !a->rope_cos || !a->rope_sin || !a->k_cache || !a->v_cache || !a->att)
         return W8A8_EINVAL;
     if ((a->q_norm == nullptr) != (a->k_norm == nullptr)) return W8A8_EINVAL;
-    if (a->head_dim % 16 || !al16(a->k_cache) || !al16(a->v_cache)) return W8A8_EALIGN;
+    if (a->head_dim % 16 || a->seq_len % 16 || !al16(a->k_cache) || !al16(a->v_cache)) return W8A8_EALIGN;
     if (!attn_supported(a->rows, a->heads, a->kv_heads, a->head_dim, a->seq_len, a->variant)) return W8A8_EINVAL;
     AttnParams p{};
     p.rows = a->rows, p.heads = a->heads, p.kv_heads = a->kv_heads, p.head_dim = a->head_dim;

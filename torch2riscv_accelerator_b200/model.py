@@ -13,8 +13,9 @@ HBM layout (all resident):
   and up rows separate (the SwiGLU kernel reads both for the same channel);
 - the embedding int8 [vocab, dim] + fp32 [vocab], shared with a tied
   classifier;
-- KV cache int8 [layers, kv_heads, seq_len, head_dim] for K and for V (a head's
-  positions contiguous);
+- KV cache int8: K [layers, kv_heads, seq_len, head_dim] (a position's row
+  contiguous), V transposed [layers, kv_heads, head_dim, seq_len] (a channel's
+  positions contiguous: p.V is a dot product over positions);
 - RoPE tables fp32 [seq_len, head_dim], pair-repeated.
 Per layer and row: 1 fused rmsnorm+quant+GEMV (wqkv), 3 attention kernels,
 1 quant+GEMV+residual (wo), 1 SwiGLU kernel, 1 GEMV+residual (w2).
@@ -51,7 +52,7 @@ class DeviceDecoder:
         self.consts = [kv_consts(kv[l, 0], kv[l, 1], cfg.head_dim) for l in range(cfg.layers)]
         L, Hk, T, hd = cfg.layers, cfg.kv_heads, cfg.seq_len, cfg.head_dim
         self.kc = torch.zeros(L, Hk, T, hd, dtype=I8, device=self.dev)
-        self.vc = torch.zeros(L, Hk, T, hd, dtype=I8, device=self.dev)
+        self.vc = torch.zeros(L, Hk, hd, T, dtype=I8, device=self.dev)      # V transposed per head
         R = max_rows
         z = lambda *s, dt=F32: torch.zeros(*s, dtype=dt, device=self.dev)
         self.tokens, self.pos = z(R, dt=I32), z(R, dt=I32)
@@ -164,7 +165,7 @@ class DeviceDecoder:
     def kv_rows(self, layer, n):
         """The cache of a layer in the reference's layout: K, V int8 [n, kv_dim]."""
         k = self.kc[layer, :, :n].permute(1, 0, 2).reshape(n, -1)
-        v = self.vc[layer, :, :n].permute(1, 0, 2).reshape(n, -1)
+        v = self.vc[layer, :, :, :n].permute(2, 0, 1).reshape(n, -1)
         return k.cpu().numpy(), v.cpu().numpy()
 
     def weight_bytes(self):
