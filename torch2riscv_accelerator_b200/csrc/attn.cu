@@ -367,6 +367,10 @@ cudaError_t launch_attn(const AttnParams& q, cudaStream_t st) {
     const AttnSmem L = attn_smem(p.rows, p.heads / p.kv_heads, p.head_dim, p.seq_len, p.chunk, p.variant);
     cudaError_t e = cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.total);
     if (e != cudaSuccess) return e;
+    // one shared-memory carveout for every kernel of the chain: no L1 / shared
+    // reconfiguration of an SM between consecutive kernels
+    e = cudaFuncSetAttribute(attn_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(p.kv_heads, g.cs);
     cfg.blockDim = dim3(kAttnThreads);

@@ -260,6 +260,10 @@ static cudaError_t launch_g(const LinearParams& p, cudaStream_t st) {
     auto kern = gemv_kernel<MR, PRO, EPI>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)t.smem);
     if (e != cudaSuccess) return e;
+    // one shared-memory carveout for every kernel of the chain: no L1 / shared
+    // reconfiguration of an SM between consecutive kernels
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    if (e != cudaSuccess) return e;
     return launch_k(kern, dim3(t.grid), dim3(kGemvThreads), t.smem, st, p, t.tr, t.slices, t.stages, t.ntiles);
 }
 

@@ -161,6 +161,7 @@ static cudaError_t launch_t(const LinearParams& p, cudaStream_t st) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
         if (e != cudaSuccess) return e;
     }
+    cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     return launch_k(kern, dim3(grid), dim3(kThreads), smem, st, p);
 }
 

@@ -31,6 +31,7 @@ __global__ void embed_kernel(const int32_t* tokens, const int8_t* emb_q, const f
 
 cudaError_t launch_embed(const int32_t* tokens, int m, const int8_t* emb_q, const float* emb_s, int vocab, int dim,
                          float* x, cudaStream_t st) {
+    cudaFuncSetAttribute(embed_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     return launch_k(embed_kernel, dim3(m), dim3(256), 0, st, tokens, emb_q, emb_s, vocab, dim, x);
 }
 
@@ -165,6 +166,7 @@ __global__ void decode_advance_kernel(int32_t* tokens, int32_t* pos, unsigned lo
 
 cudaError_t launch_decode_advance(int32_t* tokens, int32_t* pos, unsigned long long* key, int32_t* next, int rows,
                                   cudaStream_t st) {
+    cudaFuncSetAttribute(decode_advance_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     return launch_k(decode_advance_kernel, dim3(1), dim3(32), 0, st, tokens, pos, key, next, rows);
 }
 
