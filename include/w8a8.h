@@ -95,7 +95,9 @@ int w8a8_linear_fused(const float* x, const float* norm_g, float eps, int rows, 
  * h = (g * RECIP(1 + EXP(-g))) * u -> amax -> h_q = i8(h * RECIP(amax * F(1/127))).
  * w_gate, w_up: [hidden, k]; h: [rows, hidden] fp32; h_q: [rows, hidden] int8,
  * s_h: [rows]. scratch: w8a8_ffn_scratch_bytes() bytes, zero before the first
- * call, left zero by every call. Replaces ModelCompiler.ffn_up with fused SiLU
+ * call, left zero by every call. With h_q, s_h and scratch all NULL the call
+ * stops at h (a following w8a8_linear_fused on h does the same quant_act in its
+ * prologue: the decode chain uses that, it saves the grid-wide amax). Replaces ModelCompiler.ffn_up with fused SiLU
  * (llm/compile_model.py:295-328) and the FFN region of the IREE plugin
  * (FfnPlan, compiler/plugins/sa/transforms/SahlKernels.h:130-141). */
 size_t w8a8_ffn_scratch_bytes(int rows);

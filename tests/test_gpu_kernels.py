@@ -263,3 +263,23 @@ def test_classifier_fused_argmax(m):
     want = N.linear(xq, s, w, sw)[0]
     assert same_bits(y, want)[0]
     assert [ops.key_token(v) for v in host(key)] == [int(np.argmax(r)) for r in want]
+
+
+def test_ffn_swiglu_without_requant_then_fused_down_projection():
+    """The decode chain's split: the SwiGLU kernel stops at h, the down
+    projection's prologue does quant_act(h): the same bytes as the full
+    dispatch followed by the int8 linear."""
+    rng = np.random.default_rng(31)
+    k, hidden, n = 1024, 3072, 1024
+    wg, sg = quantize_rows((rng.standard_normal((hidden, k)) * 0.05).astype(F))
+    wu, su = quantize_rows((rng.standard_normal((hidden, k)) * 0.05).astype(F))
+    wd, sd = quantize_rows((rng.standard_normal((n, hidden)) * 0.05).astype(F))
+    g = (1 + 0.1 * rng.standard_normal(k)).astype(F)
+    x = rng.standard_normal((1, k)).astype(F)
+    resid = rng.standard_normal((1, n)).astype(F)
+    h, hq, sh = ops.ffn_swiglu(cu(x), cu(g), 1e-6, cu(wg), cu(sg), cu(wu), cu(su), ops.ffn_scratch(1, DEV))
+    y1 = host(ops.linear(hq, sh, cu(wd), cu(sd), resid=cu(resid)))
+    h2, none_q, none_s = ops.ffn_swiglu(cu(x), cu(g), 1e-6, cu(wg), cu(sg), cu(wu), cu(su), None, requant=False)
+    assert none_q is None and none_s is None
+    y2 = host(ops.linear_fused(h2, cu(wd), cu(sd), resid=cu(resid)))
+    assert same_bits(host(h), host(h2))[0] and same_bits(y1, y2)[0]

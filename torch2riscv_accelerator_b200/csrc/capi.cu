@@ -113,14 +113,18 @@ int w8a8_ffn_swiglu(const float* x, const float* norm_g, float eps, int rows, in
                     int8_t* h_q, float* s_h, void* scratch, size_t scratch_bytes, void* stream) {
     int st = check_linear(rows, k, w_gate, s_gate, hidden, h);
     if (st) return st;
-    if (!x || !norm_g || !w_up || !s_up || !h_q || !s_h || !scratch) return W8A8_EINVAL;
-    if (!al16(x) || !al16(norm_g) || !al16(w_up) || !al16(scratch)) return W8A8_EALIGN;
-    if (scratch_bytes < w8a8_ffn_scratch_bytes(rows)) return W8A8_ESCRATCH;
+    if (!x || !norm_g || !w_up || !s_up || (h_q == nullptr) != (s_h == nullptr)) return W8A8_EINVAL;
+    if (h_q && !scratch) return W8A8_EINVAL;
+    if (!al16(x) || !al16(norm_g) || !al16(w_up) || (scratch && !al16(scratch))) return W8A8_EALIGN;
+    if (h_q && hidden % 4) return W8A8_EALIGN;
+    if (h_q && scratch_bytes < w8a8_ffn_scratch_bytes(rows)) return W8A8_ESCRATCH;
     LinearParams p{};
     p.m = rows, p.n = hidden, p.k = k, p.x = x, p.norm_g = norm_g, p.eps = eps, p.inv_k = inv_of(k);
     p.w = w_gate, p.s_w = s_gate, p.w2 = w_up, p.s_w2 = s_up, p.y = h, p.hq = h_q, p.s_h = s_h;
-    p.counter = static_cast<uint32_t*>(scratch);
-    p.amax_bits = reinterpret_cast<uint32_t*>(static_cast<char*>(scratch) + 256);
+    if (scratch) {
+        p.counter = static_cast<uint32_t*>(scratch);
+        p.amax_bits = reinterpret_cast<uint32_t*>(static_cast<char*>(scratch) + 256);
+    }
     return cuda_status(launch_linear(p, PRO_RMSQ, EPI_SWIGLU, S(stream)));
 }
 

@@ -114,6 +114,11 @@ __global__ void __launch_bounds__(kGemvThreads, 1)
     }
     if (PRO == PRO_RMSQ)                                       // the norm gain: a constant, staged now
         for (int c = tid; c < k; c += kGemvThreads) gs[c] = __ldg(p.norm_g + c);
+    if (PRO != PRO_I8 && warp == 0) {                          // bring the RECIP / RSQRT table lines in
+        uint32_t t = g_rec_t[lane * 2] ^ g_rec_s[lane * 2] ^ g_rsq_t[lane * 4] ^ g_rsq_s[lane * 4];
+        t = __reduce_xor_sync(0xffffffffu, t);
+        if (lane == 0) red[31] = __uint_as_float(t);          // (kept: red is rewritten by the prologue)
+    }
     pdl_wait();
     pdl_trigger();
     if (EPI == EPI_RESID) {                                    // residual rows: written by earlier kernels
@@ -195,7 +200,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1)
     if (EPI == EPI_STORE && p.argmax_key != nullptr) {
         if (tid < p.m && tid < MR) atomicMax(p.argmax_key + tid, bkey[tid]);
     }
-    if (EPI != EPI_SWIGLU) return;
+    if (EPI != EPI_SWIGLU || p.hq == nullptr) return;
     // the row amax across the grid; the last CTA requantizes h (quant_act)
     if (tid < p.m && tid < MR) atomicMax(p.amax_bits + tid, bamax[tid]);
     __threadfence();
@@ -208,9 +213,24 @@ __global__ void __launch_bounds__(kGemvThreads, 1)
         const float amax = __uint_as_float(__ldcg(p.amax_bits + m));
         const float s = fmul(amax, W8A8_C127);
         const float inv = sfu_recip(s);
-        const float* hr = p.y + (size_t)m * p.n;
-        int8_t* qr = p.hq + (size_t)m * p.n;
-        for (int j = tid; j < p.n; j += kGemvThreads) qr[j] = (int8_t)to_i8(fmul(__ldcg(hr + j), inv));
+        const float4* hr = reinterpret_cast<const float4*>(p.y + (size_t)m * p.n);
+        char4* qr = reinterpret_cast<char4*>(p.hq + (size_t)m * p.n);
+        const int n4 = p.n / 4;
+        for (int j0 = tid; j0 < n4; j0 += 4 * kGemvThreads) {   // four independent loads in flight
+            float4 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int j = j0 + u * kGemvThreads;
+                if (j < n4) v[u] = __ldcg(hr + j);
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int j = j0 + u * kGemvThreads;
+                if (j < n4)
+                    qr[j] = make_char4(to_i8(fmul(v[u].x, inv)), to_i8(fmul(v[u].y, inv)), to_i8(fmul(v[u].z, inv)),
+                                       to_i8(fmul(v[u].w, inv)));
+            }
+        }
         if (tid == 0) p.s_h[m] = s;
     }
     __syncthreads();

@@ -127,7 +127,7 @@ __global__ void __launch_bounds__(kThreads) linear_kernel(LinearParams p) {
         __syncthreads();
         if (tid < p.m && tid < MR) atomicMax(p.argmax_key + tid, bkey[tid]);
     }
-    if (EPI != EPI_SWIGLU) return;
+    if (EPI != EPI_SWIGLU || p.hq == nullptr) return;
     // row amax across the grid, then the last CTA requantizes (quant_act of h)
     __syncthreads();
     if (tid < p.m && tid < MR) atomicMax(p.amax_bits + tid, bamax[tid]);

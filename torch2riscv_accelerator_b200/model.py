@@ -17,8 +17,9 @@ HBM layout (all resident):
   contiguous), V transposed [layers, kv_heads, head_dim, seq_len] (a channel's
   positions contiguous: p.V is a dot product over positions);
 - RoPE tables fp32 [seq_len, head_dim], pair-repeated.
-Per layer and row: 1 fused rmsnorm+quant+GEMV (wqkv), 3 attention kernels,
-1 quant+GEMV+residual (wo), 1 SwiGLU kernel, 1 GEMV+residual (w2).
+Per layer and row: 1 fused rmsnorm+quant+GEMV (wqkv), 1 attention kernel,
+1 quant+GEMV+residual (wo), 1 rmsnorm+quant+gate/up GEMV+SiLU kernel, 1
+quant+GEMV+residual (w2, quantizing h in its prologue).
 """
 import numpy as np
 import torch
@@ -92,17 +93,17 @@ class DeviceDecoder:
             ops.linear_fused(x, w["wqkv"], w["s_wqkv"], norm_g=w["rms_att"], eps=c.eps, out=qkv)
             ops.attn(args[l])
             ops.linear_fused(att, w["wo"], w["s_wo"], resid=x, out=x)
-            ops.ffn_swiglu(x, w["rms_ffn"], c.eps, w["w1"], w["s_w1"], w["w3"], w["s_w3"], self.ffn_scratch,
-                           h=h, h_q=hq, s_h=s_h)
-            ops.linear(hq, s_h, w["w2"], w["s_w2"], out=x, resid=x)
+            ops.ffn_swiglu(x, w["rms_ffn"], c.eps, w["w1"], w["s_w1"], w["w3"], w["s_w3"], None, h=h,
+                           requant=False)
+            ops.linear_fused(h, w["w2"], w["s_w2"], resid=x, out=x)          # quant_act(h) in the prologue
         xl = self.x[rows - logits_rows:rows]
         ops.classifier(xl, self.cls_q, self.cls_s, self.rms_final, c.eps, out=self.logits[:logits_rows],
                        argmax_key=self.key[:logits_rows] if argmax else None)
 
     def kernel_launches(self, rows=1):
-        """Kernels one run() launches: embed, per layer the qkv GEMV, 2
-        attention kernels, wo, SwiGLU, w2, then the classifier."""
-        return 1 + 6 * self.cfg.layers + 1
+        """Kernels one run() launches: embed, per layer the qkv GEMV, the
+        attention, wo, SwiGLU, w2, then the classifier."""
+        return 1 + 5 * self.cfg.layers + 1
 
     def capture(self, rows, logits_rows=1):
         """Capture run(rows) as a CUDA graph (after one eager warm-up run)."""

@@ -99,18 +99,22 @@ def ffn_scratch(rows, device):
     return torch.zeros(n, dtype=torch.uint8, device=device)
 
 
-def ffn_swiglu(x, norm_g, eps, w_gate, s_gate, w_up, s_up, scratch, h=None, h_q=None, s_h=None):
-    """Decode SwiGLU dispatch: returns (h fp32, h_q int8, s_h)."""
+def ffn_swiglu(x, norm_g, eps, w_gate, s_gate, w_up, s_up, scratch, h=None, h_q=None, s_h=None, requant=True):
+    """Decode SwiGLU dispatch: returns (h fp32, h_q int8, s_h); with
+    requant=False only h (h_q, s_h None; the down projection quantizes h)."""
     _need(x, F32, "x")
     m, k = x.shape
     hidden = w_gate.shape[0]
     dev = x.device
     h = torch.empty(m, hidden, dtype=F32, device=dev) if h is None else h
-    h_q = torch.empty(m, hidden, dtype=I8, device=dev) if h_q is None else h_q
-    s_h = torch.empty(m, dtype=F32, device=dev) if s_h is None else s_h
+    if requant:
+        h_q = torch.empty(m, hidden, dtype=I8, device=dev) if h_q is None else h_q
+        s_h = torch.empty(m, dtype=F32, device=dev) if s_h is None else s_h
+    else:
+        h_q = s_h = scratch = None
     _lib.check("w8a8_ffn_swiglu", _lib.load().w8a8_ffn_swiglu(
         _p(x), _p(norm_g), float(eps), m, k, _p(w_gate), _p(s_gate), _p(w_up), _p(s_up), hidden, _p(h), _p(h_q),
-        _p(s_h), _p(scratch), scratch.numel(), _st()))
+        _p(s_h), _p(scratch), 0 if scratch is None else scratch.numel(), _st()))
     return h, h_q, s_h
 
 
