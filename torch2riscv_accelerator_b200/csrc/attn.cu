@@ -23,7 +23,8 @@
 //     -- cluster barrier --
 //  3. CTA 0 adds the partials (exact in any order) and dequantizes: NORM
 //     f32(acc)*a_v; QSUM (f32(acc)*(RECIP(sum)*127))*a_v.
-//     -- cluster barrier: the others keep their shared memory until CTA 0 is done
+// Every value a CTA needs from another is pushed into its shared memory with
+// remote stores before the barrier that publishes it; reads are then local.
 // Cache layout per layer: K [kv_heads, seq_len, head_dim] int8 (a position's
 // row contiguous), V transposed [kv_heads, head_dim, seq_len] int8 (a channel's
 // positions contiguous, so p.V is a dot product over positions).
@@ -65,13 +66,13 @@ __host__ __device__ inline AttnSmem attn_smem(int M, int G, int hd, int T, int c
     s.ks = o;   o += a16((size_t)chunk * hd);                 // K tile [chunk][hd]
     s.vs = o;   o += a16((size_t)hd * (chunk + 16));          // V^T tile [hd][chunk + 16] (padded rows)
     s.qs = o;   o += a16((size_t)M * G * hd);                 // int8 q rows
-    s.fbuf = o; o += a16((size_t)kAttnWarps * hd * 4);        // per-warp fp32 head vector
+    s.fbuf = o; o += a16((size_t)2 * kAttnWarps * hd * 4);    // per-warp fp32 head vectors (q | k)
     s.scs = o;  o += a16((size_t)M * G * chunk * 4);          // scores of the chunk
     s.ps = o;   o += a16((size_t)M * G * chunk);              // int8 probabilities of the chunk
     s.tab = o;  o += a16((size_t)M * 2 * hd * 4);             // cos | sin rows of each row's position
     s.gain = o; o += a16((size_t)2 * hd * 4);                 // q_norm | k_norm gains
     s.etab = o; o += a16(128 * 4);                            // the EXP table (T | S)
-    s.pvp = o;  o += a16((size_t)M * G * hd * 4);             // int32 p.V partials of the chunk
+    s.pvp = o;  o += a16((size_t)kMaxCluster * M * G * hd * 4);   // [CTA][row][c] int32 p.V partials (rank 0 sums)
     s.ebuf = o; o += variant == 0 ? a16((size_t)T * 4) : 0;   // NORM: the whole row's e
     s.total = o;
     return s;
@@ -142,15 +143,18 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
     uint32_t* etab = reinterpret_cast<uint32_t*>(sm + L.etab);  // EXP T | S
     int32_t* pvp = reinterpret_cast<int32_t*>(sm + L.pvp);
     float* ebuf = reinterpret_cast<float*>(sm + L.ebuf);
-    __shared__ float lmax[kMaxRows * kMaxG];
+    __shared__ float lmax[kMaxCluster][kMaxRows * kMaxG];     // every CTA's chunk maxima (pushed by each)
     __shared__ float gmx[kMaxRows * kMaxG];
-    __shared__ int lsum[kMaxRows * kMaxG];
+    __shared__ int lsum[kMaxCluster][kMaxRows * kMaxG];      // every CTA's sums of eq (at rank 0)
     __shared__ float sq[kMaxRows * kMaxG];
     __shared__ float wred[kAttnWarps][kMaxRows * kMaxG];
     __shared__ int wsum[kAttnWarps][kMaxRows * kMaxG];
     __shared__ float rsum;
     __shared__ int lim_s[kMaxRows];
 
+    // every CTA of the cluster must have started before any remote store into its
+    // shared memory: arrive now, wait just before the first push
+    asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
     // ---- before the wait: positions, cache tiles of earlier positions, constant tables
     int maxpos = 0;
     for (int m = 0; m < M; ++m) maxpos = max(maxpos, p.pos[m]);
@@ -160,6 +164,11 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
     if (tid < 64) {
         etab[tid] = g_exp_t[tid];
         etab[64 + tid] = g_exp_s[tid];
+    }
+    if (warp == 1) {                                           // bring the RECIP / RSQRT table lines in
+        uint32_t w = g_rec_t[lane * 2] ^ g_rec_s[lane * 2] ^ g_rsq_t[lane * 4] ^ g_rsq_s[lane * 4];
+        w = __reduce_xor_sync(0xffffffffu, w);
+        if (lane == 0) rsum = __uint_as_float(w);             // (rsum is rewritten before any use)
     }
     if (nvalid > 0) {
         const int4* kbase = reinterpret_cast<const int4*>(p.kc + ((size_t)kvh * T + t0) * hd);
@@ -186,7 +195,10 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
     __syncthreads();
     if (nvalid > 0) {
         float* buf = fbuf + warp * hd;
-        // q path of every row and query head of this KV head
+        // q path of every row and query head of this KV head (warps from 0), and
+        // the K / V rows of the positions in this chunk (warps from the last one)
+        // at the same time
+        float* kbuf = fbuf + (kAttnWarps + warp) * hd;              // the K row's own buffer
         for (int r = warp; r < MG; r += kAttnWarps) {
             const int m = r / G, h = kvh * G + r % G;
             const float* src = p.qkv + (size_t)m * qkv_dim + (size_t)h * hd;
@@ -204,18 +216,18 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
             __syncwarp();
         }
         // K and V rows of the positions in this chunk: into the cache and the tiles
-        for (int m = warp; m < M; m += kAttnWarps) {
+        for (int m = kAttnWarps - 1 - warp; m < M; m += kAttnWarps) {
             const int pos = p.pos[m];
             if (pos < t0 || pos >= t0 + CH) continue;
             const float* ksrc = p.qkv + (size_t)m * qkv_dim + q_dim + (size_t)kvh * hd;
-            for (int c = lane; c < hd; c += 32) buf[c] = ksrc[c];
+            for (int c = lane; c < hd; c += 32) kbuf[c] = ksrc[c];
             __syncwarp();
-            warp_norm_rope(buf, hd, p.qk_norm ? gains + hd : nullptr, p.eps, p.inv_hd, tabs + 2 * m * hd,
+            warp_norm_rope(kbuf, hd, p.qk_norm ? gains + hd : nullptr, p.eps, p.inv_hd, tabs + 2 * m * hd,
                            tabs + (2 * m + 1) * hd, lane);
             int8_t* kdst = p.kc + ((size_t)kvh * T + pos) * hd;
             const float* vsrc = p.qkv + (size_t)m * qkv_dim + q_dim + kv_dim + (size_t)kvh * hd;
             for (int c = lane; c < hd; c += 32) {
-                const int8_t kq = (int8_t)to_i8(fmul(buf[c], p.inv_sk));
+                const int8_t kq = (int8_t)to_i8(fmul(kbuf[c], p.inv_sk));
                 const int8_t vq = (int8_t)to_i8(fmul(vsrc[c], p.inv_sv));
                 kdst[c] = kq;
                 p.vc[((size_t)kvh * hd + c) * T + pos] = vq;
@@ -234,10 +246,11 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
                 int a = 0;
                 const int4* kr = reinterpret_cast<const int4*>(ks + t * hd);
                 const int4* qr = reinterpret_cast<const int4*>(qs + r * hd);
+                int c = t % vpr;
 #pragma unroll 8
                 for (int j = 0; j < vpr; ++j) {
-                    const int c = (j + t) % vpr;
                     const int4 x = kr[c], y = qr[c];
+                    c = c + 1 == vpr ? 0 : c + 1;
                     a = dp4a(x.x, y.x, a);
                     a = dp4a(x.y, y.y, a);
                     a = dp4a(x.z, y.z, a);
@@ -251,18 +264,22 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
             if (lane == 0) wred[warp][r] = mx;
         }
         __syncthreads();
-        if (tid < MG) {
-            float s = wred[0][tid];
-            for (int w = 1; w < kAttnWarps; ++w) s = nanmax(s, wred[w][tid]);
-            lmax[tid] = s;
+    }
+    // this chunk's maxima, pushed into every CTA of the cluster (remote stores)
+    asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
+    for (int i = tid; i < MG * CS; i += kAttnThreads) {
+        const int r = i % MG, j = i / MG;
+        float s = -INFINITY;
+        if (nvalid > 0) {
+            s = wred[0][r];
+            for (int w = 1; w < kAttnWarps; ++w) s = nanmax(s, wred[w][r]);
         }
-    } else if (tid < MG) {
-        lmax[tid] = -INFINITY;
+        *cl.map_shared_rank(&lmax[rank][r], j) = s;
     }
     cl.sync();                                                 // every chunk's maxima are in place
     if (tid < MG) {
         float mx = -INFINITY;
-        for (int j = 0; j < CS; ++j) mx = nanmax(mx, *cl.map_shared_rank(lmax + tid, j));
+        for (int j = 0; j < CS; ++j) mx = nanmax(mx, lmax[j][tid]);
         gmx[tid] = mx;
     }
     __syncthreads();
@@ -309,7 +326,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
             if (tid < MG) {
                 int sum = 0;
                 for (int w = 0; w < kAttnWarps; ++w) sum += wsum[w][tid];
-                lsum[tid] = sum;
+                *cl.map_shared_rank(&lsum[rank][tid], 0) = sum;   // to rank 0
             }
         }
         __syncthreads();
@@ -329,21 +346,21 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
                 a0 = dp4a(x.z, y.z, a0);
                 a1 = dp4a(x.w, y.w, a1);
             }
-            pvp[i] = a0 + a1;
+            *cl.map_shared_rank(pvp + rank * MG * hd + i, 0) = a0 + a1;   // to rank 0
         }
     } else {
-        for (int i = tid; i < MG * hd; i += kAttnThreads) pvp[i] = 0;
-        if (tid < MG) lsum[tid] = 0;
+        for (int i = tid; i < MG * hd; i += kAttnThreads) *cl.map_shared_rank(pvp + rank * MG * hd + i, 0) = 0;
+        if (tid < MG) *cl.map_shared_rank(&lsum[rank][tid], 0) = 0;
     }
-    cl.sync();                                                 // every chunk's partials are in place
+    cl.sync();                                                 // every chunk's partials are at rank 0
     if (rank == 0) {
         for (int i = tid; i < MG * hd; i += kAttnThreads) {
             const int r = i / hd, c = i % hd;
             const int m = r / G, h = kvh * G + r % G;
             int acc = 0, ssum = 0;
             for (int j = 0; j < CS; ++j) {
-                acc += *cl.map_shared_rank(pvp + i, j);
-                if (p.variant == 1) ssum += *cl.map_shared_rank(lsum + r, j);
+                acc += pvp[j * MG * hd + i];
+                if (p.variant == 1) ssum += lsum[j][r];
             }
             const float o = i2f(acc);
             float out;
@@ -356,7 +373,6 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
             p.att[((size_t)m * H + h) * hd + c] = out;
         }
     }
-    cl.sync();                                                 // CTA 0 is done reading the others' memory
 }
 
 cudaError_t launch_attn(const AttnParams& q, cudaStream_t st) {
