@@ -21,8 +21,9 @@
 //     ordered sum, pq = i8(127 e RECIP(sum)) (llm/ref_model.py:233-242;
 //     hf_generic.py:275-290); int32 pq.V of the chunk.
 //     -- cluster barrier --
-//  3. CTA 0 adds the partials (exact in any order) and dequantizes: NORM
-//     f32(acc)*a_v; QSUM (f32(acc)*(RECIP(sum)*127))*a_v.
+//  3. reduce-scatter: CTA j adds the partials of its slice of the outputs
+//     (exact in any order) and dequantizes them: NORM f32(acc)*a_v; QSUM
+//     (f32(acc)*(RECIP(sum)*127))*a_v.
 // Every value a CTA needs from another is pushed into its shared memory with
 // remote stores before the barrier that publishes it; reads are then local.
 // Cache layout per layer: K [kv_heads, seq_len, head_dim] int8 (a position's
@@ -72,7 +73,10 @@ __host__ __device__ inline AttnSmem attn_smem(int M, int G, int hd, int T, int c
     s.tab = o;  o += a16((size_t)M * 2 * hd * 4);             // cos | sin rows of each row's position
     s.gain = o; o += a16((size_t)2 * hd * 4);                 // q_norm | k_norm gains
     s.etab = o; o += a16(128 * 4);                            // the EXP table (T | S)
-    s.pvp = o;  o += a16((size_t)kMaxCluster * M * G * hd * 4);   // [CTA][row][c] int32 p.V partials (rank 0 sums)
+    // reduce-scatter of the int32 p.V partials: with CS CTAs, CTA j finishes the
+    // outputs [j*seg, (j+1)*seg), seg = ceil(M G hd / CS), and receives every
+    // CTA's partials of that slice: CS * seg <= M G hd + CS words
+    s.pvp = o;  o += a16(((size_t)M * G * hd + kMaxCluster) * 4);   // [source CTA][seg]
     s.ebuf = o; o += variant == 0 ? a16((size_t)T * 4) : 0;   // NORM: the whole row's e
     s.total = o;
     return s;
@@ -130,6 +134,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
     const int kvh = blockIdx.x, rank = (int)cl.block_rank(), t0 = rank * CH, tid = threadIdx.x;
     const int lane = tid & 31, warp = tid >> 5;
     const int vpr = hd / 16, vstride = CH + 16;
+    const int seg = (MG * hd + CS - 1) / CS;                  // outputs finished by each CTA
     const int qkv_dim = (H + 2 * Hk) * hd, q_dim = H * hd, kv_dim = Hk * hd;
     const AttnSmem L = attn_smem(M, G, hd, T, CH, p.variant);
     int8_t* ks = reinterpret_cast<int8_t*>(sm + L.ks);          // [CH][hd]
@@ -145,7 +150,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
     float* ebuf = reinterpret_cast<float*>(sm + L.ebuf);
     __shared__ float lmax[kMaxCluster][kMaxRows * kMaxG];     // every CTA's chunk maxima (pushed by each)
     __shared__ float gmx[kMaxRows * kMaxG];
-    __shared__ int lsum[kMaxCluster][kMaxRows * kMaxG];      // every CTA's sums of eq (at rank 0)
+    __shared__ int lsum[kMaxCluster][kMaxRows * kMaxG];      // every CTA's sums of eq (pushed to all)
     __shared__ float sq[kMaxRows * kMaxG];
     __shared__ float wred[kAttnWarps][kMaxRows * kMaxG];
     __shared__ int wsum[kAttnWarps][kMaxRows * kMaxG];
@@ -323,10 +328,11 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
                 if (lane == 0) wsum[warp][r] = sum;
             }
             __syncthreads();
-            if (tid < MG) {
+            for (int i = tid; i < MG * CS; i += kAttnThreads) {   // to every CTA
+                const int r = i % MG, j = i / MG;
                 int sum = 0;
-                for (int w = 0; w < kAttnWarps; ++w) sum += wsum[w][tid];
-                *cl.map_shared_rank(&lsum[rank][tid], 0) = sum;   // to rank 0
+                for (int w = 0; w < kAttnWarps; ++w) sum += wsum[w][r];
+                *cl.map_shared_rank(&lsum[rank][r], j) = sum;
             }
         }
         __syncthreads();
@@ -346,20 +352,25 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
                 a0 = dp4a(x.z, y.z, a0);
                 a1 = dp4a(x.w, y.w, a1);
             }
-            *cl.map_shared_rank(pvp + rank * MG * hd + i, 0) = a0 + a1;   // to rank 0
+            const int own = i / seg;                           // the CTA that finishes output i
+            *cl.map_shared_rank(pvp + rank * seg + (i - own * seg), own) = a0 + a1;
         }
     } else {
-        for (int i = tid; i < MG * hd; i += kAttnThreads) *cl.map_shared_rank(pvp + rank * MG * hd + i, 0) = 0;
-        if (tid < MG) *cl.map_shared_rank(&lsum[rank][tid], 0) = 0;
-    }
-    cl.sync();                                                 // every chunk's partials are at rank 0
-    if (rank == 0) {
         for (int i = tid; i < MG * hd; i += kAttnThreads) {
+            const int own = i / seg;
+            *cl.map_shared_rank(pvp + rank * seg + (i - own * seg), own) = 0;
+        }
+        for (int i = tid; i < MG * CS; i += kAttnThreads) *cl.map_shared_rank(&lsum[rank][i % MG], i / MG) = 0;
+    }
+    cl.sync();                                                 // every CTA holds the partials of its slice
+    {
+        const int lo = rank * seg, hi = min(MG * hd, lo + seg);
+        for (int i = lo + tid; i < hi; i += kAttnThreads) {
             const int r = i / hd, c = i % hd;
             const int m = r / G, h = kvh * G + r % G;
             int acc = 0, ssum = 0;
             for (int j = 0; j < CS; ++j) {
-                acc += pvp[j * MG * hd + i];
+                acc += pvp[j * seg + (i - lo)];
                 if (p.variant == 1) ssum += lsum[j][r];
             }
             const float o = i2f(acc);
