@@ -105,6 +105,33 @@ int w8a8_ffn_swiglu(const float* x, const float* norm_g, float eps, int rows, in
                     const float* s_gate, const int8_t* w_up, const float* s_up, int hidden, float* h,
                     int8_t* h_q, float* s_h, void* scratch, size_t scratch_bytes, void* stream);
 
+/* w8a8_ffn_swiglu with the requantization of h, for a caller that cannot hand
+ * over a scratch buffer. This entry point has no counterpart in the reference:
+ * the overlay's runtime owns one buffer for everything, so the question never
+ * comes up there.
+ *
+ * Who needs it: a host that reserves all of its device memory once at start-up
+ * (an arena or a memory pool with nothing left to give), or a plugin called
+ * by a framework that hands it tensors but no allocator. cudaMalloc there is
+ * either impossible or would synchronize the whole device in the middle of a
+ * step. Here the grid-wide amax and the CTA counter live in a small static
+ * device array inside the library (one per device, 320 bytes, enough for
+ * W8A8_FFN_NOALLOC_MAX_ROWS rows), so nothing is allocated.
+ *
+ * - rows > W8A8_FFN_NOALLOC_MAX_ROWS returns W8A8_ESCRATCH (the static array
+ *   is too small); h_q and s_h are required (without them use w8a8_ffn_swiglu,
+ *   which then needs no scratch at all).
+ * - The first call on each device looks up the array's device address with
+ *   that device current; make that first call before any stream capture.
+ * - Each call clears the array on `stream` before its launch.
+ * - The array is shared by every call on the device: two calls that can run at
+ *   the same time (other streams, other host threads) race. Order them.
+ * Same arguments and results as w8a8_ffn_swiglu otherwise. */
+#define W8A8_FFN_NOALLOC_MAX_ROWS 16
+int w8a8_ffn_swiglu_noalloc(const float* x, const float* norm_g, float eps, int rows, int k, const int8_t* w_gate,
+                            const float* s_gate, const int8_t* w_up, const float* s_up, int hidden, float* h,
+                            int8_t* h_q, float* s_h, void* stream);
+
 /* Fused per-layer attention of one sequence over its int8 KV cache. */
 typedef struct {
     int rows;                  /* query rows M (1: decode step, <= 16: prefill chunk) */

@@ -1,6 +1,7 @@
 // The extern "C" entry points of include/w8a8.h: argument checks, then the
 // launches of the kernels in linear.cu, attn.cu and misc.cu.
 #include <cstdint>
+#include <mutex>
 
 #include "../../include/w8a8.h"
 #include "w8a8_internal.h"
@@ -17,6 +18,31 @@ inline cudaStream_t S(void* s) { return static_cast<cudaStream_t>(s); }
 inline bool al16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 inline int cuda_status(cudaError_t e) { return e == cudaSuccess ? W8A8_OK : W8A8_ECUDA; }
 inline float inv_of(int n) { return (float)(1.0 / (double)n); }   // F(1.0 / n), as the host computes it
+
+// Scratch of w8a8_ffn_swiglu_noalloc: the CTA counter (bytes 0-255) and one
+// amax slot per row, as w8a8_ffn_swiglu's caller-provided buffer. Static device
+// storage exists once per device and is never allocated at run time.
+static __device__ __align__(256) unsigned char g_ffn_noalloc_scratch[256 + 4 * W8A8_FFN_NOALLOC_MAX_ROWS];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_ptr[kMaxDevices] = {};
+
+// The device address of g_ffn_noalloc_scratch on the current device, looked up
+// once per device (cudaGetSymbolAddress with that device current).
+int noalloc_scratch(void** out) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return W8A8_ECUDA;
+    if (dev < 0 || dev >= kMaxDevices) return W8A8_EINVAL;
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (!g_noalloc_ptr[dev]) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_ffn_noalloc_scratch) != cudaSuccess || !p) return W8A8_ECUDA;
+        g_noalloc_ptr[dev] = p;
+    }
+    *out = g_noalloc_ptr[dev];
+    return W8A8_OK;
+}
 
 }  // namespace
 
@@ -126,6 +152,27 @@ int w8a8_ffn_swiglu(const float* x, const float* norm_g, float eps, int rows, in
         p.amax_bits = reinterpret_cast<uint32_t*>(static_cast<char*>(scratch) + 256);
     }
     return cuda_status(launch_linear(p, PRO_RMSQ, EPI_SWIGLU, S(stream)));
+}
+
+int w8a8_ffn_swiglu_noalloc(const float* x, const float* norm_g, float eps, int rows, int k, const int8_t* w_gate,
+                            const float* s_gate, const int8_t* w_up, const float* s_up, int hidden, float* h,
+                            int8_t* h_q, float* s_h, void* stream) {
+    if (rows > W8A8_FFN_NOALLOC_MAX_ROWS) return W8A8_ESCRATCH;
+    const size_t need = w8a8_ffn_scratch_bytes(rows);
+    if (need > sizeof(g_ffn_noalloc_scratch)) return W8A8_ESCRATCH;
+    // the checks of w8a8_ffn_swiglu, made here too so that nothing is queued on an error
+    int st = check_linear(rows, k, w_gate, s_gate, hidden, h);
+    if (st) return st;
+    if (!x || !norm_g || !w_up || !s_up || !h_q || !s_h) return W8A8_EINVAL;
+    if (!al16(x) || !al16(norm_g) || !al16(w_up) || hidden % 4) return W8A8_EALIGN;
+    void* scratch = nullptr;
+    st = noalloc_scratch(&scratch);
+    if (st) return st;
+    // the counter and the amax slots must start at zero; a completed call leaves
+    // them zero, a call that gave up part-way may not, so clear them every time
+    if (cudaMemsetAsync(scratch, 0, need, S(stream)) != cudaSuccess) return W8A8_ECUDA;
+    return w8a8_ffn_swiglu(x, norm_g, eps, rows, k, w_gate, s_gate, w_up, s_up, hidden, h, h_q, s_h, scratch, need,
+                           stream);
 }
 
 size_t w8a8_attn_scratch_bytes(int rows, int heads, int kv_heads, int head_dim, int seq_len) {
