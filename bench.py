@@ -37,6 +37,10 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "decode tok/s (Qwen3-0.6B shape W8A8, T=2048)"
+# DRAM bytes (read + write) of one classifier-shaped GEMV launch (151936 x 1024),
+# from one ncu capture of the same weight stream; the command and the figures
+# are in profiles/classifier_gemv_c2.txt.
+NCU_TRAFFIC = {"bytes": 156221184 + 4762624, "source": "profiles/classifier_gemv_c2.txt"}
 FPGA_TOKS = 3.41          # KV260 overlay, Qwen3-0.6B decode at T = 2048 (docs/results_v2.3.md:93-94)
 
 
@@ -269,10 +273,12 @@ def main():
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     with Clocks(local) as clk:
+        torch.cuda.nvtx.range_push("decode")             # ncu --nvtx-include decode/ selects these launches
         e0.record(st)
         for _ in range(args.steps):
             g.replay()
         e1.record(st)
+        torch.cuda.nvtx.range_pop()
         torch.cuda.synchronize()
     barrier(ws)
     dt = max_over_ranks(e0.elapsed_time(e1) / 1e3, ws)
@@ -306,10 +312,12 @@ def main():
         ops.classifier(x1, dec.cls_q, dec.cls_s, dec.rms_final, cfg.eps, out=dec.logits[:1])
     torch.cuda.synchronize()
     r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push("roofline")
     r0.record(st)
     for _ in range(n_rep):
         ops.classifier(x1, dec.cls_q, dec.cls_s, dec.rms_final, cfg.eps, out=dec.logits[:1])
     r1.record(st)
+    torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
     t_gemv = r0.elapsed_time(r1) / 1e3 / n_rep
     N, K = cfg.vocab, cfg.dim
@@ -340,8 +348,9 @@ def main():
             "e2e": {"value": ws * args.steps / dt_e2e, "unit": "tok/s", "h2d_bytes_per_step": 8,
                     "d2h_bytes_per_step": 4 * cfg.vocab},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": None, "peak_source": peak_src,
-                         "kernel": f"linear_kernel (classifier GEMV {N}x{K}, rmsnorm+quant prologue)",
+                         "frac": achieved / peak, "traffic": NCU_TRAFFIC["bytes"],
+                         "traffic_source": NCU_TRAFFIC["source"], "peak_source": peak_src,
+                         "kernel": f"gemv_kernel (classifier GEMV {N}x{K}, rmsnorm+quant prologue, fused argmax)",
                          "bytes_per_launch": gemv_bytes, "us_per_launch": t_gemv * 1e6},
             "step_roofline": {"bytes_per_step": step_bytes, "achieved_gbs": step_bytes / (dt / args.steps) / 1e9,
                               "frac": step_bytes / (dt / args.steps) / 1e9 / peak},
