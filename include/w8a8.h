@@ -62,7 +62,8 @@ int w8a8_embed(const int32_t* tokens, int rows, const int8_t* emb_q, const float
 
 /* Read and clear the current device's error flags (bit 0: an out-of-range
  * token reached w8a8_embed; bit 1: a GEMV weight-tile wait gave up after its
- * bounded spin and the kernel stopped early). Synchronous with the device.
+ * bounded spin and the kernel stopped early; bit 2: an attention cache-tile
+ * copy did not land within its bounded wait). Synchronous with the device.
  * Plays the role of the overlay's sticky list status (llm/sa_funcsim.py:62-66,
  * firmware/rt/rt_fw.c:53-60). */
 int w8a8_error_flags(uint32_t* flags);

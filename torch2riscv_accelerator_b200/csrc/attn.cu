@@ -39,6 +39,8 @@ namespace cg = cooperative_groups;
 
 namespace w8a8 {
 
+__device__ unsigned int g_attn_errors;                        // bit 2: a cache-tile copy wait gave up
+
 constexpr int kMaxG = 8;                                       // query heads per KV head
 constexpr int kAttnThreads = 256;
 constexpr int kAttnWarps = kAttnThreads / 32;
@@ -156,6 +158,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
     __shared__ int wsum[kAttnWarps][kMaxRows * kMaxG];
     __shared__ float rsum;
     __shared__ int lim_s[kMaxRows];
+    __shared__ __align__(8) uint64_t tbar;                     // the cache tiles' bulk copies landed
 
     // every CTA of the cluster must have started before any remote store into its
     // shared memory: arrive now, wait just before the first push
@@ -176,8 +179,16 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
         if (lane == 0) rsum = __uint_as_float(w);             // (rsum is rewritten before any use)
     }
     if (nvalid > 0) {
-        const int4* kbase = reinterpret_cast<const int4*>(p.kc + ((size_t)kvh * T + t0) * hd);
-        for (int i = tid; i < nvalid * vpr; i += kAttnThreads) reinterpret_cast<int4*>(ks)[i] = __ldg(kbase + i);
+        // the chunk's K rows: one contiguous block, one 1-D bulk copy (16-byte
+        // aligned: head_dim and the chunk start are multiples of 16)
+        if (tid == 0) {
+            mbar_init(&tbar, 1);
+            mbar_fence_init();
+            mbar_expect_tx(&tbar, (uint32_t)(nvalid * hd));
+            bulk_g2s(ks, p.kc + ((size_t)kvh * T + t0) * hd, (uint32_t)(nvalid * hd), &tbar);
+        }
+        // the V^T rows: a short run of positions per channel (one bulk copy each
+        // would queue hundreds of small copies): 16-byte loads
         const int vw = nv16 / 16;                              // 16-byte words per V^T row
         for (int i = tid; i < hd * vw; i += kAttnThreads) {
             const int c = i / vw, w = i % vw;
@@ -198,6 +209,11 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
     pdl_wait();
     pdl_trigger();
     __syncthreads();
+    bool tiles_ok = true;
+    if (nvalid > 0) {
+        tiles_ok = mbar_wait(&tbar, 0u);                       // issued before the wait: landed by now
+        if (!tiles_ok && tid == 0) atomicOr(&g_attn_errors, 4u);
+    }
     if (nvalid > 0) {
         float* buf = fbuf + warp * hd;
         // q path of every row and query head of this KV head (warps from 0), and
@@ -384,6 +400,14 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
             p.att[((size_t)m * H + h) * hd + c] = out;
         }
     }
+    if (!tiles_ok) mbar_wait(&tbar, 0u);                      // no copy may land after the CTA exits
+}
+
+unsigned int attn_read_clear_errors() {
+    unsigned int v = 0, zero = 0;
+    cudaMemcpyFromSymbol(&v, g_attn_errors, sizeof(v));
+    cudaMemcpyToSymbol(g_attn_errors, &zero, sizeof(zero));
+    return v;
 }
 
 cudaError_t launch_attn(const AttnParams& q, cudaStream_t st) {

@@ -87,7 +87,7 @@ int w8a8_error_flags(uint32_t* flags) {
     if (!flags) return W8A8_EINVAL;
     unsigned int v = 0;
     int st = cuda_status(read_clear_errors(&v));
-    *flags = v | gemv_read_clear_errors();
+    *flags = v | gemv_read_clear_errors() | attn_read_clear_errors();
     return st;
 }
 

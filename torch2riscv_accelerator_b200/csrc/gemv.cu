@@ -5,16 +5,25 @@
 // Weight tiles are independent of every earlier kernel, so each CTA issues its
 // first tiles before griddepcontrol.wait: under programmatic dependent launch
 // the weight stream of this layer overlaps the tail of the previous kernel.
-// After the wait come the activation prologue (the same fused rmsnorm /
-// quant_act as linear.cu) and the dot products from shared memory: a warp owns
-// one tile row (or a K-slice of it for long rows), lanes read consecutive
-// 16-byte chunks (no bank conflicts), dp4a per 4 bytes, shuffles sum the int32
-// partials (exact in any order). Epilogues as linear.cu: dequant
-// (f32(acc)*s_w)*s_x, + residual, SwiGLU with the row amax and the last CTA's
-// int8 requant, or the classifier's fused greedy argmax.
+// After the wait come the activation prologue (fused rmsnorm / quant_act) and
+// the dot products from shared memory: consumer thread t owns row t / S of a
+// tile and a K-slice of it, dp4a per 4 bytes, shuffles sum the int32 partials
+// (exact in any order). Epilogues: dequant (f32(acc)*s_w)*s_x, + residual,
+// SwiGLU with the row amax and the last CTA's int8 requant, or the
+// classifier's fused greedy argmax.
+//
+// Code size is part of the design. A decode step runs a chain of short
+// kernels; the code a kernel runs once per launch (everything after the wait
+// but the dot-product loop) is fetched cold, and an SM fetches code from L2
+// at about 10 cycles per instruction but from its own instruction caches
+// (which keep roughly the last 64 KB) at 1.5-4.5. So the prologue and
+// epilogue kinds are runtime switches of one kernel body (every GEMV of a
+// layer runs the same code, still cached from the previous launch), and only
+// the dot-product loop is unrolled.
+//
 // Reference semantics: llm/ref_model.py:191-202 (quant_act, linear),
-// llm/sa_funcsim.py:138-162 (the GEMV command), llm/compile_model.py:295-328
-// (ffn_up with fused SiLU).
+// :204-207 (rmsnorm), llm/sa_funcsim.py:138-162 (the GEMV command),
+// llm/compile_model.py:295-328 (ffn_up with fused SiLU).
 #include "linear_common.cuh"
 #include "pdl.cuh"
 
@@ -24,191 +33,163 @@ __device__ unsigned int g_gemv_errors;                        // bit 1: a tile w
 
 constexpr int kMaxStages = 8;
 constexpr size_t kRingBytes = 96 * 1024;                      // weight ring per CTA
-
-// Row n is the j-th row of this CTA: its scales (and residuals) were staged in
-// shared memory (sw, sw2: [rows of the CTA]; rs: [MR][rows of the CTA]).
-template <int MR, int EPI>
-__device__ __forceinline__ void epilogue_row(const LinearParams& p, int n, int j, int nj, const int* acc,
-                                             const int* acc2, const float* sx, const float* sw, const float* sw2,
-                                             const float* rs, uint32_t* bamax, unsigned long long* bkey) {
-#pragma unroll
-    for (int m = 0; m < MR; ++m) {
-        if (m >= p.m) continue;
-        const size_t o = (size_t)m * p.n + n;
-        const float v = fmul(fmul(i2f(acc[m]), sw[j]), sx[m]);
-        if (EPI == EPI_STORE) {
-            p.y[o] = v;
-            if (p.acc != nullptr) p.acc[o] = acc[m];
-            if (p.argmax_key != nullptr) atomicMax(&bkey[m], argmax_key(v, n));
-        } else if (EPI == EPI_RESID) {
-            p.y[o] = fadd(rs[m * nj + j], v);
-        } else {
-            const float u = fmul(fmul(i2f(acc2[m]), sw2[j]), sx[m]);
-            const float h = silu_gate(v, u);
-            p.y[o] = h;
-            atomicMax(&bamax[m], __float_as_uint(fabsf(h)));
-        }
-    }
-}
-
+constexpr size_t kStreamRingBytes = 128 * 1024;               // ... for a GEMV of many tiles per CTA
+constexpr size_t kStreamBytes = (size_t)64 << 20;             // weights from which a GEMV counts as streaming
 constexpr int kConsumers = kThreads;                          // 8 consumer warps
 constexpr int kGemvThreads = kThreads + 32;                   // + 1 producer warp
 
-template <int MR, int PRO, int EPI>
-__global__ void __launch_bounds__(kGemvThreads, 1)
-    gemv_kernel(LinearParams p, int tr, int S, int stages, int ntiles) {
-    extern __shared__ __align__(128) unsigned char smem[];
-    constexpr bool kTwo = EPI == EPI_SWIGLU;
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const bool producer = warp == kWarps;
-    const int k = p.k, nch = k / 16;
-    const size_t tile_bytes = (size_t)tr * k;
-    const size_t stage_bytes = tile_bytes * (kTwo ? 2 : 1);
-    unsigned char* ring = smem;
-    int8_t* xs = reinterpret_cast<int8_t*>(smem + stages * stage_bytes);   // [MR][k]
-    float* xf = reinterpret_cast<float*>(xs + (size_t)MR * k);            // [k]
-    const int nj = ((ntiles + (int)gridDim.x - 1) / (int)gridDim.x) * tr;   // rows of a CTA, at most
-    float* sw = xf + (PRO == PRO_I8 ? 0 : k);                               // [nj] row scales
-    float* sw2 = sw + nj;                                                   // [nj] (SwiGLU up rows)
-    float* rs = sw2 + (kTwo ? nj : 0);                                      // [MR][nj] residual rows
-    float* gs = rs + (EPI == EPI_RESID ? MR * nj : 0);                      // [k] RMSNorm gain
-    __shared__ __align__(8) uint64_t full[kMaxStages];         // tile landed (bulk-copy bytes)
-    __shared__ __align__(8) uint64_t empty[kMaxStages];        // the 8 consumer warps are done with it
-    __shared__ float sx[MR];
-    __shared__ float red[32];
-    __shared__ uint32_t bamax[MR];
-    __shared__ unsigned long long bkey[MR];
-    __shared__ int last, failed;
-    const int my = (ntiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;   // tiles of this CTA
-    if (tid < MR) {
-        bamax[tid] = 0u;
-        bkey[tid] = 0ull;
-    }
-    if (tid == 0) {
-        failed = 0;
-        for (int s = 0; s < stages; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&empty[s], kWarps);
-        }
-        mbar_fence_init();
-    }
-    __syncthreads();
-    auto issue = [&](int i) {                                  // tile i of this CTA -> stage i % stages
-        const int s = i % stages;
-        const int row0 = ((int)blockIdx.x + i * (int)gridDim.x) * tr;
-        const uint32_t bytes = (uint32_t)(min(tr, p.n - row0) * k);
-        mbar_expect_tx(&full[s], bytes * (kTwo ? 2u : 1u));
-        bulk_g2s(ring + s * stage_bytes, p.w + (size_t)row0 * k, bytes, &full[s]);
-        if (kTwo) bulk_g2s(ring + s * stage_bytes + tile_bytes, p.w2 + (size_t)row0 * k, bytes, &full[s]);
-    };
-    const int first = min(stages, my);
-    if (producer && lane == 0)
-        for (int i = 0; i < first; ++i) issue(i);              // weights: before the wait
-    // row j of this CTA = tile j / tr, row j % tr; its scales are constants too
-    for (int j = tid; j < my * tr; j += kGemvThreads) {
-        const int n = ((int)blockIdx.x + (j / tr) * (int)gridDim.x) * tr + j % tr;
-        if (n < p.n) {
-            sw[j] = __ldg(p.s_w + n);
-            if (kTwo) sw2[j] = __ldg(p.s_w2 + n);
-        }
-    }
-    if (PRO == PRO_RMSQ)                                       // the norm gain: a constant, staged now
-        for (int c = tid; c < k; c += kGemvThreads) gs[c] = __ldg(p.norm_g + c);
-    if (PRO != PRO_I8 && warp == 0) {                          // bring the RECIP / RSQRT table lines in
-        uint32_t t = g_rec_t[lane * 2] ^ g_rec_s[lane * 2] ^ g_rsq_t[lane * 4] ^ g_rsq_s[lane * 4];
-        t = __reduce_xor_sync(0xffffffffu, t);
-        if (lane == 0) red[31] = __uint_as_float(t);          // (kept: red is rewritten by the prologue)
-    }
-    pdl_wait();
-    pdl_trigger();
-    if (EPI == EPI_RESID) {                                    // residual rows: written by earlier kernels
-        for (int j = tid; j < my * tr * MR; j += kGemvThreads) {
-            const int m = j / (my * tr), jj = j % (my * tr);
-            const int n = ((int)blockIdx.x + (jj / tr) * (int)gridDim.x) * tr + jj % tr;
-            if (n < p.n && m < p.m) rs[m * nj + jj] = p.resid[(size_t)m * p.n + n];
-        }
-    }
-    prologue<MR, PRO>(p, xs, xf, sx, red, gs);
+struct GemvCfg {
+    int pro, epi;             // Prologue / Epilogue kinds
+    int tr, S;                // tile rows; consumer threads per row
+    int stages, ntiles;
+};
 
-    if (producer) {
-        if (lane == 0) {                                       // refill each stage once its consumers are done
-            for (int i = first; i < my; ++i) {
-                const int s = i % stages;
-                if (!mbar_wait(&empty[s], (uint32_t)(((i / stages) - 1) & 1))) {
-                    atomicOr(&g_gemv_errors, 2u);
-                    failed = 1;
-                    break;
-                }
-                issue(i);
-            }
+// Ordered sum of squares over D = 16 lanes (llm/ref_model.py:179-186): lane
+// l < 16 adds x[l]^2, x[l + 16]^2, ... in order, 8 loads ahead of the adds;
+// then the pairwise tree. Whole warp; the sum on every lane.
+__device__ __forceinline__ float sumsq16(const float* xf, int k, int lane) {
+    float acc = 0.f;
+    if (lane < kLanes) {
+        const int groups = k / kLanes;                        // k is a multiple of 16
+        int g = 0;
+#pragma unroll 1
+        for (; g + 8 <= groups; g += 8) {
+            float t[8];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) t[j] = xf[(g + j) * kLanes + lane];
+#pragma unroll
+            for (int j = 0; j < 8; ++j) acc = fadd(acc, fmul(t[j], t[j]));
         }
-    } else {
-        // Consumer thread t owns row r = t / S of a tile and K-slice s = t % S
-        // (S <= 32 threads per row, within one warp): chunks s, s + S, ... of 16
-        // bytes; lanes read consecutive chunks (conflict-free); the row is summed
-        // with shuffles. A warp releases the stage before its epilogue.
-        const int r = tid / S, sl = tid % S;
-        for (int i = 0; i < my; ++i) {
-            const int s = i % stages;
-            if (!mbar_wait(&full[s], (uint32_t)((i / stages) & 1))) {
-                atomicOr(&g_gemv_errors, 2u);
-                failed = 1;
-                break;
-            }
-            const int row0 = ((int)blockIdx.x + i * (int)gridDim.x) * tr;
-            const int rows = min(tr, p.n - row0);
-            const int8_t* wr = reinterpret_cast<const int8_t*>(ring + s * stage_bytes) + (size_t)r * k;
-            const int8_t* wr2 = wr + tile_bytes;
-            int acc[MR], acc2[MR];
-#pragma unroll
-            for (int m = 0; m < MR; ++m) acc[m] = acc2[m] = 0;
-            if (r < rows) {
-#pragma unroll 4
-                for (int c = sl; c < nch; c += S) {
-                    const int4 w4 = *reinterpret_cast<const int4*>(wr + c * 16);
-                    int4 u4;
-                    if (kTwo) u4 = *reinterpret_cast<const int4*>(wr2 + c * 16);
-#pragma unroll
-                    for (int m = 0; m < MR; ++m) {
-                        const int4 x4 = *reinterpret_cast<const int4*>(xs + (size_t)m * k + c * 16);
-                        acc[m] = dp4a(w4.w, x4.w, dp4a(w4.z, x4.z, dp4a(w4.y, x4.y, dp4a(w4.x, x4.x, acc[m]))));
-                        if (kTwo)
-                            acc2[m] = dp4a(u4.w, x4.w, dp4a(u4.z, x4.z, dp4a(u4.y, x4.y, dp4a(u4.x, x4.x, acc2[m]))));
-                    }
-                }
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[s]);
-#pragma unroll
-            for (int m = 0; m < MR; ++m) {
-                for (int o = S / 2; o > 0; o >>= 1) {
-                    acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], o);
-                    if (kTwo) acc2[m] += __shfl_xor_sync(0xffffffffu, acc2[m], o);
-                }
-            }
-            if (sl == 0 && r < rows)
-                epilogue_row<MR, EPI>(p, row0 + r, i * tr + r, nj, acc, acc2, sx, sw, sw2, rs, bamax, bkey);
+#pragma unroll 1
+        for (; g < groups; ++g) {
+            const float t = xf[g * kLanes + lane];
+            acc = fadd(acc, fmul(t, t));
         }
     }
-    __syncthreads();
-    if (failed) {                                              // a wait gave up: drain what is in flight, stop
-        if (producer && lane == 0)
-            for (int s = 0; s < stages; ++s) mbar_wait(&full[s], 0u), mbar_wait(&full[s], 1u);
+#pragma unroll
+    for (int s = 1; s < kLanes; s <<= 1) {
+        const float o = __shfl_down_sync(0xffffffffu, acc, s);
+        if ((lane & (2 * s - 1)) == 0) acc = fadd(acc, o);
+    }
+    return __shfl_sync(0xffffffffu, acc, 0);
+}
+
+// Activation prologue: rows m < MR of x -> int8 rows xs [MR][k] and scales
+// sx [MR] (zero rows beyond p.m). xf: fp32 staging [k]; gs: the RMSNorm gain
+// in shared memory. Every thread of the block takes part.
+template <int MR>
+__device__ __forceinline__ void gemv_prologue(const LinearParams& p, int pro, int8_t* xs, float* xf, float* sx,
+                                              const float* gs, float* red, float* bc) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, k = p.k, nt = (int)blockDim.x;
+    if (pro == PRO_I8) {
+#pragma unroll 1
+        for (int m = 0; m < MR; ++m) {
+            int4* dst = reinterpret_cast<int4*>(xs + (size_t)m * k);
+            const int4* src = reinterpret_cast<const int4*>(p.xq + (size_t)m * k);
+#pragma unroll 1
+            for (int c = tid; c < k / 16; c += nt) dst[c] = m < p.m ? __ldcg(src + c) : make_int4(0, 0, 0, 0);
+        }
+        if (tid < MR) sx[tid] = tid < p.m ? __ldcg(p.s_x + tid) : 0.f;
         __syncthreads();
         return;
     }
-    if (EPI == EPI_STORE && p.argmax_key != nullptr) {
-        if (tid < p.m && tid < MR) atomicMax(p.argmax_key + tid, bkey[tid]);
+    float4* xf4 = reinterpret_cast<float4*>(xf);
+    const float4* g4 = reinterpret_cast<const float4*>(gs);
+#pragma unroll 1
+    for (int m = 0; m < MR; ++m) {
+        char4* dst = reinterpret_cast<char4*>(xs + (size_t)m * k);
+        if (m >= p.m) {
+#pragma unroll 1
+            for (int c = tid; c < k / 4; c += nt) dst[c] = make_char4(0, 0, 0, 0);
+            if (tid == 0) sx[m] = 0.f;
+            continue;
+        }
+        const float4* xr = reinterpret_cast<const float4*>(p.x + (size_t)m * k);
+#pragma unroll 4
+        for (int c = tid; c < k / 4; c += nt) xf4[c] = __ldcg(xr + c);      // loads batched: 1-3 per thread
+        __syncthreads();
+        float r = 1.f;
+        if (pro == PRO_RMSQ) {
+            if (warp == 0) {
+                const float ss = sumsq16(xf, k, lane);
+                if (lane == 0) bc[0] = sfu_rsqrt(fadd(fmul(ss, p.inv_k), p.eps));
+            }
+            __syncthreads();
+            r = bc[0];
+        }
+        // y = (x * r) * g in place, and the row amax
+        float a = 0.f;
+#pragma unroll 4
+        for (int c = tid; c < k / 4; c += nt) {
+            float4 v = xf4[c];
+            if (pro == PRO_RMSQ) {
+                const float4 g = g4[c];
+                v = make_float4(fmul(fmul(v.x, r), g.x), fmul(fmul(v.y, r), g.y), fmul(fmul(v.z, r), g.z),
+                                fmul(fmul(v.w, r), g.w));
+                xf4[c] = v;
+            }
+            a = nanmax(a, nanmax(nanmax(fabsf(v.x), fabsf(v.y)), nanmax(fabsf(v.z), fabsf(v.w))));
+        }
+        a = block_nanmax(a, red);
+        const float s = fmul(a, W8A8_C127);
+        const float inv = sfu_recip(s);
+#pragma unroll 4
+        for (int c = tid; c < k / 4; c += nt) {
+            const float4 v = xf4[c];
+            dst[c] = make_char4(to_i8(fmul(v.x, inv)), to_i8(fmul(v.y, inv)), to_i8(fmul(v.z, inv)),
+                                to_i8(fmul(v.w, inv)));
+        }
+        if (tid == 0) {
+            sx[m] = s;
+            if (p.s_x_out != nullptr && blockIdx.x == 0) p.s_x_out[m] = s;
+        }
+        __syncthreads();                                       // xf free for the next row
     }
-    if (EPI != EPI_SWIGLU || p.hq == nullptr) return;
-    // the row amax across the grid; the last CTA requantizes h (quant_act)
-    if (tid < p.m && tid < MR) atomicMax(p.amax_bits + tid, bamax[tid]);
+}
+
+// Dot products of one row slice of a tile: 16-byte chunks c = sl, sl + S, ...
+// of the row (TWO: the gate and up rows), two independent dp4a chains.
+template <int MR, bool TWO>
+__device__ __forceinline__ void tile_dots(const int8_t* wr, const int8_t* wr2, const int8_t* xs, int k, int nch,
+                                          int sl, int S, int* acc, int* acc2) {
+    int a0[MR], a1[MR], b0[MR], b1[MR];
+#pragma unroll
+    for (int m = 0; m < MR; ++m) a0[m] = a1[m] = b0[m] = b1[m] = 0;
+    const int4 z = make_int4(0, 0, 0, 0);
+#pragma unroll 2
+    for (int c = sl; c < nch; c += 2 * S) {
+        const bool hi = c + S < nch;
+        const int4 w0 = *reinterpret_cast<const int4*>(wr + c * 16);
+        const int4 w1 = hi ? *reinterpret_cast<const int4*>(wr + (c + S) * 16) : z;
+        int4 u0 = z, u1 = z;
+        if (TWO) {
+            u0 = *reinterpret_cast<const int4*>(wr2 + c * 16);
+            u1 = hi ? *reinterpret_cast<const int4*>(wr2 + (c + S) * 16) : z;
+        }
+#pragma unroll
+        for (int m = 0; m < MR; ++m) {
+            const int4 x0 = *reinterpret_cast<const int4*>(xs + (size_t)m * k + c * 16);
+            const int4 x1 = hi ? *reinterpret_cast<const int4*>(xs + (size_t)m * k + (c + S) * 16) : z;
+            a0[m] = dp4a(w0.w, x0.w, dp4a(w0.z, x0.z, dp4a(w0.y, x0.y, dp4a(w0.x, x0.x, a0[m]))));
+            a1[m] = dp4a(w1.w, x1.w, dp4a(w1.z, x1.z, dp4a(w1.y, x1.y, dp4a(w1.x, x1.x, a1[m]))));
+            if (TWO) {
+                b0[m] = dp4a(u0.w, x0.w, dp4a(u0.z, x0.z, dp4a(u0.y, x0.y, dp4a(u0.x, x0.x, b0[m]))));
+                b1[m] = dp4a(u1.w, x1.w, dp4a(u1.z, x1.z, dp4a(u1.y, x1.y, dp4a(u1.x, x1.x, b1[m]))));
+            }
+        }
+    }
+#pragma unroll
+    for (int m = 0; m < MR; ++m) {                             // int32 sums: exact in any order
+        acc[m] = a0[m] + a1[m];
+        acc2[m] = b0[m] + b1[m];
+    }
+}
+
+// The last CTA of a SwiGLU launch: h -> int8 rows with the grid-wide amax.
+__device__ __forceinline__ void swiglu_requant(const LinearParams& p) {
+    const int tid = threadIdx.x;
     __threadfence();
-    __syncthreads();
-    if (tid == 0) last = atomicAdd(p.counter, 1u) == gridDim.x - 1;
-    __syncthreads();
-    if (!last) return;
-    __threadfence();
+#pragma unroll 1
     for (int m = 0; m < p.m; ++m) {
         const float amax = __uint_as_float(__ldcg(p.amax_bits + m));
         const float s = fmul(amax, W8A8_C127);
@@ -216,6 +197,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1)
         const float4* hr = reinterpret_cast<const float4*>(p.y + (size_t)m * p.n);
         char4* qr = reinterpret_cast<char4*>(p.hq + (size_t)m * p.n);
         const int n4 = p.n / 4;
+#pragma unroll 1
         for (int j0 = tid; j0 < n4; j0 += 4 * kGemvThreads) {   // four independent loads in flight
             float4 v[4];
 #pragma unroll
@@ -238,6 +220,196 @@ __global__ void __launch_bounds__(kGemvThreads, 1)
     if (tid == 0) *p.counter = 0u;
 }
 
+template <int MR>
+__global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(LinearParams p, GemvCfg cf) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    const int pro = cf.pro, epi = cf.epi, tr = cf.tr, S = cf.S, stages = cf.stages, ntiles = cf.ntiles;
+    const bool two = epi == EPI_SWIGLU;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const bool producer = warp == kWarps;
+    const int k = p.k, nch = k / 16;
+    const size_t tile_bytes = (size_t)tr * k;
+    const size_t stage_bytes = tile_bytes * (two ? 2 : 1);
+    const int my = (ntiles - (int)blockIdx.x + (int)gridDim.x - 1) / (int)gridDim.x;   // tiles of this CTA
+    const int nj = ((ntiles + (int)gridDim.x - 1) / (int)gridDim.x) * tr;              // rows of a CTA, at most
+    unsigned char* ring = smem;
+    int8_t* xs = reinterpret_cast<int8_t*>(smem + stages * stage_bytes);   // [MR][k]
+    float* xf = reinterpret_cast<float*>(xs + (size_t)MR * k);            // [k] (fp32 prologues)
+    float* sw = xf + (pro == PRO_I8 ? 0 : k);                               // [nj] row scales
+    float* sw2 = sw + nj;                                                   // [nj] (SwiGLU up rows)
+    float* rs = sw2 + (two ? nj : 0);                                       // [MR][nj] residual rows
+    float* gs = rs + (epi == EPI_RESID ? MR * nj : 0);                      // [k] RMSNorm gain
+    __shared__ __align__(8) uint64_t full[kMaxStages];         // tile landed (bulk-copy bytes)
+    __shared__ __align__(8) uint64_t empty[kMaxStages];        // the 8 consumer warps are done with it
+    __shared__ float sx[MR];
+    __shared__ float red[32];
+    __shared__ float bc[2];
+    __shared__ uint32_t bamax[MR];
+    __shared__ unsigned long long bkey[MR];
+    __shared__ int last, failed;
+    if (tid < MR) {
+        bamax[tid] = 0u;
+        bkey[tid] = 0ull;
+    }
+    if (tid == 0) {
+        failed = 0;
+#pragma unroll 1
+        for (int s = 0; s < stages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kWarps);
+        }
+        mbar_fence_init();
+    }
+    __syncthreads();
+    auto issue = [&](int i) {                                  // tile i of this CTA -> stage i % stages
+        const int s = i % stages;
+        const int row0 = ((int)blockIdx.x + i * (int)gridDim.x) * tr;
+        const uint32_t bytes = (uint32_t)(min(tr, p.n - row0) * k);
+        mbar_expect_tx(&full[s], bytes * (two ? 2u : 1u));
+        bulk_g2s(ring + s * stage_bytes, p.w + (size_t)row0 * k, bytes, &full[s]);
+        if (two) bulk_g2s(ring + s * stage_bytes + tile_bytes, p.w2 + (size_t)row0 * k, bytes, &full[s]);
+    };
+    const int first = min(stages, my);
+    if (producer && lane == 0) {
+#pragma unroll 1
+        for (int i = 0; i < first; ++i) issue(i);             // weights: before the wait
+    }
+    // row j of this CTA = tile j / tr, row j % tr; its scales are constants too
+#pragma unroll 1
+    for (int j = tid; j < my * tr; j += kGemvThreads) {
+        const int n = ((int)blockIdx.x + (j / tr) * (int)gridDim.x) * tr + j % tr;
+        if (n < p.n) {
+            sw[j] = __ldg(p.s_w + n);
+            if (two) sw2[j] = __ldg(p.s_w2 + n);
+        }
+    }
+    if (pro == PRO_RMSQ) {                                     // the norm gain: a constant, staged now
+#pragma unroll 1
+        for (int c = tid; c < k; c += kGemvThreads) gs[c] = __ldg(p.norm_g + c);
+    }
+    if (pro != PRO_I8 && warp == 0) {                          // bring the RECIP / RSQRT table lines in
+        uint32_t t = g_rec_t[lane * 2] ^ g_rec_s[lane * 2] ^ g_rsq_t[lane * 4] ^ g_rsq_s[lane * 4];
+        t = __reduce_xor_sync(0xffffffffu, t);
+        if (lane == 0) bc[1] = __uint_as_float(t);
+    }
+    pdl_wait();
+    pdl_trigger();
+    if (epi == EPI_RESID) {                                    // residual rows: written by earlier kernels
+#pragma unroll 4
+        for (int j = tid; j < my * tr * MR; j += kGemvThreads) {
+            const int m = j / (my * tr), jj = j % (my * tr);
+            const int n = ((int)blockIdx.x + (jj / tr) * (int)gridDim.x) * tr + jj % tr;
+            if (n < p.n && m < p.m) rs[m * nj + jj] = __ldcg(p.resid + (size_t)m * p.n + n);
+        }
+    }
+    gemv_prologue<MR>(p, pro, xs, xf, sx, gs, red, bc);        // ends with a block barrier
+
+    if (producer) {
+        if (lane == 0) {                                       // refill each stage once its consumers are done
+#pragma unroll 1
+            for (int i = first; i < my; ++i) {
+                const int s = i % stages;
+                if (!mbar_wait(&empty[s], (uint32_t)(((i / stages) - 1) & 1))) {
+                    atomicOr(&g_gemv_errors, 2u);
+                    failed = 1;
+                    break;
+                }
+                issue(i);
+            }
+        }
+    } else {
+        // Consumer thread t owns row r = t / S of a tile and K-slice s = t % S
+        // (S <= 32 threads per row, within one warp); the row is summed with
+        // shuffles. A warp releases the stage before its epilogue. The argmax
+        // key and the SwiGLU row amax are kept per thread and merged at the end.
+        const int r = tid / S, sl = tid % S;
+        uint32_t tamax[MR];
+        unsigned long long tkey[MR];
+#pragma unroll
+        for (int m = 0; m < MR; ++m) tamax[m] = 0u, tkey[m] = 0ull;
+#pragma unroll 1
+        for (int i = 0; i < my; ++i) {
+            const int s = i % stages;
+            if (!mbar_wait(&full[s], (uint32_t)((i / stages) & 1))) {
+                atomicOr(&g_gemv_errors, 2u);
+                failed = 1;
+                break;
+            }
+            const int row0 = ((int)blockIdx.x + i * (int)gridDim.x) * tr;
+            const int rows = min(tr, p.n - row0);
+            const int8_t* wr = reinterpret_cast<const int8_t*>(ring + s * stage_bytes) + (size_t)r * k;
+            int acc[MR], acc2[MR];
+#pragma unroll
+            for (int m = 0; m < MR; ++m) acc[m] = acc2[m] = 0;
+            if (r < rows) {
+                if (two) tile_dots<MR, true>(wr, wr + tile_bytes, xs, k, nch, sl, S, acc, acc2);
+                else tile_dots<MR, false>(wr, nullptr, xs, k, nch, sl, S, acc, acc2);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+#pragma unroll
+            for (int m = 0; m < MR; ++m) {
+#pragma unroll 1
+                for (int o = S / 2; o > 0; o >>= 1) {
+                    acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], o);
+                    acc2[m] += __shfl_xor_sync(0xffffffffu, acc2[m], o);
+                }
+            }
+            if (sl == 0 && r < rows) {
+                const int n = row0 + r, j = i * tr + r;
+#pragma unroll
+                for (int m = 0; m < MR; ++m) {
+                    if (m >= p.m) continue;
+                    const size_t o = (size_t)m * p.n + n;
+                    const float v = fmul(fmul(i2f(acc[m]), sw[j]), sx[m]);
+                    if (epi == EPI_STORE) {
+                        p.y[o] = v;
+                        if (p.acc != nullptr) p.acc[o] = acc[m];
+                        if (p.argmax_key != nullptr) {
+                            const unsigned long long key = argmax_key(v, n);
+                            tkey[m] = key > tkey[m] ? key : tkey[m];
+                        }
+                    } else if (epi == EPI_RESID) {
+                        p.y[o] = fadd(rs[m * nj + j], v);
+                    } else {
+                        const float u = fmul(fmul(i2f(acc2[m]), sw2[j]), sx[m]);
+                        const float h = silu_gate(v, u);
+                        p.y[o] = h;
+                        tamax[m] = max(tamax[m], __float_as_uint(fabsf(h)));   // as bits: NaN above numbers
+                    }
+                }
+            }
+        }
+        if (sl == 0) {                                         // merge the per-thread maxima
+#pragma unroll
+            for (int m = 0; m < MR; ++m) {
+                if (tkey[m] != 0ull) atomicMax(&bkey[m], tkey[m]);
+                if (tamax[m] != 0u) atomicMax(&bamax[m], tamax[m]);
+            }
+        }
+    }
+    __syncthreads();
+    if (failed) {                                              // a wait gave up: drain what is in flight, stop
+        if (producer && lane == 0) {
+#pragma unroll 1
+            for (int s = 0; s < stages; ++s) mbar_wait(&full[s], 0u), mbar_wait(&full[s], 1u);
+        }
+        __syncthreads();
+        return;
+    }
+    if (epi == EPI_STORE && p.argmax_key != nullptr) {
+        if (tid < p.m && tid < MR) atomicMax(p.argmax_key + tid, bkey[tid]);
+    }
+    if (epi != EPI_SWIGLU || p.hq == nullptr) return;
+    // the row amax across the grid; the last CTA requantizes h (quant_act)
+    if (tid < p.m && tid < MR) atomicMax(p.amax_bits + tid, bamax[tid]);
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) last = atomicAdd(p.counter, 1u) == gridDim.x - 1;
+    __syncthreads();
+    if (last) swiglu_requant(p);
+}
+
 static int sm_count() {
     static int cached[64] = {0};
     int d = 0;
@@ -248,50 +420,59 @@ static int sm_count() {
 }
 
 struct Tiling {
-    int tr, slices, stages, ntiles, grid;
+    GemvCfg cf;
+    int grid;
     size_t smem;
 };
 
-// tile rows: about 16 KB per matrix (power of two, at most 64 rows); warps
-// split a row's K when a tile has fewer than 8 rows; a 64 KB ring of stages.
+// Tile rows: a power of two between 8 and 256. A GEMV whose rows fit one tile
+// per CTA (up to 32 KB per matrix) takes that: the per-tile code then runs
+// once, and the ring is one tile (small, so the next kernel's CTAs fit beside
+// it). Otherwise about 16 KB per matrix, or 32 KB with a 128 KB ring when the
+// weights stream through each CTA many times (less fixed work per byte).
+// Consumer threads split a row's K (256 / rows threads per row).
 static Tiling tiling(const LinearParams& p, int mr, int pro, int epi) {
     Tiling t{};
-    int tr = 16384 / p.k;                                      // ~16 KB per matrix, at least 8 rows
+    const bool stream = (size_t)p.n * p.k >= kStreamBytes;
+    int tr = (stream ? 32768 : 16384) / p.k;
+    const int sms = sm_count();
+    int one = 1;                                               // rows for one tile per CTA
+    while (one * sms < p.n) one *= 2;
+    if (!stream && one > tr && (size_t)one * p.k <= 32768) tr = one;
     tr = tr < kWarps ? kWarps : (tr > kConsumers ? kConsumers : tr);
     int pw = 1;
     while (pw * 2 <= tr) pw *= 2;
-    t.tr = pw;
-    t.slices = kConsumers / t.tr;                              // consumer threads per row, at most 32
-    const size_t stage = (size_t)t.tr * p.k * (epi == EPI_SWIGLU ? 2 : 1);
-    size_t st = kRingBytes / stage;
-    t.stages = (int)(st < 2 ? 2 : (st > (size_t)kMaxStages ? kMaxStages : st));
-    t.ntiles = (p.n + t.tr - 1) / t.tr;
-    t.grid = t.ntiles < sm_count() ? t.ntiles : sm_count();
-    const size_t nj = (size_t)((t.ntiles + t.grid - 1) / t.grid) * t.tr;   // rows of a CTA, at most
-    t.smem = (size_t)t.stages * stage + (size_t)mr * p.k + (pro == PRO_I8 ? 0 : (size_t)p.k * 4) +
+    t.cf.pro = pro;
+    t.cf.epi = epi;
+    t.cf.tr = pw;
+    t.cf.S = kConsumers / pw;                                 // consumer threads per row, at most 32
+    const size_t stage = (size_t)pw * p.k * (epi == EPI_SWIGLU ? 2 : 1);
+    size_t st = (stream ? kStreamRingBytes : kRingBytes) / stage;
+    t.cf.stages = (int)(st < 2 ? 2 : (st > (size_t)kMaxStages ? kMaxStages : st));
+    t.cf.ntiles = (p.n + pw - 1) / pw;
+    t.grid = t.cf.ntiles < sms ? t.cf.ntiles : sms;
+    const int per = (t.cf.ntiles + t.grid - 1) / t.grid;     // tiles of a CTA, at most
+    if (t.cf.stages > per) t.cf.stages = per;
+    const size_t nj = (size_t)((t.cf.ntiles + t.grid - 1) / t.grid) * pw;   // rows of a CTA, at most
+    t.smem = (size_t)t.cf.stages * stage + (size_t)mr * p.k + (pro == PRO_I8 ? 0 : (size_t)p.k * 4) +
              nj * 4 * ((epi == EPI_SWIGLU ? 2 : 1) + (epi == EPI_RESID ? mr : 0)) +
              (pro == PRO_RMSQ ? (size_t)p.k * 4 : 0);
     return t;
 }
 
-template <int MR, int PRO, int EPI>
-static cudaError_t launch_g(const LinearParams& p, cudaStream_t st) {
-    const Tiling t = tiling(p, MR, PRO, EPI);
-    auto kern = gemv_kernel<MR, PRO, EPI>;
+template <int MR>
+static cudaError_t launch_g(const LinearParams& p, int pro, int epi, cudaStream_t st) {
+    const Tiling t = tiling(p, MR, pro, epi);
+    auto kern = gemv_kernel<MR>;
+    // the launch's own size, not a common maximum: the block scheduler reserves
+    // this much per CTA, and the next kernel's CTAs must fit beside this one's
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)t.smem);
     if (e != cudaSuccess) return e;
     // one shared-memory carveout for every kernel of the chain: no L1 / shared
     // reconfiguration of an SM between consecutive kernels
     e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     if (e != cudaSuccess) return e;
-    return launch_k(kern, dim3(t.grid), dim3(kGemvThreads), t.smem, st, p, t.tr, t.slices, t.stages, t.ntiles);
-}
-
-template <int PRO, int EPI>
-static cudaError_t launch_gm(const LinearParams& p, cudaStream_t st) {
-    if (p.m <= 1) return launch_g<1, PRO, EPI>(p, st);
-    if (p.m <= 2) return launch_g<2, PRO, EPI>(p, st);
-    return launch_g<4, PRO, EPI>(p, st);
+    return launch_k(kern, dim3(t.grid), dim3(kGemvThreads), t.smem, st, p, t.cf);
 }
 
 bool gemv_fits(const LinearParams& p, int pro, int epi) {
@@ -301,13 +482,11 @@ bool gemv_fits(const LinearParams& p, int pro, int epi) {
 }
 
 cudaError_t launch_gemv(const LinearParams& p, int pro, int epi, cudaStream_t st) {
-    if (pro == PRO_I8 && epi == EPI_STORE) return launch_gm<PRO_I8, EPI_STORE>(p, st);
-    if (pro == PRO_I8 && epi == EPI_RESID) return launch_gm<PRO_I8, EPI_RESID>(p, st);
-    if (pro == PRO_QUANT && epi == EPI_STORE) return launch_gm<PRO_QUANT, EPI_STORE>(p, st);
-    if (pro == PRO_QUANT && epi == EPI_RESID) return launch_gm<PRO_QUANT, EPI_RESID>(p, st);
-    if (pro == PRO_RMSQ && epi == EPI_STORE) return launch_gm<PRO_RMSQ, EPI_STORE>(p, st);
-    if (pro == PRO_RMSQ && epi == EPI_SWIGLU) return launch_gm<PRO_RMSQ, EPI_SWIGLU>(p, st);
-    return cudaErrorInvalidValue;
+    if (pro < PRO_I8 || pro > PRO_RMSQ || epi < EPI_STORE || epi > EPI_SWIGLU) return cudaErrorInvalidValue;
+    if (pro == PRO_I8 && epi == EPI_SWIGLU) return cudaErrorInvalidValue;
+    if (p.m <= 1) return launch_g<1>(p, pro, epi, st);
+    if (p.m <= 2) return launch_g<2>(p, pro, epi, st);
+    return launch_g<4>(p, pro, epi, st);
 }
 
 unsigned int gemv_read_clear_errors() {

@@ -35,6 +35,7 @@ cudaError_t launch_linear(const LinearParams& p, int pro, int epi, cudaStream_t 
 bool gemv_fits(const LinearParams& p, int pro, int epi);
 cudaError_t launch_gemv(const LinearParams& p, int pro, int epi, cudaStream_t st);
 unsigned int gemv_read_clear_errors();
+unsigned int attn_read_clear_errors();
 
 struct AttnParams {
     int rows;                 // M query rows of one sequence
