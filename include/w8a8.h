@@ -63,7 +63,8 @@ int w8a8_embed(const int32_t* tokens, int rows, const int8_t* emb_q, const float
 /* Read and clear the current device's error flags (bit 0: an out-of-range
  * token reached w8a8_embed; bit 1: a GEMV weight-tile wait gave up after its
  * bounded spin and the kernel stopped early; bit 2: an attention cache-tile
- * copy did not land within its bounded wait). Synchronous with the device.
+ * copy did not land within its bounded wait; bit 3: the same for an MoE weight
+ * tile). Synchronous with the device.
  * Plays the role of the overlay's sticky list status (llm/sa_funcsim.py:62-66,
  * firmware/rt/rt_fw.c:53-60). */
 int w8a8_error_flags(uint32_t* flags);
@@ -132,6 +133,25 @@ int w8a8_ffn_swiglu(const float* x, const float* norm_g, float eps, int rows, in
 int w8a8_ffn_swiglu_noalloc(const float* x, const float* norm_g, float eps, int rows, int k, const int8_t* w_gate,
                             const float* s_gate, const int8_t* w_up, const float* s_up, int hidden, float* h,
                             int8_t* h_q, float* s_h, void* stream);
+
+/* Mixture-of-experts FFN for up to 16 rows, each with its own Top-k:
+ * y = resid + sum_k w_k * expert_k(rmsnorm(x)), where the router's W8A8 logits
+ * (router_q [experts, dim]) give the Top-k by value (ties: the lower id),
+ * w = e * RECIP(sum e), e = EXP(v - v_0) (D = 16 ordered sum), and expert i is
+ * the SwiGLU down(quant_act((g * RECIP(1 + EXP(-g))) * u)) with gate_q, up_q
+ * [experts, expert_hidden, dim] and down_q [experts, dim, expert_hidden]; the
+ * k results are folded in k order from 0. norm_g NULL: x is already the
+ * normalized input (no RMSNorm). ids, w: [rows, top_k] outputs (the
+ * routing). resid may equal y. scratch: w8a8_moe_scratch_bytes() bytes.
+ * experts <= 64, top_k <= 16. Replaces hf_generic.QMixtralMoe.route / _row
+ * (compiler/frontend/hf_generic.py:641-657) and the MoE lowering of the IREE
+ * plugin (docs/moe_native_lowering_design.md). */
+size_t w8a8_moe_scratch_bytes(int rows, int dim, int top_k, int expert_hidden);
+int w8a8_moe_ffn(const float* x, const float* norm_g, float eps, int rows, int dim, const int8_t* router_q,
+                 const float* router_s, int experts, int top_k, const int8_t* gate_q, const float* gate_s,
+                 const int8_t* up_q, const float* up_s, int expert_hidden, const int8_t* down_q, const float* down_s,
+                 const float* resid, float* y, int32_t* ids, float* w, void* scratch, size_t scratch_bytes,
+                 void* stream);
 
 /* Fused per-layer attention of one sequence over its int8 KV cache. */
 typedef struct {

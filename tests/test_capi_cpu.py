@@ -70,3 +70,25 @@ def test_scratch_sizes(lib):
     the SwiGLU dispatch needs a counter and a row-amax word per row."""
     assert lib.w8a8_attn_scratch_bytes(16, 16, 8, 128, 2048) == 0
     assert lib.w8a8_ffn_scratch_bytes(16) >= 256 + 64
+
+
+def _moe(lib, rows=1, dim=64, experts=4, top_k=2, ih=128, scratch_bytes=None, x=16, norm_g=None):
+    sb = lib.w8a8_moe_scratch_bytes(rows, dim, top_k, ih) if scratch_bytes is None else scratch_bytes
+    return lib.w8a8_moe_ffn(x, norm_g, ctypes.c_float(1e-6), rows, dim, 16, 16, experts, top_k, 16, 16, 16, 16, ih,
+                            16, 16, 16, 16, 16, 16, 16, sb, None)
+
+
+def test_moe_argument_checks(lib):
+    """Checked before anything is queued: row and expert limits, the 16-byte
+    grid of dim / expert_hidden / pointers, and the scratch size."""
+    assert _moe(lib, rows=17) == _lib.W8A8_EINVAL
+    assert _moe(lib, experts=65) == _lib.W8A8_EINVAL
+    assert _moe(lib, top_k=5, experts=4) == _lib.W8A8_EINVAL
+    assert _moe(lib, top_k=17, experts=32) == _lib.W8A8_EINVAL
+    assert _moe(lib, dim=72) == _lib.W8A8_EALIGN
+    assert _moe(lib, ih=120) == _lib.W8A8_EALIGN
+    assert _moe(lib, x=8) == _lib.W8A8_EALIGN
+    assert _moe(lib, scratch_bytes=64) == _lib.W8A8_ESCRATCH
+    assert _moe(lib, x=None) == _lib.W8A8_EINVAL
+    # scratch: int8 row + scale + h of every slot + amax words, each 256-byte aligned
+    assert lib.w8a8_moe_scratch_bytes(1, 1024, 8, 512) == 1024 + 256 + 8 * 512 * 4 + 256

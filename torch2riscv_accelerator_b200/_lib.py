@@ -37,6 +37,8 @@ PROTOTYPES = {
     "w8a8_ffn_scratch_bytes": (Z, [I]),
     "w8a8_ffn_swiglu": (I, [P, P, F, I, I, P, P, P, P, I, P, P, P, P, Z, P]),
     "w8a8_ffn_swiglu_noalloc": (I, [P, P, F, I, I, P, P, P, P, I, P, P, P, P]),
+    "w8a8_moe_scratch_bytes": (Z, [I, I, I, I]),
+    "w8a8_moe_ffn": (I, [P, P, F, I, I, P, P, I, I, P, P, P, P, I, P, P, P, P, P, P, P, Z, P]),
     "w8a8_attn_scratch_bytes": (Z, [I, I, I, I, I]),
     "w8a8_attn": (I, [C.POINTER(W8A8AttnArgs), P]),
     "w8a8_argmax": (I, [P, I, I, P, P]),

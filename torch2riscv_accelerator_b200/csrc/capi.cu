@@ -87,7 +87,7 @@ int w8a8_error_flags(uint32_t* flags) {
     if (!flags) return W8A8_EINVAL;
     unsigned int v = 0;
     int st = cuda_status(read_clear_errors(&v));
-    *flags = v | gemv_read_clear_errors() | attn_read_clear_errors();
+    *flags = v | gemv_read_clear_errors() | attn_read_clear_errors() | moe_read_clear_errors();
     return st;
 }
 
@@ -173,6 +173,48 @@ int w8a8_ffn_swiglu_noalloc(const float* x, const float* norm_g, float eps, int 
     if (cudaMemsetAsync(scratch, 0, need, S(stream)) != cudaSuccess) return W8A8_ECUDA;
     return w8a8_ffn_swiglu(x, norm_g, eps, rows, k, w_gate, s_gate, w_up, s_up, hidden, h, h_q, s_h, scratch, need,
                            stream);
+}
+
+static size_t a256(size_t b) { return (b + 255) & ~(size_t)255; }
+
+size_t w8a8_moe_scratch_bytes(int rows, int dim, int top_k, int expert_hidden) {
+    if (rows <= 0 || dim <= 0 || top_k <= 0 || expert_hidden <= 0) return 0;
+    return a256((size_t)rows * dim) + a256((size_t)rows * 4) + a256((size_t)rows * top_k * expert_hidden * 4) +
+           a256((size_t)rows * top_k * 4);
+}
+
+int w8a8_moe_ffn(const float* x, const float* norm_g, float eps, int rows, int dim, const int8_t* router_q,
+                 const float* router_s, int experts, int top_k, const int8_t* gate_q, const float* gate_s,
+                 const int8_t* up_q, const float* up_s, int expert_hidden, const int8_t* down_q, const float* down_s,
+                 const float* resid, float* y, int32_t* ids, float* w, void* scratch, size_t scratch_bytes,
+                 void* stream) {
+    if (!x || !router_q || !router_s || !gate_q || !gate_s || !up_q || !up_s || !down_q || !down_s ||
+        !resid || !y || !ids || !w || !scratch)
+        return W8A8_EINVAL;
+    if (rows <= 0 || rows > W8A8_MAX_ROWS || dim <= 0 || experts <= 0 || experts > kMoeMaxExperts || top_k <= 0 ||
+        top_k > kMoeMaxTopK || top_k > experts || expert_hidden <= 0)
+        return W8A8_EINVAL;
+    if (dim % 16 || expert_hidden % 16) return W8A8_EALIGN;
+    if (!al16(x) || (norm_g && !al16(norm_g)) || !al16(router_q) || !al16(gate_q) || !al16(up_q) || !al16(down_q) ||
+        !al16(scratch))
+        return W8A8_EALIGN;
+    if (scratch_bytes < w8a8_moe_scratch_bytes(rows, dim, top_k, expert_hidden)) return W8A8_ESCRATCH;
+    MoeParams p{};
+    p.m = rows, p.dim = dim, p.experts = experts, p.top_k = top_k, p.ih = expert_hidden;
+    p.x = x, p.norm_g = norm_g, p.eps = eps, p.inv_dim = inv_of(dim);
+    p.rq = router_q, p.rs = router_s, p.gq = gate_q, p.gs = gate_s, p.uq = up_q, p.us = up_s;
+    p.dq = down_q, p.ds = down_s, p.resid = resid, p.y = y, p.ids = ids, p.w = w;
+    char* sp = static_cast<char*>(scratch);
+    p.xq = reinterpret_cast<int8_t*>(sp);
+    sp += a256((size_t)rows * dim);
+    p.s_x = reinterpret_cast<float*>(sp);
+    sp += a256((size_t)rows * 4);
+    p.h = reinterpret_cast<float*>(sp);
+    sp += a256((size_t)rows * top_k * expert_hidden * 4);
+    p.amax = reinterpret_cast<uint32_t*>(sp);
+    for (int i = 0; i < 3; ++i)
+        if (moe_smem(p, i) > 200 * 1024) return W8A8_EINVAL;
+    return cuda_status(launch_moe(p, S(stream)));
 }
 
 size_t w8a8_attn_scratch_bytes(int rows, int heads, int kv_heads, int head_dim, int seq_len) {

@@ -33,7 +33,8 @@ __device__ unsigned int g_gemv_errors;                        // bit 1: a tile w
 
 constexpr int kMaxStages = 8;
 constexpr size_t kRingBytes = 96 * 1024;                      // weight ring per CTA
-constexpr size_t kStreamRingBytes = 128 * 1024;               // ... for a GEMV of many tiles per CTA
+constexpr size_t kStreamRingBytes = 96 * 1024;                // ... for a GEMV of many tiles per CTA
+constexpr int kStreamCtasPerSm = 2;                           // streaming: two CTAs per SM hide more latency
 constexpr size_t kStreamBytes = (size_t)64 << 20;             // weights from which a GEMV counts as streaming
 constexpr int kConsumers = kThreads;                          // 8 consumer warps
 constexpr int kGemvThreads = kThreads + 32;                   // + 1 producer warp
@@ -349,10 +350,12 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(LinearParams p, G
             if (lane == 0) mbar_arrive(&empty[s]);
 #pragma unroll
             for (int m = 0; m < MR; ++m) {
-#pragma unroll 1
-                for (int o = S / 2; o > 0; o >>= 1) {
-                    acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], o);
-                    acc2[m] += __shfl_xor_sync(0xffffffffu, acc2[m], o);
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) {             // S <= 32: the levels below S
+                    if (o < S) {
+                        acc[m] += __shfl_xor_sync(0xffffffffu, acc[m], o);
+                        if (two) acc2[m] += __shfl_xor_sync(0xffffffffu, acc2[m], o);
+                    }
                 }
             }
             if (sl == 0 && r < rows) {
@@ -428,8 +431,9 @@ struct Tiling {
 // Tile rows: a power of two between 8 and 256. A GEMV whose rows fit one tile
 // per CTA (up to 32 KB per matrix) takes that: the per-tile code then runs
 // once, and the ring is one tile (small, so the next kernel's CTAs fit beside
-// it). Otherwise about 16 KB per matrix, or 32 KB with a 128 KB ring when the
-// weights stream through each CTA many times (less fixed work per byte).
+// it). Otherwise about 16 KB per matrix, or, when the weights stream through
+// each CTA many times, 32 KB tiles (less fixed work per byte) in a 96 KB ring
+// with two CTAs per SM (more warps to hide the dot products' latency).
 // Consumer threads split a row's K (256 / rows threads per row).
 static Tiling tiling(const LinearParams& p, int mr, int pro, int epi) {
     Tiling t{};
@@ -450,7 +454,8 @@ static Tiling tiling(const LinearParams& p, int mr, int pro, int epi) {
     size_t st = (stream ? kStreamRingBytes : kRingBytes) / stage;
     t.cf.stages = (int)(st < 2 ? 2 : (st > (size_t)kMaxStages ? kMaxStages : st));
     t.cf.ntiles = (p.n + pw - 1) / pw;
-    t.grid = t.cf.ntiles < sms ? t.cf.ntiles : sms;
+    const int slots = stream ? kStreamCtasPerSm * sms : sms;
+    t.grid = t.cf.ntiles < slots ? t.cf.ntiles : slots;
     const int per = (t.cf.ntiles + t.grid - 1) / t.grid;     // tiles of a CTA, at most
     if (t.cf.stages > per) t.cf.stages = per;
     const size_t nj = (size_t)((t.cf.ntiles + t.grid - 1) / t.grid) * pw;   // rows of a CTA, at most

@@ -1,0 +1,254 @@
+// Mixture-of-experts FFN of the W8A8 decoder (hf_generic.QMixtralMoe.route /
+// _row, compiler/frontend/hf_generic.py:641-657; the Granite-MoE router is the
+// same softmax over the Top-k logits): y = resid + sum_k w_k * expert_k(x_n),
+// x_n = rmsnorm(x), every expert a SwiGLU of W8A8 linears, for up to 16 rows,
+// each row with its own Top-k.
+//
+// Three launches (programmatic dependent launch between them):
+//  1. router, one CTA per row: fused rmsnorm + quant_act prologue (the int8
+//     row is kept for the experts), the router GEMV (its rows bulk-copied before
+//     the wait), the Top-k by value then lower id (llm docs:
+//     moe_native_lowering_design.md:342-345), e = EXP(v - v0), w = e*RECIP(sum e)
+//     with the D = 16 ordered sum; clears the experts' amax slots;
+//  2. gate / up, one CTA per (row, slot, 16 rows of the expert's hidden):
+//     h = (g*RECIP(1 + EXP(-g)))*u, the slot's amax |h| by atomic max;
+//  3. down + combine, one CTA per (row, 16 outputs): every slot's h requantized
+//     (quant_act with that amax), the k down GEMVs, and the combine folded in
+//     k order from 0: y = ((0 + w_0 y_0) + w_1 y_1) + ..., then resid + y.
+// The expert ids are known only after launch 1, so the expert weights are
+// fetched after the wait (bulk copies of whole row tiles).
+#include "linear_common.cuh"
+#include "pdl.cuh"
+
+namespace w8a8 {
+
+__device__ unsigned int g_moe_errors;                         // bit 3: a weight-tile copy wait gave up
+
+constexpr int kMoeThreads = 256;
+constexpr int kMoeTile = 16;                                   // expert rows per CTA (launches 2 and 3)
+
+// ---------------------------------------------------------------- launch 1
+__global__ void __launch_bounds__(kMoeThreads) moe_router_kernel(MoeParams p) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    const int row = blockIdx.x, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int E = p.experts, K = p.top_k, dim = p.dim;
+    int8_t* wt = reinterpret_cast<int8_t*>(smem);                         // router rows [E][dim]
+    int8_t* xs = wt + (size_t)E * dim;                                    // [dim]
+    float* xf = reinterpret_cast<float*>(xs + dim);                       // [dim] staging
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ float sx[1], red[32], sc[kMoeMaxExperts], ev[kMoeMaxExperts];
+    __shared__ int ids_s[kMoeMaxExperts];
+    if (tid == 0) {                                                       // router weights: constants
+        mbar_init(&bar, 1);
+        mbar_fence_init();
+        mbar_expect_tx(&bar, (uint32_t)(E * dim));
+        bulk_g2s(wt, p.rq, (uint32_t)(E * dim), &bar);
+    }
+    pdl_wait();
+    pdl_trigger();
+    LinearParams lp{};
+    lp.m = 1, lp.k = dim, lp.x = p.x + (size_t)row * dim, lp.norm_g = p.norm_g, lp.eps = p.eps;
+    lp.inv_k = p.inv_dim;
+    if (p.norm_g != nullptr) prologue<1, PRO_RMSQ>(lp, xs, xf, sx, red);   // both end with a block barrier
+    else prologue<1, PRO_QUANT>(lp, xs, xf, sx, red);
+    for (int c = tid; c < dim / 16; c += kMoeThreads)                     // the int8 row, for the experts
+        reinterpret_cast<int4*>(p.xq + (size_t)row * dim)[c] = reinterpret_cast<const int4*>(xs)[c];
+    if (tid == 0) p.s_x[row] = sx[0];
+    if (tid < K) p.amax[row * K + tid] = 0u;                              // the experts' atomic maxima
+    const bool ok = mbar_wait(&bar, 0u);
+    if (!ok && tid == 0) atomicOr(&g_moe_errors, 8u);
+    // scores: warp w takes rows w, w + 8, ...; (f32(acc) * s_r) * s_x
+    for (int e = warp; e < E; e += kMoeThreads / 32) {
+        int acc = 0;
+        const int4* wr = reinterpret_cast<const int4*>(wt + (size_t)e * dim);
+        const int4* xr = reinterpret_cast<const int4*>(xs);
+        for (int c = lane; c < dim / 16; c += 32) {
+            const int4 a = wr[c], b = xr[c];
+            acc = dp4a(a.w, b.w, dp4a(a.z, b.z, dp4a(a.y, b.y, dp4a(a.x, b.x, acc))));
+        }
+        acc = warp_sum_i(acc);
+        if (lane == 0) sc[e] = fmul(fmul(i2f(acc), __ldg(p.rs + e)), sx[0]);
+    }
+    __syncthreads();
+    if (warp == 0) {
+        // Top-k: keys (value, then the lower id) held two per lane; k rounds of a warp max
+        unsigned long long k0 = lane < E ? argmax_key(sc[lane], lane) : 0ull;
+        unsigned long long k1 = lane + 32 < E ? argmax_key(sc[lane + 32], lane + 32) : 0ull;
+        for (int j = 0; j < K; ++j) {
+            unsigned long long best = k0 > k1 ? k0 : k1;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+                const unsigned long long t = __shfl_xor_sync(0xffffffffu, best, o);
+                best = t > best ? t : best;
+            }
+            const int id = (int)(0xFFFFFFFFu - (uint32_t)(best & 0xFFFFFFFFull));
+            if (best == k0) k0 = 0ull;                                    // keys are unique: one lane owns it
+            if (best == k1) k1 = 0ull;
+            if (lane == 0) ids_s[j] = id;
+        }
+        __syncwarp();
+        // e_j = EXP(v_j - v_0), w_j = e_j * RECIP(sum e) (the sum in the D = 16 order)
+        const float v0 = sc[ids_s[0]];
+        for (int j = lane; j < K; j += 32) ev[j] = sfu_exp(fsub(sc[ids_s[j]], v0));
+        __syncwarp();
+        const float s = red_sum16([&](int i) { return ev[i]; }, K, lane);
+        const float rs = sfu_recip(s);
+        for (int j = lane; j < K; j += 32) {
+            p.ids[row * K + j] = ids_s[j];
+            p.w[row * K + j] = fmul(ev[j], rs);
+        }
+    }
+}
+
+// ---------------------------------------------------------------- launch 2
+__global__ void __launch_bounds__(kMoeThreads) moe_up_kernel(MoeParams p) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    const int tile = blockIdx.x, slot = blockIdx.y, row = blockIdx.z, tid = threadIdx.x, lane = tid & 31;
+    const int K = p.top_k, dim = p.dim, ih = p.ih, i0 = tile * kMoeTile;
+    int8_t* wg = reinterpret_cast<int8_t*>(smem);                        // gate rows [16][dim]
+    int8_t* wu = wg + (size_t)kMoeTile * dim;                            // up rows [16][dim]
+    int8_t* xs = wu + (size_t)kMoeTile * dim;                            // [dim]
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ float red[32];
+    __shared__ int e_s;
+    if (tid == 0) {
+        mbar_init(&bar, 1);
+        mbar_fence_init();
+    }
+    pdl_wait();
+    pdl_trigger();
+    if (tid == 0) {                                                       // the slot's expert: known now
+        const int e = p.ids[row * K + slot];
+        e_s = e;
+        const uint32_t bytes = (uint32_t)(kMoeTile * dim);
+        mbar_expect_tx(&bar, 2u * bytes);
+        bulk_g2s(wg, p.gq + ((size_t)e * ih + i0) * dim, bytes, &bar);
+        bulk_g2s(wu, p.uq + ((size_t)e * ih + i0) * dim, bytes, &bar);
+    }
+    for (int c = tid; c < dim / 16; c += kMoeThreads)
+        reinterpret_cast<int4*>(xs)[c] = __ldcg(reinterpret_cast<const int4*>(p.xq + (size_t)row * dim) + c);
+    const float sx = __ldcg(p.s_x + row);
+    __syncthreads();
+    const bool ok = mbar_wait(&bar, 0u);
+    if (!ok && tid == 0) atomicOr(&g_moe_errors, 8u);
+    const int e = e_s;
+    // thread t: row r = t / 16 of the tile, 16-byte chunks s, s + 16, ... of it
+    const int r = tid / 16, sl = tid % 16;
+    int ag = 0, au = 0;
+    for (int c = sl; c < dim / 16; c += 16) {
+        const int4 x = reinterpret_cast<const int4*>(xs)[c];
+        const int4 a = reinterpret_cast<const int4*>(wg + (size_t)r * dim)[c];
+        const int4 b = reinterpret_cast<const int4*>(wu + (size_t)r * dim)[c];
+        ag = dp4a(a.w, x.w, dp4a(a.z, x.z, dp4a(a.y, x.y, dp4a(a.x, x.x, ag))));
+        au = dp4a(b.w, x.w, dp4a(b.z, x.z, dp4a(b.y, x.y, dp4a(b.x, x.x, au))));
+    }
+#pragma unroll
+    for (int o = 8; o > 0; o >>= 1) {
+        ag += __shfl_xor_sync(0xffffffffu, ag, o);
+        au += __shfl_xor_sync(0xffffffffu, au, o);
+    }
+    uint32_t am = 0u;
+    if (sl == 0) {
+        const int i = i0 + r;
+        const float g = fmul(fmul(i2f(ag), __ldg(p.gs + (size_t)e * ih + i)), sx);
+        const float u = fmul(fmul(i2f(au), __ldg(p.us + (size_t)e * ih + i)), sx);
+        const float h = silu_gate(g, u);
+        p.h[((size_t)row * K + slot) * ih + i] = h;
+        am = __float_as_uint(fabsf(h));                                   // as bits: NaN above numbers
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) am = max(am, __shfl_xor_sync(0xffffffffu, am, o));
+    if (lane == 0 && am != 0u) atomicMax(p.amax + row * K + slot, am);
+    if (!ok) mbar_wait(&bar, 0u);                                         // no copy may land after exit
+}
+
+// ---------------------------------------------------------------- launch 3
+__global__ void __launch_bounds__(kMoeThreads) moe_down_kernel(MoeParams p) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    const int tile = blockIdx.x, row = blockIdx.y, tid = threadIdx.x;
+    const int K = p.top_k, dim = p.dim, ih = p.ih, n0 = tile * kMoeTile;
+    int8_t* wd = reinterpret_cast<int8_t*>(smem);                        // [K][16][ih] down rows
+    int8_t* hq = wd + (size_t)K * kMoeTile * ih;                         // [K][ih]
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ int e_s[kMoeMaxTopK];
+    __shared__ float w_s[kMoeMaxTopK], sh_s[kMoeMaxTopK], inv_s[kMoeMaxTopK];
+    if (tid == 0) {
+        mbar_init(&bar, 1);
+        mbar_fence_init();
+    }
+    pdl_wait();
+    pdl_trigger();
+    if (tid < K) {
+        e_s[tid] = p.ids[row * K + tid];
+        w_s[tid] = p.w[row * K + tid];
+        const float s = fmul(__uint_as_float(__ldcg(p.amax + row * K + tid)), W8A8_C127);
+        sh_s[tid] = s;
+        inv_s[tid] = sfu_recip(s);
+    }
+    __syncthreads();
+    if (tid == 0) {
+        const uint32_t bytes = (uint32_t)(kMoeTile * ih);
+        mbar_expect_tx(&bar, (uint32_t)K * bytes);
+        for (int j = 0; j < K; ++j)
+            bulk_g2s(wd + (size_t)j * kMoeTile * ih, p.dq + ((size_t)e_s[j] * dim + n0) * ih, bytes, &bar);
+    }
+    // every slot's h row -> int8 with its own scale (quant_act of that expert's h)
+    for (int i = tid; i < K * ih / 4; i += kMoeThreads) {
+        const int j = (i * 4) / ih;
+        const float4 v = __ldcg(reinterpret_cast<const float4*>(p.h + (size_t)row * K * ih) + i);
+        const float inv = inv_s[j];
+        reinterpret_cast<char4*>(hq)[i] =
+            make_char4(to_i8(fmul(v.x, inv)), to_i8(fmul(v.y, inv)), to_i8(fmul(v.z, inv)), to_i8(fmul(v.w, inv)));
+    }
+    __syncthreads();
+    const bool ok = mbar_wait(&bar, 0u);
+    if (!ok && tid == 0) atomicOr(&g_moe_errors, 8u);
+    const int r = tid / 16, sl = tid % 16, n = n0 + r;
+    float y = 0.f;
+    for (int j = 0; j < K; ++j) {                                         // k order: the combine's order
+        int acc = 0;
+        const int4* a4 = reinterpret_cast<const int4*>(wd + ((size_t)j * kMoeTile + r) * ih);
+        const int4* h4 = reinterpret_cast<const int4*>(hq + (size_t)j * ih);
+        for (int c = sl; c < ih / 16; c += 16) {
+            const int4 a = a4[c], b = h4[c];
+            acc = dp4a(a.w, b.w, dp4a(a.z, b.z, dp4a(a.y, b.y, dp4a(a.x, b.x, acc))));
+        }
+#pragma unroll
+        for (int o = 8; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+        const float yk = fmul(fmul(i2f(acc), __ldg(p.ds + (size_t)e_s[j] * dim + n)), sh_s[j]);
+        y = fadd(y, fmul(w_s[j], yk));
+    }
+    if (sl == 0) p.y[(size_t)row * dim + n] = fadd(__ldcg(p.resid + (size_t)row * dim + n), y);
+    if (!ok) mbar_wait(&bar, 0u);
+}
+
+// ---------------------------------------------------------------- host side
+size_t moe_smem(const MoeParams& p, int which) {
+    if (which == 0) return (size_t)p.experts * p.dim + (size_t)p.dim * 5;
+    if (which == 1) return (size_t)2 * kMoeTile * p.dim + p.dim;
+    return (size_t)p.top_k * kMoeTile * p.ih + (size_t)p.top_k * p.ih;
+}
+
+cudaError_t launch_moe(const MoeParams& p, cudaStream_t st) {
+    void (*kern[3])(MoeParams) = {moe_router_kernel, moe_up_kernel, moe_down_kernel};
+    const dim3 grids[3] = {dim3(p.m), dim3(p.ih / kMoeTile, p.top_k, p.m), dim3(p.dim / kMoeTile, p.m)};
+    for (int i = 0; i < 3; ++i) {
+        const size_t sm = moe_smem(p, i);
+        cudaError_t e = cudaFuncSetAttribute(kern[i], cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+        if (e != cudaSuccess) return e;
+        e = cudaFuncSetAttribute(kern[i], cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+        if (e != cudaSuccess) return e;
+        e = launch_k(kern[i], grids[i], dim3(kMoeThreads), sm, st, p);
+        if (e != cudaSuccess) return e;
+    }
+    return cudaSuccess;
+}
+
+unsigned int moe_read_clear_errors() {
+    unsigned int v = 0, zero = 0;
+    cudaMemcpyFromSymbol(&v, g_moe_errors, sizeof(v));
+    cudaMemcpyToSymbol(g_moe_errors, &zero, sizeof(zero));
+    return v;
+}
+
+}  // namespace w8a8

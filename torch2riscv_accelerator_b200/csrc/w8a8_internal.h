@@ -57,6 +57,35 @@ struct AttnParams {
     int chunk;                // cache positions per CTA
 };
 
+// Mixture-of-experts FFN (moe.cu): rows m, model dim, experts E, Top-k, expert hidden ih.
+constexpr int kMoeMaxExperts = 64;
+constexpr int kMoeMaxTopK = 16;
+struct MoeParams {
+    int m, dim, experts, top_k, ih;
+    const float* x;           // [m, dim] residual stream (the FFN input before its RMSNorm)
+    const float* norm_g;      // [dim] the FFN RMSNorm gain
+    float eps, inv_dim;
+    const int8_t* rq;         // [E, dim] router rows
+    const float* rs;          // [E]
+    const int8_t* gq;         // [E, ih, dim] gate rows
+    const float* gs;          // [E, ih]
+    const int8_t* uq;         // [E, ih, dim] up rows
+    const float* us;          // [E, ih]
+    const int8_t* dq;         // [E, dim, ih] down rows
+    const float* ds;          // [E, dim]
+    const float* resid;       // [m, dim] (may equal y)
+    float* y;                 // [m, dim] out: resid + moe
+    int32_t* ids;             // [m, k] chosen experts (out)
+    float* w;                 // [m, k] their weights (out)
+    int8_t* xq;               // scratch [m, dim]
+    float* s_x;               // scratch [m]
+    float* h;                 // scratch [m, k, ih]
+    uint32_t* amax;           // scratch [m, k]
+};
+size_t moe_smem(const MoeParams& p, int which);
+cudaError_t launch_moe(const MoeParams& p, cudaStream_t st);
+unsigned int moe_read_clear_errors();
+
 constexpr int kMaxRows = 16;  // query rows per attention call
 constexpr int kMaxCluster = 8;  // attention CTAs per KV head (portable cluster size)
 

@@ -118,6 +118,31 @@ def ffn_swiglu(x, norm_g, eps, w_gate, s_gate, w_up, s_up, scratch, h=None, h_q=
     return h, h_q, s_h
 
 
+def moe_scratch(rows, dim, top_k, expert_hidden, device):
+    n = _lib.load().w8a8_moe_scratch_bytes(rows, dim, top_k, expert_hidden)
+    return torch.zeros(n, dtype=torch.uint8, device=device)
+
+
+def moe_ffn(x, norm_g, eps, router_q, router_s, top_k, gate_q, gate_s, up_q, up_s, down_q, down_s, scratch,
+            resid=None, out=None, ids=None, w=None):
+    """MoE FFN rows (hf_generic.QMixtralMoe): returns (y = resid + moe(rmsnorm(x)),
+    ids [rows, top_k] int32, w [rows, top_k] fp32). resid defaults to x; out may
+    be resid (in place)."""
+    _need(x, F32, "x")
+    m, dim = x.shape
+    experts, ih = router_q.shape[0], gate_q.shape[1]
+    dev = x.device
+    resid = x if resid is None else resid
+    out = torch.empty(m, dim, dtype=F32, device=dev) if out is None else out
+    ids = torch.empty(m, top_k, dtype=torch.int32, device=dev) if ids is None else ids
+    w = torch.empty(m, top_k, dtype=F32, device=dev) if w is None else w
+    _lib.check("w8a8_moe_ffn", _lib.load().w8a8_moe_ffn(
+        _p(x), _p(norm_g), float(eps), m, dim, _p(router_q), _p(router_s), experts, top_k, _p(gate_q), _p(gate_s),
+        _p(up_q), _p(up_s), ih, _p(down_q), _p(down_s), _p(resid), _p(out), _p(ids), _p(w), _p(scratch),
+        scratch.numel(), _st()))
+    return out, ids, w
+
+
 def attn_scratch(rows, heads, kv_heads, head_dim, seq_len, device):
     n = _lib.load().w8a8_attn_scratch_bytes(rows, heads, kv_heads, head_dim, seq_len)
     return torch.zeros(n, dtype=torch.uint8, device=device)
