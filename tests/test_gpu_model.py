@@ -137,6 +137,21 @@ def test_c2_full_dims_two_layers_equals_oracle():
         assert dev.forward(int(toks[p])).tobytes() == ora.forward(int(toks[p]), p).tobytes()
 
 
+def test_c4_moe_two_layers_equals_oracle():
+    """Granite-MoE dimensions (dim 1024, 16/8 heads of 64, 32 experts, Top-8,
+    expert hidden 512) truncated to 2 layers and a 4096-token vocabulary: the
+    MoE FFN in the decode chain, bit-exact with the oracle for a 20-token
+    prefill (a 16-row chunk, each row with its own Top-k) and 3 decode steps."""
+    cfg = C.C4.with_(layers=2, vocab=4096)
+    qw = W.QuantWeights(cfg, seed=5, gains="random", calib_tokens=np.arange(8))
+    dev = LlamaDevice((cfg, qw, qw.kv_scales))
+    ora = OM.OracleDecoder(cfg, qw, qw.kv_scales)
+    toks = np.random.default_rng(4).integers(0, cfg.vocab, 23)
+    assert dev.prefill(toks[:20]).tobytes() == ora.forward_rows(toks[:20], range(20)).tobytes()
+    for p in range(20, 23):
+        assert dev.forward(int(toks[p])).tobytes() == ora.forward(int(toks[p]), p).tobytes()
+
+
 def test_generate_greedy_matches_forward_argmax():
     g, cfg, w = _tiny("b")
     dev = LlamaDevice((cfg, W.from_fp32(cfg, w), g["b_kv"]))

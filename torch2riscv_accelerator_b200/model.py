@@ -34,8 +34,6 @@ CHUNK = 16                                         # prefill rows per chunk (the
 class DeviceDecoder:
     def __init__(self, cfg, qw, kv_scales, device="cuda", max_rows=CHUNK):
         cfg.validate()
-        if cfg.moe:
-            raise NotImplementedError("MoE layers: not on this path yet")
         self.cfg, self.dev, self.max_rows = cfg, torch.device(device), max_rows
         t = lambda a, dt=None: torch.as_tensor(np.ascontiguousarray(a), dtype=dt).to(self.dev)
         self.emb_q, self.emb_s = t(qw.emb_q, I8), t(qw.emb_s, F32)
@@ -64,6 +62,10 @@ class DeviceDecoder:
         self.key = z(R, dt=torch.int64)                # packed greedy argmax per row (classifier epilogue)
         self.attn_scratch = ops.attn_scratch(R, cfg.heads, cfg.kv_heads, hd, T, self.dev)
         self.ffn_scratch = ops.ffn_scratch(R, self.dev)
+        if cfg.moe:                                # routing of the last run (per layer) and the MoE scratch
+            self.moe_ids = z(cfg.layers, R, cfg.top_k, dt=I32)
+            self.moe_w = z(cfg.layers, R, cfg.top_k)
+            self.moe_scratch = ops.moe_scratch(R, cfg.dim, cfg.top_k, cfg.expert_hidden, self.dev)
         self._args = {}
         self.graphs = {}
 
@@ -93,6 +95,11 @@ class DeviceDecoder:
             ops.linear_fused(x, w["wqkv"], w["s_wqkv"], norm_g=w["rms_att"], eps=c.eps, out=qkv)
             ops.attn(args[l])
             ops.linear_fused(att, w["wo"], w["s_wo"], resid=x, out=x)
+            if c.moe:                                                          # router, gate/up, down+combine
+                ops.moe_ffn(x, w["rms_ffn"], c.eps, w["router"], w["s_router"], c.top_k, w["e_gate"],
+                            w["s_e_gate"], w["e_up"], w["s_e_up"], w["e_down"], w["s_e_down"], self.moe_scratch,
+                            resid=x, out=x, ids=self.moe_ids[l, :rows], w=self.moe_w[l, :rows])
+                continue
             ops.ffn_swiglu(x, w["rms_ffn"], c.eps, w["w1"], w["s_w1"], w["w3"], w["s_w3"], None, h=h,
                            requant=False)
             ops.linear_fused(h, w["w2"], w["s_w2"], resid=x, out=x)          # quant_act(h) in the prologue
@@ -102,8 +109,9 @@ class DeviceDecoder:
 
     def kernel_launches(self, rows=1):
         """Kernels one run() launches: embed, per layer the qkv GEMV, the
-        attention, wo, SwiGLU, w2, then the classifier."""
-        return 1 + 5 * self.cfg.layers + 1
+        attention, wo, then SwiGLU and w2 (or the MoE router, gate/up and
+        down + combine), then the classifier."""
+        return 1 + (6 if self.cfg.moe else 5) * self.cfg.layers + 1
 
     def capture(self, rows, logits_rows=1):
         """Capture run(rows) as a CUDA graph (after one eager warm-up run)."""
@@ -172,8 +180,14 @@ class DeviceDecoder:
     def weight_bytes(self):
         """int8 weight bytes streamed per decode token (+ fp32 scales)."""
         c = self.cfg
-        per_layer = c.dim * c.qkv_dim + c.q_dim * c.dim + 3 * c.dim * c.hidden
-        scales = 4 * (c.qkv_dim + c.dim + 2 * c.hidden + c.dim)
+        per_layer = c.dim * c.qkv_dim + c.q_dim * c.dim
+        scales = 4 * (c.qkv_dim + c.dim)
+        if c.moe:                                  # the router and the k chosen experts
+            per_layer += c.experts * c.dim + c.top_k * 3 * c.dim * c.expert_hidden
+            scales += 4 * (c.experts + c.top_k * (2 * c.expert_hidden + c.dim))
+        else:
+            per_layer += 3 * c.dim * c.hidden
+            scales += 4 * (2 * c.hidden + c.dim)
         return c.layers * (per_layer + scales) + c.vocab * c.dim + 4 * c.vocab
 
     def kv_bytes(self, t):
