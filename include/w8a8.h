@@ -64,7 +64,7 @@ int w8a8_embed(const int32_t* tokens, int rows, const int8_t* emb_q, const float
  * token reached w8a8_embed; bit 1: a GEMV weight-tile wait gave up after its
  * bounded spin and the kernel stopped early; bit 2: an attention cache-tile
  * copy did not land within its bounded wait; bit 3: the same for an MoE weight
- * tile). Synchronous with the device.
+ * tile; bit 4: a tensor-core GEMM pipeline wait). Synchronous with the device.
  * Plays the role of the overlay's sticky list status (llm/sa_funcsim.py:62-66,
  * firmware/rt/rt_fw.c:53-60). */
 int w8a8_error_flags(uint32_t* flags);
@@ -133,6 +133,29 @@ int w8a8_ffn_swiglu(const float* x, const float* norm_g, float eps, int rows, in
 int w8a8_ffn_swiglu_noalloc(const float* x, const float* norm_g, float eps, int rows, int k, const int8_t* w_gate,
                             const float* s_gate, const int8_t* w_up, const float* s_up, int hidden, float* h,
                             int8_t* h_q, float* s_h, void* stream);
+
+/* Rows of x -> int8 rows for the tensor-core GEMM: xq = quant_act(x), or
+ * quant_act(rmsnorm(x, norm_g)) when norm_g is not NULL; s_x [rows]. Any row
+ * count. Replaces the quant_act (+ rmsnorm) steps that precede each linear of
+ * a prefill chunk (compiler/frontend/qhf.py:376-405, llm/ref_model.py:191-207). */
+int w8a8_quant_rows(const float* x, const float* norm_g, float eps, int rows, int k, int8_t* xq, float* s_x,
+                    void* stream);
+
+/* W8A8 linear for any number of rows on the tensor cores (tcgen05 kind::i8,
+ * int32 accumulators in tensor memory): the same results as w8a8_linear, bit
+ * for bit. xq [rows, k] int8 (w8a8_quant_rows), s_x [rows]; w [n, k], s_w [n];
+ * y [rows, n] = (f32(acc) * s_w) * s_x [+ resid]; acc [rows, n] or NULL.
+ * Replaces the prefill linear rows (SahlExpandKernels.cpp expandLinearRows,
+ * compiler/frontend/qhf.py:376-405) and batched decode linears
+ * (llm/runtime.py BatchLlamaDevice.step :193-208). */
+int w8a8_gemm(const int8_t* xq, const float* s_x, int rows, int k, const int8_t* w, const float* s_w, int n,
+              const float* resid, float* y, int32_t* acc, void* stream);
+
+/* The SwiGLU pair on the tensor cores: h = (g * RECIP(1 + EXP(-g))) * u with
+ * g, u the W8A8 linears of w_gate and w_up [hidden, k] (llm/ref_model.py:246-250;
+ * the prefill FFN of compiler/frontend/qhf.py:396-400). h [rows, hidden]. */
+int w8a8_gemm_swiglu(const int8_t* xq, const float* s_x, int rows, int k, const int8_t* w_gate, const float* s_gate,
+                     const int8_t* w_up, const float* s_up, int hidden, float* h, void* stream);
 
 /* Mixture-of-experts FFN for up to 16 rows, each with its own Top-k:
  * y = resid + sum_k w_k * expert_k(rmsnorm(x)), where the router's W8A8 logits

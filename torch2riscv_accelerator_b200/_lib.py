@@ -37,6 +37,9 @@ PROTOTYPES = {
     "w8a8_ffn_scratch_bytes": (Z, [I]),
     "w8a8_ffn_swiglu": (I, [P, P, F, I, I, P, P, P, P, I, P, P, P, P, Z, P]),
     "w8a8_ffn_swiglu_noalloc": (I, [P, P, F, I, I, P, P, P, P, I, P, P, P, P]),
+    "w8a8_quant_rows": (I, [P, P, F, I, I, P, P, P]),
+    "w8a8_gemm": (I, [P, P, I, I, P, P, I, P, P, P, P]),
+    "w8a8_gemm_swiglu": (I, [P, P, I, I, P, P, P, P, I, P, P]),
     "w8a8_moe_scratch_bytes": (Z, [I, I, I, I]),
     "w8a8_moe_ffn": (I, [P, P, F, I, I, P, P, I, I, P, P, P, P, I, P, P, P, P, P, P, P, Z, P]),
     "w8a8_attn_scratch_bytes": (Z, [I, I, I, I, I]),

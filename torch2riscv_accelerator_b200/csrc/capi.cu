@@ -87,7 +87,8 @@ int w8a8_error_flags(uint32_t* flags) {
     if (!flags) return W8A8_EINVAL;
     unsigned int v = 0;
     int st = cuda_status(read_clear_errors(&v));
-    *flags = v | gemv_read_clear_errors() | attn_read_clear_errors() | moe_read_clear_errors();
+    *flags = v | gemv_read_clear_errors() | attn_read_clear_errors() | moe_read_clear_errors() |
+             gemm_read_clear_errors();
     return st;
 }
 
@@ -173,6 +174,44 @@ int w8a8_ffn_swiglu_noalloc(const float* x, const float* norm_g, float eps, int 
     if (cudaMemsetAsync(scratch, 0, need, S(stream)) != cudaSuccess) return W8A8_ECUDA;
     return w8a8_ffn_swiglu(x, norm_g, eps, rows, k, w_gate, s_gate, w_up, s_up, hidden, h, h_q, s_h, scratch, need,
                            stream);
+}
+
+int w8a8_quant_rows(const float* x, const float* norm_g, float eps, int rows, int k, int8_t* xq, float* s_x,
+                    void* stream) {
+    if (!x || !xq || !s_x || rows <= 0 || k <= 0) return W8A8_EINVAL;
+    if (k % 16 || !al16(x) || !al16(xq) || (norm_g && !al16(norm_g))) return W8A8_EALIGN;
+    if ((size_t)k * 5 > 200 * 1024) return W8A8_EINVAL;
+    return cuda_status(launch_norm_quant(x, norm_g, rows, k, eps, inv_of(k), xq, s_x, S(stream)));
+}
+
+static int check_gemm(const int8_t* xq, const float* s_x, int rows, int k, const int8_t* w, const float* s_w, int n,
+                      const float* y) {
+    if (!xq || !s_x || !w || !s_w || !y || rows <= 0 || k <= 0 || n <= 0) return W8A8_EINVAL;
+    if (k % 16 || !al16(xq) || !al16(w)) return W8A8_EALIGN;
+    return W8A8_OK;
+}
+
+int w8a8_gemm(const int8_t* xq, const float* s_x, int rows, int k, const int8_t* w, const float* s_w, int n,
+              const float* resid, float* y, int32_t* acc, void* stream) {
+    int st = check_gemm(xq, s_x, rows, k, w, s_w, n, y);
+    if (st) return st;
+    if (resid && acc) return W8A8_EINVAL;
+    GemmOperands a{xq, w, nullptr};
+    GemmParams p{};
+    p.m = rows, p.n = n, p.k = k, p.s_x = s_x, p.s_w = s_w, p.resid = resid, p.y = y, p.acc = acc;
+    return cuda_status(launch_gemm(a, p, S(stream)));
+}
+
+int w8a8_gemm_swiglu(const int8_t* xq, const float* s_x, int rows, int k, const int8_t* w_gate, const float* s_gate,
+                     const int8_t* w_up, const float* s_up, int hidden, float* h, void* stream) {
+    int st = check_gemm(xq, s_x, rows, k, w_gate, s_gate, hidden, h);
+    if (st) return st;
+    if (!w_up || !s_up) return W8A8_EINVAL;
+    if (!al16(w_up)) return W8A8_EALIGN;
+    GemmOperands a{xq, w_gate, w_up};
+    GemmParams p{};
+    p.m = rows, p.n = hidden, p.k = k, p.s_x = s_x, p.s_w = s_gate, p.s_w2 = s_up, p.y = h;
+    return cuda_status(launch_gemm(a, p, S(stream)));
 }
 
 static size_t a256(size_t b) { return (b + 255) & ~(size_t)255; }

@@ -1,0 +1,271 @@
+// W8A8 GEMM on the 5th-generation tensor cores (tcgen05, kind::i8) for many
+// rows at once (prefill chunks, batched decode):
+//   acc[m][n] = sum_k xq[m][k] * W[n][k]   (int32, exact)
+//   y[m][n]   = (f32(acc) * s_w[n]) * s_x[m]  [+ resid[m][n]]
+// or, with a second weight matrix (the SwiGLU gate / up pair),
+//   h[m][n]   = (g * RECIP(1 + EXP(-g))) * u
+// (llm/ref_model.py:198-202, :246-250; hf_generic._qlinear :583-593). The int8
+// activations come quantized per row (w8a8_quant_rows); the arithmetic after
+// the exact int32 sum is the GEMV's, so the results equal it bit for bit.
+//
+// One CTA per 128 x BN output tile (BN = 128 or 256 columns), K in 128-byte
+// steps through a ring of shared-memory stages:
+//   warp 0, one thread: TMA 2-D tile loads of xq and W (128-byte swizzle), one
+//     mbarrier per stage counting the bytes;
+//   warp 1: allocates the TMEM accumulator (BN int32 columns x 128 lanes, twice
+//     for the gate / up pair); one thread issues tcgen05.mma (M = 128, N = BN,
+//     K = 32 bytes each, A and B K-major from shared memory) and commits each
+//     stage back to the producer, then the finished accumulator to the epilogue;
+//   warps 2-5: tcgen05.ld of their 32 lanes (rows), dequant and store.
+// Every wait is bounded: on a timeout the kernel sets an error bit, still
+// waits (bounded) for its MMAs, frees TMEM and returns.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "pdl.cuh"
+#include "w8a8_internal.h"
+#include "w8a8_math.cuh"
+
+namespace w8a8 {
+
+__device__ unsigned int g_gemm_errors;                        // bit 4: a GEMM pipeline wait gave up
+
+constexpr int kGemmThreads = 192;                              // 6 warps
+constexpr int kBM = 128;                                       // rows per tile (TMEM lanes)
+constexpr int kBK = 128;                                       // K bytes per stage (one 128-byte swizzle row)
+constexpr int kStages = 4;
+
+struct GemmMaps {
+    CUtensorMap a, b, b2;                                      // xq [M][K]; W [N][K]; W2 (SwiGLU up) or unused
+};
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// K-major operand tile in shared memory, 128-byte rows, 128-byte swizzle:
+// start address >> 4, LBO 1 (unused by this layout), SBO 1024 B (8 rows),
+// version 1, layout type 2 (SWIZZLE_128B). The tile base is 1024-byte aligned.
+__device__ __forceinline__ uint64_t smem_desc(const void* tile) {
+    const uint64_t a = (uint64_t)((smem_u32(tile) >> 4) & 0x3FFFu);
+    return a | (1ull << 16) | (64ull << 32) | (1ull << 46) | (2ull << 61);
+}
+
+// kind::i8 instruction descriptor: D s32, A and B signed int8, both K-major,
+// N >> 3 at bit 17, M >> 4 at bit 24.
+__host__ __device__ constexpr uint32_t idesc_i8(int M, int N) {
+    return (2u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_i8(uint32_t tmem_d, uint64_t a, uint64_t b, uint32_t idesc, uint32_t acc) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, {%5, %5, %5, %5}, p;\n}\n" ::"r"(tmem_d),
+        "l"(a), "l"(b), "r"(idesc), "r"(acc), "r"(0u));
+}
+
+__device__ __forceinline__ void mma_commit(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
+            "r"(smem_u32(dst)),
+        "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+// 16 consecutive int32 columns of this warp's 32 lanes (one row per thread)
+__device__ __forceinline__ void tmem_ld16(uint32_t taddr, int* v) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x16.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15}, [%16];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+          "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+template <int BN, bool TWO>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+    gemm_kernel(const __grid_constant__ GemmMaps maps, GemmParams p) {
+    extern __shared__ __align__(1024) unsigned char smem_raw[];
+    // 1024-byte aligned stages: A [128][128] then B [BN][128] (then B2)
+    unsigned char* smem = reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    constexpr int kA = kBM * kBK, kB = BN * kBK;
+    constexpr int kStage = kA + kB * (TWO ? 2 : 1);
+    __shared__ __align__(8) uint64_t full[kStages], empty[kStages], acc_full;
+    __shared__ uint32_t tmem_base;
+    __shared__ int failed;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int n0 = blockIdx.x * BN, m0 = blockIdx.y * kBM;
+    const int kt_n = (p.k + kBK - 1) / kBK;
+    constexpr uint32_t kCols = TWO ? 2 * BN : BN;              // TMEM columns (a power of two >= 32)
+    if (tid == 0) {
+        failed = 0;
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        mbar_init(&acc_full, 1);
+        mbar_fence_init();
+    }
+    if (warp == 1) {                                           // TMEM accumulator
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&tmem_base)),
+                     "r"(kCols));
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = tmem_base;
+    pdl_wait();                                                // xq comes from the previous kernel
+    pdl_trigger();
+
+    if (warp == 0 && lane == 0) {
+        // producer: stage s of step kt holds xq[m0.., kt*128..] and W[n0.., kt*128..]
+        for (int kt = 0; kt < kt_n; ++kt) {
+            const int s = kt % kStages;
+            if (kt >= kStages && !mbar_wait(&empty[s], (uint32_t)(((kt / kStages) - 1) & 1))) {
+                atomicOr(&g_gemm_errors, 16u);
+                failed = 1;
+                break;
+            }
+            unsigned char* st = smem + (size_t)s * kStage;
+            mbar_expect_tx(&full[s], (uint32_t)kStage);
+            tma_load_2d(st, &maps.a, kt * kBK, m0, &full[s]);
+            tma_load_2d(st + kA, &maps.b, kt * kBK, n0, &full[s]);
+            if (TWO) tma_load_2d(st + kA + kB, &maps.b2, kt * kBK, n0, &full[s]);
+        }
+    } else if (warp == 1 && lane == 0) {
+        // MMA issuer: 4 MMAs of K = 32 bytes per stage; the descriptor start
+        // address advances 32 bytes (2 in 16-byte units) inside the swizzle row
+        const uint32_t id = idesc_i8(kBM, BN);
+        bool ok = true;
+        for (int kt = 0; kt < kt_n; ++kt) {
+            const int s = kt % kStages;
+            if (!mbar_wait(&full[s], (uint32_t)((kt / kStages) & 1))) {
+                atomicOr(&g_gemm_errors, 16u);
+                failed = 1;
+                ok = false;
+                break;
+            }
+            tc_fence_after();
+            const unsigned char* st = smem + (size_t)s * kStage;
+            const uint64_t da = smem_desc(st), db = smem_desc(st + kA);
+            const uint64_t db2 = TWO ? smem_desc(st + kA + kB) : 0ull;
+#pragma unroll
+            for (int kk = 0; kk < kBK / 32; ++kk) {
+                const uint32_t acc = (kt > 0 || kk > 0) ? 1u : 0u;
+                mma_i8(tmem, da + 2 * kk, db + 2 * kk, id, acc);
+                if (TWO) mma_i8(tmem + BN, da + 2 * kk, db2 + 2 * kk, id, acc);
+            }
+            mma_commit(&empty[s]);                             // the stage is free once these MMAs read it
+        }
+        mma_commit(&acc_full);                                 // every MMA issued so far has completed
+        (void)ok;
+    } else if (warp >= 2) {
+        // epilogue: warp w reads TMEM lanes 32*(w % 4) .. +31 (rows), 16 columns at a time
+        const bool ok = mbar_wait(&acc_full, 0u);
+        tc_fence_after();
+        if (!ok) {
+            if (lane == 0) atomicOr(&g_gemm_errors, 16u);
+        } else if (!failed) {
+            const int q = warp & 3;
+            const int m = m0 + q * 32 + lane;
+            const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
+            const float sx = m < p.m ? __ldg(p.s_x + m) : 0.f;
+            for (int c0 = 0; c0 < BN; c0 += 16) {
+                int v[16], u[16];
+                tmem_ld16(tmem + lane_addr + (uint32_t)c0, v);
+                if (TWO) tmem_ld16(tmem + lane_addr + (uint32_t)(BN + c0), u);
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {
+                    const int n = n0 + c0 + j;
+                    if (m >= p.m || n >= p.n) continue;               // (after the warp-wide TMEM loads)
+                    const size_t o = (size_t)m * p.n + n;
+                    const float g = fmul(fmul(i2f(v[j]), __ldg(p.s_w + n)), sx);
+                    if (TWO) {
+                        const float up = fmul(fmul(i2f(u[j]), __ldg(p.s_w2 + n)), sx);
+                        p.y[o] = silu_gate(g, up);
+                    } else if (p.resid != nullptr) {
+                        p.y[o] = fadd(p.resid[o], g);
+                    } else {
+                        p.y[o] = g;
+                        if (p.acc != nullptr) p.acc[o] = v[j];
+                    }
+                }
+            }
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        // the accumulator's last commit has arrived (or, after a failure, wait
+        // for the MMAs issued so far before the memory goes back)
+        if (failed) mbar_wait(&acc_full, 0u);
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(kCols));
+    }
+}
+
+// ---------------------------------------------------------------- host side
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    if (fn == nullptr) {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    }
+    return fn;
+}
+
+// 2-D int8 map of a row-major [rows][k] matrix, box 128 bytes x box_rows,
+// 128-byte swizzle; rows or k beyond the matrix read as zero
+static bool make_map(CUtensorMap* map, const void* base, int rows, int k, int box_rows) {
+    auto fn = encode_fn();
+    if (fn == nullptr) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)k};
+    const cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+size_t gemm_smem(int bn, bool two) { return (size_t)kStages * (kBM * kBK + (size_t)bn * kBK * (two ? 2 : 1)) + 1024; }
+
+template <int BN, bool TWO>
+static cudaError_t launch_gemm_t(const GemmOperands& a, const GemmParams& p, cudaStream_t st) {
+    GemmMaps maps{};
+    if (!make_map(&maps.a, a.xq, p.m, p.k, kBM) || !make_map(&maps.b, a.w, p.n, p.k, BN) ||
+        (TWO && !make_map(&maps.b2, a.w2, p.n, p.k, BN)))
+        return cudaErrorInvalidValue;
+    auto kern = gemm_kernel<BN, TWO>;
+    const size_t sm = gemm_smem(BN, TWO);
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    if (e != cudaSuccess) return e;
+    const dim3 grid((p.n + BN - 1) / BN, (p.m + kBM - 1) / kBM);
+    return launch_k(kern, grid, dim3(kGemmThreads), sm, st, maps, p);
+}
+
+cudaError_t launch_gemm(const GemmOperands& a, const GemmParams& p, cudaStream_t st) {
+    if (a.w2 != nullptr) return launch_gemm_t<128, true>(a, p, st);
+    if (p.n >= 2048) return launch_gemm_t<256, false>(a, p, st);
+    return launch_gemm_t<128, false>(a, p, st);
+}
+
+unsigned int gemm_read_clear_errors() {
+    unsigned int v = 0, zero = 0;
+    cudaMemcpyFromSymbol(&v, g_gemm_errors, sizeof(v));
+    cudaMemcpyToSymbol(g_gemm_errors, &zero, sizeof(zero));
+    return v;
+}
+
+}  // namespace w8a8

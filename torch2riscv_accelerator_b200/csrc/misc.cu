@@ -1,11 +1,40 @@
 // Small kernels of the decode path: embedding dequant, RMSNorm, quant_act,
 // greedy argmax, and elementwise SFU evaluation (the device functions exposed
 // for testing).
-#include "w8a8_internal.h"
-#include "w8a8_math.cuh"
+#include "linear_common.cuh"
 #include "pdl.cuh"
 
 namespace w8a8 {
+
+// Rows of x -> int8 rows and scales for the tensor-core GEMM: quant_act(x), or
+// quant_act(rmsnorm(x, g)) with the overlay's ordered sum (the GEMV prologue's
+// arithmetic; llm/ref_model.py:191-196, :204-207). One CTA per row.
+__global__ void __launch_bounds__(kThreads) norm_quant_kernel(const float* x, const float* g, int k, float eps,
+                                                             float inv_k, int8_t* xq, float* s_x) {
+    extern __shared__ __align__(16) unsigned char nq_smem[];
+    int8_t* xs = reinterpret_cast<int8_t*>(nq_smem);                   // [k]
+    float* xf = reinterpret_cast<float*>(nq_smem + ((k + 15) & ~15));  // [k]
+    __shared__ float sx[1], red[32];
+    pdl_wait();
+    pdl_trigger();
+    const int row = blockIdx.x;
+    LinearParams lp{};
+    lp.m = 1, lp.k = k, lp.x = x + (size_t)row * k, lp.norm_g = g, lp.eps = eps, lp.inv_k = inv_k;
+    if (g != nullptr) prologue<1, PRO_RMSQ>(lp, xs, xf, sx, red);
+    else prologue<1, PRO_QUANT>(lp, xs, xf, sx, red);
+    for (int c = threadIdx.x; c < k / 16; c += blockDim.x)
+        reinterpret_cast<int4*>(xq + (size_t)row * k)[c] = reinterpret_cast<const int4*>(xs)[c];
+    if (threadIdx.x == 0) s_x[row] = sx[0];
+}
+
+cudaError_t launch_norm_quant(const float* x, const float* g, int m, int k, float eps, float inv_k, int8_t* xq,
+                              float* s_x, cudaStream_t st) {
+    const size_t sm = (size_t)((k + 15) & ~15) + (size_t)k * 4;
+    cudaError_t e = cudaFuncSetAttribute(norm_quant_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+    if (e != cudaSuccess) return e;
+    cudaFuncSetAttribute(norm_quant_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    return launch_k(norm_quant_kernel, dim3(m), dim3(kThreads), sm, st, x, g, k, eps, inv_k, xq, s_x);
+}
 
 // Device error word of this library (bit 0: a token outside [0, vocab) reached
 // the embedding kernel). Read and cleared by w8a8_error_flags().

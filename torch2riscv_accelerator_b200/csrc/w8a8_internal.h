@@ -57,6 +57,27 @@ struct AttnParams {
     int chunk;                // cache positions per CTA
 };
 
+// Tensor-core GEMM (gemm.cu): int8 operands row-major [rows][k], K-major.
+struct GemmOperands {
+    const int8_t* xq;         // [m, k] activations, quantized per row
+    const int8_t* w;          // [n, k]
+    const int8_t* w2;         // [n, k] SwiGLU up rows, or null
+};
+struct GemmParams {
+    int m, n, k;
+    const float* s_x;         // [m]
+    const float* s_w;         // [n]
+    const float* s_w2;        // [n] (with w2)
+    const float* resid;       // [m, n] or null (may alias y)
+    float* y;                 // [m, n]: dequant (+ resid), or h with w2
+    int32_t* acc;             // [m, n] raw accumulators, or null (without resid / w2)
+};
+size_t gemm_smem(int bn, bool two);
+cudaError_t launch_gemm(const GemmOperands& a, const GemmParams& p, cudaStream_t st);
+unsigned int gemm_read_clear_errors();
+cudaError_t launch_norm_quant(const float* x, const float* g, int m, int k, float eps, float inv_k, int8_t* xq,
+                              float* s_x, cudaStream_t st);
+
 // Mixture-of-experts FFN (moe.cu): rows m, model dim, experts E, Top-k, expert hidden ih.
 constexpr int kMoeMaxExperts = 64;
 constexpr int kMoeMaxTopK = 16;

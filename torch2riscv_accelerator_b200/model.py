@@ -28,11 +28,12 @@ from . import ops
 from .weights import kv_consts
 
 I8, F32, I32 = torch.int8, torch.float32, torch.int32
-CHUNK = 16                                         # prefill rows per chunk (the reference's M)
+CHUNK = 16                                         # rows of the GEMV / attention path (the reference's M)
+PREFILL = 256                                      # rows per tensor-core prefill chunk
 
 
 class DeviceDecoder:
-    def __init__(self, cfg, qw, kv_scales, device="cuda", max_rows=CHUNK):
+    def __init__(self, cfg, qw, kv_scales, device="cuda", max_rows=CHUNK, prefill_rows=PREFILL):
         cfg.validate()
         self.cfg, self.dev, self.max_rows = cfg, torch.device(device), max_rows
         t = lambda a, dt=None: torch.as_tensor(np.ascontiguousarray(a), dtype=dt).to(self.dev)
@@ -52,12 +53,16 @@ class DeviceDecoder:
         L, Hk, T, hd = cfg.layers, cfg.kv_heads, cfg.seq_len, cfg.head_dim
         self.kc = torch.zeros(L, Hk, T, hd, dtype=I8, device=self.dev)
         self.vc = torch.zeros(L, Hk, hd, T, dtype=I8, device=self.dev)      # V transposed per head
-        R = max_rows
+        R = max(max_rows, prefill_rows)
+        self.rows_cap = R
         z = lambda *s, dt=F32: torch.zeros(*s, dtype=dt, device=self.dev)
         self.tokens, self.pos = z(R, dt=I32), z(R, dt=I32)
         self.x, self.qkv, self.att = z(R, cfg.dim), z(R, cfg.qkv_dim), z(R, cfg.q_dim)
         self.h, self.hq, self.s_h = z(R, cfg.hidden), z(R, cfg.hidden, dt=I8), z(R)
-        self.logits = z(R, cfg.vocab)
+        self.logits = z(max_rows, cfg.vocab)
+        # int8 rows and scales between the row quantizer and the tensor-core GEMMs
+        self.xq_buf = z(R * max(cfg.dim, cfg.q_dim, cfg.hidden), dt=I8)
+        self.sx_buf = z(R)
         self.next_token = z(R, dt=I32)
         self.key = z(R, dt=torch.int64)                # packed greedy argmax per row (classifier epilogue)
         self.attn_scratch = ops.attn_scratch(R, cfg.heads, cfg.kv_heads, hd, T, self.dev)
@@ -65,8 +70,9 @@ class DeviceDecoder:
         if cfg.moe:                                # routing of the last run (per layer) and the MoE scratch
             self.moe_ids = z(cfg.layers, R, cfg.top_k, dt=I32)
             self.moe_w = z(cfg.layers, R, cfg.top_k)
-            self.moe_scratch = ops.moe_scratch(R, cfg.dim, cfg.top_k, cfg.expert_hidden, self.dev)
+            self.moe_scratch = ops.moe_scratch(CHUNK, cfg.dim, cfg.top_k, cfg.expert_hidden, self.dev)
         self._args = {}
+        self._sub_args = {}
         self.graphs = {}
 
     # ------------------------------------------------------------ the program
@@ -86,6 +92,8 @@ class DeviceDecoder:
         self.pos: all rows' KV rows written, the logits of the last
         `logits_rows` rows in self.logits[:logits_rows]; with argmax, their
         greedy tokens packed in self.key (which must be zero before)."""
+        if rows > CHUNK:
+            return self._run_rows(rows, logits_rows, argmax)
         c = self.cfg
         x, qkv, att = self.x[:rows], self.qkv[:rows], self.att[:rows]
         h, hq, s_h = self.h[:rows], self.hq[:rows], self.s_h[:rows]
@@ -103,6 +111,53 @@ class DeviceDecoder:
             ops.ffn_swiglu(x, w["rms_ffn"], c.eps, w["w1"], w["s_w1"], w["w3"], w["s_w3"], None, h=h,
                            requant=False)
             ops.linear_fused(h, w["w2"], w["s_w2"], resid=x, out=x)          # quant_act(h) in the prologue
+        xl = self.x[rows - logits_rows:rows]
+        ops.classifier(xl, self.cls_q, self.cls_s, self.rms_final, c.eps, out=self.logits[:logits_rows],
+                       argmax_key=self.key[:logits_rows] if argmax else None)
+
+    def _sub_attn_args(self, l, j, m):
+        a = self._sub_args.get((l, j, m))
+        if a is None:
+            c, w = self.cfg, self.layers[l]
+            a = self._sub_args[(l, j, m)] = ops.attn_args(
+                c, m, self.pos[j:j + m], self.qkv[j:j + m], self.kc[l], self.vc[l], self.att[j:j + m],
+                self.consts[l], self.cos, self.sin, self.attn_scratch, w.get("q_norm"), w.get("k_norm"))
+        return a
+
+    def _q(self, rows, k):
+        return self.xq_buf[:rows * k].view(rows, k), self.sx_buf[:rows]
+
+    def _run_rows(self, rows, logits_rows, argmax):
+        """A prefill chunk of more than 16 rows: every linear as one tensor-core
+        GEMM over all rows (the row quantizer first), the attention and the MoE
+        FFN in 16-row sub-chunks (a row's results do not depend on the chunking:
+        each row attends its own positions, whose K/V earlier sub-chunks wrote)."""
+        c = self.cfg
+        x, qkv, att, h = self.x[:rows], self.qkv[:rows], self.att[:rows], self.h[:rows]
+        ops.embed(self.tokens[:rows], self.emb_q, self.emb_s, out=x)
+        for l, w in enumerate(self.layers):
+            xq, sx = self._q(rows, c.dim)
+            ops.quant_rows(x, w["rms_att"], c.eps, xq=xq, s_x=sx)
+            ops.gemm(xq, sx, w["wqkv"], w["s_wqkv"], out=qkv)
+            for j in range(0, rows, CHUNK):
+                ops.attn(self._sub_attn_args(l, j, min(CHUNK, rows - j)))
+            aq, sa = self._q(rows, c.q_dim)
+            ops.quant_rows(att, None, 0.0, xq=aq, s_x=sa)
+            ops.gemm(aq, sa, w["wo"], w["s_wo"], out=x, resid=x)
+            if c.moe:
+                for j in range(0, rows, CHUNK):
+                    e = min(j + CHUNK, rows)
+                    ops.moe_ffn(x[j:e], w["rms_ffn"], c.eps, w["router"], w["s_router"], c.top_k, w["e_gate"],
+                                w["s_e_gate"], w["e_up"], w["s_e_up"], w["e_down"], w["s_e_down"],
+                                self.moe_scratch, resid=x[j:e], out=x[j:e], ids=self.moe_ids[l, j:e],
+                                w=self.moe_w[l, j:e])
+                continue
+            xq, sx = self._q(rows, c.dim)
+            ops.quant_rows(x, w["rms_ffn"], c.eps, xq=xq, s_x=sx)
+            ops.gemm_swiglu(xq, sx, w["w1"], w["s_w1"], w["w3"], w["s_w3"], out=h)
+            hq, sh = self._q(rows, c.hidden)
+            ops.quant_rows(h, None, 0.0, xq=hq, s_x=sh)
+            ops.gemm(hq, sh, w["w2"], w["s_w2"], out=x, resid=x)
         xl = self.x[rows - logits_rows:rows]
         ops.classifier(xl, self.cls_q, self.cls_s, self.rms_final, c.eps, out=self.logits[:logits_rows],
                        argmax_key=self.key[:logits_rows] if argmax else None)

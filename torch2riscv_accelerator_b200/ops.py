@@ -118,6 +118,37 @@ def ffn_swiglu(x, norm_g, eps, w_gate, s_gate, w_up, s_up, scratch, h=None, h_q=
     return h, h_q, s_h
 
 
+def quant_rows(x, norm_g=None, eps=0.0, xq=None, s_x=None):
+    """int8 rows and scales of x (quant_act, after rmsnorm when norm_g is given)."""
+    _need(x, F32, "x")
+    m, k = x.shape
+    xq = torch.empty(m, k, dtype=I8, device=x.device) if xq is None else xq
+    s_x = torch.empty(m, dtype=F32, device=x.device) if s_x is None else s_x
+    _lib.check("w8a8_quant_rows", _lib.load().w8a8_quant_rows(_p(x), _p(norm_g), float(eps), m, k, _p(xq), _p(s_x),
+                                                              _st()))
+    return xq, s_x
+
+
+def gemm(xq, s_x, w, s_w, out=None, acc=None, resid=None):
+    """Tensor-core W8A8 linear for any row count (same results as linear())."""
+    m, k = xq.shape
+    n = w.shape[0]
+    out = torch.empty(m, n, dtype=F32, device=xq.device) if out is None else out
+    _lib.check("w8a8_gemm", _lib.load().w8a8_gemm(_p(xq), _p(s_x), m, k, _p(w), _p(s_w), n, _p(resid), _p(out),
+                                                  _p(acc), _st()))
+    return out
+
+
+def gemm_swiglu(xq, s_x, w_gate, s_gate, w_up, s_up, out=None):
+    """Tensor-core SwiGLU pair: h = silu(g) * u for any row count."""
+    m, k = xq.shape
+    n = w_gate.shape[0]
+    out = torch.empty(m, n, dtype=F32, device=xq.device) if out is None else out
+    _lib.check("w8a8_gemm_swiglu", _lib.load().w8a8_gemm_swiglu(_p(xq), _p(s_x), m, k, _p(w_gate), _p(s_gate),
+                                                                _p(w_up), _p(s_up), n, _p(out), _st()))
+    return out
+
+
 def moe_scratch(rows, dim, top_k, expert_hidden, device):
     n = _lib.load().w8a8_moe_scratch_bytes(rows, dim, top_k, expert_hidden)
     return torch.zeros(n, dtype=torch.uint8, device=device)

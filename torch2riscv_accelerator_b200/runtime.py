@@ -16,7 +16,7 @@ import time
 import numpy as np
 import torch
 
-from .model import CHUNK, DeviceDecoder
+from .model import CHUNK, PREFILL, DeviceDecoder
 
 F = np.float32
 BOS = 1
@@ -70,7 +70,8 @@ class LlamaDevice:
         self.graphs = graphs
         self.pos = 0
         self.stats = []                                   # per token: (pos, wall seconds)
-        self._in = torch.zeros(2 * CHUNK, dtype=torch.int32).pin_memory()   # tokens | positions
+        self._rows = self.dec.rows_cap                    # most rows per launch
+        self._in = torch.zeros(2 * self._rows, dtype=torch.int32).pin_memory()   # tokens | positions
         self._out = torch.zeros(self.cfg.vocab, dtype=torch.float32).pin_memory()
 
     def reset(self):
@@ -80,7 +81,7 @@ class LlamaDevice:
 
     def _submit(self, tokens, positions, logits=True, staging=None):
         """Stage (tokens, positions) in pinned memory, copy them to the graph's
-        input buffers and launch. staging: a pinned [2*CHUNK] int32 slice that
+        input buffers and launch. staging: a pinned [2*rows_cap] int32 slice that
         stays untouched until the stream has consumed it (default: the
         single-token buffer, safe because forward() synchronizes)."""
         m = len(tokens)
@@ -88,9 +89,10 @@ class LlamaDevice:
             raise ValueError(f"token outside [0, {self.cfg.vocab})")
         buf = self._in if staging is None else staging
         buf[:m] = torch.as_tensor(tokens, dtype=torch.int32)
-        buf[CHUNK:CHUNK + m] = torch.as_tensor(positions, dtype=torch.int32)
+        R = self._rows
+        buf[R:R + m] = torch.as_tensor(positions, dtype=torch.int32)
         self.dec.tokens[:m].copy_(buf[:m], non_blocking=True)
-        self.dec.pos[:m].copy_(buf[CHUNK:CHUNK + m], non_blocking=True)
+        self.dec.pos[:m].copy_(buf[R:R + m], non_blocking=True)
         self.dec.launch(m, 1, graph=self.graphs)
         if logits:
             self._out.copy_(self.dec.logits[0], non_blocking=True)
@@ -108,22 +110,27 @@ class LlamaDevice:
         return out
 
     def prefill(self, tokens):
-        """Feed a prompt from the current position in 16-row chunks (a shorter
-        tail as a last chunk ending at the prompt's last token). Returns the
-        logits of its last token."""
+        """Feed a prompt from the current position: chunks of up to PREFILL rows
+        on the tensor cores while more than 16 rows remain, then a 16-row chunk
+        ending at the prompt's last token (it may recompute rows already done:
+        the same values are written again). Returns the logits of the last token."""
         toks = [int(t) for t in tokens]
         p0, n = self.pos, len(toks)
         if p0 + n > self.cfg.seq_len:
             raise ValueError("prompt beyond the sequence length")
         if n == 0:
             raise ValueError("empty prompt")
-        starts = list(range(0, n - CHUNK + 1, CHUNK)) if n >= CHUNK else []
-        if not starts or starts[-1] + CHUNK < n:
-            starts.append(max(n - CHUNK, 0))
-        staging = torch.zeros(len(starts), 2 * CHUNK, dtype=torch.int32).pin_memory()
-        for i, s in enumerate(starts):
-            e = min(s + CHUNK, n)
-            self._submit(toks[s:e], list(range(p0 + s, p0 + e)), logits=i == len(starts) - 1, staging=staging[i])
+        big = min(PREFILL, self._rows)
+        spans, s = [], 0
+        while n - s > CHUNK:                              # tensor-core chunks
+            e = min(s + big, n)
+            spans.append((s, e))
+            s = e
+        if s < n:                                         # the tail: one GEMV-path chunk of <= 16 rows
+            spans.append((max(n - CHUNK, 0), n))
+        staging = torch.zeros(len(spans), 2 * self._rows, dtype=torch.int32).pin_memory()
+        for i, (s, e) in enumerate(spans):
+            self._submit(toks[s:e], list(range(p0 + s, p0 + e)), logits=i == len(spans) - 1, staging=staging[i])
         torch.cuda.current_stream().synchronize()
         self.pos = p0 + n
         return self._out.numpy().copy()
