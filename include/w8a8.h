@@ -215,6 +215,14 @@ int w8a8_attn(const W8A8AttnArgs* args, void* stream);
  * seq_len needs more than 8 x 512 positions or the chunk does not fit in
  * shared memory. */
 
+/* The same attention for `slots` sequences of one row each (batched decode):
+ * slot b uses pos[b], qkv row b and att row b, and the caches at
+ * k_cache + b * slot_stride and v_cache + b * slot_stride bytes (args->rows
+ * must be 1). Each slot's row is computed exactly as a one-row w8a8_attn call.
+ * Replaces the attention of the batched list (llm/compile_batch.py via
+ * BatchLlamaDevice.step, llm/runtime.py:193-208). */
+int w8a8_attn_batch(const W8A8AttnArgs* args, int slots, size_t slot_stride, void* stream);
+
 /* Greedy token per row (np.argmax: the first maximum). Replaces
  * Sampler.__call__ at temperature 0 (llm/runtime.py:55-57). */
 int w8a8_argmax(const float* logits, int rows, int n, int32_t* out, void* stream);

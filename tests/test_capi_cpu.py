@@ -92,3 +92,21 @@ def test_moe_argument_checks(lib):
     assert _moe(lib, x=None) == _lib.W8A8_EINVAL
     # scratch: int8 row + scale + h of every slot + amax words, each 256-byte aligned
     assert lib.w8a8_moe_scratch_bytes(1, 1024, 8, 512) == 1024 + 256 + 8 * 512 * 4 + 256
+
+
+def test_gemm_and_batch_argument_checks(lib):
+    """The tensor-core GEMM, the row quantizer and the batched attention check
+    their arguments before anything is queued."""
+    assert lib.w8a8_gemm(None, 16, 1, 64, 16, 16, 64, None, 16, None, None) == _lib.W8A8_EINVAL
+    assert lib.w8a8_gemm(16, 16, 1, 72, 16, 16, 64, None, 16, None, None) == _lib.W8A8_EALIGN    # k % 16
+    assert lib.w8a8_gemm(8, 16, 1, 64, 16, 16, 64, None, 16, None, None) == _lib.W8A8_EALIGN     # xq alignment
+    assert lib.w8a8_gemm(16, 16, 1, 64, 16, 16, 64, 16, 16, 16, None) == _lib.W8A8_EINVAL       # resid + acc
+    assert lib.w8a8_gemm_swiglu(16, 16, 1, 64, 16, 16, None, 16, 64, 16, None) == _lib.W8A8_EINVAL
+    assert lib.w8a8_quant_rows(16, None, ctypes.c_float(0.0), 0, 64, 16, 16, None) == _lib.W8A8_EINVAL
+    assert lib.w8a8_quant_rows(16, None, ctypes.c_float(0.0), 1, 40, 16, 16, None) == _lib.W8A8_EALIGN
+    a = _attn_args(rows=2)
+    assert lib.w8a8_attn_batch(ctypes.byref(a), 4, 1 << 20, None) == _lib.W8A8_EINVAL            # one row per slot
+    a = _attn_args()
+    assert lib.w8a8_attn_batch(ctypes.byref(a), 0, 1 << 20, None) == _lib.W8A8_EINVAL
+    assert lib.w8a8_attn_batch(ctypes.byref(a), 4, 1000, None) == _lib.W8A8_EALIGN               # stride % 16
+    assert lib.w8a8_attn_batch(ctypes.byref(a), 4, 1024, None) == _lib.W8A8_EINVAL               # < one cache

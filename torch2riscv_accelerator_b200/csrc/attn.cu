@@ -132,6 +132,14 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
     extern __shared__ __align__(16) unsigned char sm[];
     cg::cluster_group cl = cg::this_cluster();
     const int hd = p.head_dim, H = p.heads, Hk = p.kv_heads, G = H / Hk, M = p.rows, T = p.seq_len;
+    // batched decode: grid z is the slot (one row, its own position, qkv / att
+    // rows and caches); otherwise z = 0 and one sequence's M rows
+    const size_t b = blockIdx.z;
+    const int32_t* const pos_p = p.pos + b;
+    const float* const qkv_p = p.qkv + b * (size_t)(H + 2 * Hk) * hd;
+    float* const att_p = p.att + b * (size_t)H * hd;
+    int8_t* const kc_p = p.kc + b * p.slot_stride;
+    int8_t* const vc_p = p.vc + b * p.slot_stride;
     const int CH = p.chunk, CS = p.nsplit, MG = M * G;
     const int kvh = blockIdx.x, rank = (int)cl.block_rank(), t0 = rank * CH, tid = threadIdx.x;
     const int lane = tid & 31, warp = tid >> 5;
@@ -165,10 +173,10 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
     asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
     // ---- before the wait: positions, cache tiles of earlier positions, constant tables
     int maxpos = 0;
-    for (int m = 0; m < M; ++m) maxpos = max(maxpos, p.pos[m]);
+    for (int m = 0; m < M; ++m) maxpos = max(maxpos, pos_p[m]);
     const int nvalid = min(CH, maxpos + 1 - t0);
     const int nv16 = (nvalid + 15) & ~15;                      // V^T rows are read in 16-position words
-    if (tid < M) lim_s[tid] = min(nvalid, p.pos[tid] + 1 - t0);  // positions of the chunk row m attends
+    if (tid < M) lim_s[tid] = min(nvalid, pos_p[tid] + 1 - t0);  // positions of the chunk row m attends
     if (tid < 64) {
         etab[tid] = g_exp_t[tid];
         etab[64 + tid] = g_exp_s[tid];
@@ -185,7 +193,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
             mbar_init(&tbar, 1);
             mbar_fence_init();
             mbar_expect_tx(&tbar, (uint32_t)(nvalid * hd));
-            bulk_g2s(ks, p.kc + ((size_t)kvh * T + t0) * hd, (uint32_t)(nvalid * hd), &tbar);
+            bulk_g2s(ks, kc_p + ((size_t)kvh * T + t0) * hd, (uint32_t)(nvalid * hd), &tbar);
         }
         // the V^T rows: a short run of positions per channel (one bulk copy each
         // would queue hundreds of small copies): 16-byte loads
@@ -193,10 +201,10 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
         for (int i = tid; i < hd * vw; i += kAttnThreads) {
             const int c = i / vw, w = i % vw;
             *reinterpret_cast<int4*>(vs + c * vstride + w * 16) =
-                __ldg(reinterpret_cast<const int4*>(p.vc + ((size_t)kvh * hd + c) * T + t0) + w);
+                __ldg(reinterpret_cast<const int4*>(vc_p + ((size_t)kvh * hd + c) * T + t0) + w);
         }
         for (int i = tid; i < M * hd; i += kAttnThreads) {
-            const int m = i / hd, c = i % hd, pos = p.pos[m];
+            const int m = i / hd, c = i % hd, pos = pos_p[m];
             tabs[2 * m * hd + c] = __ldg(p.cos + (size_t)pos * hd + c);
             tabs[(2 * m + 1) * hd + c] = __ldg(p.sin + (size_t)pos * hd + c);
         }
@@ -222,7 +230,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
         float* kbuf = fbuf + (kAttnWarps + warp) * hd;              // the K row's own buffer
         for (int r = warp; r < MG; r += kAttnWarps) {
             const int m = r / G, h = kvh * G + r % G;
-            const float* src = p.qkv + (size_t)m * qkv_dim + (size_t)h * hd;
+            const float* src = qkv_p + (size_t)m * qkv_dim + (size_t)h * hd;
             for (int c = lane; c < hd; c += 32) buf[c] = src[c];
             __syncwarp();
             warp_norm_rope(buf, hd, p.qk_norm ? gains : nullptr, p.eps, p.inv_hd, tabs + 2 * m * hd,
@@ -238,20 +246,20 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
         }
         // K and V rows of the positions in this chunk: into the cache and the tiles
         for (int m = kAttnWarps - 1 - warp; m < M; m += kAttnWarps) {
-            const int pos = p.pos[m];
+            const int pos = pos_p[m];
             if (pos < t0 || pos >= t0 + CH) continue;
-            const float* ksrc = p.qkv + (size_t)m * qkv_dim + q_dim + (size_t)kvh * hd;
+            const float* ksrc = qkv_p + (size_t)m * qkv_dim + q_dim + (size_t)kvh * hd;
             for (int c = lane; c < hd; c += 32) kbuf[c] = ksrc[c];
             __syncwarp();
             warp_norm_rope(kbuf, hd, p.qk_norm ? gains + hd : nullptr, p.eps, p.inv_hd, tabs + 2 * m * hd,
                            tabs + (2 * m + 1) * hd, lane);
-            int8_t* kdst = p.kc + ((size_t)kvh * T + pos) * hd;
-            const float* vsrc = p.qkv + (size_t)m * qkv_dim + q_dim + kv_dim + (size_t)kvh * hd;
+            int8_t* kdst = kc_p + ((size_t)kvh * T + pos) * hd;
+            const float* vsrc = qkv_p + (size_t)m * qkv_dim + q_dim + kv_dim + (size_t)kvh * hd;
             for (int c = lane; c < hd; c += 32) {
                 const int8_t kq = (int8_t)to_i8(fmul(kbuf[c], p.inv_sk));
                 const int8_t vq = (int8_t)to_i8(fmul(vsrc[c], p.inv_sv));
                 kdst[c] = kq;
-                p.vc[((size_t)kvh * hd + c) * T + pos] = vq;
+                vc_p[((size_t)kvh * hd + c) * T + pos] = vq;
                 ks[(pos - t0) * hd + c] = kq;
                 vs[c * vstride + (pos - t0)] = vq;
             }
@@ -310,7 +318,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
                 const int m = r / G;
                 const int lim = lim_s[m];
                 if (lim > 0) {
-                    const int n = p.pos[m] + 1;
+                    const int n = pos_p[m] + 1;
                     const float mx = gmx[r];
                     for (int t = tid; t < n; t += kAttnThreads) {
                         const int j = t / CH;
@@ -397,7 +405,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
                 const float rq = fmul(sfu_recip(i2f(ssum)), 127.f);   // sum <= 127 T: exact in fp32
                 out = fmul(fmul(o, rq), p.a_v);
             }
-            p.att[((size_t)m * H + h) * hd + c] = out;
+            att_p[((size_t)m * H + h) * hd + c] = out;
         }
     }
     if (!tiles_ok) mbar_wait(&tbar, 0u);                      // no copy may land after the CTA exits
@@ -423,7 +431,7 @@ cudaError_t launch_attn(const AttnParams& q, cudaStream_t st) {
     e = cudaFuncSetAttribute(attn_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3(p.kv_heads, g.cs);
+    cfg.gridDim = dim3(p.kv_heads, g.cs, p.slots > 0 ? p.slots : 1);
     cfg.blockDim = dim3(kAttnThreads);
     cfg.dynamicSmemBytes = L.total;
     cfg.stream = st;

@@ -261,7 +261,7 @@ size_t w8a8_attn_scratch_bytes(int rows, int heads, int kv_heads, int head_dim, 
     return 0;                                                 // the cluster kernel needs no global scratch
 }
 
-int w8a8_attn(const W8A8AttnArgs* a, void* stream) {
+static int attn_params(const W8A8AttnArgs* a, AttnParams* out) {
     if (!a) return W8A8_EINVAL;
     if (a->rows <= 0 || a->rows > kMaxRows || a->heads <= 0 || a->kv_heads <= 0 || a->heads % a->kv_heads ||
         a->heads / a->kv_heads > 8 || a->head_dim <= 0 || a->head_dim > 256 || a->seq_len <= 0 ||
@@ -279,6 +279,24 @@ int w8a8_attn(const W8A8AttnArgs* a, void* stream) {
     p.inv_hd = inv_of(a->head_dim), p.cos = a->rope_cos, p.sin = a->rope_sin;
     p.inv_sk = a->inv_sk, p.inv_sv = a->inv_sv, p.a_k = a->a_k, p.a_v = a->a_v;
     p.kc = a->k_cache, p.vc = a->v_cache, p.att = a->att;
+    *out = p;
+    return W8A8_OK;
+}
+
+int w8a8_attn(const W8A8AttnArgs* a, void* stream) {
+    AttnParams p{};
+    const int st = attn_params(a, &p);
+    return st ? st : cuda_status(launch_attn(p, S(stream)));
+}
+
+int w8a8_attn_batch(const W8A8AttnArgs* a, int slots, size_t slot_stride, void* stream) {
+    AttnParams p{};
+    const int st = attn_params(a, &p);
+    if (st) return st;
+    if (a->rows != 1 || slots <= 0 || slots > 65535) return W8A8_EINVAL;
+    if (slot_stride % 16) return W8A8_EALIGN;
+    if (slots > 1 && slot_stride < (size_t)a->kv_heads * a->seq_len * a->head_dim) return W8A8_EINVAL;
+    p.slots = slots, p.slot_stride = slot_stride;
     return cuda_status(launch_attn(p, S(stream)));
 }
 

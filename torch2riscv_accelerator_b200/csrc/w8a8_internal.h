@@ -55,6 +55,8 @@ struct AttnParams {
     float* att;               // [M, H hd] out
     int nsplit;               // CTAs per KV head (one thread-block cluster)
     int chunk;                // cache positions per CTA
+    int slots;                // batched decode: sequences (one row each; grid z), or 0
+    size_t slot_stride;       // bytes between consecutive slots' caches (batched decode)
 };
 
 // Tensor-core GEMM (gemm.cu): int8 operands row-major [rows][k], K-major.

@@ -32,24 +32,27 @@ CHUNK = 16                                         # rows of the GEMV / attentio
 PREFILL = 256                                      # rows per tensor-core prefill chunk
 
 
+def _upload(obj, cfg, qw, kv_scales):
+    """The model's tensors in HBM (int8 rows + fp32 scales, gains, RoPE tables)
+    and the per-layer KV constants, as attributes of obj."""
+    t = lambda a, dt=None: torch.as_tensor(np.ascontiguousarray(a), dtype=dt).to(obj.dev)
+    obj.emb_q, obj.emb_s = t(qw.emb_q, I8), t(qw.emb_s, F32)
+    if cfg.tied and qw.cls_q is qw.emb_q:
+        obj.cls_q, obj.cls_s = obj.emb_q, obj.emb_s
+    else:
+        obj.cls_q, obj.cls_s = t(qw.cls_q, I8), t(qw.cls_s, F32)
+    obj.rms_final = t(qw.rms_final, F32)
+    obj.cos, obj.sin = t(qw.cos, F32), t(qw.sin, F32)
+    obj.layers = [{k: t(v) for k, v in lw.items()} for lw in qw.layers]
+    kv = np.asarray(kv_scales, np.float32)
+    obj.consts = [kv_consts(kv[l, 0], kv[l, 1], cfg.head_dim) for l in range(cfg.layers)]
+
+
 class DeviceDecoder:
     def __init__(self, cfg, qw, kv_scales, device="cuda", max_rows=CHUNK, prefill_rows=PREFILL):
         cfg.validate()
         self.cfg, self.dev, self.max_rows = cfg, torch.device(device), max_rows
-        t = lambda a, dt=None: torch.as_tensor(np.ascontiguousarray(a), dtype=dt).to(self.dev)
-        self.emb_q, self.emb_s = t(qw.emb_q, I8), t(qw.emb_s, F32)
-        if cfg.tied and qw.cls_q is qw.emb_q:
-            self.cls_q, self.cls_s = self.emb_q, self.emb_s
-        else:
-            self.cls_q, self.cls_s = t(qw.cls_q, I8), t(qw.cls_s, F32)
-        self.rms_final = t(qw.rms_final, F32)
-        self.cos, self.sin = t(qw.cos, F32), t(qw.sin, F32)
-        self.layers = []
-        for lw in qw.layers:
-            d = {k: t(v) for k, v in lw.items()}
-            self.layers.append(d)
-        kv = np.asarray(kv_scales, np.float32)
-        self.consts = [kv_consts(kv[l, 0], kv[l, 1], cfg.head_dim) for l in range(cfg.layers)]
+        _upload(self, cfg, qw, kv_scales)
         L, Hk, T, hd = cfg.layers, cfg.kv_heads, cfg.seq_len, cfg.head_dim
         self.kc = torch.zeros(L, Hk, T, hd, dtype=I8, device=self.dev)
         self.vc = torch.zeros(L, Hk, hd, T, dtype=I8, device=self.dev)      # V transposed per head
@@ -248,3 +251,95 @@ class DeviceDecoder:
     def kv_bytes(self, t):
         """KV bytes read by one decode step attending t positions."""
         return self.cfg.layers * 2 * t * self.cfg.kv_dim
+
+
+class BatchDecoder:
+    """D sequences ("slots") per step, one token each, every slot with its own
+    KV cache and position (`llm/runtime.py:155-208` BatchLlamaDevice over
+    `compile_batch.BatchCompiler`). A step: every linear one tensor-core GEMM
+    over the D rows (the row quantizer first), the attention one launch over all
+    slots (grid z = slot), the MoE FFN in 16-row groups, the classifier GEMM for
+    all D rows. Each slot's results equal a one-sequence decode bit for bit."""
+
+    def __init__(self, cfg, qw, kv_scales, slots, device="cuda"):
+        cfg.validate()
+        if slots < 1:
+            raise ValueError("at least one slot")
+        self.cfg, self.dev, self.slots = cfg, torch.device(device), slots
+        _upload(self, cfg, qw, kv_scales)
+        D, L, Hk, T, hd = slots, cfg.layers, cfg.kv_heads, cfg.seq_len, cfg.head_dim
+        self.kc = torch.zeros(D, L, Hk, T, hd, dtype=I8, device=self.dev)
+        self.vc = torch.zeros(D, L, Hk, hd, T, dtype=I8, device=self.dev)   # V transposed per head
+        self.slot_stride = L * Hk * T * hd                                   # bytes between slots' caches
+        z = lambda *s, dt=F32: torch.zeros(*s, dtype=dt, device=self.dev)
+        self.tokens, self.pos = z(D, dt=I32), z(D, dt=I32)
+        self.x, self.qkv, self.att = z(D, cfg.dim), z(D, cfg.qkv_dim), z(D, cfg.q_dim)
+        self.h = z(D, cfg.hidden)
+        self.logits = z(D, cfg.vocab)
+        self.xq_buf = z(D * max(cfg.dim, cfg.q_dim, cfg.hidden), dt=I8)
+        self.sx_buf = z(D)
+        self.attn_scratch = ops.attn_scratch(1, cfg.heads, cfg.kv_heads, hd, T, self.dev)
+        if cfg.moe:
+            self.moe_ids = z(L, D, cfg.top_k, dt=I32)
+            self.moe_w = z(L, D, cfg.top_k)
+            self.moe_scratch = ops.moe_scratch(CHUNK, cfg.dim, cfg.top_k, cfg.expert_hidden, self.dev)
+        self.args = [ops.attn_args(cfg, 1, self.pos, self.qkv, self.kc[0, l], self.vc[0, l], self.att,
+                                   self.consts[l], self.cos, self.sin, self.attn_scratch, w.get("q_norm"),
+                                   w.get("k_norm"))
+                     for l, w in enumerate(self.layers)]
+        self.graph = None
+
+    def _q(self, k):
+        return self.xq_buf[:self.slots * k].view(self.slots, k), self.sx_buf
+
+    def step(self):
+        """One token of every slot (self.tokens / self.pos) -> self.logits [D, vocab]."""
+        c, D, x = self.cfg, self.slots, self.x
+        ops.embed(self.tokens, self.emb_q, self.emb_s, out=x)
+        for l, w in enumerate(self.layers):
+            xq, sx = self._q(c.dim)
+            ops.quant_rows(x, w["rms_att"], c.eps, xq=xq, s_x=sx)
+            ops.gemm(xq, sx, w["wqkv"], w["s_wqkv"], out=self.qkv)
+            ops.attn_batch(self.args[l], D, self.slot_stride)
+            aq, sa = self._q(c.q_dim)
+            ops.quant_rows(self.att, None, 0.0, xq=aq, s_x=sa)
+            ops.gemm(aq, sa, w["wo"], w["s_wo"], out=x, resid=x)
+            if c.moe:
+                for j in range(0, D, CHUNK):
+                    e = min(j + CHUNK, D)
+                    ops.moe_ffn(x[j:e], w["rms_ffn"], c.eps, w["router"], w["s_router"], c.top_k, w["e_gate"],
+                                w["s_e_gate"], w["e_up"], w["s_e_up"], w["e_down"], w["s_e_down"],
+                                self.moe_scratch, resid=x[j:e], out=x[j:e], ids=self.moe_ids[l, j:e],
+                                w=self.moe_w[l, j:e])
+                continue
+            xq, sx = self._q(c.dim)
+            ops.quant_rows(x, w["rms_ffn"], c.eps, xq=xq, s_x=sx)
+            ops.gemm_swiglu(xq, sx, w["w1"], w["s_w1"], w["w3"], w["s_w3"], out=self.h)
+            hq, sh = self._q(c.hidden)
+            ops.quant_rows(self.h, None, 0.0, xq=hq, s_x=sh)
+            ops.gemm(hq, sh, w["w2"], w["s_w2"], out=x, resid=x)
+        xq, sx = self._q(c.dim)
+        ops.quant_rows(x, self.rms_final, c.eps, xq=xq, s_x=sx)
+        ops.gemm(xq, sx, self.cls_q, self.cls_s, out=self.logits)
+
+    def capture(self):
+        """The step as a CUDA graph (after one eager warm-up step)."""
+        s = torch.cuda.Stream(device=self.dev)
+        s.wait_stream(torch.cuda.current_stream(self.dev))
+        with torch.cuda.stream(s):
+            self.step()
+        torch.cuda.current_stream(self.dev).wait_stream(s)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            self.step()
+        self.graph = g
+        return g
+
+    def clear_slot(self, b):
+        self.kc[b].zero_()
+        self.vc[b].zero_()
+
+    def kernel_launches(self):
+        c = self.cfg
+        ffn = 3 * ((self.slots + CHUNK - 1) // CHUNK) if c.moe else 4
+        return 1 + c.layers * (5 + ffn) + 2

@@ -199,6 +199,13 @@ def attn(args):
     _lib.check("w8a8_attn", _lib.load().w8a8_attn(ctypes.byref(args), _st()))
 
 
+def attn_batch(args, slots, slot_stride):
+    """Batched decode attention: slot b = row b of pos / qkv / att, caches at
+    + b * slot_stride bytes (args built for one row and slot 0's caches)."""
+    import ctypes
+    _lib.check("w8a8_attn_batch", _lib.load().w8a8_attn_batch(ctypes.byref(args), slots, slot_stride, _st()))
+
+
 def argmax(logits, out=None):
     m, n = logits.reshape(-1, logits.shape[-1]).shape
     out = torch.empty(m, dtype=I32, device=logits.device) if out is None else out

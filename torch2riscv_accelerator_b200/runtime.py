@@ -5,18 +5,21 @@ Sampler, over DeviceDecoder on a B200 instead of the overlay's descriptor ring.
 Per token, as the reference does per submit (`llm/runtime.py:107-125`): the
 (pos, token) pair goes to the device (an 8-byte host-to-device copy into the
 graph's input buffers), the captured program replays, and the logits come back
-as a float32 copy. Prompts can also be prefilled in 16-row chunks at 0, M,
-2M, ... and a last one at P - M (`compile_model`'s L6 prefill,
-`compiler/runtime/tools/sa_llm_run.c:255-300`, `qhf.QModel.prefill` :356-364):
-every row is computed exactly as a decode step, so the KV cache and logits
-equal the decode-only run bit for bit.
+as a float32 copy. Prompts can also be prefilled in chunks (`compile_model`'s
+L6 prefill, `compiler/runtime/tools/sa_llm_run.c:255-300`, `qhf.QModel.prefill`
+:356-364): every row is computed exactly as a decode step, so the KV cache and
+logits equal the decode-only run bit for bit.
+
+BatchLlamaDevice is the reference's batched runtime (`llm/runtime.py:155-241`):
+D slots, each with its own KV cache and position, one token of every slot per
+step.
 """
 import time
 
 import numpy as np
 import torch
 
-from .model import CHUNK, PREFILL, DeviceDecoder
+from .model import CHUNK, PREFILL, BatchDecoder, DeviceDecoder
 
 F = np.float32
 BOS = 1
@@ -157,6 +160,90 @@ class LlamaDevice:
                 return
             yield nxt
             token = nxt
+
+    def close(self):
+        self.dec = None
+        torch.cuda.empty_cache()
+
+
+class BatchLlamaDevice:
+    """D sequences per step (`llm/runtime.py:155-241`). model: a BatchDecoder,
+    or (cfg, QuantWeights, kv_scales) to build one with `slots` slots. Slot b
+    has its own KV cache and position; step() runs one token of every slot. A
+    slot without a sequence runs a dummy token at pos 0 (its KV row 0 is
+    rewritten when a sequence starts in it)."""
+    DUMMY = BOS
+
+    def __init__(self, model, slots=None, device="cuda", graphs=True):
+        self.dec = model if isinstance(model, BatchDecoder) else BatchDecoder(*model, slots=slots, device=device)
+        self.cfg, self.d = self.dec.cfg, self.dec.slots
+        self.graphs = graphs
+        self.stats = []                                   # per step: wall seconds
+        self._in = torch.zeros(2 * self.d, dtype=torch.int32).pin_memory()   # tokens | positions
+        self._out = torch.zeros(self.d, self.cfg.vocab, dtype=torch.float32).pin_memory()
+
+    def clear_slot(self, b):
+        """Empty the KV cache of slot b (`llm/runtime.py:187-191`)."""
+        if not 0 <= b < self.d:
+            raise ValueError(f"slot {b} outside [0, {self.d})")
+        self.dec.clear_slot(b)
+
+    def step(self, poses, tokens, perf=False):
+        """One token for each of the D slots; returns the D x vocab logits (copy)."""
+        d = self.d
+        if len(poses) != d or len(tokens) != d:
+            raise ValueError(f"{d} positions and {d} tokens expected")
+        if min(tokens) < 0 or max(tokens) >= self.cfg.vocab:
+            raise ValueError(f"token outside [0, {self.cfg.vocab})")
+        if min(poses) < 0 or max(poses) >= self.cfg.seq_len:
+            raise ValueError(f"position outside [0, {self.cfg.seq_len})")
+        t0 = time.perf_counter()
+        self._in[:d] = torch.as_tensor(tokens, dtype=torch.int32)
+        self._in[d:] = torch.as_tensor(poses, dtype=torch.int32)
+        self.dec.tokens.copy_(self._in[:d], non_blocking=True)
+        self.dec.pos.copy_(self._in[d:], non_blocking=True)
+        if self.graphs:
+            g = self.dec.graph or self.dec.capture()
+            g.replay()
+        else:
+            self.dec.step()
+        self._out.copy_(self.dec.logits, non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        self.stats.append(time.perf_counter() - t0)
+        return self._out.numpy().copy()
+
+    def generate(self, prompts, steps, stagger=0, temperature=0.0, topp=0.9, seed=1, on_logits=None):
+        """Generate for len(prompts) <= D sequences at once (`llm/runtime.py:210-241`):
+        sequence b starts at step b * stagger and runs `steps` positions (its
+        prompt tokens first, then sampled; BOS does not stop it). prompts are
+        token lists. on_logits(b, pos, logits) sees every position. Returns the
+        token lists."""
+        d, n = self.d, len(prompts)
+        if n > d:
+            raise ValueError(f"at most {d} sequences")
+        toks = [list(p) for p in prompts]
+        samplers = [Sampler(temperature, topp, seed + b) for b in range(n)]
+        out = [[t[0]] for t in toks]
+        start = [b * stagger for b in range(n)]
+        for b in range(d):
+            self.clear_slot(b)
+        total = max(start) + steps if n else 0
+        for s in range(total):
+            poses, cur, live = [0] * d, [self.DUMMY] * d, [False] * d
+            for b in range(n):
+                p = s - start[b]
+                if 0 <= p < steps:
+                    poses[b], cur[b], live[b] = p, out[b][p], True
+            logits = self.step(poses, cur)
+            for b in range(n):
+                if not live[b]:
+                    continue
+                p = poses[b]
+                if on_logits:
+                    on_logits(b, p, logits[b])
+                if p + 1 < steps:
+                    out[b].append(toks[b][p + 1] if p + 1 < len(toks[b]) else samplers[b](logits[b]))
+        return out
 
     def close(self):
         self.dec = None
