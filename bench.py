@@ -207,6 +207,83 @@ def run_reference(args, cfg, ws, rank):
     print(json.dumps(line), flush=True)
 
 
+def run_batch(args, cfg, qw, ws, rank, local):
+    """Batched decode (BatchLlamaDevice): `batch` sequences per step, each with
+    its own cache of T = 2048 positions, positions 2048 - warmup - steps ... 2047.
+    The caches hold seeded random int8 values (the step reads the same bytes
+    whatever they hold); value: replays of the captured step with the positions
+    advanced on the device; e2e: BatchLlamaDevice.step with host tokens and
+    positions and the [batch, vocab] logits back."""
+    import torch
+    from torch2riscv_accelerator_b200.model import BatchDecoder
+    from torch2riscv_accelerator_b200.runtime import BatchLlamaDevice
+    D = args.batch
+    dec = BatchDecoder(cfg, qw, qw.kv_scales, slots=D)
+    g = torch.Generator(device=dec.dev).manual_seed(args.seed + 11)
+    for t in (dec.kc, dec.vc):
+        t.copy_(torch.randint(-127, 128, t.shape, dtype=torch.int8, device=dec.dev, generator=g))
+    P = cfg.seq_len - args.warmup - args.steps
+    rng = np.random.default_rng(args.seed + 3)
+    dec.tokens.copy_(torch.as_tensor(rng.integers(0, cfg.vocab, D), dtype=torch.int32))
+    dec.pos.fill_(P)
+    graph = dec.capture()                          # (its warm-up step writes the rows of position P)
+    st = torch.cuda.current_stream()
+    for _ in range(args.warmup):
+        graph.replay()
+        dec.pos.add_(1)
+    barrier(ws)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        torch.cuda.nvtx.range_push("batch")               # ncu --nvtx-include batch/ selects these launches
+        e0.record(st)
+        for _ in range(args.steps):
+            graph.replay()
+            dec.pos.add_(1)
+        e1.record(st)
+        torch.cuda.nvtx.range_pop()
+        torch.cuda.synchronize()
+    barrier(ws)
+    dt = max_over_ranks(e0.elapsed_time(e1) / 1e3, ws)
+    # e2e: host tokens / positions in, [D, vocab] logits out, per step
+    dev = BatchLlamaDevice(dec)
+    toks = rng.integers(0, cfg.vocab, (args.warmup + args.steps, D))
+    for i in range(args.warmup):
+        dev.step([P + i] * D, [int(v) for v in toks[i]])
+    barrier(ws)
+    torch.cuda.synchronize()
+    h0, h1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    h0.record(st)
+    for i in range(args.steps):
+        dev.step([P + args.warmup + i] * D, [int(v) for v in toks[args.warmup + i]])
+    h1.record(st)
+    torch.cuda.synchronize()
+    barrier(ws)
+    dt_e2e = max_over_ranks(h0.elapsed_time(h1) / 1e3, ws)
+    if rank == 0:
+        kv_step = D * dec.slot_stride * 2 * (P + args.warmup + args.steps // 2) // cfg.seq_len
+        line = {
+            "metric": METRIC, "value": ws * D * args.steps / dt, "unit": "tok/s", "n_gpus": ws, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": 1e3 * dt / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic (N(0,0.02) weights seed 0, uniform token ids, seeded random int8 caches)",
+            "config": {"workload": f"{cfg.name}-shape W8A8 batched decode: {D} sequences per step, each at "
+                                   f"positions {P}..{cfg.seq_len - 1} of its own T=2048 cache",
+                       "model": cfg.name, "global_batch": D * ws, "seq_len": cfg.seq_len,
+                       "parallelism": f"replicas x{ws}", "attention": cfg.attn,
+                       "l2": "no flush: the step reads the weights and every slot's cache, far over the 126 MB L2"},
+            "e2e": {"value": ws * D * args.steps / dt_e2e, "unit": "tok/s", "h2d_bytes_per_step": 8 * D,
+                    "d2h_bytes_per_step": 4 * D * cfg.vocab},
+            "step_bytes": {"kv_read": kv_step,
+                           "weights": sum(t.numel() for w in dec.layers for t in w.values()
+                                          if t.dtype == torch.int8) + dec.cls_q.numel()},
+            "gpu_launches": args.steps * dec.kernel_launches(),
+            "clocks": clk.summary(), "mode": "batch",
+        }
+        print(json.dumps(line), flush=True)
+    barrier(ws)
+
+
 def config_of(cfg, args, ws):
     P = cfg.seq_len - args.warmup - args.steps
     return {"workload": f"{cfg.name}-shape W8A8 decode, batch 1 per GPU, T=2048: {P}-token prompt prefilled in "
@@ -227,6 +304,8 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-steps", type=int, default=2)
     ap.add_argument("--pdl", type=int, default=1, help="programmatic dependent launch between kernels (1) or not (0)")
+    ap.add_argument("--batch", type=int, default=1,
+                    help="sequences per step (BatchLlamaDevice); > 1 measures batched decode instead")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
@@ -249,6 +328,9 @@ def main():
     from torch2riscv_accelerator_b200 import _lib
     _lib.load().w8a8_set_pdl(args.pdl)
     qw = build_model(cfg, args.seed)
+    if args.batch > 1:
+        run_batch(args, cfg, qw, ws, rank, local)
+        return
     dec = DeviceDecoder(cfg, qw, qw.kv_scales)
     dev = LlamaDevice(dec)
     P = cfg.seq_len - args.warmup - args.steps

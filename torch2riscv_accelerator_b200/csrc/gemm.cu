@@ -16,9 +16,12 @@
 //     for the gate / up pair); one thread issues tcgen05.mma (M = 128, N = BN,
 //     K = 32 bytes each, A and B K-major from shared memory) and commits each
 //     stage back to the producer, then the finished accumulator to the epilogue;
-//   warps 2-5: tcgen05.ld of their 32 lanes (rows), dequant and store.
-// Every wait is bounded: on a timeout the kernel sets an error bit, still
-// waits (bounded) for its MMAs, frees TMEM and returns.
+//   warps 2-9: tcgen05.ld of their 32 lanes (rows), half the columns each,
+//     dequant and 16-byte stores.
+// Every wait is bounded (the producer and MMA threads spin on their stage
+// barriers: a suspended wait wakes microseconds late, once per stage): on a
+// timeout the kernel sets an error bit, still waits (bounded) for its MMAs,
+// frees TMEM and returns.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -30,7 +33,7 @@ namespace w8a8 {
 
 __device__ unsigned int g_gemm_errors;                        // bit 4: a GEMM pipeline wait gave up
 
-constexpr int kGemmThreads = 192;                              // 6 warps
+constexpr int kGemmThreads = 320;                              // 10 warps: TMA, MMA, 8 epilogue
 constexpr int kBM = 128;                                       // rows per tile (TMEM lanes)
 constexpr int kBK = 128;                                       // K bytes per stage (one 128-byte swizzle row)
 constexpr int kStages = 4;
@@ -127,7 +130,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         // producer: stage s of step kt holds xq[m0.., kt*128..] and W[n0.., kt*128..]
         for (int kt = 0; kt < kt_n; ++kt) {
             const int s = kt % kStages;
-            if (kt >= kStages && !mbar_wait(&empty[s], (uint32_t)(((kt / kStages) - 1) & 1))) {
+            if (kt >= kStages && !mbar_wait_spin(&empty[s], (uint32_t)(((kt / kStages) - 1) & 1))) {
                 atomicOr(&g_gemm_errors, 16u);
                 failed = 1;
                 break;
@@ -145,7 +148,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         bool ok = true;
         for (int kt = 0; kt < kt_n; ++kt) {
             const int s = kt % kStages;
-            if (!mbar_wait(&full[s], (uint32_t)((kt / kStages) & 1))) {
+            if (!mbar_wait_spin(&full[s], (uint32_t)((kt / kStages) & 1))) {
                 atomicOr(&g_gemm_errors, 16u);
                 failed = 1;
                 ok = false;
@@ -166,34 +169,69 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         mma_commit(&acc_full);                                 // every MMA issued so far has completed
         (void)ok;
     } else if (warp >= 2) {
-        // epilogue: warp w reads TMEM lanes 32*(w % 4) .. +31 (rows), 16 columns at a time
+        // epilogue: warps 2-9, two per TMEM lane quarter: warp w reads lanes
+        // 32*(w % 4) .. +31 (rows) and half of the columns, 16 at a time
         const bool ok = mbar_wait(&acc_full, 0u);
         tc_fence_after();
         if (!ok) {
             if (lane == 0) atomicOr(&g_gemm_errors, 16u);
         } else if (!failed) {
-            const int q = warp & 3;
+            const int q = warp & 3, half = (warp - 2) >> 2;
             const int m = m0 + q * 32 + lane;
             const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
             const float sx = m < p.m ? __ldg(p.s_x + m) : 0.f;
-            for (int c0 = 0; c0 < BN; c0 += 16) {
+            const bool vec = (p.n & 3) == 0;                 // 16-byte rows: vector loads and stores
+            for (int c0 = half * (BN / 2); c0 < (half + 1) * (BN / 2); c0 += 16) {
                 int v[16], u[16];
                 tmem_ld16(tmem + lane_addr + (uint32_t)c0, v);
                 if (TWO) tmem_ld16(tmem + lane_addr + (uint32_t)(BN + c0), u);
+                const int nb = n0 + c0;
+                if (m >= p.m || nb >= p.n) continue;                 // (after the warp-wide TMEM loads)
+                float o[16];
+                if (vec && nb + 16 <= p.n) {
+                    float sw[16], sw2[16], rs[16];
+                    const float4* s4 = reinterpret_cast<const float4*>(p.s_w + nb);
 #pragma unroll
-                for (int j = 0; j < 16; ++j) {
-                    const int n = n0 + c0 + j;
-                    if (m >= p.m || n >= p.n) continue;               // (after the warp-wide TMEM loads)
-                    const size_t o = (size_t)m * p.n + n;
+                    for (int j = 0; j < 4; ++j) reinterpret_cast<float4*>(sw)[j] = __ldg(s4 + j);
+                    if (TWO) {
+                        const float4* t4 = reinterpret_cast<const float4*>(p.s_w2 + nb);
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) reinterpret_cast<float4*>(sw2)[j] = __ldg(t4 + j);
+                    }
+                    float4* y4 = reinterpret_cast<float4*>(p.y + (size_t)m * p.n + nb);
+                    if (!TWO && p.resid != nullptr) {
+                        const float4* r4 = reinterpret_cast<const float4*>(p.resid + (size_t)m * p.n + nb);
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) reinterpret_cast<float4*>(rs)[j] = r4[j];
+                    }
+#pragma unroll
+                    for (int j = 0; j < 16; ++j) {
+                        const float g = fmul(fmul(i2f(v[j]), sw[j]), sx);
+                        if (TWO) o[j] = silu_gate(g, fmul(fmul(i2f(u[j]), sw2[j]), sx));
+                        else o[j] = p.resid != nullptr ? fadd(rs[j], g) : g;
+                    }
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) y4[j] = reinterpret_cast<const float4*>(o)[j];
+                    if (!TWO && p.resid == nullptr && p.acc != nullptr) {
+                        int4* a4 = reinterpret_cast<int4*>(p.acc + (size_t)m * p.n + nb);
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) a4[j] = reinterpret_cast<const int4*>(v)[j];
+                    }
+                    continue;
+                }
+#pragma unroll
+                for (int j = 0; j < 16; ++j) {                       // a ragged or unaligned edge
+                    const int n = nb + j;
+                    if (n >= p.n) continue;
+                    const size_t off = (size_t)m * p.n + n;
                     const float g = fmul(fmul(i2f(v[j]), __ldg(p.s_w + n)), sx);
                     if (TWO) {
-                        const float up = fmul(fmul(i2f(u[j]), __ldg(p.s_w2 + n)), sx);
-                        p.y[o] = silu_gate(g, up);
+                        p.y[off] = silu_gate(g, fmul(fmul(i2f(u[j]), __ldg(p.s_w2 + n)), sx));
                     } else if (p.resid != nullptr) {
-                        p.y[o] = fadd(p.resid[o], g);
+                        p.y[off] = fadd(p.resid[off], g);
                     } else {
-                        p.y[o] = g;
-                        if (p.acc != nullptr) p.acc[o] = v[j];
+                        p.y[off] = g;
+                        if (p.acc != nullptr) p.acc[off] = v[j];
                     }
                 }
             }

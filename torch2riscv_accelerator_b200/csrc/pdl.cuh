@@ -64,6 +64,23 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity) {
     return false;
 }
 
+// Bounded spin on the mbarrier phase (test_wait never suspends the thread):
+// for one thread of a tight producer / consumer pipeline, where a suspended
+// wait would wake late. At most 2^26 polls (a fraction of a second).
+__device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity) {
+    const uint32_t a = smem_u32(bar);
+    for (int i = 0; i < (1 << 26); ++i) {
+        uint32_t ok;
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+            : "=r"(ok)
+            : "r"(a), "r"(parity)
+            : "memory");
+        if (ok) return true;
+    }
+    return false;
+}
+
 // Sense-reversing barrier among `n` CTAs over global memory: count[0] counts
 // arrivals, gen[0] is bumped by the last one. Bounded: gives up after ~2^22
 // polls (about 0.2 s) and returns false. Call with the whole CTA; the CTA's
