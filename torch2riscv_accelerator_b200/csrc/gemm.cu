@@ -101,6 +101,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     __shared__ __align__(8) uint64_t full[kStages], empty[kStages], acc_full;
     __shared__ uint32_t tmem_base;
     __shared__ int failed;
+    __shared__ uint32_t silu_tab[256];                         // EXP / RECIP tables (SwiGLU epilogue)
+    if (TWO) stage_silu_tables(silu_tab);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int n0 = blockIdx.x * BN, m0 = blockIdx.y * kBM;
     const int kt_n = (p.k + kBK - 1) / kBK;
@@ -207,7 +209,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
                     for (int j = 0; j < 16; ++j) {
                         const float g = fmul(fmul(i2f(v[j]), sw[j]), sx);
-                        if (TWO) o[j] = silu_gate(g, fmul(fmul(i2f(u[j]), sw2[j]), sx));
+                        if (TWO) o[j] = silu_gate_tab(g, fmul(fmul(i2f(u[j]), sw2[j]), sx), silu_tab);
                         else o[j] = p.resid != nullptr ? fadd(rs[j], g) : g;
                     }
 #pragma unroll
@@ -226,7 +228,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     const size_t off = (size_t)m * p.n + n;
                     const float g = fmul(fmul(i2f(v[j]), __ldg(p.s_w + n)), sx);
                     if (TWO) {
-                        p.y[off] = silu_gate(g, fmul(fmul(i2f(u[j]), __ldg(p.s_w2 + n)), sx));
+                        p.y[off] = silu_gate_tab(g, fmul(fmul(i2f(u[j]), __ldg(p.s_w2 + n)), sx), silu_tab);
                     } else if (p.resid != nullptr) {
                         p.y[off] = fadd(p.resid[off], g);
                     } else {

@@ -248,6 +248,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(LinearParams p, G
     __shared__ uint32_t bamax[MR];
     __shared__ unsigned long long bkey[MR];
     __shared__ int last, failed;
+    __shared__ uint32_t silu_tab[256];                         // EXP / RECIP tables (SwiGLU epilogue)
     if (tid < MR) {
         bamax[tid] = 0u;
         bkey[tid] = 0ull;
@@ -284,6 +285,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(LinearParams p, G
             if (two) sw2[j] = __ldg(p.s_w2 + n);
         }
     }
+    if (two) stage_silu_tables(silu_tab);                      // constants too
     if (pro == PRO_RMSQ) {                                     // the norm gain: a constant, staged now
 #pragma unroll 1
         for (int c = tid; c < k; c += kGemvThreads) gs[c] = __ldg(p.norm_g + c);
@@ -376,7 +378,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(LinearParams p, G
                         p.y[o] = fadd(rs[m * nj + j], v);
                     } else {
                         const float u = fmul(fmul(i2f(acc2[m]), sw2[j]), sx[m]);
-                        const float h = silu_gate(v, u);
+                        const float h = silu_gate_tab(v, u, silu_tab);
                         p.y[o] = h;
                         tamax[m] = max(tamax[m], __float_as_uint(fabsf(h)));   // as bits: NaN above numbers
                     }

@@ -113,7 +113,7 @@ __device__ __forceinline__ float sfu_exp(float x) {
 
 // RECIP (llm/sfu.py:85-96): x = +-m*2^E, i = top 6 fraction bits,
 // y0 = T[i] + r*S[i], y1 = y0*(2 - m*y0), +-y1*2^-E.
-__device__ __forceinline__ float sfu_recip(float x) {
+__device__ __forceinline__ float sfu_recip_tab(float x, const uint32_t* rt, const uint32_t* rs) {
     uint32_t b = __float_as_uint(ftz(x));
     uint32_t s = b & 0x80000000u;
     int e = (int)((b >> 23) & 0xFFu);
@@ -123,10 +123,12 @@ __device__ __forceinline__ float sfu_recip(float x) {
     int i = (int)(frac >> 17);
     float m = __uint_as_float(frac | 0x3F800000u);
     float r = fmul(i2f((int)(frac & 0x1FFFFu)), 0x1p-17f);
-    float y0 = fadd(tab(g_rec_t, i), fmul(r, tab(g_rec_s, i)));
+    float y0 = fadd(__uint_as_float(rt[i]), fmul(r, __uint_as_float(rs[i])));
     float y1 = fmul(y0, fsub(2.f, fmul(m, y0)));
     return __uint_as_float(__float_as_uint(ldexp_ftz(y1, 127 - e)) | s);
 }
+
+__device__ __forceinline__ float sfu_recip(float x) { return sfu_recip_tab(x, g_rec_t, g_rec_s); }
 
 // RSQRT (llm/sfu.py:99-114): x = m*2^E, odd E uses m' = 2m; j = 64*(E odd) +
 // top 6 fraction bits; y1 = y0*(1.5 - (m'*(y0*y0))*0.5); y1 * 2^(-(E - odd)/2).
@@ -154,6 +156,22 @@ __device__ __forceinline__ float sfu_rsqrt(float x) {
 __device__ __forceinline__ float silu_gate(float g, float u) {
     float sig = sfu_recip(fadd(1.f, sfu_exp(fmul(g, -1.f))));
     return fmul(fmul(g, sig), u);
+}
+
+// The same with the EXP and RECIP tables wherever the caller keeps them (tab:
+// EXP T | EXP S | RECIP T | RECIP S, 64 words each; shared memory when every
+// lane looks up its own index: constant memory serializes divergent reads).
+__device__ __forceinline__ float silu_gate_tab(float g, float u, const uint32_t* tab) {
+    float sig = sfu_recip_tab(fadd(1.f, sfu_exp_tab(fmul(g, -1.f), tab, tab + 64)), tab + 128, tab + 192);
+    return fmul(fmul(g, sig), u);
+}
+
+// Copy the four 64-word tables of silu_gate_tab into shared memory (whole block).
+__device__ __forceinline__ void stage_silu_tables(uint32_t* tab) {
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) {
+        const int t = i >> 6, j = i & 63;
+        tab[i] = t == 0 ? g_exp_t[j] : t == 1 ? g_exp_s[j] : t == 2 ? g_rec_t[j] : g_rec_s[j];
+    }
 }
 
 // Fixed-order sum of n values v(i) (llm/ref_model.py:179-186), computed by one
