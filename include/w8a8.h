@@ -218,7 +218,9 @@ int w8a8_attn(const W8A8AttnArgs* args, void* stream);
 /* The same attention for `slots` sequences of one row each (batched decode):
  * slot b uses pos[b], qkv row b and att row b, and the caches at
  * k_cache + b * slot_stride and v_cache + b * slot_stride bytes (args->rows
- * must be 1). Each slot's row is computed exactly as a one-row w8a8_attn call.
+ * must be 1; slot_stride a multiple of head_dim and of seq_len). One CTA per
+ * (KV head, slot) streams the slot's cache through TMA tiles. Each slot's row
+ * is computed exactly as a one-row w8a8_attn call.
  * Replaces the attention of the batched list (llm/compile_batch.py via
  * BatchLlamaDevice.step, llm/runtime.py:193-208). */
 int w8a8_attn_batch(const W8A8AttnArgs* args, int slots, size_t slot_stride, void* stream);

@@ -129,7 +129,7 @@ __device__ __forceinline__ void warp_norm_rope(float* buf, int hd, const float* 
 }
 
 __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
-    extern __shared__ __align__(16) unsigned char sm[];
+    extern __shared__ __align__(128) unsigned char sm[];
     cg::cluster_group cl = cg::this_cluster();
     const int hd = p.head_dim, H = p.heads, Hk = p.kv_heads, G = H / Hk, M = p.rows, T = p.seq_len;
     // batched decode: grid z is the slot (one row, its own position, qkv / att
@@ -416,6 +416,331 @@ unsigned int attn_read_clear_errors() {
     cudaMemcpyFromSymbol(&v, g_attn_errors, sizeof(v));
     cudaMemcpyToSymbol(g_attn_errors, &zero, sizeof(zero));
     return v;
+}
+
+// ---------------------------------------------------------------------------
+// Batched decode: one CTA per (KV head, slot), no cluster. The slot's cache
+// streams through a 4-stage ring of TMA tiles (its K rows, tp positions x
+// head_dim; then its V^T rows, head_dim x tp positions) filled by a producer
+// warp; the scores of every position stay in shared memory, so the softmax
+// (global max, EXP, int8 p; NORM's ordered sum over the whole row) needs no
+// exchange. The current position's K / V row is written to the cache and
+// patched into its tile when that tile lands. Same arithmetic, step for step,
+// as the cluster kernel above (and so as a one-row decode).
+constexpr int kSbStages = 4;
+constexpr int kSbThreads = 288;                                // 8 compute warps + 1 producer warp
+constexpr int kSbWarps = 8;
+
+struct StreamMaps {
+    CUtensorMap k, v;                                          // K rows [.][hd]; V^T rows [.][T]
+};
+
+struct SbSmem {
+    size_t ring, scs, ps, qs, fbuf, tab, gain, etab, newk, newv, total;
+};
+
+__host__ __device__ inline SbSmem sb_smem(int G, int hd, int T, int tp) {
+    auto a16 = [](size_t b) { return (b + 15) & ~size_t(15); };
+    const int Tp = (T + tp - 1) / tp * tp;
+    SbSmem s{};
+    size_t o = 0;
+    s.ring = o; o += a16((size_t)kSbStages * tp * hd);        // [stage][tp * hd]
+    s.scs = o;  o += a16((size_t)G * Tp * 4);                 // scores / e of every position, per row
+    s.ps = o;   o += a16((size_t)G * Tp);                     // int8 p
+    s.qs = o;   o += a16((size_t)G * hd);
+    s.fbuf = o; o += a16((size_t)2 * kSbWarps * hd * 4);      // per-warp fp32 head vectors (q | k)
+    s.tab = o;  o += a16((size_t)2 * hd * 4);                 // cos | sin of the slot's position
+    s.gain = o; o += a16((size_t)2 * hd * 4);                 // q_norm | k_norm
+    s.etab = o; o += a16(128 * 4);
+    s.newk = o; o += a16((size_t)hd);                         // the new K / V rows (int8)
+    s.newv = o; o += a16((size_t)hd);
+    s.total = o;
+    return s;
+}
+
+__global__ void __launch_bounds__(kSbThreads, 1)
+    attn_stream_kernel(const __grid_constant__ StreamMaps maps, AttnParams p, int tp) {
+    extern __shared__ __align__(128) unsigned char sm[];
+    const int hd = p.head_dim, H = p.heads, Hk = p.kv_heads, G = H / Hk, T = p.seq_len;
+    const int kvh = blockIdx.x, slot = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const bool producer = warp == kSbWarps;
+    const int Tp = (T + tp - 1) / tp * tp;
+    const int qkv_dim = (H + 2 * Hk) * hd, q_dim = H * hd, kv_dim = Hk * hd;
+    const SbSmem L = sb_smem(G, hd, T, tp);
+    int8_t* ring = reinterpret_cast<int8_t*>(sm + L.ring);
+    float* scs = reinterpret_cast<float*>(sm + L.scs);
+    int8_t* ps = reinterpret_cast<int8_t*>(sm + L.ps);
+    int8_t* qs = reinterpret_cast<int8_t*>(sm + L.qs);
+    float* fbuf = reinterpret_cast<float*>(sm + L.fbuf);
+    float* tabs = reinterpret_cast<float*>(sm + L.tab);
+    float* gains = reinterpret_cast<float*>(sm + L.gain);
+    uint32_t* etab = reinterpret_cast<uint32_t*>(sm + L.etab);
+    int8_t* newk = reinterpret_cast<int8_t*>(sm + L.newk);
+    int8_t* newv = reinterpret_cast<int8_t*>(sm + L.newv);
+    __shared__ __align__(8) uint64_t full[kSbStages], empty[kSbStages];
+    __shared__ float sq[kMaxG], gmx[kMaxG], wred[kSbWarps][kMaxG], rcp[kMaxG];
+    __shared__ int wsum[kSbWarps][kMaxG], lsum[kMaxG];
+    __shared__ int failed;
+    const int pos = p.pos[slot];                               // written by an earlier step: read before the wait
+    const int nt = pos / tp + 1;                               // tiles with positions <= pos
+    const size_t krow0 = (size_t)slot * (p.slot_stride / hd) + (size_t)kvh * T;
+    const size_t vrow0 = (size_t)slot * (p.slot_stride / T) + (size_t)kvh * hd;
+    const uint32_t tile_bytes = (uint32_t)(tp * hd);
+    if (tid == 0) {
+        failed = 0;
+        for (int s = 0; s < kSbStages; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kSbWarps);
+        }
+        mbar_fence_init();
+    }
+    __syncthreads();
+    auto issue = [&](int i) {                                  // ring tile i: K tile i, then V tile i - nt
+        const int s = i % kSbStages;
+        mbar_expect_tx(&full[s], tile_bytes);
+        if (i < nt) tma_load_2d(ring + (size_t)s * tile_bytes, &maps.k, 0, (int)(krow0 + (size_t)i * tp), &full[s]);
+        else tma_load_2d(ring + (size_t)s * tile_bytes, &maps.v, (i - nt) * tp, (int)vrow0, &full[s]);
+    };
+    if (producer && lane == 0)                                 // cache rows of earlier steps: before the wait
+        for (int i = 0; i < kSbStages && i < 2 * nt; ++i) issue(i);
+    if (tid < 64) {
+        etab[tid] = g_exp_t[tid];
+        etab[64 + tid] = g_exp_s[tid];
+    }
+    for (int c = tid; c < hd; c += kSbThreads) {
+        tabs[c] = __ldg(p.cos + (size_t)pos * hd + c);
+        tabs[hd + c] = __ldg(p.sin + (size_t)pos * hd + c);
+        if (p.qk_norm) {
+            gains[c] = __ldg(p.q_norm + c);
+            gains[hd + c] = __ldg(p.k_norm + c);
+        }
+    }
+    pdl_wait();
+    pdl_trigger();
+    __syncthreads();
+
+    if (producer) {
+        if (lane == 0) {                                       // refill each stage once the 8 warps are done
+            for (int i = kSbStages; i < 2 * nt; ++i) {
+                const int s = i % kSbStages;
+                if (!mbar_wait_spin(&empty[s], (uint32_t)(((i / kSbStages) - 1) & 1))) {
+                    atomicOr(&g_attn_errors, 4u);
+                    failed = 1;
+                    break;
+                }
+                issue(i);
+            }
+        }
+    } else {
+        const float* qrow = p.qkv + (size_t)slot * qkv_dim;
+        // q path (warps from 0) and this position's K / V rows (the last warp)
+        for (int r = warp; r < G; r += kSbWarps) {
+            float* buf = fbuf + warp * hd;
+            const float* src = qrow + (size_t)(kvh * G + r) * hd;
+            for (int c = lane; c < hd; c += 32) buf[c] = src[c];
+            __syncwarp();
+            warp_norm_rope(buf, hd, p.qk_norm ? gains : nullptr, p.eps, p.inv_hd, tabs, tabs + hd, lane);
+            float a = 0.f;
+            for (int c = lane; c < hd; c += 32) a = nanmax(a, fabsf(buf[c]));
+            a = warp_max(a);
+            const float sc = fmul(a, W8A8_C127);
+            const float inv = sfu_recip(sc);
+            for (int c = lane; c < hd; c += 32) qs[r * hd + c] = (int8_t)to_i8(fmul(buf[c], inv));
+            if (lane == 0) sq[r] = sc;
+            __syncwarp();
+        }
+        if (warp == kSbWarps - 1) {
+            float* kb = fbuf + (kSbWarps + warp) * hd;
+            const float* ksrc = qrow + q_dim + (size_t)kvh * hd;
+            const float* vsrc = qrow + q_dim + kv_dim + (size_t)kvh * hd;
+            for (int c = lane; c < hd; c += 32) kb[c] = ksrc[c];
+            __syncwarp();
+            warp_norm_rope(kb, hd, p.qk_norm ? gains + hd : nullptr, p.eps, p.inv_hd, tabs, tabs + hd, lane);
+            int8_t* kdst = p.kc + (size_t)slot * p.slot_stride + ((size_t)kvh * T + pos) * hd;
+            int8_t* vdst = p.vc + (size_t)slot * p.slot_stride + (size_t)kvh * hd * T + pos;
+            for (int c = lane; c < hd; c += 32) {
+                const int8_t kq = (int8_t)to_i8(fmul(kb[c], p.inv_sk));
+                const int8_t vq = (int8_t)to_i8(fmul(vsrc[c], p.inv_sv));
+                kdst[c] = kq;
+                vdst[(size_t)c * T] = vq;
+                newk[c] = kq;
+                newv[c] = vq;
+            }
+        }
+        named_barrier_sync(1, kSbWarps * 32);                  // q rows and the new K / V rows are ready
+        // ---- pass 1: scores of positions <= pos; thread <-> (row, position of the tile)
+        const int vpr = hd / 16;
+        float mx[kMaxG];
+#pragma unroll
+        for (int r = 0; r < kMaxG; ++r) mx[r] = -INFINITY;
+        for (int i = 0; i < nt; ++i) {
+            const int s = i % kSbStages;
+            if (!mbar_wait_spin(&full[s], (uint32_t)((i / kSbStages) & 1))) {
+                if (tid == 0) atomicOr(&g_attn_errors, 4u);
+                failed = 1;
+            }
+            int8_t* kt = ring + (size_t)s * tile_bytes;        // [tp][hd]
+            if (i == nt - 1) {                                 // the tile holding pos: the new K row
+                if (tid < hd / 16)
+                    reinterpret_cast<int4*>(kt + (size_t)(pos - i * tp) * hd)[tid] = reinterpret_cast<const int4*>(newk)[tid];
+                named_barrier_sync(1, kSbWarps * 32);
+            }
+            for (int pr = tid; pr < G * tp; pr += kSbWarps * 32) {
+                const int r = pr / tp, t = pr % tp, tpos = i * tp + t;
+                if (tpos > pos) continue;
+                const int4* kr = reinterpret_cast<const int4*>(kt + (size_t)t * hd);
+                const int4* qr = reinterpret_cast<const int4*>(qs + r * hd);
+                int a = 0, c = t % vpr;
+                for (int j = 0; j < vpr; ++j) {
+                    const int4 x = kr[c], y = qr[c];
+                    c = c + 1 == vpr ? 0 : c + 1;
+                    a = dp4a(x.x, y.x, a);
+                    a = dp4a(x.y, y.y, a);
+                    a = dp4a(x.z, y.z, a);
+                    a = dp4a(x.w, y.w, a);
+                }
+                const float sc = fmul(fmul(i2f(a), sq[r]), p.a_k);
+                scs[r * Tp + tpos] = sc;
+#pragma unroll
+                for (int rr = 0; rr < kMaxG; ++rr)
+                    if (rr == r) mx[rr] = nanmax(mx[rr], sc);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+        }
+#pragma unroll
+        for (int r = 0; r < kMaxG; ++r) {
+            const float m = warp_max(mx[r]);
+            if (lane == 0 && r < G) wred[warp][r] = m;
+        }
+        named_barrier_sync(1, kSbWarps * 32);
+        if (tid < G) {
+            float m = wred[0][tid];
+            for (int w = 1; w < kSbWarps; ++w) m = nanmax(m, wred[w][tid]);
+            gmx[tid] = m;
+        }
+        named_barrier_sync(1, kSbWarps * 32);
+        // ---- the softmax over positions 0 .. pos of every row
+        const int n = pos + 1;
+        if (p.variant == 0) {                                  // NORM: e, the ordered sum, p = i8(127 e / sum)
+            for (int i = tid; i < G * n; i += kSbWarps * 32) {
+                const int r = i / n, t = i % n;
+                scs[r * Tp + t] = sfu_exp_tab(fsub(scs[r * Tp + t], gmx[r]), etab, etab + 64);
+            }
+            named_barrier_sync(1, kSbWarps * 32);
+            for (int r = warp; r < G; r += kSbWarps) {
+                const float* er = scs + r * Tp;
+                const float ssum = red_sum16([&](int i) { return er[i]; }, n, lane);
+                if (lane == 0) rcp[r] = sfu_recip(ssum);
+            }
+            named_barrier_sync(1, kSbWarps * 32);
+            for (int i = tid; i < G * Tp; i += kSbWarps * 32) {
+                const int r = i / Tp, t = i % Tp;
+                ps[i] = t < n ? (int8_t)to_i8(fmul(fmul(scs[r * Tp + t], rcp[r]), 127.f)) : (int8_t)0;
+            }
+        } else {                                               // QSUM: eq = i8(127 e) and its exact sum
+            int sum[kMaxG];
+#pragma unroll
+            for (int r = 0; r < kMaxG; ++r) sum[r] = 0;
+            for (int i = tid; i < G * Tp; i += kSbWarps * 32) {
+                const int r = i / Tp, t = i % Tp;
+                int q = 0;
+                if (t < n) q = to_i8(fmul(sfu_exp_tab(fsub(scs[r * Tp + t], gmx[r]), etab, etab + 64), 127.f));
+                ps[i] = (int8_t)q;
+#pragma unroll
+                for (int rr = 0; rr < kMaxG; ++rr)
+                    if (rr == r) sum[rr] += q;
+            }
+#pragma unroll
+            for (int r = 0; r < kMaxG; ++r) {
+                const int v = warp_sum_i(sum[r]);
+                if (lane == 0 && r < G) wsum[warp][r] = v;
+            }
+            named_barrier_sync(1, kSbWarps * 32);
+            if (tid < G) {
+                int v = 0;
+                for (int w = 0; w < kSbWarps; ++w) v += wsum[w][tid];
+                lsum[tid] = v;
+            }
+        }
+        named_barrier_sync(1, kSbWarps * 32);
+        // ---- pass 2: p.V over the V^T tiles; thread <-> (row, channel) pairs
+        constexpr int kMaxPairs = kMaxG * 256 / (kSbWarps * 32);
+        int acc[kMaxPairs];
+#pragma unroll
+        for (int j = 0; j < kMaxPairs; ++j) acc[j] = 0;
+        const int wpr = tp / 16;                                // 16-byte words per V^T tile row
+        for (int i = 0; i < nt; ++i) {
+            const int ri = nt + i, s = ri % kSbStages;
+            if (!mbar_wait_spin(&full[s], (uint32_t)((ri / kSbStages) & 1))) {
+                if (tid == 0) atomicOr(&g_attn_errors, 4u);
+                failed = 1;
+            }
+            int8_t* vt = ring + (size_t)s * tile_bytes;        // [hd][tp]
+            if (i == nt - 1) {                                 // the new V column
+                for (int c = tid; c < hd; c += kSbWarps * 32) vt[(size_t)c * tp + (pos - i * tp)] = newv[c];
+                named_barrier_sync(1, kSbWarps * 32);
+            }
+#pragma unroll
+            for (int j = 0; j < kMaxPairs; ++j) {
+                const int pr = tid + j * kSbWarps * 32;
+                if (pr >= G * hd) break;
+                const int r = pr / hd, c = pr % hd;
+                const int4* vr = reinterpret_cast<const int4*>(vt + (size_t)c * tp);
+                const int4* pp = reinterpret_cast<const int4*>(ps + (size_t)r * Tp + (size_t)i * tp);
+                int a0 = 0, a1 = 0, w = c % wpr;
+                for (int u = 0; u < wpr; ++u) {
+                    const int4 x = pp[w], y = vr[w];
+                    w = w + 1 == wpr ? 0 : w + 1;
+                    a0 = dp4a(x.x, y.x, a0);
+                    a1 = dp4a(x.y, y.y, a1);
+                    a0 = dp4a(x.z, y.z, a0);
+                    a1 = dp4a(x.w, y.w, a1);
+                }
+                acc[j] += a0 + a1;
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+        }
+        float* att = p.att + (size_t)slot * q_dim;
+#pragma unroll
+        for (int j = 0; j < kMaxPairs; ++j) {
+            const int pr = tid + j * kSbWarps * 32;
+            if (pr >= G * hd) break;
+            const int r = pr / hd, c = pr % hd;
+            const float o = i2f(acc[j]);
+            float out;
+            if (p.variant == 0) out = fmul(o, p.a_v);
+            else out = fmul(fmul(o, fmul(sfu_recip(i2f(lsum[r])), 127.f)), p.a_v);   // sum <= 127 T: exact
+            att[(size_t)(kvh * G + r) * hd + c] = out;
+        }
+    }
+    __syncthreads();
+    if (failed && producer && lane == 0)                       // no copy may land after the CTA exits
+        for (int s = 0; s < kSbStages; ++s) mbar_wait(&full[s], 0u), mbar_wait(&full[s], 1u);
+}
+
+size_t attn_stream_smem(int heads, int kv_heads, int head_dim, int seq_len) {
+    const int tp = seq_len < 128 ? seq_len : 128;
+    return sb_smem(heads / kv_heads, head_dim, seq_len, tp).total;
+}
+
+cudaError_t launch_attn_stream(const AttnParams& p, cudaStream_t st) {
+    const int hd = p.head_dim, T = p.seq_len, G = p.heads / p.kv_heads;
+    const int tp = T < 128 ? T : 128;
+    const size_t slot_k_rows = p.slot_stride / hd, slot_v_rows = p.slot_stride / T;
+    StreamMaps maps{};
+    const uint64_t krows = (uint64_t)(p.slots - 1) * slot_k_rows + (uint64_t)p.kv_heads * T;
+    const uint64_t vrows = (uint64_t)(p.slots - 1) * slot_v_rows + (uint64_t)p.kv_heads * hd;
+    if (!make_map_u8(&maps.k, p.kc, (uint64_t)hd, krows, (uint64_t)hd, (uint32_t)hd, (uint32_t)tp, false) ||
+        !make_map_u8(&maps.v, p.vc, (uint64_t)T, vrows, (uint64_t)T, (uint32_t)tp, (uint32_t)hd, false))
+        return cudaErrorInvalidValue;
+    const size_t smem = sb_smem(G, hd, T, tp).total;
+    cudaError_t e = cudaFuncSetAttribute(attn_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+    e = cudaFuncSetAttribute(attn_stream_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    if (e != cudaSuccess) return e;
+    return launch_k(attn_stream_kernel, dim3(p.kv_heads, p.slots), dim3(kSbThreads), smem, st, maps, p, tp);
 }
 
 cudaError_t launch_attn(const AttnParams& q, cudaStream_t st) {

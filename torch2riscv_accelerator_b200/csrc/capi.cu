@@ -296,8 +296,10 @@ int w8a8_attn_batch(const W8A8AttnArgs* a, int slots, size_t slot_stride, void* 
     if (a->rows != 1 || slots <= 0 || slots > 65535) return W8A8_EINVAL;
     if (slot_stride % 16) return W8A8_EALIGN;
     if (slots > 1 && slot_stride < (size_t)a->kv_heads * a->seq_len * a->head_dim) return W8A8_EINVAL;
+    if (slot_stride % (size_t)a->head_dim || slot_stride % (size_t)a->seq_len) return W8A8_EALIGN;
+    if (attn_stream_smem(a->heads, a->kv_heads, a->head_dim, a->seq_len) > 200 * 1024) return W8A8_EINVAL;
     p.slots = slots, p.slot_stride = slot_stride;
-    return cuda_status(launch_attn(p, S(stream)));
+    return cuda_status(launch_attn_stream(p, S(stream)));
 }
 
 int w8a8_argmax(const float* logits, int rows, int n, int32_t* out, void* stream) {

@@ -71,14 +71,6 @@ __device__ __forceinline__ void mma_commit(uint64_t* bar) {
                  : "memory");
 }
 
-__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::
-            "r"(smem_u32(dst)),
-        "l"(map), "r"(x), "r"(y), "r"(smem_u32(bar))
-        : "memory");
-}
-
 // 16 consecutive int32 columns of this warp's 32 lanes (one row per thread)
 __device__ __forceinline__ void tmem_ld16(uint32_t taddr, int* v) {
     asm volatile(
@@ -263,18 +255,23 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
+bool make_map_u8(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows, uint64_t row_stride,
+                 uint32_t box_inner, uint32_t box_rows, bool swizzle128) {
+    auto fn = encode_fn();
+    if (fn == nullptr) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)inner, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)row_stride};
+    const cuuint32_t box[2] = {box_inner, box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 // 2-D int8 map of a row-major [rows][k] matrix, box 128 bytes x box_rows,
 // 128-byte swizzle; rows or k beyond the matrix read as zero
 static bool make_map(CUtensorMap* map, const void* base, int rows, int k, int box_rows) {
-    auto fn = encode_fn();
-    if (fn == nullptr) return false;
-    const cuuint64_t dims[2] = {(cuuint64_t)k, (cuuint64_t)rows};
-    const cuuint64_t strides[1] = {(cuuint64_t)k};
-    const cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)box_rows};
-    const cuuint32_t estr[2] = {1, 1};
-    return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
-              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+    return make_map_u8(map, base, (uint64_t)k, (uint64_t)rows, (uint64_t)k, kBK, (uint32_t)box_rows, true);
 }
 
 size_t gemm_smem(int bn, bool two) { return (size_t)kStages * (kBM * kBK + (size_t)bn * kBK * (two ? 2 : 1)) + 1024; }

@@ -2,6 +2,7 @@
 #pragma once
 #include <cstddef>
 #include <cstdint>
+#include <cuda.h>
 #include <cuda_runtime.h>
 
 namespace w8a8 {
@@ -75,6 +76,10 @@ struct GemmParams {
     int32_t* acc;             // [m, n] raw accumulators, or null (without resid / w2)
 };
 size_t gemm_smem(int bn, bool two);
+// A 2-D uint8 TMA map: [rows][inner] with row_stride bytes between rows
+// (16-byte multiples), box box_inner x box_rows, optional 128-byte swizzle.
+bool make_map_u8(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows, uint64_t row_stride,
+                 uint32_t box_inner, uint32_t box_rows, bool swizzle128);
 cudaError_t launch_gemm(const GemmOperands& a, const GemmParams& p, cudaStream_t st);
 unsigned int gemm_read_clear_errors();
 cudaError_t launch_norm_quant(const float* x, const float* g, int m, int k, float eps, float inv_k, int8_t* xq,
@@ -117,6 +122,9 @@ constexpr int kMaxCluster = 8;  // attention CTAs per KV head (portable cluster 
 size_t attn_smem_needed(int rows, int heads, int kv_heads, int head_dim, int seq_len, int variant);
 bool attn_supported(int rows, int heads, int kv_heads, int head_dim, int seq_len, int variant);
 cudaError_t launch_attn(const AttnParams& p, cudaStream_t st);
+// batched decode (p.slots > 0, one row per slot): the streaming kernel
+size_t attn_stream_smem(int heads, int kv_heads, int head_dim, int seq_len);
+cudaError_t launch_attn_stream(const AttnParams& p, cudaStream_t st);
 
 cudaError_t launch_embed(const int32_t* tokens, int m, const int8_t* emb_q, const float* emb_s, int vocab, int dim,
                          float* x, cudaStream_t st);
