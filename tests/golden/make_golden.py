@@ -24,6 +24,10 @@ Fixtures:
                 device SFU.
   moe.npz       hf_generic.QMixtralMoe rows of a synthetic Mixtral block
                 (compiler/tests/test_hf_moe.synthetic_model's shape).
+  tiny_a_d8.w8a8  tiny model "a" of dm_tiny.npz written by the reference's
+                exporter (llm/export_w8a8.export, D = 8).
+  tiny_a.bin    the same fp32 weights as a llama2.c legacy checkpoint
+                (separate classifier), checked against llm/checkpoint.load.
 
     python tests/golden/make_golden.py [--skip-c0]
 """
@@ -308,14 +312,35 @@ def gen_moe():
          us=q.us.numpy(), dq=q.dq.numpy(), ds=q.ds.numpy(), top_k=q.k)
 
 
+def gen_files():
+    import checkpoint
+    from export_w8a8 import export
+    from torch2riscv_accelerator_b200 import config as C
+    from torch2riscv_accelerator_b200.loaders import write_llama2c
+    cfg, w, kv = tiny_models()["a"]
+    out = os.path.join(HERE, "tiny_a_d8.w8a8")
+    n = export(cfg, w, kv, 8, out)
+    print(f"  {out}: {n} bytes (reference exporter, D = 8)")
+    mc = C.ModelConfig("tiny-a", cfg.dim, cfg.hidden, cfg.layers, cfg.heads, cfg.kv_heads, cfg.head_size, cfg.vocab,
+                       cfg.seq_len, theta=10000.0, eps=1e-5, tied=False, attn="norm", rope="llama2c")
+    path = os.path.join(HERE, "tiny_a.bin")
+    write_llama2c(path, mc, {k: np.asarray(v, F) for k, v in w.items()})
+    rc, rw = checkpoint.load(path)
+    assert (rc.dim, rc.hidden, rc.layers, rc.heads, rc.kv_heads, rc.vocab, rc.seq_len) == \
+        (cfg.dim, cfg.hidden, cfg.layers, cfg.heads, cfg.kv_heads, cfg.vocab, cfg.seq_len)
+    for k in w:
+        assert np.array_equal(np.asarray(rw[k]), np.asarray(w[k], F)), k
+    print(f"  {path}: llm/checkpoint.load reads it back exactly")
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--skip-c0", action="store_true")
-    ap.add_argument("--only", help="comma list: sfu,convert,tiny,c0,hf,moe")
+    ap.add_argument("--only", help="comma list: sfu,convert,tiny,c0,hf,moe,files")
     a = ap.parse_args()
     only = set(a.only.split(",")) if a.only else None
     steps = [("sfu", gen_sfu), ("convert", gen_convert), ("tiny", gen_dm_tiny), ("c0", gen_dm_c0),
-             ("hf", gen_hf), ("moe", gen_moe)]
+             ("hf", gen_hf), ("moe", gen_moe), ("files", gen_files)]
     for name, fn in steps:
         if (only and name not in only) or (name == "c0" and a.skip_c0):
             continue
