@@ -294,7 +294,12 @@ static cudaError_t launch_gemm_t(const GemmOperands& a, const GemmParams& p, cud
 
 cudaError_t launch_gemm(const GemmOperands& a, const GemmParams& p, cudaStream_t st) {
     if (a.w2 != nullptr) return launch_gemm_t<128, true>(a, p, st);
-    if (p.n >= 2048) return launch_gemm_t<256, false>(a, p, st);
+    // 256-column tiles only when they still give every SM a tile
+    int sms = 0, dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const long tiles256 = (long)((p.n + 255) / 256) * ((p.m + kBM - 1) / kBM);
+    if (tiles256 >= (sms > 0 ? sms : 148)) return launch_gemm_t<256, false>(a, p, st);
     return launch_gemm_t<128, false>(a, p, st);
 }
 
