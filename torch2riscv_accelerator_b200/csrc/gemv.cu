@@ -41,7 +41,7 @@ constexpr int kGemvThreads = kThreads + 32;                   // + 1 producer wa
 
 struct GemvCfg {
     int pro, epi;             // Prologue / Epilogue kinds
-    int tr, S;                // tile rows; consumer threads per row
+    int tr, S, ls, lt;        // tile rows (tr = 1 << lt); consumer threads per row (S = 1 << ls)
     int stages, ntiles;
 };
 
@@ -263,8 +263,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(LinearParams p, G
         mbar_fence_init();
     }
     __syncthreads();
-    auto issue = [&](int i) {                                  // tile i of this CTA -> stage i % stages
-        const int s = i % stages;
+    auto issue = [&](int i, int s) {                           // tile i of this CTA -> stage s = i % stages
         const int row0 = ((int)blockIdx.x + i * (int)gridDim.x) * tr;
         const uint32_t bytes = (uint32_t)(min(tr, p.n - row0) * k);
         mbar_expect_tx(&full[s], bytes * (two ? 2u : 1u));
@@ -274,12 +273,12 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(LinearParams p, G
     const int first = min(stages, my);
     if (producer && lane == 0) {
 #pragma unroll 1
-        for (int i = 0; i < first; ++i) issue(i);             // weights: before the wait
+        for (int i = 0; i < first; ++i) issue(i, i);          // weights: before the wait
     }
     // row j of this CTA = tile j / tr, row j % tr; its scales are constants too
 #pragma unroll 1
     for (int j = tid; j < my * tr; j += kGemvThreads) {
-        const int n = ((int)blockIdx.x + (j / tr) * (int)gridDim.x) * tr + j % tr;
+        const int n = ((int)blockIdx.x + (j >> cf.lt) * (int)gridDim.x) * tr + (j & (tr - 1));
         if (n < p.n) {
             sw[j] = __ldg(p.s_w + n);
             if (two) sw2[j] = __ldg(p.s_w2 + n);
@@ -300,8 +299,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(LinearParams p, G
     if (epi == EPI_RESID) {                                    // residual rows: written by earlier kernels
 #pragma unroll 4
         for (int j = tid; j < my * tr * MR; j += kGemvThreads) {
-            const int m = j / (my * tr), jj = j % (my * tr);
-            const int n = ((int)blockIdx.x + (jj / tr) * (int)gridDim.x) * tr + jj % tr;
+            const int m = MR == 1 ? 0 : j / (my * tr), jj = MR == 1 ? j : j % (my * tr);
+            const int n = ((int)blockIdx.x + (jj >> cf.lt) * (int)gridDim.x) * tr + (jj & (tr - 1));
             if (n < p.n && m < p.m) rs[m * nj + jj] = __ldcg(p.resid + (size_t)m * p.n + n);
         }
     }
@@ -309,15 +308,16 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(LinearParams p, G
 
     if (producer) {
         if (lane == 0) {                                       // refill each stage once its consumers are done
+            int s = 0, ph = 0;                                 // tile i -> stage s, reuse phase ph
 #pragma unroll 1
             for (int i = first; i < my; ++i) {
-                const int s = i % stages;
-                if (!mbar_wait(&empty[s], (uint32_t)(((i / stages) - 1) & 1))) {
+                if (!mbar_wait(&empty[s], (uint32_t)ph)) {
                     atomicOr(&g_gemv_errors, 2u);
                     failed = 1;
                     break;
                 }
-                issue(i);
+                issue(i, s);
+                if (++s == stages) s = 0, ph ^= 1;
             }
         }
     } else {
@@ -325,15 +325,15 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(LinearParams p, G
         // (S <= 32 threads per row, within one warp); the row is summed with
         // shuffles. A warp releases the stage before its epilogue. The argmax
         // key and the SwiGLU row amax are kept per thread and merged at the end.
-        const int r = tid / S, sl = tid % S;
+        const int r = tid >> cf.ls, sl = tid & (S - 1);
         uint32_t tamax[MR];
         unsigned long long tkey[MR];
 #pragma unroll
         for (int m = 0; m < MR; ++m) tamax[m] = 0u, tkey[m] = 0ull;
+        int s = 0, ph = 0;                                     // tile i -> stage s, fill phase ph
 #pragma unroll 1
-        for (int i = 0; i < my; ++i) {
-            const int s = i % stages;
-            if (!mbar_wait(&full[s], (uint32_t)((i / stages) & 1))) {
+        for (int i = 0; i < my; ++i, (++s == stages ? (s = 0, ph ^= 1) : 0)) {
+            if (!mbar_wait(&full[s], (uint32_t)ph)) {
                 atomicOr(&g_gemv_errors, 2u);
                 failed = 1;
                 break;
@@ -349,7 +349,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(LinearParams p, G
                 else tile_dots<MR, false>(wr, nullptr, xs, k, nch, sl, S, acc, acc2);
             }
             __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[s]);
+            if (lane == 0 && i + stages < my) mbar_arrive(&empty[s]);   // only a stage that is refilled
 #pragma unroll
             for (int m = 0; m < MR; ++m) {
 #pragma unroll
@@ -452,6 +452,10 @@ static Tiling tiling(const LinearParams& p, int mr, int pro, int epi) {
     t.cf.epi = epi;
     t.cf.tr = pw;
     t.cf.S = kConsumers / pw;                                 // consumer threads per row, at most 32
+    t.cf.ls = 0;
+    while ((1 << t.cf.ls) < t.cf.S) ++t.cf.ls;
+    t.cf.lt = 0;
+    while ((1 << t.cf.lt) < pw) ++t.cf.lt;
     const size_t stage = (size_t)pw * p.k * (epi == EPI_SWIGLU ? 2 : 1);
     size_t st = (stream ? kStreamRingBytes : kRingBytes) / stage;
     t.cf.stages = (int)(st < 2 ? 2 : (st > (size_t)kMaxStages ? kMaxStages : st));
