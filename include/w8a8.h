@@ -33,7 +33,7 @@ extern "C" {
 #define W8A8_ECUDA 3    /* the CUDA launch failed (cudaGetLastError) */
 #define W8A8_ESCRATCH 4 /* the scratch buffer is smaller than required */
 
-#define W8A8_ABI_VERSION 1
+#define W8A8_ABI_VERSION 2
 #define W8A8_MAX_ROWS 16 /* query rows per call (decode: 1, prefill chunk: 16) */
 
 /* ABI version (W8A8_ABI_VERSION) and a message for a status code. */
@@ -93,6 +93,16 @@ int w8a8_linear(const int8_t* xq, const float* s_x, int rows, int k, const int8_
 int w8a8_linear_fused(const float* x, const float* norm_g, float eps, int rows, int k, const int8_t* w,
                       const float* s_w, int n, const float* resid, float* y, float* s_x_out, void* stream);
 
+/* The decode chain's form of w8a8_linear_fused (the same results): x_amax
+ * [rows] (quant_act without norm only) is max|x| per row already posted by the
+ * kernel that wrote x (w8a8_attn's att_amax, w8a8_ffn_swiglu_chain's h_amax),
+ * so the prologue skips its block-wide reduction; clear (clear_n words, or
+ * NULL) is zeroed once this kernel has waited for its predecessors: a slot
+ * whose readers have all finished, ready for the next step's atomics. */
+int w8a8_linear_chain(const float* x, const float* norm_g, float eps, const uint32_t* x_amax, int rows, int k,
+                      const int8_t* w, const float* s_w, int n, const float* resid, float* y, uint32_t* clear,
+                      int clear_n, void* stream);
+
 /* Decode SwiGLU dispatch: [rmsnorm ->] quant_act(x) -> gate and up W8A8 GEMVs ->
  * h = (g * RECIP(1 + EXP(-g))) * u -> amax -> h_q = i8(h * RECIP(amax * F(1/127))).
  * w_gate, w_up: [hidden, k]; h: [rows, hidden] fp32; h_q: [rows, hidden] int8,
@@ -106,6 +116,13 @@ size_t w8a8_ffn_scratch_bytes(int rows);
 int w8a8_ffn_swiglu(const float* x, const float* norm_g, float eps, int rows, int k, const int8_t* w_gate,
                     const float* s_gate, const int8_t* w_up, const float* s_up, int hidden, float* h,
                     int8_t* h_q, float* s_h, void* scratch, size_t scratch_bytes, void* stream);
+
+/* The decode chain's SwiGLU: stops at h (no requantization) and posts max|h|
+ * per row into h_amax (zero before the call) by atomic max for the down
+ * projection's w8a8_linear_chain; clear as in w8a8_linear_chain. */
+int w8a8_ffn_swiglu_chain(const float* x, const float* norm_g, float eps, int rows, int k, const int8_t* w_gate,
+                          const float* s_gate, const int8_t* w_up, const float* s_up, int hidden, float* h,
+                          uint32_t* h_amax, uint32_t* clear, int clear_n, void* stream);
 
 /* w8a8_ffn_swiglu with the requantization of h, for a caller that cannot hand
  * over a scratch buffer. This entry point has no counterpart in the reference:
@@ -196,6 +213,8 @@ typedef struct {
     float* att;                /* [rows, heads head_dim] out */
     void* scratch;             /* unused (w8a8_attn_scratch_bytes() is 0); kept for the ABI layout */
     size_t scratch_bytes;
+    uint32_t* att_amax;        /* [rows] or NULL: max|att| per row posted by atomic max (decode chain:
+                                  the o-projection's w8a8_linear_chain reads it; zero before the call) */
 } W8A8AttnArgs;
 
 /* QK-norm, RoPE, the K/V rows appended at pos, per-head quant_act of q,

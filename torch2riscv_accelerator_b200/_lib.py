@@ -10,7 +10,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libw8a8_b200.so")
 
 W8A8_OK, W8A8_EINVAL, W8A8_EALIGN, W8A8_ECUDA, W8A8_ESCRATCH = 0, 1, 2, 3, 4
-ABI_VERSION = 1
+ABI_VERSION = 2
 
 
 class W8A8AttnArgs(C.Structure):
@@ -19,7 +19,7 @@ class W8A8AttnArgs(C.Structure):
                 ("q_norm", C.c_void_p), ("k_norm", C.c_void_p), ("eps", C.c_float), ("rope_cos", C.c_void_p),
                 ("rope_sin", C.c_void_p), ("inv_sk", C.c_float), ("inv_sv", C.c_float), ("a_k", C.c_float),
                 ("a_v", C.c_float), ("k_cache", C.c_void_p), ("v_cache", C.c_void_p), ("att", C.c_void_p),
-                ("scratch", C.c_void_p), ("scratch_bytes", C.c_size_t)]
+                ("scratch", C.c_void_p), ("scratch_bytes", C.c_size_t), ("att_amax", C.c_void_p)]
 
 
 P, I, F, Z, L = C.c_void_p, C.c_int, C.c_float, C.c_size_t, C.c_int64
@@ -34,6 +34,8 @@ PROTOTYPES = {
     "w8a8_set_pdl": (I, [I]),
     "w8a8_linear": (I, [P, P, I, I, P, P, I, P, P, P, P]),
     "w8a8_linear_fused": (I, [P, P, F, I, I, P, P, I, P, P, P, P]),
+    "w8a8_linear_chain": (I, [P, P, F, P, I, I, P, P, I, P, P, P, I, P]),
+    "w8a8_ffn_swiglu_chain": (I, [P, P, F, I, I, P, P, P, P, I, P, P, P, I, P]),
     "w8a8_ffn_scratch_bytes": (Z, [I]),
     "w8a8_ffn_swiglu": (I, [P, P, F, I, I, P, P, P, P, I, P, P, P, P, Z, P]),
     "w8a8_ffn_swiglu_noalloc": (I, [P, P, F, I, I, P, P, P, P, I, P, P, P, P]),

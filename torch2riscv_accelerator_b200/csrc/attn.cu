@@ -166,6 +166,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
     __shared__ int wsum[kAttnWarps][kMaxRows * kMaxG];
     __shared__ float rsum;
     __shared__ int lim_s[kMaxRows];
+    __shared__ uint32_t amx[kMaxRows];                         // max|att| bits per row (decode chain)
     __shared__ __align__(8) uint64_t tbar;                     // the cache tiles' bulk copies landed
 
     // every CTA of the cluster must have started before any remote store into its
@@ -388,6 +389,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
     }
     cl.sync();                                                 // every CTA holds the partials of its slice
     {
+        if (tid < kMaxRows) amx[tid] = 0u;
+        if (p.amax_out != nullptr) __syncthreads();
         const int lo = rank * seg, hi = min(MG * hd, lo + seg);
         for (int i = lo + tid; i < hi; i += kAttnThreads) {
             const int r = i / hd, c = i % hd;
@@ -406,6 +409,11 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
                 out = fmul(fmul(o, rq), p.a_v);
             }
             att_p[((size_t)m * H + h) * hd + c] = out;
+            if (p.amax_out != nullptr) atomicMax(&amx[m], __float_as_uint(fabsf(out)));
+        }
+        if (p.amax_out != nullptr) {                           // max|att| per row for the o-projection
+            __syncthreads();
+            if (tid < M && amx[tid] != 0u) atomicMax(p.amax_out + tid, amx[tid]);
         }
     }
     if (!tiles_ok) mbar_wait(&tbar, 0u);                      // no copy may land after the CTA exits
@@ -703,6 +711,7 @@ __global__ void __launch_bounds__(kSbThreads, 1)
             if (lane == 0) mbar_arrive(&empty[s]);
         }
         float* att = p.att + (size_t)slot * q_dim;
+        uint32_t am = 0u;
 #pragma unroll
         for (int j = 0; j < kMaxPairs; ++j) {
             const int pr = tid + j * kSbWarps * 32;
@@ -713,6 +722,12 @@ __global__ void __launch_bounds__(kSbThreads, 1)
             if (p.variant == 0) out = fmul(o, p.a_v);
             else out = fmul(fmul(o, fmul(sfu_recip(i2f(lsum[r])), 127.f)), p.a_v);   // sum <= 127 T: exact
             att[(size_t)(kvh * G + r) * hd + c] = out;
+            am = max(am, __float_as_uint(fabsf(out)));
+        }
+        if (p.amax_out != nullptr) {                           // max|att| of the slot's row (decode chain)
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) am = max(am, __shfl_xor_sync(0xffffffffu, am, o));
+            if (lane == 0 && am != 0u) atomicMax(p.amax_out + slot, am);
         }
     }
     __syncthreads();

@@ -133,6 +133,39 @@ int w8a8_linear_fused(const float* x, const float* norm_g, float eps, int rows, 
     return cuda_status(launch_linear(p, pro, epi, S(stream)));
 }
 
+int w8a8_linear_chain(const float* x, const float* norm_g, float eps, const uint32_t* x_amax, int rows, int k,
+                      const int8_t* w, const float* s_w, int n, const float* resid, float* y, uint32_t* clear,
+                      int clear_n, void* stream) {
+    int st = check_linear(rows, k, w, s_w, n, y);
+    if (st) return st;
+    if (!x || (norm_g && (x_amax || resid)) || clear_n < 0 || clear_n > 256 || (clear_n > 0 && !clear))
+        return W8A8_EINVAL;
+    if (!al16(x) || (norm_g && !al16(norm_g))) return W8A8_EALIGN;
+    LinearParams p{};
+    p.m = rows, p.n = n, p.k = k, p.x = x, p.norm_g = norm_g, p.eps = eps, p.inv_k = inv_of(k);
+    p.w = w, p.s_w = s_w, p.y = y, p.resid = resid;
+    p.amax_in = x_amax, p.clear = clear, p.clear_n = clear ? clear_n : 0;
+    const int pro = norm_g ? PRO_RMSQ : PRO_QUANT, epi = resid ? EPI_RESID : EPI_STORE;
+    if (!gemv_fits(p, pro, epi)) return W8A8_EINVAL;                // the chain form is the decode GEMV's
+    return cuda_status(launch_gemv(p, pro, epi, S(stream)));
+}
+
+int w8a8_ffn_swiglu_chain(const float* x, const float* norm_g, float eps, int rows, int k, const int8_t* w_gate,
+                          const float* s_gate, const int8_t* w_up, const float* s_up, int hidden, float* h,
+                          uint32_t* h_amax, uint32_t* clear, int clear_n, void* stream) {
+    int st = check_linear(rows, k, w_gate, s_gate, hidden, h);
+    if (st) return st;
+    if (!x || !norm_g || !w_up || !s_up || !h_amax || clear_n < 0 || clear_n > 256 || (clear_n > 0 && !clear))
+        return W8A8_EINVAL;
+    if (!al16(x) || !al16(norm_g) || !al16(w_up)) return W8A8_EALIGN;
+    LinearParams p{};
+    p.m = rows, p.n = hidden, p.k = k, p.x = x, p.norm_g = norm_g, p.eps = eps, p.inv_k = inv_of(k);
+    p.w = w_gate, p.s_w = s_gate, p.w2 = w_up, p.s_w2 = s_up, p.y = h;
+    p.amax_out = h_amax, p.clear = clear, p.clear_n = clear ? clear_n : 0;
+    if (!gemv_fits(p, PRO_RMSQ, EPI_SWIGLU)) return W8A8_EINVAL;
+    return cuda_status(launch_gemv(p, PRO_RMSQ, EPI_SWIGLU, S(stream)));
+}
+
 size_t w8a8_ffn_scratch_bytes(int rows) { return 256 + 4 * (size_t)(rows > 0 ? rows : 0); }
 
 int w8a8_ffn_swiglu(const float* x, const float* norm_g, float eps, int rows, int k, const int8_t* w_gate,
@@ -278,7 +311,7 @@ static int attn_params(const W8A8AttnArgs* a, AttnParams* out) {
     p.pos = a->pos, p.qkv = a->qkv, p.q_norm = a->q_norm, p.k_norm = a->k_norm, p.eps = a->eps;
     p.inv_hd = inv_of(a->head_dim), p.cos = a->rope_cos, p.sin = a->rope_sin;
     p.inv_sk = a->inv_sk, p.inv_sv = a->inv_sv, p.a_k = a->a_k, p.a_v = a->a_v;
-    p.kc = a->k_cache, p.vc = a->v_cache, p.att = a->att;
+    p.kc = a->k_cache, p.vc = a->v_cache, p.att = a->att, p.amax_out = a->att_amax;
     *out = p;
     return W8A8_OK;
 }

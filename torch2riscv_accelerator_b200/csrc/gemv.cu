@@ -106,6 +106,8 @@ __device__ __forceinline__ void gemv_prologue(const LinearParams& p, int pro, in
             continue;
         }
         const float4* xr = reinterpret_cast<const float4*>(p.x + (size_t)m * k);
+        const bool posted = pro == PRO_QUANT && p.amax_in != nullptr;
+        const uint32_t pa = posted ? __ldcg(p.amax_in + m) : 0u;          // in flight with the x loads
 #pragma unroll 4
         for (int c = tid; c < k / 4; c += nt) xf4[c] = __ldcg(xr + c);      // loads batched: 1-3 per thread
         __syncthreads();
@@ -118,10 +120,10 @@ __device__ __forceinline__ void gemv_prologue(const LinearParams& p, int pro, in
             __syncthreads();
             r = bc[0];
         }
-        // y = (x * r) * g in place, and the row amax
+        // y = (x * r) * g in place, and the row amax (unless the producer posted it)
         float a = 0.f;
 #pragma unroll 4
-        for (int c = tid; c < k / 4; c += nt) {
+        for (int c = posted ? k / 4 : tid; c < k / 4; c += nt) {
             float4 v = xf4[c];
             if (pro == PRO_RMSQ) {
                 const float4 g = g4[c];
@@ -131,7 +133,8 @@ __device__ __forceinline__ void gemv_prologue(const LinearParams& p, int pro, in
             }
             a = nanmax(a, nanmax(nanmax(fabsf(v.x), fabsf(v.y)), nanmax(fabsf(v.z), fabsf(v.w))));
         }
-        a = block_nanmax(a, red);
+        if (posted) a = __uint_as_float(pa);
+        else a = block_nanmax(a, red);
         const float s = fmul(a, W8A8_C127);
         const float inv = sfu_recip(s);
 #pragma unroll 4
@@ -296,6 +299,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(LinearParams p, G
     }
     pdl_wait();
     pdl_trigger();
+    if (p.clear != nullptr && blockIdx.x == 0 && tid < p.clear_n) p.clear[tid] = 0u;   // its readers are done
     if (epi == EPI_RESID) {                                    // residual rows: written by earlier kernels
 #pragma unroll 4
         for (int j = tid; j < my * tr * MR; j += kGemvThreads) {
@@ -404,6 +408,9 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(LinearParams p, G
     }
     if (epi == EPI_STORE && p.argmax_key != nullptr) {
         if (tid < p.m && tid < MR) atomicMax(p.argmax_key + tid, bkey[tid]);
+    }
+    if (epi == EPI_SWIGLU && p.amax_out != nullptr) {         // max|h| for the next kernel's prologue
+        if (tid < p.m && tid < MR && bamax[tid] != 0u) atomicMax(p.amax_out + tid, bamax[tid]);
     }
     if (epi != EPI_SWIGLU || p.hq == nullptr) return;
     // the row amax across the grid; the last CTA requantizes h (quant_act)

@@ -30,6 +30,14 @@ struct LinearParams {
     uint32_t* amax_bits;      // [m] scratch, zero between launches (EPI_SWIGLU)
     uint32_t* counter;        // [1] scratch, zero between launches (EPI_SWIGLU)
     unsigned long long* argmax_key;   // [m] greedy keys (EPI_STORE, optional; zero before the launch)
+    // decode chain (optional): the producer of x posted max|x| per row by atomic
+    // max (PRO_QUANT reads it instead of reducing); a SwiGLU posts max|h| per
+    // row; `clear` (clear_n words) is zeroed after the wait (a slot whose readers
+    // have all finished)
+    const uint32_t* amax_in;
+    uint32_t* amax_out;
+    uint32_t* clear;
+    int clear_n;
 };
 
 cudaError_t launch_linear(const LinearParams& p, int pro, int epi, cudaStream_t st);
@@ -58,6 +66,7 @@ struct AttnParams {
     int chunk;                // cache positions per CTA
     int slots;                // batched decode: sequences (one row each; grid z), or 0
     size_t slot_stride;       // bytes between consecutive slots' caches (batched decode)
+    uint32_t* amax_out;       // [rows or slots] max|att| per row by atomic max, or null (decode chain)
 };
 
 // Tensor-core GEMM (gemm.cu): int8 operands row-major [rows][k], K-major.

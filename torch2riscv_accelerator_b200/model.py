@@ -30,6 +30,7 @@ from .weights import kv_consts
 I8, F32, I32 = torch.int8, torch.float32, torch.int32
 CHUNK = 16                                         # rows of the GEMV / attention path (the reference's M)
 PREFILL = 256                                      # rows per tensor-core prefill chunk
+CHAIN_ROWS = 4                                     # rows of the decode GEMV path (the latency chain)
 
 
 def _upload(obj, cfg, qw, kv_scales):
@@ -66,6 +67,10 @@ class DeviceDecoder:
         # int8 rows and scales between the row quantizer and the tensor-core GEMMs
         self.xq_buf = z(R * max(cfg.dim, cfg.q_dim, cfg.hidden), dt=I8)
         self.sx_buf = z(R)
+        # decode chain: max|att| and max|h| per layer and row (int32 words holding
+        # float bits; zero between uses)
+        self.amax_att = z(cfg.layers, CHAIN_ROWS, dt=I32)
+        self.amax_h = z(cfg.layers, CHAIN_ROWS, dt=I32)
         self.next_token = z(R, dt=I32)
         self.key = z(R, dt=torch.int64)                # packed greedy argmax per row (classifier epilogue)
         self.attn_scratch = ops.attn_scratch(R, cfg.heads, cfg.kv_heads, hd, T, self.dev)
@@ -79,14 +84,14 @@ class DeviceDecoder:
         self.graphs = {}
 
     # ------------------------------------------------------------ the program
-    def _attn_args(self, rows):
-        a = self._args.get(rows)
+    def _attn_args(self, rows, chain=False):
+        a = self._args.get((rows, chain))
         if a is None:
             c = self.cfg
-            a = self._args[rows] = [
+            a = self._args[(rows, chain)] = [
                 ops.attn_args(c, rows, self.pos, self.qkv, self.kc[l], self.vc[l], self.att, self.consts[l],
                               self.cos, self.sin, self.attn_scratch, self.layers[l].get("q_norm"),
-                              self.layers[l].get("k_norm"))
+                              self.layers[l].get("k_norm"), att_amax=self.amax_att[l] if chain else None)
                 for l in range(c.layers)]
         return a
 
@@ -100,6 +105,8 @@ class DeviceDecoder:
         c = self.cfg
         x, qkv, att = self.x[:rows], self.qkv[:rows], self.att[:rows]
         h, hq, s_h = self.h[:rows], self.hq[:rows], self.s_h[:rows]
+        if rows <= CHAIN_ROWS and not c.moe:
+            return self._run_chain(rows, logits_rows, argmax)
         args = self._attn_args(rows)
         ops.embed(self.tokens[:rows], self.emb_q, self.emb_s, out=x)
         for l, w in enumerate(self.layers):
@@ -114,6 +121,28 @@ class DeviceDecoder:
             ops.ffn_swiglu(x, w["rms_ffn"], c.eps, w["w1"], w["s_w1"], w["w3"], w["s_w3"], None, h=h,
                            requant=False)
             ops.linear_fused(h, w["w2"], w["s_w2"], resid=x, out=x)          # quant_act(h) in the prologue
+        xl = self.x[rows - logits_rows:rows]
+        ops.classifier(xl, self.cls_q, self.cls_s, self.rms_final, c.eps, out=self.logits[:logits_rows],
+                       argmax_key=self.key[:logits_rows] if argmax else None)
+
+    def _run_chain(self, rows, logits_rows, argmax):
+        """Decode rows (<= 4, the GEMV path) as the latency chain: the attention
+        and the SwiGLU post max|att| / max|h| per row by atomic max into
+        per-layer slots, the o and down projections read them instead of
+        reducing (the same bits), and each slot is zeroed by the kernel two
+        launches later, once its reader has finished."""
+        c, L = self.cfg, self.cfg.layers
+        x, qkv, att, h = self.x[:rows], self.qkv[:rows], self.att[:rows], self.h[:rows]
+        args = self._attn_args(rows, chain=True)
+        ops.embed(self.tokens[:rows], self.emb_q, self.emb_s, out=x)
+        for l, w in enumerate(self.layers):
+            ops.linear_chain(x, w["wqkv"], w["s_wqkv"], norm_g=w["rms_att"], eps=c.eps, out=qkv,
+                             clear=self.amax_h[(l - 1) % L])               # the previous layer's h slot
+            ops.attn(args[l])
+            ops.linear_chain(att, w["wo"], w["s_wo"], x_amax=self.amax_att[l], resid=x, out=x)
+            ops.ffn_swiglu_chain(x, w["rms_ffn"], c.eps, w["w1"], w["s_w1"], w["w3"], w["s_w3"], h,
+                                 self.amax_h[l], clear=self.amax_att[l])
+            ops.linear_chain(h, w["w2"], w["s_w2"], x_amax=self.amax_h[l], resid=x, out=x)
         xl = self.x[rows - logits_rows:rows]
         ops.classifier(xl, self.cls_q, self.cls_s, self.rms_final, c.eps, out=self.logits[:logits_rows],
                        argmax_key=self.key[:logits_rows] if argmax else None)

@@ -94,6 +94,28 @@ def linear_fused(x, w, s_w, norm_g=None, eps=0.0, resid=None, out=None, s_x_out=
     return out
 
 
+def linear_chain(x, w, s_w, norm_g=None, eps=0.0, x_amax=None, resid=None, out=None, clear=None):
+    """The decode chain's fused linear: quant_act(x) with max|x| posted by the
+    producer (x_amax), or rmsnorm + quant_act; `clear` zeroed after the wait."""
+    _need(x, F32, "x")
+    m, k = x.shape
+    n = w.shape[0]
+    out = torch.empty(m, n, dtype=F32, device=x.device) if out is None else out
+    _lib.check("w8a8_linear_chain", _lib.load().w8a8_linear_chain(
+        _p(x), _p(norm_g), float(eps), _p(x_amax), m, k, _p(w), _p(s_w), n, _p(resid), _p(out), _p(clear),
+        0 if clear is None else clear.numel(), _st()))
+    return out
+
+
+def ffn_swiglu_chain(x, norm_g, eps, w_gate, s_gate, w_up, s_up, h, h_amax, clear=None):
+    """The decode chain's SwiGLU: h and max|h| per row posted into h_amax."""
+    m, k = x.shape
+    _lib.check("w8a8_ffn_swiglu_chain", _lib.load().w8a8_ffn_swiglu_chain(
+        _p(x), _p(norm_g), float(eps), m, k, _p(w_gate), _p(s_gate), _p(w_up), _p(s_up), w_gate.shape[0], _p(h),
+        _p(h_amax), _p(clear), 0 if clear is None else clear.numel(), _st()))
+    return h
+
+
 def ffn_scratch(rows, device):
     n = _lib.load().w8a8_ffn_scratch_bytes(rows)
     return torch.zeros(n, dtype=torch.uint8, device=device)
@@ -182,7 +204,7 @@ def attn_scratch(rows, heads, kv_heads, head_dim, seq_len, device):
 VARIANTS = {"norm": 0, "qsum": 1}
 
 
-def attn_args(cfg, rows, pos, qkv, kc, vc, att, consts, cos, sin, scratch, q_norm=None, k_norm=None):
+def attn_args(cfg, rows, pos, qkv, kc, vc, att, consts, cos, sin, scratch, q_norm=None, k_norm=None, att_amax=None):
     """The W8A8AttnArgs block of one layer (kept alive by the caller: a CUDA
     graph replays the pointers it captured)."""
     inv_sk, inv_sv, a_k, a_v = consts
@@ -191,7 +213,7 @@ def attn_args(cfg, rows, pos, qkv, kc, vc, att, consts, cos, sin, scratch, q_nor
         variant=VARIANTS[cfg.attn], pos=_p(pos), qkv=_p(qkv), q_norm=_p(q_norm), k_norm=_p(k_norm),
         eps=float(np.float32(cfg.eps)), rope_cos=_p(cos), rope_sin=_p(sin), inv_sk=float(inv_sk),
         inv_sv=float(inv_sv), a_k=float(a_k), a_v=float(a_v), k_cache=_p(kc), v_cache=_p(vc), att=_p(att),
-        scratch=_p(scratch), scratch_bytes=scratch.numel())
+        scratch=_p(scratch), scratch_bytes=scratch.numel(), att_amax=_p(att_amax))
 
 
 def attn(args):
