@@ -33,7 +33,7 @@ extern "C" {
 #define W8A8_ECUDA 3    /* the CUDA launch failed (cudaGetLastError) */
 #define W8A8_ESCRATCH 4 /* the scratch buffer is smaller than required */
 
-#define W8A8_ABI_VERSION 2
+#define W8A8_ABI_VERSION 3
 #define W8A8_MAX_ROWS 16 /* query rows per call (decode: 1, prefill chunk: 16) */
 
 /* ABI version (W8A8_ABI_VERSION) and a message for a status code. */
@@ -64,7 +64,8 @@ int w8a8_embed(const int32_t* tokens, int rows, const int8_t* emb_q, const float
  * token reached w8a8_embed; bit 1: a GEMV weight-tile wait gave up after its
  * bounded spin and the kernel stopped early; bit 2: an attention cache-tile
  * copy did not land within its bounded wait; bit 3: the same for an MoE weight
- * tile; bit 4: a tensor-core GEMM pipeline wait). Synchronous with the device.
+ * tile; bit 4: a tensor-core GEMM pipeline wait; bit 5: a tensor-parallel
+ * exchange wait gave up). Synchronous with the device.
  * Plays the role of the overlay's sticky list status (llm/sa_funcsim.py:62-66,
  * firmware/rt/rt_fw.c:53-60). */
 int w8a8_error_flags(uint32_t* flags);
@@ -264,6 +265,113 @@ int w8a8_classifier(const float* x, const float* norm_g, float eps, int rows, in
  * (llm/runtime.py:127-148) feeding greedy tokens back. */
 int w8a8_decode_advance(int32_t* tokens, int32_t* pos, uint64_t* argmax_key, int32_t* next_token, int rows,
                         void* stream);
+
+/* ------------------------------------------------------------------------
+ * Tensor parallelism over the GPUs of one node (one process per GPU). The
+ * reference runs on one device; these entry points have no counterpart there.
+ * Its layer program is split as: q|k|v rows, gate and up rows and the
+ * classifier's vocabulary rows by rank (column split), o and down by their
+ * input columns (row split). The split stays exact: a row-split linear's int32
+ * partials are summed exactly across ranks, and quant_act's max|x| of a
+ * column-split activation is the maximum over ranks.
+ *
+ * Decode rows (at most W8A8_TP_ROWS) exchange over NVLink inside the kernels:
+ * each rank owns an exchange region (w8a8_tp_alloc) mapped into every other
+ * rank's process (w8a8_ipc_handle / w8a8_ipc_open). Values travel as 8-byte
+ * words, the step epoch in the high half and the value in the low half; a
+ * receiving kernel polls its own region until the words of this step arrived
+ * (bounded: after ~0.2 s it gives up, reads zeros and sets error bit 5). The
+ * region's first 4 bytes hold this rank's step epoch, advanced by
+ * w8a8_tp_embed; exchange blocks start at W8A8_TP_HEADER bytes, 16-byte
+ * aligned, and every rank lays them out identically. Every rank must run the
+ * same sequence of calls, and each step must end with a dependency between
+ * ranks (the greedy key exchange of w8a8_tp_advance, or a collective of the
+ * caller's) before the next step's calls. Ranks must be on distinct GPUs. */
+#define W8A8_TP_MAX_RANKS 8
+#define W8A8_TP_ROWS 4
+#define W8A8_TP_CTAS 512
+#define W8A8_TP_HEADER 256
+/* Exchange block sizes in 8-byte words for `ranks` ranks: the partials of a
+ * row-split linear with n outputs; per-CTA row maxima; per-CTA greedy keys. */
+#define W8A8_TP_PART_WORDS(ranks, n) ((size_t)(ranks) * W8A8_TP_ROWS * (size_t)(n))
+#define W8A8_TP_AMAX_WORDS(ranks) ((size_t)(ranks) * (1 + W8A8_TP_CTAS) * W8A8_TP_ROWS)
+#define W8A8_TP_KEY_WORDS(ranks) (2 * W8A8_TP_AMAX_WORDS(ranks))
+
+typedef struct {
+    int rank, ranks;                          /* 2 <= ranks <= W8A8_TP_MAX_RANKS */
+    size_t bytes;                             /* region size (the same on every rank) */
+    void* base[W8A8_TP_MAX_RANKS];            /* every rank's region as mapped in this process */
+} W8A8TpComm;
+
+/* The region: device memory of `bytes` (zeroed); its IPC handle (64 bytes);
+ * another rank's region opened in this process (peer access over NVLink). */
+int w8a8_tp_alloc(size_t bytes, void** region);
+int w8a8_tp_free(void* region);
+int w8a8_ipc_handle(const void* region, uint8_t handle[64]);
+int w8a8_ipc_open(const uint8_t handle[64], void** region);
+int w8a8_ipc_close(void* region);
+
+/* w8a8_embed, and the step epoch advanced (the first call of a step). */
+int w8a8_tp_embed(const W8A8TpComm* comm, const int32_t* tokens, int rows, const int8_t* emb_q, const float* emb_s,
+                  int vocab, int dim, float* x, void* stream);
+
+#define W8A8_TP_STORE 0   /* y = dequant (the classifier: + greedy keys to every rank) */
+#define W8A8_TP_PARTIAL 1 /* the int32 accumulators to every rank (row-split o / down) */
+#define W8A8_TP_SWIGLU 2  /* y = h of this rank's hidden rows; max|h| to every rank */
+
+/* One decode GEMV of a rank's shard (rows <= W8A8_TP_ROWS). Prologue: when
+ * part_in is set, x = resid + (f32(sum over ranks of part_in) * part_s_w) *
+ * part_s_x, stored to x_out (the preceding row-split linear, finished here);
+ * else x is read. Then [rmsnorm ->] quant_act, whose max|x| is amax_in's
+ * maximum over every rank when set (a column-split activation). Blocks are
+ * addresses in this rank's region. */
+typedef struct {
+    const W8A8TpComm* comm;
+    int rows, k, n;
+    const float* x;              /* [rows, k] (without part_in) */
+    const uint64_t* part_in;     /* partials block of the preceding row-split linear, or NULL */
+    const float* part_s_w;       /* [k] its weight scales */
+    const float* part_s_x;       /* [rows] its activation scales (its s_x_out) */
+    const float* resid;          /* [rows, k] the residual stream before it */
+    float* x_out;                /* [rows, k] after it (may not alias resid) */
+    const float* norm_g;         /* [k] RMSNorm gain, or NULL */
+    float eps;
+    const uint64_t* amax_in;     /* per-CTA max|x| block (quant_act without norm), or NULL */
+    const int8_t* w;             /* [n, k] this rank's rows */
+    const float* s_w;            /* [n] */
+    const int8_t* w_up;          /* [n, k] SwiGLU up rows */
+    const float* s_up;
+    int epilogue;                /* W8A8_TP_STORE / _PARTIAL / _SWIGLU */
+    float* y;                    /* STORE, SWIGLU: [rows, n] */
+    uint64_t* part_out;          /* PARTIAL: partials block (n outputs) */
+    uint64_t* amax_out;          /* SWIGLU: per-CTA max|h| block */
+    uint64_t* key_out;           /* STORE: per-CTA key block, or NULL */
+    int n_offset;                /* global index of output 0 (this rank's vocabulary slice) */
+    float* s_x_out;              /* [rows] the prologue's scales, or NULL */
+} W8A8TpLinearArgs;
+int w8a8_tp_linear(const W8A8TpLinearArgs* a, void* stream);
+
+/* w8a8_attn over this rank's heads (args: heads / kv_heads of the shard),
+ * posting max|att| per row to every rank's amax_out block. */
+int w8a8_tp_attn(const W8A8AttnArgs* a, const W8A8TpComm* comm, uint64_t* amax_out, void* stream);
+
+/* w8a8_decode_advance over the key block: the greedy token of the last step
+ * (the maximum key over every rank's classifier CTAs). */
+int w8a8_tp_advance(const W8A8TpComm* comm, const uint64_t* keys, int32_t* tokens, int32_t* pos,
+                    int32_t* next_token, int rows, void* stream);
+/* Seed the key block (this rank's own) so that the next w8a8_tp_advance reads
+ * `token`. */
+int w8a8_tp_seed(const W8A8TpComm* comm, uint64_t* keys, int32_t token, void* stream);
+
+/* Tensor-parallel rows beyond decode, with the caller's collectives between:
+ * max|x| per row as float bits (all-reduce MAX as int32 across ranks), then
+ * quant_act with that maximum; the linear epilogue on all-reduced int32
+ * accumulators: y = [resid +] (f32(acc) * s_w) * s_x. */
+int w8a8_row_amax(const float* x, int rows, int k, uint32_t* amax_bits, void* stream);
+int w8a8_quant_rows_posted(const float* x, const uint32_t* amax_bits, int rows, int k, int8_t* xq, float* s_x,
+                           void* stream);
+int w8a8_dequant_resid(const int32_t* acc, const float* s_x, const float* s_w, int rows, int n, const float* resid,
+                       float* y, void* stream);
 
 #ifdef __cplusplus
 }

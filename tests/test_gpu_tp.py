@@ -1,0 +1,96 @@
+"""Tensor parallelism on 2+ GPUs (one process per GPU, NCCL): every rank's
+logits and greedy tokens equal the one-GPU decoder's (itself bit-exact with the
+reference) bit for bit, through the prefill GEMM path (NCCL collectives), the
+decode rows' in-kernel NVLink exchange, and the captured on-device greedy loop.
+Skipped with fewer than 2 GPUs (ranks must be on distinct GPUs)."""
+import datetime
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from torch2riscv_accelerator_b200 import config as C
+from torch2riscv_accelerator_b200 import weights as W
+
+pytestmark = pytest.mark.gpu
+PREFILL, CHUNK2, FWD, STEPS = 40, 10, 5, 6
+
+
+CFG = C.C2.with_(layers=2, vocab=4096)
+
+
+def _model(kv=None):
+    """The test model: the quantized weights are elementwise functions of the
+    seed (identical in every process); the KV scales come from one fp32
+    calibration run (BLAS sums), made once in the parent and handed to the ranks."""
+    if kv is None:
+        qw = W.QuantWeights(CFG, seed=7, gains="random", calib_tokens=np.arange(8))
+        kv = qw.kv_scales
+    else:
+        qw = W.QuantWeights(CFG, seed=7, gains="random")
+    toks = np.random.default_rng(3).integers(0, CFG.vocab, PREFILL + CHUNK2 + FWD)
+    return CFG, qw, np.asarray(kv, np.float32), toks
+
+
+def _run(dev, toks):
+    """prefill (a 40-row and a 10-row chunk), FWD single-token forwards, then
+    STEPS replays of the captured greedy step: logits and tokens of each."""
+    out = {"p1": dev.prefill(toks[:PREFILL]), "p2": dev.prefill(toks[PREFILL:PREFILL + CHUNK2])}
+    out["fwd"] = np.stack([dev.forward(int(t)) for t in toks[PREFILL + CHUNK2:]])
+    dec = dev.dec
+    g = dec.capture_decode_step(int(np.argmax(out["fwd"][-1])), dev.pos - 1)
+    tok, lg = [], []
+    for _ in range(STEPS):
+        g.replay()
+        tok.append(int(dec.next_token[0].item()))
+        full = dec.gather_logits(1)[0] if hasattr(dec, "gather_logits") else dec.logits[0]
+        lg.append(full.cpu().numpy())
+    out["loop_tok"], out["loop_lg"] = np.array(tok), np.stack(lg)
+    return out
+
+
+def _worker(rank, ranks, port, path, kv):
+    from torch2riscv_accelerator_b200 import ops
+    from torch2riscv_accelerator_b200.tp import TpLlamaDevice
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=ranks,
+                            timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", rank))
+    dev = None
+    try:
+        cfg, qw, kv, toks = _model(kv)
+        dev = TpLlamaDevice((cfg, qw, kv))
+        out = _run(dev, toks)
+        torch.cuda.synchronize()
+        out["flags"] = np.array(ops.error_flags())
+        np.savez(f"{path}.{rank}.npz", **out)
+    finally:
+        if dev is not None:
+            dev.close()
+        dist.destroy_process_group()
+
+
+def _port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("ranks", [2, 4, 8])
+def test_tp_equals_one_gpu(ranks, tmp_path):
+    if torch.cuda.device_count() < ranks:
+        pytest.skip(f"needs {ranks} GPUs")
+    from torch2riscv_accelerator_b200.runtime import LlamaDevice
+    path = str(tmp_path / "tp")
+    cfg, qw, kv, toks = _model()
+    mp.spawn(_worker, args=(ranks, _port(), path, kv), nprocs=ranks, join=True)
+    ref = _run(LlamaDevice((cfg, qw, kv)), toks)
+    for r in range(ranks):
+        got = np.load(f"{path}.{r}.npz")
+        assert int(got["flags"]) == 0, (r, int(got["flags"]))
+        for k in ("p1", "p2", "fwd", "loop_tok", "loop_lg"):
+            assert got[k].tobytes() == ref[k].tobytes(), (r, k)

@@ -10,7 +10,9 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libw8a8_b200.so")
 
 W8A8_OK, W8A8_EINVAL, W8A8_EALIGN, W8A8_ECUDA, W8A8_ESCRATCH = 0, 1, 2, 3, 4
-ABI_VERSION = 2
+ABI_VERSION = 3
+TP_MAX_RANKS, TP_ROWS, TP_CTAS, TP_HEADER = 8, 4, 512, 256
+TP_STORE, TP_PARTIAL, TP_SWIGLU = 0, 1, 2
 
 
 class W8A8AttnArgs(C.Structure):
@@ -20,6 +22,32 @@ class W8A8AttnArgs(C.Structure):
                 ("rope_sin", C.c_void_p), ("inv_sk", C.c_float), ("inv_sv", C.c_float), ("a_k", C.c_float),
                 ("a_v", C.c_float), ("k_cache", C.c_void_p), ("v_cache", C.c_void_p), ("att", C.c_void_p),
                 ("scratch", C.c_void_p), ("scratch_bytes", C.c_size_t), ("att_amax", C.c_void_p)]
+
+
+class W8A8TpComm(C.Structure):
+    _fields_ = [("rank", C.c_int), ("ranks", C.c_int), ("bytes", C.c_size_t),
+                ("base", C.c_void_p * TP_MAX_RANKS)]
+
+
+class W8A8TpLinearArgs(C.Structure):
+    _fields_ = [("comm", C.POINTER(W8A8TpComm)), ("rows", C.c_int), ("k", C.c_int), ("n", C.c_int),
+                ("x", C.c_void_p), ("part_in", C.c_void_p), ("part_s_w", C.c_void_p), ("part_s_x", C.c_void_p),
+                ("resid", C.c_void_p), ("x_out", C.c_void_p), ("norm_g", C.c_void_p), ("eps", C.c_float),
+                ("amax_in", C.c_void_p), ("w", C.c_void_p), ("s_w", C.c_void_p), ("w_up", C.c_void_p),
+                ("s_up", C.c_void_p), ("epilogue", C.c_int), ("y", C.c_void_p), ("part_out", C.c_void_p),
+                ("amax_out", C.c_void_p), ("key_out", C.c_void_p), ("n_offset", C.c_int), ("s_x_out", C.c_void_p)]
+
+
+def tp_part_words(ranks, n):
+    return ranks * TP_ROWS * n
+
+
+def tp_amax_words(ranks):
+    return ranks * (1 + TP_CTAS) * TP_ROWS
+
+
+def tp_key_words(ranks):
+    return 2 * tp_amax_words(ranks)
 
 
 P, I, F, Z, L = C.c_void_p, C.c_int, C.c_float, C.c_size_t, C.c_int64
@@ -50,6 +78,19 @@ PROTOTYPES = {
     "w8a8_argmax": (I, [P, I, I, P, P]),
     "w8a8_classifier": (I, [P, P, F, I, I, P, P, I, P, P, P]),
     "w8a8_decode_advance": (I, [P, P, P, P, I, P]),
+    "w8a8_tp_alloc": (I, [Z, C.POINTER(P)]),
+    "w8a8_tp_free": (I, [P]),
+    "w8a8_ipc_handle": (I, [P, C.POINTER(C.c_uint8)]),
+    "w8a8_ipc_open": (I, [C.POINTER(C.c_uint8), C.POINTER(P)]),
+    "w8a8_ipc_close": (I, [P]),
+    "w8a8_tp_embed": (I, [C.POINTER(W8A8TpComm), P, I, P, P, I, I, P, P]),
+    "w8a8_tp_linear": (I, [C.POINTER(W8A8TpLinearArgs), P]),
+    "w8a8_tp_attn": (I, [C.POINTER(W8A8AttnArgs), C.POINTER(W8A8TpComm), P, P]),
+    "w8a8_tp_advance": (I, [C.POINTER(W8A8TpComm), P, P, P, P, I, P]),
+    "w8a8_tp_seed": (I, [C.POINTER(W8A8TpComm), P, C.c_int32, P]),
+    "w8a8_row_amax": (I, [P, I, I, P, P]),
+    "w8a8_quant_rows_posted": (I, [P, P, I, I, P, P, P]),
+    "w8a8_dequant_resid": (I, [P, P, P, I, I, P, P, P]),
 }
 
 _LIB = None

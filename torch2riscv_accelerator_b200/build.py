@@ -13,7 +13,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libw8a8_b200.so")
 SOURCES = ["capi.cu", "linear.cu", "gemv.cu", "attn.cu", "misc.cu", "moe.cu", "gemm.cu"]
-HEADERS = ["w8a8_math.cuh", "w8a8_internal.h", "sfu_tables.h", "pdl.cuh", "linear_common.cuh", os.path.join("..", "..", "include", "w8a8.h")]
+HEADERS = ["w8a8_math.cuh", "w8a8_internal.h", "sfu_tables.h", "pdl.cuh", "tp.cuh", "linear_common.cuh", os.path.join("..", "..", "include", "w8a8.h")]
 NVCC_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17", "-fmad=false",
               "-ftz=false", "-prec-div=true", "-prec-sqrt=true", "-Xcompiler", "-fPIC", "-shared",
               "--expt-relaxed-constexpr"]

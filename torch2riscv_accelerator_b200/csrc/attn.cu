@@ -31,6 +31,7 @@
 // positions contiguous, so p.V is a dot product over positions).
 #include <cooperative_groups.h>
 
+#include "tp.cuh"
 #include "pdl.cuh"
 #include "w8a8_internal.h"
 #include "w8a8_math.cuh"
@@ -389,8 +390,9 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
     }
     cl.sync();                                                 // every CTA holds the partials of its slice
     {
+        const bool post = p.amax_out != nullptr || p.amax_ll_out != nullptr;
         if (tid < kMaxRows) amx[tid] = 0u;
-        if (p.amax_out != nullptr) __syncthreads();
+        if (post) __syncthreads();
         const int lo = rank * seg, hi = min(MG * hd, lo + seg);
         for (int i = lo + tid; i < hi; i += kAttnThreads) {
             const int r = i / hd, c = i % hd;
@@ -409,11 +411,16 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
                 out = fmul(fmul(o, rq), p.a_v);
             }
             att_p[((size_t)m * H + h) * hd + c] = out;
-            if (p.amax_out != nullptr) atomicMax(&amx[m], __float_as_uint(fabsf(out)));
+            if (post) atomicMax(&amx[m], __float_as_uint(fabsf(out)));
         }
+        if (post) __syncthreads();
         if (p.amax_out != nullptr) {                           // max|att| per row for the o-projection
-            __syncthreads();
             if (tid < M && amx[tid] != 0u) atomicMax(p.amax_out + tid, amx[tid]);
+        }
+        if (p.amax_ll_out != nullptr && tid < kTpRows) {       // tensor parallel: to every rank
+            const uint32_t ep = tp_epoch(p.tp);
+            ll_post_cta(p.tp, p.amax_ll_out, kvh * (int)gridDim.y + rank, (int)(gridDim.x * gridDim.y), tid,
+                        tid < M ? amx[tid] : 0u, ep);
         }
     }
     if (!tiles_ok) mbar_wait(&tbar, 0u);                      // no copy may land after the CTA exits

@@ -1,6 +1,7 @@
 // The extern "C" entry points of include/w8a8.h: argument checks, then the
 // launches of the kernels in linear.cu, attn.cu and misc.cu.
 #include <cstdint>
+#include <cstring>
 #include <mutex>
 
 #include "../../include/w8a8.h"
@@ -357,6 +358,172 @@ int w8a8_decode_advance(int32_t* tokens, int32_t* pos, uint64_t* argmax_key, int
     if (!tokens || !pos || !argmax_key || rows <= 0 || rows > 32) return W8A8_EINVAL;
     return cuda_status(launch_decode_advance(tokens, pos, reinterpret_cast<unsigned long long*>(argmax_key),
                                              next_token, rows, S(stream)));
+}
+
+// ---------------------------------------------------------------- tensor parallel
+static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+static_assert(W8A8_TP_MAX_RANKS == kTpMaxRanks && W8A8_TP_ROWS == kTpRows && W8A8_TP_CTAS == kTpCtas,
+              "exchange layout");
+
+static int tp_ctx(const W8A8TpComm* c, TpCtx* t) {
+    if (!c || c->ranks < 2 || c->ranks > W8A8_TP_MAX_RANKS || c->rank < 0 || c->rank >= c->ranks ||
+        c->bytes < W8A8_TP_HEADER)
+        return W8A8_EINVAL;
+    *t = TpCtx{};
+    t->rank = c->rank, t->ranks = c->ranks;
+    for (int r = 0; r < c->ranks; ++r) {
+        if (!c->base[r]) return W8A8_EINVAL;
+        if (!al16(c->base[r])) return W8A8_EALIGN;
+        t->base[r] = static_cast<char*>(c->base[r]);
+    }
+    t->self = t->base[c->rank];
+    return W8A8_OK;
+}
+
+// a block of `words` 8-byte words inside this rank's region, past the header
+static bool tp_block(const W8A8TpComm* c, const void* p, size_t words) {
+    if (!p || !al16(p)) return false;
+    const char* b = static_cast<const char*>(c->base[c->rank]);
+    const char* q = static_cast<const char*>(p);
+    return q >= b + W8A8_TP_HEADER && (size_t)(q - b) + words * 8 <= c->bytes;
+}
+
+int w8a8_tp_alloc(size_t bytes, void** region) {
+    if (!region || bytes < W8A8_TP_HEADER) return W8A8_EINVAL;
+    void* p = nullptr;
+    if (cudaMalloc(&p, bytes) != cudaSuccess) return W8A8_ECUDA;
+    if (cudaMemset(p, 0, bytes) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) {
+        cudaFree(p);
+        return W8A8_ECUDA;
+    }
+    *region = p;
+    return W8A8_OK;
+}
+
+int w8a8_tp_free(void* region) { return region ? cuda_status(cudaFree(region)) : W8A8_EINVAL; }
+
+int w8a8_ipc_handle(const void* region, uint8_t handle[64]) {
+    if (!region || !handle) return W8A8_EINVAL;
+    cudaIpcMemHandle_t h;
+    if (cudaIpcGetMemHandle(&h, const_cast<void*>(region)) != cudaSuccess) return W8A8_ECUDA;
+    memcpy(handle, &h, sizeof(h));
+    return W8A8_OK;
+}
+
+int w8a8_ipc_open(const uint8_t handle[64], void** region) {
+    if (!handle || !region) return W8A8_EINVAL;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof(h));
+    return cuda_status(cudaIpcOpenMemHandle(region, h, cudaIpcMemLazyEnablePeerAccess));
+}
+
+int w8a8_ipc_close(void* region) { return region ? cuda_status(cudaIpcCloseMemHandle(region)) : W8A8_EINVAL; }
+
+int w8a8_tp_embed(const W8A8TpComm* comm, const int32_t* tokens, int rows, const int8_t* emb_q, const float* emb_s,
+                  int vocab, int dim, float* x, void* stream) {
+    TpCtx t;
+    int st = tp_ctx(comm, &t);
+    if (st) return st;
+    if (!tokens || !emb_q || !emb_s || !x || rows <= 0 || vocab <= 0 || dim <= 0) return W8A8_EINVAL;
+    return cuda_status(launch_embed(tokens, rows, emb_q, emb_s, vocab, dim, x, S(stream),
+                                    reinterpret_cast<uint32_t*>(t.self)));
+}
+
+int w8a8_tp_linear(const W8A8TpLinearArgs* a, void* stream) {
+    if (!a) return W8A8_EINVAL;
+    TpCtx t;
+    int st = tp_ctx(a->comm, &t);
+    if (st) return st;
+    const W8A8TpComm* c = a->comm;
+    const int epi = a->epilogue == W8A8_TP_STORE ? EPI_STORE
+                    : a->epilogue == W8A8_TP_PARTIAL ? EPI_PARTIAL
+                    : a->epilogue == W8A8_TP_SWIGLU ? EPI_SWIGLU : -1;
+    if (epi < 0 || a->rows <= 0 || a->rows > W8A8_TP_ROWS) return W8A8_EINVAL;
+    st = check_linear(a->rows, a->k, a->w, a->s_w, a->n, epi == EPI_PARTIAL ? (const void*)a->part_out : a->y);
+    if (st) return st;
+    LinearParams p{};
+    p.m = a->rows, p.n = a->n, p.k = a->k, p.x = a->x, p.norm_g = a->norm_g, p.eps = a->eps;
+    p.inv_k = inv_of(a->k), p.w = a->w, p.s_w = a->s_w, p.s_x_out = a->s_x_out, p.tp = t;
+    if (a->part_in) {
+        if (!tp_block(c, a->part_in, W8A8_TP_PART_WORDS(c->ranks, a->k)) || !a->part_s_w || !a->part_s_x ||
+            !a->resid || !a->x_out || a->x_out == a->resid)
+            return W8A8_EINVAL;
+        if (!al16(a->resid) || !al16(a->x_out) || !al16(a->part_s_w)) return W8A8_EALIGN;
+        p.part_in = a->part_in, p.part_sw = a->part_s_w, p.part_sx = a->part_s_x;
+        p.part_resid = a->resid, p.x_out = a->x_out;
+    } else {
+        if (!a->x) return W8A8_EINVAL;
+        if (!al16(a->x)) return W8A8_EALIGN;
+    }
+    if (a->norm_g && !al16(a->norm_g)) return W8A8_EALIGN;
+    if (a->amax_in) {
+        if (a->norm_g || !tp_block(c, a->amax_in, W8A8_TP_AMAX_WORDS(c->ranks))) return W8A8_EINVAL;
+        p.amax_ll = a->amax_in;
+    }
+    const int pro = a->norm_g ? PRO_RMSQ : PRO_QUANT;
+    if (epi == EPI_STORE) {
+        if (a->key_out && !tp_block(c, a->key_out, W8A8_TP_KEY_WORDS(c->ranks))) return W8A8_EINVAL;
+        if (a->n_offset < 0) return W8A8_EINVAL;
+        p.y = a->y, p.key_out = a->key_out, p.n_offset = a->n_offset;
+    } else if (epi == EPI_PARTIAL) {
+        if (!tp_block(c, a->part_out, W8A8_TP_PART_WORDS(c->ranks, a->n))) return W8A8_EINVAL;
+        p.part_out = a->part_out;
+    } else {
+        if (!a->w_up || !a->s_up || !tp_block(c, a->amax_out, W8A8_TP_AMAX_WORDS(c->ranks))) return W8A8_EINVAL;
+        if (!al16(a->w_up)) return W8A8_EALIGN;
+        p.w2 = a->w_up, p.s_w2 = a->s_up, p.y = a->y, p.amax_ll_out = a->amax_out;
+    }
+    if (!gemv_fits(p, pro, epi) || gemv_grid(p, pro, epi) > kTpCtas) return W8A8_EINVAL;
+    return cuda_status(launch_gemv(p, pro, epi, S(stream)));
+}
+
+int w8a8_tp_attn(const W8A8AttnArgs* a, const W8A8TpComm* comm, uint64_t* amax_out, void* stream) {
+    TpCtx t;
+    int st = tp_ctx(comm, &t);
+    if (st) return st;
+    AttnParams p{};
+    st = attn_params(a, &p);
+    if (st) return st;
+    if (a->rows > W8A8_TP_ROWS || !tp_block(comm, amax_out, W8A8_TP_AMAX_WORDS(comm->ranks))) return W8A8_EINVAL;
+    if ((size_t)a->kv_heads * kMaxCluster > (size_t)kTpCtas) return W8A8_EINVAL;
+    p.tp = t, p.amax_ll_out = amax_out;
+    return cuda_status(launch_attn(p, S(stream)));
+}
+
+int w8a8_tp_advance(const W8A8TpComm* comm, const uint64_t* keys, int32_t* tokens, int32_t* pos,
+                    int32_t* next_token, int rows, void* stream) {
+    TpCtx t;
+    int st = tp_ctx(comm, &t);
+    if (st) return st;
+    if (!tokens || !pos || rows <= 0 || rows > W8A8_TP_ROWS || !tp_block(comm, keys, W8A8_TP_KEY_WORDS(comm->ranks)))
+        return W8A8_EINVAL;
+    return cuda_status(launch_tp_advance(t, keys, tokens, pos, next_token, rows, S(stream)));
+}
+
+int w8a8_tp_seed(const W8A8TpComm* comm, uint64_t* keys, int32_t token, void* stream) {
+    TpCtx t;
+    int st = tp_ctx(comm, &t);
+    if (st) return st;
+    if (token < 0 || !tp_block(comm, keys, W8A8_TP_KEY_WORDS(comm->ranks))) return W8A8_EINVAL;
+    return cuda_status(launch_tp_seed(t, keys, token, S(stream)));
+}
+
+int w8a8_row_amax(const float* x, int rows, int k, uint32_t* amax_bits, void* stream) {
+    if (!x || !amax_bits || rows <= 0 || rows > 65535 || k <= 0) return W8A8_EINVAL;
+    return cuda_status(launch_row_amax(x, rows, k, amax_bits, S(stream)));
+}
+
+int w8a8_quant_rows_posted(const float* x, const uint32_t* amax_bits, int rows, int k, int8_t* xq, float* s_x,
+                           void* stream) {
+    if (!x || !amax_bits || !xq || !s_x || rows <= 0 || rows > 65535 || k <= 0) return W8A8_EINVAL;
+    if (k % 4 || !al16(x) || (reinterpret_cast<uintptr_t>(xq) & 3u)) return W8A8_EALIGN;
+    return cuda_status(launch_quant_posted(x, amax_bits, rows, k, xq, s_x, S(stream)));
+}
+
+int w8a8_dequant_resid(const int32_t* acc, const float* s_x, const float* s_w, int rows, int n, const float* resid,
+                       float* y, void* stream) {
+    if (!acc || !s_x || !s_w || !y || rows <= 0 || rows > 65535 || n <= 0) return W8A8_EINVAL;
+    return cuda_status(launch_dequant_resid(acc, s_x, s_w, rows, n, resid, y, S(stream)));
 }
 
 }  // extern "C"

@@ -26,10 +26,11 @@
 // llm/compile_model.py:295-328 (ffn_up with fused SiLU).
 #include "linear_common.cuh"
 #include "pdl.cuh"
+#include "tp.cuh"
 
 namespace w8a8 {
 
-__device__ unsigned int g_gemv_errors;                        // bit 1: a tile wait gave up
+__device__ unsigned int g_gemv_errors;    // bit 1: a tile wait gave up; bit 5: a tensor-parallel exchange wait
 
 constexpr int kMaxStages = 8;
 constexpr size_t kRingBytes = 96 * 1024;                      // weight ring per CTA
@@ -80,7 +81,8 @@ __device__ __forceinline__ float sumsq16(const float* xf, int k, int lane) {
 // in shared memory. Every thread of the block takes part.
 template <int MR>
 __device__ __forceinline__ void gemv_prologue(const LinearParams& p, int pro, int8_t* xs, float* xf, float* sx,
-                                              const float* gs, float* red, float* bc) {
+                                              const float* gs, float* red, float* bc, uint32_t ep, bool& ok,
+                                              uint32_t* cnt) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, k = p.k, nt = (int)blockDim.x;
     if (pro == PRO_I8) {
 #pragma unroll 1
@@ -106,10 +108,33 @@ __device__ __forceinline__ void gemv_prologue(const LinearParams& p, int pro, in
             continue;
         }
         const float4* xr = reinterpret_cast<const float4*>(p.x + (size_t)m * k);
-        const bool posted = pro == PRO_QUANT && p.amax_in != nullptr;
-        const uint32_t pa = posted ? __ldcg(p.amax_in + m) : 0u;          // in flight with the x loads
+        const bool posted = pro == PRO_QUANT && (p.amax_in != nullptr || p.amax_ll != nullptr);
+        uint32_t pa = pro == PRO_QUANT && p.amax_in != nullptr ? __ldcg(p.amax_in + m) : 0u;   // with the x loads
+        if (p.part_in != nullptr) {
+            // tensor parallel: the row-split linear before this one left its int32
+            // partials at every rank; x = resid + (f32(sum) * s_w) * s_x (its
+            // epilogue, with the exact sum), kept by CTA 0 as the residual stream
+            const float sxp = __ldcg(p.part_sx + m);
+            float2* xf2 = reinterpret_cast<float2*>(xf);
+            const float2* rr = reinterpret_cast<const float2*>(p.part_resid + (size_t)m * k);
+            const float2* pw = reinterpret_cast<const float2*>(p.part_sw);
+            float2* xo = reinterpret_cast<float2*>(p.x_out + (size_t)m * k);
+#pragma unroll 1
+            for (int c = tid; c < k / 2; c += nt) {
+                const float2 r = __ldcg(rr + c), w = __ldg(pw + c);
+                int s0, s1;
+                ll_sum_pair(p.tp, p.part_in, m, k, 2 * c, ep, ok, s0, s1);
+                const float2 v = make_float2(fadd(r.x, fmul(fmul(i2f(s0), w.x), sxp)),
+                                             fadd(r.y, fmul(fmul(i2f(s1), w.y), sxp)));
+                xf2[c] = v;
+                if (blockIdx.x == 0) xo[c] = v;
+            }
+        } else {
 #pragma unroll 4
-        for (int c = tid; c < k / 4; c += nt) xf4[c] = __ldcg(xr + c);      // loads batched: 1-3 per thread
+            for (int c = tid; c < k / 4; c += nt) xf4[c] = __ldcg(xr + c);  // loads batched: 1-3 per thread
+        }
+        if (pro == PRO_QUANT && p.amax_ll != nullptr)              // every rank's max|x| (its producer CTAs)
+            pa = ll_block_max(p.tp, p.amax_ll, m, ep, ok, cnt, reinterpret_cast<uint32_t*>(red));
         __syncthreads();
         float r = 1.f;
         if (pro == PRO_RMSQ) {
@@ -251,6 +276,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(LinearParams p, G
     __shared__ uint32_t bamax[MR];
     __shared__ unsigned long long bkey[MR];
     __shared__ int last, failed;
+    __shared__ uint32_t llcnt[kTpMaxRanks + 1];
     __shared__ uint32_t silu_tab[256];                         // EXP / RECIP tables (SwiGLU epilogue)
     if (tid < MR) {
         bamax[tid] = 0u;
@@ -308,7 +334,10 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(LinearParams p, G
             if (n < p.n && m < p.m) rs[m * nj + jj] = __ldcg(p.resid + (size_t)m * p.n + n);
         }
     }
-    gemv_prologue<MR>(p, pro, xs, xf, sx, gs, red, bc);        // ends with a block barrier
+    const uint32_t ep = p.tp.ranks > 1 ? tp_epoch(p.tp) : 0u;  // this step's exchange words
+    bool ok = true;
+    gemv_prologue<MR>(p, pro, xs, xf, sx, gs, red, bc, ep, ok, llcnt);   // ends with a block barrier
+    if (!ok) atomicOr(&g_gemv_errors, 32u);
 
     if (producer) {
         if (lane == 0) {                                       // refill each stage once its consumers are done
@@ -374,12 +403,17 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(LinearParams p, G
                     if (epi == EPI_STORE) {
                         p.y[o] = v;
                         if (p.acc != nullptr) p.acc[o] = acc[m];
-                        if (p.argmax_key != nullptr) {
-                            const unsigned long long key = argmax_key(v, n);
+                        if (p.argmax_key != nullptr || p.key_out != nullptr) {
+                            const unsigned long long key = argmax_key(v, n + p.n_offset);
                             tkey[m] = key > tkey[m] ? key : tkey[m];
                         }
                     } else if (epi == EPI_RESID) {
                         p.y[o] = fadd(rs[m * nj + j], v);
+                    } else if (epi == EPI_PARTIAL) {           // the int32 sum to every rank
+                        const size_t w = (size_t)(p.tp.rank * kTpRows + m) * p.n + n;
+#pragma unroll
+                        for (int q = 0; q < kTpMaxRanks; ++q)
+                            if (q < p.tp.ranks) ll_store(tp_at(p.tp, p.part_out, q) + w, (uint32_t)acc[m], ep);
                     } else {
                         const float u = fmul(fmul(i2f(acc2[m]), sw2[j]), sx[m]);
                         const float h = silu_gate_tab(v, u, silu_tab);
@@ -411,6 +445,13 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(LinearParams p, G
     }
     if (epi == EPI_SWIGLU && p.amax_out != nullptr) {         // max|h| for the next kernel's prologue
         if (tid < p.m && tid < MR && bamax[tid] != 0u) atomicMax(p.amax_out + tid, bamax[tid]);
+    }
+    if (p.tp.ranks > 1 && tid < kTpRows) {                     // this CTA's row maxima / keys to every rank
+        const int m = tid;
+        if (epi == EPI_SWIGLU && p.amax_ll_out != nullptr)
+            ll_post_cta(p.tp, p.amax_ll_out, blockIdx.x, gridDim.x, m, m < p.m && m < MR ? bamax[m] : 0u, ep);
+        if (epi == EPI_STORE && p.key_out != nullptr)
+            ll_post_key(p.tp, p.key_out, blockIdx.x, gridDim.x, m, m < p.m && m < MR ? bkey[m] : 0ull, ep);
     }
     if (epi != EPI_SWIGLU || p.hq == nullptr) return;
     // the row amax across the grid; the last CTA requantizes h (quant_act)
@@ -493,6 +534,11 @@ static cudaError_t launch_g(const LinearParams& p, int pro, int epi, cudaStream_
     return launch_k(kern, dim3(t.grid), dim3(kGemvThreads), t.smem, st, p, t.cf);
 }
 
+int gemv_grid(const LinearParams& p, int pro, int epi) {
+    const int mr = p.m <= 1 ? 1 : (p.m <= 2 ? 2 : 4);
+    return tiling(p, mr, pro, epi).grid;
+}
+
 bool gemv_fits(const LinearParams& p, int pro, int epi) {
     if (p.m > 4) return false;
     const int mr = p.m <= 1 ? 1 : (p.m <= 2 ? 2 : 4);
@@ -500,7 +546,7 @@ bool gemv_fits(const LinearParams& p, int pro, int epi) {
 }
 
 cudaError_t launch_gemv(const LinearParams& p, int pro, int epi, cudaStream_t st) {
-    if (pro < PRO_I8 || pro > PRO_RMSQ || epi < EPI_STORE || epi > EPI_SWIGLU) return cudaErrorInvalidValue;
+    if (pro < PRO_I8 || pro > PRO_RMSQ || epi < EPI_STORE || epi > EPI_PARTIAL) return cudaErrorInvalidValue;
     if (pro == PRO_I8 && epi == EPI_SWIGLU) return cudaErrorInvalidValue;
     if (p.m <= 1) return launch_g<1>(p, pro, epi, st);
     if (p.m <= 2) return launch_g<2>(p, pro, epi, st);

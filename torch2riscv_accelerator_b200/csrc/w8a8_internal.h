@@ -8,7 +8,22 @@
 namespace w8a8 {
 
 enum Prologue { PRO_I8 = 0, PRO_QUANT = 1, PRO_RMSQ = 2 };
-enum Epilogue { EPI_STORE = 0, EPI_RESID = 1, EPI_SWIGLU = 2 };
+enum Epilogue { EPI_STORE = 0, EPI_RESID = 1, EPI_SWIGLU = 2, EPI_PARTIAL = 3 };
+
+// Tensor-parallel decode: every rank owns an exchange region of the same
+// layout, mapped into every other rank's process (CUDA IPC over NVLink). A
+// kernel addresses a block of another rank's region by the block's offset in
+// its own. Exchanged values travel as 8-byte words, the step epoch in the high
+// half and the value in the low half: one store carries both, so a reader
+// polls the word until it holds this step's epoch (no fence, no flag).
+constexpr int kTpMaxRanks = 8;
+constexpr int kTpRows = 4;                // rows of a tensor-parallel decode call
+constexpr int kTpCtas = 512;              // producer CTAs an exchange block holds
+struct TpCtx {
+    int rank, ranks;                      // ranks <= 1: no exchange
+    char* self;                           // this rank's region (= base[rank])
+    char* base[kTpMaxRanks];              // every rank's region (indexed by unrolled loops only)
+};
 
 struct LinearParams {
     int m, n, k;              // rows (tokens), outputs, inputs
@@ -38,10 +53,23 @@ struct LinearParams {
     uint32_t* amax_out;
     uint32_t* clear;
     int clear_n;
+    // tensor-parallel decode (tp.ranks > 1); blocks are addresses in this rank's region
+    TpCtx tp;
+    const uint64_t* part_in;  // [ranks][kTpRows][k]: the previous row-split linear's int32 partials;
+    const float* part_sw;     //   the prologue forms x = part_resid + (f32(sum) * part_sw) * part_sx
+    const float* part_sx;     //   ([k], [m]) and CTA 0 stores it to x_out
+    const float* part_resid;  // [m, k]
+    float* x_out;             // [m, k]
+    const uint64_t* amax_ll;  // PRO_QUANT: max|x| words of every rank's producer CTAs
+    uint64_t* part_out;       // EPI_PARTIAL: int32 accumulators to every rank
+    uint64_t* amax_ll_out;    // EPI_SWIGLU: max|h| of this CTA to every rank
+    uint64_t* key_out;        // EPI_STORE: the greedy key of this CTA to every rank
+    int n_offset;             // global index of output 0 (a vocabulary slice)
 };
 
 cudaError_t launch_linear(const LinearParams& p, int pro, int epi, cudaStream_t st);
 bool gemv_fits(const LinearParams& p, int pro, int epi);
+int gemv_grid(const LinearParams& p, int pro, int epi);   // CTAs of the decode GEMV launch
 cudaError_t launch_gemv(const LinearParams& p, int pro, int epi, cudaStream_t st);
 unsigned int gemv_read_clear_errors();
 unsigned int attn_read_clear_errors();
@@ -67,6 +95,8 @@ struct AttnParams {
     int slots;                // batched decode: sequences (one row each; grid z), or 0
     size_t slot_stride;       // bytes between consecutive slots' caches (batched decode)
     uint32_t* amax_out;       // [rows or slots] max|att| per row by atomic max, or null (decode chain)
+    TpCtx tp;                 // tensor-parallel decode: max|att| words of this CTA to every rank
+    uint64_t* amax_ll_out;
 };
 
 // Tensor-core GEMM (gemm.cu): int8 operands row-major [rows][k], K-major.
@@ -136,7 +166,15 @@ size_t attn_stream_smem(int heads, int kv_heads, int head_dim, int seq_len);
 cudaError_t launch_attn_stream(const AttnParams& p, cudaStream_t st);
 
 cudaError_t launch_embed(const int32_t* tokens, int m, const int8_t* emb_q, const float* emb_s, int vocab, int dim,
-                         float* x, cudaStream_t st);
+                         float* x, cudaStream_t st, uint32_t* epoch = nullptr);
+cudaError_t launch_tp_advance(const TpCtx& tp, const uint64_t* keys, int32_t* tokens, int32_t* pos, int32_t* next,
+                              int rows, cudaStream_t st);
+cudaError_t launch_tp_seed(const TpCtx& tp, uint64_t* keys, int32_t token, cudaStream_t st);
+cudaError_t launch_row_amax(const float* x, int m, int k, uint32_t* amax, cudaStream_t st);
+cudaError_t launch_quant_posted(const float* x, const uint32_t* amax, int m, int k, int8_t* xq, float* s_x,
+                                cudaStream_t st);
+cudaError_t launch_dequant_resid(const int32_t* acc, const float* s_x, const float* s_w, int m, int n,
+                                 const float* resid, float* y, cudaStream_t st);
 cudaError_t read_clear_errors(unsigned int* out);
 cudaError_t launch_argmax(const float* logits, int m, int n, int32_t* out, cudaStream_t st);
 cudaError_t launch_sfu(int func, const float* x, float* y, long long n, cudaStream_t st);

@@ -6,6 +6,8 @@ ModelCompiler: embed, attention, ffn_up; `llm/runtime.py` Sampler). Every call
 runs on the current torch CUDA stream and raises W8A8Error on a nonzero status.
 Tensors are passed as raw device pointers; torch only owns the memory.
 """
+import ctypes
+
 import numpy as np
 import torch
 
@@ -64,7 +66,6 @@ def embed(tokens, emb_q, emb_s, out=None):
 
 def error_flags():
     """Read and clear the device error flags (bit 0: an out-of-range token)."""
-    import ctypes
     v = ctypes.c_uint32(0)
     _lib.check("w8a8_error_flags", _lib.load().w8a8_error_flags(ctypes.byref(v)))
     return v.value
@@ -254,3 +255,54 @@ def key_token(key):
 def decode_advance(tokens, pos, argmax_key, rows, next_token=None):
     _lib.check("w8a8_decode_advance", _lib.load().w8a8_decode_advance(
         _p(tokens), _p(pos), _p(argmax_key), _p(next_token), rows, _st()))
+
+
+# ------------------------------------------------------------- tensor parallel
+def tp_embed(comm, tokens, emb_q, emb_s, out):
+    """w8a8_embed that also starts a tensor-parallel step (advances the epoch)."""
+    m, (vocab, dim) = tokens.numel(), emb_q.shape
+    _lib.check("w8a8_tp_embed", _lib.load().w8a8_tp_embed(ctypes.byref(comm), _p(tokens), m, _p(emb_q), _p(emb_s),
+                                                         vocab, dim, _p(out), _st()))
+    return out
+
+
+def tp_linear(args):
+    """One decode GEMV of a rank's shard (a prepared W8A8TpLinearArgs)."""
+    _lib.check("w8a8_tp_linear", _lib.load().w8a8_tp_linear(ctypes.byref(args), _st()))
+
+
+def tp_attn(args, comm, amax_out):
+    _lib.check("w8a8_tp_attn", _lib.load().w8a8_tp_attn(ctypes.byref(args), ctypes.byref(comm), amax_out, _st()))
+
+
+def tp_advance(comm, keys, tokens, pos, rows, next_token=None):
+    _lib.check("w8a8_tp_advance", _lib.load().w8a8_tp_advance(ctypes.byref(comm), keys, _p(tokens), _p(pos),
+                                                             _p(next_token), rows, _st()))
+
+
+def tp_seed(comm, keys, token):
+    _lib.check("w8a8_tp_seed", _lib.load().w8a8_tp_seed(ctypes.byref(comm), keys, int(token), _st()))
+
+
+def row_amax(x, out):
+    """max|x| per row as float bits (int32 tensor [rows])."""
+    m, k = x.shape
+    _lib.check("w8a8_row_amax", _lib.load().w8a8_row_amax(_p(x), m, k, _p(out), _st()))
+    return out
+
+
+def quant_rows_posted(x, amax, xq, s_x):
+    """quant_act of x rows with the given max|x| bits."""
+    m, k = x.shape
+    _lib.check("w8a8_quant_rows_posted", _lib.load().w8a8_quant_rows_posted(_p(x), _p(amax), m, k, _p(xq), _p(s_x),
+                                                                           _st()))
+    return xq, s_x
+
+
+def dequant_resid(acc, s_x, s_w, out, resid=None):
+    """out = [resid +] (f32(acc) * s_w) * s_x over int32 rows acc [rows, n]."""
+    m, n = acc.shape
+    _lib.check("w8a8_dequant_resid", _lib.load().w8a8_dequant_resid(_p(acc), _p(s_x), _p(s_w), m, n, _p(resid),
+                                                                   _p(out), _st()))
+    return out
+

@@ -96,6 +96,10 @@ class LlamaDevice:
         buf[R:R + m] = torch.as_tensor(positions, dtype=torch.int32)
         self.dec.tokens[:m].copy_(buf[:m], non_blocking=True)
         self.dec.pos[:m].copy_(buf[R:R + m], non_blocking=True)
+        self._launch(m, logits)
+
+    def _launch(self, m, logits):
+        """Run m staged rows; with logits, the last row's logits into self._out."""
         self.dec.launch(m, 1, graph=self.graphs)
         if logits:
             self._out.copy_(self.dec.logits[0], non_blocking=True)
