@@ -21,8 +21,12 @@ cpu_baseline  the CPU oracle (NumPy restatement of the reference's device
 
 --impl reference times the reference's CPU path (the oracle port: the reference
 is Python and does not travel) on the same config and metric; rank 0 only.
-Multi-GPU: one process per GPU, independent replicas ("scaling": "weak"); the
-batch-1 path has no exchange step in this build.
+Multi-GPU (one process per GPU): tensor parallelism by default ("scaling":
+"strong", one sequence over all GPUs; `--parallel tp`): each rank holds a shard
+of every layer, the decode kernels exchange row maxima, int32 partial sums and
+greedy keys over NVLink inside the kernels, e2e gathers the logits with NCCL.
+`--parallel replicas` (or a config whose heads do not split) runs independent
+batch-1 replicas instead ("scaling": "weak").
 """
 import argparse
 import json
@@ -284,8 +288,16 @@ def run_batch(args, cfg, qw, ws, rank, local):
     barrier(ws)
 
 
-def config_of(cfg, args, ws):
+def config_of(cfg, args, ws, tp=False):
     P = cfg.seq_len - args.warmup - args.steps
+    if tp:
+        return {"workload": f"{cfg.name}-shape W8A8 decode, batch 1, T=2048, tensor parallel over {ws} GPUs: "
+                            f"{P}-token prompt prefilled in chunks of up to 256 rows, then {args.warmup} untimed + "
+                            f"{args.steps} timed greedy decode steps",
+                "model": cfg.name, "global_batch": 1, "seq_len": cfg.seq_len, "prompt": P,
+                "parallelism": f"tp{ws}", "attention": cfg.attn,
+                "l2": "no flush: each rank's step streams its shard of the weights and KV cache (over the L2 "
+                      "size at every rank count)"}
     return {"workload": f"{cfg.name}-shape W8A8 decode, batch 1 per GPU, T=2048: {P}-token prompt prefilled in "
                         f"16-row chunks, then {args.warmup} untimed + {args.steps} timed greedy decode steps",
             "model": cfg.name, "global_batch": ws, "seq_len": cfg.seq_len, "prompt": P,
@@ -306,6 +318,8 @@ def main():
     ap.add_argument("--pdl", type=int, default=1, help="programmatic dependent launch between kernels (1) or not (0)")
     ap.add_argument("--batch", type=int, default=1,
                     help="sequences per step (BatchLlamaDevice); > 1 measures batched decode instead")
+    ap.add_argument("--parallel", default="tp", choices=["tp", "replicas"],
+                    help="with several GPUs: one sequence tensor-parallel (tp) or independent replicas")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
@@ -331,8 +345,22 @@ def main():
     if args.batch > 1:
         run_batch(args, cfg, qw, ws, rank, local)
         return
-    dec = DeviceDecoder(cfg, qw, qw.kv_scales)
-    dev = LlamaDevice(dec)
+    tp = ws > 1 and args.parallel == "tp"
+    if tp:
+        from torch2riscv_accelerator_b200.tp import TpLlamaDevice, check_split
+        try:
+            check_split(cfg, ws)
+        except ValueError as e:
+            if rank == 0:
+                print(f"# {e}: independent replicas instead", file=sys.stderr)
+            tp = False
+    if tp:
+        dev = TpLlamaDevice((cfg, qw, qw.kv_scales))
+        dec = dev.dec
+    else:
+        dec = DeviceDecoder(cfg, qw, qw.kv_scales)
+        dev = LlamaDevice(dec)
+    seqs = 1 if tp else ws                               # sequences decoded per step over all GPUs
     P = cfg.seq_len - args.warmup - args.steps
     prompt = np.random.default_rng(args.seed + 3).integers(0, cfg.vocab, P)
     torch.cuda.synchronize()
@@ -364,7 +392,7 @@ def main():
         torch.cuda.synchronize()
     barrier(ws)
     dt = max_over_ranks(e0.elapsed_time(e1) / 1e3, ws)
-    value = ws * args.steps / dt
+    value = seqs * args.steps / dt
     final_pos = int(dec.pos[0].item())
     if ops.error_flags():
         raise RuntimeError("device error flags set during the decode steps")
@@ -402,7 +430,7 @@ def main():
     torch.cuda.nvtx.range_pop()
     torch.cuda.synchronize()
     t_gemv = r0.elapsed_time(r1) / 1e3 / n_rep
-    N, K = cfg.vocab, cfg.dim
+    N, K = dec.cls_q.shape                              # (this rank's vocabulary slice under tp)
     gemv_bytes = N * K + 4 * N + K + 4 * N
     achieved = gemv_bytes / t_gemv / 1e9
     step_bytes = dec.weight_bytes() + dec.kv_bytes(cfg.seq_len - 8)
@@ -424,14 +452,15 @@ def main():
         line = {
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": ws, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": 1e3 * dt / args.steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": value / FPGA_TOKS, "dtype": "int8",
+            "scaling": "strong" if tp else "weak", "vs_baseline": value / FPGA_TOKS, "dtype": "int8",
             "data": "synthetic (N(0,0.02) weights seed 0, uniform prompt ids)",
-            "config": config_of(cfg, args, ws),
-            "e2e": {"value": ws * args.steps / dt_e2e, "unit": "tok/s", "h2d_bytes_per_step": 8,
+            "config": config_of(cfg, args, ws, tp),
+            "e2e": {"value": seqs * args.steps / dt_e2e, "unit": "tok/s", "h2d_bytes_per_step": 8,
                     "d2h_bytes_per_step": 4 * cfg.vocab},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": NCU_TRAFFIC["bytes"],
-                         "traffic_source": NCU_TRAFFIC["source"], "peak_source": peak_src,
+                         "frac": achieved / peak, "traffic": None if tp else NCU_TRAFFIC["bytes"],
+                         "traffic_source": "not captured for a vocabulary slice" if tp else NCU_TRAFFIC["source"],
+                         "peak_source": peak_src,
                          "kernel": f"gemv_kernel (classifier GEMV {N}x{K}, rmsnorm+quant prologue, fused argmax)",
                          "bytes_per_launch": gemv_bytes, "us_per_launch": t_gemv * 1e6},
             "step_roofline": {"bytes_per_step": step_bytes, "achieved_gbs": step_bytes / (dt / args.steps) / 1e9,
@@ -448,6 +477,8 @@ def main():
         import torch.distributed as dist
         del g
         dec.graphs.clear()
+        if tp:
+            dev.close()
         dist.destroy_process_group()
 
 
