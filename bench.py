@@ -222,7 +222,17 @@ def run_batch(args, cfg, qw, ws, rank, local):
     from torch2riscv_accelerator_b200.model import BatchDecoder
     from torch2riscv_accelerator_b200.runtime import BatchLlamaDevice
     D = args.batch
-    dec = BatchDecoder(cfg, qw, qw.kv_scales, slots=D)
+    tp = ws > 1 and args.parallel == "tp"
+    if tp:
+        from torch2riscv_accelerator_b200.tp import TpBatchDecoder, TpBatchLlamaDevice, check_split
+        try:
+            check_split(cfg, ws)
+        except ValueError as e:
+            if rank == 0:
+                print(f"# {e}: independent replicas instead", file=sys.stderr)
+            tp = False
+    dec = TpBatchDecoder(cfg, qw, qw.kv_scales, slots=D) if tp else BatchDecoder(cfg, qw, qw.kv_scales, slots=D)
+    seqs = D if tp else ws * D                         # sequences per step over all GPUs
     g = torch.Generator(device=dec.dev).manual_seed(args.seed + 11)
     for t in (dec.kc, dec.vc):
         t.copy_(torch.randint(-127, 128, t.shape, dtype=torch.int8, device=dec.dev, generator=g))
@@ -230,10 +240,12 @@ def run_batch(args, cfg, qw, ws, rank, local):
     rng = np.random.default_rng(args.seed + 3)
     dec.tokens.copy_(torch.as_tensor(rng.integers(0, cfg.vocab, D), dtype=torch.int32))
     dec.pos.fill_(P)
-    graph = dec.capture()                          # (its warm-up step writes the rows of position P)
+    # one step: the captured graph (the tensor-parallel step holds NCCL
+    # collectives and runs eagerly)
+    run = dec.step if tp else dec.capture().replay   # (a capture's warm-up step writes the rows of position P)
     st = torch.cuda.current_stream()
     for _ in range(args.warmup):
-        graph.replay()
+        run()
         dec.pos.add_(1)
     barrier(ws)
     torch.cuda.synchronize()
@@ -242,7 +254,7 @@ def run_batch(args, cfg, qw, ws, rank, local):
         torch.cuda.nvtx.range_push("batch")               # ncu --nvtx-include batch/ selects these launches
         e0.record(st)
         for _ in range(args.steps):
-            graph.replay()
+            run()
             dec.pos.add_(1)
         e1.record(st)
         torch.cuda.nvtx.range_pop()
@@ -250,7 +262,7 @@ def run_batch(args, cfg, qw, ws, rank, local):
     barrier(ws)
     dt = max_over_ranks(e0.elapsed_time(e1) / 1e3, ws)
     # e2e: host tokens / positions in, [D, vocab] logits out, per step
-    dev = BatchLlamaDevice(dec)
+    dev = TpBatchLlamaDevice(dec) if tp else BatchLlamaDevice(dec)
     toks = rng.integers(0, cfg.vocab, (args.warmup + args.steps, D))
     for i in range(args.warmup):
         dev.step([P + i] * D, [int(v) for v in toks[i]])
@@ -267,16 +279,16 @@ def run_batch(args, cfg, qw, ws, rank, local):
     if rank == 0:
         kv_step = D * dec.slot_stride * 2 * (P + args.warmup + args.steps // 2) // cfg.seq_len
         line = {
-            "metric": METRIC, "value": ws * D * args.steps / dt, "unit": "tok/s", "n_gpus": ws, "steps": args.steps,
+            "metric": METRIC, "value": seqs * args.steps / dt, "unit": "tok/s", "n_gpus": ws, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": 1e3 * dt / args.steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+            "scaling": "strong" if tp else "weak", "vs_baseline": None, "dtype": "int8",
             "data": "synthetic (N(0,0.02) weights seed 0, uniform token ids, seeded random int8 caches)",
             "config": {"workload": f"{cfg.name}-shape W8A8 batched decode: {D} sequences per step, each at "
                                    f"positions {P}..{cfg.seq_len - 1} of its own T=2048 cache",
-                       "model": cfg.name, "global_batch": D * ws, "seq_len": cfg.seq_len,
-                       "parallelism": f"replicas x{ws}", "attention": cfg.attn,
+                       "model": cfg.name, "global_batch": seqs, "seq_len": cfg.seq_len,
+                       "parallelism": f"tp{ws}" if tp else f"replicas x{ws}", "attention": cfg.attn,
                        "l2": "no flush: the step reads the weights and every slot's cache, far over the 126 MB L2"},
-            "e2e": {"value": ws * D * args.steps / dt_e2e, "unit": "tok/s", "h2d_bytes_per_step": 8 * D,
+            "e2e": {"value": seqs * args.steps / dt_e2e, "unit": "tok/s", "h2d_bytes_per_step": 8 * D,
                     "d2h_bytes_per_step": 4 * D * cfg.vocab},
             "step_bytes": {"kv_read": kv_step,
                            "weights": sum(t.numel() for w in dec.layers for t in w.values()
@@ -286,6 +298,9 @@ def run_batch(args, cfg, qw, ws, rank, local):
         }
         print(json.dumps(line), flush=True)
     barrier(ws)
+    if ws > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
 
 
 def config_of(cfg, args, ws, tp=False):

@@ -206,15 +206,19 @@ class BatchLlamaDevice:
         self._in[d:] = torch.as_tensor(poses, dtype=torch.int32)
         self.dec.tokens.copy_(self._in[:d], non_blocking=True)
         self.dec.pos.copy_(self._in[d:], non_blocking=True)
+        self._out.copy_(self._run_step(), non_blocking=True)
+        torch.cuda.current_stream().synchronize()
+        self.stats.append(time.perf_counter() - t0)
+        return self._out.numpy().copy()
+
+    def _run_step(self):
+        """Run the staged step; the [D, vocab] logits tensor."""
         if self.graphs:
             g = self.dec.graph or self.dec.capture()
             g.replay()
         else:
             self.dec.step()
-        self._out.copy_(self.dec.logits, non_blocking=True)
-        torch.cuda.current_stream().synchronize()
-        self.stats.append(time.perf_counter() - t0)
-        return self._out.numpy().copy()
+        return self.dec.logits
 
     def generate(self, prompts, steps, stagger=0, temperature=0.0, topp=0.9, seed=1, on_logits=None):
         """Generate for len(prompts) <= D sequences at once (`llm/runtime.py:210-241`):

@@ -31,8 +31,8 @@ import torch
 import torch.distributed as dist
 
 from . import _lib, ops
-from .model import CHUNK, PREFILL, DeviceDecoder
-from .runtime import LlamaDevice
+from .model import CHUNK, PREFILL, BatchDecoder, DeviceDecoder
+from .runtime import BatchLlamaDevice, LlamaDevice
 
 I8, F32, I32 = torch.int8, torch.float32, torch.int32
 
@@ -243,33 +243,8 @@ class TpDecoder(DeviceDecoder):
             ops.tp_linear(down)
         ops.tp_linear(a["cls_key"] if argmax else a["cls"])
 
-    def _row_split(self, a, w, s_w, x):
-        """x += the row-split linear of a (this rank's columns): max|a| per row
-        over every rank, quant_act of the rank's columns with it, the GEMM's
-        int32 partials summed over the ranks, then the dequantization."""
-        rows, k = a.shape
-        g = self.comm.group
-        am = self.amax_bits[:rows]
-        ops.row_amax(a, am)
-        dist.all_reduce(am, op=dist.ReduceOp.MAX, group=g)
-        aq, sa = self._q(rows, k)
-        ops.quant_rows_posted(a, am, aq, sa)
-        acc = self.acc[:rows]
-        ops.gemm(aq, sa, w, s_w, out=self.ybuf[:rows], acc=acc)
-        dist.all_reduce(acc, op=dist.ReduceOp.SUM, group=g)
-        ops.dequant_resid(acc, sa, s_w, out=x, resid=x)
-
     def _run_gemm(self, rows, logits_rows):
-        # No programmatic dependent launch on this path: a kernel launched with
-        # it right after a torch.distributed collective was measured to start
-        # before the collective's result was in place (wrong rows from the
-        # first exchange on), while launched plainly every row was exact.
-        lib = _lib.load()
-        old = lib.w8a8_set_pdl(0)
-        try:
-            self._run_gemm_rows(rows, logits_rows)
-        finally:
-            lib.w8a8_set_pdl(old)
+        _no_pdl(lambda: self._run_gemm_rows(rows, logits_rows))
 
     def _run_gemm_rows(self, rows, logits_rows):
         c = self.full_cfg
@@ -281,11 +256,11 @@ class TpDecoder(DeviceDecoder):
             ops.gemm(xq, sx, w["wqkv"], w["s_wqkv"], out=self.qkv[:rows])
             for j in range(0, rows, CHUNK):
                 ops.attn(self._sub_attn_args(l, j, min(CHUNK, rows - j)))
-            self._row_split(self.att[:rows], w["wo"], w["s_wo"], x)
+            row_split(self, self.att[:rows], w["wo"], w["s_wo"], x, self.comm.group)
             xq, sx = self._q(rows, c.dim)
             ops.quant_rows(x, w["rms_ffn"], c.eps, xq=xq, s_x=sx)
             ops.gemm_swiglu(xq, sx, w["w1"], w["s_w1"], w["w3"], w["s_w3"], out=h)
-            self._row_split(h, w["w2"], w["s_w2"], x)
+            row_split(self, h, w["w2"], w["s_w2"], x, self.comm.group)
         ops.classifier(self.x[rows - logits_rows:rows], self.cls_q, self.cls_s, self.rms_final, c.eps,
                        out=self.logits[:logits_rows])
 
@@ -367,3 +342,110 @@ class TpLlamaDevice(LlamaDevice):
         self.dec.graphs.clear()
         torch.cuda.synchronize()
         self.comm.close()
+
+
+def _no_pdl(fn):
+    """Run fn with programmatic dependent launch off: kernels next to
+    torch.distributed collectives are launched plainly (with it, a kernel right
+    after a collective was measured to start before the collective's result
+    was in place)."""
+    lib = _lib.load()
+    old = lib.w8a8_set_pdl(0)
+    try:
+        return fn()
+    finally:
+        lib.w8a8_set_pdl(old)
+
+
+def row_split(dec, a, w, s_w, x, group):
+    """x += the row-split linear of a (this rank's columns of a [rows, k]):
+    max|a| per row over every rank (all-reduce MAX of the float bits), quant_act
+    of this rank's columns with it, the GEMM's int32 partials summed over the
+    ranks (all-reduce SUM, exact), then the dequantization with the residual."""
+    rows, k = a.shape
+    am = dec.amax_bits[:rows]
+    ops.row_amax(a, am)
+    dist.all_reduce(am, op=dist.ReduceOp.MAX, group=group)
+    aq, sa = dec.xq_buf[:rows * k].view(rows, k), dec.sx_buf[:rows]
+    ops.quant_rows_posted(a, am, aq, sa)
+    acc = dec.acc[:rows]
+    ops.gemm(aq, sa, w, s_w, out=dec.ybuf[:rows], acc=acc)
+    dist.all_reduce(acc, op=dist.ReduceOp.SUM, group=group)
+    ops.dequant_resid(acc, sa, s_w, out=x, resid=x)
+
+
+class TpBatchDecoder(BatchDecoder):
+    """BatchDecoder (D slots, one token each per step) over this rank's shard:
+    each rank attends its own KV heads of every slot (its part of every slot's
+    cache), the linears are the rank's GEMMs with the row-split ones completed
+    by NCCL all-reduces. self.logits: this rank's vocabulary slice [D, vocab /
+    ranks]; gather_logits() assembles [D, vocab]. Collective: every rank of the
+    group constructs it and calls step() in the same order."""
+
+    def __init__(self, cfg, qw, kv_scales, slots, group=None, device="cuda"):
+        cfg.validate()
+        self.group = group
+        self.rank, self.ranks = dist.get_rank(group), dist.get_world_size(group)
+        self.full_cfg = cfg
+        sh = shard(cfg, qw, self.rank, self.ranks)
+        super().__init__(local_config(cfg, self.ranks), sh, kv_scales, slots, device=device)
+        D = slots
+        z = lambda *s, dt=F32: torch.zeros(*s, dtype=dt, device=self.dev)
+        self.acc, self.ybuf, self.amax_bits = z(D, cfg.dim, dt=I32), z(D, cfg.dim), z(D, dt=I32)
+        self.logits_full = z(D, cfg.vocab)
+
+    def step(self):
+        _no_pdl(self._step)
+
+    def _step(self):
+        c, D, x, g = self.full_cfg, self.slots, self.x, self.group
+        ops.embed(self.tokens, self.emb_q, self.emb_s, out=x)
+        for l, w in enumerate(self.layers):
+            xq, sx = self._q(c.dim)
+            ops.quant_rows(x, w["rms_att"], c.eps, xq=xq, s_x=sx)
+            ops.gemm(xq, sx, w["wqkv"], w["s_wqkv"], out=self.qkv)
+            ops.attn_batch(self.args[l], D, self.slot_stride)
+            row_split(self, self.att, w["wo"], w["s_wo"], x, g)
+            xq, sx = self._q(c.dim)
+            ops.quant_rows(x, w["rms_ffn"], c.eps, xq=xq, s_x=sx)
+            ops.gemm_swiglu(xq, sx, w["w1"], w["s_w1"], w["w3"], w["s_w3"], out=self.h)
+            row_split(self, self.h, w["w2"], w["s_w2"], x, g)
+        xq, sx = self._q(c.dim)
+        ops.quant_rows(x, self.rms_final, c.eps, xq=xq, s_x=sx)
+        ops.gemm(xq, sx, self.cls_q, self.cls_s, out=self.logits)
+
+    def capture(self):
+        raise RuntimeError("the tensor-parallel batch step holds NCCL collectives: run it eagerly")
+
+    def gather_logits(self):
+        P, D, vs = self.ranks, self.slots, self.cfg.vocab
+        buf = torch.empty(P, D, vs, dtype=F32, device=self.dev)
+        dist.all_gather_into_tensor(buf, self.logits, group=self.group)
+        self.logits_full.copy_(buf.permute(1, 0, 2).reshape(D, P * vs))
+        return self.logits_full
+
+    def kernel_launches(self):
+        """Kernels of a step: embed; per layer quant, qkv GEMM, attention, then
+        per row-split linear amax, quant, GEMM, dequant (x2) and quant + SwiGLU
+        GEMM; final quant and classifier GEMM."""
+        return 1 + self.cfg.layers * (3 + 4 + 2 + 4) + 2
+
+
+class TpBatchLlamaDevice(BatchLlamaDevice):
+    """BatchLlamaDevice (`llm/runtime.py:155-241`) over a TpBatchDecoder: every
+    rank constructs it and calls step() / generate() in the same order; every
+    rank returns the full [D, vocab] logits."""
+
+    def __init__(self, model, slots=None, group=None, device=None):
+        if not isinstance(model, TpBatchDecoder):
+            cfg, qw, kv = model
+            dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
+            model = TpBatchDecoder(cfg, qw, kv, slots, group=group, device=dev)
+        super().__init__(model, graphs=False)
+        self.cfg = model.full_cfg
+        self._out = torch.zeros(model.slots, self.cfg.vocab, dtype=F32).pin_memory()
+
+    def _run_step(self):
+        self.dec.step()
+        return self.dec.gather_logits()
+
