@@ -222,17 +222,24 @@ def run_batch(args, cfg, qw, ws, rank, local):
     from torch2riscv_accelerator_b200.model import BatchDecoder
     from torch2riscv_accelerator_b200.runtime import BatchLlamaDevice
     D = args.batch
-    tp = ws > 1 and args.parallel == "tp"
-    if tp:
+    tp = ep = False
+    if ws > 1 and args.parallel == "tp":               # MoE: experts split (ep); else tensor parallel
+        from torch2riscv_accelerator_b200.ep import EpBatchDecoder, EpBatchLlamaDevice, check_ep
         from torch2riscv_accelerator_b200.tp import TpBatchDecoder, TpBatchLlamaDevice, check_split
         try:
-            check_split(cfg, ws)
+            (check_ep if cfg.moe else check_split)(cfg, ws)
+            ep, tp = cfg.moe, not cfg.moe
         except ValueError as e:
             if rank == 0:
                 print(f"# {e}: independent replicas instead", file=sys.stderr)
-            tp = False
-    dec = TpBatchDecoder(cfg, qw, qw.kv_scales, slots=D) if tp else BatchDecoder(cfg, qw, qw.kv_scales, slots=D)
-    seqs = D if tp else ws * D                         # sequences per step over all GPUs
+    if tp:
+        dec = TpBatchDecoder(cfg, qw, qw.kv_scales, slots=D)
+    elif ep:
+        dec = EpBatchDecoder(cfg, qw, qw.kv_scales, slots=D)
+    else:
+        dec = BatchDecoder(cfg, qw, qw.kv_scales, slots=D)
+    split = tp or ep
+    seqs = D if split else ws * D                      # sequences per step over all GPUs
     g = torch.Generator(device=dec.dev).manual_seed(args.seed + 11)
     for t in (dec.kc, dec.vc):
         t.copy_(torch.randint(-127, 128, t.shape, dtype=torch.int8, device=dec.dev, generator=g))
@@ -242,7 +249,7 @@ def run_batch(args, cfg, qw, ws, rank, local):
     dec.pos.fill_(P)
     # one step: the captured graph (the tensor-parallel step holds NCCL
     # collectives and runs eagerly)
-    run = dec.step if tp else dec.capture().replay   # (a capture's warm-up step writes the rows of position P)
+    run = dec.step if split else dec.capture().replay   # (a capture's warm-up step writes the rows of position P)
     st = torch.cuda.current_stream()
     for _ in range(args.warmup):
         run()
@@ -262,7 +269,7 @@ def run_batch(args, cfg, qw, ws, rank, local):
     barrier(ws)
     dt = max_over_ranks(e0.elapsed_time(e1) / 1e3, ws)
     # e2e: host tokens / positions in, [D, vocab] logits out, per step
-    dev = TpBatchLlamaDevice(dec) if tp else BatchLlamaDevice(dec)
+    dev = TpBatchLlamaDevice(dec) if tp else EpBatchLlamaDevice(dec) if ep else BatchLlamaDevice(dec)
     toks = rng.integers(0, cfg.vocab, (args.warmup + args.steps, D))
     for i in range(args.warmup):
         dev.step([P + i] * D, [int(v) for v in toks[i]])
@@ -281,12 +288,13 @@ def run_batch(args, cfg, qw, ws, rank, local):
         line = {
             "metric": METRIC, "value": seqs * args.steps / dt, "unit": "tok/s", "n_gpus": ws, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": 1e3 * dt / args.steps, "higher_is_better": True,
-            "scaling": "strong" if tp else "weak", "vs_baseline": None, "dtype": "int8",
+            "scaling": "strong" if split else "weak", "vs_baseline": None, "dtype": "int8",
             "data": "synthetic (N(0,0.02) weights seed 0, uniform token ids, seeded random int8 caches)",
             "config": {"workload": f"{cfg.name}-shape W8A8 batched decode: {D} sequences per step, each at "
                                    f"positions {P}..{cfg.seq_len - 1} of its own T=2048 cache",
                        "model": cfg.name, "global_batch": seqs, "seq_len": cfg.seq_len,
-                       "parallelism": f"tp{ws}" if tp else f"replicas x{ws}", "attention": cfg.attn,
+                       "parallelism": f"tp{ws}" if tp else f"ep{ws}" if ep else f"replicas x{ws}",
+                       "attention": cfg.attn,
                        "l2": "no flush: the step reads the weights and every slot's cache, far over the 126 MB L2"},
             "e2e": {"value": seqs * args.steps / dt_e2e, "unit": "tok/s", "h2d_bytes_per_step": 8 * D,
                     "d2h_bytes_per_step": 4 * D * cfg.vocab},
@@ -303,8 +311,15 @@ def run_batch(args, cfg, qw, ws, rank, local):
         dist.destroy_process_group()
 
 
-def config_of(cfg, args, ws, tp=False):
+def config_of(cfg, args, ws, tp=False, ep=False):
     P = cfg.seq_len - args.warmup - args.steps
+    if ep:
+        return {"workload": f"{cfg.name}-shape W8A8 MoE decode, batch 1, T=2048, experts split over {ws} GPUs: "
+                            f"{P}-token prompt prefilled, then {args.warmup} untimed + {args.steps} timed greedy "
+                            f"decode steps (the experts' terms exchanged inside the kernels over NVLink)",
+                "model": cfg.name, "global_batch": 1, "seq_len": cfg.seq_len, "prompt": P,
+                "parallelism": f"ep{ws}", "attention": cfg.attn,
+                "l2": "no flush: the step streams the attention weights, the chosen experts and the KV cache"}
     if tp:
         return {"workload": f"{cfg.name}-shape W8A8 decode, batch 1, T=2048, tensor parallel over {ws} GPUs: "
                             f"{P}-token prompt prefilled in chunks of up to 256 rows, then {args.warmup} untimed + "
@@ -360,22 +375,27 @@ def main():
     if args.batch > 1:
         run_batch(args, cfg, qw, ws, rank, local)
         return
-    tp = ws > 1 and args.parallel == "tp"
-    if tp:
+    tp = ep = False
+    if ws > 1 and args.parallel == "tp":               # MoE: experts split (ep); else tensor parallel
+        from torch2riscv_accelerator_b200.ep import EpLlamaDevice, check_ep
         from torch2riscv_accelerator_b200.tp import TpLlamaDevice, check_split
         try:
-            check_split(cfg, ws)
+            (check_ep if cfg.moe else check_split)(cfg, ws)
+            ep, tp = cfg.moe, not cfg.moe
         except ValueError as e:
             if rank == 0:
                 print(f"# {e}: independent replicas instead", file=sys.stderr)
-            tp = False
     if tp:
         dev = TpLlamaDevice((cfg, qw, qw.kv_scales))
+        dec = dev.dec
+    elif ep:
+        dev = EpLlamaDevice((cfg, qw, qw.kv_scales))
         dec = dev.dec
     else:
         dec = DeviceDecoder(cfg, qw, qw.kv_scales)
         dev = LlamaDevice(dec)
-    seqs = 1 if tp else ws                               # sequences decoded per step over all GPUs
+    split = tp or ep
+    seqs = 1 if split else ws                            # sequences decoded per step over all GPUs
     P = cfg.seq_len - args.warmup - args.steps
     prompt = np.random.default_rng(args.seed + 3).integers(0, cfg.vocab, P)
     torch.cuda.synchronize()
@@ -467,14 +487,16 @@ def main():
         line = {
             "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": ws, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": 1e3 * dt / args.steps, "higher_is_better": True,
-            "scaling": "strong" if tp else "weak", "vs_baseline": value / FPGA_TOKS, "dtype": "int8",
+            "scaling": "strong" if split else "weak", "vs_baseline": value / FPGA_TOKS, "dtype": "int8",
             "data": "synthetic (N(0,0.02) weights seed 0, uniform prompt ids)",
-            "config": config_of(cfg, args, ws, tp),
+            "config": config_of(cfg, args, ws, tp, ep),
             "e2e": {"value": seqs * args.steps / dt_e2e, "unit": "tok/s", "h2d_bytes_per_step": 8,
                     "d2h_bytes_per_step": 4 * cfg.vocab},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": None if tp else NCU_TRAFFIC["bytes"],
-                         "traffic_source": "not captured for a vocabulary slice" if tp else NCU_TRAFFIC["source"],
+                         "frac": achieved / peak,
+                         "traffic": NCU_TRAFFIC["bytes"] if cfg.name == "Qwen3-0.6B" and not tp else None,
+                         "traffic_source": NCU_TRAFFIC["source"] if cfg.name == "Qwen3-0.6B" and not tp else
+                         "not captured for this classifier shape",
                          "peak_source": peak_src,
                          "kernel": f"gemv_kernel (classifier GEMV {N}x{K}, rmsnorm+quant prologue, fused argmax)",
                          "bytes_per_launch": gemv_bytes, "us_per_launch": t_gemv * 1e6},
@@ -492,7 +514,7 @@ def main():
         import torch.distributed as dist
         del g
         dec.graphs.clear()
-        if tp:
+        if split:
             dev.close()
         dist.destroy_process_group()
 

@@ -194,6 +194,21 @@ int w8a8_moe_ffn(const float* x, const float* norm_g, float eps, int rows, int d
                  const float* resid, float* y, int32_t* ids, float* w, void* scratch, size_t scratch_bytes,
                  void* stream);
 
+/* Expert parallelism (no counterpart in the reference, which runs on one
+ * device): this rank holds experts [expert_lo, expert_lo + experts_local) of
+ * the router's `experts` (gate_q .. down_s hold only those, indexed from 0);
+ * the router runs whole. wy [rows, top_k, dim] receives w_j * y_j for the
+ * slots of this rank's experts and +0 for the others (no combine, no
+ * residual). An all-reduce SUM of wy over the ranks is exact (each element has
+ * one nonzero contributor), and w8a8_moe_combine then folds it in k order:
+ * y = resid + (((0 + t_0) + t_1) + ...) -- w8a8_moe_ffn's result bit for bit. */
+int w8a8_moe_ffn_ep(const float* x, const float* norm_g, float eps, int rows, int dim, const int8_t* router_q,
+                    const float* router_s, int experts, int top_k, int expert_lo, int experts_local,
+                    const int8_t* gate_q, const float* gate_s, const int8_t* up_q, const float* up_s,
+                    int expert_hidden, const int8_t* down_q, const float* down_s, float* wy, int32_t* ids, float* w,
+                    void* scratch, size_t scratch_bytes, void* stream);
+int w8a8_moe_combine(const float* wy, int rows, int top_k, int dim, const float* resid, float* y, void* stream);
+
 /* Fused per-layer attention of one sequence over its int8 KV cache. */
 typedef struct {
     int rows;                  /* query rows M (1: decode step, <= 16: prefill chunk) */
@@ -296,6 +311,10 @@ int w8a8_decode_advance(int32_t* tokens, int32_t* pos, uint64_t* argmax_key, int
 #define W8A8_TP_PART_WORDS(ranks, n) ((size_t)(ranks) * W8A8_TP_ROWS * (size_t)(n))
 #define W8A8_TP_AMAX_WORDS(ranks) ((size_t)(ranks) * (1 + W8A8_TP_CTAS) * W8A8_TP_ROWS)
 #define W8A8_TP_KEY_WORDS(ranks) (2 * W8A8_TP_AMAX_WORDS(ranks))
+/* ... and the expert-parallel MoE terms of decode rows: [ROWS][top_k][dim]
+ * terms, then [ranks][ROWS] presence words. */
+#define W8A8_TP_MOE_WORDS(ranks, top_k, dim) \
+    ((size_t)W8A8_TP_ROWS * (top_k) * (size_t)(dim) + (size_t)(ranks) * W8A8_TP_ROWS)
 
 typedef struct {
     int rank, ranks;                          /* 2 <= ranks <= W8A8_TP_MAX_RANKS */
@@ -362,6 +381,21 @@ int w8a8_tp_advance(const W8A8TpComm* comm, const uint64_t* keys, int32_t* token
 /* Seed the key block (this rank's own) so that the next w8a8_tp_advance reads
  * `token`. */
 int w8a8_tp_seed(const W8A8TpComm* comm, uint64_t* keys, int32_t token, void* stream);
+
+/* Expert parallelism over the exchange (decode rows <= W8A8_TP_ROWS): as
+ * w8a8_moe_ffn_ep, but each term w_j * y_j goes from its expert's rank into
+ * every rank's `terms` block (W8A8_TP_MOE_WORDS words), with a presence word
+ * per rank and row; w8a8_tp_moe_combine waits for the row's presence words
+ * and the k terms of each output and folds them: y = resid + (((0 + t_0) +
+ * t_1) + ...). No collective of the caller's is needed; the step is
+ * capturable in a CUDA graph. */
+int w8a8_tp_moe_ffn(const W8A8TpComm* comm, const float* x, const float* norm_g, float eps, int rows, int dim,
+                    const int8_t* router_q, const float* router_s, int experts, int top_k, int expert_lo,
+                    int experts_local, const int8_t* gate_q, const float* gate_s, const int8_t* up_q,
+                    const float* up_s, int expert_hidden, const int8_t* down_q, const float* down_s, uint64_t* terms,
+                    int32_t* ids, float* w, void* scratch, size_t scratch_bytes, void* stream);
+int w8a8_tp_moe_combine(const W8A8TpComm* comm, const uint64_t* terms, int rows, int top_k, int dim,
+                        const float* resid, float* y, void* stream);
 
 /* Tensor-parallel rows beyond decode, with the caller's collectives between:
  * max|x| per row as float bits (all-reduce MAX as int32 across ranks), then

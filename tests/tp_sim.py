@@ -74,3 +74,32 @@ class TpOracle(OM.OracleDecoder):
         dist.all_gather(out, torch.from_numpy(np.ascontiguousarray(part)))
         logits = np.concatenate([o.numpy() for o in out], axis=-1)
         return logits if all_logits else logits[0]
+
+
+def moe_ep_row(x, t, cfg, lo, n):
+    """One row of the MoE FFN as an expert-parallel rank computes it: the router
+    whole, the terms w_j * y_j of the slots whose expert is in [lo, lo + n)
+    (+0 for the others), summed over the ranks, then the k-order fold
+    (`oracle/model.py` moe_ffn_row, split by expert)."""
+    xq, s_x = N.quant_act(x[None])
+    scores, _ = N.linear(xq, s_x, t["router"], t["s_router"])
+    sc = scores[0]
+    ids = np.lexsort((np.arange(sc.size), -sc.astype(np.float64)))[:cfg.top_k]
+    v = sc[ids]
+    e = N.sfu_exp((v - v[0]).astype(F))
+    w = (e * N.sfu_recip(N.red_sum(e))).astype(F)
+    terms = np.zeros((cfg.top_k, cfg.dim), F)
+    for k, i in enumerate(ids):
+        if not lo <= i < lo + n:
+            continue
+        g, _ = N.linear(xq, s_x, t["e_gate"][i], t["s_e_gate"][i])
+        u, _ = N.linear(xq, s_x, t["e_up"][i], t["s_e_up"][i])
+        hq, s_h = N.quant_act(N.silu_gate(g, u))
+        yk, _ = N.linear(hq, s_h, t["e_down"][i], t["s_e_down"][i])
+        terms[k] = (w[k] * yk[0]).astype(F)
+    tt = torch.from_numpy(terms)
+    dist.all_reduce(tt, op=dist.ReduceOp.SUM)
+    y = np.zeros(cfg.dim, F)
+    for k in range(cfg.top_k):
+        y = (y + tt.numpy()[k]).astype(F)
+    return y

@@ -50,6 +50,10 @@ def tp_key_words(ranks):
     return 2 * tp_amax_words(ranks)
 
 
+def tp_moe_words(ranks, top_k, dim):
+    return TP_ROWS * top_k * dim + ranks * TP_ROWS
+
+
 P, I, F, Z, L = C.c_void_p, C.c_int, C.c_float, C.c_size_t, C.c_int64
 PROTOTYPES = {
     "w8a8_abi_version": (I, []),
@@ -72,6 +76,8 @@ PROTOTYPES = {
     "w8a8_gemm_swiglu": (I, [P, P, I, I, P, P, P, P, I, P, P]),
     "w8a8_moe_scratch_bytes": (Z, [I, I, I, I]),
     "w8a8_moe_ffn": (I, [P, P, F, I, I, P, P, I, I, P, P, P, P, I, P, P, P, P, P, P, P, Z, P]),
+    "w8a8_moe_ffn_ep": (I, [P, P, F, I, I, P, P, I, I, I, I, P, P, P, P, I, P, P, P, P, P, P, Z, P]),
+    "w8a8_moe_combine": (I, [P, I, I, I, P, P, P]),
     "w8a8_attn_scratch_bytes": (Z, [I, I, I, I, I]),
     "w8a8_attn": (I, [C.POINTER(W8A8AttnArgs), P]),
     "w8a8_attn_batch": (I, [C.POINTER(W8A8AttnArgs), I, Z, P]),
@@ -88,6 +94,9 @@ PROTOTYPES = {
     "w8a8_tp_attn": (I, [C.POINTER(W8A8AttnArgs), C.POINTER(W8A8TpComm), P, P]),
     "w8a8_tp_advance": (I, [C.POINTER(W8A8TpComm), P, P, P, P, I, P]),
     "w8a8_tp_seed": (I, [C.POINTER(W8A8TpComm), P, C.c_int32, P]),
+    "w8a8_tp_moe_ffn": (I, [C.POINTER(W8A8TpComm), P, P, F, I, I, P, P, I, I, I, I, P, P, P, P, I, P, P, P, P, P,
+                            P, Z, P]),
+    "w8a8_tp_moe_combine": (I, [C.POINTER(W8A8TpComm), P, I, I, I, P, P, P]),
     "w8a8_row_amax": (I, [P, I, I, P, P]),
     "w8a8_quant_rows_posted": (I, [P, P, I, I, P, P, P]),
     "w8a8_dequant_resid": (I, [P, P, P, I, I, P, P, P]),

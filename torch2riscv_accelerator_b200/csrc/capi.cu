@@ -256,14 +256,17 @@ size_t w8a8_moe_scratch_bytes(int rows, int dim, int top_k, int expert_hidden) {
            a256((size_t)rows * top_k * 4);
 }
 
-int w8a8_moe_ffn(const float* x, const float* norm_g, float eps, int rows, int dim, const int8_t* router_q,
-                 const float* router_s, int experts, int top_k, const int8_t* gate_q, const float* gate_s,
-                 const int8_t* up_q, const float* up_s, int expert_hidden, const int8_t* down_q, const float* down_s,
-                 const float* resid, float* y, int32_t* ids, float* w, void* scratch, size_t scratch_bytes,
-                 void* stream) {
+// the MoE launch of w8a8_moe_ffn (e_n = experts, wy NULL) and w8a8_moe_ffn_ep
+static int moe_launch(const float* x, const float* norm_g, float eps, int rows, int dim, const int8_t* router_q,
+                      const float* router_s, int experts, int top_k, int e_lo, int e_n, const int8_t* gate_q,
+                      const float* gate_s, const int8_t* up_q, const float* up_s, int expert_hidden,
+                      const int8_t* down_q, const float* down_s, const float* resid, float* y, float* wy,
+                      int32_t* ids, float* w, void* scratch, size_t scratch_bytes, void* stream,
+                      const TpCtx* tp = nullptr, uint64_t* wy_ll = nullptr) {
     if (!x || !router_q || !router_s || !gate_q || !gate_s || !up_q || !up_s || !down_q || !down_s ||
-        !resid || !y || !ids || !w || !scratch)
+        !ids || !w || !scratch || (wy == nullptr && wy_ll == nullptr && (!resid || !y)))
         return W8A8_EINVAL;
+    if (e_lo < 0 || e_n <= 0 || e_lo + e_n > experts) return W8A8_EINVAL;
     if (rows <= 0 || rows > W8A8_MAX_ROWS || dim <= 0 || experts <= 0 || experts > kMoeMaxExperts || top_k <= 0 ||
         top_k > kMoeMaxTopK || top_k > experts || expert_hidden <= 0)
         return W8A8_EINVAL;
@@ -277,6 +280,8 @@ int w8a8_moe_ffn(const float* x, const float* norm_g, float eps, int rows, int d
     p.x = x, p.norm_g = norm_g, p.eps = eps, p.inv_dim = inv_of(dim);
     p.rq = router_q, p.rs = router_s, p.gq = gate_q, p.gs = gate_s, p.uq = up_q, p.us = up_s;
     p.dq = down_q, p.ds = down_s, p.resid = resid, p.y = y, p.ids = ids, p.w = w;
+    p.e_lo = e_lo, p.e_n = e_n, p.wy = wy, p.wy_ll = wy_ll;
+    if (tp != nullptr) p.tp = *tp;
     char* sp = static_cast<char*>(scratch);
     p.xq = reinterpret_cast<int8_t*>(sp);
     sp += a256((size_t)rows * dim);
@@ -288,6 +293,33 @@ int w8a8_moe_ffn(const float* x, const float* norm_g, float eps, int rows, int d
     for (int i = 0; i < 3; ++i)
         if (moe_smem(p, i) > 200 * 1024) return W8A8_EINVAL;
     return cuda_status(launch_moe(p, S(stream)));
+}
+
+int w8a8_moe_ffn(const float* x, const float* norm_g, float eps, int rows, int dim, const int8_t* router_q,
+                 const float* router_s, int experts, int top_k, const int8_t* gate_q, const float* gate_s,
+                 const int8_t* up_q, const float* up_s, int expert_hidden, const int8_t* down_q, const float* down_s,
+                 const float* resid, float* y, int32_t* ids, float* w, void* scratch, size_t scratch_bytes,
+                 void* stream) {
+    return moe_launch(x, norm_g, eps, rows, dim, router_q, router_s, experts, top_k, 0, experts, gate_q, gate_s,
+                      up_q, up_s, expert_hidden, down_q, down_s, resid, y, nullptr, ids, w, scratch, scratch_bytes,
+                      stream);
+}
+
+int w8a8_moe_ffn_ep(const float* x, const float* norm_g, float eps, int rows, int dim, const int8_t* router_q,
+                    const float* router_s, int experts, int top_k, int expert_lo, int experts_local,
+                    const int8_t* gate_q, const float* gate_s, const int8_t* up_q, const float* up_s,
+                    int expert_hidden, const int8_t* down_q, const float* down_s, float* wy, int32_t* ids, float* w,
+                    void* scratch, size_t scratch_bytes, void* stream) {
+    if (!wy) return W8A8_EINVAL;
+    return moe_launch(x, norm_g, eps, rows, dim, router_q, router_s, experts, top_k, expert_lo, experts_local,
+                      gate_q, gate_s, up_q, up_s, expert_hidden, down_q, down_s, nullptr, nullptr, wy, ids, w,
+                      scratch, scratch_bytes, stream);
+}
+
+int w8a8_moe_combine(const float* wy, int rows, int top_k, int dim, const float* resid, float* y, void* stream) {
+    if (!wy || !resid || !y || rows <= 0 || rows > 65535 || top_k <= 0 || top_k > kMoeMaxTopK || dim <= 0)
+        return W8A8_EINVAL;
+    return cuda_status(launch_moe_combine(wy, rows, top_k, dim, resid, y, S(stream)));
 }
 
 size_t w8a8_attn_scratch_bytes(int rows, int heads, int kv_heads, int head_dim, int seq_len) {
@@ -524,6 +556,33 @@ int w8a8_dequant_resid(const int32_t* acc, const float* s_x, const float* s_w, i
                        float* y, void* stream) {
     if (!acc || !s_x || !s_w || !y || rows <= 0 || rows > 65535 || n <= 0) return W8A8_EINVAL;
     return cuda_status(launch_dequant_resid(acc, s_x, s_w, rows, n, resid, y, S(stream)));
+}
+
+int w8a8_tp_moe_ffn(const W8A8TpComm* comm, const float* x, const float* norm_g, float eps, int rows, int dim,
+                    const int8_t* router_q, const float* router_s, int experts, int top_k, int expert_lo,
+                    int experts_local, const int8_t* gate_q, const float* gate_s, const int8_t* up_q,
+                    const float* up_s, int expert_hidden, const int8_t* down_q, const float* down_s, uint64_t* terms,
+                    int32_t* ids, float* w, void* scratch, size_t scratch_bytes, void* stream) {
+    TpCtx t;
+    int st = tp_ctx(comm, &t);
+    if (st) return st;
+    if (rows <= 0 || rows > W8A8_TP_ROWS || top_k <= 0 || top_k > kMoeMaxTopK || dim <= 0 ||
+        !tp_block(comm, terms, W8A8_TP_MOE_WORDS(comm->ranks, top_k, dim)))
+        return W8A8_EINVAL;
+    return moe_launch(x, norm_g, eps, rows, dim, router_q, router_s, experts, top_k, expert_lo, experts_local,
+                      gate_q, gate_s, up_q, up_s, expert_hidden, down_q, down_s, nullptr, nullptr, nullptr, ids, w,
+                      scratch, scratch_bytes, stream, &t, terms);
+}
+
+int w8a8_tp_moe_combine(const W8A8TpComm* comm, const uint64_t* terms, int rows, int top_k, int dim,
+                        const float* resid, float* y, void* stream) {
+    TpCtx t;
+    int st = tp_ctx(comm, &t);
+    if (st) return st;
+    if (!resid || !y || rows <= 0 || rows > W8A8_TP_ROWS || top_k <= 0 || top_k > kMoeMaxTopK || dim <= 0 ||
+        !tp_block(comm, terms, W8A8_TP_MOE_WORDS(comm->ranks, top_k, dim)))
+        return W8A8_EINVAL;
+    return cuda_status(launch_moe_combine_ll(t, terms, rows, top_k, dim, resid, y, S(stream)));
 }
 
 }  // extern "C"

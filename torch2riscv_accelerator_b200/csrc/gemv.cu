@@ -79,7 +79,7 @@ __device__ __forceinline__ float sumsq16(const float* xf, int k, int lane) {
 // Activation prologue: rows m < MR of x -> int8 rows xs [MR][k] and scales
 // sx [MR] (zero rows beyond p.m). xf: fp32 staging [k]; gs: the RMSNorm gain
 // in shared memory. Every thread of the block takes part.
-template <int MR>
+template <int MR, bool TP>
 __device__ __forceinline__ void gemv_prologue(const LinearParams& p, int pro, int8_t* xs, float* xf, float* sx,
                                               const float* gs, float* red, float* bc, uint32_t ep, bool& ok,
                                               uint32_t* cnt) {
@@ -108,9 +108,9 @@ __device__ __forceinline__ void gemv_prologue(const LinearParams& p, int pro, in
             continue;
         }
         const float4* xr = reinterpret_cast<const float4*>(p.x + (size_t)m * k);
-        const bool posted = pro == PRO_QUANT && (p.amax_in != nullptr || p.amax_ll != nullptr);
+        const bool posted = pro == PRO_QUANT && (p.amax_in != nullptr || (TP && p.amax_ll != nullptr));
         uint32_t pa = pro == PRO_QUANT && p.amax_in != nullptr ? __ldcg(p.amax_in + m) : 0u;   // with the x loads
-        if (p.part_in != nullptr) {
+        if (TP && p.part_in != nullptr) {
             // tensor parallel: the row-split linear before this one left its int32
             // partials at every rank; x = resid + (f32(sum) * s_w) * s_x (its
             // epilogue, with the exact sum), kept by CTA 0 as the residual stream
@@ -133,7 +133,7 @@ __device__ __forceinline__ void gemv_prologue(const LinearParams& p, int pro, in
 #pragma unroll 4
             for (int c = tid; c < k / 4; c += nt) xf4[c] = __ldcg(xr + c);  // loads batched: 1-3 per thread
         }
-        if (pro == PRO_QUANT && p.amax_ll != nullptr)              // every rank's max|x| (its producer CTAs)
+        if (TP && pro == PRO_QUANT && p.amax_ll != nullptr)        // every rank's max|x| (its producer CTAs)
             pa = ll_block_max(p.tp, p.amax_ll, m, ep, ok, cnt, reinterpret_cast<uint32_t*>(red));
         __syncthreads();
         float r = 1.f;
@@ -249,7 +249,9 @@ __device__ __forceinline__ void swiglu_requant(const LinearParams& p) {
     if (tid == 0) *p.counter = 0u;
 }
 
-template <int MR>
+// TP: the tensor-parallel exchanges (a separate instantiation: the one-GPU
+// kernel keeps its code size and registers).
+template <int MR, bool TP>
 __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(LinearParams p, GemvCfg cf) {
     extern __shared__ __align__(128) unsigned char smem[];
     const int pro = cf.pro, epi = cf.epi, tr = cf.tr, S = cf.S, stages = cf.stages, ntiles = cf.ntiles;
@@ -334,10 +336,10 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(LinearParams p, G
             if (n < p.n && m < p.m) rs[m * nj + jj] = __ldcg(p.resid + (size_t)m * p.n + n);
         }
     }
-    const uint32_t ep = p.tp.ranks > 1 ? tp_epoch(p.tp) : 0u;  // this step's exchange words
+    const uint32_t ep = TP ? tp_epoch(p.tp) : 0u;             // this step's exchange words
     bool ok = true;
-    gemv_prologue<MR>(p, pro, xs, xf, sx, gs, red, bc, ep, ok, llcnt);   // ends with a block barrier
-    if (!ok) atomicOr(&g_gemv_errors, 32u);
+    gemv_prologue<MR, TP>(p, pro, xs, xf, sx, gs, red, bc, ep, ok, llcnt);   // ends with a block barrier
+    if (TP && !ok) atomicOr(&g_gemv_errors, 32u);
 
     if (producer) {
         if (lane == 0) {                                       // refill each stage once its consumers are done
@@ -403,13 +405,13 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(LinearParams p, G
                     if (epi == EPI_STORE) {
                         p.y[o] = v;
                         if (p.acc != nullptr) p.acc[o] = acc[m];
-                        if (p.argmax_key != nullptr || p.key_out != nullptr) {
-                            const unsigned long long key = argmax_key(v, n + p.n_offset);
+                        if (p.argmax_key != nullptr || (TP && p.key_out != nullptr)) {
+                            const unsigned long long key = argmax_key(v, TP ? n + p.n_offset : n);
                             tkey[m] = key > tkey[m] ? key : tkey[m];
                         }
                     } else if (epi == EPI_RESID) {
                         p.y[o] = fadd(rs[m * nj + j], v);
-                    } else if (epi == EPI_PARTIAL) {           // the int32 sum to every rank
+                    } else if (TP && epi == EPI_PARTIAL) {     // the int32 sum to every rank
                         const size_t w = (size_t)(p.tp.rank * kTpRows + m) * p.n + n;
 #pragma unroll
                         for (int q = 0; q < kTpMaxRanks; ++q)
@@ -446,7 +448,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(LinearParams p, G
     if (epi == EPI_SWIGLU && p.amax_out != nullptr) {         // max|h| for the next kernel's prologue
         if (tid < p.m && tid < MR && bamax[tid] != 0u) atomicMax(p.amax_out + tid, bamax[tid]);
     }
-    if (p.tp.ranks > 1 && tid < kTpRows) {                     // this CTA's row maxima / keys to every rank
+    if (TP && tid < kTpRows) {                                 // this CTA's row maxima / keys to every rank
         const int m = tid;
         if (epi == EPI_SWIGLU && p.amax_ll_out != nullptr)
             ll_post_cta(p.tp, p.amax_ll_out, blockIdx.x, gridDim.x, m, m < p.m && m < MR ? bamax[m] : 0u, ep);
@@ -522,7 +524,7 @@ static Tiling tiling(const LinearParams& p, int mr, int pro, int epi) {
 template <int MR>
 static cudaError_t launch_g(const LinearParams& p, int pro, int epi, cudaStream_t st) {
     const Tiling t = tiling(p, MR, pro, epi);
-    auto kern = gemv_kernel<MR>;
+    auto kern = p.tp.ranks > 1 ? gemv_kernel<MR, true> : gemv_kernel<MR, false>;
     // the launch's own size, not a common maximum: the block scheduler reserves
     // this much per CTA, and the next kernel's CTAs must fit beside this one's
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)t.smem);

@@ -19,10 +19,11 @@
 // fetched after the wait (bulk copies of whole row tiles).
 #include "linear_common.cuh"
 #include "pdl.cuh"
+#include "tp.cuh"
 
 namespace w8a8 {
 
-__device__ unsigned int g_moe_errors;                         // bit 3: a weight-tile copy wait gave up
+__device__ unsigned int g_moe_errors;     // bit 3: a weight-tile copy wait gave up; bit 5: an exchange wait
 
 constexpr int kMoeThreads = 256;
 constexpr int kMoeTile = 16;                                   // expert rows per CTA (launches 2 and 3)
@@ -118,20 +119,23 @@ __global__ void __launch_bounds__(kMoeThreads) moe_up_kernel(MoeParams p) {
     pdl_wait();
     pdl_trigger();
     if (tid == 0) {                                                       // the slot's expert: known now
-        const int e = p.ids[row * K + slot];
+        const int e = p.ids[row * K + slot] - p.e_lo;                     // this rank's index of it
         e_s = e;
-        const uint32_t bytes = (uint32_t)(kMoeTile * dim);
-        mbar_expect_tx(&bar, 2u * bytes);
-        bulk_g2s(wg, p.gq + ((size_t)e * ih + i0) * dim, bytes, &bar);
-        bulk_g2s(wu, p.uq + ((size_t)e * ih + i0) * dim, bytes, &bar);
+        if (e >= 0 && e < p.e_n) {                                        // (another rank's expert: nothing)
+            const uint32_t bytes = (uint32_t)(kMoeTile * dim);
+            mbar_expect_tx(&bar, 2u * bytes);
+            bulk_g2s(wg, p.gq + ((size_t)e * ih + i0) * dim, bytes, &bar);
+            bulk_g2s(wu, p.uq + ((size_t)e * ih + i0) * dim, bytes, &bar);
+        }
     }
     for (int c = tid; c < dim / 16; c += kMoeThreads)
         reinterpret_cast<int4*>(xs)[c] = __ldcg(reinterpret_cast<const int4*>(p.xq + (size_t)row * dim) + c);
     const float sx = __ldcg(p.s_x + row);
     __syncthreads();
+    const int e = e_s;
+    if (e < 0 || e >= p.e_n) return;                                      // no copy was issued
     const bool ok = mbar_wait(&bar, 0u);
     if (!ok && tid == 0) atomicOr(&g_moe_errors, 8u);
-    const int e = e_s;
     // thread t: row r = t / 16 of the tile, 16-byte chunks s, s + 16, ... of it
     const int r = tid / 16, sl = tid % 16;
     int ag = 0, au = 0;
@@ -170,7 +174,7 @@ __global__ void __launch_bounds__(kMoeThreads) moe_down_kernel(MoeParams p) {
     int8_t* wd = reinterpret_cast<int8_t*>(smem);                        // [K][16][ih] down rows
     int8_t* hq = wd + (size_t)K * kMoeTile * ih;                         // [K][ih]
     __shared__ __align__(8) uint64_t bar;
-    __shared__ int e_s[kMoeMaxTopK];
+    __shared__ int e_s[kMoeMaxTopK];                                     // this rank's index, or -1
     __shared__ float w_s[kMoeMaxTopK], sh_s[kMoeMaxTopK], inv_s[kMoeMaxTopK];
     if (tid == 0) {
         mbar_init(&bar, 1);
@@ -178,8 +182,16 @@ __global__ void __launch_bounds__(kMoeThreads) moe_down_kernel(MoeParams p) {
     }
     pdl_wait();
     pdl_trigger();
+    const uint32_t ep = p.wy_ll != nullptr ? tp_epoch(p.tp) : 0u;
+    if (p.wy_ll != nullptr && tile == 0 && tid == 0) {               // this rank reached layer's down: presence
+        const size_t pw = (size_t)kTpRows * K * dim + (size_t)p.tp.rank * kTpRows + row;
+#pragma unroll
+        for (int q = 0; q < kTpMaxRanks; ++q)
+            if (q < p.tp.ranks) ll_store(tp_at(p.tp, p.wy_ll, q) + pw, 1u, ep);
+    }
     if (tid < K) {
-        e_s[tid] = p.ids[row * K + tid];
+        const int e = p.ids[row * K + tid] - p.e_lo;
+        e_s[tid] = e >= 0 && e < p.e_n ? e : -1;
         w_s[tid] = p.w[row * K + tid];
         const float s = fmul(__uint_as_float(__ldcg(p.amax + row * K + tid)), W8A8_C127);
         sh_s[tid] = s;
@@ -188,9 +200,12 @@ __global__ void __launch_bounds__(kMoeThreads) moe_down_kernel(MoeParams p) {
     __syncthreads();
     if (tid == 0) {
         const uint32_t bytes = (uint32_t)(kMoeTile * ih);
-        mbar_expect_tx(&bar, (uint32_t)K * bytes);
+        uint32_t own = 0;
+        for (int j = 0; j < K; ++j) own += e_s[j] >= 0 ? 1u : 0u;
+        mbar_expect_tx(&bar, own * bytes);
         for (int j = 0; j < K; ++j)
-            bulk_g2s(wd + (size_t)j * kMoeTile * ih, p.dq + ((size_t)e_s[j] * dim + n0) * ih, bytes, &bar);
+            if (e_s[j] >= 0)
+                bulk_g2s(wd + (size_t)j * kMoeTile * ih, p.dq + ((size_t)e_s[j] * dim + n0) * ih, bytes, &bar);
     }
     // every slot's h row -> int8 with its own scale (quant_act of that expert's h)
     for (int i = tid; i < K * ih / 4; i += kMoeThreads) {
@@ -206,6 +221,10 @@ __global__ void __launch_bounds__(kMoeThreads) moe_down_kernel(MoeParams p) {
     const int r = tid / 16, sl = tid % 16, n = n0 + r;
     float y = 0.f;
     for (int j = 0; j < K; ++j) {                                         // k order: the combine's order
+        if (e_s[j] < 0) {                                                 // another rank's expert
+            if (p.wy != nullptr && sl == 0) p.wy[((size_t)row * K + j) * dim + n] = 0.f;
+            continue;                                                     // (exchange: its owner writes it)
+        }
         int acc = 0;
         const int4* a4 = reinterpret_cast<const int4*>(wd + ((size_t)j * kMoeTile + r) * ih);
         const int4* h4 = reinterpret_cast<const int4*>(hq + (size_t)j * ih);
@@ -216,10 +235,89 @@ __global__ void __launch_bounds__(kMoeThreads) moe_down_kernel(MoeParams p) {
 #pragma unroll
         for (int o = 8; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
         const float yk = fmul(fmul(i2f(acc), __ldg(p.ds + (size_t)e_s[j] * dim + n)), sh_s[j]);
-        y = fadd(y, fmul(w_s[j], yk));
+        const float t = fmul(w_s[j], yk);
+        if (p.wy_ll != nullptr) {                                         // the term to every rank
+            if (sl == 0) {
+                const size_t w = ((size_t)row * K + j) * dim + n;
+#pragma unroll
+                for (int q = 0; q < kTpMaxRanks; ++q)
+                    if (q < p.tp.ranks) ll_store(tp_at(p.tp, p.wy_ll, q) + w, __float_as_uint(t), ep);
+            }
+        } else if (p.wy != nullptr) {
+            if (sl == 0) p.wy[((size_t)row * K + j) * dim + n] = t;
+        } else {
+            y = fadd(y, t);
+        }
     }
-    if (sl == 0) p.y[(size_t)row * dim + n] = fadd(__ldcg(p.resid + (size_t)row * dim + n), y);
+    if (sl == 0 && p.wy == nullptr && p.wy_ll == nullptr)
+        p.y[(size_t)row * dim + n] = fadd(__ldcg(p.resid + (size_t)row * dim + n), y);
     if (!ok) mbar_wait(&bar, 0u);
+}
+
+// ---------------------------------------------------------------- combine
+// Expert parallelism, after the ranks' w_j * y_j terms were summed (each has one
+// nonzero contributor, so the sum is that term; a -0 becoming +0 does not change
+// the fold, which starts from +0): y = resid + (((0 + t_0) + t_1) + ...), k order.
+__global__ void __launch_bounds__(kMoeThreads) moe_combine_kernel(const float* wy, int K, int dim, const float* resid,
+                                                                  float* y) {
+    pdl_wait();
+    pdl_trigger();
+    const int row = blockIdx.y;
+    for (int n = blockIdx.x * kMoeThreads + threadIdx.x; n < dim; n += gridDim.x * kMoeThreads) {
+        float acc = 0.f;
+        for (int j = 0; j < K; ++j) acc = fadd(acc, __ldcg(wy + ((size_t)row * K + j) * dim + n));
+        y[(size_t)row * dim + n] = fadd(__ldcg(resid + (size_t)row * dim + n), acc);
+    }
+}
+
+cudaError_t launch_moe_combine(const float* wy, int m, int top_k, int dim, const float* resid, float* y,
+                               cudaStream_t st) {
+    const int bx = (dim + kMoeThreads - 1) / kMoeThreads;
+    return launch_k(moe_combine_kernel, dim3(bx, m), dim3(kMoeThreads), 0, st, wy, top_k, dim, resid, y);
+}
+
+// The same combine over exchange words: every rank's presence word of the row
+// first (the ordering between steps), then the k terms of each output (each
+// written by its expert's rank; all k loads in flight), folded in k order.
+__global__ void __launch_bounds__(kMoeThreads) moe_combine_ll_kernel(TpCtx tp, const uint64_t* wy, int K, int dim,
+                                                                     const float* resid, float* y) {
+    pdl_wait();
+    pdl_trigger();
+    const int row = blockIdx.y, tid = threadIdx.x;
+    const uint32_t ep = tp_epoch(tp);
+    bool ok = true;
+    if (tid < tp.ranks) ll_wait(wy + (size_t)kTpRows * K * dim + (size_t)tid * kTpRows + row, ep, ok);
+    __syncthreads();
+    for (int n = blockIdx.x * kMoeThreads + tid; n < dim; n += gridDim.x * kMoeThreads) {
+        uint64_t w[kMoeMaxTopK];
+        uint32_t pending = (1u << K) - 1u;
+        for (int spins = 0; pending != 0u; ++spins) {
+#pragma unroll
+            for (int j = 0; j < kMoeMaxTopK; ++j)
+                if (pending & (1u << j)) w[j] = ll_load(wy + ((size_t)row * K + j) * dim + n);
+#pragma unroll
+            for (int j = 0; j < kMoeMaxTopK; ++j)
+                if ((pending & (1u << j)) && (uint32_t)(w[j] >> 32) == ep) pending &= ~(1u << j);
+            if (pending == 0u) break;
+            if (!ok || spins >= kLlLimit) {
+                ok = false;
+                break;
+            }
+            if (spins >= kLlSpin) __nanosleep(128);
+        }
+        float acc = 0.f;
+#pragma unroll
+        for (int j = 0; j < kMoeMaxTopK; ++j)                             // k order
+            if (j < K) acc = fadd(acc, (pending & (1u << j)) ? 0.f : __uint_as_float((uint32_t)w[j]));
+        y[(size_t)row * dim + n] = fadd(__ldcg(resid + (size_t)row * dim + n), acc);
+    }
+    if (!ok) atomicOr(&g_moe_errors, 32u);
+}
+
+cudaError_t launch_moe_combine_ll(const TpCtx& tp, const uint64_t* wy_ll, int m, int top_k, int dim,
+                                  const float* resid, float* y, cudaStream_t st) {
+    const int bx = (dim + kMoeThreads - 1) / kMoeThreads;
+    return launch_k(moe_combine_ll_kernel, dim3(bx, m), dim3(kMoeThreads), 0, st, tp, wy_ll, top_k, dim, resid, y);
 }
 
 // ---------------------------------------------------------------- host side

@@ -148,9 +148,24 @@ struct MoeParams {
     float* s_x;               // scratch [m]
     float* h;                 // scratch [m, k, ih]
     uint32_t* amax;           // scratch [m, k]
+    // expert parallelism: this rank holds experts [e_lo, e_lo + e_n) (gq .. ds
+    // index them from 0); wy [m, k, dim], when set, receives w_j * y_j of the
+    // slots of those experts and +0 for the others instead of the combine
+    int e_lo, e_n;
+    float* wy;
+    // ... or, for decode rows (m <= kTpRows), the terms as exchange words into
+    // every rank's block: [kTpRows][k][dim] terms, then [ranks][kTpRows]
+    // presence words (each rank's down launch started: its earlier kernels,
+    // the previous combine included, are complete)
+    TpCtx tp;
+    uint64_t* wy_ll;
 };
 size_t moe_smem(const MoeParams& p, int which);
 cudaError_t launch_moe(const MoeParams& p, cudaStream_t st);
+cudaError_t launch_moe_combine(const float* wy, int m, int top_k, int dim, const float* resid, float* y,
+                               cudaStream_t st);
+cudaError_t launch_moe_combine_ll(const TpCtx& tp, const uint64_t* wy_ll, int m, int top_k, int dim,
+                                  const float* resid, float* y, cudaStream_t st);
 unsigned int moe_read_clear_errors();
 
 constexpr int kMaxRows = 16;  // query rows per attention call

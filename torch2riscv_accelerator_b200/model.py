@@ -108,15 +108,13 @@ class DeviceDecoder:
         if rows <= CHAIN_ROWS and not c.moe:
             return self._run_chain(rows, logits_rows, argmax)
         args = self._attn_args(rows)
-        ops.embed(self.tokens[:rows], self.emb_q, self.emb_s, out=x)
+        self._embed(rows, x)
         for l, w in enumerate(self.layers):
             ops.linear_fused(x, w["wqkv"], w["s_wqkv"], norm_g=w["rms_att"], eps=c.eps, out=qkv)
             ops.attn(args[l])
             ops.linear_fused(att, w["wo"], w["s_wo"], resid=x, out=x)
             if c.moe:                                                          # router, gate/up, down+combine
-                ops.moe_ffn(x, w["rms_ffn"], c.eps, w["router"], w["s_router"], c.top_k, w["e_gate"],
-                            w["s_e_gate"], w["e_up"], w["s_e_up"], w["e_down"], w["s_e_down"], self.moe_scratch,
-                            resid=x, out=x, ids=self.moe_ids[l, :rows], w=self.moe_w[l, :rows])
+                self._moe_rows(l, x)
                 continue
             ops.ffn_swiglu(x, w["rms_ffn"], c.eps, w["w1"], w["s_w1"], w["w3"], w["s_w3"], None, h=h,
                            requant=False)
@@ -146,6 +144,22 @@ class DeviceDecoder:
         xl = self.x[rows - logits_rows:rows]
         ops.classifier(xl, self.cls_q, self.cls_s, self.rms_final, c.eps, out=self.logits[:logits_rows],
                        argmax_key=self.key[:logits_rows] if argmax else None)
+
+    def _embed(self, rows, x):
+        ops.embed(self.tokens[:rows], self.emb_q, self.emb_s, out=x)
+
+    def _moe(self, l, x, j):
+        """The MoE FFN of layer l on rows x (at most 16, starting at row j):
+        x = x + moe(rmsnorm(x)); the routing into moe_ids / moe_w."""
+        c, w, e = self.cfg, self.layers[l], j + x.shape[0]
+        ops.moe_ffn(x, w["rms_ffn"], c.eps, w["router"], w["s_router"], c.top_k, w["e_gate"], w["s_e_gate"],
+                    w["e_up"], w["s_e_up"], w["e_down"], w["s_e_down"], self.moe_scratch, resid=x, out=x,
+                    ids=self.moe_ids[l, j:e], w=self.moe_w[l, j:e])
+
+    def _moe_rows(self, l, x):
+        """The MoE FFN of layer l on all rows of x, in 16-row groups."""
+        for j in range(0, x.shape[0], CHUNK):
+            self._moe(l, x[j:j + CHUNK], j)
 
     def _sub_attn_args(self, l, j, m):
         a = self._sub_args.get((l, j, m))
@@ -177,12 +191,7 @@ class DeviceDecoder:
             ops.quant_rows(att, None, 0.0, xq=aq, s_x=sa)
             ops.gemm(aq, sa, w["wo"], w["s_wo"], out=x, resid=x)
             if c.moe:
-                for j in range(0, rows, CHUNK):
-                    e = min(j + CHUNK, rows)
-                    ops.moe_ffn(x[j:e], w["rms_ffn"], c.eps, w["router"], w["s_router"], c.top_k, w["e_gate"],
-                                w["s_e_gate"], w["e_up"], w["s_e_up"], w["e_down"], w["s_e_down"],
-                                self.moe_scratch, resid=x[j:e], out=x[j:e], ids=self.moe_ids[l, j:e],
-                                w=self.moe_w[l, j:e])
+                self._moe_rows(l, x)
                 continue
             xq, sx = self._q(rows, c.dim)
             ops.quant_rows(x, w["rms_ffn"], c.eps, xq=xq, s_x=sx)
@@ -318,6 +327,9 @@ class BatchDecoder:
                      for l, w in enumerate(self.layers)]
         self.graph = None
 
+    _moe = DeviceDecoder._moe                      # the MoE FFN of 16-row groups of slots
+    _moe_rows = DeviceDecoder._moe_rows
+
     def _q(self, k):
         return self.xq_buf[:self.slots * k].view(self.slots, k), self.sx_buf
 
@@ -334,12 +346,7 @@ class BatchDecoder:
             ops.quant_rows(self.att, None, 0.0, xq=aq, s_x=sa)
             ops.gemm(aq, sa, w["wo"], w["s_wo"], out=x, resid=x)
             if c.moe:
-                for j in range(0, D, CHUNK):
-                    e = min(j + CHUNK, D)
-                    ops.moe_ffn(x[j:e], w["rms_ffn"], c.eps, w["router"], w["s_router"], c.top_k, w["e_gate"],
-                                w["s_e_gate"], w["e_up"], w["s_e_up"], w["e_down"], w["s_e_down"],
-                                self.moe_scratch, resid=x[j:e], out=x[j:e], ids=self.moe_ids[l, j:e],
-                                w=self.moe_w[l, j:e])
+                self._moe_rows(l, x)
                 continue
             xq, sx = self._q(c.dim)
             ops.quant_rows(x, w["rms_ffn"], c.eps, xq=xq, s_x=sx)

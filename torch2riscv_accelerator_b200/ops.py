@@ -197,6 +197,28 @@ def moe_ffn(x, norm_g, eps, router_q, router_s, top_k, gate_q, gate_s, up_q, up_
     return out, ids, w
 
 
+def moe_ffn_ep(x, norm_g, eps, router_q, router_s, top_k, expert_lo, gate_q, gate_s, up_q, up_s, down_q, down_s,
+               scratch, wy, ids, w):
+    """Expert parallelism: the MoE FFN rows over this rank's experts
+    [expert_lo, expert_lo + gate_q.shape[0]); wy [rows, top_k, dim] receives
+    w_j * y_j of their slots and +0 for the others."""
+    _need(x, F32, "x")
+    m, dim = x.shape
+    experts, (local, ih) = router_q.shape[0], gate_q.shape[:2]
+    _lib.check("w8a8_moe_ffn_ep", _lib.load().w8a8_moe_ffn_ep(
+        _p(x), _p(norm_g), float(eps), m, dim, _p(router_q), _p(router_s), experts, top_k, int(expert_lo), local,
+        _p(gate_q), _p(gate_s), _p(up_q), _p(up_s), ih, _p(down_q), _p(down_s), _p(wy), _p(ids), _p(w),
+        _p(scratch), scratch.numel(), _st()))
+    return wy
+
+
+def moe_combine(wy, resid, out):
+    """out = resid + the k-order fold of wy [rows, top_k, dim]."""
+    m, k, dim = wy.shape
+    _lib.check("w8a8_moe_combine", _lib.load().w8a8_moe_combine(_p(wy), m, k, dim, _p(resid), _p(out), _st()))
+    return out
+
+
 def attn_scratch(rows, heads, kv_heads, head_dim, seq_len, device):
     n = _lib.load().w8a8_attn_scratch_bytes(rows, heads, kv_heads, head_dim, seq_len)
     return torch.zeros(n, dtype=torch.uint8, device=device)
@@ -282,6 +304,26 @@ def tp_advance(comm, keys, tokens, pos, rows, next_token=None):
 
 def tp_seed(comm, keys, token):
     _lib.check("w8a8_tp_seed", _lib.load().w8a8_tp_seed(ctypes.byref(comm), keys, int(token), _st()))
+
+
+def tp_moe_ffn(comm, x, norm_g, eps, router_q, router_s, top_k, expert_lo, gate_q, gate_s, up_q, up_s, down_q,
+               down_s, scratch, terms, ids, w):
+    """Expert parallelism over the exchange: the terms of this rank's experts'
+    slots into every rank's `terms` block (decode rows)."""
+    _need(x, F32, "x")
+    m, dim = x.shape
+    experts, (local, ih) = router_q.shape[0], gate_q.shape[:2]
+    _lib.check("w8a8_tp_moe_ffn", _lib.load().w8a8_tp_moe_ffn(
+        ctypes.byref(comm), _p(x), _p(norm_g), float(eps), m, dim, _p(router_q), _p(router_s), experts, top_k,
+        int(expert_lo), local, _p(gate_q), _p(gate_s), _p(up_q), _p(up_s), ih, _p(down_q), _p(down_s), terms,
+        _p(ids), _p(w), _p(scratch), scratch.numel(), _st()))
+
+
+def tp_moe_combine(comm, terms, rows, top_k, resid, out):
+    dim = resid.shape[-1]
+    _lib.check("w8a8_tp_moe_combine", _lib.load().w8a8_tp_moe_combine(ctypes.byref(comm), terms, rows, top_k, dim,
+                                                                     _p(resid), _p(out), _st()))
+    return out
 
 
 def row_amax(x, out):

@@ -97,20 +97,21 @@ class TpComm:
     IPC; the handles travel over the torch.distributed group). Collective:
     every rank of the group constructs it with the same model shape."""
 
-    KINDS = ("att", "o", "h", "down")             # per layer: max|att|, o partials, max|h|, down partials
-
-    def __init__(self, cfg, device, group=None):
+    def __init__(self, cfg, device, group=None, sizes=None):
+        """sizes: words of each per-layer block kind; by default the tensor-
+        parallel decoder's (max|att|, o partials, max|h|, down partials)."""
         self.group = group
         self.rank, self.ranks = dist.get_rank(group), dist.get_world_size(group)
         P, L = self.ranks, cfg.layers
         lib = _lib.load()
-        sizes = {"att": _lib.tp_amax_words(P), "o": _lib.tp_part_words(P, cfg.dim), "h": _lib.tp_amax_words(P),
-                 "down": _lib.tp_part_words(P, cfg.dim)}
+        if sizes is None:
+            sizes = {"att": _lib.tp_amax_words(P), "o": _lib.tp_part_words(P, cfg.dim), "h": _lib.tp_amax_words(P),
+                     "down": _lib.tp_part_words(P, cfg.dim)}
         off, self._off = _lib.TP_HEADER, {}
         for l in range(L):
-            for kind in self.KINDS:
+            for kind, words in sizes.items():
                 self._off[(l, kind)] = off
-                off += 8 * sizes[kind]
+                off += 8 * words
         self._off["keys"] = off
         off += 8 * _lib.tp_key_words(P)
         self.bytes = off
