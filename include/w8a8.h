@@ -33,7 +33,7 @@ extern "C" {
 #define W8A8_ECUDA 3    /* the CUDA launch failed (cudaGetLastError) */
 #define W8A8_ESCRATCH 4 /* the scratch buffer is smaller than required */
 
-#define W8A8_ABI_VERSION 3
+#define W8A8_ABI_VERSION 4
 #define W8A8_MAX_ROWS 16 /* query rows per call (decode: 1, prefill chunk: 16) */
 
 /* ABI version (W8A8_ABI_VERSION) and a message for a status code. */
@@ -231,6 +231,17 @@ typedef struct {
     size_t scratch_bytes;
     uint32_t* att_amax;        /* [rows] or NULL: max|att| per row posted by atomic max (decode chain:
                                   the o-projection's w8a8_linear_chain reads it; zero before the call) */
+    /* Per cache channel scales ([kv_heads * head_dim] fp32 each, or NULL for
+     * the per-layer inv_sk / inv_sv / a_v), as hf_generic.SaCache
+     * (compiler/frontend/hf_generic.py:153-187) computes them on the host from
+     * calibrate_kv(channel=...) scales: K per channel -- k_scale = s_k (q * s_k
+     * per head channel before q's quantization), inv_sk_ch = F(1) / s_k, and
+     * a_k above = F(1 / sqrt(head_dim)); V per channel -- inv_sv_ch = F(1) /
+     * s_v, a_v_ch = s_v * F(1/127). K and V are independent. */
+    const float* k_scale;
+    const float* inv_sk_ch;
+    const float* inv_sv_ch;
+    const float* a_v_ch;
 } W8A8AttnArgs;
 
 /* QK-norm, RoPE, the K/V rows appended at pos, per-head quant_act of q,

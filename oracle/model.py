@@ -23,18 +23,25 @@ from . import numerics as N
 F = np.float32
 
 
-def attention_rows(q, kc, vc, positions, a_k, a_v, heads, kv_heads, head_dim, variant):
+def attention_rows(q, kc, vc, positions, a_k, a_v, heads, kv_heads, head_dim, variant, k_scale=None):
     """Attention of rows q [M, heads*head_dim] (after QK-norm and RoPE) over one
     layer's int8 cache kc / vc [T, kv_heads*head_dim]; row m attends t <= positions[m].
-    NORM: `llm/ref_model.py:233-243`; QSUM: `compiler/frontend/hf_generic.py:264-292`."""
+    NORM: `llm/ref_model.py:233-243`; QSUM: `compiler/frontend/hf_generic.py:264-292`.
+    Per cache channel scales (`hf_generic.py:241-246`, :290): k_scale
+    [kv_heads*head_dim] multiplies each query head's channels (those of its KV
+    head) before the query's quantization; a_v may be [kv_heads*head_dim]."""
     M = q.shape[0]
     G = heads // kv_heads
+    per_q = lambda v: np.asarray(v, F).reshape(kv_heads, head_dim)[np.arange(heads) // G]   # [H, hd]
+    av = per_q(a_v) if np.ndim(a_v) else F(a_v)
     out = np.empty((M, heads * head_dim), F)
     for m in range(M):
         n = int(positions[m]) + 1
         K = kc[:n].reshape(n, kv_heads, head_dim).astype(np.int64)
         V = vc[:n].reshape(n, kv_heads, head_dim).astype(np.int64)
         qh = q[m].reshape(heads, head_dim)
+        if k_scale is not None:
+            qh = (qh * per_q(k_scale)).astype(F)
         qq, s_q = N.quant_act(qh)                                         # [H, hd], [H]
         kh = K[:, np.arange(heads) // G, :]                                # [n, H, hd]
         acc = np.einsum("hd,thd->ht", qq.astype(np.int64), kh)            # [H, n] exact
@@ -46,13 +53,13 @@ def attention_rows(q, kc, vc, positions, a_k, a_v, heads, kv_heads, head_dim, va
             r = N.sfu_recip(N.red_sum_rows(e))
             pq = N.to_i8(((e * r[:, None]).astype(F) * F(127)).astype(F)).astype(np.int64)
             pv = np.einsum("ht,thd->hd", pq, vh)
-            o = (pv.astype(F) * F(a_v)).astype(F)
+            o = (pv.astype(F) * av).astype(F)
         else:
             eq = N.to_i8((e * F(127.0)).astype(F))
             pv = np.einsum("ht,thd->hd", eq.astype(np.int64), vh)
             ssum = eq.astype(np.int64).sum(axis=1).astype(F)              # exact: at most 127*T < 2^24
             rq = (N.sfu_recip(ssum) * F(127.0)).astype(F)
-            o = ((pv.astype(F) * rq[:, None]).astype(F) * F(a_v)).astype(F)
+            o = ((pv.astype(F) * rq[:, None]).astype(F) * av).astype(F)
         out[m] = o.reshape(-1)
     return out
 
@@ -63,7 +70,8 @@ def attn_layer(cfg, qkv, pos, kc, vc, consts, cos_tab, sin_tab, q_norm=None, k_n
     [T, kv_dim] first (`llm/ref_model.py:228-229`), then attention_rows."""
     c = cfg
     M, H, Hk, hd = qkv.shape[0], c.heads, c.kv_heads, c.head_dim
-    inv_sk, inv_sv, a_k, a_v = consts
+    inv_sk, inv_sv, a_k, a_v = consts[:4]                               # (arrays: per cache channel)
+    k_scale = consts[4] if len(consts) > 4 else None
     pos = np.asarray(pos, np.int64)
     cos, sin = cos_tab[pos], sin_tab[pos]
     q = qkv[:, :c.q_dim].reshape(M, H, hd)
@@ -77,7 +85,7 @@ def attn_layer(cfg, qkv, pos, kc, vc, consts, cos_tab, sin_tab, q_norm=None, k_n
     for m in range(M):
         kc[pos[m]] = N.to_i8((k[m] * inv_sk).astype(F))
         vc[pos[m]] = N.to_i8((v[m] * inv_sv).astype(F))
-    return attention_rows(q, kc, vc, pos, a_k, a_v, H, Hk, hd, c.attn)
+    return attention_rows(q, kc, vc, pos, a_k, a_v, H, Hk, hd, c.attn, k_scale)
 
 
 def moe_ffn_row(x, t, cfg):
@@ -110,15 +118,35 @@ class OracleDecoder:
     kv_scales [layers, 2] (static per-layer K and V scales)."""
 
     def __init__(self, cfg, qw, kv_scales):
+        """kv_scales: [layers, 2] per layer, or [layers, 2, kv_dim] per cache
+        channel (`hf_generic.calibrate_kv(channel=...)`; a part whose row holds
+        one value is per layer)."""
         self.cfg, self.qw = cfg, qw
         self.kv = np.asarray(kv_scales, F)
         self.consts = []
         for l in range(cfg.layers):
-            s_k, s_v = F(self.kv[l, 0]), F(self.kv[l, 1])
-            self.consts.append((F(1.0 / s_k), F(1.0 / s_v), F(float(s_k) / np.sqrt(cfg.head_dim)),
-                                F(float(s_v) / 127.0)))
+            self.consts.append(self.layer_consts(self.kv[l], cfg.head_dim))
         self._w64 = {}
         self.reset()
+
+    @staticmethod
+    def layer_consts(kv_l, hd):
+        """(inv_sk, inv_sv, a_k, a_v, k_scale): per layer `llm/ref_model.py:230-231`
+        and `llm/export_w8a8.py:68-72`; per channel `hf_generic.SaCache`
+        (:153-187): K -- q * s_k before its quantization, F(1) / s_k into the
+        cache, scores * F(1 / sqrt(hd)); V -- F(1) / s_v into the cache, the
+        output * (s_v * F(1/127)) per channel."""
+        if kv_l.ndim == 1:
+            s_k, s_v = F(kv_l[0]), F(kv_l[1])
+            return F(1.0 / s_k), F(1.0 / s_v), F(float(s_k) / np.sqrt(hd)), F(float(s_v) / 127.0), None
+        s_k, s_v = F(kv_l[0, 0]), F(kv_l[1, 0])
+        inv_sk, a_k, k_scale = F(1.0 / s_k), F(float(s_k) / np.sqrt(hd)), None
+        inv_sv, a_v = F(1.0 / s_v), F(float(s_v) / 127.0)
+        if np.any(kv_l[0] != s_k):
+            inv_sk, a_k, k_scale = (F(1.0) / kv_l[0]).astype(F), F(1.0 / np.sqrt(hd)), kv_l[0].astype(F)
+        if np.any(kv_l[1] != s_v):
+            inv_sv, a_v = (F(1.0) / kv_l[1]).astype(F), (kv_l[1] * F(1.0 / 127.0)).astype(F)
+        return inv_sk, inv_sv, a_k, a_v, k_scale
 
     def reset(self):
         c = self.cfg

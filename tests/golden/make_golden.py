@@ -22,6 +22,8 @@ Fixtures:
                 hf_generic.SaDecoder (QSUM attention) under the device SFU.
   qhf_qwen3.npz the same weights through qhf.QModel (NORM attention) under the
                 device SFU.
+  hf_qwen3_ch.npz  the same tiny Qwen3 with KV scales per cache channel from
+                hf_generic.calibrate_kv(channel="kv"), through SaDecoder
   moe.npz       hf_generic.QMixtralMoe rows of a synthetic Mixtral block
                 (compiler/tests/test_hf_moe.synthetic_model's shape).
   tiny_a_d8.w8a8  tiny model "a" of dm_tiny.npz written by the reference's
@@ -288,6 +290,62 @@ def gen_hf():
     print(f"  hf QSUM argmax {hlog.argmax(1).tolist()}, qhf NORM argmax {qlog.argmax(1).tolist()}")
 
 
+def gen_hf_channel():
+    """Per cache channel KV scales: the reference's own calibration
+    (hf_generic.calibrate_kv(channel="kv") on the fp32 model after the RoPE /
+    norm rewrites) and its SaDecoder (QSUM attention, SaCache per-channel
+    constants) under the device SFU, on the tiny Qwen3 of gen_hf."""
+    import torch
+    import hf_generic as H
+    import test_hf_generic as THG
+    from transformers import Qwen3Config, Qwen3ForCausalLM
+    from torch2riscv_accelerator_b200.weights import rope_tables
+    torch.set_grad_enabled(False)
+    cfg, w = qwen3_weights()
+    rng = np.random.default_rng(23)
+    calib = rng.integers(0, cfg.vocab, 40)
+    toks = rng.integers(0, cfg.vocab, 10)
+    hc = Qwen3Config(vocab_size=cfg.vocab, hidden_size=cfg.dim, intermediate_size=cfg.hidden,
+                     num_hidden_layers=cfg.layers, num_attention_heads=cfg.heads, num_key_value_heads=cfg.kv_heads,
+                     head_dim=cfg.head_dim, max_position_embeddings=cfg.seq_len, tie_word_embeddings=True,
+                     rms_norm_eps=cfg.eps, rope_theta=cfg.theta, attention_bias=False)
+    m = Qwen3ForCausalLM(hc).eval()
+    t = lambda a: torch.from_numpy(np.ascontiguousarray(a, F))
+    m.model.embed_tokens.weight.copy_(t(w["tok"]))
+    m.model.norm.weight.copy_(t(w["rms_final"]))
+    for l, layer in enumerate(m.model.layers):
+        a = layer.self_attn
+        a.q_proj.weight.copy_(t(_deinterleave_rows(w["wq"][l], cfg.heads, cfg.head_dim)))
+        a.k_proj.weight.copy_(t(_deinterleave_rows(w["wk"][l], cfg.kv_heads, cfg.head_dim)))
+        a.v_proj.weight.copy_(t(w["wv"][l]))
+        a.o_proj.weight.copy_(t(w["wo"][l]))
+        a.q_norm.weight.copy_(t(_deinterleave_rows(w["q_norm"][l], 1, cfg.head_dim)))
+        a.k_norm.weight.copy_(t(_deinterleave_rows(w["k_norm"][l], 1, cfg.head_dim)))
+        layer.mlp.gate_proj.weight.copy_(t(w["w1"][l]))
+        layer.mlp.up_proj.weight.copy_(t(w["w3"][l]))
+        layer.mlp.down_proj.weight.copy_(t(w["w2"][l]))
+        layer.input_layernorm.weight.copy_(t(w["rms_att"][l]))
+        layer.post_attention_layernorm.weight.copy_(t(w["rms_ffn"][l]))
+    H.rope_rewrite(m, cfg.seq_len)
+    H.norm_rewrite(m)
+    cos, sin = rope_tables(cfg)
+    for mod in m.modules():                        # the repo's tables (qhf.rope_tables' method)
+        if isinstance(mod, H.RopeTable):
+            mod.cos_t.copy_(t(cos))
+            mod.sin_t.copy_(t(sin))
+    kv = H.calibrate_kv(m, [int(x) for x in calib], cfg.seq_len, channel="kv")
+    assert kv.shape == (cfg.layers, 2, cfg.kv_dim)
+    H.quantize(m)
+    dec = H.SaDecoder(m, cfg.seq_len, kv)
+    with THG.device_sfu():
+        hlog = np.stack([dec(torch.tensor([[int(tk)]]), torch.tensor([[p]]))[0, 0].numpy()
+                         for p, tk in enumerate(toks)]).astype(F)
+    L, T = cfg.layers, len(toks)
+    kc = dec.kc.numpy().reshape(L, cfg.seq_len, cfg.kv_dim)[:, :T]
+    save("hf_qwen3_ch.npz", kv=kv, calib=calib, tokens=toks, logits=hlog, kc=kc)
+    print(f"  hf QSUM per-channel argmax {hlog.argmax(1).tolist()}")
+
+
 def gen_moe():
     import torch
     import hf_generic as H
@@ -336,11 +394,11 @@ def gen_files():
 def main():
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--skip-c0", action="store_true")
-    ap.add_argument("--only", help="comma list: sfu,convert,tiny,c0,hf,moe,files")
+    ap.add_argument("--only", help="comma list: sfu,convert,tiny,c0,hf,hfch,moe,files")
     a = ap.parse_args()
     only = set(a.only.split(",")) if a.only else None
     steps = [("sfu", gen_sfu), ("convert", gen_convert), ("tiny", gen_dm_tiny), ("c0", gen_dm_c0),
-             ("hf", gen_hf), ("moe", gen_moe), ("files", gen_files)]
+             ("hf", gen_hf), ("hfch", gen_hf_channel), ("moe", gen_moe), ("files", gen_files)]
     for name, fn in steps:
         if (only and name not in only) or (name == "c0" and a.skip_c0):
             continue

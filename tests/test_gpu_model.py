@@ -78,6 +78,45 @@ def test_hf_path_equals_oracle_and_near_reference(attn, fixture):
         assert np.max(np.abs(lg - ref)) <= 2e-3 * float(ref.max() - ref.min())
 
 
+@pytest.mark.parametrize("attn", ["qsum", "norm"])
+def test_per_channel_kv_equals_oracle(attn):
+    """Per cache channel K and V scales (the reference's own calibration,
+    hf_qwen3_ch.npz; hf_generic.SaCache): a 9-token prefill (the cluster
+    kernel's 16-row path) then decode rows, logits and KV bit-exact with the
+    oracle; QSUM within the reduction-order tolerance of the reference."""
+    g = golden("hf_qwen3_ch.npz")
+    cfg, w = _qwen3_tiny(attn)
+    dev = LlamaDevice((cfg, W.from_fp32(cfg, w), g["kv"]))
+    ora = OM.OracleDecoder(cfg, OM.quantize_model(cfg, w), g["kv"])
+    toks = g["tokens"]
+    assert dev.prefill(toks[:4]).tobytes() == ora.forward_rows(toks[:4], range(4)).tobytes()
+    for pos in range(4, len(toks)):
+        lg = dev.forward(int(toks[pos]))
+        assert lg.tobytes() == ora.forward(int(toks[pos]), pos).tobytes(), f"pos {pos}"
+        if attn == "qsum":
+            ref = g["logits"][pos]
+            assert np.max(np.abs(lg - ref)) <= 2e-3 * float(ref.max() - ref.min())
+    n = len(toks)
+    for l in range(cfg.layers):
+        k, v = dev.dec.kv_rows(l, n)
+        assert np.array_equal(k, ora.kc[l, :n]) and np.array_equal(v, ora.vc[l, :n])
+
+
+def test_per_channel_kv_c2_dims_prefill_and_decode():
+    """C2 dimensions with per-channel K and V scales from this repo's
+    calibration: a 40-row tensor-core prefill (attention in 16-row
+    sub-chunks) and decode rows, bit-exact with the oracle."""
+    cfg = C.C2.with_(layers=2, vocab=4096)
+    w = W.fp32_model(cfg, 2, gains="random")
+    kv = W.calibrate_kv(cfg, w, np.arange(12), channel="kv")
+    dev = LlamaDevice((cfg, W.from_fp32(cfg, w), kv))
+    ora = OM.OracleDecoder(cfg, OM.quantize_model(cfg, w), kv)
+    toks = np.random.default_rng(2).integers(0, cfg.vocab, 43)
+    assert dev.prefill(toks[:40]).tobytes() == ora.forward_rows(toks[:40], range(40)).tobytes()
+    for p in range(40, 43):
+        assert dev.forward(int(toks[p])).tobytes() == ora.forward(int(toks[p]), p).tobytes()
+
+
 def test_prefill_chunks_equal_decode_steps():
     """A prompt prefilled in 16-row chunks (the last at P - 16) gives the same
     KV cache and last logits as feeding it token by token

@@ -125,7 +125,8 @@ def _qwen3():
     return cfg, w
 
 
-@pytest.mark.parametrize("variant,fixture", [("qsum", "hf_qwen3.npz"), ("norm", "qhf_qwen3.npz")])
+@pytest.mark.parametrize("variant,fixture", [("qsum", "hf_qwen3.npz"), ("norm", "qhf_qwen3.npz"),
+                                             ("qsum", "hf_qwen3_ch.npz")])
 def test_oracle_close_to_hf_path(variant, fixture):
     """QK-norm + GQA + tied + theta 1e6: the oracle against the reference's
     eager HF-path models under the device SFU (hf_generic.SaDecoder for QSUM,
@@ -165,3 +166,21 @@ def test_oracle_moe_rows_match_reference():
         assert list(ids) == list(g["ids"][r])
         assert np.array_equal(w, g["w"][r])
         assert np.array_equal(y, g["y"][r]), f"row {r}: max diff {np.max(np.abs(y - g['y'][r]))}"
+
+
+def test_per_channel_calibration_matches_the_reference():
+    """KV scales per cache channel from this repo's fp32 calibration run equal
+    the reference's calibrate_kv(channel="kv") (hf_qwen3_ch.npz) up to fp32
+    summation order; a part whose row is constant stays per layer."""
+    g = golden("hf_qwen3_ch.npz")
+    cfg, w = _qwen3()
+    kv = W.calibrate_kv(cfg, w, g["calib"], channel="kv")
+    assert kv.shape == g["kv"].shape == (cfg.layers, 2, cfg.kv_dim)
+    np.testing.assert_allclose(kv, g["kv"], rtol=1e-4)
+    per_layer = W.calibrate_kv(cfg, w, g["calib"])
+    np.testing.assert_allclose(per_layer, g["kv"].max(-1), rtol=1e-4)
+    k_only = W.calibrate_kv(cfg, w, g["calib"], channel="k")
+    assert np.all(k_only[:, 1] == k_only[:, 1, :1])             # V: one value per layer
+    consts, ch = W.layer_kv_consts(k_only[0], cfg.head_dim)
+    assert set(ch) == {"k_scale", "inv_sk_ch"} and consts[2] == np.float32(1.0 / np.sqrt(cfg.head_dim))
+

@@ -10,7 +10,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libw8a8_b200.so")
 
 W8A8_OK, W8A8_EINVAL, W8A8_EALIGN, W8A8_ECUDA, W8A8_ESCRATCH = 0, 1, 2, 3, 4
-ABI_VERSION = 3
+ABI_VERSION = 4
 TP_MAX_RANKS, TP_ROWS, TP_CTAS, TP_HEADER = 8, 4, 512, 256
 TP_STORE, TP_PARTIAL, TP_SWIGLU = 0, 1, 2
 
@@ -21,7 +21,9 @@ class W8A8AttnArgs(C.Structure):
                 ("q_norm", C.c_void_p), ("k_norm", C.c_void_p), ("eps", C.c_float), ("rope_cos", C.c_void_p),
                 ("rope_sin", C.c_void_p), ("inv_sk", C.c_float), ("inv_sv", C.c_float), ("a_k", C.c_float),
                 ("a_v", C.c_float), ("k_cache", C.c_void_p), ("v_cache", C.c_void_p), ("att", C.c_void_p),
-                ("scratch", C.c_void_p), ("scratch_bytes", C.c_size_t), ("att_amax", C.c_void_p)]
+                ("scratch", C.c_void_p), ("scratch_bytes", C.c_size_t), ("att_amax", C.c_void_p),
+                ("k_scale", C.c_void_p), ("inv_sk_ch", C.c_void_p), ("inv_sv_ch", C.c_void_p),
+                ("a_v_ch", C.c_void_p)]
 
 
 class W8A8TpComm(C.Structure):

@@ -237,6 +237,10 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
             __syncwarp();
             warp_norm_rope(buf, hd, p.qk_norm ? gains : nullptr, p.eps, p.inv_hd, tabs + 2 * m * hd,
                            tabs + (2 * m + 1) * hd, lane);
+            if (p.k_ch != nullptr) {                           // K per channel: its scale folded into q
+                for (int c = lane; c < hd; c += 32) buf[c] = fmul(buf[c], p.k_ch[kvh * hd + c]);
+                __syncwarp();
+            }
             float a = 0.f;
             for (int c = lane; c < hd; c += 32) a = nanmax(a, fabsf(buf[c]));
             a = warp_max(a);
@@ -258,8 +262,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
             int8_t* kdst = kc_p + ((size_t)kvh * T + pos) * hd;
             const float* vsrc = qkv_p + (size_t)m * qkv_dim + q_dim + kv_dim + (size_t)kvh * hd;
             for (int c = lane; c < hd; c += 32) {
-                const int8_t kq = (int8_t)to_i8(fmul(kbuf[c], p.inv_sk));
-                const int8_t vq = (int8_t)to_i8(fmul(vsrc[c], p.inv_sv));
+                const int8_t kq = (int8_t)to_i8(fmul(kbuf[c], p.inv_sk_ch ? p.inv_sk_ch[kvh * hd + c] : p.inv_sk));
+                const int8_t vq = (int8_t)to_i8(fmul(vsrc[c], p.inv_sv_ch ? p.inv_sv_ch[kvh * hd + c] : p.inv_sv));
                 kdst[c] = kq;
                 vc_p[((size_t)kvh * hd + c) * T + pos] = vq;
                 ks[(pos - t0) * hd + c] = kq;
@@ -403,12 +407,13 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
                 if (p.variant == 1) ssum += lsum[j][r];
             }
             const float o = i2f(acc);
+            const float av = p.a_v_ch ? p.a_v_ch[kvh * hd + c] : p.a_v;   // V per channel or per layer
             float out;
             if (p.variant == 0) {
-                out = fmul(o, p.a_v);
+                out = fmul(o, av);
             } else {
                 const float rq = fmul(sfu_recip(i2f(ssum)), 127.f);   // sum <= 127 T: exact in fp32
-                out = fmul(fmul(o, rq), p.a_v);
+                out = fmul(fmul(o, rq), av);
             }
             att_p[((size_t)m * H + h) * hd + c] = out;
             if (post) atomicMax(&amx[m], __float_as_uint(fabsf(out)));
@@ -555,6 +560,10 @@ __global__ void __launch_bounds__(kSbThreads, 1)
             for (int c = lane; c < hd; c += 32) buf[c] = src[c];
             __syncwarp();
             warp_norm_rope(buf, hd, p.qk_norm ? gains : nullptr, p.eps, p.inv_hd, tabs, tabs + hd, lane);
+            if (p.k_ch != nullptr) {                           // K per channel: its scale folded into q
+                for (int c = lane; c < hd; c += 32) buf[c] = fmul(buf[c], p.k_ch[kvh * hd + c]);
+                __syncwarp();
+            }
             float a = 0.f;
             for (int c = lane; c < hd; c += 32) a = nanmax(a, fabsf(buf[c]));
             a = warp_max(a);
@@ -574,8 +583,8 @@ __global__ void __launch_bounds__(kSbThreads, 1)
             int8_t* kdst = p.kc + (size_t)slot * p.slot_stride + ((size_t)kvh * T + pos) * hd;
             int8_t* vdst = p.vc + (size_t)slot * p.slot_stride + (size_t)kvh * hd * T + pos;
             for (int c = lane; c < hd; c += 32) {
-                const int8_t kq = (int8_t)to_i8(fmul(kb[c], p.inv_sk));
-                const int8_t vq = (int8_t)to_i8(fmul(vsrc[c], p.inv_sv));
+                const int8_t kq = (int8_t)to_i8(fmul(kb[c], p.inv_sk_ch ? p.inv_sk_ch[kvh * hd + c] : p.inv_sk));
+                const int8_t vq = (int8_t)to_i8(fmul(vsrc[c], p.inv_sv_ch ? p.inv_sv_ch[kvh * hd + c] : p.inv_sv));
                 kdst[c] = kq;
                 vdst[(size_t)c * T] = vq;
                 newk[c] = kq;
@@ -725,9 +734,10 @@ __global__ void __launch_bounds__(kSbThreads, 1)
             if (pr >= G * hd) break;
             const int r = pr / hd, c = pr % hd;
             const float o = i2f(acc[j]);
+            const float av = p.a_v_ch ? p.a_v_ch[kvh * hd + c] : p.a_v;   // V per channel or per layer
             float out;
-            if (p.variant == 0) out = fmul(o, p.a_v);
-            else out = fmul(fmul(o, fmul(sfu_recip(i2f(lsum[r])), 127.f)), p.a_v);   // sum <= 127 T: exact
+            if (p.variant == 0) out = fmul(o, av);
+            else out = fmul(fmul(o, fmul(sfu_recip(i2f(lsum[r])), 127.f)), av);   // sum <= 127 T: exact
             att[(size_t)(kvh * G + r) * hd + c] = out;
             am = max(am, __float_as_uint(fabsf(out)));
         }

@@ -345,6 +345,9 @@ static int attn_params(const W8A8AttnArgs* a, AttnParams* out) {
     p.inv_hd = inv_of(a->head_dim), p.cos = a->rope_cos, p.sin = a->rope_sin;
     p.inv_sk = a->inv_sk, p.inv_sv = a->inv_sv, p.a_k = a->a_k, p.a_v = a->a_v;
     p.kc = a->k_cache, p.vc = a->v_cache, p.att = a->att, p.amax_out = a->att_amax;
+    if ((a->k_scale == nullptr) != (a->inv_sk_ch == nullptr) || (a->inv_sv_ch == nullptr) != (a->a_v_ch == nullptr))
+        return W8A8_EINVAL;                                   // a part is per channel or not, whole
+    p.k_ch = a->k_scale, p.inv_sk_ch = a->inv_sk_ch, p.inv_sv_ch = a->inv_sv_ch, p.a_v_ch = a->a_v_ch;
     *out = p;
     return W8A8_OK;
 }

@@ -95,6 +95,12 @@ struct AttnParams {
     int slots;                // batched decode: sequences (one row each; grid z), or 0
     size_t slot_stride;       // bytes between consecutive slots' caches (batched decode)
     uint32_t* amax_out;       // [rows or slots] max|att| per row by atomic max, or null (decode chain)
+    // per cache channel [kv_heads * head_dim], or null for the per-layer scalars:
+    // K's scale (folded into q before its quantization) and 1 / s_k; 1 / s_v, a_v
+    const float* k_ch;
+    const float* inv_sk_ch;
+    const float* inv_sv_ch;
+    const float* a_v_ch;
     TpCtx tp;                 // tensor-parallel decode: max|att| words of this CTA to every rank
     uint64_t* amax_ll_out;
 };

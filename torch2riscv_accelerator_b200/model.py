@@ -25,7 +25,7 @@ import numpy as np
 import torch
 
 from . import ops
-from .weights import kv_consts
+from .weights import layer_kv_consts
 
 I8, F32, I32 = torch.int8, torch.float32, torch.int32
 CHUNK = 16                                         # rows of the GEMV / attention path (the reference's M)
@@ -33,9 +33,12 @@ PREFILL = 256                                      # rows per tensor-core prefil
 CHAIN_ROWS = 4                                     # rows of the decode GEMV path (the latency chain)
 
 
-def _upload(obj, cfg, qw, kv_scales):
+def _upload(obj, cfg, qw, kv_scales, kv_cols=None):
     """The model's tensors in HBM (int8 rows + fp32 scales, gains, RoPE tables)
-    and the per-layer KV constants, as attributes of obj."""
+    and the per-layer KV constants, as attributes of obj. kv_cols: the cache
+    channels this decoder holds (a shard's KV heads) of per-channel scales; the
+    constants come from the whole row (whether a layer is per channel is the
+    whole model's), then the channels are sliced."""
     t = lambda a, dt=None: torch.as_tensor(np.ascontiguousarray(a), dtype=dt).to(obj.dev)
     obj.emb_q, obj.emb_s = t(qw.emb_q, I8), t(qw.emb_s, F32)
     if cfg.tied and qw.cls_q is qw.emb_q:
@@ -46,14 +49,19 @@ def _upload(obj, cfg, qw, kv_scales):
     obj.cos, obj.sin = t(qw.cos, F32), t(qw.sin, F32)
     obj.layers = [{k: t(v) for k, v in lw.items()} for lw in qw.layers]
     kv = np.asarray(kv_scales, np.float32)
-    obj.consts = [kv_consts(kv[l, 0], kv[l, 1], cfg.head_dim) for l in range(cfg.layers)]
+    cols = kv_cols if kv_cols is not None else slice(0, cfg.kv_dim)
+    if kv.shape[:2] != (cfg.layers, 2) or (kv.ndim == 3 and len(range(kv.shape[2])[cols]) != cfg.kv_dim):
+        raise ValueError(f"KV scales {kv.shape}: [layers, 2] or [layers, 2, kv_dim] expected")
+    both = [layer_kv_consts(kv[l], cfg.head_dim) for l in range(cfg.layers)]
+    obj.consts = [c for c, _ in both]
+    obj.kv_ch = [None if ch is None else {k: t(v[cols], F32) for k, v in ch.items()} for _, ch in both]
 
 
 class DeviceDecoder:
-    def __init__(self, cfg, qw, kv_scales, device="cuda", max_rows=CHUNK, prefill_rows=PREFILL):
+    def __init__(self, cfg, qw, kv_scales, device="cuda", max_rows=CHUNK, prefill_rows=PREFILL, kv_cols=None):
         cfg.validate()
         self.cfg, self.dev, self.max_rows = cfg, torch.device(device), max_rows
-        _upload(self, cfg, qw, kv_scales)
+        _upload(self, cfg, qw, kv_scales, kv_cols)
         L, Hk, T, hd = cfg.layers, cfg.kv_heads, cfg.seq_len, cfg.head_dim
         self.kc = torch.zeros(L, Hk, T, hd, dtype=I8, device=self.dev)
         self.vc = torch.zeros(L, Hk, hd, T, dtype=I8, device=self.dev)      # V transposed per head
@@ -91,7 +99,8 @@ class DeviceDecoder:
             a = self._args[(rows, chain)] = [
                 ops.attn_args(c, rows, self.pos, self.qkv, self.kc[l], self.vc[l], self.att, self.consts[l],
                               self.cos, self.sin, self.attn_scratch, self.layers[l].get("q_norm"),
-                              self.layers[l].get("k_norm"), att_amax=self.amax_att[l] if chain else None)
+                              self.layers[l].get("k_norm"), att_amax=self.amax_att[l] if chain else None,
+                              ch=self.kv_ch[l])
                 for l in range(c.layers)]
         return a
 
@@ -167,7 +176,8 @@ class DeviceDecoder:
             c, w = self.cfg, self.layers[l]
             a = self._sub_args[(l, j, m)] = ops.attn_args(
                 c, m, self.pos[j:j + m], self.qkv[j:j + m], self.kc[l], self.vc[l], self.att[j:j + m],
-                self.consts[l], self.cos, self.sin, self.attn_scratch, w.get("q_norm"), w.get("k_norm"))
+                self.consts[l], self.cos, self.sin, self.attn_scratch, w.get("q_norm"), w.get("k_norm"),
+                ch=self.kv_ch[l])
         return a
 
     def _q(self, rows, k):
@@ -299,12 +309,12 @@ class BatchDecoder:
     slots (grid z = slot), the MoE FFN in 16-row groups, the classifier GEMM for
     all D rows. Each slot's results equal a one-sequence decode bit for bit."""
 
-    def __init__(self, cfg, qw, kv_scales, slots, device="cuda"):
+    def __init__(self, cfg, qw, kv_scales, slots, device="cuda", kv_cols=None):
         cfg.validate()
         if slots < 1:
             raise ValueError("at least one slot")
         self.cfg, self.dev, self.slots = cfg, torch.device(device), slots
-        _upload(self, cfg, qw, kv_scales)
+        _upload(self, cfg, qw, kv_scales, kv_cols)
         D, L, Hk, T, hd = slots, cfg.layers, cfg.kv_heads, cfg.seq_len, cfg.head_dim
         self.kc = torch.zeros(D, L, Hk, T, hd, dtype=I8, device=self.dev)
         self.vc = torch.zeros(D, L, Hk, hd, T, dtype=I8, device=self.dev)   # V transposed per head
@@ -323,7 +333,7 @@ class BatchDecoder:
             self.moe_scratch = ops.moe_scratch(CHUNK, cfg.dim, cfg.top_k, cfg.expert_hidden, self.dev)
         self.args = [ops.attn_args(cfg, 1, self.pos, self.qkv, self.kc[0, l], self.vc[0, l], self.att,
                                    self.consts[l], self.cos, self.sin, self.attn_scratch, w.get("q_norm"),
-                                   w.get("k_norm"))
+                                   w.get("k_norm"), ch=self.kv_ch[l])
                      for l, w in enumerate(self.layers)]
         self.graph = None
 

@@ -227,16 +227,20 @@ def attn_scratch(rows, heads, kv_heads, head_dim, seq_len, device):
 VARIANTS = {"norm": 0, "qsum": 1}
 
 
-def attn_args(cfg, rows, pos, qkv, kc, vc, att, consts, cos, sin, scratch, q_norm=None, k_norm=None, att_amax=None):
+def attn_args(cfg, rows, pos, qkv, kc, vc, att, consts, cos, sin, scratch, q_norm=None, k_norm=None, att_amax=None,
+              ch=None):
     """The W8A8AttnArgs block of one layer (kept alive by the caller: a CUDA
-    graph replays the pointers it captured)."""
+    graph replays the pointers it captured). ch: the per-channel KV constants
+    (device tensors k_scale / inv_sk_ch, inv_sv_ch / a_v_ch) or None."""
     inv_sk, inv_sv, a_k, a_v = consts
+    ch = ch or {}
     return _lib.W8A8AttnArgs(
         rows=rows, heads=cfg.heads, kv_heads=cfg.kv_heads, head_dim=cfg.head_dim, seq_len=cfg.seq_len,
         variant=VARIANTS[cfg.attn], pos=_p(pos), qkv=_p(qkv), q_norm=_p(q_norm), k_norm=_p(k_norm),
         eps=float(np.float32(cfg.eps)), rope_cos=_p(cos), rope_sin=_p(sin), inv_sk=float(inv_sk),
         inv_sv=float(inv_sv), a_k=float(a_k), a_v=float(a_v), k_cache=_p(kc), v_cache=_p(vc), att=_p(att),
-        scratch=_p(scratch), scratch_bytes=scratch.numel(), att_amax=_p(att_amax))
+        scratch=_p(scratch), scratch_bytes=scratch.numel(), att_amax=_p(att_amax), k_scale=_p(ch.get("k_scale")),
+        inv_sk_ch=_p(ch.get("inv_sk_ch")), inv_sv_ch=_p(ch.get("inv_sv_ch")), a_v_ch=_p(ch.get("a_v_ch")))
 
 
 def attn(args):

@@ -63,6 +63,12 @@ def local_config(cfg, ranks):
                      vocab=cfg.vocab // ranks)
 
 
+def kv_columns(cfg, rank, ranks):
+    """The cache channels of a rank's KV heads (per-channel KV scales)."""
+    w = cfg.kv_dim // ranks
+    return slice(rank * w, (rank + 1) * w)
+
+
 def shard(cfg, qw, rank, ranks):
     """Rank `rank`'s shard of the quantized model (a host-side view; the
     quantization is the whole model's, so scales are unchanged)."""
@@ -173,7 +179,7 @@ class TpDecoder(DeviceDecoder):
         self.full_cfg, self.comm = cfg, comm
         sh = shard(cfg, qw, comm.rank, comm.ranks)
         super().__init__(local_config(cfg, comm.ranks), sh, kv_scales, device=device, max_rows=max_rows,
-                         prefill_rows=prefill_rows)
+                         prefill_rows=prefill_rows, kv_cols=kv_columns(cfg, comm.rank, comm.ranks))
         self.vocab_offset = sh.vocab_offset
         R, L = self.rows_cap, cfg.layers
         z = lambda *s, dt=F32: torch.zeros(*s, dtype=dt, device=self.dev)
@@ -389,7 +395,8 @@ class TpBatchDecoder(BatchDecoder):
         self.rank, self.ranks = dist.get_rank(group), dist.get_world_size(group)
         self.full_cfg = cfg
         sh = shard(cfg, qw, self.rank, self.ranks)
-        super().__init__(local_config(cfg, self.ranks), sh, kv_scales, slots, device=device)
+        super().__init__(local_config(cfg, self.ranks), sh, kv_scales, slots, device=device,
+                         kv_cols=kv_columns(cfg, self.rank, self.ranks))
         D = slots
         z = lambda *s, dt=F32: torch.zeros(*s, dtype=dt, device=self.dev)
         self.acc, self.ybuf, self.amax_bits = z(D, cfg.dim, dt=I32), z(D, cfg.dim), z(D, dt=I32)

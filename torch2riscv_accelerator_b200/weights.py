@@ -78,15 +78,38 @@ def kv_consts(s_k, s_v, head_dim):
     return (F(1.0 / s_k), F(1.0 / s_v), F(float(s_k) / np.sqrt(head_dim)), F(float(s_v) / 127.0))
 
 
+def layer_kv_consts(kv_l, head_dim):
+    """A layer's KV constants from its scales: [2] (per layer) or [2, kv_dim]
+    (per cache channel, `calibrate_kv(channel=...)`; a part whose row holds a
+    single value is per layer), as `hf_generic.SaCache` (:153-187) computes them:
+    ((inv_sk, inv_sv, a_k, a_v) scalars, per-channel arrays or None). K per
+    channel: k_scale = s_k (folded into q), inv_sk_ch = F(1) / s_k, a_k =
+    F(1 / sqrt(head_dim)); V per channel: inv_sv_ch = F(1) / s_v, a_v_ch =
+    s_v * F(1/127)."""
+    kv_l = np.asarray(kv_l, F)
+    if kv_l.ndim == 1:
+        return kv_consts(kv_l[0], kv_l[1], head_dim), None
+    inv_sk, inv_sv, a_k, a_v = kv_consts(kv_l[0, 0], kv_l[1, 0], head_dim)
+    ch = {}
+    if not np.all(kv_l[0] == kv_l[0, 0]):
+        ch["k_scale"], ch["inv_sk_ch"] = kv_l[0].copy(), (F(1.0) / kv_l[0]).astype(F)
+        a_k = F(1.0 / np.sqrt(head_dim))
+    if not np.all(kv_l[1] == kv_l[1, 0]):
+        ch["inv_sv_ch"], ch["a_v_ch"] = (F(1.0) / kv_l[1]).astype(F), (kv_l[1] * F(1.0 / 127.0)).astype(F)
+    return (inv_sk, inv_sv, a_k, a_v), (ch or None)
+
+
 class QuantWeights:
     """The quantized model on the host: int8 rows + fp32 scales per linear layer
     (q|k|v rows fused as wqkv, w1|w3 as w13, `llm/export_w8a8.py:90-93`),
     fp32 gains, the int8 embedding (shared with a tied classifier)."""
 
-    def __init__(self, cfg, seed=0, gains="ones", layers=None, with_cls=True, calib_tokens=None):
+    def __init__(self, cfg, seed=0, gains="ones", layers=None, with_cls=True, calib_tokens=None, kv_channel=""):
         """calib_tokens: token ids of an fp32 calibration run; the static KV
         scales it gives are in self.kv_scales (`compiler/frontend/qhf.py:245-251`
-        calibrate_kv: max|k|, max|v| per layer after RoPE / QK-norm, / 127)."""
+        calibrate_kv: max|k|, max|v| per layer after RoPE / QK-norm, / 127);
+        kv_channel "k" / "v" / "kv": those parts per cache channel
+        (`compiler/frontend/hf_generic.py:466-491`), kv_scales [layers, 2, kv_dim]."""
         cfg.validate()
         self.cfg, self.seed = cfg, seed
         g = lambda n, l=-1: gen_tensor(cfg, seed, n, l, gains)
@@ -99,7 +122,7 @@ class QuantWeights:
         cal = None if calib_tokens is None else tok[np.asarray(calib_tokens)].astype(F)
         del tok
         L = cfg.layers if layers is None else layers
-        amax = np.zeros((L, 2), F)
+        amax = np.zeros((L, 2, cfg.kv_dim), F)
         self.layers = []
         for l in range(L):
             t = {"rms_att": g("rms_att", l), "rms_ffn": g("rms_ffn", l)}
@@ -121,7 +144,40 @@ class QuantWeights:
             if cal is not None:
                 cal, amax[l, 0], amax[l, 1] = calibrate_layer(cfg, cal, t, f32, self.cos, self.sin)
             self.layers.append(t)
-        self.kv_scales = (np.maximum(amax, F(1e-8)) / F(127.0)).astype(F) if cal is not None else None
+        self.kv_amax = amax if cal is not None else None
+        self.kv_scales = kv_scales_of(amax, kv_channel) if cal is not None else None
+
+
+def kv_scales_of(amax, channel=""):
+    """Static KV scales from the calibration maxima amax [layers, 2, kv_dim]
+    (`hf_generic.calibrate_kv` :466-491): max / 127 per layer ([layers, 2]), or
+    with channel "k" / "v" / "kv" those parts per cache channel and the others'
+    rows the layer's single value ([layers, 2, kv_dim]); at least 1e-8."""
+    amax = np.asarray(amax, F)
+    if not channel:
+        return (np.maximum(amax.max(-1), F(1e-8)) / F(127.0)).astype(F)
+    out = np.repeat(amax.max(-1, keepdims=True), amax.shape[-1], -1)
+    for j, part in enumerate("kv"):
+        if part in channel:
+            out[:, j] = amax[:, j]
+    return (np.maximum(out, F(1e-8)) / F(127.0)).astype(F)
+
+
+def calibrate_kv(cfg, w, tokens, channel=""):
+    """KV scales from an fp32 run of the model w (fp32 tensors in the
+    reference's naming, `llm/checkpoint.py:33-59`) over `tokens` from position
+    0: the maxima of |k|, |v| per cache channel as they are written (after
+    QK-norm and RoPE), then kv_scales_of (`hf_generic.calibrate_kv`)."""
+    cos, sin = rope_tables(cfg)
+    x = w["tok"][np.asarray(tokens)].astype(F)
+    amax = np.zeros((cfg.layers, 2, cfg.kv_dim), F)
+    for l in range(cfg.layers):
+        t = {"rms_att": w["rms_att"][l], "rms_ffn": w["rms_ffn"][l]}
+        if cfg.qk_norm:
+            t["q_norm"], t["k_norm"] = w["q_norm"][l], w["k_norm"][l]
+        f32 = {n: w[n][l] for n in ("wq", "wk", "wv", "wo", "w1", "w3", "w2")}
+        x, amax[l, 0], amax[l, 1] = calibrate_layer(cfg, x, t, f32, cos, sin)
+    return kv_scales_of(amax, channel)
 
 
 def _rms32(x, g, eps):
@@ -137,7 +193,7 @@ def _swapneg(v):
 def calibrate_layer(cfg, x, t, f32, cos, sin):
     """One layer of the fp32 model (`compiler/frontend/qhf.py:210-242`
     Fp32Model.forward, all calibration tokens at once with a causal mask):
-    returns (x after the layer, max|k|, max|v|)."""
+    returns (x after the layer, max|k|, max|v| per cache channel [kv_dim])."""
     c = cfg
     n = x.shape[0]
     H, Hk, hd, G = c.heads, c.kv_heads, c.head_dim, c.group
@@ -171,7 +227,7 @@ def calibrate_layer(cfg, x, t, f32, cos, sin):
     else:
         h1, h3 = xb @ f32["w1"].T, xb @ f32["w3"].T
         x = (x + ((h1 / (1 + np.exp(-h1))) * h3) @ f32["w2"].T).astype(F)
-    return x, F(np.abs(k).max()), F(np.abs(v).max())
+    return x, np.abs(k).max(axis=0).reshape(-1), np.abs(v).max(axis=0).reshape(-1)
 
 
 def from_fp32(cfg, w):
