@@ -33,7 +33,7 @@ extern "C" {
 #define W8A8_ECUDA 3    /* the CUDA launch failed (cudaGetLastError) */
 #define W8A8_ESCRATCH 4 /* the scratch buffer is smaller than required */
 
-#define W8A8_ABI_VERSION 4
+#define W8A8_ABI_VERSION 5
 #define W8A8_MAX_ROWS 16 /* query rows per call (decode: 1, prefill chunk: 16) */
 
 /* ABI version (W8A8_ABI_VERSION) and a message for a status code. */
@@ -41,7 +41,8 @@ int w8a8_abi_version(void);
 const char* w8a8_status_string(int status);
 
 /* Elementwise SFU: func 0 EXP, 1 RECIP, 2 RSQRT (llm/sfu.py:69, :85, :99),
- * 3 SiLU g*RECIP(1 + EXP(-g)) (llm/ref_model.py:249). */
+ * 3 SiLU g*RECIP(1 + EXP(-g)) (llm/ref_model.py:249), 4 GELU-tanh
+ * g*RECIP(EXP(g*(A + (g*g)*B)) + 1) (compiler/frontend/hf_generic.py:840-856). */
 int w8a8_sfu(int func, const float* x, float* y, int64_t n, void* stream);
 
 /* Per-token dynamic int8 of `rows` rows of k values: s_x = max|x| * F(1/127),
@@ -124,6 +125,19 @@ int w8a8_ffn_swiglu(const float* x, const float* norm_g, float eps, int rows, in
 int w8a8_ffn_swiglu_chain(const float* x, const float* norm_g, float eps, int rows, int k, const int8_t* w_gate,
                           const float* s_gate, const int8_t* w_up, const float* s_up, int hidden, float* h,
                           uint32_t* h_amax, uint32_t* clear, int clear_n, void* stream);
+
+/* Gated activations of the FFN dispatch: SiLU (Llama, Qwen3, Granite) or GELU's
+ * tanh approximation (Gemma: hf_generic.SaGELUTanh, :840-856, with
+ * A = F(-2 sqrt(2/pi)), B = F(-2 sqrt(2/pi) * 0.044715) as the reference's
+ * host computes them). w8a8_ffn_gated / w8a8_gemm_gated are w8a8_ffn_swiglu /
+ * w8a8_gemm_swiglu with h = act(g) * u. */
+#define W8A8_ACT_SILU 0
+#define W8A8_ACT_GELU_TANH 1
+int w8a8_ffn_gated(const float* x, const float* norm_g, float eps, int rows, int k, const int8_t* w_gate,
+                   const float* s_gate, const int8_t* w_up, const float* s_up, int hidden, int act, float* h,
+                   int8_t* h_q, float* s_h, void* scratch, size_t scratch_bytes, void* stream);
+int w8a8_gemm_gated(const int8_t* xq, const float* s_x, int rows, int k, const int8_t* w_gate, const float* s_gate,
+                    const int8_t* w_up, const float* s_up, int hidden, int act, float* h, void* stream);
 
 /* w8a8_ffn_swiglu with the requantization of h, for a caller that cannot hand
  * over a scratch buffer. This entry point has no counterpart in the reference:
@@ -378,6 +392,7 @@ typedef struct {
     uint64_t* key_out;           /* STORE: per-CTA key block, or NULL */
     int n_offset;                /* global index of output 0 (this rank's vocabulary slice) */
     float* s_x_out;              /* [rows] the prologue's scales, or NULL */
+    int act;                     /* SWIGLU: W8A8_ACT_SILU or W8A8_ACT_GELU_TANH */
 } W8A8TpLinearArgs;
 int w8a8_tp_linear(const W8A8TpLinearArgs* a, void* stream);
 

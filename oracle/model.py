@@ -185,7 +185,7 @@ class OracleDecoder:
                 xq, s_x = N.quant_act(xn)
                 h1 = self._lin(xq, s_x, ("w1", l), t["w1"], t["s_w1"])
                 h3 = self._lin(xq, s_x, ("w3", l), t["w3"], t["s_w3"])
-                hq, s_h = N.quant_act(N.silu_gate(h1, h3))
+                hq, s_h = N.quant_act(N.gate(h1, h3, getattr(c, "act", "silu")))
                 x = (x + self._lin(hq, s_h, ("w2", l), t["w2"], t["s_w2"])).astype(F)
             if trace is not None:
                 trace.setdefault("x", []).append(x.copy())

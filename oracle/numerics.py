@@ -251,6 +251,25 @@ def silu_gate(g, u):
     return (((g * sig).astype(F)) * u).astype(F)
 
 
+GELU_A = F(-2.0 * np.sqrt(2.0 / np.pi))                  # `compiler/frontend/hf_generic.py:848-849`
+GELU_B = F(-2.0 * np.sqrt(2.0 / np.pi) * 0.044715)
+
+
+def gelu_gate(g, u):
+    """h = (g*RECIP(EXP(z) + 1))*u, z = g*(A + (g*g)*B): GELU's tanh approximation
+    with multiplies, adds, EXP and RECIP only (`compiler/frontend/hf_generic.py:840-856`
+    SaGELUTanh; the gated MLP's act(gate) * up)."""
+    g = np.asarray(g, F)
+    with np.errstate(over="ignore", invalid="ignore"):                  # (inf, NaN: as the device)
+        z = (g * (GELU_A + ((g * g).astype(F) * GELU_B).astype(F)).astype(F)).astype(F)
+        sig = sfu_recip((sfu_exp(z) + F(1)).astype(F))
+        return (((g * sig).astype(F)) * u).astype(F)
+
+
+def gate(g, u, act="silu"):
+    return gelu_gate(g, u) if act == "gelu_tanh" else silu_gate(g, u)
+
+
 def quantize_rows(wt):
     """Offline per-output-channel int8 (`llm/ref_model.py:142-148`;
     `hf_generic._quantize_rows` :558-565 sets s = 1 for all-zero rows):

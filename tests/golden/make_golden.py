@@ -24,6 +24,7 @@ Fixtures:
                 device SFU.
   hf_qwen3_ch.npz  the same tiny Qwen3 with KV scales per cache channel from
                 hf_generic.calibrate_kv(channel="kv"), through SaDecoder
+  gelu.npz      hf_generic.SaGELUTanh (GELU-tanh gate) under the device SFU
   moe.npz       hf_generic.QMixtralMoe rows of a synthetic Mixtral block
                 (compiler/tests/test_hf_moe.synthetic_model's shape).
   tiny_a_d8.w8a8  tiny model "a" of dm_tiny.npz written by the reference's
@@ -346,6 +347,22 @@ def gen_hf_channel():
     print(f"  hf QSUM per-channel argmax {hlog.argmax(1).tolist()}")
 
 
+def gen_gelu():
+    """hf_generic.SaGELUTanh (the GELU-tanh gate of Gemma-class models) under the
+    device SFU on ranges, random values and special values."""
+    import torch
+    import hf_generic as H
+    import test_hf_generic as THG
+    torch.set_grad_enabled(False)
+    rng = np.random.default_rng(31)
+    x = np.concatenate([np.linspace(-12, 12, 2401, dtype=F), (rng.standard_normal(4000) * 3).astype(F),
+                        np.array([0.0, -0.0, 1e-30, -1e-30, 60.0, -60.0, 1e4, -1e4, 3e38, -3e38, np.inf, -np.inf,
+                                  np.nan], F)]).astype(F)
+    with THG.device_sfu():
+        y = H.SaGELUTanh()(torch.from_numpy(x)).numpy().astype(F)
+    save("gelu.npz", x=x, y=y, a=np.float32(H.SaGELUTanh.A), b=np.float32(H.SaGELUTanh.B))
+
+
 def gen_moe():
     import torch
     import hf_generic as H
@@ -394,11 +411,11 @@ def gen_files():
 def main():
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--skip-c0", action="store_true")
-    ap.add_argument("--only", help="comma list: sfu,convert,tiny,c0,hf,hfch,moe,files")
+    ap.add_argument("--only", help="comma list: sfu,convert,tiny,c0,hf,hfch,gelu,moe,files")
     a = ap.parse_args()
     only = set(a.only.split(",")) if a.only else None
     steps = [("sfu", gen_sfu), ("convert", gen_convert), ("tiny", gen_dm_tiny), ("c0", gen_dm_c0),
-             ("hf", gen_hf), ("hfch", gen_hf_channel), ("moe", gen_moe), ("files", gen_files)]
+             ("hf", gen_hf), ("hfch", gen_hf_channel), ("gelu", gen_gelu), ("moe", gen_moe), ("files", gen_files)]
     for name, fn in steps:
         if (only and name not in only) or (name == "c0" and a.skip_c0):
             continue

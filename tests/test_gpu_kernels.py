@@ -51,6 +51,27 @@ def test_silu_gate_bit_exact():
     assert ok
 
 
+def same_bits_nan(got, want):
+    """Bit-exact, except that a NaN equals any NaN: a NaN made by an invalid
+    operation (-inf * 0, NaN inputs) carries the hardware's default pattern
+    (x86 0xFFC00000, the GPU's canonical one), not a value of the algorithm."""
+    g, w = np.asarray(got, F).ravel(), np.asarray(want, F).ravel()
+    gn, wn = np.isnan(g), np.isnan(w)
+    bad = np.flatnonzero((gn != wn) | (~gn & (g.view(np.uint32) != w.view(np.uint32))))
+    return bad.size == 0, bad[:5]
+
+
+def test_gelu_gate_bit_exact_with_reference():
+    """GELU-tanh (SaGELUTanh under the device SFU, gelu.npz) on the device,
+    and the oracle's restatement on random bit patterns."""
+    g = golden("gelu.npz")
+    ok, bad = same_bits_nan(host(ops.sfu(ops.SFU_GELU, cu(g["x"]))), g["y"])
+    assert ok, bad
+    x = np.random.default_rng(4).integers(0, 2**32, 1 << 18, dtype=np.uint64).astype(np.uint32).view(F)
+    ok, bad = same_bits_nan(host(ops.sfu(ops.SFU_GELU, cu(x))), N.gelu_gate(x, np.ones_like(x)))
+    assert ok, bad
+
+
 # ------------------------------------------------------------ vector ops
 @pytest.mark.parametrize("k", [48, 288, 1024, 3072, 100])
 def test_quant_act_and_rmsnorm(k):

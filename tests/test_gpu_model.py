@@ -117,6 +117,27 @@ def test_per_channel_kv_c2_dims_prefill_and_decode():
         assert dev.forward(int(toks[p])).tobytes() == ora.forward(int(toks[p]), p).tobytes()
 
 
+@pytest.mark.parametrize("attn", ["qsum", "norm"])
+def test_gelu_tanh_model_equals_oracle(attn):
+    """A Gemma-style gated MLP (GELU-tanh gate, hf_generic.SaGELUTanh): a
+    40-row tensor-core prefill, a 9-row chunk (the 5-16 row linear path) and
+    decode rows (the GEMV path), logits and KV bit-exact with the oracle."""
+    cfg = C.ModelConfig("gelu", 128, 256, 2, 8, 2, 16, 200, 128, theta=1e4, eps=1e-6, tied=True, attn=attn,
+                        rope="hf", act="gelu_tanh")
+    w = W.fp32_model(cfg, 8, gains="random", std=0.1)
+    kv = W.calibrate_kv(cfg, w, np.arange(10))
+    dev = LlamaDevice((cfg, W.from_fp32(cfg, w), kv))
+    ora = OM.OracleDecoder(cfg, OM.quantize_model(cfg, w), kv)
+    toks = np.random.default_rng(5).integers(0, cfg.vocab, 52)
+    assert dev.prefill(toks[:40]).tobytes() == ora.forward_rows(toks[:40], range(40)).tobytes()
+    assert dev.prefill(toks[40:49]).tobytes() == ora.forward_rows(toks[40:49], range(40, 49)).tobytes()
+    for p in range(49, 52):
+        assert dev.forward(int(toks[p])).tobytes() == ora.forward(int(toks[p]), p).tobytes()
+    for l in range(cfg.layers):
+        k, v = dev.dec.kv_rows(l, 52)
+        assert np.array_equal(k, ora.kc[l, :52]) and np.array_equal(v, ora.vc[l, :52])
+
+
 def test_prefill_chunks_equal_decode_steps():
     """A prompt prefilled in 16-row chunks (the last at P - 16) gives the same
     KV cache and last logits as feeding it token by token

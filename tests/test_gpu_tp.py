@@ -23,17 +23,18 @@ PREFILL, CHUNK2, FWD, STEPS = 40, 10, 5, 6
 CFG = C.C2.with_(layers=2, vocab=4096)
 
 
-def _model(kv=None):
+def _model(kv=None, act="silu"):
     """The test model: the quantized weights are elementwise functions of the
     seed (identical in every process); the KV scales come from one fp32
     calibration run (BLAS sums), made once in the parent and handed to the ranks."""
+    cfg = CFG.with_(act=act)
     if kv is None:
-        qw = W.QuantWeights(CFG, seed=7, gains="random", calib_tokens=np.arange(8))
+        qw = W.QuantWeights(cfg, seed=7, gains="random", calib_tokens=np.arange(8))
         kv = qw.kv_scales
     else:
-        qw = W.QuantWeights(CFG, seed=7, gains="random")
-    toks = np.random.default_rng(3).integers(0, CFG.vocab, PREFILL + CHUNK2 + FWD)
-    return CFG, qw, np.asarray(kv, np.float32), toks
+        qw = W.QuantWeights(cfg, seed=7, gains="random")
+    toks = np.random.default_rng(3).integers(0, cfg.vocab, PREFILL + CHUNK2 + FWD)
+    return cfg, qw, np.asarray(kv, np.float32), toks
 
 
 def _run(dev, toks):
@@ -53,7 +54,7 @@ def _run(dev, toks):
     return out
 
 
-def _worker(rank, ranks, port, path, kv):
+def _worker(rank, ranks, port, path, kv, act):
     from torch2riscv_accelerator_b200 import ops
     from torch2riscv_accelerator_b200.tp import TpLlamaDevice
     torch.cuda.set_device(rank)
@@ -61,7 +62,7 @@ def _worker(rank, ranks, port, path, kv):
                             timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", rank))
     dev = None
     try:
-        cfg, qw, kv, toks = _model(kv)
+        cfg, qw, kv, toks = _model(kv, act)
         dev = TpLlamaDevice((cfg, qw, kv))
         out = _run(dev, toks)
         torch.cuda.synchronize()
@@ -80,14 +81,14 @@ def _port():
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("ranks", [2, 4, 8])
-def test_tp_equals_one_gpu(ranks, tmp_path):
+@pytest.mark.parametrize("ranks,act", [(2, "silu"), (2, "gelu_tanh"), (4, "silu"), (8, "silu")])
+def test_tp_equals_one_gpu(ranks, act, tmp_path):
     if torch.cuda.device_count() < ranks:
         pytest.skip(f"needs {ranks} GPUs")
     from torch2riscv_accelerator_b200.runtime import LlamaDevice
     path = str(tmp_path / "tp")
-    cfg, qw, kv, toks = _model()
-    mp.spawn(_worker, args=(ranks, _port(), path, kv), nprocs=ranks, join=True)
+    cfg, qw, kv, toks = _model(act=act)
+    mp.spawn(_worker, args=(ranks, _port(), path, kv, act), nprocs=ranks, join=True)
     ref = _run(LlamaDevice((cfg, qw, kv)), toks)
     for r in range(ranks):
         got = np.load(f"{path}.{r}.npz")

@@ -184,3 +184,15 @@ def test_per_channel_calibration_matches_the_reference():
     consts, ch = W.layer_kv_consts(k_only[0], cfg.head_dim)
     assert set(ch) == {"k_scale", "inv_sk_ch"} and consts[2] == np.float32(1.0 / np.sqrt(cfg.head_dim))
 
+
+def test_gelu_gate_equals_reference():
+    """The oracle's GELU-tanh gate equals hf_generic.SaGELUTanh under the device
+    SFU bit for bit (ranges, random values, +-0, huge, inf, NaN), with the
+    reference's constants."""
+    g = golden("gelu.npz")
+    assert g["a"] == N.GELU_A and g["b"] == N.GELU_B
+    y = N.gelu_gate(g["x"], np.float32(1))
+    assert np.array_equal(y.view(np.uint32), g["y"].view(np.uint32))     # (NumPy and torch: the same host NaN)
+    with pytest.raises(ValueError):
+        C.C4.with_(act="gelu_tanh").validate()                # MoE experts are SiLU
+

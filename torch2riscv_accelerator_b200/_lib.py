@@ -10,7 +10,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libw8a8_b200.so")
 
 W8A8_OK, W8A8_EINVAL, W8A8_EALIGN, W8A8_ECUDA, W8A8_ESCRATCH = 0, 1, 2, 3, 4
-ABI_VERSION = 4
+ABI_VERSION = 5
+ACT_SILU, ACT_GELU_TANH = 0, 1
 TP_MAX_RANKS, TP_ROWS, TP_CTAS, TP_HEADER = 8, 4, 512, 256
 TP_STORE, TP_PARTIAL, TP_SWIGLU = 0, 1, 2
 
@@ -37,7 +38,8 @@ class W8A8TpLinearArgs(C.Structure):
                 ("resid", C.c_void_p), ("x_out", C.c_void_p), ("norm_g", C.c_void_p), ("eps", C.c_float),
                 ("amax_in", C.c_void_p), ("w", C.c_void_p), ("s_w", C.c_void_p), ("w_up", C.c_void_p),
                 ("s_up", C.c_void_p), ("epilogue", C.c_int), ("y", C.c_void_p), ("part_out", C.c_void_p),
-                ("amax_out", C.c_void_p), ("key_out", C.c_void_p), ("n_offset", C.c_int), ("s_x_out", C.c_void_p)]
+                ("amax_out", C.c_void_p), ("key_out", C.c_void_p), ("n_offset", C.c_int), ("s_x_out", C.c_void_p),
+                ("act", C.c_int)]
 
 
 def tp_part_words(ranks, n):
@@ -73,6 +75,8 @@ PROTOTYPES = {
     "w8a8_ffn_scratch_bytes": (Z, [I]),
     "w8a8_ffn_swiglu": (I, [P, P, F, I, I, P, P, P, P, I, P, P, P, P, Z, P]),
     "w8a8_ffn_swiglu_noalloc": (I, [P, P, F, I, I, P, P, P, P, I, P, P, P, P]),
+    "w8a8_ffn_gated": (I, [P, P, F, I, I, P, P, P, P, I, I, P, P, P, P, Z, P]),
+    "w8a8_gemm_gated": (I, [P, P, I, I, P, P, P, P, I, I, P, P]),
     "w8a8_quant_rows": (I, [P, P, F, I, I, P, P, P]),
     "w8a8_gemm": (I, [P, P, I, I, P, P, I, P, P, P, P]),
     "w8a8_gemm_swiglu": (I, [P, P, I, I, P, P, P, P, I, P, P]),

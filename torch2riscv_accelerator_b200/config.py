@@ -38,6 +38,7 @@ class ModelConfig:
     experts: int = 0
     top_k: int = 0
     expert_hidden: int = 0
+    act: str = "silu"                  # the gated MLP's activation: "silu" or "gelu_tanh" (Gemma-class)
 
     @property
     def q_dim(self):
@@ -73,6 +74,8 @@ class ModelConfig:
             raise ValueError(f"{self.name}: attn {self.attn!r} / rope {self.rope!r}")
         if self.moe and not (1 <= self.top_k <= self.experts <= 64 and self.expert_hidden % 16 == 0):
             raise ValueError(f"{self.name}: MoE experts {self.experts} top_k {self.top_k}")
+        if self.act not in ("silu", "gelu_tanh") or (self.moe and self.act != "silu"):
+            raise ValueError(f"{self.name}: activation {self.act!r} (MoE experts: silu)")
         return self
 
 

@@ -63,7 +63,7 @@ const char* w8a8_status_string(int s) {
 }
 
 int w8a8_sfu(int func, const float* x, float* y, int64_t n, void* stream) {
-    if (func < 0 || func > 3 || n < 0 || (n > 0 && (!x || !y))) return W8A8_EINVAL;
+    if (func < 0 || func > 4 || n < 0 || (n > 0 && (!x || !y))) return W8A8_EINVAL;
     if (n == 0) return W8A8_OK;
     return cuda_status(launch_sfu(func, x, y, n, S(stream)));
 }
@@ -169,9 +169,22 @@ int w8a8_ffn_swiglu_chain(const float* x, const float* norm_g, float eps, int ro
 
 size_t w8a8_ffn_scratch_bytes(int rows) { return 256 + 4 * (size_t)(rows > 0 ? rows : 0); }
 
+static bool set_act(int act, int* kind, float* a, float* b) {
+    if (act != W8A8_ACT_SILU && act != W8A8_ACT_GELU_TANH) return false;
+    *kind = act, *a = gelu_a_const(), *b = gelu_b_const();
+    return true;
+}
+
 int w8a8_ffn_swiglu(const float* x, const float* norm_g, float eps, int rows, int k, const int8_t* w_gate,
                     const float* s_gate, const int8_t* w_up, const float* s_up, int hidden, float* h,
                     int8_t* h_q, float* s_h, void* scratch, size_t scratch_bytes, void* stream) {
+    return w8a8_ffn_gated(x, norm_g, eps, rows, k, w_gate, s_gate, w_up, s_up, hidden, W8A8_ACT_SILU, h, h_q, s_h,
+                          scratch, scratch_bytes, stream);
+}
+
+int w8a8_ffn_gated(const float* x, const float* norm_g, float eps, int rows, int k, const int8_t* w_gate,
+                   const float* s_gate, const int8_t* w_up, const float* s_up, int hidden, int act, float* h,
+                   int8_t* h_q, float* s_h, void* scratch, size_t scratch_bytes, void* stream) {
     int st = check_linear(rows, k, w_gate, s_gate, hidden, h);
     if (st) return st;
     if (!x || !norm_g || !w_up || !s_up || (h_q == nullptr) != (s_h == nullptr)) return W8A8_EINVAL;
@@ -182,6 +195,7 @@ int w8a8_ffn_swiglu(const float* x, const float* norm_g, float eps, int rows, in
     LinearParams p{};
     p.m = rows, p.n = hidden, p.k = k, p.x = x, p.norm_g = norm_g, p.eps = eps, p.inv_k = inv_of(k);
     p.w = w_gate, p.s_w = s_gate, p.w2 = w_up, p.s_w2 = s_up, p.y = h, p.hq = h_q, p.s_h = s_h;
+    if (!set_act(act, &p.act, &p.act_a, &p.act_b)) return W8A8_EINVAL;
     if (scratch) {
         p.counter = static_cast<uint32_t*>(scratch);
         p.amax_bits = reinterpret_cast<uint32_t*>(static_cast<char*>(scratch) + 256);
@@ -238,6 +252,11 @@ int w8a8_gemm(const int8_t* xq, const float* s_x, int rows, int k, const int8_t*
 
 int w8a8_gemm_swiglu(const int8_t* xq, const float* s_x, int rows, int k, const int8_t* w_gate, const float* s_gate,
                      const int8_t* w_up, const float* s_up, int hidden, float* h, void* stream) {
+    return w8a8_gemm_gated(xq, s_x, rows, k, w_gate, s_gate, w_up, s_up, hidden, W8A8_ACT_SILU, h, stream);
+}
+
+int w8a8_gemm_gated(const int8_t* xq, const float* s_x, int rows, int k, const int8_t* w_gate, const float* s_gate,
+                    const int8_t* w_up, const float* s_up, int hidden, int act, float* h, void* stream) {
     int st = check_gemm(xq, s_x, rows, k, w_gate, s_gate, hidden, h);
     if (st) return st;
     if (!w_up || !s_up) return W8A8_EINVAL;
@@ -245,6 +264,7 @@ int w8a8_gemm_swiglu(const int8_t* xq, const float* s_x, int rows, int k, const 
     GemmOperands a{xq, w_gate, w_up};
     GemmParams p{};
     p.m = rows, p.n = hidden, p.k = k, p.s_x = s_x, p.s_w = s_gate, p.s_w2 = s_up, p.y = h;
+    if (!set_act(act, &p.act, &p.act_a, &p.act_b)) return W8A8_EINVAL;
     return cuda_status(launch_gemm(a, p, S(stream)));
 }
 
@@ -507,6 +527,7 @@ int w8a8_tp_linear(const W8A8TpLinearArgs* a, void* stream) {
         if (!a->w_up || !a->s_up || !tp_block(c, a->amax_out, W8A8_TP_AMAX_WORDS(c->ranks))) return W8A8_EINVAL;
         if (!al16(a->w_up)) return W8A8_EALIGN;
         p.w2 = a->w_up, p.s_w2 = a->s_up, p.y = a->y, p.amax_ll_out = a->amax_out;
+        if (!set_act(a->act, &p.act, &p.act_a, &p.act_b)) return W8A8_EINVAL;
     }
     if (!gemv_fits(p, pro, epi) || gemv_grid(p, pro, epi) > kTpCtas) return W8A8_EINVAL;
     return cuda_status(launch_gemv(p, pro, epi, S(stream)));

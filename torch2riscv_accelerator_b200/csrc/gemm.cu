@@ -95,6 +95,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     __shared__ int failed;
     __shared__ uint32_t silu_tab[256];                         // EXP / RECIP tables (SwiGLU epilogue)
     if (TWO) stage_silu_tables(silu_tab);
+    const GateAct act{p.act, p.act_a, p.act_b};
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int n0 = blockIdx.x * BN, m0 = blockIdx.y * kBM;
     const int kt_n = (p.k + kBK - 1) / kBK;
@@ -201,7 +202,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 #pragma unroll
                     for (int j = 0; j < 16; ++j) {
                         const float g = fmul(fmul(i2f(v[j]), sw[j]), sx);
-                        if (TWO) o[j] = silu_gate_tab(g, fmul(fmul(i2f(u[j]), sw2[j]), sx), silu_tab);
+                        if (TWO) o[j] = gate_tab(g, fmul(fmul(i2f(u[j]), sw2[j]), sx), silu_tab, act);
                         else o[j] = p.resid != nullptr ? fadd(rs[j], g) : g;
                     }
 #pragma unroll
@@ -220,7 +221,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     const size_t off = (size_t)m * p.n + n;
                     const float g = fmul(fmul(i2f(v[j]), __ldg(p.s_w + n)), sx);
                     if (TWO) {
-                        p.y[off] = silu_gate_tab(g, fmul(fmul(i2f(u[j]), __ldg(p.s_w2 + n)), sx), silu_tab);
+                        p.y[off] = gate_tab(g, fmul(fmul(i2f(u[j]), __ldg(p.s_w2 + n)), sx), silu_tab, act);
                     } else if (p.resid != nullptr) {
                         p.y[off] = fadd(p.resid[off], g);
                     } else {

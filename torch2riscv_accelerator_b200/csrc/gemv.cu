@@ -418,7 +418,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(LinearParams p, G
                             if (q < p.tp.ranks) ll_store(tp_at(p.tp, p.part_out, q) + w, (uint32_t)acc[m], ep);
                     } else {
                         const float u = fmul(fmul(i2f(acc2[m]), sw2[j]), sx[m]);
-                        const float h = silu_gate_tab(v, u, silu_tab);
+                        const float h = gate_tab(v, u, silu_tab, GateAct{p.act, p.act_a, p.act_b});
                         p.y[o] = h;
                         tamax[m] = max(tamax[m], __float_as_uint(fabsf(h)));   // as bits: NaN above numbers
                     }

@@ -117,7 +117,7 @@ __global__ void __launch_bounds__(kThreads) linear_kernel(LinearParams p) {
                 p.y[o] = fadd(p.resid[o], v);
             } else {
                 const float u = fmul(fmul(i2f(acc2[kTwo ? r : 0][m]), __ldg(p.s_w2 + n)), sx[m]);
-                const float h = silu_gate(v, u);
+                const float h = gate(v, u, GateAct{p.act, p.act_a, p.act_b});
                 p.y[o] = h;
                 atomicMax(&bamax[m], __float_as_uint(fabsf(h)));
             }

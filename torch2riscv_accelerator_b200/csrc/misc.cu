@@ -161,12 +161,16 @@ cudaError_t launch_argmax(const float* logits, int m, int n, int32_t* out, cudaS
 }
 
 // func: 0 EXP, 1 RECIP, 2 RSQRT, 3 SiLU gate g*sigma(g) (u = 1)
-__global__ void sfu_kernel(int func, const float* x, float* y, long long n) {
+__global__ void sfu_kernel(int func, const float* x, float* y, long long n, float gelu_a, float gelu_b) {
     pdl_wait();
     pdl_trigger();
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
         const float v = x[i];
-        y[i] = func == 0 ? sfu_exp(v) : func == 1 ? sfu_recip(v) : func == 2 ? sfu_rsqrt(v) : silu_gate(v, 1.f);
+        y[i] = func == 0   ? sfu_exp(v)
+               : func == 1 ? sfu_recip(v)
+               : func == 2 ? sfu_rsqrt(v)
+               : func == 3 ? silu_gate(v, 1.f)
+                           : gelu_gate(v, 1.f, gelu_a, gelu_b);
     }
 }
 
@@ -174,7 +178,7 @@ cudaError_t launch_sfu(int func, const float* x, float* y, long long n, cudaStre
     long long blocks = (n + 255) / 256;
     if (blocks > 148 * 16) blocks = 148 * 16;
     if (blocks < 1) blocks = 1;
-    return launch_k(sfu_kernel, dim3((int)blocks), dim3(256), 0, st, func, x, y, n);
+    return launch_k(sfu_kernel, dim3((int)blocks), dim3(256), 0, st, func, x, y, n, gelu_a_const(), gelu_b_const());
 }
 
 // The on-device decode loop's step: the previous step's greedy token (the

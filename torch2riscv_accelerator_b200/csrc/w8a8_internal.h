@@ -5,7 +5,14 @@
 #include <cuda.h>
 #include <cuda_runtime.h>
 
+#include <cmath>
+
 namespace w8a8 {
+
+// GELU-tanh constants as the reference computes them on the host
+// (compiler/frontend/hf_generic.py:848-849: float64, rounded once to float32).
+inline float gelu_a_const() { return (float)(-2.0 * std::sqrt(2.0 / 3.141592653589793)); }
+inline float gelu_b_const() { return (float)(-2.0 * std::sqrt(2.0 / 3.141592653589793) * 0.044715); }
 
 enum Prologue { PRO_I8 = 0, PRO_QUANT = 1, PRO_RMSQ = 2 };
 enum Epilogue { EPI_STORE = 0, EPI_RESID = 1, EPI_SWIGLU = 2, EPI_PARTIAL = 3 };
@@ -53,6 +60,8 @@ struct LinearParams {
     uint32_t* amax_out;
     uint32_t* clear;
     int clear_n;
+    int act;                  // EPI_SWIGLU's gate: 0 SiLU, 1 GELU-tanh (constants act_a, act_b)
+    float act_a, act_b;
     // tensor-parallel decode (tp.ranks > 1); blocks are addresses in this rank's region
     TpCtx tp;
     const uint64_t* part_in;  // [ranks][kTpRows][k]: the previous row-split linear's int32 partials;
@@ -119,6 +128,8 @@ struct GemmParams {
     const float* resid;       // [m, n] or null (may alias y)
     float* y;                 // [m, n]: dequant (+ resid), or h with w2
     int32_t* acc;             // [m, n] raw accumulators, or null (without resid / w2)
+    int act;                  // with w2: the gate, 0 SiLU, 1 GELU-tanh (constants act_a, act_b)
+    float act_a, act_b;
 };
 size_t gemm_smem(int bn, bool two);
 // A 2-D uint8 TMA map: [rows][inner] with row_stride bytes between rows

@@ -166,6 +166,34 @@ __device__ __forceinline__ float silu_gate_tab(float g, float u, const uint32_t*
     return fmul(fmul(g, sig), u);
 }
 
+// GELU's tanh approximation as the overlay computes it
+// (compiler/frontend/hf_generic.py:840-856, SaGELUTanh): z = g * (A + (g * g) * B),
+// g * RECIP(EXP(z) + 1) -- multiplies, adds, EXP and RECIP only -- then * u.
+// A = F(-2 sqrt(2 / pi)), B = F(-2 sqrt(2 / pi) * 0.044715), from the host.
+__device__ __forceinline__ float gelu_gate(float g, float u, float a, float b) {
+    const float z = fmul(g, fadd(a, fmul(fmul(g, g), b)));
+    return fmul(fmul(g, sfu_recip(fadd(sfu_exp(z), 1.f))), u);
+}
+
+__device__ __forceinline__ float gelu_gate_tab(float g, float u, const uint32_t* tab, float a, float b) {
+    const float z = fmul(g, fadd(a, fmul(fmul(g, g), b)));
+    return fmul(fmul(g, sfu_recip_tab(fadd(sfu_exp_tab(z, tab, tab + 64), 1.f), tab + 128, tab + 192)), u);
+}
+
+// The gated activation of a kind (0 SiLU, 1 GELU-tanh): act(g) * u.
+struct GateAct {
+    int kind;
+    float a, b;                // GELU-tanh constants
+};
+
+__device__ __forceinline__ float gate_tab(float g, float u, const uint32_t* tab, const GateAct& act) {
+    return act.kind == 1 ? gelu_gate_tab(g, u, tab, act.a, act.b) : silu_gate_tab(g, u, tab);
+}
+
+__device__ __forceinline__ float gate(float g, float u, const GateAct& act) {
+    return act.kind == 1 ? gelu_gate(g, u, act.a, act.b) : silu_gate(g, u);
+}
+
 // Copy the four 64-word tables of silu_gate_tab into shared memory (whole block).
 __device__ __forceinline__ void stage_silu_tables(uint32_t* tab) {
     for (int i = threadIdx.x; i < 256; i += blockDim.x) {

@@ -114,7 +114,7 @@ class DeviceDecoder:
         c = self.cfg
         x, qkv, att = self.x[:rows], self.qkv[:rows], self.att[:rows]
         h, hq, s_h = self.h[:rows], self.hq[:rows], self.s_h[:rows]
-        if rows <= CHAIN_ROWS and not c.moe:
+        if rows <= CHAIN_ROWS and not c.moe and c.act == "silu":
             return self._run_chain(rows, logits_rows, argmax)
         args = self._attn_args(rows)
         self._embed(rows, x)
@@ -126,7 +126,7 @@ class DeviceDecoder:
                 self._moe_rows(l, x)
                 continue
             ops.ffn_swiglu(x, w["rms_ffn"], c.eps, w["w1"], w["s_w1"], w["w3"], w["s_w3"], None, h=h,
-                           requant=False)
+                           requant=False, act=c.act)
             ops.linear_fused(h, w["w2"], w["s_w2"], resid=x, out=x)          # quant_act(h) in the prologue
         xl = self.x[rows - logits_rows:rows]
         ops.classifier(xl, self.cls_q, self.cls_s, self.rms_final, c.eps, out=self.logits[:logits_rows],
@@ -205,7 +205,7 @@ class DeviceDecoder:
                 continue
             xq, sx = self._q(rows, c.dim)
             ops.quant_rows(x, w["rms_ffn"], c.eps, xq=xq, s_x=sx)
-            ops.gemm_swiglu(xq, sx, w["w1"], w["s_w1"], w["w3"], w["s_w3"], out=h)
+            ops.gemm_swiglu(xq, sx, w["w1"], w["s_w1"], w["w3"], w["s_w3"], out=h, act=c.act)
             hq, sh = self._q(rows, c.hidden)
             ops.quant_rows(h, None, 0.0, xq=hq, s_x=sh)
             ops.gemm(hq, sh, w["w2"], w["s_w2"], out=x, resid=x)
@@ -360,7 +360,7 @@ class BatchDecoder:
                 continue
             xq, sx = self._q(c.dim)
             ops.quant_rows(x, w["rms_ffn"], c.eps, xq=xq, s_x=sx)
-            ops.gemm_swiglu(xq, sx, w["w1"], w["s_w1"], w["w3"], w["s_w3"], out=self.h)
+            ops.gemm_swiglu(xq, sx, w["w1"], w["s_w1"], w["w3"], w["s_w3"], out=self.h, act=c.act)
             hq, sh = self._q(c.hidden)
             ops.quant_rows(self.h, None, 0.0, xq=hq, s_x=sh)
             ops.gemm(hq, sh, w["w2"], w["s_w2"], out=x, resid=x)

@@ -14,7 +14,8 @@ import torch
 from . import _lib
 
 F32, I8, I32 = torch.float32, torch.int8, torch.int32
-SFU_EXP, SFU_RECIP, SFU_RSQRT, SFU_SILU = 0, 1, 2, 3
+SFU_EXP, SFU_RECIP, SFU_RSQRT, SFU_SILU, SFU_GELU = 0, 1, 2, 3, 4
+ACTS = {"silu": 0, "gelu_tanh": 1}
 
 
 def _p(t):
@@ -122,9 +123,11 @@ def ffn_scratch(rows, device):
     return torch.zeros(n, dtype=torch.uint8, device=device)
 
 
-def ffn_swiglu(x, norm_g, eps, w_gate, s_gate, w_up, s_up, scratch, h=None, h_q=None, s_h=None, requant=True):
+def ffn_swiglu(x, norm_g, eps, w_gate, s_gate, w_up, s_up, scratch, h=None, h_q=None, s_h=None, requant=True,
+               act="silu"):
     """Decode SwiGLU dispatch: returns (h fp32, h_q int8, s_h); with
-    requant=False only h (h_q, s_h None; the down projection quantizes h)."""
+    requant=False only h (h_q, s_h None; the down projection quantizes h).
+    act: the gate, "silu" or "gelu_tanh"."""
     _need(x, F32, "x")
     m, k = x.shape
     hidden = w_gate.shape[0]
@@ -135,9 +138,9 @@ def ffn_swiglu(x, norm_g, eps, w_gate, s_gate, w_up, s_up, scratch, h=None, h_q=
         s_h = torch.empty(m, dtype=F32, device=dev) if s_h is None else s_h
     else:
         h_q = s_h = scratch = None
-    _lib.check("w8a8_ffn_swiglu", _lib.load().w8a8_ffn_swiglu(
-        _p(x), _p(norm_g), float(eps), m, k, _p(w_gate), _p(s_gate), _p(w_up), _p(s_up), hidden, _p(h), _p(h_q),
-        _p(s_h), _p(scratch), 0 if scratch is None else scratch.numel(), _st()))
+    _lib.check("w8a8_ffn_gated", _lib.load().w8a8_ffn_gated(
+        _p(x), _p(norm_g), float(eps), m, k, _p(w_gate), _p(s_gate), _p(w_up), _p(s_up), hidden, ACTS[act], _p(h),
+        _p(h_q), _p(s_h), _p(scratch), 0 if scratch is None else scratch.numel(), _st()))
     return h, h_q, s_h
 
 
@@ -162,13 +165,14 @@ def gemm(xq, s_x, w, s_w, out=None, acc=None, resid=None):
     return out
 
 
-def gemm_swiglu(xq, s_x, w_gate, s_gate, w_up, s_up, out=None):
-    """Tensor-core SwiGLU pair: h = silu(g) * u for any row count."""
+def gemm_swiglu(xq, s_x, w_gate, s_gate, w_up, s_up, out=None, act="silu"):
+    """Tensor-core gated pair: h = act(g) * u for any row count (act "silu"
+    or "gelu_tanh")."""
     m, k = xq.shape
     n = w_gate.shape[0]
     out = torch.empty(m, n, dtype=F32, device=xq.device) if out is None else out
-    _lib.check("w8a8_gemm_swiglu", _lib.load().w8a8_gemm_swiglu(_p(xq), _p(s_x), m, k, _p(w_gate), _p(s_gate),
-                                                                _p(w_up), _p(s_up), n, _p(out), _st()))
+    _lib.check("w8a8_gemm_gated", _lib.load().w8a8_gemm_gated(_p(xq), _p(s_x), m, k, _p(w_gate), _p(s_gate),
+                                                              _p(w_up), _p(s_up), n, ACTS[act], _p(out), _st()))
     return out
 
 

@@ -216,7 +216,7 @@ class TpDecoder(DeviceDecoder):
             ffn = A(k=c.dim, n=lc.hidden, part_in=comm.block(l, "o"), part_s_w=p(w["s_wo"]),
                     part_s_x=p(self.sx_o[l]), resid=p(xa), x_out=p(xb), norm_g=p(w["rms_ffn"]), eps=c.eps,
                     w=p(w["w1"]), s_w=p(w["s_w1"]), w_up=p(w["w3"]), s_up=p(w["s_w3"]),
-                    epilogue=_lib.TP_SWIGLU, y=p(self.h), amax_out=comm.block(l, "h"))
+                    epilogue=_lib.TP_SWIGLU, y=p(self.h), amax_out=comm.block(l, "h"), act=ops.ACTS[c.act])
             down = A(k=lc.hidden, n=c.dim, x=p(self.h), amax_in=comm.block(l, "h"), w=p(w["w2"]),
                      s_w=p(w["s_w2"]), epilogue=_lib.TP_PARTIAL, part_out=comm.block(l, "down"),
                      s_x_out=p(self.sx_d[l]))
@@ -266,7 +266,7 @@ class TpDecoder(DeviceDecoder):
             row_split(self, self.att[:rows], w["wo"], w["s_wo"], x, self.comm.group)
             xq, sx = self._q(rows, c.dim)
             ops.quant_rows(x, w["rms_ffn"], c.eps, xq=xq, s_x=sx)
-            ops.gemm_swiglu(xq, sx, w["w1"], w["s_w1"], w["w3"], w["s_w3"], out=h)
+            ops.gemm_swiglu(xq, sx, w["w1"], w["s_w1"], w["w3"], w["s_w3"], out=h, act=c.act)
             row_split(self, h, w["w2"], w["s_w2"], x, self.comm.group)
         ops.classifier(self.x[rows - logits_rows:rows], self.cls_q, self.cls_s, self.rms_final, c.eps,
                        out=self.logits[:logits_rows])
@@ -416,7 +416,7 @@ class TpBatchDecoder(BatchDecoder):
             row_split(self, self.att, w["wo"], w["s_wo"], x, g)
             xq, sx = self._q(c.dim)
             ops.quant_rows(x, w["rms_ffn"], c.eps, xq=xq, s_x=sx)
-            ops.gemm_swiglu(xq, sx, w["w1"], w["s_w1"], w["w3"], w["s_w3"], out=self.h)
+            ops.gemm_swiglu(xq, sx, w["w1"], w["s_w1"], w["w3"], w["s_w3"], out=self.h, act=c.act)
             row_split(self, self.h, w["w2"], w["s_w2"], x, g)
         xq, sx = self._q(c.dim)
         ops.quant_rows(x, self.rms_final, c.eps, xq=xq, s_x=sx)

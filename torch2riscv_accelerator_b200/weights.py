@@ -226,7 +226,11 @@ def calibrate_layer(cfg, x, t, f32, cos, sin):
         x = (x + y).astype(F)
     else:
         h1, h3 = xb @ f32["w1"].T, xb @ f32["w3"].T
-        x = (x + ((h1 / (1 + np.exp(-h1))) * h3) @ f32["w2"].T).astype(F)
+        if c.act == "gelu_tanh":                     # torch's gelu(approximate="tanh") in fp32
+            a = (F(0.5) * h1 * (F(1) + np.tanh(F(np.sqrt(2.0 / np.pi)) * (h1 + F(0.044715) * h1 ** 3)))).astype(F)
+        else:
+            a = h1 / (1 + np.exp(-h1))
+        x = (x + (a * h3) @ f32["w2"].T).astype(F)
     return x, np.abs(k).max(axis=0).reshape(-1), np.abs(v).max(axis=0).reshape(-1)
 
 
