@@ -164,20 +164,43 @@ def kv_scales_of(amax, channel=""):
 
 
 def calibrate_kv(cfg, w, tokens, channel=""):
-    """KV scales from an fp32 run of the model w (fp32 tensors in the
-    reference's naming, `llm/checkpoint.py:33-59`) over `tokens` from position
-    0: the maxima of |k|, |v| per cache channel as they are written (after
-    QK-norm and RoPE), then kv_scales_of (`hf_generic.calibrate_kv`)."""
+    """KV scales from fp32 runs of the model w (fp32 tensors in the
+    reference's naming, `llm/checkpoint.py:33-59`) over `tokens` (one sequence,
+    or a list of sequences each from position 0): the maxima of |k|, |v| per
+    cache channel as they are written (after QK-norm and RoPE) over all runs,
+    then kv_scales_of (`hf_generic.calibrate_kv`)."""
+    runs = [tokens] if np.ndim(tokens[0]) == 0 else list(tokens)
+    cos, sin = rope_tables(cfg)
+    amax = np.zeros((cfg.layers, 2, cfg.kv_dim), F)
+    names = ("wq", "wk", "wv", "wo") + (("router", "e_gate", "e_up", "e_down") if cfg.moe else ("w1", "w3", "w2"))
+    for run in runs:
+        x = w["tok"][np.asarray(run)].astype(F)
+        for l in range(cfg.layers):
+            t = {"rms_att": w["rms_att"][l], "rms_ffn": w["rms_ffn"][l]}
+            if cfg.qk_norm:
+                t["q_norm"], t["k_norm"] = w["q_norm"][l], w["k_norm"][l]
+            x, k, v = calibrate_layer(cfg, x, t, {n: w[n][l] for n in names}, cos, sin)
+            amax[l, 0], amax[l, 1] = np.maximum(amax[l, 0], k), np.maximum(amax[l, 1], v)
+    return kv_scales_of(amax, channel)
+
+
+def fp32_forward(cfg, w, tokens, last_only=False):
+    """The fp32 model's logits at every position of `tokens` (from position 0,
+    causal): the reference's Fp32Model (`llm/ref_model.py`, `qhf.py:210-242`)
+    in NumPy float32, for quality evaluation. w: fp32 tensors in the
+    reference's naming (plus router / e_gate / e_up / e_down for MoE)."""
     cos, sin = rope_tables(cfg)
     x = w["tok"][np.asarray(tokens)].astype(F)
-    amax = np.zeros((cfg.layers, 2, cfg.kv_dim), F)
     for l in range(cfg.layers):
         t = {"rms_att": w["rms_att"][l], "rms_ffn": w["rms_ffn"][l]}
         if cfg.qk_norm:
             t["q_norm"], t["k_norm"] = w["q_norm"][l], w["k_norm"][l]
-        f32 = {n: w[n][l] for n in ("wq", "wk", "wv", "wo", "w1", "w3", "w2")}
-        x, amax[l, 0], amax[l, 1] = calibrate_layer(cfg, x, t, f32, cos, sin)
-    return kv_scales_of(amax, channel)
+        names = ("wq", "wk", "wv", "wo") + (("router", "e_gate", "e_up", "e_down") if cfg.moe else ("w1", "w3", "w2"))
+        x, _, _ = calibrate_layer(cfg, x, t, {n: w[n][l] for n in names}, cos, sin)
+    wcls = w.get("wcls", w["tok"]) if not cfg.tied else w["tok"]
+    if last_only:
+        x = x[-1:]
+    return (_rms32(x, w["rms_final"], cfg.eps) @ wcls.T).astype(F)
 
 
 def _rms32(x, g, eps):
@@ -253,8 +276,8 @@ def from_fp32(cfg, w):
         t = {"rms_att": np.asarray(w["rms_att"][l], F), "rms_ffn": np.asarray(w["rms_ffn"][l], F)}
         t["wqkv"], t["s_wqkv"] = quantize_rows(np.concatenate([w["wq"][l], w["wk"][l], w["wv"][l]]))
         t["wo"], t["s_wo"] = quantize_rows(w["wo"][l])
-        for n in ("w1", "w3", "w2"):
-            t[n], t["s_" + n] = quantize_rows(w[n][l])
+        for n in (("router", "e_gate", "e_up", "e_down") if cfg.moe else ("w1", "w3", "w2")):
+            t[n], t["s_" + n] = quantize_rows(w[n][l])            # (experts: per output row of each)
         if cfg.qk_norm:
             t["q_norm"], t["k_norm"] = np.asarray(w["q_norm"][l], F), np.asarray(w["k_norm"][l], F)
         qw.layers.append(t)
@@ -267,7 +290,8 @@ def fp32_model(cfg, seed, gains="ones", std=0.02, layers=None):
     g = lambda n, l=-1: gen_tensor(cfg, seed, n, l, gains, std)
     L = cfg.layers if layers is None else layers
     w = {"tok": g("tok"), "rms_final": g("rms_final")}
-    names = ["rms_att", "rms_ffn", "wq", "wk", "wv", "wo", "w1", "w2", "w3"]
+    names = ["rms_att", "rms_ffn", "wq", "wk", "wv", "wo"]
+    names += ["router", "e_gate", "e_up", "e_down"] if cfg.moe else ["w1", "w2", "w3"]
     if cfg.qk_norm:
         names += ["q_norm", "k_norm"]
     for n in names:
