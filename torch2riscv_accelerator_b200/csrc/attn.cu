@@ -440,31 +440,46 @@ unsigned int attn_read_clear_errors() {
 
 // ---------------------------------------------------------------------------
 // Batched decode: one CTA per (KV head, slot), no cluster. The slot's cache
-// streams through a 4-stage ring of TMA tiles (its K rows, tp positions x
-// head_dim; then its V^T rows, head_dim x tp positions) filled by a producer
-// warp; the scores of every position stay in shared memory, so the softmax
+// streams through a 4-stage ring filled by a producer warp: its K rows as TMA
+// tiles of tp positions x head_dim, then its V^T rows by channel group (cg
+// channels x positions 0 .. pos, one contiguous bulk copy per channel: V^T
+// tiles along positions would read 128-byte pieces of 2 KB rows, which the
+// HBM served at a third of its bandwidth); the scores of every position stay in shared memory, so the softmax
 // (global max, EXP, int8 p; NORM's ordered sum over the whole row) needs no
 // exchange. The current position's K / V row is written to the cache and
 // patched into its tile when that tile lands. Same arithmetic, step for step,
 // as the cluster kernel above (and so as a one-row decode).
-constexpr int kSbStages = 4;
+#ifndef W8A8_SB_STAGES
+#define W8A8_SB_STAGES 4
+#endif
+#ifndef W8A8_SB_TP
+#define W8A8_SB_TP 128
+#endif
+constexpr int kSbStages = W8A8_SB_STAGES;                      // ring stages
+constexpr int kSbTile = W8A8_SB_TP;                            // cache positions per tile (at most)
 constexpr int kSbThreads = 288;                                // 8 compute warps + 1 producer warp
 constexpr int kSbWarps = 8;
 
 struct StreamMaps {
-    CUtensorMap k, v;                                          // K rows [.][hd]; V^T rows [.][T]
+    CUtensorMap k;                                             // K rows [.][hd]
 };
 
 struct SbSmem {
     size_t ring, scs, ps, qs, fbuf, tab, gain, etab, newk, newv, total;
 };
 
+// bytes of a ring stage: a K tile (tp x hd), at least one V^T row (T)
+__host__ __device__ inline size_t sb_stage(int hd, int T, int tp) {
+    const size_t k = (size_t)tp * hd, tp_round = (size_t)((T + tp - 1) / tp * tp);
+    return k > tp_round ? k : tp_round;
+}
+
 __host__ __device__ inline SbSmem sb_smem(int G, int hd, int T, int tp) {
     auto a16 = [](size_t b) { return (b + 15) & ~size_t(15); };
     const int Tp = (T + tp - 1) / tp * tp;
     SbSmem s{};
     size_t o = 0;
-    s.ring = o; o += a16((size_t)kSbStages * tp * hd);        // [stage][tp * hd]
+    s.ring = o; o += a16((size_t)kSbStages * sb_stage(hd, T, tp));   // [stage]: a K tile or a V^T channel group
     s.scs = o;  o += a16((size_t)G * Tp * 4);                 // scores / e of every position, per row
     s.ps = o;   o += a16((size_t)G * Tp);                     // int8 p
     s.qs = o;   o += a16((size_t)G * hd);
@@ -502,10 +517,18 @@ __global__ void __launch_bounds__(kSbThreads, 1)
     __shared__ int wsum[kSbWarps][kMaxG], lsum[kMaxG];
     __shared__ int failed;
     const int pos = p.pos[slot];                               // written by an earlier step: read before the wait
-    const int nt = pos / tp + 1;                               // tiles with positions <= pos
+    const int nt = pos / tp + 1;                               // K tiles with positions <= pos
     const size_t krow0 = (size_t)slot * (p.slot_stride / hd) + (size_t)kvh * T;
-    const size_t vrow0 = (size_t)slot * (p.slot_stride / T) + (size_t)kvh * hd;
-    const uint32_t tile_bytes = (uint32_t)(tp * hd);
+    const int8_t* vbase = p.vc + (size_t)slot * p.slot_stride + (size_t)kvh * hd * T;   // this head's V^T rows
+    const uint32_t tile_bytes = (uint32_t)(tp * hd);             // a K tile
+    const size_t stage_bytes = sb_stage(hd, T, tp);
+    // V^T tiles by channel group: cg channels x positions [0, nv) each, every
+    // channel's run one contiguous bulk copy (sequential HBM reads); cg the
+    // largest divisor of hd, at most 16 (copies per tile), whose tile fits a stage
+    const int nv = ((pos + 1) + 15) & ~15;
+    int cg = hd < 16 ? hd : 16;
+    while (cg > 1 && (hd % cg != 0 || (size_t)cg * nv > stage_bytes)) --cg;
+    const int nvt = hd / cg, ntiles = nt + nvt;
     if (tid == 0) {
         failed = 0;
         for (int s = 0; s < kSbStages; ++s) {
@@ -517,12 +540,18 @@ __global__ void __launch_bounds__(kSbThreads, 1)
     __syncthreads();
     auto issue = [&](int i) {                                  // ring tile i: K tile i, then V tile i - nt
         const int s = i % kSbStages;
-        mbar_expect_tx(&full[s], tile_bytes);
-        if (i < nt) tma_load_2d(ring + (size_t)s * tile_bytes, &maps.k, 0, (int)(krow0 + (size_t)i * tp), &full[s]);
-        else tma_load_2d(ring + (size_t)s * tile_bytes, &maps.v, (i - nt) * tp, (int)vrow0, &full[s]);
+        int8_t* dst = ring + (size_t)s * stage_bytes;
+        if (i < nt) {
+            mbar_expect_tx(&full[s], tile_bytes);
+            tma_load_2d(dst, &maps.k, 0, (int)(krow0 + (size_t)i * tp), &full[s]);
+        } else {
+            const int c0 = (i - nt) * cg;
+            mbar_expect_tx(&full[s], (uint32_t)(cg * nv));
+            for (int c = 0; c < cg; ++c) bulk_g2s(dst + (size_t)c * nv, vbase + (size_t)(c0 + c) * T, (uint32_t)nv, &full[s]);
+        }
     };
     if (producer && lane == 0)                                 // cache rows of earlier steps: before the wait
-        for (int i = 0; i < kSbStages && i < 2 * nt; ++i) issue(i);
+        for (int i = 0; i < kSbStages && i < ntiles; ++i) issue(i);
     if (tid < 64) {
         etab[tid] = g_exp_t[tid];
         etab[64 + tid] = g_exp_s[tid];
@@ -541,7 +570,7 @@ __global__ void __launch_bounds__(kSbThreads, 1)
 
     if (producer) {
         if (lane == 0) {                                       // refill each stage once the 8 warps are done
-            for (int i = kSbStages; i < 2 * nt; ++i) {
+            for (int i = kSbStages; i < ntiles; ++i) {
                 const int s = i % kSbStages;
                 if (!mbar_wait_spin(&empty[s], (uint32_t)(((i / kSbStages) - 1) & 1))) {
                     atomicOr(&g_attn_errors, 4u);
@@ -603,10 +632,12 @@ __global__ void __launch_bounds__(kSbThreads, 1)
                 if (tid == 0) atomicOr(&g_attn_errors, 4u);
                 failed = 1;
             }
-            int8_t* kt = ring + (size_t)s * tile_bytes;        // [tp][hd]
+            int8_t* kt = ring + (size_t)s * stage_bytes;        // [tp][hd]
             if (i == nt - 1) {                                 // the tile holding pos: the new K row
-                if (tid < hd / 16)
+                if (tid < hd / 16) {
                     reinterpret_cast<int4*>(kt + (size_t)(pos - i * tp) * hd)[tid] = reinterpret_cast<const int4*>(newk)[tid];
+                    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // before the stage's next copy
+                }
                 named_barrier_sync(1, kSbWarps * 32);
             }
             for (int pr = tid; pr < G * tp; pr += kSbWarps * 32) {
@@ -688,58 +719,56 @@ __global__ void __launch_bounds__(kSbThreads, 1)
             }
         }
         named_barrier_sync(1, kSbWarps * 32);
-        // ---- pass 2: p.V over the V^T tiles; thread <-> (row, channel) pairs
-        constexpr int kMaxPairs = kMaxG * 256 / (kSbWarps * 32);
-        int acc[kMaxPairs];
-#pragma unroll
-        for (int j = 0; j < kMaxPairs; ++j) acc[j] = 0;
-        const int wpr = tp / 16;                                // 16-byte words per V^T tile row
-        for (int i = 0; i < nt; ++i) {
-            const int ri = nt + i, s = ri % kSbStages;
+        // ---- pass 2: p.V over the channel-group tiles: each output (row r,
+        // channel c) is one dot product of p[r][0, nv) with V^T[c][0, nv) inside
+        // one tile (positions past pos have p = 0); 16 threads per output, a
+        // shuffle sum (int32: exact in any order)
+        float* att = p.att + (size_t)slot * q_dim;
+        uint32_t am = 0u;
+        const int nw = nv / 16, sl = tid & 15;                  // 16-byte words per row; this thread's slice
+        for (int j = 0; j < nvt; ++j) {
+            const int ri = nt + j, s = ri % kSbStages, c0 = j * cg;
             if (!mbar_wait_spin(&full[s], (uint32_t)((ri / kSbStages) & 1))) {
                 if (tid == 0) atomicOr(&g_attn_errors, 4u);
                 failed = 1;
             }
-            int8_t* vt = ring + (size_t)s * tile_bytes;        // [hd][tp]
-            if (i == nt - 1) {                                 // the new V column
-                for (int c = tid; c < hd; c += kSbWarps * 32) vt[(size_t)c * tp + (pos - i * tp)] = newv[c];
-                named_barrier_sync(1, kSbWarps * 32);
+            int8_t* vt = ring + (size_t)s * stage_bytes;        // [cg][nv]
+            for (int c = tid; c < cg; c += kSbWarps * 32) {    // the new column
+                vt[(size_t)c * nv + pos] = newv[c0 + c];
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");       // before the stage's next copy
             }
-#pragma unroll
-            for (int j = 0; j < kMaxPairs; ++j) {
-                const int pr = tid + j * kSbWarps * 32;
-                if (pr >= G * hd) break;
-                const int r = pr / hd, c = pr % hd;
-                const int4* vr = reinterpret_cast<const int4*>(vt + (size_t)c * tp);
-                const int4* pp = reinterpret_cast<const int4*>(ps + (size_t)r * Tp + (size_t)i * tp);
-                int a0 = 0, a1 = 0, w = c % wpr;
-                for (int u = 0; u < wpr; ++u) {
-                    const int4 x = pp[w], y = vr[w];
-                    w = w + 1 == wpr ? 0 : w + 1;
-                    a0 = dp4a(x.x, y.x, a0);
-                    a1 = dp4a(x.y, y.y, a1);
-                    a0 = dp4a(x.z, y.z, a0);
-                    a1 = dp4a(x.w, y.w, a1);
+            named_barrier_sync(1, kSbWarps * 32);
+            for (int o0 = 0; o0 < G * cg; o0 += kSbWarps * 32 / 16) {
+                const int o = o0 + (tid >> 4);
+                const int r = o / cg, cl = o - r * cg;
+                int a0 = 0, a1 = 0;
+                if (o < G * cg) {
+                    const int4* vr = reinterpret_cast<const int4*>(vt + (size_t)cl * nv);
+                    const int4* pp = reinterpret_cast<const int4*>(ps + (size_t)r * Tp);
+                    for (int w = sl; w < nw; w += 16) {
+                        const int4 x = pp[w], y = vr[w];
+                        a0 = dp4a(x.x, y.x, a0);
+                        a1 = dp4a(x.y, y.y, a1);
+                        a0 = dp4a(x.z, y.z, a0);
+                        a1 = dp4a(x.w, y.w, a1);
+                    }
                 }
-                acc[j] += a0 + a1;
+                int a = a0 + a1;
+#pragma unroll
+                for (int m = 8; m > 0; m >>= 1) a += __shfl_xor_sync(0xffffffffu, a, m);
+                if (sl == 0 && o < G * cg) {
+                    const int c = c0 + cl;
+                    const float ov = i2f(a);
+                    const float av = p.a_v_ch ? p.a_v_ch[kvh * hd + c] : p.a_v;   // V per channel or per layer
+                    float out;
+                    if (p.variant == 0) out = fmul(ov, av);
+                    else out = fmul(fmul(ov, fmul(sfu_recip(i2f(lsum[r])), 127.f)), av);   // sum <= 127 T: exact
+                    att[(size_t)(kvh * G + r) * hd + c] = out;
+                    am = max(am, __float_as_uint(fabsf(out)));
+                }
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);
-        }
-        float* att = p.att + (size_t)slot * q_dim;
-        uint32_t am = 0u;
-#pragma unroll
-        for (int j = 0; j < kMaxPairs; ++j) {
-            const int pr = tid + j * kSbWarps * 32;
-            if (pr >= G * hd) break;
-            const int r = pr / hd, c = pr % hd;
-            const float o = i2f(acc[j]);
-            const float av = p.a_v_ch ? p.a_v_ch[kvh * hd + c] : p.a_v;   // V per channel or per layer
-            float out;
-            if (p.variant == 0) out = fmul(o, av);
-            else out = fmul(fmul(o, fmul(sfu_recip(i2f(lsum[r])), 127.f)), av);   // sum <= 127 T: exact
-            att[(size_t)(kvh * G + r) * hd + c] = out;
-            am = max(am, __float_as_uint(fabsf(out)));
         }
         if (p.amax_out != nullptr) {                           // max|att| of the slot's row (decode chain)
 #pragma unroll
@@ -753,19 +782,17 @@ __global__ void __launch_bounds__(kSbThreads, 1)
 }
 
 size_t attn_stream_smem(int heads, int kv_heads, int head_dim, int seq_len) {
-    const int tp = seq_len < 128 ? seq_len : 128;
+    const int tp = seq_len < kSbTile ? seq_len : kSbTile;
     return sb_smem(heads / kv_heads, head_dim, seq_len, tp).total;
 }
 
 cudaError_t launch_attn_stream(const AttnParams& p, cudaStream_t st) {
     const int hd = p.head_dim, T = p.seq_len, G = p.heads / p.kv_heads;
-    const int tp = T < 128 ? T : 128;
-    const size_t slot_k_rows = p.slot_stride / hd, slot_v_rows = p.slot_stride / T;
+    const int tp = T < kSbTile ? T : kSbTile;
+    const size_t slot_k_rows = p.slot_stride / hd;
     StreamMaps maps{};
     const uint64_t krows = (uint64_t)(p.slots - 1) * slot_k_rows + (uint64_t)p.kv_heads * T;
-    const uint64_t vrows = (uint64_t)(p.slots - 1) * slot_v_rows + (uint64_t)p.kv_heads * hd;
-    if (!make_map_u8(&maps.k, p.kc, (uint64_t)hd, krows, (uint64_t)hd, (uint32_t)hd, (uint32_t)tp, false) ||
-        !make_map_u8(&maps.v, p.vc, (uint64_t)T, vrows, (uint64_t)T, (uint32_t)tp, (uint32_t)hd, false))
+    if (!make_map_u8(&maps.k, p.kc, (uint64_t)hd, krows, (uint64_t)hd, (uint32_t)hd, (uint32_t)tp, false))
         return cudaErrorInvalidValue;
     const size_t smem = sb_smem(G, hd, T, tp).total;
     cudaError_t e = cudaFuncSetAttribute(attn_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
