@@ -493,10 +493,14 @@ __host__ __device__ inline SbSmem sb_smem(int G, int hd, int T, int tp) {
     return s;
 }
 
+// HD, TP: head_dim and positions per K tile when known at compile time (the
+// common shapes: constant indexing, unrolled dot loops), or 0: from the launch.
+template <int HD, int TP>
 __global__ void __launch_bounds__(kSbThreads, 1)
-    attn_stream_kernel(const __grid_constant__ StreamMaps maps, AttnParams p, int tp) {
+    attn_stream_kernel(const __grid_constant__ StreamMaps maps, AttnParams p, int tp_arg) {
     extern __shared__ __align__(128) unsigned char sm[];
-    const int hd = p.head_dim, H = p.heads, Hk = p.kv_heads, G = H / Hk, T = p.seq_len;
+    const int hd = HD > 0 ? HD : p.head_dim, H = p.heads, Hk = p.kv_heads, G = H / Hk, T = p.seq_len;
+    const int tp = TP > 0 ? TP : tp_arg;
     const int kvh = blockIdx.x, slot = blockIdx.y, tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const bool producer = warp == kSbWarps;
     const int Tp = (T + tp - 1) / tp * tp;
@@ -628,7 +632,7 @@ __global__ void __launch_bounds__(kSbThreads, 1)
         for (int r = 0; r < kMaxG; ++r) mx[r] = -INFINITY;
         for (int i = 0; i < nt; ++i) {
             const int s = i % kSbStages;
-            if (!mbar_wait_spin(&full[s], (uint32_t)((i / kSbStages) & 1))) {
+            if (!mbar_wait(&full[s], (uint32_t)((i / kSbStages) & 1))) {   // (suspends: no polling issue slots)
                 if (tid == 0) atomicOr(&g_attn_errors, 4u);
                 failed = 1;
             }
@@ -645,14 +649,27 @@ __global__ void __launch_bounds__(kSbThreads, 1)
                 if (tpos > pos) continue;
                 const int4* kr = reinterpret_cast<const int4*>(kt + (size_t)t * hd);
                 const int4* qr = reinterpret_cast<const int4*>(qs + r * hd);
-                int a = 0, c = t % vpr;
-                for (int j = 0; j < vpr; ++j) {
-                    const int4 x = kr[c], y = qr[c];
-                    c = c + 1 == vpr ? 0 : c + 1;
-                    a = dp4a(x.x, y.x, a);
-                    a = dp4a(x.y, y.y, a);
-                    a = dp4a(x.z, y.z, a);
-                    a = dp4a(x.w, y.w, a);
+                int a = 0;
+                if (HD > 0) {                                  // rows' words in a rotated order: conflict-free
+#pragma unroll
+                    for (int j = 0; j < HD / 16; ++j) {
+                        const int c = (t + j) & (HD / 16 - 1);
+                        const int4 x = kr[c], y = qr[c];
+                        a = dp4a(x.x, y.x, a);
+                        a = dp4a(x.y, y.y, a);
+                        a = dp4a(x.z, y.z, a);
+                        a = dp4a(x.w, y.w, a);
+                    }
+                } else {
+                    int c = t % vpr;
+                    for (int j = 0; j < vpr; ++j) {
+                        const int4 x = kr[c], y = qr[c];
+                        c = c + 1 == vpr ? 0 : c + 1;
+                        a = dp4a(x.x, y.x, a);
+                        a = dp4a(x.y, y.y, a);
+                        a = dp4a(x.z, y.z, a);
+                        a = dp4a(x.w, y.w, a);
+                    }
                 }
                 const float sc = fmul(fmul(i2f(a), sq[r]), p.a_k);
                 scs[r * Tp + tpos] = sc;
@@ -675,12 +692,15 @@ __global__ void __launch_bounds__(kSbThreads, 1)
             gmx[tid] = m;
         }
         named_barrier_sync(1, kSbWarps * 32);
-        // ---- the softmax over positions 0 .. pos of every row
+        // ---- the softmax over positions 0 .. pos of every row (row by row, four
+        // positions per thread)
         const int n = pos + 1;
+        constexpr int kC = kSbWarps * 32;                      // consumer threads
         if (p.variant == 0) {                                  // NORM: e, the ordered sum, p = i8(127 e / sum)
-            for (int i = tid; i < G * n; i += kSbWarps * 32) {
-                const int r = i / n, t = i % n;
-                scs[r * Tp + t] = sfu_exp_tab(fsub(scs[r * Tp + t], gmx[r]), etab, etab + 64);
+            for (int r = 0; r < G; ++r) {
+                float* er = scs + r * Tp;
+                const float m = gmx[r];
+                for (int t = tid; t < n; t += kC) er[t] = sfu_exp_tab(fsub(er[t], m), etab, etab + 64);
             }
             named_barrier_sync(1, kSbWarps * 32);
             for (int r = warp; r < G; r += kSbWarps) {
@@ -689,27 +709,32 @@ __global__ void __launch_bounds__(kSbThreads, 1)
                 if (lane == 0) rcp[r] = sfu_recip(ssum);
             }
             named_barrier_sync(1, kSbWarps * 32);
-            for (int i = tid; i < G * Tp; i += kSbWarps * 32) {
-                const int r = i / Tp, t = i % Tp;
-                ps[i] = t < n ? (int8_t)to_i8(fmul(fmul(scs[r * Tp + t], rcp[r]), 127.f)) : (int8_t)0;
+            for (int r = 0; r < G; ++r) {
+                const float* er = scs + r * Tp;
+                const float rr = rcp[r];
+                for (int t4 = 4 * tid; t4 < Tp; t4 += 4 * kC) {
+                    int q[4];
+#pragma unroll
+                    for (int u = 0; u < 4; ++u)
+                        q[u] = t4 + u < n ? to_i8(fmul(fmul(er[t4 + u], rr), 127.f)) : 0;
+                    *reinterpret_cast<char4*>(ps + r * Tp + t4) = make_char4(q[0], q[1], q[2], q[3]);
+                }
             }
         } else {                                               // QSUM: eq = i8(127 e) and its exact sum
-            int sum[kMaxG];
+            for (int r = 0; r < G; ++r) {
+                const float* sr = scs + r * Tp;
+                const float m = gmx[r];
+                int sum = 0;
+                for (int t4 = 4 * tid; t4 < Tp; t4 += 4 * kC) {
+                    int q[4];
 #pragma unroll
-            for (int r = 0; r < kMaxG; ++r) sum[r] = 0;
-            for (int i = tid; i < G * Tp; i += kSbWarps * 32) {
-                const int r = i / Tp, t = i % Tp;
-                int q = 0;
-                if (t < n) q = to_i8(fmul(sfu_exp_tab(fsub(scs[r * Tp + t], gmx[r]), etab, etab + 64), 127.f));
-                ps[i] = (int8_t)q;
-#pragma unroll
-                for (int rr = 0; rr < kMaxG; ++rr)
-                    if (rr == r) sum[rr] += q;
-            }
-#pragma unroll
-            for (int r = 0; r < kMaxG; ++r) {
-                const int v = warp_sum_i(sum[r]);
-                if (lane == 0 && r < G) wsum[warp][r] = v;
+                    for (int u = 0; u < 4; ++u)
+                        q[u] = t4 + u < n ? to_i8(fmul(sfu_exp_tab(fsub(sr[t4 + u], m), etab, etab + 64), 127.f)) : 0;
+                    *reinterpret_cast<char4*>(ps + r * Tp + t4) = make_char4(q[0], q[1], q[2], q[3]);
+                    sum += (q[0] + q[1]) + (q[2] + q[3]);
+                }
+                sum = warp_sum_i(sum);
+                if (lane == 0) wsum[warp][r] = sum;
             }
             named_barrier_sync(1, kSbWarps * 32);
             if (tid < G) {
@@ -728,7 +753,7 @@ __global__ void __launch_bounds__(kSbThreads, 1)
         const int nw = nv / 16, sl = tid & 15;                  // 16-byte words per row; this thread's slice
         for (int j = 0; j < nvt; ++j) {
             const int ri = nt + j, s = ri % kSbStages, c0 = j * cg;
-            if (!mbar_wait_spin(&full[s], (uint32_t)((ri / kSbStages) & 1))) {
+            if (!mbar_wait(&full[s], (uint32_t)((ri / kSbStages) & 1))) {
                 if (tid == 0) atomicOr(&g_attn_errors, 4u);
                 failed = 1;
             }
@@ -795,11 +820,13 @@ cudaError_t launch_attn_stream(const AttnParams& p, cudaStream_t st) {
     if (!make_map_u8(&maps.k, p.kc, (uint64_t)hd, krows, (uint64_t)hd, (uint32_t)hd, (uint32_t)tp, false))
         return cudaErrorInvalidValue;
     const size_t smem = sb_smem(G, hd, T, tp).total;
-    cudaError_t e = cudaFuncSetAttribute(attn_stream_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    auto kern = hd == 128 && tp == 128 ? attn_stream_kernel<128, 128>
+                : hd == 64 && tp == 128 ? attn_stream_kernel<64, 128> : attn_stream_kernel<0, 0>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
-    e = cudaFuncSetAttribute(attn_stream_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     if (e != cudaSuccess) return e;
-    return launch_k(attn_stream_kernel, dim3(p.kv_heads, p.slots), dim3(kSbThreads), smem, st, maps, p, tp);
+    return launch_k(kern, dim3(p.kv_heads, p.slots), dim3(kSbThreads), smem, st, maps, p, tp);
 }
 
 cudaError_t launch_attn(const AttnParams& q, cudaStream_t st) {
