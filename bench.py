@@ -311,6 +311,47 @@ def run_batch(args, cfg, qw, ws, rank, local):
         dist.destroy_process_group()
 
 
+def run_kernel(args, cfg):
+    """One kernel timed alone (the profiling case of `profiles/`): the batched
+    decode attention of one layer, --batch slots each attending 2041 positions
+    of its own seeded random int8 cache (K, V 2 x 2041 x head_dim bytes per
+    slot and KV head)."""
+    import hashlib
+
+    import torch
+    from torch2riscv_accelerator_b200 import ops
+    from torch2riscv_accelerator_b200.weights import kv_consts, rope_tables
+    D, Hk, hd, T = args.batch, cfg.kv_heads, cfg.head_dim, cfg.seq_len
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(args.seed + 1)
+    kc = torch.randint(-127, 128, (D, Hk, T, hd), dtype=torch.int8, device=dev, generator=g)
+    vc = torch.randint(-127, 128, (D, Hk, hd, T), dtype=torch.int8, device=dev, generator=g)
+    qkv = torch.randn(D, cfg.qkv_dim, device=dev, generator=g)
+    pos = torch.full((D,), T - 8, dtype=torch.int32, device=dev)
+    att = torch.zeros(D, cfg.q_dim, device=dev)
+    cos, sin = [torch.as_tensor(a).to(dev) for a in rope_tables(cfg)]
+    gain = torch.ones(hd, device=dev) if cfg.qk_norm else None
+    scratch = ops.attn_scratch(1, cfg.heads, Hk, hd, T, dev)
+    a = ops.attn_args(cfg, 1, pos, qkv, kc[0], vc[0], att, kv_consts(0.05, 0.04, hd), cos, sin, scratch, gain, gain)
+    for _ in range(args.warmup):
+        ops.attn_batch(a, D, Hk * T * hd)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        ops.attn_batch(a, D, Hk * T * hd)
+    e1.record()
+    torch.cuda.synchronize()
+    us = e0.elapsed_time(e1) / args.steps * 1e3
+    nbytes = D * Hk * 2 * (T - 7) * hd
+    peak, peak_src = peaks()
+    print(json.dumps({"kernel": "attn_stream_kernel", "config": {"model": cfg.name, "slots": D, "positions": T - 7},
+                      "us_per_launch": us, "bytes_per_launch": nbytes, "GBs": nbytes / us / 1e3,
+                      "frac": nbytes / us / 1e3 / peak, "peak": peak, "peak_source": peak_src,
+                      "att_sha": hashlib.sha256(att.cpu().numpy().tobytes()).hexdigest()[:16],
+                      "error_flags": ops.error_flags()}), flush=True)
+
+
 def config_of(cfg, args, ws, tp=False, ep=False):
     P = cfg.seq_len - args.warmup - args.steps
     if ep:
@@ -350,6 +391,9 @@ def main():
                     help="sequences per step (BatchLlamaDevice); > 1 measures batched decode instead")
     ap.add_argument("--parallel", default="tp", choices=["tp", "replicas"],
                     help="with several GPUs: one sequence tensor-parallel (tp) or independent replicas")
+    ap.add_argument("--kernel", choices=["attn_batch"],
+                    help="time one kernel alone instead (profiling): attn_batch = the batched decode attention "
+                         "over one layer's caches of --batch slots at position 2040")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
@@ -361,6 +405,9 @@ def main():
     if args.impl == "reference":
         run_reference(args, cfg, ws, rank)
         barrier(ws)
+        return
+    if args.kernel:
+        run_kernel(args, cfg)
         return
 
     import torch

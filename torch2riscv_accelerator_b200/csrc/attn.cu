@@ -449,11 +449,16 @@ unsigned int attn_read_clear_errors() {
 // exchange. The current position's K / V row is written to the cache and
 // patched into its tile when that tile lands. Same arithmetic, step for step,
 // as the cluster kernel above (and so as a one-row decode).
+// Ring stages and CTAs per SM of the batched kernel: 3 x 3 measured best at
+// 128 slots of the Qwen3 shape (138 us; 4 stages x 2 CTAs 162 us)
 #ifndef W8A8_SB_STAGES
-#define W8A8_SB_STAGES 4
+#define W8A8_SB_STAGES 3
 #endif
 #ifndef W8A8_SB_TP
 #define W8A8_SB_TP 128
+#endif
+#ifndef W8A8_SB_MINB
+#define W8A8_SB_MINB 3
 #endif
 constexpr int kSbStages = W8A8_SB_STAGES;                      // ring stages
 constexpr int kSbTile = W8A8_SB_TP;                            // cache positions per tile (at most)
@@ -483,7 +488,7 @@ __host__ __device__ inline SbSmem sb_smem(int G, int hd, int T, int tp) {
     s.scs = o;  o += a16((size_t)G * Tp * 4);                 // scores / e of every position, per row
     s.ps = o;   o += a16((size_t)G * Tp);                     // int8 p
     s.qs = o;   o += a16((size_t)G * hd);
-    s.fbuf = o; o += a16((size_t)2 * kSbWarps * hd * 4);      // per-warp fp32 head vectors (q | k)
+    s.fbuf = o; o += a16((size_t)((G < kSbWarps ? G : kSbWarps) + 1) * hd * 4);   // fp32 q rows (a warp each), the K row
     s.tab = o;  o += a16((size_t)2 * hd * 4);                 // cos | sin of the slot's position
     s.gain = o; o += a16((size_t)2 * hd * 4);                 // q_norm | k_norm
     s.etab = o; o += a16(128 * 4);
@@ -496,7 +501,7 @@ __host__ __device__ inline SbSmem sb_smem(int G, int hd, int T, int tp) {
 // HD, TP: head_dim and positions per K tile when known at compile time (the
 // common shapes: constant indexing, unrolled dot loops), or 0: from the launch.
 template <int HD, int TP>
-__global__ void __launch_bounds__(kSbThreads, 1)
+__global__ void __launch_bounds__(kSbThreads, W8A8_SB_MINB)
     attn_stream_kernel(const __grid_constant__ StreamMaps maps, AttnParams p, int tp_arg) {
     extern __shared__ __align__(128) unsigned char sm[];
     const int hd = HD > 0 ? HD : p.head_dim, H = p.heads, Hk = p.kv_heads, G = H / Hk, T = p.seq_len;
@@ -607,7 +612,7 @@ __global__ void __launch_bounds__(kSbThreads, 1)
             __syncwarp();
         }
         if (warp == kSbWarps - 1) {
-            float* kb = fbuf + (kSbWarps + warp) * hd;
+            float* kb = fbuf + (G < kSbWarps ? G : kSbWarps) * hd;   // after the q rows' buffers
             const float* ksrc = qrow + q_dim + (size_t)kvh * hd;
             const float* vsrc = qrow + q_dim + kv_dim + (size_t)kvh * hd;
             for (int c = lane; c < hd; c += 32) kb[c] = ksrc[c];
@@ -651,15 +656,17 @@ __global__ void __launch_bounds__(kSbThreads, 1)
                 const int4* qr = reinterpret_cast<const int4*>(qs + r * hd);
                 int a = 0;
                 if (HD > 0) {                                  // rows' words in a rotated order: conflict-free
+                    int a0 = 0, a1 = 0, a2 = 0, a3 = 0;        // four independent chains
 #pragma unroll
                     for (int j = 0; j < HD / 16; ++j) {
                         const int c = (t + j) & (HD / 16 - 1);
                         const int4 x = kr[c], y = qr[c];
-                        a = dp4a(x.x, y.x, a);
-                        a = dp4a(x.y, y.y, a);
-                        a = dp4a(x.z, y.z, a);
-                        a = dp4a(x.w, y.w, a);
+                        a0 = dp4a(x.x, y.x, a0);
+                        a1 = dp4a(x.y, y.y, a1);
+                        a2 = dp4a(x.z, y.z, a2);
+                        a3 = dp4a(x.w, y.w, a3);
                     }
+                    a = (a0 + a1) + (a2 + a3);
                 } else {
                     int c = t % vpr;
                     for (int j = 0; j < vpr; ++j) {
@@ -757,16 +764,11 @@ __global__ void __launch_bounds__(kSbThreads, 1)
                 if (tid == 0) atomicOr(&g_attn_errors, 4u);
                 failed = 1;
             }
-            int8_t* vt = ring + (size_t)s * stage_bytes;        // [cg][nv]
-            for (int c = tid; c < cg; c += kSbWarps * 32) {    // the new column
-                vt[(size_t)c * nv + pos] = newv[c0 + c];
-                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");       // before the stage's next copy
-            }
-            named_barrier_sync(1, kSbWarps * 32);
+            const int8_t* vt = ring + (size_t)s * stage_bytes;  // [cg][nv]
             for (int o0 = 0; o0 < G * cg; o0 += kSbWarps * 32 / 16) {
                 const int o = o0 + (tid >> 4);
                 const int r = o / cg, cl = o - r * cg;
-                int a0 = 0, a1 = 0;
+                int a0 = 0, a1 = 0, a2 = 0, a3 = 0;
                 if (o < G * cg) {
                     const int4* vr = reinterpret_cast<const int4*>(vt + (size_t)cl * nv);
                     const int4* pp = reinterpret_cast<const int4*>(ps + (size_t)r * Tp);
@@ -774,15 +776,19 @@ __global__ void __launch_bounds__(kSbThreads, 1)
                         const int4 x = pp[w], y = vr[w];
                         a0 = dp4a(x.x, y.x, a0);
                         a1 = dp4a(x.y, y.y, a1);
-                        a0 = dp4a(x.z, y.z, a0);
-                        a1 = dp4a(x.w, y.w, a1);
+                        a2 = dp4a(x.z, y.z, a2);
+                        a3 = dp4a(x.w, y.w, a3);
                     }
                 }
-                int a = a0 + a1;
+                int a = (a0 + a1) + (a2 + a3);
 #pragma unroll
                 for (int m = 8; m > 0; m >>= 1) a += __shfl_xor_sync(0xffffffffu, a, m);
                 if (sl == 0 && o < G * cg) {
                     const int c = c0 + cl;
+                    // the copy brought the cache's column pos before or after this
+                    // step's write: exchange it for the new V value (exact int32)
+                    const int pq = ps[(size_t)r * Tp + pos];
+                    a += pq * ((int)newv[c] - (int)vt[(size_t)cl * nv + pos]);
                     const float ov = i2f(a);
                     const float av = p.a_v_ch ? p.a_v_ch[kvh * hd + c] : p.a_v;   // V per channel or per layer
                     float out;
