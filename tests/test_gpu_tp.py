@@ -23,13 +23,13 @@ PREFILL, CHUNK2, FWD, STEPS = 40, 10, 5, 6
 CFG = C.C2.with_(layers=2, vocab=4096)
 
 
-def _model(kv=None, act="silu"):
+def _model(kv=None, act="silu", channel=""):
     """The test model: the quantized weights are elementwise functions of the
     seed (identical in every process); the KV scales come from one fp32
     calibration run (BLAS sums), made once in the parent and handed to the ranks."""
     cfg = CFG.with_(act=act)
     if kv is None:
-        qw = W.QuantWeights(cfg, seed=7, gains="random", calib_tokens=np.arange(8))
+        qw = W.QuantWeights(cfg, seed=7, gains="random", calib_tokens=np.arange(8), kv_channel=channel)
         kv = qw.kv_scales
     else:
         qw = W.QuantWeights(cfg, seed=7, gains="random")
@@ -81,13 +81,15 @@ def _port():
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
-@pytest.mark.parametrize("ranks,act", [(2, "silu"), (2, "gelu_tanh"), (4, "silu"), (8, "silu")])
-def test_tp_equals_one_gpu(ranks, act, tmp_path):
+@pytest.mark.parametrize("ranks,act,channel", [(2, "silu", ""), (2, "gelu_tanh", ""), (2, "silu", "kv"),
+                                               (4, "silu", ""), (8, "silu", "kv")])
+def test_tp_equals_one_gpu(ranks, act, channel, tmp_path):
+    """channel "kv": per-channel KV scales, each rank holding its KV heads' channels."""
     if torch.cuda.device_count() < ranks:
         pytest.skip(f"needs {ranks} GPUs")
     from torch2riscv_accelerator_b200.runtime import LlamaDevice
     path = str(tmp_path / "tp")
-    cfg, qw, kv, toks = _model(act=act)
+    cfg, qw, kv, toks = _model(act=act, channel=channel)
     mp.spawn(_worker, args=(ranks, _port(), path, kv, act), nprocs=ranks, join=True)
     ref = _run(LlamaDevice((cfg, qw, kv)), toks)
     for r in range(ranks):

@@ -440,7 +440,7 @@ unsigned int attn_read_clear_errors() {
 
 // ---------------------------------------------------------------------------
 // Batched decode: one CTA per (KV head, slot), no cluster. The slot's cache
-// streams through a 4-stage ring filled by a producer warp: its K rows as TMA
+// streams through a 3-stage ring filled by a producer warp: its K rows as TMA
 // tiles of tp positions x head_dim, then its V^T rows by channel group (cg
 // channels x positions 0 .. pos, one contiguous bulk copy per channel: V^T
 // tiles along positions would read 128-byte pieces of 2 KB rows, which the

@@ -293,15 +293,40 @@ static cudaError_t launch_gemm_t(const GemmOperands& a, const GemmParams& p, cud
     return launch_k(kern, grid, dim3(kGemmThreads), sm, st, maps, p);
 }
 
+// Tile width by an estimate of the GEMM's time: waves of CTAs (one per SM) x
+// (a fixed cost per CTA + the bytes it streams, its 128-row A slab and its
+// BN-row weight slab(s), at a per-CTA rate), with the constants fitted to
+// B200 timings (2 us, 40 GB/s). A GEMM of few rows (batched decode: one
+// 128-row tile) gets narrow tiles that spread the weight stream over the SMs;
+// long prefill chunks and the classifier keep 256-column tiles.
+static double gemm_cost(long tiles, int bn, int k, bool two, int sms) {
+    const long waves = (tiles + sms - 1) / sms;
+    return (double)waves * (2.0 + (double)(kBM + (two ? 2 : 1) * bn) * k / 40e3);
+}
+
 cudaError_t launch_gemm(const GemmOperands& a, const GemmParams& p, cudaStream_t st) {
-    if (a.w2 != nullptr) return launch_gemm_t<128, true>(a, p, st);
-    // 256-column tiles only when they still give every SM a tile
     int sms = 0, dev = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const long tiles256 = (long)((p.n + 255) / 256) * ((p.m + kBM - 1) / kBM);
-    if (tiles256 >= (sms > 0 ? sms : 148)) return launch_gemm_t<256, false>(a, p, st);
-    return launch_gemm_t<128, false>(a, p, st);
+    if (sms <= 0) sms = 148;
+    const bool two = a.w2 != nullptr;
+    const long mt = (p.m + kBM - 1) / kBM;
+    int best = 32;
+    double cbest = 1e300;
+    for (int bn : {32, 64, 128, 256}) {
+        if (two && bn > 128) continue;                         // 2 x BN TMEM columns
+        const double c = gemm_cost((long)((p.n + bn - 1) / bn) * mt, bn, p.k, two, sms);
+        if (c < cbest * (1.0 - 1e-9)) best = bn, cbest = c;   // ties: the narrower
+    }
+    if (two) {
+        if (best == 128) return launch_gemm_t<128, true>(a, p, st);
+        if (best == 64) return launch_gemm_t<64, true>(a, p, st);
+        return launch_gemm_t<32, true>(a, p, st);
+    }
+    if (best == 256) return launch_gemm_t<256, false>(a, p, st);
+    if (best == 128) return launch_gemm_t<128, false>(a, p, st);
+    if (best == 64) return launch_gemm_t<64, false>(a, p, st);
+    return launch_gemm_t<32, false>(a, p, st);
 }
 
 unsigned int gemm_read_clear_errors() {
