@@ -268,6 +268,16 @@ typedef struct {
  * (SahlKernels.h:155-177). */
 size_t w8a8_attn_scratch_bytes(int rows, int heads, int kv_heads, int head_dim, int seq_len);
 int w8a8_attn(const W8A8AttnArgs* args, void* stream);
+
+/* A prefill chunk of any number of rows of one sequence (rows at their own
+ * positions, e.g. 256): w8a8_kv_append writes every row's K and V (QK-norm,
+ * RoPE, int8, as w8a8_attn does) into the cache; then w8a8_attn_prefill runs
+ * the attention of all rows in one launch, in groups of 16 (each row attends
+ * t <= its position, all of them written). The same results as w8a8_attn over
+ * consecutive 16-row chunks (hf_generic._attention_rows :306-363, each chunk's
+ * K/V written before its attention), bit for bit. */
+int w8a8_kv_append(const W8A8AttnArgs* args, void* stream);
+int w8a8_attn_prefill(const W8A8AttnArgs* args, void* stream);
 /* One launch: a thread-block cluster of up to 8 CTAs per KV head, each CTA
  * holding a chunk of up to 512 cache positions in shared memory; the chunks
  * meet at the hardware cluster barrier and exchange maxima and int32 partial

@@ -251,6 +251,52 @@ def test_attention_bit_exact(case):
     assert same_bits(host(att), want)[0]
 
 
+PREFILL_CASES = [
+    (16, 8, 128, 2048, "qsum", True, list(range(100, 145))),      # 16 + 16 + 13 rows
+    (32, 8, 64, 2048, "qsum", False, list(range(1000, 1070))),     # across 128-position chunk boundaries
+    (6, 6, 48, 256, "norm", False, list(range(0, 40))),
+    (16, 8, 128, 2048, "norm", True, list(range(1990, 2048))),
+]
+
+
+@pytest.mark.parametrize("case", PREFILL_CASES)
+def test_prefill_attention_groups_bit_exact(case):
+    """A prefill chunk of more than 16 rows: every row's K/V appended
+    (w8a8_kv_append), then one attention launch in 16-row groups
+    (w8a8_attn_prefill): the outputs and the cache equal the oracle's (which
+    writes the chunk's rows before attending, as the reference's chunks do)."""
+    H, Hk, hd, T, variant, qkn, pos = case
+    cfg = C.ModelConfig("att", 64, 64, 1, H, Hk, hd, 64, T, theta=1e6, eps=1e-6, qk_norm=qkn, attn=variant,
+                        rope="hf")
+    rng = np.random.default_rng(hd + len(pos))
+    M, n0 = len(pos), min(pos)
+    qkv = (rng.standard_normal((M, cfg.qkv_dim)) * 2).astype(F)
+    kc = np.zeros((T, cfg.kv_dim), np.int8)
+    vc = np.zeros((T, cfg.kv_dim), np.int8)
+    kc[:n0] = rng.integers(-127, 128, (n0, cfg.kv_dim))
+    vc[:n0] = rng.integers(-127, 128, (n0, cfg.kv_dim))
+    qn = (1 + 0.1 * rng.standard_normal(hd)).astype(F) if qkn else None
+    kn = (1 + 0.1 * rng.standard_normal(hd)).astype(F) if qkn else None
+    cos, sin = rope_tables(cfg)
+    consts = kv_consts(F(0.05), F(0.03), hd)
+    dk = cu(kc.reshape(T, Hk, hd).transpose(1, 0, 2))
+    dv = cu(vc.reshape(T, Hk, hd).transpose(1, 2, 0))
+    att = torch.zeros(M, cfg.q_dim, device=DEV)
+    scratch = ops.attn_scratch(16, H, Hk, hd, T, DEV)
+    dqn, dkn = (cu(qn), cu(kn)) if qkn else (None, None)
+    args = ops.attn_args(cfg, M, cu(np.array(pos, np.int32)), cu(qkv), dk, dv, att, consts, cu(cos), cu(sin),
+                         scratch, dqn, dkn)
+    ops.kv_append(args)
+    ops.attn_prefill(args)
+    want = OM.attn_layer(cfg, qkv, pos, kc, vc, consts, cos, sin, qn, kn)
+    gk = host(dk).transpose(1, 0, 2).reshape(T, -1)
+    gv = host(dv).transpose(2, 0, 1).reshape(T, -1)
+    assert np.array_equal(gk, kc) and np.array_equal(gv, vc), "KV rows"
+    ok, bad = same_bits(host(att), want)
+    assert ok, bad
+    assert ops.error_flags() == 0
+
+
 def test_embed_out_of_range_token_sets_error_flag():
     """The embedding kernel's bounds check: a token outside the table reads
     nothing, writes a zero row and raises the device error flag."""

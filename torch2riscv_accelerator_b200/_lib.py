@@ -87,6 +87,8 @@ PROTOTYPES = {
     "w8a8_attn_scratch_bytes": (Z, [I, I, I, I, I]),
     "w8a8_attn": (I, [C.POINTER(W8A8AttnArgs), P]),
     "w8a8_attn_batch": (I, [C.POINTER(W8A8AttnArgs), I, Z, P]),
+    "w8a8_kv_append": (I, [C.POINTER(W8A8AttnArgs), P]),
+    "w8a8_attn_prefill": (I, [C.POINTER(W8A8AttnArgs), P]),
     "w8a8_argmax": (I, [P, I, I, P, P]),
     "w8a8_classifier": (I, [P, P, F, I, I, P, P, I, P, P, P]),
     "w8a8_decode_advance": (I, [P, P, P, P, I, P]),

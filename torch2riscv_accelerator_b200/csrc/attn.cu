@@ -132,15 +132,19 @@ __device__ __forceinline__ void warp_norm_rope(float* buf, int hd, const float* 
 __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
     extern __shared__ __align__(128) unsigned char sm[];
     cg::cluster_group cl = cg::this_cluster();
-    const int hd = p.head_dim, H = p.heads, Hk = p.kv_heads, G = H / Hk, M = p.rows, T = p.seq_len;
+    const int hd = p.head_dim, H = p.heads, Hk = p.kv_heads, G = H / Hk, T = p.seq_len;
     // batched decode: grid z is the slot (one row, its own position, qkv / att
-    // rows and caches); otherwise z = 0 and one sequence's M rows
-    const size_t b = blockIdx.z;
-    const int32_t* const pos_p = p.pos + b;
-    const float* const qkv_p = p.qkv + b * (size_t)(H + 2 * Hk) * hd;
-    float* const att_p = p.att + b * (size_t)H * hd;
-    int8_t* const kc_p = p.kc + b * p.slot_stride;
-    int8_t* const vc_p = p.vc + b * p.slot_stride;
+    // rows and caches); prefill groups: z is a group of <= 16 rows of one
+    // sequence (their K / V already in the cache); otherwise z = 0 and one
+    // sequence's M rows
+    const bool grp = p.groups > 0;
+    const size_t b = blockIdx.z, r0 = grp ? b * kMaxRows : b;
+    const int M = grp ? min(kMaxRows, p.rows - (int)r0) : p.rows;
+    const int32_t* const pos_p = p.pos + r0;
+    const float* const qkv_p = p.qkv + r0 * (size_t)(H + 2 * Hk) * hd;
+    float* const att_p = p.att + r0 * (size_t)H * hd;
+    int8_t* const kc_p = p.kc + (grp ? 0 : b * p.slot_stride);
+    int8_t* const vc_p = p.vc + (grp ? 0 : b * p.slot_stride);
     const int CH = p.chunk, CS = p.nsplit, MG = M * G;
     const int kvh = blockIdx.x, rank = (int)cl.block_rank(), t0 = rank * CH, tid = threadIdx.x;
     const int lane = tid & 31, warp = tid >> 5;
@@ -188,23 +192,28 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
         w = __reduce_xor_sync(0xffffffffu, w);
         if (lane == 0) rsum = __uint_as_float(w);             // (rsum is rewritten before any use)
     }
-    if (nvalid > 0) {
-        // the chunk's K rows: one contiguous block, one 1-D bulk copy (16-byte
-        // aligned: head_dim and the chunk start are multiples of 16)
+    // the chunk's cache tiles: K rows as one contiguous block by one 1-D bulk copy
+    // (16-byte aligned: head_dim and the chunk start are multiples of 16), the
+    // V^T rows (a short run of positions per channel: one bulk copy each would
+    // queue hundreds of small copies) by 16-byte loads. Before the wait when they
+    // hold earlier steps' rows; after it for prefill groups (the rows of this
+    // call were appended by the kernel before)
+    auto load_tiles = [&]() {
         if (tid == 0) {
             mbar_init(&tbar, 1);
             mbar_fence_init();
             mbar_expect_tx(&tbar, (uint32_t)(nvalid * hd));
             bulk_g2s(ks, kc_p + ((size_t)kvh * T + t0) * hd, (uint32_t)(nvalid * hd), &tbar);
         }
-        // the V^T rows: a short run of positions per channel (one bulk copy each
-        // would queue hundreds of small copies): 16-byte loads
         const int vw = nv16 / 16;                              // 16-byte words per V^T row
         for (int i = tid; i < hd * vw; i += kAttnThreads) {
             const int c = i / vw, w = i % vw;
             *reinterpret_cast<int4*>(vs + c * vstride + w * 16) =
-                __ldg(reinterpret_cast<const int4*>(vc_p + ((size_t)kvh * hd + c) * T + t0) + w);
+                __ldcg(reinterpret_cast<const int4*>(vc_p + ((size_t)kvh * hd + c) * T + t0) + w);
         }
+    };
+    if (nvalid > 0) {
+        if (!grp) load_tiles();
         for (int i = tid; i < M * hd; i += kAttnThreads) {
             const int m = i / hd, c = i % hd, pos = pos_p[m];
             tabs[2 * m * hd + c] = __ldg(p.cos + (size_t)pos * hd + c);
@@ -218,10 +227,11 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
     }
     pdl_wait();
     pdl_trigger();
+    if (grp && nvalid > 0) load_tiles();
     __syncthreads();
     bool tiles_ok = true;
     if (nvalid > 0) {
-        tiles_ok = mbar_wait(&tbar, 0u);                       // issued before the wait: landed by now
+        tiles_ok = mbar_wait(&tbar, 0u);                       // (issued before the wait: landed by now)
         if (!tiles_ok && tid == 0) atomicOr(&g_attn_errors, 4u);
     }
     if (nvalid > 0) {
@@ -251,7 +261,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
             __syncwarp();
         }
         // K and V rows of the positions in this chunk: into the cache and the tiles
-        for (int m = kAttnWarps - 1 - warp; m < M; m += kAttnWarps) {
+        // (prefill groups: already in both)
+        for (int m = kAttnWarps - 1 - warp; !grp && m < M; m += kAttnWarps) {
             const int pos = pos_p[m];
             if (pos < t0 || pos >= t0 + CH) continue;
             const float* ksrc = qkv_p + (size_t)m * qkv_dim + q_dim + (size_t)kvh * hd;
@@ -835,12 +846,47 @@ cudaError_t launch_attn_stream(const AttnParams& p, cudaStream_t st) {
     return launch_k(kern, dim3(p.kv_heads, p.slots), dim3(kSbThreads), smem, st, maps, p, tp);
 }
 
+// Prefill: every row's K and V (QK-norm + RoPE + int8, the attention kernel's
+// own arithmetic) into the cache, before one attention launch over all the
+// rows' groups. One CTA per row, one warp per KV head.
+__global__ void __launch_bounds__(kAttnThreads) kv_append_kernel(AttnParams p) {
+    extern __shared__ __align__(16) unsigned char kv_sm[];
+    const int hd = p.head_dim, H = p.heads, Hk = p.kv_heads, T = p.seq_len;
+    const int m = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int qkv_dim = (H + 2 * Hk) * hd, q_dim = H * hd, kv_dim = Hk * hd;
+    float* buf = reinterpret_cast<float*>(kv_sm) + warp * hd;
+    pdl_wait();
+    pdl_trigger();
+    const int pos = p.pos[m];
+    const float* row = p.qkv + (size_t)m * qkv_dim;
+    for (int h = warp; h < Hk; h += kAttnWarps) {
+        for (int c = lane; c < hd; c += 32) buf[c] = row[q_dim + h * hd + c];
+        __syncwarp();
+        warp_norm_rope(buf, hd, p.qk_norm ? p.k_norm : nullptr, p.eps, p.inv_hd, p.cos + (size_t)pos * hd,
+                       p.sin + (size_t)pos * hd, lane);
+        const float* vsrc = row + q_dim + kv_dim + (size_t)h * hd;
+        for (int c = lane; c < hd; c += 32) {
+            p.kc[((size_t)h * T + pos) * hd + c] =
+                (int8_t)to_i8(fmul(buf[c], p.inv_sk_ch ? p.inv_sk_ch[h * hd + c] : p.inv_sk));
+            p.vc[((size_t)h * hd + c) * T + pos] =
+                (int8_t)to_i8(fmul(vsrc[c], p.inv_sv_ch ? p.inv_sv_ch[h * hd + c] : p.inv_sv));
+        }
+        __syncwarp();
+    }
+}
+
+cudaError_t launch_kv_append(const AttnParams& p, cudaStream_t st) {
+    const size_t smem = (size_t)kAttnWarps * p.head_dim * 4;
+    return launch_k(kv_append_kernel, dim3(p.rows), dim3(kAttnThreads), smem, st, p);
+}
+
 cudaError_t launch_attn(const AttnParams& q, cudaStream_t st) {
     AttnParams p = q;
     const AttnGeom g = attn_geom(p.seq_len);
     p.nsplit = g.cs;
     p.chunk = g.chunk;
-    const AttnSmem L = attn_smem(p.rows, p.heads / p.kv_heads, p.head_dim, p.seq_len, p.chunk, p.variant);
+    const int mr = p.groups > 0 ? (p.rows < kMaxRows ? p.rows : kMaxRows) : p.rows;   // rows of a CTA, at most
+    const AttnSmem L = attn_smem(mr, p.heads / p.kv_heads, p.head_dim, p.seq_len, p.chunk, p.variant);
     cudaError_t e = cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.total);
     if (e != cudaSuccess) return e;
     // one shared-memory carveout for every kernel of the chain: no L1 / shared
@@ -848,7 +894,7 @@ cudaError_t launch_attn(const AttnParams& q, cudaStream_t st) {
     e = cudaFuncSetAttribute(attn_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3(p.kv_heads, g.cs, p.slots > 0 ? p.slots : 1);
+    cfg.gridDim = dim3(p.kv_heads, g.cs, p.slots > 0 ? p.slots : p.groups > 0 ? p.groups : 1);
     cfg.blockDim = dim3(kAttnThreads);
     cfg.dynamicSmemBytes = L.total;
     cfg.stream = st;

@@ -378,6 +378,31 @@ int w8a8_attn(const W8A8AttnArgs* a, void* stream) {
     return st ? st : cuda_status(launch_attn(p, S(stream)));
 }
 
+// rows of one sequence beyond 16 (a prefill chunk): checked as a 16-row call
+static int attn_rows_params(const W8A8AttnArgs* a, AttnParams* out) {
+    if (!a || a->rows <= 0 || a->rows > 65535 * kMaxRows) return W8A8_EINVAL;
+    W8A8AttnArgs c = *a;
+    c.rows = a->rows < kMaxRows ? a->rows : kMaxRows;
+    const int st = attn_params(&c, out);
+    if (st) return st;
+    out->rows = a->rows;
+    return W8A8_OK;
+}
+
+int w8a8_kv_append(const W8A8AttnArgs* a, void* stream) {
+    AttnParams p{};
+    const int st = attn_rows_params(a, &p);
+    return st ? st : cuda_status(launch_kv_append(p, S(stream)));
+}
+
+int w8a8_attn_prefill(const W8A8AttnArgs* a, void* stream) {
+    AttnParams p{};
+    const int st = attn_rows_params(a, &p);
+    if (st) return st;
+    p.groups = (a->rows + kMaxRows - 1) / kMaxRows;
+    return cuda_status(launch_attn(p, S(stream)));
+}
+
 int w8a8_attn_batch(const W8A8AttnArgs* a, int slots, size_t slot_stride, void* stream) {
     AttnParams p{};
     const int st = attn_params(a, &p);

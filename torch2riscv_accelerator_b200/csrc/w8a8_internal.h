@@ -103,6 +103,8 @@ struct AttnParams {
     int chunk;                // cache positions per CTA
     int slots;                // batched decode: sequences (one row each; grid z), or 0
     size_t slot_stride;       // bytes between consecutive slots' caches (batched decode)
+    int groups;               // prefill: grid z = groups of <= 16 of the rows, whose K / V rows
+                              // are already in the cache (kv_append); or 0
     uint32_t* amax_out;       // [rows or slots] max|att| per row by atomic max, or null (decode chain)
     // per cache channel [kv_heads * head_dim], or null for the per-layer scalars:
     // K's scale (folded into q before its quantization) and 1 / s_k; 1 / s_v, a_v
@@ -193,6 +195,7 @@ constexpr int kMaxCluster = 8;  // attention CTAs per KV head (portable cluster 
 size_t attn_smem_needed(int rows, int heads, int kv_heads, int head_dim, int seq_len, int variant);
 bool attn_supported(int rows, int heads, int kv_heads, int head_dim, int seq_len, int variant);
 cudaError_t launch_attn(const AttnParams& p, cudaStream_t st);
+cudaError_t launch_kv_append(const AttnParams& p, cudaStream_t st);   // rows' K / V into the cache
 // batched decode (p.slots > 0, one row per slot): the streaming kernel
 size_t attn_stream_smem(int heads, int kv_heads, int head_dim, int seq_len);
 cudaError_t launch_attn_stream(const AttnParams& p, cudaStream_t st);

@@ -185,9 +185,10 @@ class DeviceDecoder:
 
     def _run_rows(self, rows, logits_rows, argmax):
         """A prefill chunk of more than 16 rows: every linear as one tensor-core
-        GEMM over all rows (the row quantizer first), the attention and the MoE
-        FFN in 16-row sub-chunks (a row's results do not depend on the chunking:
-        each row attends its own positions, whose K/V earlier sub-chunks wrote)."""
+        GEMM over all rows (the row quantizer first); every row's K/V appended,
+        then one attention launch over the rows in 16-row groups; the MoE FFN in
+        16-row groups (a row's results do not depend on the chunking: each row
+        attends positions up to its own, all written first)."""
         c = self.cfg
         x, qkv, att, h = self.x[:rows], self.qkv[:rows], self.att[:rows], self.h[:rows]
         ops.embed(self.tokens[:rows], self.emb_q, self.emb_s, out=x)
@@ -195,8 +196,9 @@ class DeviceDecoder:
             xq, sx = self._q(rows, c.dim)
             ops.quant_rows(x, w["rms_att"], c.eps, xq=xq, s_x=sx)
             ops.gemm(xq, sx, w["wqkv"], w["s_wqkv"], out=qkv)
-            for j in range(0, rows, CHUNK):
-                ops.attn(self._sub_attn_args(l, j, min(CHUNK, rows - j)))
+            a = self._sub_attn_args(l, 0, rows)                 # all rows: K / V first, then one attention
+            ops.kv_append(a)
+            ops.attn_prefill(a)
             aq, sa = self._q(rows, c.q_dim)
             ops.quant_rows(att, None, 0.0, xq=aq, s_x=sa)
             ops.gemm(aq, sa, w["wo"], w["s_wo"], out=x, resid=x)

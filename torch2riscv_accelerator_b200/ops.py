@@ -252,6 +252,16 @@ def attn(args):
     _lib.check("w8a8_attn", _lib.load().w8a8_attn(ctypes.byref(args), _st()))
 
 
+def kv_append(args):
+    """Every row's K / V (args.rows rows, any number) into the cache."""
+    _lib.check("w8a8_kv_append", _lib.load().w8a8_kv_append(ctypes.byref(args), _st()))
+
+
+def attn_prefill(args):
+    """The attention of all args.rows rows (their K / V appended before) in one launch."""
+    _lib.check("w8a8_attn_prefill", _lib.load().w8a8_attn_prefill(ctypes.byref(args), _st()))
+
+
 def attn_batch(args, slots, slot_stride):
     """Batched decode attention: slot b = row b of pos / qkv / att, caches at
     + b * slot_stride bytes (args built for one row and slot 0's caches)."""

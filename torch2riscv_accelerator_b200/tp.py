@@ -261,8 +261,9 @@ class TpDecoder(DeviceDecoder):
             xq, sx = self._q(rows, c.dim)
             ops.quant_rows(x, w["rms_att"], c.eps, xq=xq, s_x=sx)
             ops.gemm(xq, sx, w["wqkv"], w["s_wqkv"], out=self.qkv[:rows])
-            for j in range(0, rows, CHUNK):
-                ops.attn(self._sub_attn_args(l, j, min(CHUNK, rows - j)))
+            a = self._sub_attn_args(l, 0, rows)
+            ops.kv_append(a)
+            ops.attn_prefill(a)
             row_split(self, self.att[:rows], w["wo"], w["s_wo"], x, self.comm.group)
             xq, sx = self._q(rows, c.dim)
             ops.quant_rows(x, w["rms_ffn"], c.eps, xq=xq, s_x=sx)
