@@ -223,6 +223,22 @@ int w8a8_moe_ffn_ep(const float* x, const float* norm_g, float eps, int rows, in
                     void* scratch, size_t scratch_bytes, void* stream);
 int w8a8_moe_combine(const float* wy, int rows, int top_k, int dim, const float* resid, float* y, void* stream);
 
+/* The MoE FFN of w8a8_moe_ffn (wy NULL: y = resid + the k-order fold, with
+ * expert_lo 0 and experts_local = experts) or of w8a8_moe_ffn_ep (wy non-NULL:
+ * the terms, resid and y unused) for up to W8A8_MOE_MAX_ROWS rows (batched
+ * decode, prefill chunks), the same results bit for bit. The rows' (row, slot)
+ * pairs are grouped by expert on the device, so each expert's weight tiles are
+ * read once per call rather than once per pair. scratch:
+ * w8a8_moe_rows_scratch_bytes() bytes. The reference runs the MoE per row
+ * (compiler/frontend/hf_generic.py:641-657); this is that loop over a batch. */
+#define W8A8_MOE_MAX_ROWS 4096
+size_t w8a8_moe_rows_scratch_bytes(int rows, int dim, int experts, int top_k, int expert_hidden);
+int w8a8_moe_ffn_rows(const float* x, const float* norm_g, float eps, int rows, int dim, const int8_t* router_q,
+                      const float* router_s, int experts, int top_k, int expert_lo, int experts_local,
+                      const int8_t* gate_q, const float* gate_s, const int8_t* up_q, const float* up_s,
+                      int expert_hidden, const int8_t* down_q, const float* down_s, const float* resid, float* y,
+                      float* wy, int32_t* ids, float* w, void* scratch, size_t scratch_bytes, void* stream);
+
 /* Fused per-layer attention of one sequence over its int8 KV cache. */
 typedef struct {
     int rows;                  /* query rows M (1: decode step, <= 16: prefill chunk) */

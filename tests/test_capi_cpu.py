@@ -94,6 +94,24 @@ def test_moe_argument_checks(lib):
     assert lib.w8a8_moe_scratch_bytes(1, 1024, 8, 512) == 1024 + 256 + 8 * 512 * 4 + 256
 
 
+def test_moe_rows_argument_checks(lib):
+    """The grouped MoE entry: up to W8A8_MOE_MAX_ROWS rows, the one-GPU form
+    (no wy) with all experts only, its own scratch size."""
+    def call(rows=64, lo=0, local=4, wy=None, sb=None, x=16):
+        sb = lib.w8a8_moe_rows_scratch_bytes(rows, 64, 4, 2, 128) if sb is None else sb
+        return lib.w8a8_moe_ffn_rows(x, None, ctypes.c_float(1e-6), rows, 64, 16, 16, 4, 2, lo, local, 16, 16, 16,
+                                     16, 128, 16, 16, 16, 16, wy, 16, 16, 16, sb, None)
+    assert call(rows=4097) == _lib.W8A8_EINVAL
+    assert call(lo=2, local=2) == _lib.W8A8_EINVAL                # one-GPU form: every expert
+    assert call(lo=3, local=2, wy=16) == _lib.W8A8_EINVAL         # past the router's experts
+    assert call(sb=lib.w8a8_moe_scratch_bytes(64, 64, 2, 128)) == _lib.W8A8_ESCRATCH
+    assert call(x=8) == _lib.W8A8_EALIGN
+    assert call(x=None) == _lib.W8A8_EINVAL
+    # + the terms [rows, top_k, dim], expert offsets, the pair list
+    assert (lib.w8a8_moe_rows_scratch_bytes(64, 64, 4, 2, 128) ==
+            lib.w8a8_moe_scratch_bytes(64, 64, 2, 128) + 64 * 2 * 64 * 4 + 256 + 512)
+
+
 def test_gemm_and_batch_argument_checks(lib):
     """The tensor-core GEMM, the row quantizer and the batched attention check
     their arguments before anything is queued."""

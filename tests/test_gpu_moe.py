@@ -81,3 +81,73 @@ def test_moe_c4_shape_against_oracle(rows):
         assert np.array_equal(ids[m], idm.astype(np.int32)), m
         assert np.array_equal(bits(w[m]), bits(wm)), m
         assert np.array_equal(bits(y[m]), bits((resid[m] + ym).astype(F))), m
+
+
+def run_rows(x, t, top_k, norm_g, eps, resid=None, expert_lo=0, local=None):
+    """The grouped entry (w8a8_moe_ffn_rows): y (resid given) or the terms of
+    experts [expert_lo, expert_lo + local)."""
+    m, dim = x.shape
+    E, ih = t["e_gate"].shape[:2]
+    local = E if local is None else local
+    sl = slice(expert_lo, expert_lo + local)
+    scratch = ops.moe_rows_scratch(m, dim, E, top_k, ih, DEV)
+    wy = None if resid is not None else torch.full((m, top_k, dim), float("nan"), device=DEV)
+    args = (cu(x), cu(norm_g), eps, cu(t["router"]), cu(t["s_router"]), top_k, cu(t["e_gate"][sl]),
+            cu(t["s_e_gate"][sl]), cu(t["e_up"][sl]), cu(t["s_e_up"][sl]), cu(t["e_down"][sl]),
+            cu(t["s_e_down"][sl]), scratch)
+    if resid is not None:
+        rd = cu(resid)
+        y, ids, w = ops.moe_ffn_rows(*args, resid=rd, out=rd)
+    else:
+        y, ids, w = ops.moe_ffn_rows(*args, expert_lo=expert_lo, wy=wy)
+    assert ops.error_flags() == 0
+    return host(y), host(ids), host(w)
+
+
+@pytest.mark.parametrize("rows", [17, 64, 203])
+def test_moe_grouped_rows_equal_per_row_path(rows):
+    """More than 16 rows grouped by expert: the same routing and outputs, bit
+    for bit, as the per-row kernels over 16-row groups; the first rows also
+    against the oracle."""
+    cfg = C.C4
+    rng = np.random.default_rng(70 + rows)
+    t = c4_tables(rng, cfg.experts, cfg.dim, cfg.expert_hidden)
+    x = rng.standard_normal((rows, cfg.dim)).astype(F)
+    g = (1 + 0.1 * rng.standard_normal(cfg.dim)).astype(F)
+    resid = rng.standard_normal((rows, cfg.dim)).astype(F)
+    y, ids, w = run_rows(x, t, cfg.top_k, g, cfg.eps, resid=resid)
+    for j in range(0, rows, 16):
+        yj, idj, wj = run(x[j:j + 16], t, cfg.top_k, norm_g=g, eps=cfg.eps, resid=resid[j:j + 16])
+        assert np.array_equal(ids[j:j + 16], idj), j
+        assert np.array_equal(bits(w[j:j + 16]), bits(wj)), j
+        assert np.array_equal(bits(y[j:j + 16]), bits(yj)), j
+    xn = N.rmsnorm(x, g, cfg.eps)
+    for m in range(3):
+        ym, _, _ = OM.moe_ffn_row(xn[m], t, cfg)
+        assert np.array_equal(bits(y[m]), bits((resid[m] + ym).astype(F))), m
+
+
+@pytest.mark.parametrize("ranks", [2, 4])
+def test_moe_grouped_rows_expert_parallel_terms(ranks):
+    """Expert parallelism through the grouped entry: each rank's terms are
+    w_j * y_j for its experts and +0 elsewhere, their sum folded by
+    w8a8_moe_combine equals the one-GPU result bit for bit."""
+    cfg = C.C4
+    rows = 40
+    rng = np.random.default_rng(90 + ranks)
+    t = c4_tables(rng, cfg.experts, cfg.dim, cfg.expert_hidden)
+    x = rng.standard_normal((rows, cfg.dim)).astype(F)
+    g = (1 + 0.1 * rng.standard_normal(cfg.dim)).astype(F)
+    resid = rng.standard_normal((rows, cfg.dim)).astype(F)
+    y, ids, w = run_rows(x, t, cfg.top_k, g, cfg.eps, resid=resid)
+    n = cfg.experts // ranks
+    total = np.zeros((rows, cfg.top_k, cfg.dim), F)
+    for r in range(ranks):
+        wy, idr, wr = run_rows(x, t, cfg.top_k, g, cfg.eps, expert_lo=r * n, local=n)
+        assert np.array_equal(idr, ids) and np.array_equal(bits(wr), bits(w))
+        mine = (idr >= r * n) & (idr < (r + 1) * n)
+        assert not np.isnan(wy).any()
+        assert np.all(bits(wy[~mine]) == 0)                       # +0 for other ranks' experts
+        total = (total + wy).astype(F)
+    out = ops.moe_combine(cu(total), cu(resid), torch.empty(rows, cfg.dim, device=DEV))
+    assert np.array_equal(bits(host(out)), bits(y))

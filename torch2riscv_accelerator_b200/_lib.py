@@ -84,6 +84,8 @@ PROTOTYPES = {
     "w8a8_moe_ffn": (I, [P, P, F, I, I, P, P, I, I, P, P, P, P, I, P, P, P, P, P, P, P, Z, P]),
     "w8a8_moe_ffn_ep": (I, [P, P, F, I, I, P, P, I, I, I, I, P, P, P, P, I, P, P, P, P, P, P, Z, P]),
     "w8a8_moe_combine": (I, [P, I, I, I, P, P, P]),
+    "w8a8_moe_rows_scratch_bytes": (Z, [I, I, I, I, I]),
+    "w8a8_moe_ffn_rows": (I, [P, P, F, I, I, P, P, I, I, I, I, P, P, P, P, I, P, P, P, P, P, P, P, P, Z, P]),
     "w8a8_attn_scratch_bytes": (Z, [I, I, I, I, I]),
     "w8a8_attn": (I, [C.POINTER(W8A8AttnArgs), P]),
     "w8a8_attn_batch": (I, [C.POINTER(W8A8AttnArgs), I, Z, P]),

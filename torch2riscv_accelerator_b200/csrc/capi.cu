@@ -282,19 +282,22 @@ static int moe_launch(const float* x, const float* norm_g, float eps, int rows, 
                       const float* gate_s, const int8_t* up_q, const float* up_s, int expert_hidden,
                       const int8_t* down_q, const float* down_s, const float* resid, float* y, float* wy,
                       int32_t* ids, float* w, void* scratch, size_t scratch_bytes, void* stream,
-                      const TpCtx* tp = nullptr, uint64_t* wy_ll = nullptr) {
+                      const TpCtx* tp = nullptr, uint64_t* wy_ll = nullptr, bool grouped = false) {
     if (!x || !router_q || !router_s || !gate_q || !gate_s || !up_q || !up_s || !down_q || !down_s ||
         !ids || !w || !scratch || (wy == nullptr && wy_ll == nullptr && (!resid || !y)))
         return W8A8_EINVAL;
     if (e_lo < 0 || e_n <= 0 || e_lo + e_n > experts) return W8A8_EINVAL;
-    if (rows <= 0 || rows > W8A8_MAX_ROWS || dim <= 0 || experts <= 0 || experts > kMoeMaxExperts || top_k <= 0 ||
+    if (rows <= 0 || rows > (grouped ? W8A8_MOE_MAX_ROWS : W8A8_MAX_ROWS) || dim <= 0 || experts <= 0 ||
+        experts > kMoeMaxExperts || top_k <= 0 ||
         top_k > kMoeMaxTopK || top_k > experts || expert_hidden <= 0)
         return W8A8_EINVAL;
     if (dim % 16 || expert_hidden % 16) return W8A8_EALIGN;
     if (!al16(x) || (norm_g && !al16(norm_g)) || !al16(router_q) || !al16(gate_q) || !al16(up_q) || !al16(down_q) ||
         !al16(scratch))
         return W8A8_EALIGN;
-    if (scratch_bytes < w8a8_moe_scratch_bytes(rows, dim, top_k, expert_hidden)) return W8A8_ESCRATCH;
+    if (scratch_bytes < (grouped ? w8a8_moe_rows_scratch_bytes(rows, dim, experts, top_k, expert_hidden)
+                                 : w8a8_moe_scratch_bytes(rows, dim, top_k, expert_hidden)))
+        return W8A8_ESCRATCH;
     MoeParams p{};
     p.m = rows, p.dim = dim, p.experts = experts, p.top_k = top_k, p.ih = expert_hidden;
     p.x = x, p.norm_g = norm_g, p.eps = eps, p.inv_dim = inv_of(dim);
@@ -310,9 +313,37 @@ static int moe_launch(const float* x, const float* norm_g, float eps, int rows, 
     p.h = reinterpret_cast<float*>(sp);
     sp += a256((size_t)rows * top_k * expert_hidden * 4);
     p.amax = reinterpret_cast<uint32_t*>(sp);
+    if (grouped) {
+        sp += a256((size_t)rows * top_k * 4);
+        if (p.wy == nullptr) p.wy = reinterpret_cast<float*>(sp);          // the terms, then the combine
+        sp += a256((size_t)rows * top_k * dim * 4);
+        p.offs = reinterpret_cast<int*>(sp);
+        sp += a256((size_t)(experts + 2) * 4);
+        p.pairs = reinterpret_cast<int*>(sp);
+        if (moe_smem(p, 0) > 200 * 1024 || moe_rows_smem(p, 1) > 200 * 1024 || moe_rows_smem(p, 2) > 200 * 1024)
+            return W8A8_EINVAL;
+        return cuda_status(launch_moe_rows(p, wy == nullptr, S(stream)));
+    }
     for (int i = 0; i < 3; ++i)
         if (moe_smem(p, i) > 200 * 1024) return W8A8_EINVAL;
     return cuda_status(launch_moe(p, S(stream)));
+}
+
+size_t w8a8_moe_rows_scratch_bytes(int rows, int dim, int experts, int top_k, int expert_hidden) {
+    if (rows <= 0 || dim <= 0 || experts <= 0 || top_k <= 0 || expert_hidden <= 0) return 0;
+    return w8a8_moe_scratch_bytes(rows, dim, top_k, expert_hidden) + a256((size_t)rows * top_k * dim * 4) +
+           a256((size_t)(experts + 2) * 4) + a256((size_t)rows * top_k * 4);
+}
+
+int w8a8_moe_ffn_rows(const float* x, const float* norm_g, float eps, int rows, int dim, const int8_t* router_q,
+                      const float* router_s, int experts, int top_k, int expert_lo, int experts_local,
+                      const int8_t* gate_q, const float* gate_s, const int8_t* up_q, const float* up_s,
+                      int expert_hidden, const int8_t* down_q, const float* down_s, const float* resid, float* y,
+                      float* wy, int32_t* ids, float* w, void* scratch, size_t scratch_bytes, void* stream) {
+    if (wy == nullptr && (expert_lo != 0 || experts_local != experts)) return W8A8_EINVAL;
+    return moe_launch(x, norm_g, eps, rows, dim, router_q, router_s, experts, top_k, expert_lo, experts_local,
+                      gate_q, gate_s, up_q, up_s, expert_hidden, down_q, down_s, wy ? nullptr : resid,
+                      wy ? nullptr : y, wy, ids, w, scratch, scratch_bytes, stream, nullptr, nullptr, true);
 }
 
 int w8a8_moe_ffn(const float* x, const float* norm_g, float eps, int rows, int dim, const int8_t* router_q,

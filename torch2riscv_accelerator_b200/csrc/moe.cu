@@ -320,6 +320,222 @@ cudaError_t launch_moe_combine_ll(const TpCtx& tp, const uint64_t* wy_ll, int m,
     return launch_k(moe_combine_ll_kernel, dim3(bx, m), dim3(kMoeThreads), 0, st, tp, wy_ll, top_k, dim, resid, y);
 }
 
+// ---------------------------------------------------------------- many rows
+// Batched decode and prefill chunks: the rows' (row, slot) pairs grouped by
+// expert, so that each expert's weight tiles are read once for all the rows that
+// chose it (the per-row kernels above read them once per pair). Launches: the
+// router (as above), the group lists, gate/up and down by (tile, expert), and
+// the k-order combine (moe_combine_kernel) unless the terms go out for an
+// expert-parallel sum. Each pair's arithmetic is the per-row kernels' own, so
+// the results are the same bit for bit.
+constexpr int kMoePairs = 4;                                   // pairs per pass of a grouped CTA
+
+// One CTA: the pairs (row * k + slot) by this rank's expert index, in row order
+// within an expert; bucket e_n holds the pairs of other ranks' experts.
+__global__ void __launch_bounds__(kMoeThreads) moe_group_kernel(MoeParams p) {
+    __shared__ int cnt[kMoeMaxExperts + 1], base[kMoeMaxExperts + 1];
+    pdl_wait();
+    pdl_trigger();
+    const int tid = threadIdx.x, B = p.e_n, n = p.m * p.top_k;
+    auto bucket = [&](int q) {
+        const int e = p.ids[q] - p.e_lo;
+        return e >= 0 && e < B ? e : B;
+    };
+    for (int e = tid; e <= B; e += kMoeThreads) cnt[e] = 0;
+    __syncthreads();
+    for (int q = tid; q < n; q += kMoeThreads) atomicAdd(&cnt[bucket(q)], 1);
+    __syncthreads();
+    if (tid == 0) {
+        int o = 0;
+        for (int e = 0; e <= B; ++e) base[e] = o, p.offs[e] = o, o += cnt[e];
+        p.offs[B + 1] = o;
+    }
+    __syncthreads();
+    // positions in q order: warp-serial over the pairs, a ballot per 32
+    if (tid < 32) {
+        for (int e = 0; e <= B; ++e) cnt[e] = 0;
+        __syncwarp();
+        for (int q0 = 0; q0 < n; q0 += 32) {
+            const int q = q0 + tid;
+            const int e = q < n ? bucket(q) : -1;
+            const unsigned same = __match_any_sync(0xffffffffu, e);
+            const int rank = __popc(same & ((1u << tid) - 1u));
+            if (e >= 0) p.pairs[base[e] + cnt[e] + rank] = q;
+            __syncwarp();
+            if (e >= 0 && rank == 0) cnt[e] += __popc(same);
+            __syncwarp();
+        }
+    }
+}
+
+// gate / up: CTA (tile, expert) holds the expert's 16 gate and up rows and
+// computes them for its pairs, kMoePairs at a time: h and each pair's max|h|.
+__global__ void __launch_bounds__(kMoeThreads) moe_up_rows_kernel(MoeParams p) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    const int tile = blockIdx.x, e = blockIdx.y, tid = threadIdx.x, lane = tid & 31;
+    const int K = p.top_k, dim = p.dim, ih = p.ih, i0 = tile * kMoeTile, nc = dim / 16;
+    int8_t* wg = reinterpret_cast<int8_t*>(smem);                        // gate rows [16][dim]
+    int8_t* wu = wg + (size_t)kMoeTile * dim;                            // up rows [16][dim]
+    int4* xs = reinterpret_cast<int4*>(wu + (size_t)kMoeTile * dim);     // [kMoePairs][dim]
+    __shared__ __align__(8) uint64_t bar;
+    if (tid == 0) {                                                       // the weights: constants
+        mbar_init(&bar, 1);
+        mbar_fence_init();
+        const uint32_t bytes = (uint32_t)(kMoeTile * dim);
+        mbar_expect_tx(&bar, 2u * bytes);
+        bulk_g2s(wg, p.gq + ((size_t)e * ih + i0) * dim, bytes, &bar);
+        bulk_g2s(wu, p.uq + ((size_t)e * ih + i0) * dim, bytes, &bar);
+    }
+    pdl_wait();
+    pdl_trigger();
+    __syncthreads();
+    const bool ok = mbar_wait(&bar, 0u);
+    if (!ok && tid == 0) atomicOr(&g_moe_errors, 8u);
+    const int q0 = p.offs[e], q1 = p.offs[e + 1];
+    const int r = tid / 16, sl = tid % 16, i = i0 + r;
+    const float gs = __ldg(p.gs + (size_t)e * ih + i), us = __ldg(p.us + (size_t)e * ih + i);
+    const int4* ga = reinterpret_cast<const int4*>(wg + (size_t)r * dim);
+    const int4* ua = reinterpret_cast<const int4*>(wu + (size_t)r * dim);
+    for (int q = q0; q < q1 && ok; q += kMoePairs) {
+        const int np = min(kMoePairs, q1 - q);
+        for (int c = tid; c < np * nc; c += kMoeThreads) {
+            const int row = p.pairs[q + c / nc] / K;
+            xs[c] = __ldcg(reinterpret_cast<const int4*>(p.xq + (size_t)row * dim) + c % nc);
+        }
+        __syncthreads();
+        int ag[kMoePairs], au[kMoePairs];
+#pragma unroll
+        for (int j = 0; j < kMoePairs; ++j) ag[j] = 0, au[j] = 0;
+        for (int c = sl; c < nc; c += 16) {
+            const int4 a = ga[c], b = ua[c];
+#pragma unroll
+            for (int j = 0; j < kMoePairs; ++j) {
+                if (j < np) {
+                    const int4 x = xs[j * nc + c];
+                    ag[j] = dp4a(a.w, x.w, dp4a(a.z, x.z, dp4a(a.y, x.y, dp4a(a.x, x.x, ag[j]))));
+                    au[j] = dp4a(b.w, x.w, dp4a(b.z, x.z, dp4a(b.y, x.y, dp4a(b.x, x.x, au[j]))));
+                }
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < kMoePairs; ++j) {
+#pragma unroll
+            for (int o = 8; o > 0; o >>= 1) {
+                ag[j] += __shfl_xor_sync(0xffffffffu, ag[j], o);
+                au[j] += __shfl_xor_sync(0xffffffffu, au[j], o);
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < kMoePairs; ++j) {
+            if (j < np) {                                                 // (np is the same on every thread)
+                const int pr = p.pairs[q + j];
+                uint32_t am = 0u;
+                if (sl == 0) {
+                    const float sx = __ldcg(p.s_x + pr / K);
+                    const float g = fmul(fmul(i2f(ag[j]), gs), sx);
+                    const float u = fmul(fmul(i2f(au[j]), us), sx);
+                    const float h = silu_gate(g, u);
+                    p.h[(size_t)pr * ih + i] = h;
+                    am = __float_as_uint(fabsf(h));                       // as bits: NaN above numbers
+                }
+#pragma unroll
+                for (int o = 16; o > 0; o >>= 1) am = max(am, __shfl_xor_sync(0xffffffffu, am, o));
+                if (lane == 0 && am != 0u) atomicMax(p.amax + pr, am);
+            }
+        }
+        __syncthreads();                                                  // xs free for the next pass
+    }
+    if (!ok) mbar_wait(&bar, 0u);                                         // no copy may land after exit
+}
+
+// down: CTA (tile, expert) holds the expert's 16 down rows and, kMoePairs pairs
+// at a time, requantizes their h (quant_act with each pair's max) and stores
+// w_j * y_j. CTAs (tile, e_n) store +0 for the pairs of other ranks' experts.
+__global__ void __launch_bounds__(kMoeThreads) moe_down_rows_kernel(MoeParams p) {
+    extern __shared__ __align__(128) unsigned char smem[];
+    const int tile = blockIdx.x, e = blockIdx.y, tid = threadIdx.x;
+    const int dim = p.dim, ih = p.ih, n0 = tile * kMoeTile, nc = ih / 16;
+    int8_t* wd = reinterpret_cast<int8_t*>(smem);                        // [16][ih] down rows
+    char4* hq = reinterpret_cast<char4*>(wd + (size_t)kMoeTile * ih);    // [kMoePairs][ih]
+    __shared__ __align__(8) uint64_t bar;
+    __shared__ float s_s[kMoePairs], inv_s[kMoePairs];
+    const bool own = e < p.e_n;
+    if (tid == 0 && own) {                                                // the weights: constants
+        mbar_init(&bar, 1);
+        mbar_fence_init();
+        const uint32_t bytes = (uint32_t)(kMoeTile * ih);
+        mbar_expect_tx(&bar, bytes);
+        bulk_g2s(wd, p.dq + ((size_t)e * dim + n0) * ih, bytes, &bar);
+    }
+    pdl_wait();
+    pdl_trigger();
+    const int q0 = p.offs[e], q1 = p.offs[e + 1];
+    if (!own) {                                                           // another rank's: +0
+        for (int t = tid; t < (q1 - q0) * kMoeTile; t += kMoeThreads)
+            p.wy[(size_t)p.pairs[q0 + t / kMoeTile] * dim + n0 + t % kMoeTile] = 0.f;
+        return;
+    }
+    __syncthreads();
+    const bool ok = mbar_wait(&bar, 0u);
+    if (!ok && tid == 0) atomicOr(&g_moe_errors, 8u);
+    const int r = tid / 16, sl = tid % 16, n = n0 + r;
+    const float ds = __ldg(p.ds + (size_t)e * dim + n);
+    const int4* a4 = reinterpret_cast<const int4*>(wd + (size_t)r * ih);
+    const int4* h4 = reinterpret_cast<const int4*>(hq);
+    for (int q = q0; q < q1 && ok; q += kMoePairs) {
+        const int np = min(kMoePairs, q1 - q);
+        if (tid < np) {
+            const float s = fmul(__uint_as_float(__ldcg(p.amax + p.pairs[q + tid])), W8A8_C127);
+            s_s[tid] = s;
+            inv_s[tid] = sfu_recip(s);
+        }
+        __syncthreads();
+        for (int c = tid; c < np * (ih / 4); c += kMoeThreads) {
+            const int j = c / (ih / 4);
+            const float4 v = __ldcg(reinterpret_cast<const float4*>(p.h + (size_t)p.pairs[q + j] * ih) + c % (ih / 4));
+            const float inv = inv_s[j];
+            hq[c] = make_char4(to_i8(fmul(v.x, inv)), to_i8(fmul(v.y, inv)), to_i8(fmul(v.z, inv)),
+                               to_i8(fmul(v.w, inv)));
+        }
+        __syncthreads();
+        int acc[kMoePairs];
+#pragma unroll
+        for (int j = 0; j < kMoePairs; ++j) acc[j] = 0;
+        for (int c = sl; c < nc; c += 16) {
+            const int4 a = a4[c];
+#pragma unroll
+            for (int j = 0; j < kMoePairs; ++j) {
+                if (j < np) {
+                    const int4 b = h4[j * nc + c];
+                    acc[j] = dp4a(a.w, b.w, dp4a(a.z, b.z, dp4a(a.y, b.y, dp4a(a.x, b.x, acc[j]))));
+                }
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < kMoePairs; ++j) {
+#pragma unroll
+            for (int o = 8; o > 0; o >>= 1) acc[j] += __shfl_xor_sync(0xffffffffu, acc[j], o);
+        }
+        if (sl == 0) {
+#pragma unroll
+            for (int j = 0; j < kMoePairs; ++j) {
+                if (j < np) {
+                    const int pr = p.pairs[q + j];
+                    const float yk = fmul(fmul(i2f(acc[j]), ds), s_s[j]);
+                    p.wy[(size_t)pr * dim + n] = fmul(__ldcg(p.w + pr), yk);
+                }
+            }
+        }
+        __syncthreads();                                                  // hq, s_s free for the next pass
+    }
+    if (!ok) mbar_wait(&bar, 0u);
+}
+
+size_t moe_rows_smem(const MoeParams& p, int which) {
+    if (which == 1) return (size_t)2 * kMoeTile * p.dim + (size_t)kMoePairs * p.dim;
+    return (size_t)kMoeTile * p.ih + (size_t)kMoePairs * p.ih;
+}
+
 // ---------------------------------------------------------------- host side
 size_t moe_smem(const MoeParams& p, int which) {
     if (which == 0) return (size_t)p.experts * p.dim + (size_t)p.dim * 5;
@@ -340,6 +556,25 @@ cudaError_t launch_moe(const MoeParams& p, cudaStream_t st) {
         if (e != cudaSuccess) return e;
     }
     return cudaSuccess;
+}
+
+cudaError_t launch_moe_rows(const MoeParams& p, bool combine, cudaStream_t st) {
+    struct L {
+        void (*k)(MoeParams);
+        dim3 grid;
+        size_t sm;
+    } ls[4] = {{moe_router_kernel, dim3(p.m), moe_smem(p, 0)},
+               {moe_group_kernel, dim3(1), 0},
+               {moe_up_rows_kernel, dim3(p.ih / kMoeTile, p.e_n), moe_rows_smem(p, 1)},
+               {moe_down_rows_kernel, dim3(p.dim / kMoeTile, p.e_n + (p.e_n < p.experts ? 1 : 0)),
+                moe_rows_smem(p, 2)}};
+    for (const L& l : ls) {
+        cudaError_t e = cudaFuncSetAttribute(l.k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)l.sm);
+        if (e != cudaSuccess) return e;
+        e = launch_k(l.k, l.grid, dim3(kMoeThreads), l.sm, st, p);
+        if (e != cudaSuccess) return e;
+    }
+    return combine ? launch_moe_combine(p.wy, p.m, p.top_k, p.dim, p.resid, p.y, st) : cudaSuccess;
 }
 
 unsigned int moe_read_clear_errors() {

@@ -178,11 +178,19 @@ struct MoeParams {
     // the previous combine included, are complete)
     TpCtx tp;
     uint64_t* wy_ll;
+    // many rows (grouped by expert): the pairs row * k + slot of this rank's
+    // expert e in pairs[offs[e] .. offs[e + 1]), of other ranks' experts in
+    // pairs[offs[e_n] .. offs[e_n + 1]) (built by the group kernel)
+    int* offs;
+    int* pairs;
 };
 size_t moe_smem(const MoeParams& p, int which);
 cudaError_t launch_moe(const MoeParams& p, cudaStream_t st);
 cudaError_t launch_moe_combine(const float* wy, int m, int top_k, int dim, const float* resid, float* y,
                                cudaStream_t st);
+// many rows, grouped by expert (combine: fold p.wy onto p.resid into p.y)
+cudaError_t launch_moe_rows(const MoeParams& p, bool combine, cudaStream_t st);
+size_t moe_rows_smem(const MoeParams& p, int which);
 cudaError_t launch_moe_combine_ll(const TpCtx& tp, const uint64_t* wy_ll, int m, int top_k, int dim,
                                   const float* resid, float* y, cudaStream_t st);
 unsigned int moe_read_clear_errors();

@@ -82,8 +82,8 @@ class EpDecoder(DeviceDecoder):
 
     def _moe_rows(self, l, x):
         """Decode rows: the terms over the exchange, then the combine. More
-        rows: every 16-row group's terms into one buffer, one all-reduce for all
-        rows, one k-order combine."""
+        rows: all rows' terms into one buffer (grouped by expert above 16 rows),
+        one all-reduce, one k-order combine."""
         c, w, rows = self.cfg, self.layers[l], x.shape[0]
         if hasattr(self, "comm") and self._exchange(rows):
             blk = self.comm.block(l, "moe")
@@ -93,11 +93,15 @@ class EpDecoder(DeviceDecoder):
             ops.tp_moe_combine(self.comm.c, blk, rows, c.top_k, x, x)
             return
         wy = self.wy[:rows]
-        for j in range(0, rows, CHUNK):
-            e = min(j + CHUNK, rows)
-            ops.moe_ffn_ep(x[j:e], w["rms_ffn"], c.eps, w["router"], w["s_router"], c.top_k, self.expert_lo,
+        if rows > CHUNK:                                       # grouped by expert
+            ops.moe_ffn_rows(x, w["rms_ffn"], c.eps, w["router"], w["s_router"], c.top_k, w["e_gate"],
+                             w["s_e_gate"], w["e_up"], w["s_e_up"], w["e_down"], w["s_e_down"],
+                             self.moe_rows_scratch, ids=self.moe_ids[l, :rows], w=self.moe_w[l, :rows],
+                             expert_lo=self.expert_lo, wy=wy)
+        else:
+            ops.moe_ffn_ep(x, w["rms_ffn"], c.eps, w["router"], w["s_router"], c.top_k, self.expert_lo,
                            w["e_gate"], w["s_e_gate"], w["e_up"], w["s_e_up"], w["e_down"], w["s_e_down"],
-                           self.moe_scratch, wy[j:e], self.moe_ids[l, j:e], self.moe_w[l, j:e])
+                           self.moe_scratch, wy, self.moe_ids[l, :rows], self.moe_w[l, :rows])
         dist.all_reduce(wy, op=dist.ReduceOp.SUM, group=self.group)
         ops.moe_combine(wy, x, out=x)
 
@@ -190,7 +194,10 @@ class EpBatchDecoder(BatchDecoder):
         raise RuntimeError("the expert-parallel step holds NCCL collectives: run it eagerly")
 
     def kernel_launches(self):
-        return super().kernel_launches() + self.cfg.layers                 # + the combine per layer
+        c = self.cfg
+        if self.slots > CHUNK:                                              # grouped: the combine already counted
+            return super().kernel_launches()
+        return super().kernel_launches() + c.layers                         # + the combine per layer
 
 
 class EpBatchLlamaDevice(BatchLlamaDevice):

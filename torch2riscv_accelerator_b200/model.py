@@ -87,6 +87,8 @@ class DeviceDecoder:
             self.moe_ids = z(cfg.layers, R, cfg.top_k, dt=I32)
             self.moe_w = z(cfg.layers, R, cfg.top_k)
             self.moe_scratch = ops.moe_scratch(CHUNK, cfg.dim, cfg.top_k, cfg.expert_hidden, self.dev)
+            self.moe_rows_scratch = (ops.moe_rows_scratch(R, cfg.dim, cfg.experts, cfg.top_k, cfg.expert_hidden,
+                                                          self.dev) if R > CHUNK else None)
         self._args = {}
         self._sub_args = {}
         self.graphs = {}
@@ -166,9 +168,15 @@ class DeviceDecoder:
                     ids=self.moe_ids[l, j:e], w=self.moe_w[l, j:e])
 
     def _moe_rows(self, l, x):
-        """The MoE FFN of layer l on all rows of x, in 16-row groups."""
-        for j in range(0, x.shape[0], CHUNK):
-            self._moe(l, x[j:j + CHUNK], j)
+        """The MoE FFN of layer l on all rows of x: more than 16 rows grouped by
+        expert (each expert's weights read once), else the per-row kernels."""
+        rows = x.shape[0]
+        if rows <= CHUNK:
+            return self._moe(l, x, 0)
+        c, w = self.cfg, self.layers[l]
+        ops.moe_ffn_rows(x, w["rms_ffn"], c.eps, w["router"], w["s_router"], c.top_k, w["e_gate"], w["s_e_gate"],
+                         w["e_up"], w["s_e_up"], w["e_down"], w["s_e_down"], self.moe_rows_scratch, resid=x, out=x,
+                         ids=self.moe_ids[l, :rows], w=self.moe_w[l, :rows])
 
     def _sub_attn_args(self, l, j, m):
         a = self._sub_args.get((l, j, m))
@@ -333,13 +341,15 @@ class BatchDecoder:
             self.moe_ids = z(L, D, cfg.top_k, dt=I32)
             self.moe_w = z(L, D, cfg.top_k)
             self.moe_scratch = ops.moe_scratch(CHUNK, cfg.dim, cfg.top_k, cfg.expert_hidden, self.dev)
+            self.moe_rows_scratch = (ops.moe_rows_scratch(D, cfg.dim, cfg.experts, cfg.top_k, cfg.expert_hidden,
+                                                          self.dev) if D > CHUNK else None)
         self.args = [ops.attn_args(cfg, 1, self.pos, self.qkv, self.kc[0, l], self.vc[0, l], self.att,
                                    self.consts[l], self.cos, self.sin, self.attn_scratch, w.get("q_norm"),
                                    w.get("k_norm"), ch=self.kv_ch[l])
                      for l, w in enumerate(self.layers)]
         self.graph = None
 
-    _moe = DeviceDecoder._moe                      # the MoE FFN of 16-row groups of slots
+    _moe = DeviceDecoder._moe                      # the MoE FFN of all slots
     _moe_rows = DeviceDecoder._moe_rows
 
     def _q(self, k):
@@ -389,5 +399,5 @@ class BatchDecoder:
 
     def kernel_launches(self):
         c = self.cfg
-        ffn = 3 * ((self.slots + CHUNK - 1) // CHUNK) if c.moe else 4
+        ffn = (5 if self.slots > CHUNK else 3) if c.moe else 4     # grouped: router, lists, up, down, combine
         return 1 + c.layers * (5 + ffn) + 2

@@ -216,6 +216,35 @@ def moe_ffn_ep(x, norm_g, eps, router_q, router_s, top_k, expert_lo, gate_q, gat
     return wy
 
 
+MOE_MAX_ROWS = 4096
+
+
+def moe_rows_scratch(rows, dim, experts, top_k, expert_hidden, device):
+    n = _lib.load().w8a8_moe_rows_scratch_bytes(rows, dim, experts, top_k, expert_hidden)
+    return torch.zeros(n, dtype=torch.uint8, device=device)
+
+
+def moe_ffn_rows(x, norm_g, eps, router_q, router_s, top_k, gate_q, gate_s, up_q, up_s, down_q, down_s, scratch,
+                 resid=None, out=None, ids=None, w=None, expert_lo=0, wy=None):
+    """moe_ffn (wy None) or moe_ffn_ep (wy given, expert_lo: this rank's first
+    expert) for many rows at once, the pairs grouped by expert; scratch from
+    moe_rows_scratch."""
+    _need(x, F32, "x")
+    m, dim = x.shape
+    experts, (local, ih) = router_q.shape[0], gate_q.shape[:2]
+    dev = x.device
+    if wy is None:
+        resid = x if resid is None else resid
+        out = torch.empty(m, dim, dtype=F32, device=dev) if out is None else out
+    ids = torch.empty(m, top_k, dtype=torch.int32, device=dev) if ids is None else ids
+    w = torch.empty(m, top_k, dtype=F32, device=dev) if w is None else w
+    _lib.check("w8a8_moe_ffn_rows", _lib.load().w8a8_moe_ffn_rows(
+        _p(x), _p(norm_g), float(eps), m, dim, _p(router_q), _p(router_s), experts, top_k, int(expert_lo), local,
+        _p(gate_q), _p(gate_s), _p(up_q), _p(up_s), ih, _p(down_q), _p(down_s), _p(resid), _p(out), _p(wy),
+        _p(ids), _p(w), _p(scratch), scratch.numel(), _st()))
+    return (out if wy is None else wy), ids, w
+
+
 def moe_combine(wy, resid, out):
     """out = resid + the k-order fold of wy [rows, top_k, dim]."""
     m, k, dim = wy.shape
