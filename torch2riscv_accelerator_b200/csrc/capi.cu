@@ -291,7 +291,7 @@ static int moe_launch(const float* x, const float* norm_g, float eps, int rows, 
         experts > kMoeMaxExperts || top_k <= 0 ||
         top_k > kMoeMaxTopK || top_k > experts || expert_hidden <= 0)
         return W8A8_EINVAL;
-    if (dim % 16 || expert_hidden % 16) return W8A8_EALIGN;
+    if (dim % (grouped ? 32 : 16) || expert_hidden % 16) return W8A8_EALIGN;
     if (!al16(x) || (norm_g && !al16(norm_g)) || !al16(router_q) || !al16(gate_q) || !al16(up_q) || !al16(down_q) ||
         !al16(scratch))
         return W8A8_EALIGN;

@@ -328,7 +328,9 @@ cudaError_t launch_moe_combine_ll(const TpCtx& tp, const uint64_t* wy_ll, int m,
 // the k-order combine (moe_combine_kernel) unless the terms go out for an
 // expert-parallel sum. Each pair's arithmetic is the per-row kernels' own, so
 // the results are the same bit for bit.
-constexpr int kMoePairs = 4;                                   // pairs per pass of a grouped CTA
+constexpr int kMoePairs = 16;                                  // pairs per pass of a grouped CTA
+constexpr int kMoeDownTile = 32;                               // down rows per grouped CTA
+constexpr int kMoePad = 16;                                    // bytes after each staged row (banks)
 
 // One CTA: the pairs (row * k + slot) by this rank's expert index, in row order
 // within an expert; bucket e_n holds the pairs of other ranks' experts.
@@ -368,16 +370,21 @@ __global__ void __launch_bounds__(kMoeThreads) moe_group_kernel(MoeParams p) {
     }
 }
 
-// gate / up: CTA (tile, expert) holds the expert's 16 gate and up rows and
-// computes them for its pairs, kMoePairs at a time: h and each pair's max|h|.
+// gate / up: CTA (tile, expert) holds the expert's 16 gate and up rows; per
+// pass, the int8 rows of up to 16 of its pairs. Thread (r, j) computes row
+// i0 + r of pair j over the whole dim: h and, through shared memory, the
+// pair's max|h| over the tile.
 __global__ void __launch_bounds__(kMoeThreads) moe_up_rows_kernel(MoeParams p) {
     extern __shared__ __align__(128) unsigned char smem[];
     const int tile = blockIdx.x, e = blockIdx.y, tid = threadIdx.x, lane = tid & 31;
-    const int K = p.top_k, dim = p.dim, ih = p.ih, i0 = tile * kMoeTile, nc = dim / 16;
+    const int K = p.top_k, dim = p.dim, ih = p.ih, i0 = tile * kMoeTile, nc = dim / 16, xstr = dim + kMoePad;
     int8_t* wg = reinterpret_cast<int8_t*>(smem);                        // gate rows [16][dim]
     int8_t* wu = wg + (size_t)kMoeTile * dim;                            // up rows [16][dim]
-    int4* xs = reinterpret_cast<int4*>(wu + (size_t)kMoeTile * dim);     // [kMoePairs][dim]
+    int8_t* xs = wu + (size_t)kMoeTile * dim;                            // [kMoePairs][dim + pad]
     __shared__ __align__(8) uint64_t bar;
+    __shared__ int pr_s[kMoePairs];
+    __shared__ float sx_s[kMoePairs];
+    __shared__ uint32_t am_s[kMoePairs];
     if (tid == 0) {                                                       // the weights: constants
         mbar_init(&bar, 1);
         mbar_fence_init();
@@ -388,82 +395,73 @@ __global__ void __launch_bounds__(kMoeThreads) moe_up_rows_kernel(MoeParams p) {
     }
     pdl_wait();
     pdl_trigger();
+    const int q0 = p.offs[e], q1 = p.offs[e + 1];
+    const int r = tid / kMoePairs, j = tid % kMoePairs, i = i0 + r;
+    const float gs = __ldg(p.gs + (size_t)e * ih + i), us = __ldg(p.us + (size_t)e * ih + i);
     __syncthreads();
     const bool ok = mbar_wait(&bar, 0u);
     if (!ok && tid == 0) atomicOr(&g_moe_errors, 8u);
-    const int q0 = p.offs[e], q1 = p.offs[e + 1];
-    const int r = tid / 16, sl = tid % 16, i = i0 + r;
-    const float gs = __ldg(p.gs + (size_t)e * ih + i), us = __ldg(p.us + (size_t)e * ih + i);
     const int4* ga = reinterpret_cast<const int4*>(wg + (size_t)r * dim);
     const int4* ua = reinterpret_cast<const int4*>(wu + (size_t)r * dim);
+    const int4* xa = reinterpret_cast<const int4*>(xs + (size_t)j * xstr);
     for (int q = q0; q < q1 && ok; q += kMoePairs) {
         const int np = min(kMoePairs, q1 - q);
-        for (int c = tid; c < np * nc; c += kMoeThreads) {
-            const int row = p.pairs[q + c / nc] / K;
-            xs[c] = __ldcg(reinterpret_cast<const int4*>(p.xq + (size_t)row * dim) + c % nc);
+        if (tid < np) {
+            const int pr = p.pairs[q + tid];
+            pr_s[tid] = pr;
+            sx_s[tid] = __ldcg(p.s_x + pr / K);
+            am_s[tid] = 0u;
         }
         __syncthreads();
-        int ag[kMoePairs], au[kMoePairs];
-#pragma unroll
-        for (int j = 0; j < kMoePairs; ++j) ag[j] = 0, au[j] = 0;
-        for (int c = sl; c < nc; c += 16) {
-            const int4 a = ga[c], b = ua[c];
-#pragma unroll
-            for (int j = 0; j < kMoePairs; ++j) {
-                if (j < np) {
-                    const int4 x = xs[j * nc + c];
-                    ag[j] = dp4a(a.w, x.w, dp4a(a.z, x.z, dp4a(a.y, x.y, dp4a(a.x, x.x, ag[j]))));
-                    au[j] = dp4a(b.w, x.w, dp4a(b.z, x.z, dp4a(b.y, x.y, dp4a(b.x, x.x, au[j]))));
-                }
-            }
+        for (int c = tid; c < np * nc; c += kMoeThreads) {                // every row of the pass at once
+            const int jj = c / nc, cc = c % nc;
+            reinterpret_cast<int4*>(xs + (size_t)jj * xstr)[cc] =
+                __ldcg(reinterpret_cast<const int4*>(p.xq + (size_t)(pr_s[jj] / K) * dim) + cc);
         }
-#pragma unroll
-        for (int j = 0; j < kMoePairs; ++j) {
-#pragma unroll
-            for (int o = 8; o > 0; o >>= 1) {
-                ag[j] += __shfl_xor_sync(0xffffffffu, ag[j], o);
-                au[j] += __shfl_xor_sync(0xffffffffu, au[j], o);
+        __syncthreads();
+        uint32_t am = 0u;
+        if (j < np) {
+            int ag = 0, au = 0;
+#pragma unroll 4
+            for (int c = 0; c < nc; ++c) {
+                const int4 a = ga[c], b = ua[c], x = xa[c];
+                ag = dp4a(a.w, x.w, dp4a(a.z, x.z, dp4a(a.y, x.y, dp4a(a.x, x.x, ag))));
+                au = dp4a(b.w, x.w, dp4a(b.z, x.z, dp4a(b.y, x.y, dp4a(b.x, x.x, au))));
             }
+            const float sx = sx_s[j];
+            const float g = fmul(fmul(i2f(ag), gs), sx);
+            const float u = fmul(fmul(i2f(au), us), sx);
+            const float h = silu_gate(g, u);
+            p.h[(size_t)pr_s[j] * ih + i] = h;
+            am = __float_as_uint(fabsf(h));                               // as bits: NaN above numbers
         }
-#pragma unroll
-        for (int j = 0; j < kMoePairs; ++j) {
-            if (j < np) {                                                 // (np is the same on every thread)
-                const int pr = p.pairs[q + j];
-                uint32_t am = 0u;
-                if (sl == 0) {
-                    const float sx = __ldcg(p.s_x + pr / K);
-                    const float g = fmul(fmul(i2f(ag[j]), gs), sx);
-                    const float u = fmul(fmul(i2f(au[j]), us), sx);
-                    const float h = silu_gate(g, u);
-                    p.h[(size_t)pr * ih + i] = h;
-                    am = __float_as_uint(fabsf(h));                       // as bits: NaN above numbers
-                }
-#pragma unroll
-                for (int o = 16; o > 0; o >>= 1) am = max(am, __shfl_xor_sync(0xffffffffu, am, o));
-                if (lane == 0 && am != 0u) atomicMax(p.amax + pr, am);
-            }
-        }
-        __syncthreads();                                                  // xs free for the next pass
+        am = max(am, __shfl_xor_sync(0xffffffffu, am, 16));               // rows r, r + 1: the same pair
+        if (lane < 16 && am != 0u) atomicMax(&am_s[j], am);
+        __syncthreads();
+        if (tid < np && am_s[tid] != 0u) atomicMax(p.amax + pr_s[tid], am_s[tid]);
+        __syncthreads();                                                  // xs, pr_s free for the next pass
     }
     if (!ok) mbar_wait(&bar, 0u);                                         // no copy may land after exit
 }
 
-// down: CTA (tile, expert) holds the expert's 16 down rows and, kMoePairs pairs
-// at a time, requantizes their h (quant_act with each pair's max) and stores
-// w_j * y_j. CTAs (tile, e_n) store +0 for the pairs of other ranks' experts.
+// down: CTA (tile, expert) holds 32 of the expert's down rows; per pass, up to
+// 16 of its pairs' h rows requantized (quant_act with each pair's max). Thread
+// (r, j) computes rows n0 + r and n0 + r + 16 of pair j and stores w_j * y_j.
+// CTAs (tile, e_n) store +0 for the pairs of other ranks' experts.
 __global__ void __launch_bounds__(kMoeThreads) moe_down_rows_kernel(MoeParams p) {
     extern __shared__ __align__(128) unsigned char smem[];
     const int tile = blockIdx.x, e = blockIdx.y, tid = threadIdx.x;
-    const int dim = p.dim, ih = p.ih, n0 = tile * kMoeTile, nc = ih / 16;
-    int8_t* wd = reinterpret_cast<int8_t*>(smem);                        // [16][ih] down rows
-    char4* hq = reinterpret_cast<char4*>(wd + (size_t)kMoeTile * ih);    // [kMoePairs][ih]
+    const int dim = p.dim, ih = p.ih, n0 = tile * kMoeDownTile, nc = ih / 16, hstr = ih + kMoePad;
+    int8_t* wd = reinterpret_cast<int8_t*>(smem);                        // [32][ih] down rows
+    int8_t* hq = wd + (size_t)kMoeDownTile * ih;                         // [kMoePairs][ih + pad]
     __shared__ __align__(8) uint64_t bar;
-    __shared__ float s_s[kMoePairs], inv_s[kMoePairs];
+    __shared__ int pr_s[kMoePairs];
+    __shared__ float s_s[kMoePairs], inv_s[kMoePairs], w_s[kMoePairs];
     const bool own = e < p.e_n;
     if (tid == 0 && own) {                                                // the weights: constants
         mbar_init(&bar, 1);
         mbar_fence_init();
-        const uint32_t bytes = (uint32_t)(kMoeTile * ih);
+        const uint32_t bytes = (uint32_t)(kMoeDownTile * ih);
         mbar_expect_tx(&bar, bytes);
         bulk_g2s(wd, p.dq + ((size_t)e * dim + n0) * ih, bytes, &bar);
     }
@@ -471,69 +469,59 @@ __global__ void __launch_bounds__(kMoeThreads) moe_down_rows_kernel(MoeParams p)
     pdl_trigger();
     const int q0 = p.offs[e], q1 = p.offs[e + 1];
     if (!own) {                                                           // another rank's: +0
-        for (int t = tid; t < (q1 - q0) * kMoeTile; t += kMoeThreads)
-            p.wy[(size_t)p.pairs[q0 + t / kMoeTile] * dim + n0 + t % kMoeTile] = 0.f;
+        for (int t = tid; t < (q1 - q0) * kMoeDownTile; t += kMoeThreads)
+            p.wy[(size_t)p.pairs[q0 + t / kMoeDownTile] * dim + n0 + t % kMoeDownTile] = 0.f;
         return;
     }
+    const int r = tid / kMoePairs, j = tid % kMoePairs, n = n0 + r;
+    const float ds0 = __ldg(p.ds + (size_t)e * dim + n), ds1 = __ldg(p.ds + (size_t)e * dim + n + 16);
     __syncthreads();
     const bool ok = mbar_wait(&bar, 0u);
     if (!ok && tid == 0) atomicOr(&g_moe_errors, 8u);
-    const int r = tid / 16, sl = tid % 16, n = n0 + r;
-    const float ds = __ldg(p.ds + (size_t)e * dim + n);
-    const int4* a4 = reinterpret_cast<const int4*>(wd + (size_t)r * ih);
-    const int4* h4 = reinterpret_cast<const int4*>(hq);
+    const int4* a0 = reinterpret_cast<const int4*>(wd + (size_t)r * ih);
+    const int4* a1 = reinterpret_cast<const int4*>(wd + (size_t)(r + 16) * ih);
+    const int4* ha = reinterpret_cast<const int4*>(hq + (size_t)j * hstr);
     for (int q = q0; q < q1 && ok; q += kMoePairs) {
         const int np = min(kMoePairs, q1 - q);
         if (tid < np) {
-            const float s = fmul(__uint_as_float(__ldcg(p.amax + p.pairs[q + tid])), W8A8_C127);
+            const int pr = p.pairs[q + tid];
+            pr_s[tid] = pr;
+            const float s = fmul(__uint_as_float(__ldcg(p.amax + pr)), W8A8_C127);
             s_s[tid] = s;
             inv_s[tid] = sfu_recip(s);
+            w_s[tid] = __ldcg(p.w + pr);
         }
         __syncthreads();
-        for (int c = tid; c < np * (ih / 4); c += kMoeThreads) {
-            const int j = c / (ih / 4);
-            const float4 v = __ldcg(reinterpret_cast<const float4*>(p.h + (size_t)p.pairs[q + j] * ih) + c % (ih / 4));
-            const float inv = inv_s[j];
-            hq[c] = make_char4(to_i8(fmul(v.x, inv)), to_i8(fmul(v.y, inv)), to_i8(fmul(v.z, inv)),
-                               to_i8(fmul(v.w, inv)));
+        for (int c = tid; c < np * (ih / 4); c += kMoeThreads) {          // every h row of the pass at once
+            const int jj = c / (ih / 4), cc = c % (ih / 4);
+            const float4 v = __ldcg(reinterpret_cast<const float4*>(p.h + (size_t)pr_s[jj] * ih) + cc);
+            const float inv = inv_s[jj];
+            reinterpret_cast<char4*>(hq + (size_t)jj * hstr)[cc] =
+                make_char4(to_i8(fmul(v.x, inv)), to_i8(fmul(v.y, inv)), to_i8(fmul(v.z, inv)),
+                           to_i8(fmul(v.w, inv)));
         }
         __syncthreads();
-        int acc[kMoePairs];
-#pragma unroll
-        for (int j = 0; j < kMoePairs; ++j) acc[j] = 0;
-        for (int c = sl; c < nc; c += 16) {
-            const int4 a = a4[c];
-#pragma unroll
-            for (int j = 0; j < kMoePairs; ++j) {
-                if (j < np) {
-                    const int4 b = h4[j * nc + c];
-                    acc[j] = dp4a(a.w, b.w, dp4a(a.z, b.z, dp4a(a.y, b.y, dp4a(a.x, b.x, acc[j]))));
-                }
+        if (j < np) {
+            int c0 = 0, c1 = 0;
+#pragma unroll 4
+            for (int c = 0; c < nc; ++c) {
+                const int4 x = ha[c], u = a0[c], v = a1[c];
+                c0 = dp4a(u.w, x.w, dp4a(u.z, x.z, dp4a(u.y, x.y, dp4a(u.x, x.x, c0))));
+                c1 = dp4a(v.w, x.w, dp4a(v.z, x.z, dp4a(v.y, x.y, dp4a(v.x, x.x, c1))));
             }
+            const int pr = pr_s[j];
+            const float s = s_s[j], w = w_s[j];
+            p.wy[(size_t)pr * dim + n] = fmul(w, fmul(fmul(i2f(c0), ds0), s));
+            p.wy[(size_t)pr * dim + n + 16] = fmul(w, fmul(fmul(i2f(c1), ds1), s));
         }
-#pragma unroll
-        for (int j = 0; j < kMoePairs; ++j) {
-#pragma unroll
-            for (int o = 8; o > 0; o >>= 1) acc[j] += __shfl_xor_sync(0xffffffffu, acc[j], o);
-        }
-        if (sl == 0) {
-#pragma unroll
-            for (int j = 0; j < kMoePairs; ++j) {
-                if (j < np) {
-                    const int pr = p.pairs[q + j];
-                    const float yk = fmul(fmul(i2f(acc[j]), ds), s_s[j]);
-                    p.wy[(size_t)pr * dim + n] = fmul(__ldcg(p.w + pr), yk);
-                }
-            }
-        }
-        __syncthreads();                                                  // hq, s_s free for the next pass
+        __syncthreads();                                                  // hq, pr_s free for the next pass
     }
     if (!ok) mbar_wait(&bar, 0u);
 }
 
 size_t moe_rows_smem(const MoeParams& p, int which) {
-    if (which == 1) return (size_t)2 * kMoeTile * p.dim + (size_t)kMoePairs * p.dim;
-    return (size_t)kMoeTile * p.ih + (size_t)kMoePairs * p.ih;
+    if (which == 1) return (size_t)2 * kMoeTile * p.dim + (size_t)kMoePairs * (p.dim + kMoePad);
+    return (size_t)kMoeDownTile * p.ih + (size_t)kMoePairs * (p.ih + kMoePad);
 }
 
 // ---------------------------------------------------------------- host side
@@ -566,7 +554,7 @@ cudaError_t launch_moe_rows(const MoeParams& p, bool combine, cudaStream_t st) {
     } ls[4] = {{moe_router_kernel, dim3(p.m), moe_smem(p, 0)},
                {moe_group_kernel, dim3(1), 0},
                {moe_up_rows_kernel, dim3(p.ih / kMoeTile, p.e_n), moe_rows_smem(p, 1)},
-               {moe_down_rows_kernel, dim3(p.dim / kMoeTile, p.e_n + (p.e_n < p.experts ? 1 : 0)),
+               {moe_down_rows_kernel, dim3(p.dim / kMoeDownTile, p.e_n + (p.e_n < p.experts ? 1 : 0)),
                 moe_rows_smem(p, 2)}};
     for (const L& l : ls) {
         cudaError_t e = cudaFuncSetAttribute(l.k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)l.sm);
