@@ -40,13 +40,14 @@ def test_batch_generate_slots_equal_single_sequences(graphs):
             assert seen[(b, p)].tobytes() == ref[p].tobytes(), (b, p)
 
 
-@pytest.mark.parametrize("moe,channel", [(False, ""), (True, ""), (False, "kv")])
-def test_batch_step_full_dims_mixed_positions(moe, channel):
-    """C2 (dense, QK-norm, 128-dim heads) or C4 (MoE) dimensions, 2 layers,
-    20 slots (GEMMs of 20 rows, MoE in groups of 16 and 4), each slot at its own
-    position after a slot-specific history; C2 also with per-channel KV scales
-    (the batched stream kernel's per-channel path)."""
-    cfg = (C.C4 if moe else C.C2).with_(layers=2, vocab=4096)
+@pytest.mark.parametrize("name,channel", [("C2", ""), ("C4", ""), ("C2", "kv"), ("C1", "")])
+def test_batch_step_full_dims_mixed_positions(name, channel):
+    """C2 (dense, QK-norm, 128-dim heads), C4 (MoE; 64-dim heads, 6 ring
+    stages) or C1 (3 query heads per KV head, 5 ring stages) dimensions, 2
+    layers, 20 slots (GEMMs of 20 rows, the MoE grouped by expert), each slot at
+    its own position after a slot-specific history; C2 also with per-channel KV
+    scales (the batched stream kernel's per-channel path)."""
+    cfg = getattr(C, name).with_(layers=2, vocab=4096)
     qw = W.QuantWeights(cfg, seed=7, gains="random", calib_tokens=np.arange(8), kv_channel=channel)
     kv = qw.kv_scales                                               # (per cache channel with "kv")
     D, steps = 20, 4

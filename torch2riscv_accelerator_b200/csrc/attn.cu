@@ -471,7 +471,8 @@ unsigned int attn_read_clear_errors() {
 #ifndef W8A8_SB_MINB
 #define W8A8_SB_MINB 3
 #endif
-constexpr int kSbStages = W8A8_SB_STAGES;                      // ring stages
+constexpr int kSbStages = W8A8_SB_STAGES;                      // ring stages (at least)
+constexpr int kSbMaxStages = 8;                                // ring stages (at most)
 constexpr int kSbTile = W8A8_SB_TP;                            // cache positions per tile (at most)
 constexpr int kSbThreads = 288;                                // 8 compute warps + 1 producer warp
 constexpr int kSbWarps = 8;
@@ -490,12 +491,12 @@ __host__ __device__ inline size_t sb_stage(int hd, int T, int tp) {
     return k > tp_round ? k : tp_round;
 }
 
-__host__ __device__ inline SbSmem sb_smem(int G, int hd, int T, int tp) {
+__host__ __device__ inline SbSmem sb_smem(int G, int hd, int T, int tp, int ns) {
     auto a16 = [](size_t b) { return (b + 15) & ~size_t(15); };
     const int Tp = (T + tp - 1) / tp * tp;
     SbSmem s{};
     size_t o = 0;
-    s.ring = o; o += a16((size_t)kSbStages * sb_stage(hd, T, tp));   // [stage]: a K tile or a V^T channel group
+    s.ring = o; o += a16((size_t)ns * sb_stage(hd, T, tp));   // [stage]: a K tile or a V^T channel group
     s.scs = o;  o += a16((size_t)G * Tp * 4);                 // scores / e of every position, per row
     s.ps = o;   o += a16((size_t)G * Tp);                     // int8 p
     s.qs = o;   o += a16((size_t)G * hd);
@@ -511,9 +512,11 @@ __host__ __device__ inline SbSmem sb_smem(int G, int hd, int T, int tp) {
 
 // HD, TP: head_dim and positions per K tile when known at compile time (the
 // common shapes: constant indexing, unrolled dot loops), or 0: from the launch.
-template <int HD, int TP>
-__global__ void __launch_bounds__(kSbThreads, W8A8_SB_MINB)
-    attn_stream_kernel(const __grid_constant__ StreamMaps maps, AttnParams p, int tp_arg) {
+// MINB: CTAs an SM must hold by registers (4: for shapes whose shared memory
+// allows 4, e.g. 64-dim heads with two query heads per KV head)
+template <int HD, int TP, int MINB = W8A8_SB_MINB>
+__global__ void __launch_bounds__(kSbThreads, MINB)
+    attn_stream_kernel(const __grid_constant__ StreamMaps maps, AttnParams p, int tp_arg, int ns) {
     extern __shared__ __align__(128) unsigned char sm[];
     const int hd = HD > 0 ? HD : p.head_dim, H = p.heads, Hk = p.kv_heads, G = H / Hk, T = p.seq_len;
     const int tp = TP > 0 ? TP : tp_arg;
@@ -521,7 +524,7 @@ __global__ void __launch_bounds__(kSbThreads, W8A8_SB_MINB)
     const bool producer = warp == kSbWarps;
     const int Tp = (T + tp - 1) / tp * tp;
     const int qkv_dim = (H + 2 * Hk) * hd, q_dim = H * hd, kv_dim = Hk * hd;
-    const SbSmem L = sb_smem(G, hd, T, tp);
+    const SbSmem L = sb_smem(G, hd, T, tp, ns);
     int8_t* ring = reinterpret_cast<int8_t*>(sm + L.ring);
     float* scs = reinterpret_cast<float*>(sm + L.scs);
     int8_t* ps = reinterpret_cast<int8_t*>(sm + L.ps);
@@ -532,7 +535,7 @@ __global__ void __launch_bounds__(kSbThreads, W8A8_SB_MINB)
     uint32_t* etab = reinterpret_cast<uint32_t*>(sm + L.etab);
     int8_t* newk = reinterpret_cast<int8_t*>(sm + L.newk);
     int8_t* newv = reinterpret_cast<int8_t*>(sm + L.newv);
-    __shared__ __align__(8) uint64_t full[kSbStages], empty[kSbStages];
+    __shared__ __align__(8) uint64_t full[kSbMaxStages], empty[kSbMaxStages];
     __shared__ float sq[kMaxG], gmx[kMaxG], wred[kSbWarps][kMaxG], rcp[kMaxG];
     __shared__ int wsum[kSbWarps][kMaxG], lsum[kMaxG];
     __shared__ int failed;
@@ -551,7 +554,7 @@ __global__ void __launch_bounds__(kSbThreads, W8A8_SB_MINB)
     const int nvt = hd / cg, ntiles = nt + nvt;
     if (tid == 0) {
         failed = 0;
-        for (int s = 0; s < kSbStages; ++s) {
+        for (int s = 0; s < ns; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kSbWarps);
         }
@@ -559,7 +562,7 @@ __global__ void __launch_bounds__(kSbThreads, W8A8_SB_MINB)
     }
     __syncthreads();
     auto issue = [&](int i) {                                  // ring tile i: K tile i, then V tile i - nt
-        const int s = i % kSbStages;
+        const int s = i % ns;
         int8_t* dst = ring + (size_t)s * stage_bytes;
         if (i < nt) {
             mbar_expect_tx(&full[s], tile_bytes);
@@ -571,7 +574,7 @@ __global__ void __launch_bounds__(kSbThreads, W8A8_SB_MINB)
         }
     };
     if (producer && lane == 0)                                 // cache rows of earlier steps: before the wait
-        for (int i = 0; i < kSbStages && i < ntiles; ++i) issue(i);
+        for (int i = 0; i < ns && i < ntiles; ++i) issue(i);
     if (tid < 64) {
         etab[tid] = g_exp_t[tid];
         etab[64 + tid] = g_exp_s[tid];
@@ -590,9 +593,9 @@ __global__ void __launch_bounds__(kSbThreads, W8A8_SB_MINB)
 
     if (producer) {
         if (lane == 0) {                                       // refill each stage once the 8 warps are done
-            for (int i = kSbStages; i < ntiles; ++i) {
-                const int s = i % kSbStages;
-                if (!mbar_wait_spin(&empty[s], (uint32_t)(((i / kSbStages) - 1) & 1))) {
+            for (int i = ns; i < ntiles; ++i) {
+                const int s = i % ns;
+                if (!mbar_wait(&empty[s], (uint32_t)(((i / ns) - 1) & 1))) {   // suspends: no issue slots
                     atomicOr(&g_attn_errors, 4u);
                     failed = 1;
                     break;
@@ -643,12 +646,20 @@ __global__ void __launch_bounds__(kSbThreads, W8A8_SB_MINB)
         named_barrier_sync(1, kSbWarps * 32);                  // q rows and the new K / V rows are ready
         // ---- pass 1: scores of positions <= pos; thread <-> (row, position of the tile)
         const int vpr = hd / 16;
-        float mx[kMaxG];
+        // running maxima: with a compile-time tile that divides the 256 consumer
+        // threads, pass k of a thread is always row tid / TP + k * (256 / TP) (one
+        // per warp); otherwise one per row, selected per position
+        constexpr bool kRowOf = TP > 0 && (kSbWarps * 32) % (TP > 0 ? TP : 1) == 0;
+        constexpr int kPasses = kRowOf ? (kMaxG * TP + kSbWarps * 32 - 1) / (kSbWarps * 32) : 1;
+        float mk[kPasses];
 #pragma unroll
-        for (int r = 0; r < kMaxG; ++r) mx[r] = -INFINITY;
+        for (int k = 0; k < kPasses; ++k) mk[k] = -INFINITY;
+        float mx[kRowOf ? 1 : kMaxG];
+#pragma unroll
+        for (int r = 0; r < (kRowOf ? 1 : kMaxG); ++r) mx[r] = -INFINITY;
         for (int i = 0; i < nt; ++i) {
-            const int s = i % kSbStages;
-            if (!mbar_wait(&full[s], (uint32_t)((i / kSbStages) & 1))) {   // (suspends: no polling issue slots)
+            const int s = i % ns;
+            if (!mbar_wait(&full[s], (uint32_t)((i / ns) & 1))) {   // (suspends: no polling issue slots)
                 if (tid == 0) atomicOr(&g_attn_errors, 4u);
                 failed = 1;
             }
@@ -660,7 +671,9 @@ __global__ void __launch_bounds__(kSbThreads, W8A8_SB_MINB)
                 }
                 named_barrier_sync(1, kSbWarps * 32);
             }
-            for (int pr = tid; pr < G * tp; pr += kSbWarps * 32) {
+#pragma unroll
+            for (int k = 0; k < (kRowOf ? kPasses : 1); ++k)
+            for (int pr = tid + k * kSbWarps * 32; pr < G * tp; pr += (kRowOf ? kPasses : 1) * kSbWarps * 32) {
                 const int r = pr / tp, t = pr % tp, tpos = i * tp + t;
                 if (tpos > pos) continue;
                 const int4* kr = reinterpret_cast<const int4*>(kt + (size_t)t * hd);
@@ -691,17 +704,32 @@ __global__ void __launch_bounds__(kSbThreads, W8A8_SB_MINB)
                 }
                 const float sc = fmul(fmul(i2f(a), sq[r]), p.a_k);
                 scs[r * Tp + tpos] = sc;
+                if constexpr (kRowOf) {
+                    mk[k] = nanmax(mk[k], sc);
+                } else {
 #pragma unroll
-                for (int rr = 0; rr < kMaxG; ++rr)
-                    if (rr == r) mx[rr] = nanmax(mx[rr], sc);
+                    for (int rr = 0; rr < (kRowOf ? 1 : kMaxG); ++rr)
+                        if (rr == r) mx[rr] = nanmax(mx[rr], sc);
+                }
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);
         }
+        if constexpr (kRowOf) {
+            if (lane < G) wred[warp][lane] = -INFINITY;              // rows this warp never visits
+            __syncwarp();
 #pragma unroll
-        for (int r = 0; r < kMaxG; ++r) {
-            const float m = warp_max(mx[r]);
-            if (lane == 0 && r < G) wred[warp][r] = m;
+            for (int k = 0; k < kPasses; ++k) {
+                const int pr0 = warp * 32 + k * kSbWarps * 32;      // the warp's first (row, position)
+                const float m = warp_max(mk[k]);
+                if (lane == 0 && pr0 < G * tp) wred[warp][pr0 / TP] = m;
+            }
+        } else {
+#pragma unroll
+            for (int r = 0; r < (kRowOf ? 1 : kMaxG); ++r) {
+                const float m = warp_max(mx[r]);
+                if (lane == 0 && r < G) wred[warp][r] = m;
+            }
         }
         named_barrier_sync(1, kSbWarps * 32);
         if (tid < G) {
@@ -770,8 +798,8 @@ __global__ void __launch_bounds__(kSbThreads, W8A8_SB_MINB)
         uint32_t am = 0u;
         const int nw = nv / 16, sl = tid & 15;                  // 16-byte words per row; this thread's slice
         for (int j = 0; j < nvt; ++j) {
-            const int ri = nt + j, s = ri % kSbStages, c0 = j * cg;
-            if (!mbar_wait(&full[s], (uint32_t)((ri / kSbStages) & 1))) {
+            const int ri = nt + j, s = ri % ns, c0 = j * cg;
+            if (!mbar_wait(&full[s], (uint32_t)((ri / ns) & 1))) {
                 if (tid == 0) atomicOr(&g_attn_errors, 4u);
                 failed = 1;
             }
@@ -820,12 +848,35 @@ __global__ void __launch_bounds__(kSbThreads, W8A8_SB_MINB)
     }
     __syncthreads();
     if (failed && producer && lane == 0)                       // no copy may land after the CTA exits
-        for (int s = 0; s < kSbStages; ++s) mbar_wait(&full[s], 0u), mbar_wait(&full[s], 1u);
+        for (int s = 0; s < ns; ++s) mbar_wait(&full[s], 0u), mbar_wait(&full[s], 1u);
 }
 
 size_t attn_stream_smem(int heads, int kv_heads, int head_dim, int seq_len) {
-    const int tp = seq_len < kSbTile ? seq_len : kSbTile;
-    return sb_smem(heads / kv_heads, head_dim, seq_len, tp).total;
+    const int tp = seq_len < kSbTile ? seq_len : kSbTile, G = heads / kv_heads;
+    return sb_smem(G, head_dim, seq_len, tp, kSbStages).total;             // (the launch may add stages)
+}
+
+using SbKernel = void (*)(StreamMaps, AttnParams, int, int);
+
+// Ring stages: the most CTAs on an SM first, then as many stages as keep that
+// count (small stages, as at head_dim 64, then hold more bytes in flight); at
+// least kSbStages. Each host thread keeps its last answer (one shape per model).
+static int sb_stages(SbKernel kern, int G, int hd, int T, int tp) {
+    static thread_local SbKernel c_kern = nullptr;
+    static thread_local int c_key[4] = {0, 0, 0, 0}, c_ns = 0;
+    if (kern == c_kern && c_key[0] == G && c_key[1] == hd && c_key[2] == T && c_key[3] == tp) return c_ns;
+    int best = kSbStages, occ_best = -1;
+    for (int ns = kSbStages; ns <= kSbMaxStages; ++ns) {
+        const size_t smem = sb_smem(G, hd, T, tp, ns).total;
+        if (smem > 200 * 1024) break;
+        int occ = 0;
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess ||
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, kern, kSbThreads, smem) != cudaSuccess)
+            break;
+        if (occ >= occ_best && occ > 0) best = ns, occ_best = occ;
+    }
+    c_kern = kern, c_key[0] = G, c_key[1] = hd, c_key[2] = T, c_key[3] = tp, c_ns = best;
+    return best;
 }
 
 cudaError_t launch_attn_stream(const AttnParams& p, cudaStream_t st) {
@@ -836,14 +887,24 @@ cudaError_t launch_attn_stream(const AttnParams& p, cudaStream_t st) {
     const uint64_t krows = (uint64_t)(p.slots - 1) * slot_k_rows + (uint64_t)p.kv_heads * T;
     if (!make_map_u8(&maps.k, p.kc, (uint64_t)hd, krows, (uint64_t)hd, (uint32_t)hd, (uint32_t)tp, false))
         return cudaErrorInvalidValue;
-    const size_t smem = sb_smem(G, hd, T, tp).total;
-    auto kern = hd == 128 && tp == 128 ? attn_stream_kernel<128, 128>
-                : hd == 64 && tp == 128 ? attn_stream_kernel<64, 128> : attn_stream_kernel<0, 0>;
+    SbKernel kern = hd == 128 && tp == 128 ? attn_stream_kernel<128, 128>
+                    : hd == 64 && tp == 128 ? attn_stream_kernel<64, 128> : attn_stream_kernel<0, 0>;
+    if (hd == 64 && tp == 128) {                               // 4 CTAs on an SM where the memory allows it
+        SbKernel k4 = attn_stream_kernel<64, 128, 4>;
+        const size_t sm3 = sb_smem(G, hd, T, tp, kSbStages).total;
+        int occ = 0;
+        if (sm3 <= 200 * 1024 &&
+            cudaFuncSetAttribute(k4, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm3) == cudaSuccess &&
+            cudaOccupancyMaxActiveBlocksPerMultiprocessor(&occ, k4, kSbThreads, sm3) == cudaSuccess && occ >= 4)
+            kern = k4;
+    }
+    const int ns = sb_stages(kern, G, hd, T, tp);
+    const size_t smem = sb_smem(G, hd, T, tp, ns).total;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return e;
     e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     if (e != cudaSuccess) return e;
-    return launch_k(kern, dim3(p.kv_heads, p.slots), dim3(kSbThreads), smem, st, maps, p, tp);
+    return launch_k(kern, dim3(p.kv_heads, p.slots), dim3(kSbThreads), smem, st, maps, p, tp, ns);
 }
 
 // Prefill: every row's K and V (QK-norm + RoPE + int8, the attention kernel's
