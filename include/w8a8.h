@@ -66,7 +66,9 @@ int w8a8_embed(const int32_t* tokens, int rows, const int8_t* emb_q, const float
  * bounded spin and the kernel stopped early; bit 2: an attention cache-tile
  * copy did not land within its bounded wait; bit 3: the same for an MoE weight
  * tile; bit 4: a tensor-core GEMM pipeline wait; bit 5: a tensor-parallel
- * exchange wait gave up). Synchronous with the device.
+ * exchange wait gave up; bit 6: w8a8_moe_ffn_rows found more pairs of one
+ * expert than rows, routing that is not Top-k, and skipped the excess).
+ * Synchronous with the device.
  * Plays the role of the overlay's sticky list status (llm/sa_funcsim.py:62-66,
  * firmware/rt/rt_fw.c:53-60). */
 int w8a8_error_flags(uint32_t* flags);

@@ -107,9 +107,9 @@ def test_moe_rows_argument_checks(lib):
     assert call(sb=lib.w8a8_moe_scratch_bytes(64, 64, 2, 128)) == _lib.W8A8_ESCRATCH
     assert call(x=8) == _lib.W8A8_EALIGN
     assert call(x=None) == _lib.W8A8_EINVAL
-    # + the terms [rows, top_k, dim], expert offsets, the pair list
+    # + the terms [rows, top_k, dim]
     assert (lib.w8a8_moe_rows_scratch_bytes(64, 64, 4, 2, 128) ==
-            lib.w8a8_moe_scratch_bytes(64, 64, 2, 128) + 64 * 2 * 64 * 4 + 256 + 512)
+            lib.w8a8_moe_scratch_bytes(64, 64, 2, 128) + 64 * 2 * 64 * 4)
 
 
 def test_gemm_and_batch_argument_checks(lib):

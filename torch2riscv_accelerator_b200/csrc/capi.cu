@@ -316,10 +316,6 @@ static int moe_launch(const float* x, const float* norm_g, float eps, int rows, 
     if (grouped) {
         sp += a256((size_t)rows * top_k * 4);
         if (p.wy == nullptr) p.wy = reinterpret_cast<float*>(sp);          // the terms, then the combine
-        sp += a256((size_t)rows * top_k * dim * 4);
-        p.offs = reinterpret_cast<int*>(sp);
-        sp += a256((size_t)(experts + 2) * 4);
-        p.pairs = reinterpret_cast<int*>(sp);
         if (moe_smem(p, 0) > 200 * 1024 || moe_rows_smem(p, 1) > 200 * 1024 || moe_rows_smem(p, 2) > 200 * 1024)
             return W8A8_EINVAL;
         return cuda_status(launch_moe_rows(p, wy == nullptr, S(stream)));
@@ -331,8 +327,7 @@ static int moe_launch(const float* x, const float* norm_g, float eps, int rows, 
 
 size_t w8a8_moe_rows_scratch_bytes(int rows, int dim, int experts, int top_k, int expert_hidden) {
     if (rows <= 0 || dim <= 0 || experts <= 0 || top_k <= 0 || expert_hidden <= 0) return 0;
-    return w8a8_moe_scratch_bytes(rows, dim, top_k, expert_hidden) + a256((size_t)rows * top_k * dim * 4) +
-           a256((size_t)(experts + 2) * 4) + a256((size_t)rows * top_k * 4);
+    return w8a8_moe_scratch_bytes(rows, dim, top_k, expert_hidden) + a256((size_t)rows * top_k * dim * 4);
 }
 
 int w8a8_moe_ffn_rows(const float* x, const float* norm_g, float eps, int rows, int dim, const int8_t* router_q,

@@ -23,7 +23,8 @@
 
 namespace w8a8 {
 
-__device__ unsigned int g_moe_errors;     // bit 3: a weight-tile copy wait gave up; bit 5: an exchange wait
+__device__ unsigned int g_moe_errors;     // bit 3: a weight-tile copy wait gave up; bit 5: an exchange wait;
+                                          // bit 6: more pairs of one expert than rows
 
 constexpr int kMoeThreads = 256;
 constexpr int kMoeTile = 16;                                   // expert rows per CTA (launches 2 and 3)
@@ -110,7 +111,6 @@ __global__ void __launch_bounds__(kMoeThreads) moe_up_kernel(MoeParams p) {
     int8_t* wu = wg + (size_t)kMoeTile * dim;                            // up rows [16][dim]
     int8_t* xs = wu + (size_t)kMoeTile * dim;                            // [dim]
     __shared__ __align__(8) uint64_t bar;
-    __shared__ float red[32];
     __shared__ int e_s;
     if (tid == 0) {
         mbar_init(&bar, 1);
@@ -324,7 +324,8 @@ cudaError_t launch_moe_combine_ll(const TpCtx& tp, const uint64_t* wy_ll, int m,
 // Batched decode and prefill chunks: the rows' (row, slot) pairs grouped by
 // expert, so that each expert's weight tiles are read once for all the rows that
 // chose it (the per-row kernels above read them once per pair). Launches: the
-// router (as above), the group lists, gate/up and down by (tile, expert), and
+// router (as above), gate/up and down by (tile, expert), each CTA listing its
+// expert's pairs from the routing, and
 // the k-order combine (moe_combine_kernel) unless the terms go out for an
 // expert-parallel sum. Each pair's arithmetic is the per-row kernels' own, so
 // the results are the same bit for bit.
@@ -332,42 +333,49 @@ constexpr int kMoePairs = 16;                                  // pairs per pass
 constexpr int kMoeDownTile = 32;                               // down rows per grouped CTA
 constexpr int kMoePad = 16;                                    // bytes after each staged row (banks)
 
-// One CTA: the pairs (row * k + slot) by this rank's expert index, in row order
-// within an expert; bucket e_n holds the pairs of other ranks' experts.
-__global__ void __launch_bounds__(kMoeThreads) moe_group_kernel(MoeParams p) {
-    __shared__ int cnt[kMoeMaxExperts + 1], base[kMoeMaxExperts + 1];
-    pdl_wait();
-    pdl_trigger();
-    const int tid = threadIdx.x, B = p.e_n, n = p.m * p.top_k;
-    auto bucket = [&](int q) {
-        const int e = p.ids[q] - p.e_lo;
-        return e >= 0 && e < B ? e : B;
-    };
-    for (int e = tid; e <= B; e += kMoeThreads) cnt[e] = 0;
-    __syncthreads();
-    for (int q = tid; q < n; q += kMoeThreads) atomicAdd(&cnt[bucket(q)], 1);
-    __syncthreads();
-    if (tid == 0) {
-        int o = 0;
-        for (int e = 0; e <= B; ++e) base[e] = o, p.offs[e] = o, o += cnt[e];
-        p.offs[B + 1] = o;
-    }
-    __syncthreads();
-    // positions in q order: warp-serial over the pairs, a ballot per 32
-    if (tid < 32) {
-        for (int e = 0; e <= B; ++e) cnt[e] = 0;
-        __syncwarp();
-        for (int q0 = 0; q0 < n; q0 += 32) {
-            const int q = q0 + tid;
-            const int e = q < n ? bucket(q) : -1;
-            const unsigned same = __match_any_sync(0xffffffffu, e);
-            const int rank = __popc(same & ((1u << tid) - 1u));
-            if (e >= 0) p.pairs[base[e] + cnt[e] + rank] = q;
-            __syncwarp();
-            if (e >= 0 && rank == 0) cnt[e] += __popc(same);
-            __syncwarp();
+// The pairs q = row * k + slot of this rank's expert e into list[], in q
+// order; their count. A row chooses an expert at most once, so at most m; list
+// holds cap = m entries, and a larger count (routing that is not Top-k) stores
+// none past it and sets error bit 6. Every thread of the CTA calls it (block
+// barriers inside). Each CTA scans the routing itself: one read of the ids, no
+// separate list launch.
+__device__ int moe_list_pairs(const MoeParams& p, int e, int* list, int cap) {
+    __shared__ int wcnt[kMoeThreads / 32];
+    constexpr int kPer = 8;                                       // ids per thread per round
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, n = p.m * p.top_k;
+    int total = 0;
+    for (int base = 0; base < n; base += kPer * kMoeThreads) {
+        int id[kPer];
+#pragma unroll
+        for (int u = 0; u < kPer; ++u) {                          // all loads of the round in flight
+            const int q = base + u * kMoeThreads + tid;
+            id[u] = q < n ? __ldcg(p.ids + q) : -1;
+        }
+#pragma unroll
+        for (int u = 0; u < kPer; ++u) {
+            if (base + u * kMoeThreads >= n) break;               // (uniform)
+            const int q = base + u * kMoeThreads + tid;
+            const bool mine = q < n && id[u] - p.e_lo == e;
+            const unsigned bal = __ballot_sync(0xffffffffu, mine);
+            if (lane == 0) wcnt[warp] = __popc(bal);
+            __syncthreads();
+            int off = total, all = 0;
+#pragma unroll
+            for (int w = 0; w < kMoeThreads / 32; ++w) {
+                off += w < warp ? wcnt[w] : 0;
+                all += wcnt[w];
+            }
+            const int at = off + __popc(bal & ((1u << lane) - 1u));
+            if (mine && at < cap) list[at] = q;
+            total += all;
+            __syncthreads();                                      // wcnt free for the next round
         }
     }
+    if (total > cap) {
+        if (tid == 0) atomicOr(&g_moe_errors, 64u);
+        total = cap;
+    }
+    return total;
 }
 
 // gate / up: CTA (tile, expert) holds the expert's 16 gate and up rows; per
@@ -381,6 +389,7 @@ __global__ void __launch_bounds__(kMoeThreads) moe_up_rows_kernel(MoeParams p) {
     int8_t* wg = reinterpret_cast<int8_t*>(smem);                        // gate rows [16][dim]
     int8_t* wu = wg + (size_t)kMoeTile * dim;                            // up rows [16][dim]
     int8_t* xs = wu + (size_t)kMoeTile * dim;                            // [kMoePairs][dim + pad]
+    int* list = reinterpret_cast<int*>(xs + (size_t)kMoePairs * xstr);  // [m]: this expert's pairs
     __shared__ __align__(8) uint64_t bar;
     __shared__ int pr_s[kMoePairs];
     __shared__ float sx_s[kMoePairs];
@@ -395,10 +404,9 @@ __global__ void __launch_bounds__(kMoeThreads) moe_up_rows_kernel(MoeParams p) {
     }
     pdl_wait();
     pdl_trigger();
-    const int q0 = p.offs[e], q1 = p.offs[e + 1];
+    const int q0 = 0, q1 = moe_list_pairs(p, e, list, p.m);             // (ends with a block barrier)
     const int r = tid / kMoePairs, j = tid % kMoePairs, i = i0 + r;
     const float gs = __ldg(p.gs + (size_t)e * ih + i), us = __ldg(p.us + (size_t)e * ih + i);
-    __syncthreads();
     const bool ok = mbar_wait(&bar, 0u);
     if (!ok && tid == 0) atomicOr(&g_moe_errors, 8u);
     const int4* ga = reinterpret_cast<const int4*>(wg + (size_t)r * dim);
@@ -407,7 +415,7 @@ __global__ void __launch_bounds__(kMoeThreads) moe_up_rows_kernel(MoeParams p) {
     for (int q = q0; q < q1 && ok; q += kMoePairs) {
         const int np = min(kMoePairs, q1 - q);
         if (tid < np) {
-            const int pr = p.pairs[q + tid];
+            const int pr = list[q + tid];
             pr_s[tid] = pr;
             sx_s[tid] = __ldcg(p.s_x + pr / K);
             am_s[tid] = 0u;
@@ -421,13 +429,17 @@ __global__ void __launch_bounds__(kMoeThreads) moe_up_rows_kernel(MoeParams p) {
         __syncthreads();
         uint32_t am = 0u;
         if (j < np) {
-            int ag = 0, au = 0;
+            int ag = 0, au = 0, ag1 = 0, au1 = 0;                        // two chains each (exact int32)
 #pragma unroll 4
-            for (int c = 0; c < nc; ++c) {
+            for (int c = 0; c < nc; c += 2) {                             // (nc even: dim % 32 == 0)
                 const int4 a = ga[c], b = ua[c], x = xa[c];
+                const int4 a1 = ga[c + 1], b1 = ua[c + 1], x1 = xa[c + 1];
                 ag = dp4a(a.w, x.w, dp4a(a.z, x.z, dp4a(a.y, x.y, dp4a(a.x, x.x, ag))));
                 au = dp4a(b.w, x.w, dp4a(b.z, x.z, dp4a(b.y, x.y, dp4a(b.x, x.x, au))));
+                ag1 = dp4a(a1.w, x1.w, dp4a(a1.z, x1.z, dp4a(a1.y, x1.y, dp4a(a1.x, x1.x, ag1))));
+                au1 = dp4a(b1.w, x1.w, dp4a(b1.z, x1.z, dp4a(b1.y, x1.y, dp4a(b1.x, x1.x, au1))));
             }
+            ag += ag1, au += au1;
             const float sx = sx_s[j];
             const float g = fmul(fmul(i2f(ag), gs), sx);
             const float u = fmul(fmul(i2f(au), us), sx);
@@ -454,6 +466,7 @@ __global__ void __launch_bounds__(kMoeThreads) moe_down_rows_kernel(MoeParams p)
     const int dim = p.dim, ih = p.ih, n0 = tile * kMoeDownTile, nc = ih / 16, hstr = ih + kMoePad;
     int8_t* wd = reinterpret_cast<int8_t*>(smem);                        // [32][ih] down rows
     int8_t* hq = wd + (size_t)kMoeDownTile * ih;                         // [kMoePairs][ih + pad]
+    int* list = reinterpret_cast<int*>(hq + (size_t)kMoePairs * hstr);  // [m]: this bucket's pairs
     __shared__ __align__(8) uint64_t bar;
     __shared__ int pr_s[kMoePairs];
     __shared__ float s_s[kMoePairs], inv_s[kMoePairs], w_s[kMoePairs];
@@ -467,15 +480,17 @@ __global__ void __launch_bounds__(kMoeThreads) moe_down_rows_kernel(MoeParams p)
     }
     pdl_wait();
     pdl_trigger();
-    const int q0 = p.offs[e], q1 = p.offs[e + 1];
-    if (!own) {                                                           // another rank's: +0
-        for (int t = tid; t < (q1 - q0) * kMoeDownTile; t += kMoeThreads)
-            p.wy[(size_t)p.pairs[q0 + t / kMoeDownTile] * dim + n0 + t % kMoeDownTile] = 0.f;
+    if (!own) {                                                           // other ranks' experts: +0
+        const int n = p.m * p.top_k;                                     // (up to k per row: no list)
+        for (int t = tid; t < n * kMoeDownTile; t += kMoeThreads) {
+            const int q = t / kMoeDownTile, x = __ldcg(p.ids + q) - p.e_lo;
+            if (x < 0 || x >= p.e_n) p.wy[(size_t)q * dim + n0 + t % kMoeDownTile] = 0.f;
+        }
         return;
     }
+    const int q0 = 0, q1 = moe_list_pairs(p, e, list, p.m);             // (ends with a block barrier)
     const int r = tid / kMoePairs, j = tid % kMoePairs, n = n0 + r;
     const float ds0 = __ldg(p.ds + (size_t)e * dim + n), ds1 = __ldg(p.ds + (size_t)e * dim + n + 16);
-    __syncthreads();
     const bool ok = mbar_wait(&bar, 0u);
     if (!ok && tid == 0) atomicOr(&g_moe_errors, 8u);
     const int4* a0 = reinterpret_cast<const int4*>(wd + (size_t)r * ih);
@@ -484,7 +499,7 @@ __global__ void __launch_bounds__(kMoeThreads) moe_down_rows_kernel(MoeParams p)
     for (int q = q0; q < q1 && ok; q += kMoePairs) {
         const int np = min(kMoePairs, q1 - q);
         if (tid < np) {
-            const int pr = p.pairs[q + tid];
+            const int pr = list[q + tid];
             pr_s[tid] = pr;
             const float s = fmul(__uint_as_float(__ldcg(p.amax + pr)), W8A8_C127);
             s_s[tid] = s;
@@ -520,8 +535,9 @@ __global__ void __launch_bounds__(kMoeThreads) moe_down_rows_kernel(MoeParams p)
 }
 
 size_t moe_rows_smem(const MoeParams& p, int which) {
-    if (which == 1) return (size_t)2 * kMoeTile * p.dim + (size_t)kMoePairs * (p.dim + kMoePad);
-    return (size_t)kMoeDownTile * p.ih + (size_t)kMoePairs * (p.ih + kMoePad);
+    const size_t list = (size_t)p.m * 4;                                 // a bucket holds at most one pair per row
+    if (which == 1) return (size_t)2 * kMoeTile * p.dim + (size_t)kMoePairs * (p.dim + kMoePad) + list;
+    return (size_t)kMoeDownTile * p.ih + (size_t)kMoePairs * (p.ih + kMoePad) + list;
 }
 
 // ---------------------------------------------------------------- host side
@@ -551,8 +567,7 @@ cudaError_t launch_moe_rows(const MoeParams& p, bool combine, cudaStream_t st) {
         void (*k)(MoeParams);
         dim3 grid;
         size_t sm;
-    } ls[4] = {{moe_router_kernel, dim3(p.m), moe_smem(p, 0)},
-               {moe_group_kernel, dim3(1), 0},
+    } ls[3] = {{moe_router_kernel, dim3(p.m), moe_smem(p, 0)},
                {moe_up_rows_kernel, dim3(p.ih / kMoeTile, p.e_n), moe_rows_smem(p, 1)},
                {moe_down_rows_kernel, dim3(p.dim / kMoeDownTile, p.e_n + (p.e_n < p.experts ? 1 : 0)),
                 moe_rows_smem(p, 2)}};

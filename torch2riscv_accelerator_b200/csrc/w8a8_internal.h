@@ -178,11 +178,6 @@ struct MoeParams {
     // the previous combine included, are complete)
     TpCtx tp;
     uint64_t* wy_ll;
-    // many rows (grouped by expert): the pairs row * k + slot of this rank's
-    // expert e in pairs[offs[e] .. offs[e + 1]), of other ranks' experts in
-    // pairs[offs[e_n] .. offs[e_n + 1]) (built by the group kernel)
-    int* offs;
-    int* pairs;
 };
 size_t moe_smem(const MoeParams& p, int which);
 cudaError_t launch_moe(const MoeParams& p, cudaStream_t st);

@@ -399,5 +399,5 @@ class BatchDecoder:
 
     def kernel_launches(self):
         c = self.cfg
-        ffn = (5 if self.slots > CHUNK else 3) if c.moe else 4     # grouped: router, lists, up, down, combine
+        ffn = (4 if self.slots > CHUNK else 3) if c.moe else 4     # grouped: router, up, down, combine
         return 1 + c.layers * (5 + ffn) + 2
