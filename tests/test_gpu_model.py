@@ -200,8 +200,9 @@ def test_c2_full_dims_two_layers_equals_oracle():
 def test_c4_moe_two_layers_equals_oracle():
     """Granite-MoE dimensions (dim 1024, 16/8 heads of 64, 32 experts, Top-8,
     expert hidden 512) truncated to 2 layers and a 4096-token vocabulary: the
-    MoE FFN in the decode chain, bit-exact with the oracle for a 20-token
-    prefill (a 16-row chunk, each row with its own Top-k) and 3 decode steps."""
+    MoE FFN bit-exact with the oracle for a 20-token prefill (the 20 rows'
+    MoE grouped by expert, each row with its own Top-k) and 3 decode steps
+    (the per-row kernels)."""
     cfg = C.C4.with_(layers=2, vocab=4096)
     qw = W.QuantWeights(cfg, seed=5, gains="random", calib_tokens=np.arange(8))
     dev = LlamaDevice((cfg, qw, qw.kv_scales))
