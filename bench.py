@@ -352,6 +352,59 @@ def run_kernel(args, cfg):
                       "error_flags": ops.error_flags()}), flush=True)
 
 
+def run_moe_kernel(args, cfg):
+    """The MoE FFN of one layer alone (the profiling case of `profiles/`):
+    --batch rows (more than 16) of a seeded random activation through
+    w8a8_moe_ffn_rows (router, grouped gate/up, grouped down, k-order combine:
+    4 launches a call) over seeded random int8 experts of the config's shape.
+    Algorithmic bytes: every expert's weights once, their scales, the router,
+    the rows in and out."""
+    import hashlib
+
+    import torch
+    from torch2riscv_accelerator_b200 import ops
+    if not cfg.moe or args.batch <= 16:
+        raise SystemExit("--kernel moe_rows wants a MoE config and --batch > 16")
+    D, dim, E, K, ih = args.batch, cfg.dim, cfg.experts, cfg.top_k, cfg.expert_hidden
+    dev = torch.device("cuda", 0)
+    g = torch.Generator(device=dev).manual_seed(args.seed + 2)
+    i8 = lambda *s: torch.randint(-127, 128, s, dtype=torch.int8, device=dev, generator=g)
+    sc = lambda *s: torch.rand(*s, device=dev, generator=g) * 1e-3 + 1e-4
+    router, s_router = i8(E, dim), sc(E)
+    gq, gs, uq, us, dq, ds = i8(E, ih, dim), sc(E, ih), i8(E, ih, dim), sc(E, ih), i8(E, dim, ih), sc(E, dim)
+    x = torch.randn(D, dim, device=dev, generator=g)
+    resid = torch.randn(D, dim, device=dev, generator=g)
+    norm_g = torch.ones(dim, device=dev)
+    out = torch.empty_like(x)
+    ids = torch.empty(D, K, dtype=torch.int32, device=dev)
+    w = torch.empty(D, K, device=dev)
+    scratch = ops.moe_rows_scratch(D, dim, E, K, ih, dev)
+
+    def call():
+        ops.moe_ffn_rows(x, norm_g, cfg.eps, router, s_router, K, gq, gs, uq, us, dq, ds, scratch, resid=resid,
+                         out=out, ids=ids, w=w)
+
+    for _ in range(args.warmup):
+        call()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(args.steps):
+        call()
+    e1.record()
+    torch.cuda.synchronize()
+    us_call = e0.elapsed_time(e1) / args.steps * 1e3
+    nbytes = E * 3 * ih * dim + 4 * E * (2 * ih + dim) + E * dim + 4 * E + 3 * 4 * D * dim
+    int_ops = 2 * D * K * 3 * ih * dim + 2 * D * E * dim
+    peak, peak_src = peaks()
+    print(json.dumps({"kernel": "moe_rows (router, up, down, combine)", "config": {"model": cfg.name, "rows": D,
+                      "experts": E, "top_k": K}, "us_per_call": us_call, "bytes_per_call": nbytes,
+                      "GBs": nbytes / us_call / 1e3, "frac": nbytes / us_call / 1e3 / peak, "peak": peak,
+                      "peak_source": peak_src, "int8_tops": int_ops / us_call / 1e6,
+                      "y_sha": hashlib.sha256(out.cpu().numpy().tobytes()).hexdigest()[:16],
+                      "error_flags": ops.error_flags()}), flush=True)
+
+
 def config_of(cfg, args, ws, tp=False, ep=False):
     P = cfg.seq_len - args.warmup - args.steps
     if ep:
@@ -391,9 +444,10 @@ def main():
                     help="sequences per step (BatchLlamaDevice); > 1 measures batched decode instead")
     ap.add_argument("--parallel", default="tp", choices=["tp", "replicas"],
                     help="with several GPUs: one sequence tensor-parallel (tp) or independent replicas")
-    ap.add_argument("--kernel", choices=["attn_batch"],
+    ap.add_argument("--kernel", choices=["attn_batch", "moe_rows"],
                     help="time one kernel alone instead (profiling): attn_batch = the batched decode attention "
-                         "over one layer's caches of --batch slots at position 2040")
+                         "over one layer's caches of --batch slots at position 2040; moe_rows = one layer's MoE "
+                         "FFN over --batch rows (a MoE --config)")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
@@ -407,7 +461,7 @@ def main():
         barrier(ws)
         return
     if args.kernel:
-        run_kernel(args, cfg)
+        (run_moe_kernel if args.kernel == "moe_rows" else run_kernel)(args, cfg)
         return
 
     import torch
