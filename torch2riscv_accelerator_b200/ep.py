@@ -93,15 +93,17 @@ class EpDecoder(DeviceDecoder):
             ops.tp_moe_combine(self.comm.c, blk, rows, c.top_k, x, x)
             return
         wy = self.wy[:rows]
-        if rows > CHUNK:                                       # grouped by expert
+        if rows > CHUNK and c.dim % 32 == 0:                   # grouped by expert
             ops.moe_ffn_rows(x, w["rms_ffn"], c.eps, w["router"], w["s_router"], c.top_k, w["e_gate"],
                              w["s_e_gate"], w["e_up"], w["s_e_up"], w["e_down"], w["s_e_down"],
                              self.moe_rows_scratch, ids=self.moe_ids[l, :rows], w=self.moe_w[l, :rows],
                              expert_lo=self.expert_lo, wy=wy)
         else:
-            ops.moe_ffn_ep(x, w["rms_ffn"], c.eps, w["router"], w["s_router"], c.top_k, self.expert_lo,
-                           w["e_gate"], w["s_e_gate"], w["e_up"], w["s_e_up"], w["e_down"], w["s_e_down"],
-                           self.moe_scratch, wy, self.moe_ids[l, :rows], self.moe_w[l, :rows])
+            for j in range(0, rows, CHUNK):
+                e = min(j + CHUNK, rows)
+                ops.moe_ffn_ep(x[j:e], w["rms_ffn"], c.eps, w["router"], w["s_router"], c.top_k, self.expert_lo,
+                               w["e_gate"], w["s_e_gate"], w["e_up"], w["s_e_up"], w["e_down"], w["s_e_down"],
+                               self.moe_scratch, wy[j:e], self.moe_ids[l, j:e], self.moe_w[l, j:e])
         dist.all_reduce(wy, op=dist.ReduceOp.SUM, group=self.group)
         ops.moe_combine(wy, x, out=x)
 
@@ -195,7 +197,7 @@ class EpBatchDecoder(BatchDecoder):
 
     def kernel_launches(self):
         c = self.cfg
-        if self.slots > CHUNK:                                              # grouped: the combine already counted
+        if self.slots > CHUNK and c.dim % 32 == 0:                          # grouped: the combine already counted
             return super().kernel_launches()
         return super().kernel_launches() + c.layers                         # + the combine per layer
 

@@ -88,7 +88,7 @@ class DeviceDecoder:
             self.moe_w = z(cfg.layers, R, cfg.top_k)
             self.moe_scratch = ops.moe_scratch(CHUNK, cfg.dim, cfg.top_k, cfg.expert_hidden, self.dev)
             self.moe_rows_scratch = (ops.moe_rows_scratch(R, cfg.dim, cfg.experts, cfg.top_k, cfg.expert_hidden,
-                                                          self.dev) if R > CHUNK else None)
+                                                          self.dev) if R > CHUNK and cfg.dim % 32 == 0 else None)
         self._args = {}
         self._sub_args = {}
         self.graphs = {}
@@ -169,11 +169,15 @@ class DeviceDecoder:
 
     def _moe_rows(self, l, x):
         """The MoE FFN of layer l on all rows of x: more than 16 rows grouped by
-        expert (each expert's weights read once), else the per-row kernels."""
+        expert (each expert's weights read once), else (or for a dim that is not
+        a multiple of 32, which the grouped kernels need) the per-row kernels in
+        16-row groups."""
         rows = x.shape[0]
-        if rows <= CHUNK:
-            return self._moe(l, x, 0)
         c, w = self.cfg, self.layers[l]
+        if rows <= CHUNK or c.dim % 32:
+            for j in range(0, rows, CHUNK):
+                self._moe(l, x[j:j + CHUNK], j)
+            return
         ops.moe_ffn_rows(x, w["rms_ffn"], c.eps, w["router"], w["s_router"], c.top_k, w["e_gate"], w["s_e_gate"],
                          w["e_up"], w["s_e_up"], w["e_down"], w["s_e_down"], self.moe_rows_scratch, resid=x, out=x,
                          ids=self.moe_ids[l, :rows], w=self.moe_w[l, :rows])
@@ -342,7 +346,7 @@ class BatchDecoder:
             self.moe_w = z(L, D, cfg.top_k)
             self.moe_scratch = ops.moe_scratch(CHUNK, cfg.dim, cfg.top_k, cfg.expert_hidden, self.dev)
             self.moe_rows_scratch = (ops.moe_rows_scratch(D, cfg.dim, cfg.experts, cfg.top_k, cfg.expert_hidden,
-                                                          self.dev) if D > CHUNK else None)
+                                                          self.dev) if D > CHUNK and cfg.dim % 32 == 0 else None)
         self.args = [ops.attn_args(cfg, 1, self.pos, self.qkv, self.kc[0, l], self.vc[0, l], self.att,
                                    self.consts[l], self.cos, self.sin, self.attn_scratch, w.get("q_norm"),
                                    w.get("k_norm"), ch=self.kv_ch[l])
@@ -399,5 +403,6 @@ class BatchDecoder:
 
     def kernel_launches(self):
         c = self.cfg
-        ffn = (4 if self.slots > CHUNK else 3) if c.moe else 4     # grouped: router, up, down, combine
+        grouped = self.slots > CHUNK and c.dim % 32 == 0           # router, up, down, combine
+        ffn = (4 if grouped else 3 * ((self.slots + CHUNK - 1) // CHUNK)) if c.moe else 4
         return 1 + c.layers * (5 + ffn) + 2
