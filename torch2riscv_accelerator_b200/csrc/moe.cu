@@ -324,9 +324,10 @@ cudaError_t launch_moe_combine_ll(const TpCtx& tp, const uint64_t* wy_ll, int m,
 // Batched decode and prefill chunks: the rows' (row, slot) pairs grouped by
 // expert, so that each expert's weight tiles are read once for all the rows that
 // chose it (the per-row kernels above read them once per pair). Launches: the
-// router (as above), gate/up and down by (tile, expert), each CTA listing its
-// expert's pairs from the routing, and
-// the k-order combine (moe_combine_kernel) unless the terms go out for an
+// router (as above); gate/up and down with one CTA per (tile, expert), each
+// listing its expert's pairs from the routing ids itself (expert parallelism
+// adds a down column for the other ranks' pairs, stored as +0); then the
+// k-order combine (moe_combine_kernel) unless the terms go out for an
 // expert-parallel sum. Each pair's arithmetic is the per-row kernels' own, so
 // the results are the same bit for bit.
 constexpr int kMoePairs = 16;                                  // pairs per pass of a grouped CTA
