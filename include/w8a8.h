@@ -230,7 +230,8 @@ int w8a8_moe_combine(const float* wy, int rows, int top_k, int dim, const float*
  * the terms, resid and y unused) for up to W8A8_MOE_MAX_ROWS rows (batched
  * decode, prefill chunks), the same results bit for bit. The rows' (row, slot)
  * pairs are grouped by expert on the device, so each expert's weight tiles are
- * read once per call rather than once per pair. scratch:
+ * read once per call rather than once per pair (above 128 rows on the tensor
+ * cores: grouped tcgen05 GEMMs over per-expert slabs of the rows). scratch:
  * w8a8_moe_rows_scratch_bytes() bytes (its size does not depend on `experts`,
  * which it takes for the call's own argument list); dim a multiple of 32. The reference runs the MoE per row
  * (compiler/frontend/hf_generic.py:641-657); this is that loop over a batch. */

@@ -316,6 +316,26 @@ static int moe_launch(const float* x, const float* norm_g, float eps, int rows, 
     if (grouped) {
         sp += a256((size_t)rows * top_k * 4);
         if (p.wy == nullptr) p.wy = reinterpret_cast<float*>(sp);          // the terms, then the combine
+        sp += a256((size_t)rows * top_k * dim * 4);
+        // the tensor-core path's slabs (sized for all `experts`: e_n <= experts).
+        // Above 128 rows (prefill chunks) the tensor cores; at batched-decode
+        // sizes the CUDA-core kernels, whose step measured faster on B200 (the
+        // tensor-core path's count reset and two more launches cost more than
+        // its GEMMs save there)
+        const size_t mcap = ((size_t)rows + 127) / 128 * 128;
+        const bool tc = rows > 128;
+        p.mcap = (int)mcap;
+        p.slab_x = tc ? reinterpret_cast<int8_t*>(sp) : nullptr;
+        sp += a256((size_t)experts * mcap * dim);
+        p.slab_h = reinterpret_cast<int8_t*>(sp);
+        sp += a256((size_t)experts * mcap * expert_hidden);
+        p.cnt = reinterpret_cast<int*>(sp);
+        sp += a256((size_t)experts * 4);
+        p.slab_pair = reinterpret_cast<int*>(sp);
+        sp += a256((size_t)experts * mcap * 4);
+        p.pair_pos = reinterpret_cast<int*>(sp);
+        sp += a256((size_t)rows * top_k * 4);
+        p.s_h = reinterpret_cast<float*>(sp);
         if (moe_smem(p, 0) > 200 * 1024 || moe_rows_smem(p, 1) > 200 * 1024 || moe_rows_smem(p, 2) > 200 * 1024)
             return W8A8_EINVAL;
         return cuda_status(launch_moe_rows(p, wy == nullptr, S(stream)));
@@ -327,7 +347,10 @@ static int moe_launch(const float* x, const float* norm_g, float eps, int rows, 
 
 size_t w8a8_moe_rows_scratch_bytes(int rows, int dim, int experts, int top_k, int expert_hidden) {
     if (rows <= 0 || dim <= 0 || experts <= 0 || top_k <= 0 || expert_hidden <= 0) return 0;
-    return w8a8_moe_scratch_bytes(rows, dim, top_k, expert_hidden) + a256((size_t)rows * top_k * dim * 4);
+    const size_t mcap = ((size_t)rows + 127) / 128 * 128;                // slab rows per expert
+    return w8a8_moe_scratch_bytes(rows, dim, top_k, expert_hidden) + a256((size_t)rows * top_k * dim * 4) +
+           a256((size_t)experts * mcap * dim) + a256((size_t)experts * mcap * expert_hidden) +
+           a256((size_t)experts * 4) + a256((size_t)experts * mcap * 4) + 2 * a256((size_t)rows * top_k * 4);
 }
 
 int w8a8_moe_ffn_rows(const float* x, const float* norm_g, float eps, int rows, int dim, const int8_t* router_q,

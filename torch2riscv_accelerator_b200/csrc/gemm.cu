@@ -82,7 +82,7 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, int* v) {
     asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
-template <int BN, bool TWO>
+template <int BN, bool TWO, bool GRP = false>
 __global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_kernel(const __grid_constant__ GemmMaps maps, GemmParams p) {
     extern __shared__ __align__(1024) unsigned char smem_raw[];
@@ -97,7 +97,10 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     if (TWO) stage_silu_tables(silu_tab);
     const GateAct act{p.act, p.act_a, p.act_b};
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int n0 = blockIdx.x * BN, m0 = blockIdx.y * kBM;
+    // grouped: expert ge, tile gt of its slab; A and B rows offset to them
+    const int ge = GRP ? (int)blockIdx.y / p.g_mtiles : 0, gt = GRP ? (int)blockIdx.y % p.g_mtiles : 0;
+    const int n0 = blockIdx.x * BN, m0 = GRP ? ge * p.g_mcap + gt * kBM : blockIdx.y * kBM;
+    const int nb0 = GRP ? ge * p.n + n0 : n0;                 // B row of column n0
     const int kt_n = (p.k + kBK - 1) / kBK;
     constexpr uint32_t kCols = TWO ? 2 * BN : BN;              // TMEM columns (a power of two >= 32)
     if (tid == 0) {
@@ -133,8 +136,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             unsigned char* st = smem + (size_t)s * kStage;
             mbar_expect_tx(&full[s], (uint32_t)kStage);
             tma_load_2d(st, &maps.a, kt * kBK, m0, &full[s]);
-            tma_load_2d(st + kA, &maps.b, kt * kBK, n0, &full[s]);
-            if (TWO) tma_load_2d(st + kA + kB, &maps.b2, kt * kBK, n0, &full[s]);
+            tma_load_2d(st + kA, &maps.b, kt * kBK, nb0, &full[s]);
+            if (TWO) tma_load_2d(st + kA + kB, &maps.b2, kt * kBK, nb0, &full[s]);
         }
     } else if (warp == 1 && lane == 0) {
         // MMA issuer: 4 MMAs of K = 32 bytes per stage; the descriptor start
@@ -172,29 +175,45 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             if (lane == 0) atomicOr(&g_gemm_errors, 16u);
         } else if (!failed) {
             const int q = warp & 3, half = (warp - 2) >> 2;
-            const int m = m0 + q * 32 + lane;
             const uint32_t lane_addr = (uint32_t)(q * 32) << 16;
-            const float sx = m < p.m ? __ldg(p.s_x + m) : 0.f;
+            // this thread's row: valid, its output row, s_x (grouped: the pair)
+            int m = m0 + q * 32 + lane;
+            bool valid = m < p.m;
+            float sx = 0.f, wj = 0.f;
+            if (GRP) {
+                const int local = gt * kBM + q * 32 + lane;
+                valid = local < __ldcg(p.g_cnt + ge);
+                m = valid ? __ldcg(p.g_pair + (size_t)ge * p.g_mcap + local) : 0;
+                if (valid) {
+                    sx = __ldcg(p.s_x + (TWO ? m / p.g_top_k : m));
+                    if (!TWO) wj = __ldcg(p.g_w + m);
+                }
+            } else if (valid) {
+                sx = __ldg(p.s_x + m);
+            }
+            const float* s_w = p.s_w + (GRP ? (size_t)ge * p.n : 0);
+            const float* s_w2 = TWO ? p.s_w2 + (GRP ? (size_t)ge * p.n : 0) : nullptr;
+            uint32_t am = 0u;                                  // grouped, with w2: max|h| of the row
             const bool vec = (p.n & 3) == 0;                 // 16-byte rows: vector loads and stores
             for (int c0 = half * (BN / 2); c0 < (half + 1) * (BN / 2); c0 += 16) {
                 int v[16], u[16];
                 tmem_ld16(tmem + lane_addr + (uint32_t)c0, v);
                 if (TWO) tmem_ld16(tmem + lane_addr + (uint32_t)(BN + c0), u);
                 const int nb = n0 + c0;
-                if (m >= p.m || nb >= p.n) continue;                 // (after the warp-wide TMEM loads)
+                if (!valid || nb >= p.n) continue;                   // (after the warp-wide TMEM loads)
                 float o[16];
                 if (vec && nb + 16 <= p.n) {
                     float sw[16], sw2[16], rs[16];
-                    const float4* s4 = reinterpret_cast<const float4*>(p.s_w + nb);
+                    const float4* s4 = reinterpret_cast<const float4*>(s_w + nb);
 #pragma unroll
                     for (int j = 0; j < 4; ++j) reinterpret_cast<float4*>(sw)[j] = __ldg(s4 + j);
                     if (TWO) {
-                        const float4* t4 = reinterpret_cast<const float4*>(p.s_w2 + nb);
+                        const float4* t4 = reinterpret_cast<const float4*>(s_w2 + nb);
 #pragma unroll
                         for (int j = 0; j < 4; ++j) reinterpret_cast<float4*>(sw2)[j] = __ldg(t4 + j);
                     }
                     float4* y4 = reinterpret_cast<float4*>(p.y + (size_t)m * p.n + nb);
-                    if (!TWO && p.resid != nullptr) {
+                    if (!GRP && !TWO && p.resid != nullptr) {
                         const float4* r4 = reinterpret_cast<const float4*>(p.resid + (size_t)m * p.n + nb);
 #pragma unroll
                         for (int j = 0; j < 4; ++j) reinterpret_cast<float4*>(rs)[j] = r4[j];
@@ -203,25 +222,28 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                     for (int j = 0; j < 16; ++j) {
                         const float g = fmul(fmul(i2f(v[j]), sw[j]), sx);
                         if (TWO) o[j] = gate_tab(g, fmul(fmul(i2f(u[j]), sw2[j]), sx), silu_tab, act);
+                        else if (GRP) o[j] = fmul(wj, g);
                         else o[j] = p.resid != nullptr ? fadd(rs[j], g) : g;
+                        if (GRP && TWO) am = max(am, __float_as_uint(fabsf(o[j])));   // NaN above numbers
                     }
 #pragma unroll
                     for (int j = 0; j < 4; ++j) y4[j] = reinterpret_cast<const float4*>(o)[j];
-                    if (!TWO && p.resid == nullptr && p.acc != nullptr) {
+                    if (!GRP && !TWO && p.resid == nullptr && p.acc != nullptr) {
                         int4* a4 = reinterpret_cast<int4*>(p.acc + (size_t)m * p.n + nb);
 #pragma unroll
                         for (int j = 0; j < 4; ++j) a4[j] = reinterpret_cast<const int4*>(v)[j];
                     }
                     continue;
                 }
+                if constexpr (!GRP) {                                // (grouped: n % 16 == 0, never ragged)
 #pragma unroll
                 for (int j = 0; j < 16; ++j) {                       // a ragged or unaligned edge
                     const int n = nb + j;
                     if (n >= p.n) continue;
                     const size_t off = (size_t)m * p.n + n;
-                    const float g = fmul(fmul(i2f(v[j]), __ldg(p.s_w + n)), sx);
+                    const float g = fmul(fmul(i2f(v[j]), __ldg(s_w + n)), sx);
                     if (TWO) {
-                        p.y[off] = gate_tab(g, fmul(fmul(i2f(u[j]), __ldg(p.s_w2 + n)), sx), silu_tab, act);
+                        p.y[off] = gate_tab(g, fmul(fmul(i2f(u[j]), __ldg(s_w2 + n)), sx), silu_tab, act);
                     } else if (p.resid != nullptr) {
                         p.y[off] = fadd(p.resid[off], g);
                     } else {
@@ -229,7 +251,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
                         if (p.acc != nullptr) p.acc[off] = v[j];
                     }
                 }
+                }
             }
+            if (GRP && TWO && valid && am != 0u) atomicMax(p.g_amax + m, am);
         }
     }
     tc_fence_before();
@@ -277,19 +301,21 @@ static bool make_map(CUtensorMap* map, const void* base, int rows, int k, int bo
 
 size_t gemm_smem(int bn, bool two) { return (size_t)kStages * (kBM * kBK + (size_t)bn * kBK * (two ? 2 : 1)) + 1024; }
 
-template <int BN, bool TWO>
-static cudaError_t launch_gemm_t(const GemmOperands& a, const GemmParams& p, cudaStream_t st) {
+template <int BN, bool TWO, bool GRP = false>
+static cudaError_t launch_gemm_t(const GemmOperands& a, const GemmParams& p, cudaStream_t st, int experts = 1) {
     GemmMaps maps{};
-    if (!make_map(&maps.a, a.xq, p.m, p.k, kBM) || !make_map(&maps.b, a.w, p.n, p.k, BN) ||
-        (TWO && !make_map(&maps.b2, a.w2, p.n, p.k, BN)))
+    // grouped: A = every expert's slab, B = every expert's n rows
+    const int a_rows = GRP ? experts * p.g_mcap : p.m, b_rows = GRP ? experts * p.n : p.n;
+    if (!make_map(&maps.a, a.xq, a_rows, p.k, kBM) || !make_map(&maps.b, a.w, b_rows, p.k, BN) ||
+        (TWO && !make_map(&maps.b2, a.w2, b_rows, p.k, BN)))
         return cudaErrorInvalidValue;
-    auto kern = gemm_kernel<BN, TWO>;
+    auto kern = gemm_kernel<BN, TWO, GRP>;
     const size_t sm = gemm_smem(BN, TWO);
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
     if (e != cudaSuccess) return e;
     e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     if (e != cudaSuccess) return e;
-    const dim3 grid((p.n + BN - 1) / BN, (p.m + kBM - 1) / kBM);
+    const dim3 grid((p.n + BN - 1) / BN, GRP ? experts * p.g_mtiles : (p.m + kBM - 1) / kBM);
     return launch_k(kern, grid, dim3(kGemmThreads), sm, st, maps, p);
 }
 
@@ -327,6 +353,34 @@ cudaError_t launch_gemm(const GemmOperands& a, const GemmParams& p, cudaStream_t
     if (best == 128) return launch_gemm_t<128, false>(a, p, st);
     if (best == 64) return launch_gemm_t<64, false>(a, p, st);
     return launch_gemm_t<32, false>(a, p, st);
+}
+
+// Grouped (MoE experts): every expert's slab of g_mcap rows against its own
+// weights; tile width by the same estimate over experts x slab tiles x column
+// tiles. n a multiple of 16 (whole 16-column epilogue groups).
+cudaError_t launch_gemm_grouped(const GemmOperands& a, const GemmParams& p, int experts, cudaStream_t st) {
+    if (experts <= 0 || p.n % 16 != 0 || p.g_mcap % kBM != 0 || p.g_mtiles * kBM != p.g_mcap)
+        return cudaErrorInvalidValue;
+    int sms = 0, dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (sms <= 0) sms = 148;
+    const bool two = a.w2 != nullptr;
+    const long mt = (long)experts * p.g_mtiles;
+    int best = 32;
+    double cbest = 1e300;
+    for (int bn : {32, 64, 128}) {
+        const double c = gemm_cost((long)((p.n + bn - 1) / bn) * mt, bn, p.k, two, sms);
+        if (c < cbest * (1.0 - 1e-9)) best = bn, cbest = c;
+    }
+    if (two) {
+        if (best == 128) return launch_gemm_t<128, true, true>(a, p, st, experts);
+        if (best == 64) return launch_gemm_t<64, true, true>(a, p, st, experts);
+        return launch_gemm_t<32, true, true>(a, p, st, experts);
+    }
+    if (best == 128) return launch_gemm_t<128, false, true>(a, p, st, experts);
+    if (best == 64) return launch_gemm_t<64, false, true>(a, p, st, experts);
+    return launch_gemm_t<32, false, true>(a, p, st, experts);
 }
 
 unsigned int gemm_read_clear_errors() {

@@ -100,6 +100,31 @@ __global__ void __launch_bounds__(kMoeThreads) moe_router_kernel(MoeParams p) {
             p.w[row * K + j] = fmul(ev[j], rs);
         }
     }
+    if (p.slab_x != nullptr) {                                            // tensor-core path: into the slabs
+        __shared__ int pos_s[kMoeMaxTopK];
+        __syncthreads();                                                  // ids_s complete
+        if (tid < K) {
+            const int e = ids_s[tid] - p.e_lo;
+            int pos = -1;
+            if (e >= 0 && e < p.e_n) {                                    // this rank's expert: the next slab row
+                const int r = atomicAdd(p.cnt + e, 1);                    // (< m <= mcap: one pair per row)
+                if (r < p.mcap) {
+                    pos = e * p.mcap + r;
+                    p.slab_pair[pos] = row * K + tid;
+                } else {
+                    atomicOr(&g_moe_errors, 64u);
+                }
+            }
+            pos_s[tid] = pos;
+            p.pair_pos[row * K + tid] = pos;
+        }
+        __syncthreads();
+        for (int c = tid; c < K * (dim / 16); c += kMoeThreads) {
+            const int j = c / (dim / 16), cc = c % (dim / 16);
+            if (pos_s[j] >= 0)
+                reinterpret_cast<int4*>(p.slab_x + (size_t)pos_s[j] * dim)[cc] = reinterpret_cast<const int4*>(xs)[cc];
+        }
+    }
 }
 
 // ---------------------------------------------------------------- launch 2
@@ -535,6 +560,65 @@ __global__ void __launch_bounds__(kMoeThreads) moe_down_rows_kernel(MoeParams p)
     if (!ok) mbar_wait(&bar, 0u);
 }
 
+// Tensor-core path, between the grouped gate/up and down GEMMs: each pair's h
+// requantized (quant_act with its max|h|, the per-row kernels' arithmetic) into
+// its slab row, its scale into s_h; a pair of another rank's expert stores +0
+// terms instead. One CTA per pair.
+constexpr int kQuantHThreads = 128;
+__global__ void __launch_bounds__(kQuantHThreads) moe_quant_h_kernel(MoeParams p) {
+    const int pr = blockIdx.x, tid = threadIdx.x;
+    pdl_wait();
+    pdl_trigger();
+    const int pos = __ldcg(p.pair_pos + pr);
+    if (pos < 0) {
+        for (int n = tid; n < p.dim; n += kQuantHThreads) p.wy[(size_t)pr * p.dim + n] = 0.f;
+        return;
+    }
+    const float s = fmul(__uint_as_float(__ldcg(p.amax + pr)), W8A8_C127);
+    const float inv = sfu_recip(s);
+    if (tid == 0) p.s_h[pr] = s;
+    const float4* h4 = reinterpret_cast<const float4*>(p.h + (size_t)pr * p.ih);
+    char4* d4 = reinterpret_cast<char4*>(p.slab_h + (size_t)pos * p.ih);
+    for (int i = tid; i < p.ih / 4; i += kQuantHThreads) {
+        const float4 v = __ldcg(h4 + i);
+        d4[i] = make_char4(to_i8(fmul(v.x, inv)), to_i8(fmul(v.y, inv)), to_i8(fmul(v.z, inv)),
+                           to_i8(fmul(v.w, inv)));
+    }
+}
+
+// Many rows on the tensor cores: the router fills each expert's slab; a
+// grouped tcgen05 GEMM per matrix pair (gate / up with the SwiGLU and each
+// pair's max|h| in its epilogue; down with w_j folded in), the requantizer in
+// between; then the k-order combine unless the terms go out for an
+// expert-parallel sum.
+static cudaError_t launch_moe_rows_tc(const MoeParams& p, bool combine, cudaStream_t st) {
+    cudaError_t e = cudaMemsetAsync(p.cnt, 0, (size_t)p.e_n * sizeof(int), st);
+    if (e != cudaSuccess) return e;
+    const size_t sm0 = moe_smem(p, 0);
+    e = cudaFuncSetAttribute(moe_router_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm0);
+    if (e != cudaSuccess) return e;
+    e = launch_k(moe_router_kernel, dim3(p.m), dim3(kMoeThreads), sm0, st, p);
+    if (e != cudaSuccess) return e;
+    GemmParams g{};
+    g.g_cnt = p.cnt, g.g_pair = p.slab_pair, g.g_mcap = p.mcap, g.g_mtiles = p.mcap / 128, g.g_top_k = p.top_k;
+    GemmOperands up{};
+    up.xq = p.slab_x, up.w = p.gq, up.w2 = p.uq;
+    GemmParams gu = g;
+    gu.m = p.e_n * p.mcap, gu.n = p.ih, gu.k = p.dim, gu.s_x = p.s_x, gu.s_w = p.gs, gu.s_w2 = p.us, gu.y = p.h;
+    gu.act = 0, gu.g_amax = p.amax;                                       // SiLU
+    e = launch_gemm_grouped(up, gu, p.e_n, st);
+    if (e != cudaSuccess) return e;
+    e = launch_k(moe_quant_h_kernel, dim3(p.m * p.top_k), dim3(kQuantHThreads), 0, st, p);
+    if (e != cudaSuccess) return e;
+    GemmOperands dn{};
+    dn.xq = p.slab_h, dn.w = p.dq;
+    GemmParams gd = g;
+    gd.m = p.e_n * p.mcap, gd.n = p.dim, gd.k = p.ih, gd.s_x = p.s_h, gd.s_w = p.ds, gd.y = p.wy, gd.g_w = p.w;
+    e = launch_gemm_grouped(dn, gd, p.e_n, st);
+    if (e != cudaSuccess) return e;
+    return combine ? launch_moe_combine(p.wy, p.m, p.top_k, p.dim, p.resid, p.y, st) : cudaSuccess;
+}
+
 size_t moe_rows_smem(const MoeParams& p, int which) {
     const size_t list = (size_t)p.m * 4;                                 // a bucket holds at most one pair per row
     if (which == 1) return (size_t)2 * kMoeTile * p.dim + (size_t)kMoePairs * (p.dim + kMoePad) + list;
@@ -564,6 +648,7 @@ cudaError_t launch_moe(const MoeParams& p, cudaStream_t st) {
 }
 
 cudaError_t launch_moe_rows(const MoeParams& p, bool combine, cudaStream_t st) {
+    if (p.slab_x != nullptr) return launch_moe_rows_tc(p, combine, st);
     struct L {
         void (*k)(MoeParams);
         dim3 grid;

@@ -132,6 +132,16 @@ struct GemmParams {
     int32_t* acc;             // [m, n] raw accumulators, or null (without resid / w2)
     int act;                  // with w2: the gate, 0 SiLU, 1 GELU-tanh (constants act_a, act_b)
     float act_a, act_b;
+    // grouped (MoE experts): CTA row blockIdx.y = expert e * g_mtiles + tile;
+    // A rows come from e's slab of g_mcap rows, B rows and the column scales
+    // from e's block of n rows; slab row r < g_cnt[e] holds pair
+    // g_pair[e * g_mcap + r] (row * g_top_k + slot), the output row. s_x is
+    // per input row (index pair / g_top_k) with w2, per pair without.
+    const int* g_cnt;
+    const int* g_pair;
+    int g_mcap, g_mtiles, g_top_k;
+    const float* g_w;         // without w2: the pair's weight folded in (w_j * y_j)
+    uint32_t* g_amax;         // with w2: the pair's max|h| (float bits, atomic max)
 };
 size_t gemm_smem(int bn, bool two);
 // A 2-D uint8 TMA map: [rows][inner] with row_stride bytes between rows
@@ -139,6 +149,8 @@ size_t gemm_smem(int bn, bool two);
 bool make_map_u8(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows, uint64_t row_stride,
                  uint32_t box_inner, uint32_t box_rows, bool swizzle128);
 cudaError_t launch_gemm(const GemmOperands& a, const GemmParams& p, cudaStream_t st);
+// grouped: a.xq = the slabs [experts * g_mcap][k], a.w (a.w2) = [experts * n][k]
+cudaError_t launch_gemm_grouped(const GemmOperands& a, const GemmParams& p, int experts, cudaStream_t st);
 unsigned int gemm_read_clear_errors();
 cudaError_t launch_norm_quant(const float* x, const float* g, int m, int k, float eps, float inv_k, int8_t* xq,
                               float* s_x, cudaStream_t st);
@@ -178,6 +190,15 @@ struct MoeParams {
     // the previous combine included, are complete)
     TpCtx tp;
     uint64_t* wy_ll;
+    // many rows on the tensor cores: each of this rank's experts has a slab of
+    // mcap rows (a multiple of 128) that the router fills in arrival order
+    int8_t* slab_x;           // [e_n][mcap][dim] the int8 rows of the expert's pairs
+    int8_t* slab_h;           // [e_n][mcap][ih] their requantized h
+    int* cnt;                 // [e_n] rows in each slab (zeroed before the router)
+    int* slab_pair;           // [e_n][mcap] the pair (row * k + slot) of each slab row
+    int* pair_pos;            // [m * k] the slab row (e * mcap + r) of each pair, -1: another rank's expert
+    float* s_h;               // [m * k] each pair's h scale
+    int mcap;
 };
 size_t moe_smem(const MoeParams& p, int which);
 cudaError_t launch_moe(const MoeParams& p, cudaStream_t st);
