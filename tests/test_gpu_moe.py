@@ -106,9 +106,10 @@ def run_rows(x, t, top_k, norm_g, eps, resid=None, expert_lo=0, local=None):
 
 @pytest.mark.parametrize("rows", [17, 64, 203])
 def test_moe_grouped_rows_equal_per_row_path(rows):
-    """More than 16 rows grouped by expert: the same routing and outputs, bit
-    for bit, as the per-row kernels over 16-row groups; the first rows also
-    against the oracle."""
+    """More than 16 rows grouped by expert (17 and 64: the CUDA-core kernels;
+    203: the tensor-core path): the same routing and outputs, bit for bit, as
+    the per-row kernels over 16-row groups; the first rows also against the
+    oracle."""
     cfg = C.C4
     rng = np.random.default_rng(70 + rows)
     t = c4_tables(rng, cfg.experts, cfg.dim, cfg.expert_hidden)
@@ -127,14 +128,14 @@ def test_moe_grouped_rows_equal_per_row_path(rows):
         assert np.array_equal(bits(y[m]), bits((resid[m] + ym).astype(F))), m
 
 
-@pytest.mark.parametrize("ranks", [2, 4])
-def test_moe_grouped_rows_expert_parallel_terms(ranks):
-    """Expert parallelism through the grouped entry: each rank's terms are
-    w_j * y_j for its experts and +0 elsewhere, their sum folded by
-    w8a8_moe_combine equals the one-GPU result bit for bit."""
+@pytest.mark.parametrize("ranks,rows", [(2, 40), (4, 40), (2, 150)])
+def test_moe_grouped_rows_expert_parallel_terms(ranks, rows):
+    """Expert parallelism through the grouped entry (40 rows: the CUDA-core
+    kernels; 150: the tensor-core path, two slab tiles per expert): each
+    rank's terms are w_j * y_j for its experts and +0 elsewhere, their sum
+    folded by w8a8_moe_combine equals the one-GPU result bit for bit."""
     cfg = C.C4
-    rows = 40
-    rng = np.random.default_rng(90 + ranks)
+    rng = np.random.default_rng(90 + ranks + rows)
     t = c4_tables(rng, cfg.experts, cfg.dim, cfg.expert_hidden)
     x = rng.standard_normal((rows, cfg.dim)).astype(F)
     g = (1 + 0.1 * rng.standard_normal(cfg.dim)).astype(F)
