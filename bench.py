@@ -41,11 +41,11 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, ROOT)
 
 METRIC = "decode tok/s (Qwen3-0.6B shape W8A8, T=2048)"
-# DRAM bytes (read + write) of one classifier-shaped GEMV launch (151936 x 1024),
-# from one ncu capture of the same weight stream; the command and the figures
-# are in profiles/classifier_gemv_c2.txt.
-NCU_TRAFFIC = {"bytes": 156221184 + 4762624, "source": "profiles/classifier_gemv_c2.txt"}
-FPGA_TOKS = 3.41          # KV260 overlay, Qwen3-0.6B decode at T = 2048 (docs/results_v2.3.md:93-94)
+# DRAM bytes (read + write) per launch of a kernel kind of the C2 step, from one
+# ncu capture each; the commands and the figures are in the named profiles.
+NCU_TRAFFIC = {"classifier GEMV (rmsnorm + quant)": {"bytes": 156221184 + 4762624,
+                                                       "source": "profiles/classifier_gemv_c2.txt"}}
+FPGA_TOKS = 3.41          # the reference's KV260 overlay, Qwen3-0.6B decode at T = 2048 (docs/results_v2.3.md:93-94)
 
 
 def peaks():
@@ -153,16 +153,19 @@ def cpu_threads():
         return os.cpu_count() or 1
 
 
-def oracle_decode(cfg, qw, kv_scales, kc, vc, start, tokens, all_layers=True):
+def oracle_decode(cfg, qw, kv_scales, kc, vc, start, tokens, logits=None):
     """Time the oracle's decode steps at positions start, start + 1, ... from a
-    given cache state (kc / vc [layers, seq_len, kv_dim] int8)."""
+    given cache state (kc / vc [layers, seq_len, kv_dim] int8); each step's
+    logits appended to `logits` when it is a list."""
     from oracle import model as OM
     ora = OM.OracleDecoder(cfg, qw, kv_scales)
     ora.kc[:], ora.vc[:] = kc, vc
     ora._w64 = _NoCache()
     t0 = time.perf_counter()
     for i, t in enumerate(tokens):
-        ora.forward(int(t), start + i)
+        out = ora.forward(int(t), start + i)
+        if logits is not None:
+            logits.append(np.asarray(out, np.float32).copy())
     return time.perf_counter() - t0
 
 
@@ -187,6 +190,7 @@ def run_reference(args, cfg, ws, rank):
     prefilled on the CPU: 2032 oracle prefill steps would take hours)."""
     if rank != 0:
         return
+    tp, ep = split_kind(cfg, args, ws)
     qw = build_model(cfg, args.seed)
     P = cfg.seq_len - args.warmup - args.steps
     rng = np.random.default_rng(args.seed + 2)
@@ -197,12 +201,15 @@ def run_reference(args, cfg, ws, rank):
     toks = rng.integers(0, cfg.vocab, args.warmup + args.steps)
     oracle_decode(cfg, qw, qw.kv_scales, kc, vc, P, toks[:args.warmup])
     dt = oracle_decode(cfg, qw, qw.kv_scales, kc, vc, P + args.warmup, toks[args.warmup:])
-    v = args.steps / dt
     cores = len(os.sched_getaffinity(0))
+    # the repo arm's configuration at this N: one sequence (tensor / expert
+    # parallel) or N replicas; the CPU decodes the same sequences either way
+    seqs = 1 if (tp or ep) else ws
+    v = seqs * args.steps / (seqs * dt)
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": ws, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": 1e3 * dt / args.steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": v / FPGA_TOKS, "dtype": "int8", "data": "synthetic",
-            "config": config_of(cfg, args, ws),
+            "scaling": "strong" if (tp or ep) else "weak", "vs_baseline": v / FPGA_TOKS, "dtype": "int8",
+            "data": "synthetic", "config": config_of(cfg, args, ws, tp, ep),
             "cpu_baseline": {"value": v, "unit": "tok/s", "cores": cpu_threads(), "kind": "port",
                              "sample": f"{args.steps} full decode steps (all {cfg.layers} layers + classifier) at "
                                        f"positions {P + args.warmup}..{cfg.seq_len - 1} from a seeded int8 KV cache; "
@@ -222,31 +229,61 @@ def run_batch(args, cfg, qw, ws, rank, local):
     from torch2riscv_accelerator_b200.model import BatchDecoder
     from torch2riscv_accelerator_b200.runtime import BatchLlamaDevice
     D = args.batch
-    tp = ep = False
-    if ws > 1 and args.parallel == "tp":               # MoE: experts split (ep); else tensor parallel
-        from torch2riscv_accelerator_b200.ep import EpBatchDecoder, EpBatchLlamaDevice, check_ep
-        from torch2riscv_accelerator_b200.tp import TpBatchDecoder, TpBatchLlamaDevice, check_split
-        try:
-            (check_ep if cfg.moe else check_split)(cfg, ws)
-            ep, tp = cfg.moe, not cfg.moe
-        except ValueError as e:
-            if rank == 0:
-                print(f"# {e}: independent replicas instead", file=sys.stderr)
+    tp, ep = split_kind(cfg, args, ws)
     if tp:
+        from torch2riscv_accelerator_b200.tp import TpBatchDecoder, TpBatchLlamaDevice
         dec = TpBatchDecoder(cfg, qw, qw.kv_scales, slots=D)
     elif ep:
+        from torch2riscv_accelerator_b200.ep import EpBatchDecoder, EpBatchLlamaDevice
         dec = EpBatchDecoder(cfg, qw, qw.kv_scales, slots=D)
     else:
         dec = BatchDecoder(cfg, qw, qw.kv_scales, slots=D)
     split = tp or ep
     seqs = D if split else ws * D                      # sequences per step over all GPUs
+    # seeded caches of the whole model, the same on every rank (a tensor-parallel
+    # rank keeps its KV heads)
+    L, Hk, T, hd = cfg.layers, cfg.kv_heads, cfg.seq_len, cfg.head_dim
     g = torch.Generator(device=dec.dev).manual_seed(args.seed + 11)
-    for t in (dec.kc, dec.vc):
-        t.copy_(torch.randint(-127, 128, t.shape, dtype=torch.int8, device=dec.dev, generator=g))
+    kfull = torch.randint(-127, 128, (D, L, Hk, T, hd), dtype=torch.int8, device=dec.dev, generator=g)
+    vfull = torch.randint(-127, 128, (D, L, Hk, hd, T), dtype=torch.int8, device=dec.dev, generator=g)
+    heads = slice(rank * (Hk // ws), (rank + 1) * (Hk // ws)) if tp else slice(0, Hk)
+    dec.kc.copy_(kfull[:, :, heads])
+    dec.vc.copy_(vfull[:, :, heads])
     P = cfg.seq_len - args.warmup - args.steps
     rng = np.random.default_rng(args.seed + 3)
-    dec.tokens.copy_(torch.as_tensor(rng.integers(0, cfg.vocab, D), dtype=torch.int32))
+    tok0 = torch.as_tensor(rng.integers(0, cfg.vocab, D), dtype=torch.int32)
+    dec.tokens.copy_(tok0)
     dec.pos.fill_(P)
+    # parity: the first step (position P of every slot) against a one-GPU
+    # BatchDecoder of the whole model (N > 1) or the oracle on two slots (N = 1)
+    dec.step()
+    got = (dec.gather_logits() if tp else dec.logits).cpu().numpy()
+    parity = None
+    if rank == 0:
+        if split:
+            ref = BatchDecoder(cfg, qw, qw.kv_scales, slots=D)
+            ref.kc.copy_(kfull)
+            ref.vc.copy_(vfull)
+            ref.tokens.copy_(tok0)
+            ref.pos.fill_(P)
+            ref.step()
+            want = ref.logits.cpu().numpy()
+            parity = {"reference": f"one-GPU BatchDecoder of the whole model, the first step of all {D} slots",
+                      "logits_equal": bool(np.array_equal(got.view(np.uint32), want.view(np.uint32))),
+                      "tokens_equal": bool(np.array_equal(got.argmax(1), want.argmax(1)))}
+            del ref
+        elif not args.no_cpu_baseline:
+            ok = []
+            for b in sorted({0, D - 1}):
+                kc = kfull[b].permute(0, 2, 1, 3).reshape(L, T, Hk * hd).cpu().numpy()
+                vc = vfull[b].permute(0, 3, 1, 2).reshape(L, T, Hk * hd).cpu().numpy()
+                ora = []
+                oracle_decode(cfg, qw, qw.kv_scales, kc, vc, P, [int(tok0[b])], logits=ora)
+                ok.append(np.array_equal(ora[0].view(np.uint32), got[b].view(np.uint32)))
+            parity = {"reference": f"the oracle: slots {sorted({0, D - 1})}, the first step at position {P} "
+                                   "from the seeded cache state", "logits_equal": all(ok), "tokens_equal": all(ok)}
+    del kfull, vfull
+    torch.cuda.empty_cache()
     # one step: the captured graph (the tensor-parallel step holds NCCL
     # collectives and runs eagerly)
     run = dec.step if split else dec.capture().replay   # (a capture's warm-up step writes the rows of position P)
@@ -302,9 +339,11 @@ def run_batch(args, cfg, qw, ws, rank, local):
                            "weights": sum(t.numel() for w in dec.layers for t in w.values()
                                           if t.dtype == torch.int8) + dec.cls_q.numel()},
             "gpu_launches": args.steps * dec.kernel_launches(),
-            "clocks": clk.summary(), "mode": "batch",
+            "clocks": clk.summary(), "mode": "batch", "parity": parity,
         }
         print(json.dumps(line), flush=True)
+        if parity is not None and not (parity["logits_equal"] and parity["tokens_equal"]):
+            raise RuntimeError(f"parity failed: {parity}")
     barrier(ws)
     if ws > 1:
         import torch.distributed as dist
@@ -405,6 +444,91 @@ def run_moe_kernel(args, cfg):
                       "error_flags": ops.error_flags()}), flush=True)
 
 
+def kernel_table(dec, reps=5):
+    """Each kernel kind of a batch-1 decode step (one sequence, this GPU's
+    shard), launched for every layer back to back with plain stream ordering
+    (no overlap between launches) inside a CUDA graph, timed with CUDA events:
+    microseconds per launch, algorithmic bytes per launch, GB/s. Every layer
+    reads its own weights and cache, so the loop's data is far over the L2.
+    The residual stream is restored afterwards."""
+    import torch
+
+    from torch2riscv_accelerator_b200 import _lib, ops
+    c, L = dec.cfg, dec.cfg.layers
+    w, x, qkv, att, h = dec.layers, dec.x[:1], dec.qkv[:1], dec.att[:1], dec.h[:1]
+    t = int(dec.pos[0].item()) + 1                      # positions attended
+    aa = dec._attn_args(1)
+    kinds = [
+        ("qkv GEMV (rmsnorm + quant prologue)", "gemv_kernel", L,
+         lambda l: ops.linear_fused(x, w[l]["wqkv"], w[l]["s_wqkv"], norm_g=w[l]["rms_att"], eps=c.eps, out=qkv),
+         c.qkv_dim * c.dim + 8 * c.qkv_dim + c.dim),
+        ("attention (cluster kernel, KV cache)", "attn_kernel", L, lambda l: ops.attn(aa[l]),
+         2 * t * c.kv_dim + 4 * (c.qkv_dim + c.q_dim)),
+        ("o_proj GEMV (+ residual)", "gemv_kernel", L,
+         lambda l: ops.linear_fused(att, w[l]["wo"], w[l]["s_wo"], resid=x, out=x),
+         c.dim * c.q_dim + 8 * c.dim + c.q_dim + 4 * c.dim),
+    ]
+    if not c.moe:
+        kinds += [
+            ("gate|up GEMV (rmsnorm + quant, SiLU gate)", "gemv_kernel", L,
+             lambda l: ops.ffn_swiglu(x, w[l]["rms_ffn"], c.eps, w[l]["w1"], w[l]["s_w1"], w[l]["w3"], w[l]["s_w3"],
+                                      None, h=h, requant=False, act=c.act),
+             2 * c.hidden * c.dim + 8 * c.hidden + c.dim + 4 * c.hidden),
+            ("down GEMV (+ residual)", "gemv_kernel", L,
+             lambda l: ops.linear_fused(h, w[l]["w2"], w[l]["s_w2"], resid=x, out=x),
+             c.dim * c.hidden + 8 * c.dim + c.hidden + 4 * c.dim)]
+    kinds.append(("classifier GEMV (rmsnorm + quant)", "gemv_kernel", 1,
+                  lambda l: ops.classifier(x, dec.cls_q, dec.cls_s, dec.rms_final, c.eps, out=dec.logits[:1]),
+                  dec.cls_q.shape[0] * (c.dim + 8) + c.dim))
+    saved = dec.x.clone()
+    lib = _lib.load()
+    old = lib.w8a8_set_pdl(0)
+    out = []
+    try:
+        for name, kern, n, fn, nbytes in kinds:
+            for l in range(n):                          # first calls outside the capture
+                fn(l)
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                for l in range(n):
+                    fn(l)
+            for _ in range(2):
+                g.replay()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(reps):
+                g.replay()
+            e1.record()
+            torch.cuda.synchronize()
+            us = e0.elapsed_time(e1) * 1e3 / (reps * n)
+            out.append({"kind": name, "kernel": kern, "launches_per_step": n, "us_per_launch": us,
+                        "bytes_per_launch": nbytes, "GBs": nbytes / us / 1e3})
+            del g
+    finally:
+        lib.w8a8_set_pdl(old)
+        dec.x.copy_(saved)
+        torch.cuda.synchronize()
+    return out
+
+
+def split_kind(cfg, args, ws):
+    """(tensor parallel, expert parallel) for N GPUs: a MoE config splits its
+    experts, a dense one its heads; independent replicas when the shape does
+    not split or --parallel replicas."""
+    if ws <= 1 or args.parallel != "tp":
+        return False, False
+    from torch2riscv_accelerator_b200.ep import check_ep
+    from torch2riscv_accelerator_b200.tp import check_split
+    try:
+        (check_ep if cfg.moe else check_split)(cfg, ws)
+    except ValueError as e:
+        if int(os.environ.get("RANK", "0")) == 0:
+            print(f"# {e}: independent replicas instead", file=sys.stderr)
+        return False, False
+    return not cfg.moe, cfg.moe
+
+
 def config_of(cfg, args, ws, tp=False, ep=False):
     P = cfg.seq_len - args.warmup - args.steps
     if ep:
@@ -476,20 +600,13 @@ def main():
     if args.batch > 1:
         run_batch(args, cfg, qw, ws, rank, local)
         return
-    tp = ep = False
-    if ws > 1 and args.parallel == "tp":               # MoE: experts split (ep); else tensor parallel
-        from torch2riscv_accelerator_b200.ep import EpLlamaDevice, check_ep
-        from torch2riscv_accelerator_b200.tp import TpLlamaDevice, check_split
-        try:
-            (check_ep if cfg.moe else check_split)(cfg, ws)
-            ep, tp = cfg.moe, not cfg.moe
-        except ValueError as e:
-            if rank == 0:
-                print(f"# {e}: independent replicas instead", file=sys.stderr)
+    tp, ep = split_kind(cfg, args, ws)
     if tp:
+        from torch2riscv_accelerator_b200.tp import TpLlamaDevice
         dev = TpLlamaDevice((cfg, qw, qw.kv_scales))
         dec = dev.dec
     elif ep:
+        from torch2riscv_accelerator_b200.ep import EpLlamaDevice
         dev = EpLlamaDevice((cfg, qw, qw.kv_scales))
         dec = dev.dec
     else:
@@ -502,7 +619,15 @@ def main():
     torch.cuda.synchronize()
     t0 = time.perf_counter()
     start_tok = int(np.argmax(dev.prefill(prompt)))
+    prefill_first_s = time.perf_counter() - t0        # includes the first-call graph captures
+    dev.pos = 0                                        # again, warm: the same rows rewritten with the same values
+    barrier(ws)
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    warm_tok = int(np.argmax(dev.prefill(prompt)))
     prefill_s = time.perf_counter() - t0
+    if warm_tok != start_tok:
+        raise RuntimeError("a second prefill of the prompt changed its last token")
     st = torch.cuda.current_stream()
 
     # ---- value: device-resident decode steps (captured step graph)
@@ -537,38 +662,60 @@ def main():
     rewind()
     dev.pos = P
     tok = start_tok
+    e2e_toks = [tok]
     for _ in range(args.warmup):
         tok = int(np.argmax(dev.forward(tok)))
+        e2e_toks.append(tok)
     barrier(ws)
     torch.cuda.synchronize()
     h0, h1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     h0.record(st)
     for _ in range(args.steps):
-        tok = int(np.argmax(dev.forward(tok)))
+        logits = dev.forward(tok)
+        tok = int(np.argmax(logits))
+        e2e_toks.append(tok)
     h1.record(st)
     torch.cuda.synchronize()
     barrier(ws)
     dt_e2e = max_over_ranks(h0.elapsed_time(h1) / 1e3, ws)
 
-    # ---- roofline: the classifier GEMV alone
+    # ---- parity of the measured steps: the graph's own tokens step by step
+    # (untimed replays of the same graph from the same start) and its last
+    # logits, against the e2e run and, at N > 1, a one-GPU decoder of the same
+    # model on rank 0 (itself bit-exact with the oracle, checked at N = 1 below)
+    rewind()
+    graph_toks = []
+    for _ in range(args.warmup + args.steps):
+        g.replay()
+        graph_toks.append(int(dec.next_token[0].item()))
+    if not tp:                                          # the last step's greedy key (tensor parallel: per rank)
+        graph_toks.append(int(0xFFFFFFFF - (int(dec.key[0].item()) & 0xFFFFFFFF)))
+    graph_logits = (dec.gather_logits(1)[0] if tp else dec.logits[0]).cpu().numpy()
+    parity = {"graph_tokens_equal_e2e": graph_toks == e2e_toks[:len(graph_toks)],
+              "graph_logits_equal_e2e": bool(np.array_equal(graph_logits.view(np.uint32),
+                                                            np.asarray(logits, np.float32).view(np.uint32)))}
+    if split and rank == 0:
+        ref = LlamaDevice(DeviceDecoder(cfg, qw, qw.kv_scales))
+        rt = int(np.argmax(ref.prefill(prompt)))
+        ref_toks = [rt]
+        for _ in range(args.warmup + args.steps):
+            ref_logits = ref.forward(rt)
+            rt = int(np.argmax(ref_logits))
+            ref_toks.append(rt)
+        parity.update({"reference": "one-GPU DeviceDecoder of the same model, same prompt and steps",
+                       "tokens_equal": ref_toks == e2e_toks,
+                       "logits_equal": bool(np.array_equal(np.asarray(ref_logits, np.float32).view(np.uint32),
+                                                           np.asarray(logits, np.float32).view(np.uint32)))})
+        ref.close()
+
+    # ---- roofline: every kernel kind of the step, the dominant one (most
+    # time per step) reported
     peak, peak_src = peaks()
-    x1 = dec.x[:1]
-    n_rep = 20
-    for _ in range(3):
-        ops.classifier(x1, dec.cls_q, dec.cls_s, dec.rms_final, cfg.eps, out=dec.logits[:1])
-    torch.cuda.synchronize()
-    r0, r1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    torch.cuda.nvtx.range_push("roofline")
-    r0.record(st)
-    for _ in range(n_rep):
-        ops.classifier(x1, dec.cls_q, dec.cls_s, dec.rms_final, cfg.eps, out=dec.logits[:1])
-    r1.record(st)
-    torch.cuda.nvtx.range_pop()
-    torch.cuda.synchronize()
-    t_gemv = r0.elapsed_time(r1) / 1e3 / n_rep
-    N, K = dec.cls_q.shape                              # (this rank's vocabulary slice under tp)
-    gemv_bytes = N * K + 4 * N + K + 4 * N
-    achieved = gemv_bytes / t_gemv / 1e9
+    table = kernel_table(dec) if not ep else []
+    for k in table:
+        k["frac"] = k["GBs"] / peak
+        k["us_per_step"] = k["us_per_launch"] * k["launches_per_step"]
+    dom = max(table, key=lambda k: k["us_per_step"]) if table else None
     step_bytes = dec.weight_bytes() + dec.kv_bytes(cfg.seq_len - 8)
 
     # ---- CPU baseline: the oracle from the same cache state (rank 0, N = 1)
@@ -578,7 +725,16 @@ def main():
         kc = np.stack([dec.kv_rows(l, cfg.seq_len)[0] for l in range(L)])
         vc = np.stack([dec.kv_rows(l, cfg.seq_len)[1] for l in range(L)])
         toks = np.random.default_rng(5).integers(0, cfg.vocab, args.cpu_steps)
-        cdt = oracle_decode(cfg, qw, qw.kv_scales, kc, vc, P, toks)
+        ora_logits = []
+        cdt = oracle_decode(cfg, qw, qw.kv_scales, kc, vc, P, toks, logits=ora_logits)
+        dev.pos = P                                     # the same steps on the GPU, from the same cache state
+        gpu_logits = [dev.forward(int(t)) for t in toks]
+        parity.update({"reference": f"the oracle: {args.cpu_steps} full decode steps at positions "
+                                    f"{P}..{P + args.cpu_steps - 1} from the GPU's KV-cache state",
+                       "logits_equal": all(np.array_equal(a.view(np.uint32), b.view(np.uint32))
+                                           for a, b in zip(ora_logits, gpu_logits)),
+                       "tokens_equal": [int(np.argmax(a)) for a in ora_logits] ==
+                                       [int(np.argmax(b)) for b in gpu_logits]})
         cpu = {"value": args.cpu_steps / cdt, "unit": "tok/s", "cores": cpu_threads(), "kind": "port",
                "sample": f"{args.cpu_steps} full decode steps (all {L} layers + classifier) at positions "
                          f"{P}..{P + args.cpu_steps - 1} from the GPU's KV-cache state (NumPy oracle, float64 "
@@ -593,23 +749,28 @@ def main():
             "config": config_of(cfg, args, ws, tp, ep),
             "e2e": {"value": seqs * args.steps / dt_e2e, "unit": "tok/s", "h2d_bytes_per_step": 8,
                     "d2h_bytes_per_step": 4 * cfg.vocab},
-            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak,
-                         "traffic": NCU_TRAFFIC["bytes"] if cfg.name == "Qwen3-0.6B" and not tp else None,
-                         "traffic_source": NCU_TRAFFIC["source"] if cfg.name == "Qwen3-0.6B" and not tp else
-                         "not captured for this classifier shape",
-                         "peak_source": peak_src,
-                         "kernel": f"gemv_kernel (classifier GEMV {N}x{K}, rmsnorm+quant prologue, fused argmax)",
-                         "bytes_per_launch": gemv_bytes, "us_per_launch": t_gemv * 1e6},
+            "roofline": None if dom is None else {
+                "bound": "hbm", "achieved": dom["GBs"], "peak": peak, "unit": "GB/s", "frac": dom["frac"],
+                "traffic": NCU_TRAFFIC.get(dom["kind"], {}).get("bytes") if cfg.name == "Qwen3-0.6B" and ws == 1
+                else None,
+                "traffic_source": NCU_TRAFFIC.get(dom["kind"], {}).get("source", "not captured for this shape"),
+                "peak_source": peak_src, "kernel": f"{dom['kernel']}: {dom['kind']}",
+                "bytes_per_launch": dom["bytes_per_launch"], "us_per_launch": dom["us_per_launch"],
+                "timing": "CUDA events over the kernel's launches for every layer, back to back without overlap"},
+            "kernels": table,
             "step_roofline": {"bytes_per_step": step_bytes, "achieved_gbs": step_bytes / (dt / args.steps) / 1e9,
                               "frac": step_bytes / (dt / args.steps) / 1e9 / peak},
             "cpu_baseline": cpu,
             "gpu_launches": args.steps * (1 + dec.kernel_launches(1)),
             "clocks": clk.summary(),
-            "prefill": {"tokens": P, "seconds": prefill_s, "tok_s": P / prefill_s},
-            "final_pos": final_pos, "pdl": bool(args.pdl),
+            "prefill": {"tokens": P, "seconds": prefill_s, "tok_s": P / prefill_s,
+                        "first_call_seconds": prefill_first_s,
+                        "timing": "host clock around LlamaDevice.prefill (synchronized), second call"},
+            "final_pos": final_pos, "pdl": bool(args.pdl), "parity": parity,
         }
         print(json.dumps(line), flush=True)
+        if not all(v for k, v in parity.items() if k != "reference"):
+            raise RuntimeError(f"parity failed: {parity}")
     barrier(ws)
     if ws > 1:
         import torch.distributed as dist

@@ -33,7 +33,7 @@ extern "C" {
 #define W8A8_ECUDA 3    /* the CUDA launch failed (cudaGetLastError) */
 #define W8A8_ESCRATCH 4 /* the scratch buffer is smaller than required */
 
-#define W8A8_ABI_VERSION 5
+#define W8A8_ABI_VERSION 6
 #define W8A8_MAX_ROWS 16 /* query rows per call (decode: 1, prefill chunk: 16) */
 
 /* ABI version (W8A8_ABI_VERSION) and a message for a status code. */
@@ -78,6 +78,15 @@ int w8a8_error_flags(uint32_t* flags);
  * identical either way; with it a kernel starts streaming its weights while
  * its predecessor finishes. Process-wide; not for concurrent callers. */
 int w8a8_set_pdl(int enable);
+
+/* Device timeline (trace builds only, -DW8A8_TRACE: libw8a8_b200_trace.so):
+ * point the instrumented decode kernels at `records` (capacity records of 3
+ * uint64: global timer ns, SM clock, kind << 56 | mark << 48 | smid << 32 |
+ * CTA) and the device counter of records taken; null pointers stop recording.
+ * W8A8_EINVAL in a normal build. The counterpart of the overlay's event
+ * counters and profile dump (rtl/sysarray/sa_perf.v,
+ * compiler/runtime/sa/sa_context.c:507-535). */
+int w8a8_trace_bind(void* records, uint32_t* counter, uint32_t capacity);
 
 /* W8A8 linear on int8 activations: acc = xq . W^T (int32), y = (f32(acc) * s_w) * s_x,
  * or y = resid + that when resid is not NULL (resid may equal y).
@@ -232,8 +241,11 @@ int w8a8_moe_combine(const float* wy, int rows, int top_k, int dim, const float*
  * pairs are grouped by expert on the device, so each expert's weight tiles are
  * read once per call rather than once per pair (above 128 rows on the tensor
  * cores: grouped tcgen05 GEMMs over per-expert slabs of the rows). scratch:
- * w8a8_moe_rows_scratch_bytes() bytes (its size does not depend on `experts`,
- * which it takes for the call's own argument list); dim a multiple of 32. The reference runs the MoE per row
+ * w8a8_moe_rows_scratch_bytes() bytes: the w8a8_moe_ffn scratch plus
+ * rows * top_k * dim fp32 terms, and above 128 rows each expert's slabs,
+ * experts * ceil(rows / 128) * 128 * (dim + expert_hidden + 4) bytes, with two
+ * rows * top_k per-pair arrays (about 200 MB at 4096 rows of a 32-expert,
+ * dim 1024, hidden 512 layer); dim a multiple of 32. The reference runs the MoE per row
  * (compiler/frontend/hf_generic.py:641-657); this is that loop over a batch. */
 #define W8A8_MOE_MAX_ROWS 4096
 size_t w8a8_moe_rows_scratch_bytes(int rows, int dim, int experts, int top_k, int expert_hidden);

@@ -2,7 +2,8 @@
 """Generate the golden fixtures that pin the oracle to the reference.
 
 Runs the reference's OWN code (Torch2RISCV-accelerator, imported unchanged
-from REF_ROOT, default /root/reference) and saves its inputs and outputs as
+from the checkout named by the REF_ROOT environment variable, which is
+required) and saves its inputs and outputs as
 small .npz files beside this script. Only this generator touches the reference;
 the tests read the .npz files (the reference is absent on GPU boxes).
 
@@ -29,10 +30,12 @@ Fixtures:
                 (compiler/tests/test_hf_moe.synthetic_model's shape).
   tiny_a_d8.w8a8  tiny model "a" of dm_tiny.npz written by the reference's
                 exporter (llm/export_w8a8.export, D = 8).
+  sampler.npz   llm/runtime.py's Sampler (run.c's sampler) token streams on
+                seeded logits for several temperatures, top-p values and seeds.
   tiny_a.bin    the same fp32 weights as a llama2.c legacy checkpoint
                 (separate classifier), checked against llm/checkpoint.load.
 
-    python tests/golden/make_golden.py [--skip-c0]
+    REF_ROOT=<reference checkout> python tests/golden/make_golden.py [--skip-c0]
 """
 import argparse
 import hashlib
@@ -43,7 +46,9 @@ import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 REPO = os.path.abspath(os.path.join(HERE, "..", ".."))
-REF = os.environ.get("REF_ROOT", "/root/reference")
+REF = os.environ.get("REF_ROOT")
+if not REF or not os.path.isdir(os.path.join(REF, "llm")):
+    raise SystemExit("set REF_ROOT to a checkout of Torch2RISCV-accelerator (the directory holding llm/)")
 sys.path.insert(0, REPO)
 sys.path.insert(0, os.path.join(REF, "llm"))
 sys.path.insert(0, os.path.join(REF, "driver"))
@@ -387,6 +392,26 @@ def gen_moe():
          us=q.us.numpy(), dq=q.dq.numpy(), ds=q.ds.numpy(), top_k=q.k)
 
 
+def gen_sampler():
+    """llm/runtime.py's Sampler (run.c's xorshift / softmax / top-p) on seeded
+    logits rows: the token stream of each (temperature, topp, seed)."""
+    src = open(os.path.join(REF, "llm", "runtime.py")).read()
+    a = src.index("class Sampler")
+    b = src.index("\nclass ", a + 1)
+    ns = {"np": np, "F": F}
+    exec(src[a:b], ns)                       # the class alone (the module imports the board tooling)
+    rng = np.random.default_rng(17)
+    logits = (rng.standard_normal((48, 512)) * 3).astype(F)
+    logits[::5, :12] = logits[::5, :1]       # tied maxima and tied probabilities
+    cfgs = np.array([(0.0, 0.9, 1), (1.0, 0.9, 1), (0.7, 0.95, 7), (1.3, 0.0, 3), (0.5, 1.0, 0), (1.0, 0.5, 42),
+                     (2.0, 0.99, 5)], np.float64)
+    streams = []
+    for t, p, seed in cfgs:
+        smp = ns["Sampler"](float(t), float(p), int(seed))
+        streams.append([smp(row) for row in logits])
+    save("sampler.npz", logits=logits, cfgs=cfgs, tokens=np.array(streams, np.int64))
+
+
 def gen_files():
     import checkpoint
     from export_w8a8 import export
@@ -411,11 +436,12 @@ def gen_files():
 def main():
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--skip-c0", action="store_true")
-    ap.add_argument("--only", help="comma list: sfu,convert,tiny,c0,hf,hfch,gelu,moe,files")
+    ap.add_argument("--only", help="comma list: sfu,convert,tiny,c0,hf,hfch,gelu,moe,sampler,files")
     a = ap.parse_args()
     only = set(a.only.split(",")) if a.only else None
     steps = [("sfu", gen_sfu), ("convert", gen_convert), ("tiny", gen_dm_tiny), ("c0", gen_dm_c0),
-             ("hf", gen_hf), ("hfch", gen_hf_channel), ("gelu", gen_gelu), ("moe", gen_moe), ("files", gen_files)]
+             ("hf", gen_hf), ("hfch", gen_hf_channel), ("gelu", gen_gelu), ("moe", gen_moe), ("sampler", gen_sampler),
+             ("files", gen_files)]
     for name, fn in steps:
         if (only and name not in only) or (name == "c0" and a.skip_c0):
             continue

@@ -107,12 +107,15 @@ def test_moe_rows_argument_checks(lib):
     assert call(sb=lib.w8a8_moe_scratch_bytes(64, 64, 2, 128)) == _lib.W8A8_ESCRATCH
     assert call(x=8) == _lib.W8A8_EALIGN
     assert call(x=None) == _lib.W8A8_EINVAL
-    # + the terms [rows, top_k, dim], then per expert a 128-row slab of int8 x
-    # and of int8 h, its row count and pair list, and per pair its slab row and
-    # h scale (each 256-byte aligned)
+    # + the terms [rows, top_k, dim]; above 128 rows (the tensor-core path)
+    # per expert a slab of int8 x and of int8 h (rows rounded up to 128), its
+    # row count and pair list, and per pair its slab row and h scale (each
+    # 256-byte aligned)
     assert (lib.w8a8_moe_rows_scratch_bytes(64, 64, 4, 2, 128) ==
-            lib.w8a8_moe_scratch_bytes(64, 64, 2, 128) + 64 * 2 * 64 * 4 + 4 * 128 * 64 + 4 * 128 * 128 + 256
-            + 4 * 128 * 4 + 2 * 512)
+            lib.w8a8_moe_scratch_bytes(64, 64, 2, 128) + 64 * 2 * 64 * 4)
+    assert (lib.w8a8_moe_rows_scratch_bytes(200, 64, 4, 2, 128) ==
+            lib.w8a8_moe_scratch_bytes(200, 64, 2, 128) + 200 * 2 * 64 * 4 + 4 * 256 * 64 + 4 * 256 * 128 + 256
+            + 4 * 256 * 4 + 2 * 1792)
 
 
 def test_gemm_and_batch_argument_checks(lib):

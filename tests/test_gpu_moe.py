@@ -152,3 +152,77 @@ def test_moe_grouped_rows_expert_parallel_terms(ranks, rows):
         total = (total + wy).astype(F)
     out = ops.moe_combine(cu(total), cu(resid), torch.empty(rows, cfg.dim, device=DEV))
     assert np.array_equal(bits(host(out)), bits(y))
+
+
+def skewed_case(rows, seed):
+    """C4 tables and rows whose routing piles onto a few experts: every row
+    shares one direction that router row 5 (and partly 9) follows, so expert 5
+    is in every row's Top-k (rows pairs: ceil(rows / 128) slab tiles) and a
+    few others in most."""
+    cfg = C.C4
+    rng = np.random.default_rng(seed)
+    t = c4_tables(rng, cfg.experts, cfg.dim, cfg.expert_hidden)
+    common = rng.standard_normal(cfg.dim).astype(F)
+    r = (rng.standard_normal((cfg.experts, cfg.dim)) * 0.05).astype(F)
+    r[5] = common * 0.05
+    r[9] = common * 0.04 + r[9] * 0.2
+    t["router"], t["s_router"] = quantize_rows(r)
+    x = (rng.standard_normal((rows, cfg.dim)) * 0.3 + common).astype(F)
+    g = (1 + 0.1 * rng.standard_normal(cfg.dim)).astype(F)
+    resid = rng.standard_normal((rows, cfg.dim)).astype(F)
+    return cfg, t, x, g, resid
+
+
+@pytest.mark.parametrize("rows", [300])
+def test_moe_grouped_rows_several_slab_tiles(rows):
+    """Experts with more than 128 and more than 256 pairs (the grouped
+    GEMMs' second and third slab tiles hold valid rows): bit-exact with the
+    per-row kernels over 16-row groups, and the expert-parallel terms of 2
+    ranks summed equal the one-GPU result."""
+    cfg, t, x, g, resid = skewed_case(rows, 123)
+    y, ids, w = run_rows(x, t, cfg.top_k, g, cfg.eps, resid=resid)
+    counts = np.bincount(ids.ravel(), minlength=cfg.experts)
+    assert counts[5] == rows and counts.max() > 256 and (counts > 128).sum() >= 3
+    for j in range(0, rows, 16):
+        yj, idj, wj = run(x[j:j + 16], t, cfg.top_k, norm_g=g, eps=cfg.eps, resid=resid[j:j + 16])
+        assert np.array_equal(ids[j:j + 16], idj), j
+        assert np.array_equal(bits(w[j:j + 16]), bits(wj)), j
+        assert np.array_equal(bits(y[j:j + 16]), bits(yj)), j
+    n = cfg.experts // 2
+    total = np.zeros((rows, cfg.top_k, cfg.dim), F)
+    for r in range(2):
+        wy, idr, _ = run_rows(x, t, cfg.top_k, g, cfg.eps, expert_lo=r * n, local=n)
+        assert np.array_equal(idr, ids)
+        total = (total + wy).astype(F)
+    out = ops.moe_combine(cu(total), cu(resid), torch.empty(rows, cfg.dim, device=DEV))
+    assert np.array_equal(bits(host(out)), bits(y))
+
+
+def test_moe_router_tie_goes_to_the_lower_expert():
+    """Router rows duplicated so that experts' scores tie exactly: Top-k keeps
+    the lower expert id first (docs/moe_native_lowering_design.md:340-345),
+    on the GPU as in the oracle, through the per-row and the grouped entries."""
+    cfg = C.C4
+    rng = np.random.default_rng(321)
+    t = c4_tables(rng, cfg.experts, cfg.dim, cfg.expert_hidden)
+    rq, rs = t["router"].copy(), t["s_router"].copy()
+    for dst, src in ((20, 3), (7, 3), (30, 11), (12, 11), (25, 0)):
+        rq[dst], rs[dst] = rq[src], rs[src]
+    t["router"], t["s_router"] = rq, rs
+    x = rng.standard_normal((40, cfg.dim)).astype(F)
+    g = (1 + 0.1 * rng.standard_normal(cfg.dim)).astype(F)
+    resid = rng.standard_normal((40, cfg.dim)).astype(F)
+    y, ids, w = run(x[:16], t, cfg.top_k, norm_g=g, eps=cfg.eps, resid=resid[:16])
+    xn = N.rmsnorm(x, g, cfg.eps)
+    tied = 0
+    for m in range(16):
+        ym, idm, wm = OM.moe_ffn_row(xn[m], t, cfg)
+        assert np.array_equal(ids[m], idm.astype(np.int32)), m
+        assert np.array_equal(bits(y[m]), bits((resid[m] + ym).astype(F))), m
+        for a, b in ((3, 7), (3, 20), (11, 12), (11, 30), (0, 25)):
+            if a in ids[m] and b in ids[m]:
+                tied += 1
+                assert list(ids[m]).index(min(a, b)) < list(ids[m]).index(max(a, b))
+    assert tied > 0
+    y2, ids2, w2 = run_rows(x, t, cfg.top_k, g, cfg.eps, resid=resid)
+    assert np.array_equal(ids2[:16], ids) and np.array_equal(bits(y2[:16]), bits(y))

@@ -7,10 +7,12 @@ import ctypes as C
 import os
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "libw8a8_b200.so")
+# W8A8_B200_LIB selects another build of the same ABI (the trace build,
+# libw8a8_b200_trace.so); the default is the in-tree library
+LIB_PATH = os.environ.get("W8A8_B200_LIB") or os.path.join(HERE, "libw8a8_b200.so")
 
 W8A8_OK, W8A8_EINVAL, W8A8_EALIGN, W8A8_ECUDA, W8A8_ESCRATCH = 0, 1, 2, 3, 4
-ABI_VERSION = 5
+ABI_VERSION = 6
 ACT_SILU, ACT_GELU_TANH = 0, 1
 TP_MAX_RANKS, TP_ROWS, TP_CTAS, TP_HEADER = 8, 4, 512, 256
 TP_STORE, TP_PARTIAL, TP_SWIGLU = 0, 1, 2
@@ -68,6 +70,7 @@ PROTOTYPES = {
     "w8a8_embed": (I, [P, I, P, P, I, I, P, P]),
     "w8a8_error_flags": (I, [C.POINTER(C.c_uint32)]),
     "w8a8_set_pdl": (I, [I]),
+    "w8a8_trace_bind": (I, [P, P, C.c_uint32]),
     "w8a8_linear": (I, [P, P, I, I, P, P, I, P, P, P, P]),
     "w8a8_linear_fused": (I, [P, P, F, I, I, P, P, I, P, P, P, P]),
     "w8a8_linear_chain": (I, [P, P, F, P, I, I, P, P, I, P, P, P, I, P]),

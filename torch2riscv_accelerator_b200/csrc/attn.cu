@@ -33,12 +33,15 @@
 
 #include "tp.cuh"
 #include "pdl.cuh"
+#include "trace.cuh"
 #include "w8a8_internal.h"
 #include "w8a8_math.cuh"
 
 namespace cg = cooperative_groups;
 
 namespace w8a8 {
+
+W8A8_TRACE_BINDER(trace_bind_attn)
 
 __device__ unsigned int g_attn_errors;                        // bit 2: a cache-tile copy wait gave up
 
@@ -131,6 +134,7 @@ __device__ __forceinline__ void warp_norm_rope(float* buf, int hd, const float* 
 
 __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
     extern __shared__ __align__(128) unsigned char sm[];
+    W8A8_TRACE_BEGIN(TR_ATTN);
     cg::cluster_group cl = cg::this_cluster();
     const int hd = p.head_dim, H = p.heads, Hk = p.kv_heads, G = H / Hk, T = p.seq_len;
     // batched decode: grid z is the slot (one row, its own position, qkv / att
@@ -226,14 +230,17 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
             }
     }
     pdl_wait();
+    W8A8_MARK(TR_ATTN, 1);
     pdl_trigger();
     if (grp && nvalid > 0) load_tiles();
     __syncthreads();
+    W8A8_MARK(TR_ATTN, 8);
     bool tiles_ok = true;
     if (nvalid > 0) {
         tiles_ok = mbar_wait(&tbar, 0u);                       // (issued before the wait: landed by now)
         if (!tiles_ok && tid == 0) atomicOr(&g_attn_errors, 4u);
     }
+    W8A8_MARK(TR_ATTN, 9);
     if (nvalid > 0) {
         float* buf = fbuf + warp * hd;
         // q path of every row and query head of this KV head (warps from 0), and
@@ -245,8 +252,10 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
             const float* src = qkv_p + (size_t)m * qkv_dim + (size_t)h * hd;
             for (int c = lane; c < hd; c += 32) buf[c] = src[c];
             __syncwarp();
+            if (r == 0) W8A8_MARK(TR_ATTN, 10);
             warp_norm_rope(buf, hd, p.qk_norm ? gains : nullptr, p.eps, p.inv_hd, tabs + 2 * m * hd,
                            tabs + (2 * m + 1) * hd, lane);
+            if (r == 0) W8A8_MARK(TR_ATTN, 11);
             if (p.k_ch != nullptr) {                           // K per channel: its scale folded into q
                 for (int c = lane; c < hd; c += 32) buf[c] = fmul(buf[c], p.k_ch[kvh * hd + c]);
                 __syncwarp();
@@ -259,6 +268,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
             for (int c = lane; c < hd; c += 32) qs[r * hd + c] = (int8_t)to_i8(fmul(buf[c], inv));
             if (lane == 0) sq[r] = s;
             __syncwarp();
+            if (r == 0) W8A8_MARK(TR_ATTN, 12);
         }
         // K and V rows of the positions in this chunk: into the cache and the tiles
         // (prefill groups: already in both)
@@ -283,6 +293,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
             __syncwarp();
         }
         __syncthreads();
+        W8A8_MARK(TR_ATTN, 2);
         // scores: thread t <-> positions t0 + t (+ 256); the row's 16-byte words are
         // read in a rotated order (conflict-free without padding)
         for (int r = 0; r < MG; ++r) {
@@ -311,6 +322,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
         }
         __syncthreads();
     }
+    W8A8_MARK(TR_ATTN, 3);
     // this chunk's maxima, pushed into every CTA of the cluster (remote stores)
     asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
     for (int i = tid; i < MG * CS; i += kAttnThreads) {
@@ -323,6 +335,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
         *cl.map_shared_rank(&lmax[rank][r], j) = s;
     }
     cl.sync();                                                 // every chunk's maxima are in place
+    W8A8_MARK(TR_ATTN, 4);
     if (tid < MG) {
         float mx = -INFINITY;
         for (int j = 0; j < CS; ++j) mx = nanmax(mx, lmax[j][tid]);
@@ -377,6 +390,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
             }
         }
         __syncthreads();
+        W8A8_MARK(TR_ATTN, 13);
         // p.V: thread <-> (row r, channel c) pairs; dp4a over 16-position words of
         // the int8 probabilities and the V^T row (padded: conflict-free)
         for (int i = tid; i < MG * hd; i += kAttnThreads) {
@@ -403,7 +417,9 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
         }
         for (int i = tid; i < MG * CS; i += kAttnThreads) *cl.map_shared_rank(&lsum[rank][i % MG], i / MG) = 0;
     }
+    W8A8_MARK(TR_ATTN, 5);
     cl.sync();                                                 // every CTA holds the partials of its slice
+    W8A8_MARK(TR_ATTN, 6);
     {
         const bool post = p.amax_out != nullptr || p.amax_ll_out != nullptr;
         if (tid < kMaxRows) amx[tid] = 0u;
@@ -440,6 +456,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
         }
     }
     if (!tiles_ok) mbar_wait(&tbar, 0u);                      // no copy may land after the CTA exits
+    W8A8_MARK(TR_ATTN, 7);
 }
 
 unsigned int attn_read_clear_errors() {

@@ -5,6 +5,7 @@
 #include <mutex>
 
 #include "../../include/w8a8.h"
+#include "trace.cuh"
 #include "w8a8_internal.h"
 
 using namespace w8a8;
@@ -97,6 +98,14 @@ int w8a8_set_pdl(int enable) {
     const int old = g_use_pdl;
     g_use_pdl = enable ? 1 : 0;
     return old;
+}
+
+int w8a8_trace_bind(void* records, uint32_t* counter, uint32_t capacity) {
+    if ((records == nullptr) != (counter == nullptr)) return W8A8_EINVAL;
+    if (trace_bind_gemv(records, counter, capacity) || trace_bind_attn(records, counter, capacity) ||
+        trace_bind_misc(records, counter, capacity))
+        return W8A8_EINVAL;                                    // not a trace build
+    return W8A8_OK;
 }
 
 static int check_linear(int rows, int k, const void* w, const float* s_w, int n, const void* y) {
@@ -323,19 +332,20 @@ static int moe_launch(const float* x, const float* norm_g, float eps, int rows, 
         // tensor-core path's count reset and two more launches cost more than
         // its GEMMs save there)
         const size_t mcap = ((size_t)rows + 127) / 128 * 128;
-        const bool tc = rows > 128;
-        p.mcap = (int)mcap;
-        p.slab_x = tc ? reinterpret_cast<int8_t*>(sp) : nullptr;
-        sp += a256((size_t)experts * mcap * dim);
-        p.slab_h = reinterpret_cast<int8_t*>(sp);
-        sp += a256((size_t)experts * mcap * expert_hidden);
-        p.cnt = reinterpret_cast<int*>(sp);
-        sp += a256((size_t)experts * 4);
-        p.slab_pair = reinterpret_cast<int*>(sp);
-        sp += a256((size_t)experts * mcap * 4);
-        p.pair_pos = reinterpret_cast<int*>(sp);
-        sp += a256((size_t)rows * top_k * 4);
-        p.s_h = reinterpret_cast<float*>(sp);
+        if (rows > 128) {
+            p.mcap = (int)mcap;
+            p.slab_x = reinterpret_cast<int8_t*>(sp);
+            sp += a256((size_t)experts * mcap * dim);
+            p.slab_h = reinterpret_cast<int8_t*>(sp);
+            sp += a256((size_t)experts * mcap * expert_hidden);
+            p.cnt = reinterpret_cast<int*>(sp);
+            sp += a256((size_t)experts * 4);
+            p.slab_pair = reinterpret_cast<int*>(sp);
+            sp += a256((size_t)experts * mcap * 4);
+            p.pair_pos = reinterpret_cast<int*>(sp);
+            sp += a256((size_t)rows * top_k * 4);
+            p.s_h = reinterpret_cast<float*>(sp);
+        }
         if (moe_smem(p, 0) > 200 * 1024 || moe_rows_smem(p, 1) > 200 * 1024 || moe_rows_smem(p, 2) > 200 * 1024)
             return W8A8_EINVAL;
         return cuda_status(launch_moe_rows(p, wy == nullptr, S(stream)));
@@ -348,8 +358,9 @@ static int moe_launch(const float* x, const float* norm_g, float eps, int rows, 
 size_t w8a8_moe_rows_scratch_bytes(int rows, int dim, int experts, int top_k, int expert_hidden) {
     if (rows <= 0 || dim <= 0 || experts <= 0 || top_k <= 0 || expert_hidden <= 0) return 0;
     const size_t mcap = ((size_t)rows + 127) / 128 * 128;                // slab rows per expert
-    return w8a8_moe_scratch_bytes(rows, dim, top_k, expert_hidden) + a256((size_t)rows * top_k * dim * 4) +
-           a256((size_t)experts * mcap * dim) + a256((size_t)experts * mcap * expert_hidden) +
+    const size_t base = w8a8_moe_scratch_bytes(rows, dim, top_k, expert_hidden) + a256((size_t)rows * top_k * dim * 4);
+    if (rows <= 128) return base;                                         // the CUDA-core kernels: no slabs
+    return base + a256((size_t)experts * mcap * dim) + a256((size_t)experts * mcap * expert_hidden) +
            a256((size_t)experts * 4) + a256((size_t)experts * mcap * 4) + 2 * a256((size_t)rows * top_k * 4);
 }
 

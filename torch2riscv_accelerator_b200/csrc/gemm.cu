@@ -123,8 +123,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const uint32_t tmem = tmem_base;
     pdl_wait();                                                // xq comes from the previous kernel
     pdl_trigger();
+    // grouped: a slab tile beyond the expert's row count has no valid row; its
+    // CTA loads nothing and issues no MMA (most tiles of a long prefill chunk,
+    // where each expert's slab is sized for every row)
+    const bool idle = GRP && gt * kBM >= __ldcg(p.g_cnt + ge);
 
-    if (warp == 0 && lane == 0) {
+    if (idle) {
+    } else if (warp == 0 && lane == 0) {
         // producer: stage s of step kt holds xq[m0.., kt*128..] and W[n0.., kt*128..]
         for (int kt = 0; kt < kt_n; ++kt) {
             const int s = kt % kStages;

@@ -27,8 +27,11 @@
 #include "linear_common.cuh"
 #include "pdl.cuh"
 #include "tp.cuh"
+#include "trace.cuh"
 
 namespace w8a8 {
+
+W8A8_TRACE_BINDER(trace_bind_gemv)
 
 __device__ unsigned int g_gemv_errors;    // bit 1: a tile wait gave up; bit 5: a tensor-parallel exchange wait
 
@@ -136,6 +139,7 @@ __device__ __forceinline__ void gemv_prologue(const LinearParams& p, int pro, in
         if (TP && pro == PRO_QUANT && p.amax_ll != nullptr)        // every rank's max|x| (its producer CTAs)
             pa = ll_block_max(p.tp, p.amax_ll, m, ep, ok, cnt, reinterpret_cast<uint32_t*>(red));
         __syncthreads();
+        W8A8_MARK(TR_GEMV, 6);
         float r = 1.f;
         if (pro == PRO_RMSQ) {
             if (warp == 0) {
@@ -144,6 +148,7 @@ __device__ __forceinline__ void gemv_prologue(const LinearParams& p, int pro, in
             }
             __syncthreads();
             r = bc[0];
+            W8A8_MARK(TR_GEMV, 7);
         }
         // y = (x * r) * g in place, and the row amax (unless the producer posted it)
         float a = 0.f;
@@ -160,8 +165,10 @@ __device__ __forceinline__ void gemv_prologue(const LinearParams& p, int pro, in
         }
         if (posted) a = __uint_as_float(pa);
         else a = block_nanmax(a, red);
+        W8A8_MARK(TR_GEMV, 8);
         const float s = fmul(a, W8A8_C127);
         const float inv = sfu_recip(s);
+        W8A8_MARK(TR_GEMV, 9);
 #pragma unroll 4
         for (int c = tid; c < k / 4; c += nt) {
             const float4 v = xf4[c];
@@ -254,6 +261,7 @@ __device__ __forceinline__ void swiglu_requant(const LinearParams& p) {
 template <int MR, bool TP>
 __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(LinearParams p, GemvCfg cf) {
     extern __shared__ __align__(128) unsigned char smem[];
+    W8A8_TRACE_BEGIN(TR_GEMV);
     const int pro = cf.pro, epi = cf.epi, tr = cf.tr, S = cf.S, stages = cf.stages, ntiles = cf.ntiles;
     const bool two = epi == EPI_SWIGLU;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -326,6 +334,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(LinearParams p, G
         if (lane == 0) bc[1] = __uint_as_float(t);
     }
     pdl_wait();
+    W8A8_MARK(TR_GEMV, 1);
     pdl_trigger();
     if (p.clear != nullptr && blockIdx.x == 0 && tid < p.clear_n) p.clear[tid] = 0u;   // its readers are done
     if (epi == EPI_RESID) {                                    // residual rows: written by earlier kernels
@@ -340,6 +349,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(LinearParams p, G
     bool ok = true;
     gemv_prologue<MR, TP>(p, pro, xs, xf, sx, gs, red, bc, ep, ok, llcnt);   // ends with a block barrier
     if (TP && !ok) atomicOr(&g_gemv_errors, 32u);
+    W8A8_MARK(TR_GEMV, 2);
 
     if (producer) {
         if (lane == 0) {                                       // refill each stage once its consumers are done
@@ -373,6 +383,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(LinearParams p, G
                 failed = 1;
                 break;
             }
+            if (i == 0) W8A8_MARK(TR_GEMV, 10);
             const int row0 = ((int)blockIdx.x + i * (int)gridDim.x) * tr;
             const int rows = min(tr, p.n - row0);
             const int8_t* wr = reinterpret_cast<const int8_t*>(ring + s * stage_bytes) + (size_t)r * k;
@@ -384,6 +395,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(LinearParams p, G
                 else tile_dots<MR, false>(wr, nullptr, xs, k, nch, sl, S, acc, acc2);
             }
             __syncwarp();
+            if (i == 0) W8A8_MARK(TR_GEMV, 11);
             if (lane == 0 && i + stages < my) mbar_arrive(&empty[s]);   // only a stage that is refilled
 #pragma unroll
             for (int m = 0; m < MR; ++m) {
@@ -433,6 +445,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(LinearParams p, G
             }
         }
     }
+    W8A8_MARK(TR_GEMV, 3);
     __syncthreads();
     if (failed) {                                              // a wait gave up: drain what is in flight, stop
         if (producer && lane == 0) {
@@ -455,6 +468,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(LinearParams p, G
         if (epi == EPI_STORE && p.key_out != nullptr)
             ll_post_key(p.tp, p.key_out, blockIdx.x, gridDim.x, m, m < p.m && m < MR ? bkey[m] : 0ull, ep);
     }
+    W8A8_MARK(TR_GEMV, 4);
     if (epi != EPI_SWIGLU || p.hq == nullptr) return;
     // the row amax across the grid; the last CTA requantizes h (quant_act)
     if (tid < p.m && tid < MR) atomicMax(p.amax_bits + tid, bamax[tid]);
@@ -463,6 +477,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(LinearParams p, G
     if (tid == 0) last = atomicAdd(p.counter, 1u) == gridDim.x - 1;
     __syncthreads();
     if (last) swiglu_requant(p);
+    W8A8_MARK(TR_GEMV, 5);
 }
 
 static int sm_count() {

@@ -4,8 +4,11 @@
 #include "linear_common.cuh"
 #include "pdl.cuh"
 #include "tp.cuh"
+#include "trace.cuh"
 
 namespace w8a8 {
+
+W8A8_TRACE_BINDER(trace_bind_misc)
 
 // Rows of x -> int8 rows and scales for the tensor-core GEMM: quant_act(x), or
 // quant_act(rmsnorm(x, g)) with the overlay's ordered sum (the GEMV prologue's
@@ -45,7 +48,9 @@ __device__ unsigned int g_w8a8_errors;
 // a token outside the table reads nothing: its row is zero and the error bit is set.
 __global__ void embed_kernel(const int32_t* tokens, const int8_t* emb_q, const float* emb_s, int vocab, int dim,
                              float* x, uint32_t* epoch) {
+    W8A8_TRACE_BEGIN(TR_EMBED);
     pdl_wait();
+    W8A8_MARK(TR_EMBED, 1);
     pdl_trigger();
     const int m = blockIdx.x;
     if (epoch != nullptr && m == 0 && threadIdx.x == 0) *epoch += 1u;   // tensor parallel: a new step
@@ -58,6 +63,7 @@ __global__ void embed_kernel(const int32_t* tokens, const int8_t* emb_q, const f
     const float s = emb_s[tok];
     const int8_t* q = emb_q + (size_t)tok * dim;
     for (int i = threadIdx.x; i < dim; i += blockDim.x) x[(size_t)m * dim + i] = fmul(i2f(q[i]), s);
+    W8A8_MARK(TR_EMBED, 2);
 }
 
 cudaError_t launch_embed(const int32_t* tokens, int m, const int8_t* emb_q, const float* emb_s, int vocab, int dim,
@@ -187,7 +193,9 @@ cudaError_t launch_sfu(int func, const float* x, float* y, long long n, cudaStre
 // (llm/runtime.py:127-148 on the host).
 __global__ void decode_advance_kernel(int32_t* tokens, int32_t* pos, unsigned long long* key, int32_t* next,
                                       int rows) {
+    W8A8_TRACE_BEGIN(TR_ADVANCE);
     pdl_wait();
+    W8A8_MARK(TR_ADVANCE, 1);
     pdl_trigger();
     const int m = threadIdx.x;
     if (m < rows) {
@@ -197,6 +205,7 @@ __global__ void decode_advance_kernel(int32_t* tokens, int32_t* pos, unsigned lo
         key[m] = 0ull;
         pos[m] += 1;
     }
+    W8A8_MARK(TR_ADVANCE, 2);
 }
 
 cudaError_t launch_decode_advance(int32_t* tokens, int32_t* pos, unsigned long long* key, int32_t* next, int rows,

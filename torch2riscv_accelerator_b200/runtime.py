@@ -25,42 +25,75 @@ F = np.float32
 BOS = 1
 
 
+_U64 = (1 << 64) - 1
+
+
+class XorShift64Star:
+    """run.c's generator (random_u32 / random_f32): the 64-bit state goes
+    through xorshift steps 12 (right), 25 (left), 27 (right); an output is the
+    high 32 bits of state * 0x2545F4914F6CDD1D, and a uniform float in [0, 1)
+    is its top 24 bits over 2^24. A zero seed would stay zero, so it runs as 1."""
+
+    def __init__(self, seed):
+        self.state = (int(seed) & _U64) or 1
+
+    def u32(self):
+        x = self.state
+        x ^= x >> 12
+        x = (x ^ (x << 25)) & _U64
+        x ^= x >> 27
+        self.state = x
+        return ((x * 0x2545F4914F6CDD1D) & _U64) >> 32
+
+    def unit(self):
+        return (self.u32() >> 8) / float(1 << 24)
+
+
+def softmax_f32(logits, temperature):
+    """float32 softmax of logits / temperature: exp(z - max z) over its float32
+    sum (the run.c sampler's probabilities, as llm/runtime.py forms them)."""
+    z = np.asarray(logits, F) / F(temperature)
+    e = np.exp(z - z.max())
+    return e / e.sum(dtype=F)
+
+
+def first_above(cdf, u):
+    """Index of the first cumulative probability above u, or the last index
+    when rounding left every entry at or below it (run.c sample_mult)."""
+    return min(int(np.searchsorted(cdf, u, side="right")), len(cdf) - 1)
+
+
+def nucleus_draw(p, topp, u):
+    """run.c sample_topp: candidates with p >= (1 - topp) / (n - 1), in
+    descending order (equal probabilities by index), kept up to the first
+    prefix whose float32 sum exceeds topp; then the draw u * (that sum) over
+    the kept prefix."""
+    cand = np.flatnonzero(p >= (1.0 - topp) / (p.size - 1))
+    order = cand[np.argsort(-p[cand], kind="stable")]
+    cdf = np.cumsum(p[order], dtype=F)
+    last = first_above(cdf, F(topp))
+    return int(order[first_above(cdf[:last + 1], u * float(cdf[last]))])
+
+
 class Sampler:
-    """run.c's sampler (temperature, top-p, xorshift RNG), `llm/runtime.py:37-72`."""
-    MASK = (1 << 64) - 1
+    """The next token from a row of logits, as run.c's sampler does it (the
+    reference's host runtime keeps that sampler: llm/runtime.py:37-72):
+    temperature 0 is greedy (the first maximum); otherwise one uniform draw per
+    call over softmax(logits / temperature), from the whole distribution when
+    topp is outside (0, 1), else from the top-p nucleus."""
 
     def __init__(self, temperature=0.0, topp=0.9, seed=1):
-        self.t, self.topp, self.state = temperature, topp, seed & self.MASK or 1
-
-    def _u32(self):
-        s = self.state
-        s ^= s >> 12
-        s ^= (s << 25) & self.MASK
-        s ^= s >> 27
-        self.state = s
-        return ((s * 0x2545F4914F6CDD1D) & self.MASK) >> 32
-
-    def _f32(self):
-        return (self._u32() >> 8) / 16777216.0
+        self.temperature, self.topp = float(temperature), float(topp)
+        self.rng = XorShift64Star(seed)
 
     def __call__(self, logits):
-        if self.t == 0:
+        if self.temperature == 0.0:
             return int(np.argmax(logits))
-        x = np.asarray(logits, F) / F(self.t)
-        p = np.exp((x - x.max()).astype(F)).astype(F)
-        p /= p.sum(dtype=F)
-        coin = self._f32()
-        if self.topp <= 0 or self.topp >= 1:
-            c = np.cumsum(p, dtype=F)
-            return int(min(np.searchsorted(c, coin, side="right"), p.size - 1))
-        cutoff = (1.0 - self.topp) / (p.size - 1)
-        idx = np.flatnonzero(p >= cutoff)
-        idx = idx[np.argsort(-p[idx], kind="stable")]
-        c = np.cumsum(p[idx], dtype=F)
-        last = int(min(np.searchsorted(c, F(self.topp), side="right"), idx.size - 1))
-        r = coin * float(c[last])
-        k = int(min(np.searchsorted(c[:last + 1], r, side="right"), last))
-        return int(idx[k])
+        p = softmax_f32(logits, self.temperature)
+        u = self.rng.unit()
+        if 0.0 < self.topp < 1.0:
+            return nucleus_draw(p, self.topp, u)
+        return first_above(np.cumsum(p, dtype=F), u)
 
 
 class LlamaDevice:
