@@ -132,7 +132,48 @@ __device__ __forceinline__ void warp_norm_rope(float* buf, int hd, const float* 
     __syncwarp();
 }
 
-__global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
+// The same head vector in registers: lane l holds elements c = l + 32 i (i < 8,
+// c < hd). RMSNorm's ordered sum is red_sum16's: lane l < 16 adds the squares
+// of elements l, l + 16, l + 32, ... in order (the odd groups come from lane
+// l + 16), then the pairwise tree over the 16 lanes. RoPE's neighbour c ^ 1 is
+// lane l ^ 1. Every value is the shared-memory form's bit for bit.
+__device__ __forceinline__ void reg_norm_rope(float (&v)[8], int hd, const float* g, float eps, float inv_hd,
+                                              const float* cosr, const float* sinr, int lane, const SfuSmem* sf) {
+    if (g != nullptr) {
+        float sq[8], pt[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) sq[i] = lane + 32 * i < hd ? fmul(v[i], v[i]) : 0.f;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) pt[i] = __shfl_down_sync(0xffffffffu, sq[i], 16);
+        float acc = 0.f;
+        if (lane < kLanes) {
+            acc = sq[0];
+            const int groups = hd / kLanes;
+#pragma unroll
+            for (int j = 1; j < 16; ++j)
+                if (j < groups) acc = fadd(acc, (j & 1) ? pt[j >> 1] : sq[j >> 1]);
+        }
+#pragma unroll
+        for (int s = 1; s < kLanes; s <<= 1) {
+            const float o = __shfl_down_sync(0xffffffffu, acc, s);
+            if ((lane & (2 * s - 1)) == 0) acc = fadd(acc, o);
+        }
+        const float r = sfu_rsqrt_s(fadd(fmul(__shfl_sync(0xffffffffu, acc, 0), inv_hd), eps), sf);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+            const int c = lane + 32 * i;
+            if (c < hd) v[i] = fmul(fmul(v[i], r), g[c]);
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+        const float nb = __shfl_xor_sync(0xffffffffu, v[i], 1);
+        const int c = lane + 32 * i;
+        if (c < hd) v[i] = fadd(fmul(v[i], cosr[c]), fmul((c & 1) ? nb : -nb, sinr[c]));
+    }
+}
+
+__global__ void __maxnreg__(104) attn_kernel(AttnParams p) {
     extern __shared__ __align__(128) unsigned char sm[];
     W8A8_TRACE_BEGIN(TR_ATTN);
     cg::cluster_group cl = cg::this_cluster();
@@ -170,13 +211,14 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
     __shared__ float lmax[kMaxCluster][kMaxRows * kMaxG];     // every CTA's chunk maxima (pushed by each)
     __shared__ float gmx[kMaxRows * kMaxG];
     __shared__ int lsum[kMaxCluster][kMaxRows * kMaxG];      // every CTA's sums of eq (pushed to all)
+    __shared__ int wsum[kAttnWarps][kMaxRows * kMaxG];
     __shared__ float sq[kMaxRows * kMaxG];
     __shared__ float wred[kAttnWarps][kMaxRows * kMaxG];
-    __shared__ int wsum[kAttnWarps][kMaxRows * kMaxG];
     __shared__ float rsum;
     __shared__ int lim_s[kMaxRows];
     __shared__ uint32_t amx[kMaxRows];                         // max|att| bits per row (decode chain)
     __shared__ __align__(8) uint64_t tbar;                     // the cache tiles' bulk copies landed
+    __shared__ SfuSmem sfs;                                    // RECIP / RSQRT on the critical path
 
     // every CTA of the cluster must have started before any remote store into its
     // shared memory: arrive now, wait just before the first push
@@ -191,11 +233,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
         etab[tid] = g_exp_t[tid];
         etab[64 + tid] = g_exp_s[tid];
     }
-    if (warp == 1) {                                           // bring the RECIP / RSQRT table lines in
-        uint32_t w = g_rec_t[lane * 2] ^ g_rec_s[lane * 2] ^ g_rsq_t[lane * 4] ^ g_rsq_s[lane * 4];
-        w = __reduce_xor_sync(0xffffffffu, w);
-        if (lane == 0) rsum = __uint_as_float(w);             // (rsum is rewritten before any use)
-    }
+    stage_sfu(&sfs);                                           // (read after the barrier below the wait)
     // the chunk's cache tiles: K rows as one contiguous block by one 1-D bulk copy
     // (16-byte aligned: head_dim and the chunk start are multiples of 16), the
     // V^T rows (a short run of positions per channel: one bulk copy each would
@@ -232,42 +270,60 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
     pdl_wait();
     W8A8_MARK(TR_ATTN, 1);
     pdl_trigger();
+    // the q rows of this warp's first (row, query head), and the K / V row of a
+    // position in this chunk, loaded into registers now: their latency overlaps
+    // the barrier below (the cache tiles' own stores must finish before a K / V
+    // row is patched into them)
+    const int r_first = warp;
+    float qv[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) qv[i] = 0.f;
+    if (nvalid > 0 && r_first < MG) {
+        const int m = r_first / G, h = kvh * G + r_first % G;
+        const float* src = qkv_p + (size_t)m * qkv_dim + (size_t)h * hd;
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+            if (lane + 32 * i < hd) qv[i] = src[lane + 32 * i];
+    }
     if (grp && nvalid > 0) load_tiles();
     __syncthreads();
     W8A8_MARK(TR_ATTN, 8);
     bool tiles_ok = true;
     if (nvalid > 0) {
-        tiles_ok = mbar_wait(&tbar, 0u);                       // (issued before the wait: landed by now)
-        if (!tiles_ok && tid == 0) atomicOr(&g_attn_errors, 4u);
-    }
-    W8A8_MARK(TR_ATTN, 9);
-    if (nvalid > 0) {
-        float* buf = fbuf + warp * hd;
-        // q path of every row and query head of this KV head (warps from 0), and
-        // the K / V rows of the positions in this chunk (warps from the last one)
-        // at the same time
-        float* kbuf = fbuf + (kAttnWarps + warp) * hd;              // the K row's own buffer
+        // q path of every row and query head of this KV head (warps from 0), in
+        // registers, and the K / V rows of the positions in this chunk (warps
+        // from the last one) at the same time
         for (int r = warp; r < MG; r += kAttnWarps) {
             const int m = r / G, h = kvh * G + r % G;
-            const float* src = qkv_p + (size_t)m * qkv_dim + (size_t)h * hd;
-            for (int c = lane; c < hd; c += 32) buf[c] = src[c];
-            __syncwarp();
-            if (r == 0) W8A8_MARK(TR_ATTN, 10);
-            warp_norm_rope(buf, hd, p.qk_norm ? gains : nullptr, p.eps, p.inv_hd, tabs + 2 * m * hd,
-                           tabs + (2 * m + 1) * hd, lane);
-            if (r == 0) W8A8_MARK(TR_ATTN, 11);
-            if (p.k_ch != nullptr) {                           // K per channel: its scale folded into q
-                for (int c = lane; c < hd; c += 32) buf[c] = fmul(buf[c], p.k_ch[kvh * hd + c]);
-                __syncwarp();
+            float v[8];
+            if (r == r_first) {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) v[i] = qv[i];
+            } else {
+                const float* src = qkv_p + (size_t)m * qkv_dim + (size_t)h * hd;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) v[i] = lane + 32 * i < hd ? src[lane + 32 * i] : 0.f;
             }
+            float kch[8];                                      // K per channel: its scale folded into q
+#pragma unroll
+            for (int i = 0; i < 8; ++i) kch[i] = p.k_ch != nullptr && lane + 32 * i < hd ? __ldg(p.k_ch + kvh * hd + lane + 32 * i) : 1.f;
+            if (r == 0) W8A8_MARK(TR_ATTN, 10);
+            reg_norm_rope(v, hd, p.qk_norm ? gains : nullptr, p.eps, p.inv_hd, tabs + 2 * m * hd,
+                          tabs + (2 * m + 1) * hd, lane, &sfs);
+            if (r == 0) W8A8_MARK(TR_ATTN, 11);
             float a = 0.f;
-            for (int c = lane; c < hd; c += 32) a = nanmax(a, fabsf(buf[c]));
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                if (p.k_ch != nullptr) v[i] = fmul(v[i], kch[i]);
+                if (lane + 32 * i < hd) a = nanmax(a, fabsf(v[i]));
+            }
             a = warp_max(a);
             const float s = fmul(a, W8A8_C127);
-            const float inv = sfu_recip(s);
-            for (int c = lane; c < hd; c += 32) qs[r * hd + c] = (int8_t)to_i8(fmul(buf[c], inv));
+            const float inv = sfu_recip_s(s, &sfs);
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                if (lane + 32 * i < hd) qs[r * hd + lane + 32 * i] = (int8_t)to_i8(fmul(v[i], inv));
             if (lane == 0) sq[r] = s;
-            __syncwarp();
             if (r == 0) W8A8_MARK(TR_ATTN, 12);
         }
         // K and V rows of the positions in this chunk: into the cache and the tiles
@@ -276,15 +332,25 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
             const int pos = pos_p[m];
             if (pos < t0 || pos >= t0 + CH) continue;
             const float* ksrc = qkv_p + (size_t)m * qkv_dim + q_dim + (size_t)kvh * hd;
-            for (int c = lane; c < hd; c += 32) kbuf[c] = ksrc[c];
-            __syncwarp();
-            warp_norm_rope(kbuf, hd, p.qk_norm ? gains + hd : nullptr, p.eps, p.inv_hd, tabs + 2 * m * hd,
-                           tabs + (2 * m + 1) * hd, lane);
+            const float* vsrc = ksrc + kv_dim;
+            float kv[8], vv[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const bool in = lane + 32 * i < hd;
+                kv[i] = in ? ksrc[lane + 32 * i] : 0.f;
+                vv[i] = in ? vsrc[lane + 32 * i] : 0.f;
+            }
+            reg_norm_rope(kv, hd, p.qk_norm ? gains + hd : nullptr, p.eps, p.inv_hd, tabs + 2 * m * hd,
+                          tabs + (2 * m + 1) * hd, lane, &sfs);
+            const bool landed = mbar_wait(&tbar, 0u);          // the tiles' copy first, then the patch
+            if (!landed && lane == 0) atomicOr(&g_attn_errors, 4u);
             int8_t* kdst = kc_p + ((size_t)kvh * T + pos) * hd;
-            const float* vsrc = qkv_p + (size_t)m * qkv_dim + q_dim + kv_dim + (size_t)kvh * hd;
-            for (int c = lane; c < hd; c += 32) {
-                const int8_t kq = (int8_t)to_i8(fmul(kbuf[c], p.inv_sk_ch ? p.inv_sk_ch[kvh * hd + c] : p.inv_sk));
-                const int8_t vq = (int8_t)to_i8(fmul(vsrc[c], p.inv_sv_ch ? p.inv_sv_ch[kvh * hd + c] : p.inv_sv));
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int c = lane + 32 * i;
+                if (c >= hd) continue;
+                const int8_t kq = (int8_t)to_i8(fmul(kv[i], p.inv_sk_ch ? p.inv_sk_ch[kvh * hd + c] : p.inv_sk));
+                const int8_t vq = (int8_t)to_i8(fmul(vv[i], p.inv_sv_ch ? p.inv_sv_ch[kvh * hd + c] : p.inv_sv));
                 kdst[c] = kq;
                 vc_p[((size_t)kvh * hd + c) * T + pos] = vq;
                 ks[(pos - t0) * hd + c] = kq;
@@ -292,6 +358,8 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
             }
             __syncwarp();
         }
+        tiles_ok = mbar_wait(&tbar, 0u);                       // (issued before the wait: landed by now)
+        if (!tiles_ok && tid == 0) atomicOr(&g_attn_errors, 4u);
         __syncthreads();
         W8A8_MARK(TR_ATTN, 2);
         // scores: thread t <-> positions t0 + t (+ 256); the row's 16-byte words are
@@ -313,9 +381,9 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
                     a = dp4a(x.z, y.z, a);
                     a = dp4a(x.w, y.w, a);
                 }
-                const float s = fmul(fmul(i2f(a), sq[r]), p.a_k);
-                scs[r * CH + t] = s;
-                mx = nanmax(mx, s);
+                const float sc = fmul(fmul(i2f(a), sq[r]), p.a_k);
+                scs[r * CH + t] = sc;
+                mx = nanmax(mx, sc);
             }
             mx = warp_max(mx);
             if (lane == 0) wred[warp][r] = mx;
@@ -358,7 +426,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
                     __syncthreads();
                     if (warp == 0) {
                         const float ssum = red_sum16([&](int i) { return ebuf[i]; }, n, lane);
-                        if (lane == 0) rsum = sfu_recip(ssum);
+                        if (lane == 0) rsum = sfu_recip_s(ssum, &sfs);
                     }
                     __syncthreads();
                 }
@@ -439,7 +507,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_kernel(AttnParams p) {
             if (p.variant == 0) {
                 out = fmul(o, av);
             } else {
-                const float rq = fmul(sfu_recip(i2f(ssum)), 127.f);   // sum <= 127 T: exact in fp32
+                const float rq = fmul(sfu_recip_s(i2f(ssum), &sfs), 127.f);   // sum <= 127 T: exact in fp32
                 out = fmul(fmul(o, rq), av);
             }
             att_p[((size_t)m * H + h) * hd + c] = out;

@@ -85,7 +85,7 @@ __device__ __forceinline__ float sumsq16(const float* xf, int k, int lane) {
 template <int MR, bool TP>
 __device__ __forceinline__ void gemv_prologue(const LinearParams& p, int pro, int8_t* xs, float* xf, float* sx,
                                               const float* gs, float* red, float* bc, uint32_t ep, bool& ok,
-                                              uint32_t* cnt) {
+                                              uint32_t* cnt, const SfuSmem* sf) {
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5, k = p.k, nt = (int)blockDim.x;
     if (pro == PRO_I8) {
 #pragma unroll 1
@@ -144,7 +144,7 @@ __device__ __forceinline__ void gemv_prologue(const LinearParams& p, int pro, in
         if (pro == PRO_RMSQ) {
             if (warp == 0) {
                 const float ss = sumsq16(xf, k, lane);
-                if (lane == 0) bc[0] = sfu_rsqrt(fadd(fmul(ss, p.inv_k), p.eps));
+                if (lane == 0) bc[0] = sfu_rsqrt_s(fadd(fmul(ss, p.inv_k), p.eps), sf);
             }
             __syncthreads();
             r = bc[0];
@@ -167,7 +167,7 @@ __device__ __forceinline__ void gemv_prologue(const LinearParams& p, int pro, in
         else a = block_nanmax(a, red);
         W8A8_MARK(TR_GEMV, 8);
         const float s = fmul(a, W8A8_C127);
-        const float inv = sfu_recip(s);
+        const float inv = sfu_recip_s(s, sf);
         W8A8_MARK(TR_GEMV, 9);
 #pragma unroll 4
         for (int c = tid; c < k / 4; c += nt) {
@@ -222,14 +222,14 @@ __device__ __forceinline__ void tile_dots(const int8_t* wr, const int8_t* wr2, c
 }
 
 // The last CTA of a SwiGLU launch: h -> int8 rows with the grid-wide amax.
-__device__ __forceinline__ void swiglu_requant(const LinearParams& p) {
+__device__ __forceinline__ void swiglu_requant(const LinearParams& p, const SfuSmem* sf) {
     const int tid = threadIdx.x;
     __threadfence();
 #pragma unroll 1
     for (int m = 0; m < p.m; ++m) {
         const float amax = __uint_as_float(__ldcg(p.amax_bits + m));
         const float s = fmul(amax, W8A8_C127);
-        const float inv = sfu_recip(s);
+        const float inv = sfu_recip_s(s, sf);
         const float4* hr = reinterpret_cast<const float4*>(p.y + (size_t)m * p.n);
         char4* qr = reinterpret_cast<char4*>(p.hq + (size_t)m * p.n);
         const int n4 = p.n / 4;
@@ -288,6 +288,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(LinearParams p, G
     __shared__ int last, failed;
     __shared__ uint32_t llcnt[kTpMaxRanks + 1];
     __shared__ uint32_t silu_tab[256];                         // EXP / RECIP tables (SwiGLU epilogue)
+    __shared__ SfuSmem sfs;                                    // RECIP / RSQRT (prologue, requant)
     if (tid < MR) {
         bamax[tid] = 0u;
         bkey[tid] = 0ull;
@@ -328,11 +329,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(LinearParams p, G
 #pragma unroll 1
         for (int c = tid; c < k; c += kGemvThreads) gs[c] = __ldg(p.norm_g + c);
     }
-    if (pro != PRO_I8 && warp == 0) {                          // bring the RECIP / RSQRT table lines in
-        uint32_t t = g_rec_t[lane * 2] ^ g_rec_s[lane * 2] ^ g_rsq_t[lane * 4] ^ g_rsq_s[lane * 4];
-        t = __reduce_xor_sync(0xffffffffu, t);
-        if (lane == 0) bc[1] = __uint_as_float(t);
-    }
+    if (pro != PRO_I8 || two) stage_sfu(&sfs);               // constants too (read after later barriers)
     pdl_wait();
     W8A8_MARK(TR_GEMV, 1);
     pdl_trigger();
@@ -347,7 +344,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(LinearParams p, G
     }
     const uint32_t ep = TP ? tp_epoch(p.tp) : 0u;             // this step's exchange words
     bool ok = true;
-    gemv_prologue<MR, TP>(p, pro, xs, xf, sx, gs, red, bc, ep, ok, llcnt);   // ends with a block barrier
+    gemv_prologue<MR, TP>(p, pro, xs, xf, sx, gs, red, bc, ep, ok, llcnt, &sfs);   // ends with a block barrier
     if (TP && !ok) atomicOr(&g_gemv_errors, 32u);
     W8A8_MARK(TR_GEMV, 2);
 
@@ -476,7 +473,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(LinearParams p, G
     __syncthreads();
     if (tid == 0) last = atomicAdd(p.counter, 1u) == gridDim.x - 1;
     __syncthreads();
-    if (last) swiglu_requant(p);
+    if (last) swiglu_requant(p, &sfs);
     W8A8_MARK(TR_GEMV, 5);
 }
 

@@ -132,7 +132,8 @@ __device__ __forceinline__ float sfu_recip(float x) { return sfu_recip_tab(x, g_
 
 // RSQRT (llm/sfu.py:99-114): x = m*2^E, odd E uses m' = 2m; j = 64*(E odd) +
 // top 6 fraction bits; y1 = y0*(1.5 - (m'*(y0*y0))*0.5); y1 * 2^(-(E - odd)/2).
-__device__ __forceinline__ float sfu_rsqrt(float x) {
+// rt, rs: the T and S tables wherever the caller keeps them.
+__device__ __forceinline__ float sfu_rsqrt_tab(float x, const uint32_t* rt, const uint32_t* rs) {
     uint32_t b = __float_as_uint(ftz(x));
     uint32_t s = b >> 31;
     int e = (int)((b >> 23) & 0xFFu);
@@ -146,11 +147,36 @@ __device__ __forceinline__ float sfu_rsqrt(float x) {
     int j = odd * 64 + (int)(frac >> 17);
     float m2 = __uint_as_float(frac | ((uint32_t)(127 + odd) << 23));
     float r = fmul(i2f((int)(frac & 0x1FFFFu)), 0x1p-17f);
-    float y0 = fadd(tab(g_rsq_t, j), fmul(r, tab(g_rsq_s, j)));
+    float y0 = fadd(__uint_as_float(rt[j]), fmul(r, __uint_as_float(rs[j])));
     float d = fsub(1.5f, fmul(fmul(m2, fmul(y0, y0)), 0.5f));
     float y1 = fmul(y0, d);
     return ldexp_ftz(y1, -((E - odd) / 2));
 }
+
+__device__ __forceinline__ float sfu_rsqrt(float x) { return sfu_rsqrt_tab(x, g_rsq_t, g_rsq_s); }
+
+// RECIP and RSQRT tables in shared memory, for the scalar lookups on a
+// kernel's critical path (quant_act's scale, RMSNorm's factor): a lookup in
+// constant memory that misses the SM's constant cache costs an L2 round trip.
+struct SfuSmem {
+    uint32_t rec_t[64], rec_s[64], rsq_t[128], rsq_s[128];
+};
+
+// Every thread of the block takes part; a block barrier must separate it from
+// the first lookup.
+__device__ __forceinline__ void stage_sfu(SfuSmem* sf) {
+    for (int i = threadIdx.x; i < 128; i += blockDim.x) {
+        if (i < 64) {
+            sf->rec_t[i] = g_rec_t[i];
+            sf->rec_s[i] = g_rec_s[i];
+        }
+        sf->rsq_t[i] = g_rsq_t[i];
+        sf->rsq_s[i] = g_rsq_s[i];
+    }
+}
+
+__device__ __forceinline__ float sfu_recip_s(float x, const SfuSmem* sf) { return sfu_recip_tab(x, sf->rec_t, sf->rec_s); }
+__device__ __forceinline__ float sfu_rsqrt_s(float x, const SfuSmem* sf) { return sfu_rsqrt_tab(x, sf->rsq_t, sf->rsq_s); }
 
 // SiLU gating (llm/ref_model.py:249-250): (g * RECIP(1 + EXP(g * -1))) * u
 __device__ __forceinline__ float silu_gate(float g, float u) {
