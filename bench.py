@@ -43,8 +43,14 @@ sys.path.insert(0, ROOT)
 METRIC = "decode tok/s (Qwen3-0.6B shape W8A8, T=2048)"
 # DRAM bytes (read + write) per launch of a kernel kind of the C2 step, from one
 # ncu capture each; the commands and the figures are in the named profiles.
+_LAYER = "profiles/decode_layer_c2_kernels.md"
 NCU_TRAFFIC = {"classifier GEMV (rmsnorm + quant)": {"bytes": 156221184 + 4762624,
-                                                       "source": "profiles/classifier_gemv_c2.txt"}}
+                                                       "source": "profiles/classifier_gemv_c2.txt"},
+               "attention (cluster kernel, KV cache)": {"bytes": 4299776, "source": _LAYER},
+               "qkv GEMV (rmsnorm + quant prologue)": {"bytes": 4279040, "source": _LAYER},
+               "o_proj GEMV (+ residual)": {"bytes": 2173696, "source": _LAYER},
+               "gate|up GEMV (rmsnorm + quant, SiLU gate)": {"bytes": 6385152, "source": _LAYER},
+               "down GEMV (+ residual)": {"bytes": 3226624, "source": _LAYER}}
 FPGA_TOKS = 3.41          # the reference's KV260 overlay, Qwen3-0.6B decode at T = 2048 (docs/results_v2.3.md:93-94)
 
 
@@ -715,6 +721,8 @@ def main():
     for k in table:
         k["frac"] = k["GBs"] / peak
         k["us_per_step"] = k["us_per_launch"] * k["launches_per_step"]
+        if cfg.name == "Qwen3-0.6B" and ws == 1 and k["kind"] in NCU_TRAFFIC:
+            k["traffic"] = NCU_TRAFFIC[k["kind"]]["bytes"]
     dom = max(table, key=lambda k: k["us_per_step"]) if table else None
     step_bytes = dec.weight_bytes() + dec.kv_bytes(cfg.seq_len - 8)
 
