@@ -40,10 +40,11 @@ def test_batch_generate_slots_equal_single_sequences(graphs):
             assert seen[(b, p)].tobytes() == ref[p].tobytes(), (b, p)
 
 
-@pytest.mark.parametrize("name,channel", [("C2", ""), ("C4", ""), ("C2", "kv"), ("C1", "")])
+@pytest.mark.parametrize("name,channel", [("C2", ""), ("C4", ""), ("C2", "kv"), ("C1", ""), ("C3", "")])
 def test_batch_step_full_dims_mixed_positions(name, channel):
     """C2 (dense, QK-norm, 128-dim heads), C4 (MoE; 64-dim heads, 6 ring
-    stages) or C1 (3 query heads per KV head, 5 ring stages) dimensions, 2
+    stages), C1 (3 query heads per KV head, 5 ring stages) or C3 (4 query heads
+    per KV head, 64-dim heads, dim 2048, hidden 8192) dimensions, 2
     layers, 20 slots (GEMMs of 20 rows, the MoE grouped by expert), each slot at
     its own position after a slot-specific history; C2 also with per-channel KV
     scales (the batched stream kernel's per-channel path)."""
@@ -65,3 +66,33 @@ def test_batch_step_full_dims_mixed_positions(name, channel):
         single.pos = int(offs[b])                                   # the same (empty) history before offs[b]
         for s in range(steps):
             assert single.forward(int(seqs[b][s])).tobytes() == got[b][s].tobytes(), (b, s)
+
+
+def test_batch_step_against_the_oracle():
+    """Batched decode checked against the oracle directly (not only against the
+    one-sequence GPU runtime): C3 dimensions (32 / 8 heads of 64), 2 layers, 18
+    slots at their own positions after their own histories; slots 0, 9 and 17
+    re-run on the oracle from the same tokens, logits bit for bit."""
+    from oracle import model as OM
+    cfg = C.C3.with_(layers=2, vocab=2048)
+    qw = W.QuantWeights(cfg, seed=3, gains="random", calib_tokens=np.arange(8))
+    kv = qw.kv_scales
+    D, steps = 18, 3
+    rng = np.random.default_rng(21)
+    hist = [list(rng.integers(0, cfg.vocab, int(n))) for n in rng.integers(1, 12, D)]
+    dev = BatchLlamaDevice((cfg, qw, kv), slots=D)
+    for b in range(D):
+        dev.clear_slot(b)
+    L = max(len(h) for h in hist)
+    last = [None] * D
+    for s in range(L):                                              # each slot's own history, then stops
+        live = [s < len(hist[b]) for b in range(D)]
+        lg = dev.step([s if live[b] else 0 for b in range(D)], [hist[b][s] if live[b] else 0 for b in range(D)])
+        for b in range(D):
+            if live[b] and s == len(hist[b]) - 1:
+                last[b] = lg[b].copy()
+    for b in (0, 9, 17):
+        ora = OM.OracleDecoder(cfg, qw, kv)
+        for p, t in enumerate(hist[b]):
+            want = np.asarray(ora.forward(int(t), p), np.float32)
+        assert want.tobytes() == last[b].tobytes(), b

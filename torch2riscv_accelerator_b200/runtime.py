@@ -14,6 +14,7 @@ BatchLlamaDevice is the reference's batched runtime (`llm/runtime.py:155-241`):
 D slots, each with its own KV cache and position, one token of every slot per
 step.
 """
+import os
 import time
 
 import numpy as np
@@ -96,12 +97,32 @@ class Sampler:
         return first_above(np.cumsum(p, dtype=F), u)
 
 
-class LlamaDevice:
-    """One sequence on one GPU. model: a DeviceDecoder, or (cfg, QuantWeights,
-    kv_scales) to build one. graphs: replay captured CUDA graphs (default)."""
+def _model_of(model):
+    """(cfg, weights, kv_scales) from a .w8a8 path (the reference's device
+    model file, `llm/export_w8a8.py`) or the tuple itself."""
+    if isinstance(model, (str, bytes, os.PathLike)):
+        from .loaders import read_w8a8
+        return read_w8a8(os.fspath(model))
+    return model
 
-    def __init__(self, model, device="cuda", graphs=True):
-        self.dec = model if isinstance(model, DeviceDecoder) else DeviceDecoder(*model, device=device)
+
+class LlamaDevice:
+    """One sequence on one GPU. model: a DeviceDecoder, (cfg, QuantWeights,
+    kv_scales) to build one, or the path of a .w8a8 model file as the
+    reference's constructor takes it (`llm/runtime.py:75-97`:
+    `LlamaDevice(model_path, tokenizer_path=None, bitfile=None, firmware=None,
+    use_irq=True, device=None)`). The overlay's bitstream, firmware and
+    interrupt mode have no counterpart on a GPU and are accepted for the same
+    call; tokenizers are outside this library (token ids in, logits out).
+    graphs: replay captured CUDA graphs (default)."""
+
+    def __init__(self, model, tokenizer_path=None, bitfile=None, firmware=None, use_irq=True, device="cuda",
+                 graphs=True):
+        if isinstance(model, DeviceDecoder):
+            self.dec = model
+        else:
+            self.dec = DeviceDecoder(*_model_of(model), device=device if device is not None else "cuda")
+        self.tokenizer_path = tokenizer_path
         self.cfg = self.dec.cfg
         self.graphs = graphs
         self.pos = 0
@@ -109,6 +130,11 @@ class LlamaDevice:
         self._rows = self.dec.rows_cap                    # most rows per launch
         self._in = torch.zeros(2 * self._rows, dtype=torch.int32).pin_memory()   # tokens | positions
         self._out = torch.zeros(self.cfg.vocab, dtype=torch.float32).pin_memory()
+
+    @classmethod
+    def from_w8a8(cls, path, **kw):
+        """A device for the model file at `path` (the reference exporter's .w8a8)."""
+        return cls(os.fspath(path), **kw)
 
     def reset(self):
         """Start a new sequence: empty KV cache, pos 0 (`llm/runtime.py:101-105`)."""
@@ -289,3 +315,58 @@ class BatchLlamaDevice:
     def close(self):
         self.dec = None
         torch.cuda.empty_cache()
+
+
+class DeviceRig:
+    """The B200 in the place of the overlay's functional simulator in the
+    reference's tests: `llm/test_l4.py:58-85` (Rig: the model, io area and KV
+    cache in the simulator's DDR, `run(dl, pos, token)` executing the list with
+    `SaFuncSim.run_list`, `llm/sa_funcsim.py:420`, then `logits()`, `x()`,
+    `kv_cache()` read back). Here `program()` builds the decoder's one-token
+    program once (the counterpart of `ModelCompiler(m).build()`: a CUDA graph
+    of the step, its inputs (pos, token) read from device memory as the list
+    reads PARAM and the argument block); `run(program, pos, token)` executes
+    it for any position and token and returns the number of kernels launched
+    (the list's count of decoded descriptors); the readers give the reference
+    rig's layouts (kv_cache [layers, 2, seq_len, kv_dim] int8). A device error
+    flag raised by the step (a token outside the vocabulary, a bounded wait
+    that gave up) is raised as RuntimeError, as the simulator raises SaError.
+    model: as LlamaDevice (a .w8a8 path, (cfg, weights, kv_scales) or a
+    DeviceDecoder)."""
+
+    def __init__(self, model, device="cuda"):
+        self.dec = model if isinstance(model, DeviceDecoder) else DeviceDecoder(*_model_of(model), device=device)
+        self.cfg = self.dec.cfg
+        self._prog = None
+
+    def program(self):
+        if self._prog is None:
+            self._prog = self.dec.capture(1, 1)
+        return self._prog
+
+    def run(self, program, pos, token):
+        from . import ops
+        c = self.cfg
+        if not 0 <= int(pos) < c.seq_len:
+            raise ValueError(f"position {pos} outside [0, {c.seq_len})")
+        self.dec.tokens[0] = int(token)
+        self.dec.pos[0] = int(pos)
+        program.replay()
+        torch.cuda.current_stream().synchronize()
+        flags = ops.error_flags()
+        if flags:
+            raise RuntimeError(f"pos {pos}: device error flags {flags:#x}")
+        return self.dec.kernel_launches(1)
+
+    def logits(self):
+        return self.dec.logits[0].cpu().numpy().copy()
+
+    def x(self):
+        return self.dec.x[0].cpu().numpy().copy()
+
+    def kv_cache(self):
+        c = self.cfg
+        out = np.empty((c.layers, 2, c.seq_len, c.kv_dim), np.int8)
+        for l in range(c.layers):
+            out[l, 0], out[l, 1] = self.dec.kv_rows(l, c.seq_len)
+        return out
