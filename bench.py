@@ -198,7 +198,7 @@ def run_reference(args, cfg, ws, rank):
         return
     tp, ep = split_kind(cfg, args, ws)
     qw = build_model(cfg, args.seed)
-    P = cfg.seq_len - args.warmup - args.steps
+    P = prompt_len(cfg, args)
     rng = np.random.default_rng(args.seed + 2)
     kc = np.zeros((cfg.layers, cfg.seq_len, cfg.kv_dim), np.int8)
     vc = np.zeros_like(kc)
@@ -212,7 +212,7 @@ def run_reference(args, cfg, ws, rank):
     # parallel) or N replicas; the CPU decodes the same sequences either way
     seqs = 1 if (tp or ep) else ws
     v = seqs * args.steps / (seqs * dt)
-    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "tok/s", "n_gpus": ws, "steps": args.steps,
+    line = {"impl": "reference", "metric": metric_of(cfg, args), "value": v, "unit": "tok/s", "n_gpus": ws, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": 1e3 * dt / args.steps, "higher_is_better": True,
             "scaling": "strong" if (tp or ep) else "weak", "vs_baseline": v / FPGA_TOKS, "dtype": "int8",
             "data": "synthetic", "config": config_of(cfg, args, ws, tp, ep),
@@ -329,7 +329,7 @@ def run_batch(args, cfg, qw, ws, rank, local):
     if rank == 0:
         kv_step = D * dec.slot_stride * 2 * (P + args.warmup + args.steps // 2) // cfg.seq_len
         line = {
-            "metric": METRIC, "value": seqs * args.steps / dt, "unit": "tok/s", "n_gpus": ws, "steps": args.steps,
+            "metric": metric_of(cfg, args), "value": seqs * args.steps / dt, "unit": "tok/s", "n_gpus": ws, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": 1e3 * dt / args.steps, "higher_is_better": True,
             "scaling": "strong" if split else "weak", "vs_baseline": None, "dtype": "int8",
             "data": "synthetic (N(0,0.02) weights seed 0, uniform token ids, seeded random int8 caches)",
@@ -354,6 +354,106 @@ def run_batch(args, cfg, qw, ws, rank, local):
     if ws > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
+
+
+# BASELINE.json's batched workloads as written: slots, prompt-length range,
+# decode tokens per sequence (C1, C3, C4; C2's batch 128 is run_batch's case)
+STATED = {"SmolLM2-135M": (64, (40, 40), 256), "Llama-3.2-1B": (256, (64, 1024), 128),
+          "Granite-3.1-1B-A400M": (64, (64, 64), 128), "Qwen3-0.6B": (128, (2032, 2032), 16)}
+
+
+def run_stated(args, cfg, qw, ws, rank, local):
+    """The config's batched workload as BASELINE.json states it, on one GPU:
+    D sequences with seeded prompt lengths and token ids; every step runs one
+    token of every live slot (its prompt's next token, then its greedy token)
+    at the slot's own position, as the reference's BatchLlamaDevice.generate
+    loop does (llm/runtime.py:210-241), until every sequence has its decode
+    tokens; a finished slot runs the dummy token at position 0. value: the
+    captured step replayed with the schedule on the device (tokens chosen by
+    device argmax), all slots' tokens per second; e2e: BatchLlamaDevice.step
+    with host tokens and the [D, vocab] logits back, on the first 48 steps."""
+    import torch
+    from torch2riscv_accelerator_b200 import ops
+    from torch2riscv_accelerator_b200.model import BatchDecoder
+    from torch2riscv_accelerator_b200.runtime import BOS, BatchLlamaDevice
+    if ws > 1 or cfg.name not in STATED:
+        raise SystemExit("--workload stated: one GPU and a config with a stated batched workload")
+    D, (lo, hi), gen = STATED[cfg.name]
+    rng = np.random.default_rng(args.seed + 7)
+    lens = rng.integers(lo, hi + 1, D)
+    prompts = rng.integers(0, cfg.vocab, (D, hi))
+    total = int(lens.max()) + gen
+    dec = BatchDecoder(cfg, qw, qw.kv_scales, slots=D)
+    dev = dec.dev
+    pr = torch.as_tensor(prompts, dtype=torch.int32, device=dev)
+    ln = torch.as_tensor(lens, dtype=torch.int32, device=dev)
+    greedy = torch.zeros(D, dtype=torch.int32, device=dev)
+    g = dec.capture()
+    st = torch.cuda.current_stream()
+
+    def step(s):
+        live = ln + gen > s
+        tok = torch.where(ln > s, pr[:, min(s, hi - 1)], greedy)
+        dec.tokens.copy_(torch.where(live, tok, torch.full_like(tok, BOS)))
+        dec.pos.copy_(torch.where(live, torch.full_like(ln, s), torch.zeros_like(ln)))
+        g.replay()
+        ops.argmax(dec.logits, out=greedy)
+
+    for s in range(args.warmup):
+        step(s)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with Clocks(local) as clk:
+        e0.record(st)
+        for s in range(total):
+            step(s)
+        e1.record(st)
+        torch.cuda.synchronize()
+    dt = e0.elapsed_time(e1) / 1e3
+    processed = int((lens + gen).sum())
+    # e2e: the same schedule through the runtime API, host tokens and logits
+    bdev = BatchLlamaDevice(dec)
+    n_e2e = min(48, total)
+    hg = np.zeros(D, np.int64)
+    h0, h1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    live_e2e = 0
+    h0.record(st)
+    for s in range(n_e2e):
+        live = lens + gen > s
+        tok = np.where(lens > s, prompts[:, min(s, hi - 1)], hg)
+        lg = bdev.step([s if live[b] else 0 for b in range(D)], [int(tok[b]) if live[b] else BOS for b in range(D)])
+        hg = lg.argmax(1)
+        live_e2e += int(live.sum())
+    h1.record(st)
+    torch.cuda.synchronize()
+    dt_e2e = h0.elapsed_time(h1) / 1e3
+    # bytes: every step streams the weights and each live slot's cache up to its position
+    wbytes = sum(t.numel() for w in dec.layers for t in w.values() if t.dtype == torch.int8) + dec.cls_q.numel()
+    kv = sum(2 * cfg.layers * cfg.kv_dim * int(min(s, l + gen - 1) + 1)
+             for l in lens for s in range(int(l) + gen))
+    nbytes = total * wbytes + kv
+    peak, peak_src = peaks()
+    if rank == 0:
+        line = {
+            "metric": metric_of(cfg, args), "value": processed / dt, "unit": "tok/s", "n_gpus": ws, "steps": total,
+            "warmup": args.warmup, "ms_per_step": 1e3 * dt / total, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "int8",
+            "data": "synthetic (N(0,0.02) weights seed 0, seeded prompt lengths and uniform token ids)",
+            "config": {"workload": f"{cfg.name}-shape W8A8 batched decode as stated: {D} sequences, prompt lengths "
+                                   f"U[{lo}, {hi}] fed one token per step, then {gen} greedy decode tokens each; "
+                                   f"{total} steps, every live slot one token per step",
+                       "model": cfg.name, "global_batch": D, "seq_len": cfg.seq_len, "parallelism": "replicas x1",
+                       "attention": cfg.attn, "l2": "no flush: every step streams the weights and the live caches"},
+            "decode_tok_s": D * gen / dt, "tokens_processed": processed,
+            "e2e": {"value": live_e2e / dt_e2e, "unit": "tok/s", "steps": n_e2e, "h2d_bytes_per_step": 8 * D,
+                    "d2h_bytes_per_step": 4 * D * cfg.vocab},
+            "roofline": {"bound": "hbm", "achieved": nbytes / dt / 1e9, "peak": peak, "unit": "GB/s",
+                         "frac": nbytes / dt / 1e9 / peak, "peak_source": peak_src, "traffic": None,
+                         "kernel": "the whole step (weights once per step + each live slot's KV up to its position)",
+                         "bytes": nbytes},
+            "gpu_launches": total * dec.kernel_launches(), "clocks": clk.summary(), "mode": "stated",
+        }
+        print(json.dumps(line), flush=True)
 
 
 def run_kernel(args, cfg):
@@ -535,8 +635,22 @@ def split_kind(cfg, args, ws):
     return not cfg.moe, cfg.moe
 
 
+def metric_of(cfg, args):
+    """BASELINE.json's metric for its workload (Qwen3 shape, batch 1, T = 2048);
+    other workloads name their own."""
+    if cfg.name == "Qwen3-0.6B" and args.batch <= 1 and not args.prompt:
+        return METRIC
+    return f"decode tok/s ({cfg.name} shape W8A8)"
+
+
+def prompt_len(cfg, args):
+    """Batch-1 prompt length: --prompt, else the context filled to its last
+    warmup + steps positions (T = 2048 for the Qwen3 shape)."""
+    return args.prompt if args.prompt else cfg.seq_len - args.warmup - args.steps
+
+
 def config_of(cfg, args, ws, tp=False, ep=False):
-    P = cfg.seq_len - args.warmup - args.steps
+    P = prompt_len(cfg, args)
     if ep:
         return {"workload": f"{cfg.name}-shape W8A8 MoE decode, batch 1, T=2048, experts split over {ws} GPUs: "
                             f"{P}-token prompt prefilled, then {args.warmup} untimed + {args.steps} timed greedy "
@@ -552,11 +666,12 @@ def config_of(cfg, args, ws, tp=False, ep=False):
                 "parallelism": f"tp{ws}", "attention": cfg.attn,
                 "l2": "no flush: each rank's step streams its shard of the weights and KV cache (over the L2 "
                       "size at every rank count)"}
-    return {"workload": f"{cfg.name}-shape W8A8 decode, batch 1 per GPU, T=2048: {P}-token prompt prefilled in "
-                        f"16-row chunks, then {args.warmup} untimed + {args.steps} timed greedy decode steps",
+    return {"workload": f"{cfg.name}-shape W8A8 decode, batch 1 per GPU, T={cfg.seq_len}: {P}-token prompt prefilled "
+                        f"in chunks, then {args.warmup} untimed + {args.steps} timed greedy decode steps",
             "model": cfg.name, "global_batch": ws, "seq_len": cfg.seq_len, "prompt": P,
             "parallelism": f"replicas x{ws}", "attention": cfg.attn,
-            "l2": "no flush: the step streams 596 MB of weights + 117 MB of KV, over 4x the 126 MB L2"}
+            "l2": "no flush: the step streams the whole model's weights (596 MB for the Qwen3 shape) and its KV "
+                  "cache, over the 126 MB L2"}
 
 
 def main():
@@ -574,6 +689,11 @@ def main():
                     help="sequences per step (BatchLlamaDevice); > 1 measures batched decode instead")
     ap.add_argument("--parallel", default="tp", choices=["tp", "replicas"],
                     help="with several GPUs: one sequence tensor-parallel (tp) or independent replicas")
+    ap.add_argument("--prompt", type=int, default=0,
+                    help="batch 1: prompt length (default: the context filled to its last warmup + steps positions)")
+    ap.add_argument("--workload", default="bench", choices=["bench", "stated"],
+                    help="with --batch: 'stated' runs BASELINE.json's batched workload of the config as written "
+                         "(seeded prompts fed one token per step, then greedy decode; every slot its own lengths)")
     ap.add_argument("--kernel", choices=["attn_batch", "moe_rows"],
                     help="time one kernel alone instead (profiling): attn_batch = the batched decode attention "
                          "over one layer's caches of --batch slots at position 2040; moe_rows = one layer's MoE "
@@ -584,7 +704,10 @@ def main():
     from torch2riscv_accelerator_b200.config import CONFIGS
     cfg = CONFIGS[args.config]
     ws, rank, local = dist_init()
-    if args.warmup + args.steps > 64:
+    if args.prompt:
+        if not 1 <= args.prompt <= cfg.seq_len - args.warmup - args.steps:
+            raise SystemExit(f"--prompt + warmup + steps must fit the context of {cfg.seq_len}")
+    elif args.warmup + args.steps > 64:
         raise SystemExit("warmup + steps must leave a prompt of >= 1984 tokens (at most 64)")
     if args.impl == "reference":
         run_reference(args, cfg, ws, rank)
@@ -603,6 +726,9 @@ def main():
     from torch2riscv_accelerator_b200 import _lib
     _lib.load().w8a8_set_pdl(args.pdl)
     qw = build_model(cfg, args.seed)
+    if args.batch > 1 and args.workload == "stated":
+        run_stated(args, cfg, qw, ws, rank, local)
+        return
     if args.batch > 1:
         run_batch(args, cfg, qw, ws, rank, local)
         return
@@ -620,7 +746,7 @@ def main():
         dev = LlamaDevice(dec)
     split = tp or ep
     seqs = 1 if split else ws                            # sequences decoded per step over all GPUs
-    P = cfg.seq_len - args.warmup - args.steps
+    P = prompt_len(cfg, args)
     prompt = np.random.default_rng(args.seed + 3).integers(0, cfg.vocab, P)
     torch.cuda.synchronize()
     t0 = time.perf_counter()
@@ -750,7 +876,7 @@ def main():
 
     if rank == 0:
         line = {
-            "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": ws, "steps": args.steps,
+            "metric": metric_of(cfg, args), "value": value, "unit": "tok/s", "n_gpus": ws, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": 1e3 * dt / args.steps, "higher_is_better": True,
             "scaling": "strong" if split else "weak", "vs_baseline": value / FPGA_TOKS, "dtype": "int8",
             "data": "synthetic (N(0,0.02) weights seed 0, uniform prompt ids)",
