@@ -17,7 +17,7 @@ CSRC = os.path.join(HERE, "csrc")
 LIB = os.path.join(HERE, "libw8a8_b200.so")
 TRACE_LIB = os.path.join(HERE, "libw8a8_b200_trace.so")
 SOURCES = ["capi.cu", "linear.cu", "gemv.cu", "attn.cu", "misc.cu", "moe.cu", "gemm.cu"]
-HEADERS = ["w8a8_math.cuh", "w8a8_internal.h", "sfu_tables.h", "pdl.cuh", "tp.cuh", "linear_common.cuh", "trace.cuh",
+HEADERS = ["w8a8_math.cuh", "w8a8_internal.h", "sfu_tables.h", "pdl.cuh", "tp.cuh", "linear_common.cuh", "trace.cuh", "tc.cuh",
            os.path.join("..", "..", "include", "w8a8.h")]
 NVCC_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17", "-fmad=false",
               "-ftz=false", "-prec-div=true", "-prec-sqrt=true", "-Xcompiler", "-fPIC", "-shared",

@@ -12,7 +12,10 @@ from release to end, and the median duration of each phase (SM clock between
 consecutive marks of a CTA, converted at the clock given).
 
     python -m torch2riscv_accelerator_b200.trace [--config Qwen3-0.6B] [--steps 3]
-        [--out timeline.npy] [--sm-ghz 1.965]
+        [--batch D] [--out timeline.npy] [--sm-ghz 1.965]
+
+--batch D traces the batched step instead (D slots at position T - 8 of
+seeded random caches): the instrumented kernels it launches (embed).
 
 Mark numbers per kernel (csrc/gemv.cu, csrc/attn.cu): GEMV 0 entry, 1 wait
 returned, 6 x staged, 7 RMSNorm factor, 8 row max, 9 scale, 2 prologue done,
@@ -34,12 +37,63 @@ MARKS = 16                                         # records reserved per CTA (k
 KIND = {1: "gemv", 2: "attn", 3: "embed", 4: "advance"}
 
 
+def _bind(rec, cnt, cap):
+    from . import _lib
+    _lib.check("w8a8_trace_bind", _lib.load().w8a8_trace_bind(rec.data_ptr(), cnt.data_ptr(), cap))
+
+
+def _load_trace_lib():
+    os.environ["W8A8_B200_LIB"] = TRACE_LIB
+    from . import _lib
+    if _lib._LIB is not None and _lib.LIB_PATH != TRACE_LIB:
+        raise RuntimeError("the plain library is already loaded in this process")
+    _lib.LIB_PATH = TRACE_LIB
+    return _lib.load(TRACE_LIB)
+
+
+def capture_batch(config="Qwen3-0.6B", slots=128, steps=3, seed=0):
+    """The batched step (BatchDecoder, `slots` slots at position T - 8 of
+    seeded random int8 caches), captured and replayed `steps` times with the
+    records bound; returns (records, ms per step)."""
+    lib = _load_trace_lib()
+    import torch
+
+    from .config import CONFIGS
+    from .model import BatchDecoder
+    from .weights import QuantWeights
+    cfg = CONFIGS[config]
+    qw = QuantWeights(cfg, seed=seed, calib_tokens=np.random.default_rng(seed + 1).integers(0, cfg.vocab, 16))
+    dec = BatchDecoder(cfg, qw, qw.kv_scales, slots=slots)
+    g = torch.Generator(device=dec.dev).manual_seed(seed + 11)
+    for t in (dec.kc, dec.vc):
+        t.copy_(torch.randint(-127, 128, t.shape, dtype=torch.int8, device=dec.dev, generator=g))
+    dec.tokens.copy_(torch.as_tensor(np.random.default_rng(seed + 3).integers(0, cfg.vocab, slots), dtype=torch.int32))
+    dec.pos.fill_(cfg.seq_len - 8)
+    graph = dec.capture()
+    for _ in range(3):
+        graph.replay()
+    torch.cuda.synchronize()
+    cap = 1 << 21
+    rec = torch.zeros(cap * 3, dtype=torch.int64, device=dec.dev)
+    cnt = torch.zeros(1, dtype=torch.int32, device=dec.dev)
+    _bind(rec, cnt, cap)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        graph.replay()
+    e1.record()
+    torch.cuda.synchronize()
+    lib.w8a8_trace_bind(None, None, 0)
+    n = min(int(cnt.item()), cap)
+    return rec[:n * 3].view(n, 3).cpu().numpy().view(np.uint64), e0.elapsed_time(e1) / steps
+
+
 def capture(config="Qwen3-0.6B", steps=3, seed=0):
     """Prefill a seeded prompt to T - 16 positions, capture the decode step,
     replay it `steps` times with the records bound; returns the records
     [n, 3] uint64 and the mean ms per step (the trace build is slower than the
     plain one: its marks are extra stores)."""
-    os.environ["W8A8_B200_LIB"] = TRACE_LIB
+    lib = _load_trace_lib()
     import torch
 
     from . import _lib
@@ -47,10 +101,6 @@ def capture(config="Qwen3-0.6B", steps=3, seed=0):
     from .model import DeviceDecoder
     from .runtime import LlamaDevice
     from .weights import QuantWeights
-    if _lib._LIB is not None and _lib.LIB_PATH != TRACE_LIB:
-        raise RuntimeError("the plain library is already loaded in this process")
-    _lib.LIB_PATH = TRACE_LIB
-    lib = _lib.load(TRACE_LIB)
     cfg = CONFIGS[config]
     qw = QuantWeights(cfg, seed=seed, calib_tokens=np.random.default_rng(seed + 1).integers(0, cfg.vocab, 16))
     dec = DeviceDecoder(cfg, qw, qw.kv_scales)
@@ -138,18 +188,20 @@ def main():
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--config", default="Qwen3-0.6B")
     ap.add_argument("--steps", type=int, default=3)
+    ap.add_argument("--batch", type=int, default=0, help="trace the batched step of this many slots")
     ap.add_argument("--out", default=None, help="save the raw records (.npy)")
     ap.add_argument("--sm-ghz", type=float, default=1.965, help="SM clock for the clock64 durations")
     a = ap.parse_args()
-    raw, ms = capture(a.config, a.steps)
+    raw, ms = capture_batch(a.config, a.batch, a.steps) if a.batch else capture(a.config, a.steps)
     if a.out:
         np.save(a.out, raw)
     kinds, span, n = summarise(raw, a.sm_ghz)
     print(f"{a.config}: {a.steps} replays of the decode step, {ms:.3f} ms per step (trace build), "
           f"{n} launches over {span:.1f} us")
     for name, k in kinds.items():
-        print(f"{name:8s} launches {k['launches']:4d} CTAs {k['ctas']} gap {k['gap_us']:.2f} us, "
-              f"release to end {k['release_to_end_us']:.2f} us")
+        gap = "-" if k["gap_us"] is None else f"{k['gap_us']:.2f}"
+        rel = "-" if k["release_to_end_us"] is None else f"{k['release_to_end_us']:.2f}"
+        print(f"{name:8s} launches {k['launches']:4d} CTAs {k['ctas']} gap {gap} us, release to end {rel} us")
         print(f"         phases (us): {k['phases_us']}")
     return 0
 
