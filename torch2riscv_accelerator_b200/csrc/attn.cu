@@ -107,10 +107,12 @@ __device__ __forceinline__ float warp_max(float v) {
 // One head vector in shared memory (buf[hd], loaded by the warp): optional
 // RMSNorm with gain g, then RoPE with the position's table rows; in place.
 __device__ __forceinline__ void warp_norm_rope(float* buf, int hd, const float* g, float eps, float inv_hd,
-                                               const float* cosr, const float* sinr, int lane) {
+                                               const float* cosr, const float* sinr, int lane,
+                                               const SfuSmem* sf = nullptr) {
     if (g != nullptr) {
         const float ss = red_sum16([&](int i) { return fmul(buf[i], buf[i]); }, hd, lane);
-        const float r = sfu_rsqrt(fadd(fmul(ss, inv_hd), eps));
+        const float x = fadd(fmul(ss, inv_hd), eps);
+        const float r = sf != nullptr ? sfu_rsqrt_s(x, sf) : sfu_rsqrt(x);
         for (int c = lane; c < hd; c += 32) buf[c] = fmul(fmul(buf[c], r), g[c]);
         __syncwarp();
     }
@@ -623,6 +625,8 @@ __global__ void __launch_bounds__(kSbThreads, MINB)
     __shared__ __align__(8) uint64_t full[kSbMaxStages], empty[kSbMaxStages];
     __shared__ float sq[kMaxG], gmx[kMaxG], wred[kSbWarps][kMaxG], rcp[kMaxG];
     __shared__ int wsum[kSbWarps][kMaxG], lsum[kMaxG];
+    __shared__ float rqs[kMaxG];                               // QSUM: RECIP(sum eq) * 127 per row
+    __shared__ SfuSmem sfs;                                    // RECIP / RSQRT (q path, softmax scales)
     __shared__ int failed;
     const int pos = p.pos[slot];                               // written by an earlier step: read before the wait
     const int nt = pos / tp + 1;                               // K tiles with positions <= pos
@@ -664,6 +668,7 @@ __global__ void __launch_bounds__(kSbThreads, MINB)
         etab[tid] = g_exp_t[tid];
         etab[64 + tid] = g_exp_s[tid];
     }
+    stage_sfu(&sfs);                                           // (read after the barrier below the wait)
     for (int c = tid; c < hd; c += kSbThreads) {
         tabs[c] = __ldg(p.cos + (size_t)pos * hd + c);
         tabs[hd + c] = __ldg(p.sin + (size_t)pos * hd + c);
@@ -696,7 +701,7 @@ __global__ void __launch_bounds__(kSbThreads, MINB)
             const float* src = qrow + (size_t)(kvh * G + r) * hd;
             for (int c = lane; c < hd; c += 32) buf[c] = src[c];
             __syncwarp();
-            warp_norm_rope(buf, hd, p.qk_norm ? gains : nullptr, p.eps, p.inv_hd, tabs, tabs + hd, lane);
+            warp_norm_rope(buf, hd, p.qk_norm ? gains : nullptr, p.eps, p.inv_hd, tabs, tabs + hd, lane, &sfs);
             if (p.k_ch != nullptr) {                           // K per channel: its scale folded into q
                 for (int c = lane; c < hd; c += 32) buf[c] = fmul(buf[c], p.k_ch[kvh * hd + c]);
                 __syncwarp();
@@ -705,7 +710,7 @@ __global__ void __launch_bounds__(kSbThreads, MINB)
             for (int c = lane; c < hd; c += 32) a = nanmax(a, fabsf(buf[c]));
             a = warp_max(a);
             const float sc = fmul(a, W8A8_C127);
-            const float inv = sfu_recip(sc);
+            const float inv = sfu_recip_s(sc, &sfs);
             for (int c = lane; c < hd; c += 32) qs[r * hd + c] = (int8_t)to_i8(fmul(buf[c], inv));
             if (lane == 0) sq[r] = sc;
             __syncwarp();
@@ -716,7 +721,7 @@ __global__ void __launch_bounds__(kSbThreads, MINB)
             const float* vsrc = qrow + q_dim + kv_dim + (size_t)kvh * hd;
             for (int c = lane; c < hd; c += 32) kb[c] = ksrc[c];
             __syncwarp();
-            warp_norm_rope(kb, hd, p.qk_norm ? gains + hd : nullptr, p.eps, p.inv_hd, tabs, tabs + hd, lane);
+            warp_norm_rope(kb, hd, p.qk_norm ? gains + hd : nullptr, p.eps, p.inv_hd, tabs, tabs + hd, lane, &sfs);
             int8_t* kdst = p.kc + (size_t)slot * p.slot_stride + ((size_t)kvh * T + pos) * hd;
             int8_t* vdst = p.vc + (size_t)slot * p.slot_stride + (size_t)kvh * hd * T + pos;
             for (int c = lane; c < hd; c += 32) {
@@ -837,7 +842,7 @@ __global__ void __launch_bounds__(kSbThreads, MINB)
             for (int r = warp; r < G; r += kSbWarps) {
                 const float* er = scs + r * Tp;
                 const float ssum = red_sum16([&](int i) { return er[i]; }, n, lane);
-                if (lane == 0) rcp[r] = sfu_recip(ssum);
+                if (lane == 0) rcp[r] = sfu_recip_s(ssum, &sfs);
             }
             named_barrier_sync(1, kSbWarps * 32);
             for (int r = 0; r < G; ++r) {
@@ -872,6 +877,7 @@ __global__ void __launch_bounds__(kSbThreads, MINB)
                 int v = 0;
                 for (int w = 0; w < kSbWarps; ++w) v += wsum[w][tid];
                 lsum[tid] = v;
+                rqs[tid] = fmul(sfu_recip_s(i2f(v), &sfs), 127.f);   // sum <= 127 T: exact in fp32
             }
         }
         named_barrier_sync(1, kSbWarps * 32);
@@ -917,7 +923,7 @@ __global__ void __launch_bounds__(kSbThreads, MINB)
                     const float av = p.a_v_ch ? p.a_v_ch[kvh * hd + c] : p.a_v;   // V per channel or per layer
                     float out;
                     if (p.variant == 0) out = fmul(ov, av);
-                    else out = fmul(fmul(ov, fmul(sfu_recip(i2f(lsum[r])), 127.f)), av);   // sum <= 127 T: exact
+                    else out = fmul(fmul(ov, rqs[r]), av);
                     att[(size_t)(kvh * G + r) * hd + c] = out;
                     am = max(am, __float_as_uint(fabsf(out)));
                 }
