@@ -231,10 +231,7 @@ __global__ void __maxnreg__(104) attn_kernel(AttnParams p) {
     const int nvalid = min(CH, maxpos + 1 - t0);
     const int nv16 = (nvalid + 15) & ~15;                      // V^T rows are read in 16-position words
     if (tid < M) lim_s[tid] = min(nvalid, pos_p[tid] + 1 - t0);  // positions of the chunk row m attends
-    if (tid < 64) {
-        etab[tid] = g_exp_t[tid];
-        etab[64 + tid] = g_exp_s[tid];
-    }
+    stage_exp_table(etab);
     stage_sfu(&sfs);                                           // (read after the barrier below the wait)
     // the chunk's cache tiles: K rows as one contiguous block by one 1-D bulk copy
     // (16-byte aligned: head_dim and the chunk start are multiples of 16), the
@@ -664,10 +661,7 @@ __global__ void __launch_bounds__(kSbThreads, MINB)
     };
     if (producer && lane == 0)                                 // cache rows of earlier steps: before the wait
         for (int i = 0; i < ns && i < ntiles; ++i) issue(i);
-    if (tid < 64) {
-        etab[tid] = g_exp_t[tid];
-        etab[64 + tid] = g_exp_s[tid];
-    }
+    stage_exp_table(etab);
     stage_sfu(&sfs);                                           // (read after the barrier below the wait)
     for (int c = tid; c < hd; c += kSbThreads) {
         tabs[c] = __ldg(p.cos + (size_t)pos * hd + c);

@@ -54,7 +54,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     __shared__ __align__(8) uint64_t full[kStages], empty[kStages], acc_full;
     __shared__ uint32_t tmem_base;
     __shared__ int failed;
-    __shared__ uint32_t silu_tab[256];                         // EXP / RECIP tables (SwiGLU epilogue)
+    __shared__ __align__(16) uint32_t silu_tab[256];           // EXP / RECIP tables (SwiGLU epilogue)
     if (TWO) stage_silu_tables(silu_tab);
     const GateAct act{p.act, p.act_a, p.act_b};
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;

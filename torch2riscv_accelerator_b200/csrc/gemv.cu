@@ -287,7 +287,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(LinearParams p, G
     __shared__ unsigned long long bkey[MR];
     __shared__ int last, failed;
     __shared__ uint32_t llcnt[kTpMaxRanks + 1];
-    __shared__ uint32_t silu_tab[256];                         // EXP / RECIP tables (SwiGLU epilogue)
+    __shared__ __align__(16) uint32_t silu_tab[256];           // EXP / RECIP tables (SwiGLU epilogue)
     __shared__ SfuSmem sfs;                                    // RECIP / RSQRT (prologue, requant)
     if (tid < MR) {
         bamax[tid] = 0u;
@@ -315,21 +315,45 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(LinearParams p, G
 #pragma unroll 1
         for (int i = 0; i < first; ++i) issue(i, i);          // weights: before the wait
     }
-    // row j of this CTA = tile j / tr, row j % tr; its scales are constants too
+    // Constants, staged now. Each thread issues all its loads before its first
+    // store (a store waits for its load: one memory latency per batch, not per
+    // element). Row j of this CTA = tile j / tr, row j % tr.
 #pragma unroll 1
-    for (int j = tid; j < my * tr; j += kGemvThreads) {
-        const int n = ((int)blockIdx.x + (j >> cf.lt) * (int)gridDim.x) * tr + (j & (tr - 1));
-        if (n < p.n) {
-            sw[j] = __ldg(p.s_w + n);
-            if (two) sw2[j] = __ldg(p.s_w2 + n);
+    for (int j0 = tid; j0 < my * tr; j0 += 2 * kGemvThreads) {
+        float a[2], b[2];
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            const int j = j0 + u * kGemvThreads;
+            const int n = ((int)blockIdx.x + (j >> cf.lt) * (int)gridDim.x) * tr + (j & (tr - 1));
+            const bool v = j < my * tr && n < p.n;
+            a[u] = v ? __ldg(p.s_w + n) : 0.f;
+            b[u] = v && two ? __ldg(p.s_w2 + n) : 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < 2; ++u) {
+            const int j = j0 + u * kGemvThreads;
+            if (j < my * tr) {
+                sw[j] = a[u];
+                if (two) sw2[j] = b[u];
+            }
         }
     }
-    if (two) stage_silu_tables(silu_tab);                      // constants too
-    if (pro == PRO_RMSQ) {                                     // the norm gain: a constant, staged now
+    if (two) stage_silu_tables(silu_tab);
+    if (pro == PRO_RMSQ) {                                     // the norm gain
 #pragma unroll 1
-        for (int c = tid; c < k; c += kGemvThreads) gs[c] = __ldg(p.norm_g + c);
+        for (int c0 = tid; c0 < k; c0 += 4 * kGemvThreads) {
+            float v[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int c = c0 + u * kGemvThreads;
+                v[u] = c < k ? __ldg(p.norm_g + c) : 0.f;
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u)
+                if (c0 + u * kGemvThreads < k) gs[c0 + u * kGemvThreads] = v[u];
+        }
     }
-    if (pro != PRO_I8 || two) stage_sfu(&sfs);               // constants too (read after later barriers)
+    if (pro != PRO_I8 || two) stage_sfu(&sfs);               // (read after later barriers)
     pdl_wait();
     W8A8_MARK(TR_GEMV, 1);
     pdl_trigger();

@@ -36,6 +36,28 @@ __constant__ __align__(16) static uint32_t g_rec_s[64] = W8A8_SFU_RECIP_S_INIT;
 __constant__ __align__(16) static uint32_t g_rsq_t[128] = W8A8_SFU_RSQRT_T_INIT;
 __constant__ __align__(16) static uint32_t g_rsq_s[128] = W8A8_SFU_RSQRT_S_INIT;
 
+// The same tables in global memory, in the layouts the kernels stage into
+// shared memory: a warp reading constant memory at 32 different indices is
+// served one index at a time, a 16-byte global load per thread at once. So
+// staging (before a kernel's programmatic-launch wait, on the path of the
+// launch when the previous kernel ends early) copies these blocks.
+// g_sfu_block: RECIP T | S, RSQRT T | S (SfuSmem); g_gate_block: EXP T | S,
+// RECIP T | S (the gate tables; its first half is the EXP table alone).
+__device__ __align__(16) static const uint32_t g_sfu_block[384] = {
+    W8A8_SFU_RECIP_T_LIST, W8A8_SFU_RECIP_S_LIST, W8A8_SFU_RSQRT_T_LIST, W8A8_SFU_RSQRT_S_LIST};
+__device__ __align__(16) static const uint32_t g_gate_block[256] = {
+    W8A8_SFU_EXP_T_LIST, W8A8_SFU_EXP_S_LIST, W8A8_SFU_RECIP_T_LIST, W8A8_SFU_RECIP_S_LIST};
+
+// Copy `words` (a multiple of 4) of a 16-byte aligned global block into
+// 16-byte aligned shared memory, one 16-byte load per thread.
+__device__ __forceinline__ void stage_block16(uint32_t* dst, const uint32_t* src, int words) {
+    for (int i = threadIdx.x; i < words / 4; i += blockDim.x)
+        reinterpret_cast<uint4*>(dst)[i] = __ldg(reinterpret_cast<const uint4*>(src) + i);
+}
+
+// The EXP table (T | S, 128 words) into 16-byte aligned shared memory.
+__device__ __forceinline__ void stage_exp_table(uint32_t* etab) { stage_block16(etab, g_gate_block, 128); }
+
 __device__ __forceinline__ float fmul(float a, float b) { return __fmul_rn(a, b); }
 __device__ __forceinline__ float fadd(float a, float b) { return __fadd_rn(a, b); }
 __device__ __forceinline__ float fsub(float a, float b) { return __fsub_rn(a, b); }
@@ -158,22 +180,13 @@ __device__ __forceinline__ float sfu_rsqrt(float x) { return sfu_rsqrt_tab(x, g_
 // RECIP and RSQRT tables in shared memory, for the scalar lookups on a
 // kernel's critical path (quant_act's scale, RMSNorm's factor): a lookup in
 // constant memory that misses the SM's constant cache costs an L2 round trip.
-struct SfuSmem {
+struct __align__(16) SfuSmem {
     uint32_t rec_t[64], rec_s[64], rsq_t[128], rsq_s[128];
 };
 
 // Every thread of the block takes part; a block barrier must separate it from
 // the first lookup.
-__device__ __forceinline__ void stage_sfu(SfuSmem* sf) {
-    for (int i = threadIdx.x; i < 128; i += blockDim.x) {
-        if (i < 64) {
-            sf->rec_t[i] = g_rec_t[i];
-            sf->rec_s[i] = g_rec_s[i];
-        }
-        sf->rsq_t[i] = g_rsq_t[i];
-        sf->rsq_s[i] = g_rsq_s[i];
-    }
-}
+__device__ __forceinline__ void stage_sfu(SfuSmem* sf) { stage_block16(sf->rec_t, g_sfu_block, 384); }
 
 __device__ __forceinline__ float sfu_recip_s(float x, const SfuSmem* sf) { return sfu_recip_tab(x, sf->rec_t, sf->rec_s); }
 __device__ __forceinline__ float sfu_rsqrt_s(float x, const SfuSmem* sf) { return sfu_rsqrt_tab(x, sf->rsq_t, sf->rsq_s); }
@@ -220,13 +233,9 @@ __device__ __forceinline__ float gate(float g, float u, const GateAct& act) {
     return act.kind == 1 ? gelu_gate(g, u, act.a, act.b) : silu_gate(g, u);
 }
 
-// Copy the four 64-word tables of silu_gate_tab into shared memory (whole block).
-__device__ __forceinline__ void stage_silu_tables(uint32_t* tab) {
-    for (int i = threadIdx.x; i < 256; i += blockDim.x) {
-        const int t = i >> 6, j = i & 63;
-        tab[i] = t == 0 ? g_exp_t[j] : t == 1 ? g_exp_s[j] : t == 2 ? g_rec_t[j] : g_rec_s[j];
-    }
-}
+// Copy the four 64-word tables of silu_gate_tab into 16-byte aligned shared
+// memory (whole block).
+__device__ __forceinline__ void stage_silu_tables(uint32_t* tab) { stage_block16(tab, g_gate_block, 256); }
 
 // Fixed-order sum of n values v(i) (llm/ref_model.py:179-186), computed by one
 // full warp: lane l < 16 adds v(l), v(16 + l), v(32 + l), ... in order (zero
