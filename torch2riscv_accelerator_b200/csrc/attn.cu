@@ -175,11 +175,16 @@ __device__ __forceinline__ void reg_norm_rope(float (&v)[8], int hd, const float
     }
 }
 
+// HD: the head dimension as a compile-time constant (0: p.head_dim). The
+// per-lane loops over a head vector (8 groups of 32 lanes, for head dims up to
+// 256) then keep only the groups the head has: their code runs once per launch
+// and is fetched cold, so the dead groups of a runtime bound cost time.
+template <int HD>
 __global__ void __maxnreg__(104) attn_kernel(AttnParams p) {
     extern __shared__ __align__(128) unsigned char sm[];
     W8A8_TRACE_BEGIN(TR_ATTN);
     cg::cluster_group cl = cg::this_cluster();
-    const int hd = p.head_dim, H = p.heads, Hk = p.kv_heads, G = H / Hk, T = p.seq_len;
+    const int hd = HD > 0 ? HD : p.head_dim, H = p.heads, Hk = p.kv_heads, G = H / Hk, T = p.seq_len;
     // batched decode: grid z is the slot (one row, its own position, qkv / att
     // rows and caches); prefill groups: z is a group of <= 16 rows of one
     // sequence (their K / V already in the cache); otherwise z = 0 and one
@@ -246,11 +251,21 @@ __global__ void __maxnreg__(104) attn_kernel(AttnParams p) {
             mbar_expect_tx(&tbar, (uint32_t)(nvalid * hd));
             bulk_g2s(ks, kc_p + ((size_t)kvh * T + t0) * hd, (uint32_t)(nvalid * hd), &tbar);
         }
-        const int vw = nv16 / 16;                              // 16-byte words per V^T row
-        for (int i = tid; i < hd * vw; i += kAttnThreads) {
-            const int c = i / vw, w = i % vw;
-            *reinterpret_cast<int4*>(vs + c * vstride + w * 16) =
-                __ldcg(reinterpret_cast<const int4*>(vc_p + ((size_t)kvh * hd + c) * T + t0) + w);
+        // 4 words in flight per thread: a store waits for its load, so one
+        // memory latency per 4 words, not per word
+        const int vw = nv16 / 16, nw = hd * vw;               // 16-byte words per V^T row, in all
+        for (int i0 = tid; i0 < nw; i0 += 4 * kAttnThreads) {
+            int4 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int i = i0 + u * kAttnThreads, c = i / vw, w = i % vw;
+                if (i < nw) v[u] = __ldcg(reinterpret_cast<const int4*>(vc_p + ((size_t)kvh * hd + c) * T + t0) + w);
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int i = i0 + u * kAttnThreads, c = i / vw, w = i % vw;
+                if (i < nw) *reinterpret_cast<int4*>(vs + c * vstride + w * 16) = v[u];
+            }
         }
     };
     if (nvalid > 0) {
@@ -266,6 +281,7 @@ __global__ void __maxnreg__(104) attn_kernel(AttnParams p) {
                 gains[hd + c] = __ldg(p.k_norm + c);
             }
     }
+    W8A8_MARK(TR_ATTN, 14);
     pdl_wait();
     W8A8_MARK(TR_ATTN, 1);
     pdl_trigger();
@@ -1033,11 +1049,15 @@ cudaError_t launch_attn(const AttnParams& q, cudaStream_t st) {
     p.chunk = g.chunk;
     const int mr = p.groups > 0 ? (p.rows < kMaxRows ? p.rows : kMaxRows) : p.rows;   // rows of a CTA, at most
     const AttnSmem L = attn_smem(mr, p.heads / p.kv_heads, p.head_dim, p.seq_len, p.chunk, p.variant);
-    cudaError_t e = cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.total);
+    auto kern = p.head_dim == 128 ? attn_kernel<128>
+              : p.head_dim == 64  ? attn_kernel<64>
+              : p.head_dim == 48  ? attn_kernel<48>
+                                  : attn_kernel<0>;
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.total);
     if (e != cudaSuccess) return e;
     // one shared-memory carveout for every kernel of the chain: no L1 / shared
     // reconfiguration of an SM between consecutive kernels
-    e = cudaFuncSetAttribute(attn_kernel, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
     if (e != cudaSuccess) return e;
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3(p.kv_heads, g.cs, p.slots > 0 ? p.slots : p.groups > 0 ? p.groups : 1);
@@ -1053,7 +1073,7 @@ cudaError_t launch_attn(const AttnParams& q, cudaStream_t st) {
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = g_use_pdl ? 2 : 1;
-    return cudaLaunchKernelEx(&cfg, attn_kernel, p);
+    return cudaLaunchKernelEx(&cfg, kern, p);
 }
 
 }  // namespace w8a8

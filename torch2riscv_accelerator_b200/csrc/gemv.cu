@@ -150,9 +150,11 @@ __device__ __forceinline__ void gemv_prologue(const LinearParams& p, int pro, in
             r = bc[0];
             W8A8_MARK(TR_GEMV, 7);
         }
-        // y = (x * r) * g in place, and the row amax (unless the producer posted it)
+        // y = (x * r) * g in place, and the row amax (unless the producer posted it).
+        // This loop and the int8 one below run once or a few times per thread
+        // from shared memory: not unrolled (their code is fetched cold each launch)
         float a = 0.f;
-#pragma unroll 4
+#pragma unroll 1
         for (int c = posted ? k / 4 : tid; c < k / 4; c += nt) {
             float4 v = xf4[c];
             if (pro == PRO_RMSQ) {
@@ -169,7 +171,7 @@ __device__ __forceinline__ void gemv_prologue(const LinearParams& p, int pro, in
         const float s = fmul(a, W8A8_C127);
         const float inv = sfu_recip_s(s, sf);
         W8A8_MARK(TR_GEMV, 9);
-#pragma unroll 4
+#pragma unroll 1
         for (int c = tid; c < k / 4; c += nt) {
             const float4 v = xf4[c];
             dst[c] = make_char4(to_i8(fmul(v.x, inv)), to_i8(fmul(v.y, inv)), to_i8(fmul(v.z, inv)),
@@ -354,6 +356,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(LinearParams p, G
         }
     }
     if (pro != PRO_I8 || two) stage_sfu(&sfs);               // (read after later barriers)
+    W8A8_MARK(TR_GEMV, 12);
     pdl_wait();
     W8A8_MARK(TR_GEMV, 1);
     pdl_trigger();

@@ -9,7 +9,8 @@
 // critical path); marks are taken by thread 0 wherever it passes them. Without
 // W8A8_TRACE the macros expand to nothing.
 //
-// Record (3 x u64): global timer ns, clock64, kind << 56 | tag << 48 | smid << 32 | cta.
+// Record (3 x u64): global timer ns, clock64,
+// kind << 56 | tag << 48 | smid << 32 | CTAs of the launch << 16 | cta (low 16 bits).
 #pragma once
 #include <cstdint>
 #include <cuda_runtime.h>
@@ -32,10 +33,12 @@ __device__ __forceinline__ void tr_write(unsigned int slot, int kind, int tag) {
     asm volatile("mov.u32 %0, %%smid;" : "=r"(sm));
     const uint64_t ck = clock64();
     const uint32_t cta = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);
+    const uint32_t ctas = gridDim.x * gridDim.y * gridDim.z;
     unsigned long long* r = g_tr_buf + 3ull * slot;
     r[0] = gt;
     r[1] = ck;
-    r[2] = ((uint64_t)kind << 56) | ((uint64_t)tag << 48) | ((uint64_t)sm << 32) | cta;
+    r[2] = ((uint64_t)kind << 56) | ((uint64_t)tag << 48) | ((uint64_t)(sm & 0xFFu) << 32) |
+           ((uint64_t)(ctas & 0xFFFFu) << 16) | (cta & 0xFFFFu);
 }
 
 // The CTA's base slot (shared by every function of the kernel).

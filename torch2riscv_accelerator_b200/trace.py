@@ -17,12 +17,14 @@ consecutive marks of a CTA, converted at the clock given).
 --batch D traces the batched step instead (D slots at position T - 8 of
 seeded random caches): the instrumented kernels it launches (embed).
 
-Mark numbers per kernel (csrc/gemv.cu, csrc/attn.cu): GEMV 0 entry, 1 wait
-returned, 6 x staged, 7 RMSNorm factor, 8 row max, 9 scale, 2 prologue done,
-10 first tile landed, 11 its dot products, 3 tiles done, 4 epilogue, 5 SwiGLU
-requant; attention 0 entry, 1 wait returned, 8 barrier, 10 q loaded, 11 QK-norm
-and RoPE, 12 q quantized, 2 K / V row and barrier, 3 scores, 4 maxima
-exchanged, 13 probabilities, 5 p.V pushed, 6 partials exchanged, 7 end.
+Mark numbers per kernel (csrc/gemv.cu, csrc/attn.cu): GEMV 0 entry, 12
+constants staged (before the wait), 1 wait returned, 6 x staged, 7 RMSNorm
+factor, 8 row max, 9 scale, 2 prologue done, 10 first tile landed, 11 its dot
+products, 3 tiles done, 4 epilogue, 5 SwiGLU requant; attention 0 entry, 14
+cache tiles and constants staged (before the wait), 1 wait returned, 8
+barrier, 10 q loaded, 11 QK-norm and RoPE, 12 q quantized, 2 K / V row and
+barrier, 3 scores, 4 maxima exchanged, 13 probabilities, 5 p.V pushed, 6
+partials exchanged, 7 end.
 """
 import argparse
 import os
@@ -130,19 +132,22 @@ def capture(config="Qwen3-0.6B", steps=3, seed=0):
 
 def launches(raw):
     """Group the records into launches: CTAs' record blocks in reservation
-    order, a new launch when the kernel kind changes or a CTA index repeats
-    (a launch's CTAs all reserve before the next launch's first CTA: it starts
-    only after every CTA of this one has passed its wait)."""
+    order (a launch's CTAs all reserve before the next launch's first CTA: it
+    starts only after every CTA of this one has passed its wait), a new launch
+    when the kernel kind or the launch's CTA count changes, a CTA index repeats
+    or the launch has all its CTAs."""
     meta = raw[:, 2]
     kind = (meta >> np.uint64(56)).astype(int)
     tag = ((meta >> np.uint64(48)) & np.uint64(0xFF)).astype(int)
-    cta = (meta & np.uint64(0xFFFFFFFF)).astype(int)
+    grid = ((meta >> np.uint64(16)) & np.uint64(0xFFFF)).astype(int)
+    cta = (meta & np.uint64(0xFFFF)).astype(int)
     out, cur = [], None
     for i in range(0, len(raw) - MARKS + 1, MARKS):
         if raw[i, 0] == 0 or tag[i] != 0:
             continue
-        if cur is None or cur["k"] != kind[i] or cta[i] in cur["ctas"]:
-            cur = {"k": kind[i], "kind": KIND.get(int(kind[i]), str(kind[i])), "ctas": {}}
+        if (cur is None or cur["k"] != kind[i] or cur["grid"] != grid[i] or cta[i] in cur["ctas"]
+                or len(cur["ctas"]) == cur["grid"]):
+            cur = {"k": kind[i], "kind": KIND.get(int(kind[i]), str(kind[i])), "grid": grid[i], "ctas": {}}
             out.append(cur)
         blk = raw[i:i + MARKS]
         cur["ctas"][cta[i]] = {j: (int(blk[j, 0]), int(blk[j, 1])) for j in range(MARKS) if blk[j, 0] != 0}
