@@ -131,18 +131,21 @@ def test_linear_worst_case_accumulator(k):
     assert np.array_equal(host(acc)[0], want)
 
 
-def test_linear_classifier_shape_sampled_rows():
-    """The C2 classifier (151936 x 1024): every output bit-exact, checked against
-    the oracle on a sample of rows."""
-    n, k = 151936, 1024
+@pytest.mark.parametrize("n,k", [(151936, 1024), (128256, 2048)])
+def test_linear_classifier_shape_sampled_rows(n, k):
+    """The C2 and C3 classifiers (151936 x 1024: two streaming CTAs per SM;
+    128256 x 2048: one CTA with the deeper ring): every output bit-exact,
+    checked against the oracle on a sample of rows; one row and four."""
     rng = np.random.default_rng(11)
     w, sw = quantize_rows((rng.standard_normal((n, k)) * 0.02).astype(F))
-    x = rng.standard_normal((1, k)).astype(F)
-    xq, sx = N.quant_act(x)
-    y = host(ops.linear(cu(xq), cu(sx), cu(w), cu(sw)))
     rows = np.concatenate([np.arange(64), rng.integers(0, n, 2000), np.arange(n - 64, n)])
-    wy, _ = N.linear(xq, sx, w[rows], sw[rows])
-    assert same_bits(y[:, rows], wy)[0]
+    wd, swd = cu(w), cu(sw)
+    for m in (1, 4):
+        x = rng.standard_normal((m, k)).astype(F)
+        xq, sx = N.quant_act(x)
+        y = host(ops.linear(cu(xq), cu(sx), wd, swd))
+        wy, _ = N.linear(xq, sx, w[rows], sw[rows])
+        assert same_bits(y[:, rows], wy)[0], m
 
 
 @pytest.mark.parametrize("m", [1, 16])
