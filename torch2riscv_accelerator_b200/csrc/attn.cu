@@ -179,17 +179,20 @@ __device__ __forceinline__ void reg_norm_rope(float (&v)[8], int hd, const float
 // per-lane loops over a head vector (8 groups of 32 lanes, for head dims up to
 // 256) then keep only the groups the head has: their code runs once per launch
 // and is fetched cold, so the dead groups of a runtime bound cost time.
-template <int HD>
+// VAR (0 NORM, 1 QSUM) and GRP (1: prefill groups, 0: decode rows) >= 0 fix
+// the softmax variant and the row mode the same way (-1: from p).
+template <int HD, int VAR = -1, int GRP = -1>
 __global__ void __maxnreg__(104) attn_kernel(AttnParams p) {
     extern __shared__ __align__(128) unsigned char sm[];
     W8A8_TRACE_BEGIN(TR_ATTN);
     cg::cluster_group cl = cg::this_cluster();
     const int hd = HD > 0 ? HD : p.head_dim, H = p.heads, Hk = p.kv_heads, G = H / Hk, T = p.seq_len;
+    const int variant = VAR >= 0 ? VAR : p.variant;
     // batched decode: grid z is the slot (one row, its own position, qkv / att
     // rows and caches); prefill groups: z is a group of <= 16 rows of one
     // sequence (their K / V already in the cache); otherwise z = 0 and one
     // sequence's M rows
-    const bool grp = p.groups > 0;
+    const bool grp = GRP >= 0 ? GRP == 1 : p.groups > 0;
     const size_t b = blockIdx.z, r0 = grp ? b * kMaxRows : b;
     const int M = grp ? min(kMaxRows, p.rows - (int)r0) : p.rows;
     const int32_t* const pos_p = p.pos + r0;
@@ -203,7 +206,7 @@ __global__ void __maxnreg__(104) attn_kernel(AttnParams p) {
     const int vpr = hd / 16, vstride = CH + 16;
     const int seg = (MG * hd + CS - 1) / CS;                  // outputs finished by each CTA
     const int qkv_dim = (H + 2 * Hk) * hd, q_dim = H * hd, kv_dim = Hk * hd;
-    const AttnSmem L = attn_smem(M, G, hd, T, CH, p.variant);
+    const AttnSmem L = attn_smem(M, G, hd, T, CH, variant);
     int8_t* ks = reinterpret_cast<int8_t*>(sm + L.ks);          // [CH][hd]
     int8_t* vs = reinterpret_cast<int8_t*>(sm + L.vs);          // [hd][CH + 16]: V transposed
     int8_t* qs = reinterpret_cast<int8_t*>(sm + L.qs);
@@ -426,7 +429,7 @@ __global__ void __maxnreg__(104) attn_kernel(AttnParams p) {
     }
     __syncthreads();
     if (nvalid > 0) {
-        if (p.variant == 0) {                                  // NORM: each row's whole e for the ordered sum
+        if (variant == 0) {                                    // NORM: each row's whole e for the ordered sum
             for (int r = 0; r < MG; ++r) {
                 const int m = r / G;
                 const int lim = lim_s[m];
@@ -514,12 +517,12 @@ __global__ void __maxnreg__(104) attn_kernel(AttnParams p) {
             int acc = 0, ssum = 0;
             for (int j = 0; j < CS; ++j) {
                 acc += pvp[j * seg + (i - lo)];
-                if (p.variant == 1) ssum += lsum[j][r];
+                if (variant == 1) ssum += lsum[j][r];
             }
             const float o = i2f(acc);
             const float av = p.a_v_ch ? p.a_v_ch[kvh * hd + c] : p.a_v;   // V per channel or per layer
             float out;
-            if (p.variant == 0) {
+            if (variant == 0) {
                 out = fmul(o, av);
             } else {
                 const float rq = fmul(sfu_recip_s(i2f(ssum), &sfs), 127.f);   // sum <= 127 T: exact in fp32
@@ -1042,6 +1045,16 @@ cudaError_t launch_kv_append(const AttnParams& p, cudaStream_t st) {
     return launch_k(kv_append_kernel, dim3(p.rows), dim3(kAttnThreads), smem, st, p);
 }
 
+using AttnKern = void (*)(AttnParams);
+
+// The instance for a head dim: decode rows with the variant compiled in, or
+// prefill groups (either variant).
+template <int HD>
+static AttnKern attn_pick(int variant, bool grp) {
+    if (grp) return attn_kernel<HD, -1, 1>;
+    return variant == 0 ? attn_kernel<HD, 0, 0> : attn_kernel<HD, 1, 0>;
+}
+
 cudaError_t launch_attn(const AttnParams& q, cudaStream_t st) {
     AttnParams p = q;
     const AttnGeom g = attn_geom(p.seq_len);
@@ -1049,9 +1062,11 @@ cudaError_t launch_attn(const AttnParams& q, cudaStream_t st) {
     p.chunk = g.chunk;
     const int mr = p.groups > 0 ? (p.rows < kMaxRows ? p.rows : kMaxRows) : p.rows;   // rows of a CTA, at most
     const AttnSmem L = attn_smem(mr, p.heads / p.kv_heads, p.head_dim, p.seq_len, p.chunk, p.variant);
-    auto kern = p.head_dim == 128 ? attn_kernel<128>
-              : p.head_dim == 64  ? attn_kernel<64>
-              : p.head_dim == 48  ? attn_kernel<48>
+    const bool grp = p.groups > 0;
+    const int var = p.variant;
+    auto kern = p.head_dim == 128 ? attn_pick<128>(var, grp)
+              : p.head_dim == 64  ? attn_pick<64>(var, grp)
+              : p.head_dim == 48  ? attn_pick<48>(var, grp)
                                   : attn_kernel<0>;
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.total);
     if (e != cudaSuccess) return e;
