@@ -608,10 +608,12 @@ def kernel_table(dec, reps=5):
             for _ in range(2):
                 g.replay()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            torch.cuda.nvtx.range_push(f"kernels:{name.split()[0]}")   # ncu --nvtx-include "kernels:classifier/"
             e0.record()
             for _ in range(reps):
                 g.replay()
             e1.record()
+            torch.cuda.nvtx.range_pop()
             torch.cuda.synchronize()
             us = e0.elapsed_time(e1) * 1e3 / (reps * per)
             out.append({"kind": name, "kernel": kern, "launches_per_step": n, "us_per_launch": us,
