@@ -44,13 +44,13 @@ METRIC = "decode tok/s (Qwen3-0.6B shape W8A8, T=2048)"
 # DRAM bytes (read + write) per launch of a kernel kind of the C2 step, from one
 # ncu capture each; the commands and the figures are in the named profiles.
 _LAYER = "profiles/decode_layer_c2_kernels.md"
-NCU_TRAFFIC = {"classifier GEMV (rmsnorm + quant)": {"bytes": 156221184 + 4762624,
+NCU_TRAFFIC = {"classifier GEMV (rmsnorm + quant)": {"bytes": 152923904 + 6045184,
                                                        "source": "profiles/classifier_gemv_c2.txt"},
-               "attention (cluster kernel, KV cache)": {"bytes": 4299776, "source": _LAYER},
-               "qkv GEMV (rmsnorm + quant prologue)": {"bytes": 4279040, "source": _LAYER},
-               "o_proj GEMV (+ residual)": {"bytes": 2173696, "source": _LAYER},
-               "gate|up GEMV (rmsnorm + quant, SiLU gate)": {"bytes": 6385152, "source": _LAYER},
-               "down GEMV (+ residual)": {"bytes": 3226624, "source": _LAYER}}
+               "attention (cluster kernel, KV cache)": {"bytes": 4279040, "source": _LAYER},
+               "qkv GEMV (rmsnorm + quant prologue)": {"bytes": 4252672, "source": _LAYER},
+               "o_proj GEMV (+ residual)": {"bytes": 2144512, "source": _LAYER},
+               "gate|up GEMV (rmsnorm + quant, SiLU gate)": {"bytes": 6370560, "source": _LAYER},
+               "down GEMV (+ residual)": {"bytes": 3197440, "source": _LAYER}}
 FPGA_TOKS = 3.41          # the reference's KV260 overlay, Qwen3-0.6B decode at T = 2048 (docs/results_v2.3.md:93-94)
 
 
@@ -691,6 +691,8 @@ def main():
     ap.add_argument("--config", default="Qwen3-0.6B")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--sustain", type=float, default=1.0,
+                    help="seconds of rewound decode windows replayed after the timed steps (0: none)")
     ap.add_argument("--cpu-steps", type=int, default=2)
     ap.add_argument("--pdl", type=int, default=1, help="programmatic dependent launch between kernels (1) or not (0)")
     ap.add_argument("--batch", type=int, default=1,
@@ -797,6 +799,34 @@ def main():
     final_pos = int(dec.pos[0].item())
     if ops.error_flags():
         raise RuntimeError("device error flags set during the decode steps")
+
+    # ---- sustained: the window of warmup + steps positions replayed from its
+    # start (the same tokens, the same cache rows rewritten with the same
+    # values) for about a second, clocks sampled throughout; every rank runs
+    # the same number of passes
+    window = args.warmup + args.steps
+    passes = max(1, int(args.sustain / (dt / args.steps * window))) if args.sustain > 0 else 0
+    sustained = None
+    if passes:
+        barrier(ws)
+        torch.cuda.synchronize()
+        s0, s1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with Clocks(local) as clk_s:
+            s0.record(st)
+            for _ in range(passes):
+                rewind()
+                for _ in range(window):
+                    g.replay()
+            s1.record(st)
+            torch.cuda.synchronize()
+        barrier(ws)
+        dts = max_over_ranks(s0.elapsed_time(s1) / 1e3, ws)
+        if ops.error_flags():
+            raise RuntimeError("device error flags set during the sustained steps")
+        sustained = {"value": seqs * passes * window / dts, "unit": "tok/s", "steps": passes * window,
+                     "seconds": dts, "clocks": clk_s.summary(),
+                     "timing": f"CUDA events around {passes} replays of the {window}-step window (positions "
+                               f"{P}..{P + window - 1}), each rewound to its first position (a device copy)"}
 
     # ---- e2e: LlamaDevice.forward with host inputs / outputs
     rewind()
@@ -905,6 +935,7 @@ def main():
             "cpu_baseline": cpu,
             "gpu_launches": args.steps * (1 + dec.kernel_launches(1)),
             "clocks": clk.summary(),
+            "sustained": sustained,
             "prefill": {"tokens": P, "seconds": prefill_s, "tok_s": P / prefill_s,
                         "first_call_seconds": prefill_first_s,
                         "timing": "host clock around LlamaDevice.prefill (synchronized), second call"},
