@@ -407,7 +407,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(LinearParams p, G
         int s = 0, ph = 0;                                     // tile i -> stage s, fill phase ph
 #pragma unroll 1
         for (int i = 0; i < my; ++i, (++s == stages ? (s = 0, ph ^= 1) : 0)) {
-            if (!mbar_wait(&full[s], (uint32_t)ph)) {
+            if (!mbar_wait_spin(&full[s], (uint32_t)ph)) {      // a spin: a suspended wait wakes late
                 atomicOr(&g_gemv_errors, 2u);
                 failed = 1;
                 break;
