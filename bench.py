@@ -290,9 +290,9 @@ def run_batch(args, cfg, qw, ws, rank, local):
                                    "from the seeded cache state", "logits_equal": all(ok), "tokens_equal": all(ok)}
     del kfull, vfull
     torch.cuda.empty_cache()
-    # one step: the captured graph (the tensor-parallel step holds NCCL
-    # collectives and runs eagerly)
-    run = dec.step if split else dec.capture().replay   # (a capture's warm-up step writes the rows of position P)
+    # one step: the captured graph (the tensor-parallel one with its NCCL
+    # all-reduces; the expert-parallel step runs eagerly)
+    run = dec.step if ep else dec.capture().replay      # (a capture's warm-up step writes the rows of position P)
     st = torch.cuda.current_stream()
     for _ in range(args.warmup):
         run()
@@ -351,6 +351,8 @@ def run_batch(args, cfg, qw, ws, rank, local):
         if parity is not None and not (parity["logits_equal"] and parity["tokens_equal"]):
             raise RuntimeError(f"parity failed: {parity}")
     barrier(ws)
+    run = None
+    dev.close()                                         # the step graph (NCCL work at N > 1) released first
     if ws > 1:
         import torch.distributed as dist
         dist.destroy_process_group()

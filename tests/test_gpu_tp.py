@@ -109,34 +109,40 @@ def _batch_inputs():
     return seqs, offs
 
 
-def _batch_worker(rank, ranks, port, path, kv):
+def _batch_worker(rank, ranks, port, path, kv, graphs):
     from torch2riscv_accelerator_b200 import ops
     from torch2riscv_accelerator_b200.tp import TpBatchLlamaDevice
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=ranks,
                             timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", rank))
+    dev = None
     try:
         cfg, qw, kv, _ = _model(kv)
-        dev = TpBatchLlamaDevice((cfg, qw, kv), slots=BATCH)
+        dev = TpBatchLlamaDevice((cfg, qw, kv), slots=BATCH, graphs=graphs)
         seqs, offs = _batch_inputs()
         lg = np.stack([dev.step([int(o) + s for o in offs], [int(t) for t in seqs[s]]) for s in range(BSTEPS)])
         torch.cuda.synchronize()
         np.savez(f"{path}.{rank}.npz", lg=lg, flags=np.array(ops.error_flags()))
     finally:
+        if dev is not None:
+            dev.close()                                # its graph holds NCCL work: released first
         dist.destroy_process_group()
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+@pytest.mark.parametrize("graphs", [False, True])
 @pytest.mark.parametrize("ranks", [2, 4, 8])
-def test_tp_batch_equals_one_gpu(ranks, tmp_path):
-    """Batched decode (20 slots at their own positions) over `ranks` GPUs: the
-    full [D, vocab] logits of every step equal the one-GPU BatchDecoder's."""
+def test_tp_batch_equals_one_gpu(ranks, graphs, tmp_path):
+    """Batched decode (20 slots at their own positions) over `ranks` GPUs, the
+    step launched eagerly or replayed as one CUDA graph with its NCCL
+    all-reduces: the full [D, vocab] logits of every step equal the one-GPU
+    BatchDecoder's."""
     if torch.cuda.device_count() < ranks:
         pytest.skip(f"needs {ranks} GPUs")
     from torch2riscv_accelerator_b200.runtime import BatchLlamaDevice
     path = str(tmp_path / "tpb")
     cfg, qw, kv, _ = _model()
-    mp.spawn(_batch_worker, args=(ranks, _port(), path, kv), nprocs=ranks, join=True)
+    mp.spawn(_batch_worker, args=(ranks, _port(), path, kv, graphs), nprocs=ranks, join=True)
     dev = BatchLlamaDevice((cfg, qw, kv), slots=BATCH)
     seqs, offs = _batch_inputs()
     ref = np.stack([dev.step([int(o) + s for o in offs], [int(t) for t in seqs[s]]) for s in range(BSTEPS)])

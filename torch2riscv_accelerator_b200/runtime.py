@@ -313,6 +313,9 @@ class BatchLlamaDevice:
         return out
 
     def close(self):
+        if self.dec is not None:
+            self.dec.graph = None                         # a graph may hold NCCL work (tensor parallel)
+            torch.cuda.synchronize()
         self.dec = None
         torch.cuda.empty_cache()
 

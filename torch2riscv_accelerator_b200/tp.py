@@ -424,7 +424,13 @@ class TpBatchDecoder(BatchDecoder):
         ops.gemm(xq, sx, self.cls_q, self.cls_s, out=self.logits)
 
     def capture(self):
-        raise RuntimeError("the tensor-parallel batch step holds NCCL collectives: run it eagerly")
+        """The step as one CUDA graph, its NCCL all-reduces included (a
+        collective: every rank captures, in the same order, after the eager
+        warm-up step inside has run the same collectives). The launches stay
+        plain (no programmatic dependent launch). Release the graph (the
+        device's close(), or `self.graph = None`) before the process group is
+        destroyed: a graph that holds NCCL work keeps its communicator busy."""
+        return BatchDecoder.capture(self)
 
     def gather_logits(self):
         P, D, vs = self.ranks, self.slots, self.cfg.vocab
@@ -443,14 +449,16 @@ class TpBatchDecoder(BatchDecoder):
 class TpBatchLlamaDevice(BatchLlamaDevice):
     """BatchLlamaDevice (`llm/runtime.py:155-241`) over a TpBatchDecoder: every
     rank constructs it and calls step() / generate() in the same order; every
-    rank returns the full [D, vocab] logits."""
+    rank returns the full [D, vocab] logits. graphs: replay the step as one
+    CUDA graph with its collectives (close() before the process group ends),
+    else launch it eagerly."""
 
-    def __init__(self, model, slots=None, group=None, device=None):
+    def __init__(self, model, slots=None, group=None, device=None, graphs=True):
         if not isinstance(model, TpBatchDecoder):
             cfg, qw, kv = model
             dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
             model = TpBatchDecoder(cfg, qw, kv, slots, group=group, device=dev)
-        super().__init__(model, graphs=False)
+        super().__init__(model, graphs=graphs)
         self.cfg = model.full_cfg
         self._out = torch.zeros(model.slots, self.cfg.vocab, dtype=F32).pin_memory()
 
