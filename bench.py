@@ -684,7 +684,7 @@ def config_of(cfg, args, ws, tp=False, ep=False):
                   "cache, over the 126 MB L2"}
 
 
-def main():
+def build_parser():
     ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=13)
@@ -710,7 +710,11 @@ def main():
                     help="time one kernel alone instead (profiling): attn_batch = the batched decode attention "
                          "over one layer's caches of --batch slots at position 2040; moe_rows = one layer's MoE "
                          "FFN over --batch rows (a MoE --config)")
-    args = ap.parse_args()
+    return ap
+
+
+def main():
+    args = build_parser().parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
     from torch2riscv_accelerator_b200.config import CONFIGS
